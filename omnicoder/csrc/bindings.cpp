@@ -1,0 +1,238 @@
+// Python bindings of the omnicoder sm_100a kernels (module omnicoder._C).
+//
+// Every entry point validates devices, dtypes, shapes and alignment on the
+// host and launches on the current PyTorch CUDA stream.  Kernels report
+// device-side failures (bounded waits that ran out, failed bounds checks) in a
+// per-device status block that `status()` reads.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <vector>
+
+#include "gemm_sm100.h"
+#include "kernels.h"
+
+namespace omni {
+
+// ---------------------------------------------------------------------------
+// Status block (one per device, allocated on first use, never freed)
+// ---------------------------------------------------------------------------
+static std::mutex g_status_mu;
+static std::vector<void*> g_status(64, nullptr);
+
+void* status_ptr() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_status_mu);
+  if (g_status[dev] == nullptr) {
+    void* p = nullptr;
+    C10_CUDA_CHECK(cudaMalloc(&p, 16));
+    C10_CUDA_CHECK(cudaMemset(p, 0, 16));
+    g_status[dev] = p;
+  }
+  return g_status[dev];
+}
+
+std::vector<int64_t> status_read() {
+  int h[4] = {0, 0, 0, 0};
+  C10_CUDA_CHECK(cudaMemcpy(h, status_ptr(), 16, cudaMemcpyDeviceToHost));
+  return {h[0], h[1], h[2]};
+}
+
+void status_reset() { C10_CUDA_CHECK(cudaMemset(status_ptr(), 0, 16)); }
+
+#define CHECK_CUDA_T(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bfloat16")
+#define CHECK_ROWMAJOR(x) TORCH_CHECK((x).dim() >= 2 && (x).stride(-1) == 1, #x " must have a contiguous last dim")
+
+static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// ---------------------------------------------------------------------------
+// GEMM
+// ---------------------------------------------------------------------------
+// Dense: C = alpha * op(A) op(B)^T.
+//   a_mn=false: A [M,K]; a_mn=true: A [K,M].  b_mn=false: B [N,K]; b_mn=true: B [K,N].
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn, int64_t epilogue,
+          double alpha, const c10::optional<at::Tensor>& R, const c10::optional<at::Tensor>& H, int64_t block_n) {
+  CHECK_CUDA_T(A);
+  CHECK_CUDA_T(B);
+  CHECK_CUDA_T(C);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D operands expected");
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(B);
+  CHECK_ROWMAJOR(C);
+  const c10::cuda::CUDAGuard guard(A.device());
+  GemmDesc d;
+  d.mode = GEMM_DENSE;
+  d.epilogue = (int)epilogue;
+  d.block_n = (int)block_n;
+  d.a_mn_major = a_mn;
+  d.b_mn_major = b_mn;
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm: reduction dims differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(K % 8 == 0 && M > 0 && N > 0 && K > 0, "gemm: K must be a positive multiple of 8");
+  d.M = (int)M;
+  d.N = (int)N;
+  d.K = (int)K;
+  d.A = A.data_ptr();
+  d.lda = A.stride(0);
+  d.rows_a = A.size(0);
+  d.K_extent_a = K;
+  d.B = B.data_ptr();
+  d.ldb = B.stride(0);
+  d.K_extent_b = K;
+  d.C = C.data_ptr();
+  d.ldc = C.stride(0);
+  d.alpha = (float)alpha;
+  const int64_t out_cols = epilogue == EPI_SWIGLU ? N / 2 : (epilogue == EPI_SWIGLU_BWD ? 2 * N : N);
+  TORCH_CHECK(C.size(0) == M && C.size(1) == out_cols, "gemm: output shape mismatch");
+  if (epilogue == EPI_STORE_F32 || epilogue == EPI_ACCUM_F32) {
+    TORCH_CHECK(C.scalar_type() == at::kFloat, "gemm: fp32 output expected");
+  } else {
+    CHECK_BF16(C);
+  }
+  if (epilogue == EPI_ADD_BF16 || epilogue == EPI_SWIGLU_BWD) {
+    TORCH_CHECK(R.has_value(), "gemm: epilogue needs R");
+    CHECK_BF16(R.value());
+    CHECK_ROWMAJOR(R.value());
+    d.R = R->data_ptr();
+    d.ldr = R->stride(0);
+  }
+  if (epilogue == EPI_SWIGLU) {
+    TORCH_CHECK(N % 64 == 0, "gemm swiglu: N must be a multiple of 64");
+    if (H.has_value()) {
+      CHECK_BF16(H.value());
+      TORCH_CHECK(H->size(0) == M && H->size(1) == N, "gemm swiglu: H shape");
+      d.H = H->data_ptr();
+      d.ldh = H->stride(0);
+    }
+  }
+  if (epilogue == EPI_SWIGLU_BWD) TORCH_CHECK(N % 32 == 0, "gemm swiglu bwd: N must be a multiple of 32");
+  d.status = status_ptr();
+  gemm_sm100_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Grouped-M: rows of A ([rows, K], K-major) segmented by offsets [G+1];
+// B is [G, N, K] (b_mn=false) or [G, K, N] (b_mn=true).
+void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor& C,
+                    bool b_mn, int64_t epilogue, double alpha, const c10::optional<at::Tensor>& R,
+                    const c10::optional<at::Tensor>& H, int64_t block_n, int64_t max_rows_hint) {
+  CHECK_CUDA_T(A);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_ROWMAJOR(A);
+  TORCH_CHECK(B.dim() == 3 && B.is_contiguous(), "gemm_grouped_m: B must be a contiguous [G, ., .] stack");
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda() && offsets.numel() == B.size(0) + 1,
+              "gemm_grouped_m: offsets must be int32 [G+1] on the device");
+  const c10::cuda::CUDAGuard guard(A.device());
+  GemmDesc d;
+  d.mode = GEMM_GROUPED_M;
+  d.epilogue = (int)epilogue;
+  d.block_n = (int)block_n;
+  d.a_mn_major = false;
+  d.b_mn_major = b_mn;
+  const int64_t G = B.size(0);
+  const int64_t K = A.size(1);
+  const int64_t N = b_mn ? B.size(2) : B.size(1);
+  TORCH_CHECK((b_mn ? B.size(1) : B.size(2)) == K, "gemm_grouped_m: reduction dims differ");
+  TORCH_CHECK(K % 8 == 0, "gemm_grouped_m: K must be a multiple of 8");
+  d.M = (int)A.size(0);
+  d.N = (int)N;
+  d.K = (int)K;
+  d.A = A.data_ptr();
+  d.lda = A.stride(0);
+  d.rows_a = A.size(0);
+  d.K_extent_a = K;
+  d.B = B.data_ptr();
+  d.ldb = B.stride(1);
+  d.b_group_stride = B.stride(0);
+  d.K_extent_b = K;
+  d.num_groups = (int)G;
+  d.group_offsets = offsets.data_ptr<int>();
+  d.max_rows_hint = (int)max_rows_hint;
+  d.C = C.data_ptr();
+  d.ldc = C.stride(0);
+  d.alpha = (float)alpha;
+  CHECK_BF16(C);
+  CHECK_ROWMAJOR(C);
+  if (epilogue == EPI_SWIGLU_BWD) {
+    TORCH_CHECK(R.has_value(), "gemm_grouped_m: swiglu bwd needs R");
+    d.R = R->data_ptr();
+    d.ldr = R->stride(0);
+  }
+  if (epilogue == EPI_SWIGLU && H.has_value()) {
+    d.H = H->data_ptr();
+    d.ldh = H->stride(0);
+  }
+  d.status = status_ptr();
+  gemm_sm100_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Grouped-K: C[g] (M x N) = alpha * A[rows_g]^T B[rows_g] with A [rows, M], B [rows, N].
+void gemm_grouped_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor& C,
+                    int64_t epilogue, double alpha, int64_t block_n) {
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(B);
+  TORCH_CHECK(C.dim() == 3 && C.is_contiguous(), "gemm_grouped_k: C must be a contiguous [G, M, N] stack");
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.numel() == C.size(0) + 1, "gemm_grouped_k: offsets");
+  const c10::cuda::CUDAGuard guard(A.device());
+  GemmDesc d;
+  d.mode = GEMM_GROUPED_K;
+  d.epilogue = (int)epilogue;
+  d.block_n = (int)block_n;
+  d.a_mn_major = true;
+  d.b_mn_major = true;
+  d.M = (int)A.size(1);
+  d.N = (int)B.size(1);
+  d.K = 0;
+  TORCH_CHECK(C.size(1) == d.M && C.size(2) == d.N, "gemm_grouped_k: output shape");
+  d.A = A.data_ptr();
+  d.lda = A.stride(0);
+  d.rows_a = A.size(0);
+  d.K_extent_a = A.size(0);
+  d.B = B.data_ptr();
+  d.ldb = B.stride(0);
+  d.K_extent_b = B.size(0);
+  d.num_groups = (int)C.size(0);
+  d.group_offsets = offsets.data_ptr<int>();
+  d.C = C.data_ptr();
+  d.ldc = C.stride(1);
+  d.c_group_stride = C.stride(0);
+  d.alpha = (float)alpha;
+  if (epilogue == EPI_STORE_F32 || epilogue == EPI_ACCUM_F32) {
+    TORCH_CHECK(C.scalar_type() == at::kFloat, "gemm_grouped_k: fp32 output expected");
+  } else {
+    CHECK_BF16(C);
+  }
+  d.status = status_ptr();
+  gemm_sm100_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace omni
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "omnicoder sm_100a kernels (tcgen05/TMEM/TMA)";
+  m.def("status", &omni::status_read, "Read the device status block: [code, info, count]");
+  m.def("status_reset", &omni::status_reset);
+  m.def("gemm", &omni::gemm, "tcgen05 GEMM", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
+        py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
+        py::arg("H") = py::none(), py::arg("block_n") = 256);
+  m.def("gemm_grouped_m", &omni::gemm_grouped_m, py::arg("A"), py::arg("B"), py::arg("offsets"), py::arg("C"),
+        py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
+        py::arg("H") = py::none(), py::arg("block_n") = 256, py::arg("max_rows_hint") = 0);
+  m.def("gemm_grouped_k", &omni::gemm_grouped_k, py::arg("A"), py::arg("B"), py::arg("offsets"), py::arg("C"),
+        py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("block_n") = 256);
+  omni::register_kernels(m);
+}

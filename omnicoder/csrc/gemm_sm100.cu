@@ -1,0 +1,677 @@
+// tcgen05 / TMEM / TMA GEMM for sm_100a.
+//
+// C[M,N] = alpha * sum_k A[M,k] * B[N,k]   (fp32 accumulation in tensor memory)
+//
+// Operand storage (bf16, row-major in global memory):
+//   A K-major  : A stored [M, K]          A MN-major : A stored [K, M]
+//   B K-major  : B stored [N, K]          B MN-major : B stored [K, N]
+// This covers every linear-layer GEMM of training: Y = X W^T (K,K),
+// dX = dY W (K,MN) and dW = dY^T X (MN,MN).
+//
+// Modes:
+//   dense     : one problem.
+//   grouped-M : rows of A are segmented into groups (experts) by a device
+//               offset table whose entries are multiples of 128; group g uses
+//               B[g] (a [G, N, K] or [G, K, N] weight stack).  The row count is
+//               read on the device, so no host synchronisation is needed.
+//   grouped-K : the reduction runs over the rows of group g only and the
+//               output is C[g] (expert weight gradients).
+//
+// Kernel structure (one persistent CTA per SM, 192 threads):
+//   warp 0     : TMA producer (one lane), 4-6 stage shared-memory ring
+//   warp 1     : TMEM allocator + tcgen05.mma issuer (one lane)
+//   warps 2..5 : epilogue; each warp owns the 32 TMEM lanes (rows) that its
+//                warp index selects, reads 32 fp32 columns per tcgen05.ld,
+//                applies the fused epilogue and stores to global memory.
+// The accumulator is double buffered in TMEM so the epilogue of tile i
+// overlaps the main loop of tile i+1.
+//
+// The epilogue fusions cover what the reference's linear layers and expert FFN
+// do around their GEMMs (src/omnicoder/modeling/kernels/moe_scatter.py:738-753
+// applies bias + GELU between the two batched expert GEMMs; the spec family
+// uses SwiGLU instead).
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "gemm_sm100.h"
+
+namespace omni {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+constexpr int kSwizzleChunk = 8192;  // bytes of one 64(MN) x 64(K) bf16 swizzled box
+
+struct GemmArgs {
+  int M, N, K;
+  int num_groups;
+  const int* group_offsets;  // [G+1], multiples of 128 (grouped modes)
+  void* C;
+  long long ldc;
+  long long c_group_stride;  // elements between C[g] and C[g+1] (grouped-K)
+  const void* R;             // residual (EPI_ADD_BF16) or pre-activation H (EPI_SWIGLU_BWD)
+  long long ldr;
+  void* H;                   // pre-activation store (EPI_SWIGLU)
+  long long ldh;
+  float alpha;
+  StatusBlock* status;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStageA = kBM * kBK * 2;    // 16 KB
+  static constexpr int kStageB = BN * kBK * 2;     // 32 KB at BN=256
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kTmemCols = 2 * BN;         // double-buffered accumulator
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct TileInfo {
+  int m0, n0, g, k0, num_kb;
+  int m_limit;  // rows >= m_limit are not stored
+};
+
+template <int BN, int MODE>
+__device__ __forceinline__ int total_tiles(const GemmArgs& p, const int* s_off) {
+  const int num_n = (p.N + BN - 1) / BN;
+  if (MODE == GEMM_DENSE) return ((p.M + kBM - 1) / kBM) * num_n;
+  if (MODE == GEMM_GROUPED_M) return (s_off[p.num_groups] / kBM) * num_n;
+  return p.num_groups * ((p.M + kBM - 1) / kBM) * num_n;
+}
+
+template <int BN, int MODE>
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, int t, const int* s_off) {
+  TileInfo ti;
+  const int num_n = (p.N + BN - 1) / BN;
+  if (MODE == GEMM_DENSE) {
+    // Grouped raster: 8 M-tiles share each sweep over N for L2 reuse of B.
+    const int num_m = (p.M + kBM - 1) / kBM;
+    constexpr int GM = 8;
+    const int per_group = GM * num_n;
+    const int grp = t / per_group;
+    const int first_m = grp * GM;
+    const int gsize = min(num_m - first_m, GM);
+    const int r = t - grp * per_group;
+    ti.m0 = (first_m + r % gsize) * kBM;
+    ti.n0 = (r / gsize) * BN;
+    ti.g = 0;
+    ti.k0 = 0;
+    ti.num_kb = (p.K + kBK - 1) / kBK;
+    ti.m_limit = p.M;
+  } else if (MODE == GEMM_GROUPED_M) {
+    const int mt = t / num_n;
+    ti.m0 = mt * kBM;
+    ti.n0 = (t - mt * num_n) * BN;
+    int g = 0;
+    while (g + 1 < p.num_groups && s_off[g + 1] <= ti.m0) ++g;
+    ti.g = g;
+    ti.k0 = 0;
+    ti.num_kb = (p.K + kBK - 1) / kBK;
+    ti.m_limit = s_off[g + 1];
+  } else {
+    const int num_m = (p.M + kBM - 1) / kBM;
+    const int per_g = num_m * num_n;
+    const int g = t / per_g;
+    const int r = t - g * per_g;
+    ti.g = g;
+    ti.m0 = (r / num_n) * kBM;
+    ti.n0 = (r % num_n) * BN;
+    ti.k0 = s_off[g];
+    ti.num_kb = (s_off[g + 1] - s_off[g]) / kBK;
+    ti.m_limit = p.M;
+  }
+  return ti;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue: 32 accumulator columns of one row -> global memory
+// ---------------------------------------------------------------------------
+template <int EPI>
+__device__ __forceinline__ void store_chunk(const GemmArgs& p, int row, int col, int g, const float* v,
+                                            bool row_ok) {
+  if (!row_ok) return;
+  const int ncols = min(32, p.N - col);
+  if (ncols <= 0) return;
+  if (EPI == EPI_STORE_BF16 || EPI == EPI_ADD_BF16) {
+    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)g * p.c_group_stride +
+                       (long long)row * p.ldc + col;
+    float o[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) o[j] = v[j] * p.alpha;
+    if (EPI == EPI_ADD_BF16) {
+      const __nv_bfloat16* R = reinterpret_cast<const __nv_bfloat16*>(p.R) + (long long)row * p.ldr + col;
+      if (ncols == 32) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 r = *reinterpret_cast<const uint4*>(R + q * 8);
+          const uint32_t* rw = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            o[q * 8 + 2 * j] += bf16_lo(rw[j]);
+            o[q * 8 + 2 * j + 1] += bf16_hi(rw[j]);
+          }
+        }
+      } else {
+        for (int j = 0; j < ncols; ++j) o[j] += __bfloat162float(R[j]);
+      }
+    }
+    if (ncols == 32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(o[q * 8 + 0], o[q * 8 + 1]);
+        w.y = pack_bf16x2(o[q * 8 + 2], o[q * 8 + 3]);
+        w.z = pack_bf16x2(o[q * 8 + 4], o[q * 8 + 5]);
+        w.w = pack_bf16x2(o[q * 8 + 6], o[q * 8 + 7]);
+        *reinterpret_cast<uint4*>(C + q * 8) = w;
+      }
+    } else {
+      for (int j = 0; j < ncols; ++j) C[j] = __float2bfloat16(o[j]);
+    }
+  } else if (EPI == EPI_STORE_F32 || EPI == EPI_ACCUM_F32) {
+    float* C = reinterpret_cast<float*>(p.C) + (long long)g * p.c_group_stride + (long long)row * p.ldc + col;
+    if (ncols == 32) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 w = make_float4(v[4 * q] * p.alpha, v[4 * q + 1] * p.alpha, v[4 * q + 2] * p.alpha,
+                               v[4 * q + 3] * p.alpha);
+        if (EPI == EPI_ACCUM_F32) {
+          float4 c = *reinterpret_cast<const float4*>(C + 4 * q);
+          w.x += c.x;
+          w.y += c.y;
+          w.z += c.z;
+          w.w += c.w;
+        }
+        *reinterpret_cast<float4*>(C + 4 * q) = w;
+      }
+    } else {
+      for (int j = 0; j < ncols; ++j) C[j] = v[j] * p.alpha + (EPI == EPI_ACCUM_F32 ? C[j] : 0.f);
+    }
+  }
+}
+
+// SwiGLU forward epilogue.  The gate/up weight rows are interleaved in blocks
+// of 32: accumulator columns [64j, 64j+32) are gate rows 32j.., columns
+// [64j+32, 64j+64) the matching up rows.  Output column 32j+i of the
+// activation is silu(gate_i) * up_i.  The raw (gate, up) pair is also stored
+// (interleaved, as computed) for the backward pass.
+__device__ __forceinline__ void store_swiglu(const GemmArgs& p, int row, int col /*acc col of gate chunk*/,
+                                             const float* gt, const float* up, bool row_ok) {
+  if (!row_ok || col >= p.N) return;
+  const int ocol = col >> 1;
+  __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)row * p.ldc + ocol;
+  uint32_t packed[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float a0 = silu_f(gt[2 * j]) * up[2 * j];
+    const float a1 = silu_f(gt[2 * j + 1]) * up[2 * j + 1];
+    packed[j] = pack_bf16x2(a0, a1);
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(C + q * 8) =
+        make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+  if (p.H != nullptr) {
+    __nv_bfloat16* H = reinterpret_cast<__nv_bfloat16*>(p.H) + (long long)row * p.ldh + col;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      *reinterpret_cast<uint4*>(H + q * 8) =
+          make_uint4(pack_bf16x2(gt[8 * q], gt[8 * q + 1]), pack_bf16x2(gt[8 * q + 2], gt[8 * q + 3]),
+                     pack_bf16x2(gt[8 * q + 4], gt[8 * q + 5]), pack_bf16x2(gt[8 * q + 6], gt[8 * q + 7]));
+      *reinterpret_cast<uint4*>(H + 32 + q * 8) =
+          make_uint4(pack_bf16x2(up[8 * q], up[8 * q + 1]), pack_bf16x2(up[8 * q + 2], up[8 * q + 3]),
+                     pack_bf16x2(up[8 * q + 4], up[8 * q + 5]), pack_bf16x2(up[8 * q + 6], up[8 * q + 7]));
+    }
+  }
+}
+
+// SwiGLU backward epilogue: the accumulator holds dA (gradient of the
+// activation, 32 columns starting at activation column `col`).  R points at
+// the saved interleaved pre-activation H; the output C is dH in the same
+// interleaved layout (ldc counts dH columns = 2 * activation columns).
+__device__ __forceinline__ void store_swiglu_bwd(const GemmArgs& p, int row, int col, const float* da,
+                                                 bool row_ok) {
+  if (!row_ok || col >= p.N) return;
+  const __nv_bfloat16* H = reinterpret_cast<const __nv_bfloat16*>(p.R) + (long long)row * p.ldr + 2 * col;
+  __nv_bfloat16* D = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)row * p.ldc + 2 * col;
+  float gt[32], up[32];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 a = *reinterpret_cast<const uint4*>(H + q * 8);
+    uint4 b = *reinterpret_cast<const uint4*>(H + 32 + q * 8);
+    const uint32_t* aw = reinterpret_cast<const uint32_t*>(&a);
+    const uint32_t* bw = reinterpret_cast<const uint32_t*>(&b);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      gt[q * 8 + 2 * j] = bf16_lo(aw[j]);
+      gt[q * 8 + 2 * j + 1] = bf16_hi(aw[j]);
+      up[q * 8 + 2 * j] = bf16_lo(bw[j]);
+      up[q * 8 + 2 * j + 1] = bf16_hi(bw[j]);
+    }
+  }
+  uint32_t dg[16], du[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float r[2], s[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float g = gt[2 * j + h], u = up[2 * j + h], d = da[2 * j + h] * p.alpha;
+      const float sg = 1.0f / (1.0f + __expf(-g));
+      const float si = g * sg;
+      s[h] = d * si;                                // d/du
+      r[h] = d * u * (sg * (1.0f + g * (1.0f - sg)));  // d/dg
+    }
+    dg[j] = pack_bf16x2(r[0], r[1]);
+    du[j] = pack_bf16x2(s[0], s[1]);
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    *reinterpret_cast<uint4*>(D + q * 8) = make_uint4(dg[4 * q], dg[4 * q + 1], dg[4 * q + 2], dg[4 * q + 3]);
+    *reinterpret_cast<uint4*>(D + 32 + q * 8) =
+        make_uint4(du[4 * q], du[4 * q + 1], du[4 * q + 2], du[4 * q + 3]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      GemmArgs p) {
+  using C_ = Cfg<BN>;
+  constexpr int S = C_::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * C_::kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;  // [2]
+  uint64_t* drain_bar = tempty_bar + 2;  // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  __shared__ int s_off[GEMM_MAX_GROUPS + 1];
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (MODE != GEMM_DENSE) {
+    for (int i = threadIdx.x; i <= p.num_groups; i += kThreads) s_off[i] = p.group_offsets[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4);
+    }
+    mbar_init(drain_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C_::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int ntiles = total_tiles<BN, MODE>(p, s_off);
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, MODE>(p, t, s_off);
+        for (int kb = 0; kb < ti.num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + stage * C_::kStageBytes;
+          uint8_t* sB = sA + C_::kStageA;
+          mbar_arrive_expect_tx(&full_bar[stage], C_::kStageBytes);
+          const int k = ti.k0 + kb * kBK;
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, &full_bar[stage], k, ti.m0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < kBM / 64; ++i) tma_load_2d(sA + i * kSwizzleChunk, &tmA, &full_bar[stage], ti.m0 + 64 * i, k);
+          }
+          if (!B_MN) {
+            if (MODE == GEMM_GROUPED_M)
+              tma_load_3d(sB, &tmB, &full_bar[stage], k, ti.n0, ti.g);
+            else
+              tma_load_2d(sB, &tmB, &full_bar[stage], k, ti.n0);
+          } else {
+#pragma unroll
+            for (int i = 0; i < BN / 64; ++i) {
+              if (MODE == GEMM_GROUPED_M)
+                tma_load_3d(sB + i * kSwizzleChunk, &tmB, &full_bar[stage], ti.n0 + 64 * i, k, ti.g);
+              else
+                tma_load_2d(sB + i * kSwizzleChunk, &tmB, &full_bar[stage], ti.n0 + 64 * i, k);
+            }
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(kBM, BN, A_MN, B_MN, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, MODE>(p, t, s_off);
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) break;
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = 0; kb < ti.num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.status, STATUS_TIMEOUT_TMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C_::kStageBytes);
+          const uint32_t b_addr = a_addr + C_::kStageA;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a_addr + kk * 2048, kSwizzleChunk, 1024)
+                                        : umma_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + kk * 2048, kSwizzleChunk, 1024)
+                                        : umma_desc_sw128(b_addr + kk * 32, 16, 1024);
+            tc_mma_f16(tmem_d, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // Drain: wait for every MMA this thread issued before TMEM is released.
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, p.status, STATUS_TIMEOUT_DRAIN);
+    }
+  } else {
+    // ------------------------------ Epilogue ----------------------------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const TileInfo ti = tile_info<BN, MODE>(p, t, s_off);
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, STATUS_TIMEOUT_TMEM_FULL)) break;
+      tc_fence_after();
+      const int row = ti.m0 + row_in_tile;
+      const bool row_ok = row < ti.m_limit;
+      const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(quarter * 32) << 16);
+      const bool zero = ti.num_kb == 0;
+      if (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          float gt[32], up[32];
+          tmem_ld32(tbase + c * 64, gt);
+          tmem_ld32(tbase + c * 64 + 32, up);
+          tc_wait_ld();
+          store_swiglu(p, row, ti.n0 + c * 64, gt, up, row_ok);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          tc_wait_ld();
+          if (zero) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          if (EPI == EPI_SWIGLU_BWD)
+            store_swiglu_bwd(p, row, ti.n0 + c * 32, v, row_ok);
+          else
+            store_chunk<EPI>(p, row, ti.n0 + c * 32, ti.g, v, row_ok);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || ptr == nullptr)
+      throw std::runtime_error("omnicoder: cuTensorMapEncodeTiled entry point not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// rank-2 or rank-3 bf16 tensor map with 128-byte swizzle.  dims[0] is the
+// contiguous dimension; strides are in bytes for dims 1.. .
+static CUtensorMap make_tmap(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                             const uint32_t* box) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    throw std::runtime_error("omnicoder gemm: operand base address must be 16-byte aligned");
+  for (int i = 0; i + 1 < rank; ++i)
+    if (strides_bytes[i] % 16 != 0)
+      throw std::runtime_error("omnicoder gemm: operand row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t d[3], s[2];
+  cuuint32_t b[3], es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("omnicoder gemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
+static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
+  using C_ = Cfg<BN>;
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, MODE>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes);
+    attr_set = true;
+  }
+  // A operand tensor map.
+  CUtensorMap tmA, tmB;
+  {
+    if (!A_MN) {  // A stored [rowsA, K] with row stride lda
+      uint64_t dims[2] = {(uint64_t)d.K_extent_a, (uint64_t)d.rows_a};
+      uint64_t str[1] = {(uint64_t)d.lda * 2};
+      uint32_t box[2] = {64, 128};
+      tmA = make_tmap(d.A, 2, dims, str, box);
+    } else {      // A stored [K, M] with row stride lda
+      uint64_t dims[2] = {(uint64_t)d.M, (uint64_t)d.K_extent_a};
+      uint64_t str[1] = {(uint64_t)d.lda * 2};
+      uint32_t box[2] = {64, 64};
+      tmA = make_tmap(d.A, 2, dims, str, box);
+    }
+  }
+  {
+    if (!B_MN) {  // B stored [N, K] (per group when grouped-M)
+      if (MODE == GEMM_GROUPED_M) {
+        uint64_t dims[3] = {(uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.num_groups};
+        uint64_t str[2] = {(uint64_t)d.ldb * 2, (uint64_t)d.b_group_stride * 2};
+        uint32_t box[3] = {64, (uint32_t)BN, 1};
+        tmB = make_tmap(d.B, 3, dims, str, box);
+      } else {
+        uint64_t dims[2] = {(uint64_t)d.K_extent_b, (uint64_t)d.N};
+        uint64_t str[1] = {(uint64_t)d.ldb * 2};
+        uint32_t box[2] = {64, (uint32_t)BN};
+        tmB = make_tmap(d.B, 2, dims, str, box);
+      }
+    } else {      // B stored [K, N]
+      if (MODE == GEMM_GROUPED_M) {
+        uint64_t dims[3] = {(uint64_t)d.N, (uint64_t)d.K, (uint64_t)d.num_groups};
+        uint64_t str[2] = {(uint64_t)d.ldb * 2, (uint64_t)d.b_group_stride * 2};
+        uint32_t box[3] = {64, 64, 1};
+        tmB = make_tmap(d.B, 3, dims, str, box);
+      } else {
+        uint64_t dims[2] = {(uint64_t)d.N, (uint64_t)d.K_extent_b};
+        uint64_t str[1] = {(uint64_t)d.ldb * 2};
+        uint32_t box[2] = {64, 64};
+        tmB = make_tmap(d.B, 2, dims, str, box);
+      }
+    }
+  }
+  GemmArgs p;
+  p.M = d.M;
+  p.N = d.N;
+  p.K = d.K;
+  p.num_groups = d.num_groups;
+  p.group_offsets = d.group_offsets;
+  p.C = d.C;
+  p.ldc = d.ldc;
+  p.c_group_stride = d.c_group_stride;
+  p.R = d.R;
+  p.ldr = d.ldr;
+  p.H = d.H;
+  p.ldh = d.ldh;
+  p.alpha = d.alpha;
+  p.status = reinterpret_cast<StatusBlock*>(d.status);
+  int grid = num_sms();
+  if (MODE == GEMM_DENSE) {
+    const int tiles = ((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
+    grid = tiles < grid ? tiles : grid;
+  } else if (MODE == GEMM_GROUPED_K) {
+    const int tiles = d.num_groups * ((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
+    grid = tiles < grid ? tiles : grid;
+  } else if (d.max_rows_hint > 0) {
+    const int tiles = (d.max_rows_hint / kBM) * ((d.N + BN - 1) / BN);
+    grid = tiles < grid ? tiles : grid;
+  }
+  if (grid < 1) grid = 1;
+  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(tmA, tmB, p);
+}
+
+template <bool A_MN, bool B_MN, int EPI, int MODE>
+static void dispatch_bn(const GemmDesc& d, cudaStream_t s) {
+  if (d.block_n == 128)
+    launch_impl<128, A_MN, B_MN, EPI, MODE>(d, s);
+  else
+    launch_impl<256, A_MN, B_MN, EPI, MODE>(d, s);
+}
+
+// Epilogue / layout combinations that training actually uses; others are
+// rejected so the number of kernel instantiations stays small.
+template <bool A_MN, bool B_MN, int EPI, int MODE>
+constexpr bool combo_supported() {
+  if (EPI == EPI_SWIGLU) return !A_MN && !B_MN && MODE != GEMM_GROUPED_K;
+  if (EPI == EPI_SWIGLU_BWD) return !A_MN && B_MN && MODE != GEMM_GROUPED_K;
+  if (EPI == EPI_ADD_BF16) return !A_MN && MODE == GEMM_DENSE;
+  if (EPI == EPI_STORE_F32 || EPI == EPI_ACCUM_F32) return A_MN && B_MN;
+  return true;
+}
+
+template <bool A_MN, bool B_MN, int EPI, int MODE>
+static void dispatch_checked(const GemmDesc& d, cudaStream_t s) {
+  if constexpr (combo_supported<A_MN, B_MN, EPI, MODE>()) {
+    dispatch_bn<A_MN, B_MN, EPI, MODE>(d, s);
+  } else {
+    throw std::runtime_error("omnicoder gemm: unsupported epilogue/layout/mode combination");
+  }
+}
+
+template <bool A_MN, bool B_MN, int MODE>
+static void dispatch_epi(const GemmDesc& d, cudaStream_t s) {
+  switch (d.epilogue) {
+    case EPI_STORE_BF16: dispatch_checked<A_MN, B_MN, EPI_STORE_BF16, MODE>(d, s); break;
+    case EPI_STORE_F32: dispatch_checked<A_MN, B_MN, EPI_STORE_F32, MODE>(d, s); break;
+    case EPI_ACCUM_F32: dispatch_checked<A_MN, B_MN, EPI_ACCUM_F32, MODE>(d, s); break;
+    case EPI_ADD_BF16: dispatch_checked<A_MN, B_MN, EPI_ADD_BF16, MODE>(d, s); break;
+    case EPI_SWIGLU: dispatch_checked<A_MN, B_MN, EPI_SWIGLU, MODE>(d, s); break;
+    case EPI_SWIGLU_BWD: dispatch_checked<A_MN, B_MN, EPI_SWIGLU_BWD, MODE>(d, s); break;
+    default: throw std::runtime_error("omnicoder gemm: unknown epilogue");
+  }
+}
+
+void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream) {
+  if (d.num_groups > GEMM_MAX_GROUPS) throw std::runtime_error("omnicoder gemm: too many groups");
+  if (d.K % 8 != 0 && !(d.mode == GEMM_GROUPED_K)) throw std::runtime_error("omnicoder gemm: K must be a multiple of 8");
+  const int combo = (d.a_mn_major ? 2 : 0) | (d.b_mn_major ? 1 : 0);
+  switch (d.mode) {
+    case GEMM_DENSE:
+      if (combo == 0) dispatch_epi<false, false, GEMM_DENSE>(d, stream);
+      else if (combo == 1) dispatch_epi<false, true, GEMM_DENSE>(d, stream);
+      else if (combo == 3) dispatch_epi<true, true, GEMM_DENSE>(d, stream);
+      else throw std::runtime_error("omnicoder gemm: unsupported major combination");
+      break;
+    case GEMM_GROUPED_M:
+      if (combo == 0) dispatch_epi<false, false, GEMM_GROUPED_M>(d, stream);
+      else if (combo == 1) dispatch_epi<false, true, GEMM_GROUPED_M>(d, stream);
+      else throw std::runtime_error("omnicoder gemm: unsupported major combination (grouped-M)");
+      break;
+    case GEMM_GROUPED_K:
+      if (combo == 3) dispatch_epi<true, true, GEMM_GROUPED_K>(d, stream);
+      else throw std::runtime_error("omnicoder gemm: grouped-K needs MN-major A and B");
+      break;
+    default:
+      throw std::runtime_error("omnicoder gemm: unknown mode");
+  }
+}
+
+}  // namespace omni

@@ -1,0 +1,295 @@
+// Tensor-level bindings of the memory-bound, loss, optimiser and routing
+// kernels.  Shapes, dtypes and alignment are checked here; the kernels assume
+// them.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels.h"
+
+namespace omni {
+
+namespace {
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_bf16(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name,
+              " must be a contiguous CUDA bf16 tensor");
+}
+void check_f32(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), name,
+              " must be a contiguous CUDA fp32 tensor");
+}
+void check_i32(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous(), name,
+              " must be a contiguous CUDA int32 tensor");
+}
+template <typename T>
+T* opt_ptr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+}  // namespace
+
+// ---- norms -----------------------------------------------------------------
+std::vector<at::Tensor> rmsnorm_fwd_t(const at::Tensor& x, const c10::optional<at::Tensor>& res, const at::Tensor& w,
+                                      double eps) {
+  check_bf16(x, "x");
+  check_bf16(w, "w");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t dim = x.size(-1), rows = x.numel() / dim;
+  TORCH_CHECK(dim % 8 == 0 && w.numel() == dim, "rmsnorm: dim must be a multiple of 8 and match w");
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  at::Tensor h;
+  if (res.has_value()) {
+    check_bf16(*res, "res");
+    TORCH_CHECK(res->sizes() == x.sizes(), "rmsnorm: residual shape");
+    h = at::empty_like(x);
+  }
+  rmsnorm_fwd(x.data_ptr(), res.has_value() ? res->data_ptr() : nullptr, res.has_value() ? h.data_ptr() : nullptr,
+              w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), (int)rows, (int)dim, (float)eps, stream());
+  if (res.has_value()) return {y, rstd, h};
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> rmsnorm_bwd_t(const at::Tensor& x, const at::Tensor& w, const at::Tensor& rstd,
+                                      const at::Tensor& dy, const c10::optional<at::Tensor>& dres) {
+  check_bf16(x, "x");
+  check_bf16(dy, "dy");
+  check_f32(rstd, "rstd");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t dim = x.size(-1), rows = x.numel() / dim;
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({dim}, x.options().dtype(at::kFloat));
+  if (dres.has_value()) check_bf16(*dres, "dres");
+  rmsnorm_bwd(x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dy.data_ptr(), opt_ptr<void>(dres), dx.data_ptr(),
+              dw.data_ptr<float>(), (int)rows, (int)dim, stream());
+  return {dx, dw};
+}
+
+std::vector<at::Tensor> layernorm_fwd_t(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, double eps) {
+  check_bf16(x, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t dim = x.size(-1), rows = x.numel() / dim;
+  TORCH_CHECK(dim % 8 == 0, "layernorm: dim must be a multiple of 8");
+  auto y = at::empty_like(x);
+  auto mean = at::empty({rows}, x.options().dtype(at::kFloat));
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  layernorm_fwd(x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr(), mean.data_ptr<float>(),
+                rstd.data_ptr<float>(), (int)rows, (int)dim, (float)eps, stream());
+  return {y, mean, rstd};
+}
+
+std::vector<at::Tensor> layernorm_bwd_t(const at::Tensor& x, const at::Tensor& w, const at::Tensor& mean,
+                                        const at::Tensor& rstd, const at::Tensor& dy) {
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t dim = x.size(-1), rows = x.numel() / dim;
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({dim}, x.options().dtype(at::kFloat));
+  auto db = at::zeros({dim}, x.options().dtype(at::kFloat));
+  layernorm_bwd(x.data_ptr(), w.data_ptr(), mean.data_ptr<float>(), rstd.data_ptr<float>(), dy.data_ptr(),
+                dx.data_ptr(), dw.data_ptr<float>(), db.data_ptr<float>(), (int)rows, (int)dim, stream());
+  return {dx, dw, db};
+}
+
+// ---- rope (in place) ---------------------------------------------------------
+void rope_t(at::Tensor& x, const at::Tensor& cs, const c10::optional<at::Tensor>& pos, int64_t pos0, int64_t seq,
+            int64_t tokens, int64_t heads, int64_t row_stride, int64_t head_stride, int64_t off, int64_t rot,
+            bool interleaved, double sign) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, "rope: x must be CUDA bf16");
+  check_f32(cs, "cs");
+  TORCH_CHECK(cs.dim() == 3 && cs.size(0) == 2 && cs.size(2) == rot / 2, "rope: cs must be [2, max_pos, rot/2]");
+  const c10::cuda::CUDAGuard g(x.device());
+  if (pos.has_value()) check_i32(*pos, "pos");
+  rope_apply(x.data_ptr(), cs.data_ptr<float>(), (int)cs.size(1), opt_ptr<int>(pos), (int)pos0, (int)seq,
+             (int)tokens, (int)heads, row_stride, head_stride, (int)off, (int)rot, interleaved, (float)sign, stream());
+}
+
+// ---- embedding ---------------------------------------------------------------
+at::Tensor embedding_fwd_t(const at::Tensor& ids, const at::Tensor& w) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embedding: ids must be contiguous int64");
+  check_bf16(w, "w");
+  const c10::cuda::CUDAGuard g(w.device());
+  const int64_t dim = w.size(1);
+  TORCH_CHECK(dim % 8 == 0, "embedding: dim must be a multiple of 8");
+  auto sizes = ids.sizes().vec();
+  sizes.push_back(dim);
+  auto out = at::empty(sizes, w.options());
+  embedding_fwd(ids.data_ptr<int64_t>(), w.data_ptr(), out.data_ptr(), (int)ids.numel(), (int)dim, (int)w.size(0),
+                stream());
+  return out;
+}
+
+void embedding_bwd_t(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& dw) {
+  check_bf16(dout, "dout");
+  check_f32(dw, "dw");
+  const c10::cuda::CUDAGuard g(dw.device());
+  embedding_bwd(ids.data_ptr<int64_t>(), dout.data_ptr(), dw.data_ptr<float>(), (int)ids.numel(), (int)dw.size(1),
+                (int)dw.size(0), stream());
+}
+
+// ---- cross entropy -----------------------------------------------------------
+std::vector<at::Tensor> cross_entropy_t(const at::Tensor& logits, const at::Tensor& labels,
+                                        const c10::optional<at::Tensor>& dlogits, double grad_scale, double z_loss) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 &&
+                  logits.stride(1) == 1 && logits.stride(0) % 8 == 0,
+              "cross_entropy: logits must be 2-D bf16 with row stride multiple of 8");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() == logits.size(0),
+              "cross_entropy: labels must be int64 [rows]");
+  const c10::cuda::CUDAGuard g(logits.device());
+  const int64_t rows = logits.size(0);
+  auto loss = at::empty({rows}, logits.options().dtype(at::kFloat));
+  auto lse = at::empty({rows}, logits.options().dtype(at::kFloat));
+  void* d = nullptr;
+  if (dlogits.has_value()) {
+    TORCH_CHECK(dlogits->strides() == logits.strides() && dlogits->sizes() == logits.sizes(),
+                "cross_entropy: dlogits layout must match logits");
+    d = dlogits->data_ptr();
+  }
+  cross_entropy_fwd_bwd(logits.data_ptr(), logits.stride(0), labels.data_ptr<int64_t>(), loss.data_ptr<float>(),
+                        lse.data_ptr<float>(), d, (int)rows, (int)logits.size(1), (float)grad_scale, (float)z_loss,
+                        stream());
+  return {loss, lse};
+}
+
+// ---- optimiser ---------------------------------------------------------------
+void adamw_t(at::Tensor& p, at::Tensor& m, at::Tensor& v, const at::Tensor& g, const c10::optional<at::Tensor>& pb,
+             double lr, double b1, double b2, double eps, double wd, int64_t step, double grad_scale,
+             const c10::optional<at::Tensor>& norm_sq, double max_norm) {
+  check_f32(p, "p");
+  check_f32(m, "m");
+  check_f32(v, "v");
+  check_bf16(g, "g");
+  TORCH_CHECK(p.numel() == g.numel() && m.numel() == p.numel() && v.numel() == p.numel(), "adamw: sizes");
+  const c10::cuda::CUDAGuard gd(p.device());
+  const double bc1 = 1.0 - std::pow(b1, (double)step);
+  const double bc2 = 1.0 - std::pow(b2, (double)step);
+  if (pb.has_value()) check_bf16(*pb, "p_bf16");
+  adamw_step(p.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), g.data_ptr(), opt_ptr<void>(pb),
+             p.numel(), (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, (float)bc1, (float)bc2,
+             (float)grad_scale, opt_ptr<float>(norm_sq), (float)max_norm, stream());
+}
+
+void sq_norm_t(const at::Tensor& g, double scale, at::Tensor& out) {
+  check_bf16(g, "g");
+  check_f32(out, "out");
+  const c10::cuda::CUDAGuard gd(g.device());
+  sq_norm_accum(g.data_ptr(), g.numel(), (float)scale, out.data_ptr<float>(), stream());
+}
+
+// ---- MoE routing -------------------------------------------------------------
+std::vector<at::Tensor> router_topk_t(const at::Tensor& logits, int64_t k, bool renorm) {
+  check_f32(logits, "logits");
+  const c10::cuda::CUDAGuard g(logits.device());
+  const int64_t T = logits.size(0), E = logits.size(1);
+  TORCH_CHECK(E <= 256 && k <= 16 && k <= E, "router: E <= 256, k <= 16");
+  auto idx = at::empty({T, k}, logits.options().dtype(at::kInt));
+  auto w = at::empty({T, k}, logits.options());
+  auto probs = at::empty({T, E}, logits.options());
+  router_topk(logits.data_ptr<float>(), idx.data_ptr<int>(), w.data_ptr<float>(), probs.data_ptr<float>(), (int)T,
+              (int)E, (int)k, renorm, stream());
+  return {idx, w, probs};
+}
+
+// Returns counts[E], offsets[E+1], pos[T*K], src[cap_rows].
+std::vector<at::Tensor> moe_plan_t(const at::Tensor& idx, int64_t E, int64_t capacity, int64_t cap_rows) {
+  check_i32(idx, "idx");
+  const c10::cuda::CUDAGuard g(idx.device());
+  const int64_t T = idx.size(0), K = idx.size(1);
+  TORCH_CHECK(E <= 256, "moe_plan: E <= 256");
+  auto o = idx.options();
+  auto counts = at::empty({E}, o);
+  auto offsets = at::empty({E + 1}, o);
+  auto pos = at::empty({T, K}, o);
+  auto src = at::empty({cap_rows}, o);
+  const int64_t nblocks = (T * K + 1023) / 1024;
+  auto ws = at::empty({std::max<int64_t>(1, 2 * nblocks * E)}, o);
+  moe_permute_plan(idx.data_ptr<int>(), (int)T, (int)K, (int)E, (int)capacity, counts.data_ptr<int>(),
+                   offsets.data_ptr<int>(), pos.data_ptr<int>(), src.data_ptr<int>(), (int)cap_rows,
+                   ws.data_ptr<int>(), stream());
+  return {counts, offsets, pos, src};
+}
+
+void moe_gather_t(const at::Tensor& x, const at::Tensor& src, at::Tensor& x_perm, int64_t K, const at::Tensor& offsets) {
+  check_bf16(x, "x");
+  check_bf16(x_perm, "x_perm");
+  const c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.size(-1) % 8 == 0, "moe_gather: dim % 8");
+  moe_gather(x.data_ptr(), src.data_ptr<int>(), x_perm.data_ptr(), (int)x_perm.size(0), (int)K, (int)x.size(-1),
+             offsets.data_ptr<int>(), (int)offsets.numel() - 1, stream());
+}
+
+at::Tensor moe_combine_t(const at::Tensor& y_perm, const at::Tensor& pos, const at::Tensor& w,
+                         const c10::optional<at::Tensor>& add) {
+  check_bf16(y_perm, "y_perm");
+  check_f32(w, "w");
+  const c10::cuda::CUDAGuard g(y_perm.device());
+  const int64_t T = pos.size(0), K = pos.size(1), dim = y_perm.size(1);
+  auto out = at::empty({T, dim}, y_perm.options());
+  if (add.has_value()) check_bf16(*add, "add");
+  moe_combine(y_perm.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(), opt_ptr<void>(add), out.data_ptr(),
+              (int)T, (int)K, (int)dim, stream());
+  return out;
+}
+
+std::vector<at::Tensor> moe_combine_bwd_t(const at::Tensor& dout, const at::Tensor& y_perm, const at::Tensor& src,
+                                          const at::Tensor& w, const at::Tensor& offsets, int64_t K) {
+  check_bf16(dout, "dout");
+  const c10::cuda::CUDAGuard g(dout.device());
+  auto dy = at::empty_like(y_perm);
+  auto dw = at::zeros_like(w);
+  moe_combine_bwd(dout.data_ptr(), y_perm.data_ptr(), src.data_ptr<int>(), w.data_ptr<float>(), dy.data_ptr(),
+                  dw.data_ptr<float>(), (int)y_perm.size(0), (int)K, (int)y_perm.size(1), offsets.data_ptr<int>(),
+                  (int)offsets.numel() - 1, stream());
+  return {dy, dw};
+}
+
+at::Tensor moe_scatter_add_t(const at::Tensor& dx_perm, const at::Tensor& pos, const c10::optional<at::Tensor>& add) {
+  check_bf16(dx_perm, "dx_perm");
+  const c10::cuda::CUDAGuard g(dx_perm.device());
+  const int64_t T = pos.size(0), K = pos.size(1), dim = dx_perm.size(1);
+  auto dx = at::empty({T, dim}, dx_perm.options());
+  moe_scatter_add(dx_perm.data_ptr(), pos.data_ptr<int>(), opt_ptr<void>(add), dx.data_ptr(), (int)T, (int)K,
+                  (int)dim, stream());
+  return dx;
+}
+
+std::vector<at::Tensor> router_bwd_t(const at::Tensor& logits, const at::Tensor& probs, const at::Tensor& idx,
+                                     const at::Tensor& dw, const at::Tensor& counts, bool renorm, double aux_alpha,
+                                     double z_beta) {
+  const c10::cuda::CUDAGuard g(logits.device());
+  const int64_t T = logits.size(0), E = logits.size(1), K = idx.size(1);
+  auto dlogits = at::empty({T, E}, logits.options().dtype(at::kBFloat16));
+  auto aux = at::zeros({2}, logits.options());
+  router_bwd(logits.data_ptr<float>(), probs.data_ptr<float>(), idx.data_ptr<int>(), dw.data_ptr<float>(),
+             counts.data_ptr<int>(), dlogits.data_ptr(), (int)T, (int)E, (int)K, renorm, (float)aux_alpha,
+             (float)z_beta, aux.data_ptr<float>(), stream());
+  return {dlogits, aux};
+}
+
+void register_kernels(pybind11::module_& m) {
+  m.def("rmsnorm_fwd", &rmsnorm_fwd_t, py::arg("x"), py::arg("res"), py::arg("w"), py::arg("eps"));
+  m.def("rmsnorm_bwd", &rmsnorm_bwd_t, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dres"));
+  m.def("layernorm_fwd", &layernorm_fwd_t);
+  m.def("layernorm_bwd", &layernorm_bwd_t);
+  m.def("rope", &rope_t, py::arg("x"), py::arg("cs"), py::arg("pos"), py::arg("pos0"), py::arg("seq"),
+        py::arg("tokens"), py::arg("heads"), py::arg("row_stride"), py::arg("head_stride"), py::arg("off"),
+        py::arg("rot"), py::arg("interleaved"), py::arg("sign"));
+  m.def("embedding_fwd", &embedding_fwd_t);
+  m.def("embedding_bwd", &embedding_bwd_t);
+  m.def("cross_entropy", &cross_entropy_t, py::arg("logits"), py::arg("labels"), py::arg("dlogits"),
+        py::arg("grad_scale"), py::arg("z_loss"));
+  m.def("adamw", &adamw_t, py::arg("p"), py::arg("m"), py::arg("v"), py::arg("g"), py::arg("p_bf16"), py::arg("lr"),
+        py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"), py::arg("grad_scale"),
+        py::arg("norm_sq"), py::arg("max_norm"));
+  m.def("sq_norm", &sq_norm_t);
+  m.def("router_topk", &router_topk_t);
+  m.def("moe_plan", &moe_plan_t);
+  m.def("moe_gather", &moe_gather_t);
+  m.def("moe_combine", &moe_combine_t);
+  m.def("moe_combine_bwd", &moe_combine_bwd_t);
+  m.def("moe_scatter_add", &moe_scatter_add_t);
+  m.def("router_bwd", &router_bwd_t);
+}
+
+}  // namespace omni

@@ -1,0 +1,152 @@
+"""tcgen05 GEMM numerics against a plain fp32 PyTorch matmul of the same bf16 inputs."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+EPI_BF16, EPI_F32, EPI_ACC, EPI_ADD, EPI_SWIGLU, EPI_SWIGLU_BWD = range(6)
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-6)).item()
+
+
+def _mk(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 256), (300, 520, 200), (1024, 768, 1408), (64, 32, 32)])
+@pytest.mark.parametrize("block_n", [128, 256])
+def test_dense_kk(cuda_ext, M, N, K, block_n):
+    torch.manual_seed(0)
+    A, B = _mk(M, K), _mk(N, K)
+    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(A, B, C, False, False, EPI_BF16, 1.0, None, None, block_n)
+    ref = A.float() @ B.float().T
+    assert _rel(C, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 384), (200, 136, 128), (512, 2048, 1408)])
+def test_dense_k_mn(cuda_ext, M, N, K):
+    # dX = dY @ W  with W stored [K_red, N]
+    torch.manual_seed(1)
+    A, B = _mk(M, K), _mk(K, N)
+    C = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(A, B, C, False, True, EPI_BF16, 1.0, None, None, 256)
+    ref = A.float() @ B.float()
+    assert _rel(C, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 384), (192, 320, 1000), (2048, 1408, 512)])
+def test_dense_mn_mn(cuda_ext, M, N, K):
+    # dW = dY^T X with dY [K_red, M], X [K_red, N]
+    torch.manual_seed(2)
+    A, B = _mk(K, M), _mk(K, N)
+    C = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    cuda_ext.gemm(A, B, C, True, True, EPI_F32, 0.5, None, None, 256)
+    ref = 0.5 * (A.float().T @ B.float())
+    assert _rel(C, ref) < 2e-3
+    C2 = C.clone()
+    cuda_ext.gemm(A, B, C2, True, True, EPI_ACC, 1.0, None, None, 128)
+    assert _rel(C2, C + ref / 0.5) < 2e-3
+    Cb = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(A, B, Cb, True, True, EPI_BF16, 1.0, None, None, 256)
+    assert _rel(Cb, ref / 0.5) < 1e-2
+
+
+def test_dense_add_residual(cuda_ext):
+    torch.manual_seed(3)
+    A, B, R = _mk(384, 512), _mk(256, 512), _mk(384, 256)
+    C = torch.empty(384, 256, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(A, B, C, False, False, EPI_ADD, 1.0, R, None, 256)
+    ref = A.float() @ B.float().T + R.float()
+    assert _rel(C, ref) < 1e-2
+    # in place: C = acc + C
+    C2 = R.clone()
+    cuda_ext.gemm(A, B, C2, False, False, EPI_ADD, 1.0, C2, None, 256)
+    assert _rel(C2, ref) < 1e-2
+
+
+def _interleave(w1, w3, blk=32):
+    F, D = w1.shape
+    return torch.stack([w1.view(F // blk, blk, D), w3.view(F // blk, blk, D)], 1).reshape(2 * F, D)
+
+
+def test_dense_swiglu_fwd_bwd(cuda_ext):
+    torch.manual_seed(4)
+    T, D, F = 256, 512, 384
+    x = _mk(T, D)
+    w1, w3 = _mk(F, D, scale=0.05), _mk(F, D, scale=0.05)
+    w13 = _interleave(w1, w3)
+    act = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    H = torch.empty(T, 2 * F, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(x, w13, act, False, False, EPI_SWIGLU, 1.0, None, H, 256)
+    g = x.float() @ w1.float().T
+    u = x.float() @ w3.float().T
+    ref = torch.nn.functional.silu(g) * u
+    assert _rel(act, ref) < 2e-2
+    assert _rel(H, x.float() @ w13.float().T) < 1e-2
+    # backward: dAct = dY @ W2 ; dH = swiglu'(H) * dAct
+    w2 = _mk(D, F, scale=0.05)
+    dy = _mk(T, D)
+    dH = torch.empty(T, 2 * F, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(dy, w2, dH, False, True, EPI_SWIGLU_BWD, 1.0, H, None, 256)
+    da = dy.float() @ w2.float()
+    Hf = H.float().view(T, F // 32, 2, 32)
+    gg, uu = Hf[:, :, 0].reshape(T, F), Hf[:, :, 1].reshape(T, F)
+    sg = torch.sigmoid(gg)
+    dg = da * uu * sg * (1 + gg * (1 - sg))
+    du = da * gg * sg
+    ref_dh = torch.stack([dg.view(T, F // 32, 32), du.view(T, F // 32, 32)], 2).reshape(T, 2 * F)
+    assert _rel(dH, ref_dh) < 2e-2
+
+
+def _offsets(counts):
+    pad = [(c + 127) // 128 * 128 for c in counts]
+    off = [0]
+    for p in pad:
+        off.append(off[-1] + p)
+    return off
+
+
+@pytest.mark.parametrize("b_mn", [False, True])
+def test_grouped_m(cuda_ext, b_mn):
+    torch.manual_seed(5)
+    G, N, K = 5, 384, 256
+    counts = [130, 0, 7, 256, 300]
+    off = _offsets(counts)
+    rows = off[-1] + 128
+    A = torch.zeros(rows, K, device="cuda", dtype=torch.bfloat16)
+    for g in range(G):
+        A[off[g]:off[g] + counts[g]] = _mk(counts[g], K)
+    B = _mk(G, K, N) if b_mn else _mk(G, N, K)
+    offs = torch.tensor(off, device="cuda", dtype=torch.int32)
+    C = torch.full((rows, N), 7.0, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm_grouped_m(A, B, offs, C, b_mn, EPI_BF16, 1.0, None, None, 256, rows)
+    for g in range(G):
+        Bg = B[g].float() if b_mn else B[g].float().T
+        ref = A[off[g]:off[g + 1]].float() @ Bg
+        if off[g + 1] > off[g]:
+            assert _rel(C[off[g]:off[g + 1]], ref) < 1e-2, g
+
+
+def test_grouped_k(cuda_ext):
+    torch.manual_seed(6)
+    G, M, N = 4, 256, 384
+    counts = [128, 0, 250, 513]
+    off = _offsets(counts)
+    rows = off[-1]
+    A = torch.zeros(rows, M, device="cuda", dtype=torch.bfloat16)
+    B = torch.zeros(rows, N, device="cuda", dtype=torch.bfloat16)
+    for g in range(G):
+        A[off[g]:off[g] + counts[g]] = _mk(counts[g], M)
+        B[off[g]:off[g] + counts[g]] = _mk(counts[g], N)
+    offs = torch.tensor(off, device="cuda", dtype=torch.int32)
+    C = torch.full((G, M, N), 3.0, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm_grouped_k(A, B, offs, C, EPI_BF16, 1.0, 256)
+    for g in range(G):
+        ref = A[off[g]:off[g + 1]].float().T @ B[off[g]:off[g + 1]].float()
+        if counts[g] == 0:
+            assert C[g].abs().max().item() == 0.0
+        else:
+            assert _rel(C[g], ref) < 1e-2, g
