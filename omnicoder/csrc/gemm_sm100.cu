@@ -623,7 +623,8 @@ constexpr bool combo_supported() {
   if (EPI == EPI_SWIGLU) return !A_MN && !B_MN && MODE != GEMM_GROUPED_K;
   if (EPI == EPI_SWIGLU_BWD) return !A_MN && B_MN && MODE != GEMM_GROUPED_K;
   if (EPI == EPI_ADD_BF16) return !A_MN && MODE == GEMM_DENSE;
-  if (EPI == EPI_STORE_F32 || EPI == EPI_ACCUM_F32) return A_MN && B_MN;
+  if (EPI == EPI_STORE_F32) return (A_MN && B_MN) || (!A_MN && !B_MN && MODE == GEMM_DENSE);
+  if (EPI == EPI_ACCUM_F32) return A_MN && B_MN;
   return true;
 }
 

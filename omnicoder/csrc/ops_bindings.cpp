@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "attention.h"
 #include "kernels.h"
 
 namespace omni {
@@ -267,6 +268,71 @@ std::vector<at::Tensor> router_bwd_t(const at::Tensor& logits, const at::Tensor&
   return {dlogits, aux};
 }
 
+
+// ---- attention -----------------------------------------------------------------
+namespace {
+AttnTensors attn_desc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                      const c10::optional<at::Tensor>& kr, int64_t seq, bool causal, int64_t window, double scale) {
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "attention: q/k/v must be [T, heads, dim]");
+  for (const at::Tensor* t : {&q, &k, &v}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->stride(2) == 1,
+                "attention: q/k/v must be CUDA bf16 with a contiguous last dim");
+  }
+  AttnTensors a{};
+  a.q = q.data_ptr(); a.q_row = q.stride(0); a.q_head = q.stride(1);
+  a.k = k.data_ptr(); a.k_row = k.stride(0); a.k_head = k.stride(1);
+  a.v = v.data_ptr(); a.v_row = v.stride(0); a.v_head = v.stride(1);
+  a.T = (int)q.size(0); a.S = (int)seq; a.H = (int)q.size(1); a.Hk = (int)k.size(1);
+  a.DQ = (int)q.size(2); a.DV = (int)v.size(2);
+  a.DR = 0;
+  if (kr.has_value()) {
+    TORCH_CHECK(kr->dim() == 2 && kr->stride(1) == 1 && kr->scalar_type() == at::kBFloat16, "attention: k_rope [T, 64]");
+    a.kr = kr->data_ptr(); a.kr_row = kr->stride(0); a.DR = (int)kr->size(1);
+  }
+  TORCH_CHECK(a.DQ == k.size(2) + a.DR, "attention: q dim must equal k dim (+ rope dim)");
+  TORCH_CHECK(v.size(1) == k.size(1) && k.size(0) == q.size(0), "attention: k/v heads or tokens differ");
+  a.causal = causal ? 1 : 0; a.window = (int)window; a.scale = (float)scale;
+  return a;
+}
+}  // namespace
+
+std::vector<at::Tensor> attn_fwd_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                   const c10::optional<at::Tensor>& kr, int64_t seq, bool causal, int64_t window,
+                                   double scale) {
+  const c10::cuda::CUDAGuard g(q.device());
+  AttnTensors a = attn_desc(q, k, v, kr, seq, causal, window, scale);
+  auto o = at::empty({q.size(0), q.size(1), v.size(2)}, q.options());
+  auto lse = at::empty({q.size(1), q.size(0)}, q.options().dtype(at::kFloat));
+  attention_fwd(a, o.data_ptr(), lse.data_ptr<float>(), status_ptr(), stream());
+  return {o, lse};
+}
+
+// Returns [dq, dk, dv] (+ dk_rope summed over heads).  Optional output buffers
+// (which may be strided views into one gradient tensor) avoid extra copies.
+std::vector<at::Tensor> attn_bwd_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                   const c10::optional<at::Tensor>& kr, const at::Tensor& o, const at::Tensor& lse,
+                                   const at::Tensor& dO, int64_t seq, bool causal, int64_t window, double scale,
+                                   const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
+                                   const c10::optional<at::Tensor>& dv_out) {
+  const c10::cuda::CUDAGuard g(q.device());
+  AttnTensors a = attn_desc(q, k, v, kr, seq, causal, window, scale);
+  TORCH_CHECK(dO.is_contiguous() && o.is_contiguous(), "attention bwd: o and dO must be contiguous");
+  auto dq = dq_out.has_value() ? *dq_out : at::empty(q.sizes(), q.options());
+  auto dk = dk_out.has_value() ? *dk_out : at::empty(k.sizes(), k.options());
+  auto dv = dv_out.has_value() ? *dv_out : at::empty(v.sizes(), v.options());
+  TORCH_CHECK(dq.stride(2) == 1 && dk.stride(2) == 1 && dv.stride(2) == 1, "attention bwd: outputs need unit last stride");
+  at::Tensor dkr_heads;
+  if (kr.has_value()) dkr_heads = at::empty({q.size(0), k.size(1), kr->size(1)}, q.options());
+  auto delta = at::empty({q.size(1), q.size(0)}, q.options().dtype(at::kFloat));
+  attention_bwd(a, o.data_ptr(), lse.data_ptr<float>(), dO.data_ptr(), delta.data_ptr<float>(), dq.data_ptr(),
+                dq.stride(0), dq.stride(1), dk.data_ptr(), dk.stride(0), dk.stride(1),
+                kr.has_value() ? dkr_heads.data_ptr() : nullptr, kr.has_value() ? dkr_heads.stride(0) : 0,
+                kr.has_value() ? dkr_heads.stride(1) : 0, dv.data_ptr(), dv.stride(0), dv.stride(1), status_ptr(),
+                stream());
+  if (kr.has_value()) return {dq, dk, dv, dkr_heads.sum(1)};
+  return {dq, dk, dv};
+}
+
 void register_kernels(pybind11::module_& m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd_t, py::arg("x"), py::arg("res"), py::arg("w"), py::arg("eps"));
   m.def("rmsnorm_bwd", &rmsnorm_bwd_t, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dres"));
@@ -290,6 +356,11 @@ void register_kernels(pybind11::module_& m) {
   m.def("moe_combine_bwd", &moe_combine_bwd_t);
   m.def("moe_scatter_add", &moe_scatter_add_t);
   m.def("router_bwd", &router_bwd_t);
+  m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_rope"), py::arg("seq"),
+        py::arg("causal"), py::arg("window"), py::arg("scale"));
+  m.def("attn_bwd", &attn_bwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_rope"), py::arg("o"),
+        py::arg("lse"), py::arg("dO"), py::arg("seq"), py::arg("causal"), py::arg("window"), py::arg("scale"),
+        py::arg("dq_out") = py::none(), py::arg("dk_out") = py::none(), py::arg("dv_out") = py::none());
 }
 
 }  // namespace omni

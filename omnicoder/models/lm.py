@@ -1,0 +1,282 @@
+"""Decoder-only LM of the spec family: RMSNorm, RoPE, MHA / GQA / MLA attention,
+dense SwiGLU or routed-expert (+ shared expert) SwiGLU FFN, tied or untied
+embeddings, optional multi-token-prediction and verifier heads.
+
+What it replaces in the reference: OmniTransformer (src/omnicoder/modeling/
+transformer_moe.py:1016) with LatentKVAttention (attention.py:349), MoELayer
+(moe_layer.py:36) and the MTP/verifier heads (transformer_moe.py:1253-1399).
+That model's quirks (128-token truncation, detached experts, 16-slot decode
+window, LayerNorm/GELU experts) live in :mod:`omnicoder.models.compat`; this
+family computes exact causal attention, routes with gradients and scales to
+the long-context configs.
+
+Layout notes (kernel-driven, converted by :meth:`OmniLM.export_state_dict`):
+  * SwiGLU gate/up weights are one [2F, D] (or [E, 2F, D]) tensor with gate and
+    up rows interleaved in blocks of 32 (the fused GEMM epilogue consumes pairs
+    of 32-column accumulator chunks).
+  * Residual adds are fused into the output-projection / down-projection GEMM
+    epilogues: blocks take and return the residual stream.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from ..config import ModelConfig
+from ..ops import (RopeTable, apply_rope, attention, embedding, layer_norm, linear, lm_head_cross_entropy, moe_ffn,
+                   rms_norm, swiglu_mlp)
+from ..ops.gemm import interleave_gate_up, split_gate_up
+
+
+# device/dtype that parameters are created with (set by build_model)
+_FACTORY: dict = {"device": "cpu", "dtype": torch.float32}
+
+
+def _empty(*shape) -> torch.Tensor:
+    return torch.empty(*shape, **_FACTORY)
+
+
+def _ones(n: int) -> nn.Parameter:
+    return nn.Parameter(torch.ones(n, **_FACTORY))
+
+
+def _init(t: torch.Tensor, std: float) -> nn.Parameter:
+    with torch.no_grad():
+        t.normal_(0.0, std)
+    return nn.Parameter(t)
+
+
+class Norm(nn.Module):
+    def __init__(self, dim: int, kind: str, eps: float):
+        super().__init__()
+        self.kind, self.eps = kind, eps
+        self.weight = _ones(dim)
+        self.bias = nn.Parameter(torch.zeros(dim, **_FACTORY)) if kind == "layernorm" else None
+
+    def forward(self, x):
+        if self.kind == "layernorm":
+            return layer_norm(x, self.weight, self.bias, self.eps)
+        return rms_norm(x, self.weight, self.eps)
+
+
+class GQAttention(nn.Module):
+    """MHA (n_kv_heads == n_heads) or GQA with a fused QKV projection."""
+
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        self.cfg = cfg
+        D, H, Hk, hd = cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
+        self.H, self.Hk, self.hd = H, Hk, hd
+        self.wqkv = _init(_empty((H + 2 * Hk) * hd, D), cfg.init_std)
+        self.wo = _init(_empty(D, H * hd), cfg.init_std)
+
+    def qkv(self, y, rope: RopeTable, positions):
+        T = y.shape[0]
+        qkv = linear(y, self.wqkv).view(T, self.H + 2 * self.Hk, self.hd)
+        qkv = apply_rope(qkv, rope, positions, heads=self.H + self.Hk, interleaved=self.cfg.attn.rope_interleaved)
+        q = qkv[:, :self.H]
+        k = qkv[:, self.H:self.H + self.Hk]
+        v = qkv[:, self.H + self.Hk:]
+        return q, k, v, None
+
+    def forward(self, y, h, rope, positions, seq):
+        q, k, v, kr = self.qkv(y, rope, positions)
+        o = attention(q, k, v, kr, seq=seq, causal=True, window=self.cfg.attn.window)
+        return linear(o.reshape(y.shape[0], -1), self.wo, residual=h)
+
+
+class MLAttention(nn.Module):
+    """Multi-head latent attention: keys/values come from a low-rank latent
+    (kv_lora_rank) plus a shared rope key of qk_rope_dim."""
+
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        a = cfg.attn
+        self.cfg = cfg
+        D, H = cfg.d_model, cfg.n_heads
+        self.H, self.dn, self.dr, self.dv, self.r = H, a.qk_nope_dim, a.qk_rope_dim, a.v_head_dim, a.kv_lora_rank
+        self.wq = _init(_empty(H * (self.dn + self.dr), D), cfg.init_std)
+        self.wkv_a = _init(_empty(self.r + self.dr, D), cfg.init_std)
+        self.kv_norm = _ones(self.r)
+        self.wkv_b = _init(_empty(H * (self.dn + self.dv), self.r), cfg.init_std)
+        self.wo = _init(_empty(D, H * self.dv), cfg.init_std)
+
+    def latent(self, y, rope: RopeTable, positions):
+        """Compressed KV of the tokens: (normalised latent c [T, r], rotated rope key [T, dr])."""
+        T = y.shape[0]
+        kva = linear(y, self.wkv_a)
+        c = rms_norm(kva[:, :self.r].contiguous(), self.kv_norm, self.cfg.norm_eps)
+        kr = kva[:, self.r:].contiguous().view(T, 1, self.dr)
+        kr = apply_rope(kr, rope, positions, interleaved=self.cfg.attn.rope_interleaved).view(T, self.dr)
+        return c, kr
+
+    def qkv(self, y, rope: RopeTable, positions):
+        T = y.shape[0]
+        q = linear(y, self.wq).view(T, self.H, self.dn + self.dr)
+        q = apply_rope(q, rope, positions, off=self.dn, interleaved=self.cfg.attn.rope_interleaved)
+        c, kr = self.latent(y, rope, positions)
+        kv = linear(c, self.wkv_b).view(T, self.H, self.dn + self.dv)
+        return q, kv[:, :, :self.dn], kv[:, :, self.dn:], kr
+
+    def forward(self, y, h, rope, positions, seq):
+        q, k, v, kr = self.qkv(y, rope, positions)
+        o = attention(q, k, v, kr, seq=seq, causal=True, window=self.cfg.attn.window,
+                      scale=1.0 / math.sqrt(self.dn + self.dr))
+        return linear(o.reshape(y.shape[0], -1), self.wo, residual=h)
+
+
+class DenseFFN(nn.Module):
+    def __init__(self, D: int, F: int, std: float):
+        super().__init__()
+        self.w13 = _init(_empty(2 * F, D), std)
+        self.w2 = _init(_empty(D, F), std)
+
+    def forward(self, y, h):
+        return swiglu_mlp(y, self.w13, self.w2, residual=h), None
+
+
+class MoEFFN(nn.Module):
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        m = cfg.moe
+        D = cfg.d_model
+        self.cfg = cfg
+        self.router = _init(_empty(m.n_experts, D), cfg.init_std)
+        self.w13 = _init(_empty(m.n_experts, 2 * m.ffn_dim, D), cfg.init_std)
+        self.w2 = _init(_empty(m.n_experts, D, m.ffn_dim), cfg.init_std)
+        self.shared = DenseFFN(D, m.ffn_dim * m.n_shared_experts, cfg.init_std) if m.n_shared_experts > 0 else None
+        self.aux_grad_scale = 1.0
+
+    def forward(self, y, h):
+        m = self.cfg.moe
+        T = y.shape[0]
+        base = self.shared(y, h)[0] if self.shared is not None else h
+        out, aux = moe_ffn(y, self.router, self.w13, self.w2, m.top_k, m.capacity(T), m.renorm_topk,
+                           m.aux_loss_alpha, m.z_loss_beta, add=base, aux_grad_scale=self.aux_grad_scale)
+        return out, aux
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: ModelConfig, layer: int):
+        super().__init__()
+        self.attn_norm = Norm(cfg.d_model, cfg.norm, cfg.norm_eps)
+        self.attn = MLAttention(cfg) if cfg.attn.kind == "mla" else GQAttention(cfg)
+        self.ffn_norm = Norm(cfg.d_model, cfg.norm, cfg.norm_eps)
+        self.ffn = MoEFFN(cfg) if cfg.is_moe_layer(layer) else DenseFFN(cfg.d_model, cfg.ffn_dim, cfg.init_std)
+
+    def forward(self, h, rope, positions, seq):
+        h = self.attn(self.attn_norm(h), h, rope, positions, seq)
+        return self.ffn(self.ffn_norm(h), h)
+
+
+class OmniLM(nn.Module):
+    """The spec-family language model.  `forward(ids, labels)` returns a dict with
+    `loss` (CE + auxiliary), `ce`, `aux` and, without labels, `logits` of the last
+    position (or all positions with `all_logits=True`)."""
+
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        self.cfg = cfg
+        D, V = cfg.d_model, cfg.vocab_size
+        self.embed = _init(_empty(V, D), cfg.init_std)
+        self.blocks = nn.ModuleList([Block(cfg, i) for i in range(cfg.n_layers)])
+        self.norm_f = Norm(D, cfg.norm, cfg.norm_eps)
+        self.lm_head = None if cfg.tie_embeddings else _init(_empty(V, D), cfg.init_std)
+        self.mtp_heads = nn.ParameterList([_init(_empty(V, D), cfg.init_std) for _ in range(cfg.mtp_heads)])
+        self.verifier = _init(_empty(V, D), cfg.init_std) if cfg.verifier_head else None
+        rot = cfg.attn.qk_rope_dim if cfg.attn.kind == "mla" else cfg.head_dim
+        self.rope = RopeTable(rot, cfg.max_seq_len, cfg.attn.rope_theta, cfg.attn.rope_scale)
+
+    # ------------------------------------------------------------------
+    @property
+    def head_weight(self) -> torch.Tensor:
+        return self.embed if self.lm_head is None else self.lm_head
+
+    def set_aux_grad_scale(self, s: float):
+        for b in self.blocks:
+            if isinstance(b.ffn, MoEFFN):
+                b.ffn.aux_grad_scale = s
+
+    def hidden(self, ids: torch.Tensor, positions: torch.Tensor | None = None):
+        """Final normalised hidden states [B*S, D] and the summed auxiliary loss."""
+        B, S = ids.shape
+        if ids.is_cuda:
+            self.rope.to(ids.device)
+        h = embedding(ids.reshape(-1), self.embed)
+        if positions is None:
+            positions = torch.arange(S, device=ids.device).repeat(B)
+        aux_total = None
+        for blk in self.blocks:
+            h, aux = blk(h, self.rope, positions, S)
+            if aux is not None:
+                aux_total = aux if aux_total is None else aux_total + aux
+        return self.norm_f(h), aux_total
+
+    def forward(self, ids: torch.Tensor, labels: torch.Tensor | None = None, all_logits: bool = False,
+                assume_all_valid: bool = False):
+        y, aux = self.hidden(ids)
+        out = {}
+        if labels is not None:
+            ce = lm_head_cross_entropy(y, self.head_weight, labels, assume_all_valid=assume_all_valid)
+            loss = ce
+            if self.cfg.mtp_heads > 0:
+                B, S = ids.shape
+                for j, w in enumerate(self.mtp_heads):
+                    shift = j + 1
+                    lab = torch.full_like(labels, -100)
+                    lab[:, :S - shift] = labels[:, shift:]
+                    loss = loss + 0.5 * lm_head_cross_entropy(y, w, lab)
+            out["ce"] = ce
+            out["aux"] = aux if aux is not None else torch.zeros((), device=ids.device)
+            out["loss"] = loss + (aux if aux is not None else 0.0)
+        else:
+            B, S = ids.shape
+            yy = y if all_logits else y.view(B, S, -1)[:, -1]
+            out["logits"] = linear(yy, self.head_weight).float().view(B, S if all_logits else 1, -1)
+        return out
+
+    # ------------------------------------------------------------------
+    def export_state_dict(self) -> dict[str, torch.Tensor]:
+        """state_dict with SwiGLU gate/up split into separate `w1`/`w3` tensors."""
+        sd = {}
+        for k, v in self.state_dict().items():
+            if k.endswith(".w13"):
+                w1, w3 = split_gate_up(v)
+                sd[k[:-4] + ".w1"] = w1
+                sd[k[:-4] + ".w3"] = w3
+            else:
+                sd[k] = v
+        return sd
+
+    def load_export_state_dict(self, sd: dict[str, torch.Tensor], strict: bool = True):
+        merged = {}
+        for k, v in sd.items():
+            if k.endswith(".w1"):
+                merged[k[:-3] + ".w13"] = interleave_gate_up(v, sd[k[:-3] + ".w3"])
+            elif k.endswith(".w3"):
+                continue
+            else:
+                merged[k] = v
+        return self.load_state_dict(merged, strict=strict)
+
+
+def build_model(cfg: ModelConfig, device="cpu", dtype=None, seed: int | None = 0) -> OmniLM:
+    """Random-init model N(0, init_std) created directly on `device` (bf16 on CUDA,
+    fp32 on CPU by default)."""
+    global _FACTORY
+    if seed is not None:
+        torch.manual_seed(seed)
+        if str(device).startswith("cuda"):
+            torch.cuda.manual_seed(seed)
+    if dtype is None:
+        dtype = torch.bfloat16 if str(device).startswith("cuda") else torch.float32
+    old = _FACTORY
+    _FACTORY = {"device": torch.device(device), "dtype": dtype}
+    try:
+        m = OmniLM(cfg)
+    finally:
+        _FACTORY = old
+    m.rope.to(device)
+    return m

@@ -1,0 +1,103 @@
+"""Tensor-level wrappers of the tcgen05 GEMM.
+
+Conventions (all bf16, fp32 accumulation):
+  ``mm_nt(a, b)``  = a @ b.T   a [M,K], b [N,K]     (forward of a linear layer)
+  ``mm_nn(a, b)``  = a @ b     a [M,K], b [K,N]     (input gradient)
+  ``mm_tn(a, b)``  = a.T @ b   a [K,M], b [K,N]     (weight gradient)
+On CPU the same functions run torch.matmul; that path is the fp32 oracle.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+
+EPI_BF16, EPI_F32, EPI_ACC_F32, EPI_ADD, EPI_SWIGLU, EPI_SWIGLU_BWD = range(6)
+
+
+def _c2d(t: torch.Tensor) -> torch.Tensor:
+    return t if (t.dim() == 2 and t.stride(-1) == 1) else t.reshape(-1, t.shape[-1]).contiguous()
+
+
+def mm_nt(a: torch.Tensor, b: torch.Tensor, residual: torch.Tensor | None = None, out_f32: bool = False,
+          out: torch.Tensor | None = None) -> torch.Tensor:
+    if not _ext.use_cuda(a):
+        y = a @ b.t()
+        if residual is not None:
+            y = y + residual
+        return y.float() if out_f32 else y
+    C = _ext.load()
+    a = _c2d(a)
+    b = b.contiguous()
+    M, N = a.shape[0], b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, device=a.device, dtype=torch.float32 if out_f32 else torch.bfloat16)
+    if residual is not None:
+        C.gemm(a, b, out, False, False, EPI_ADD, 1.0, _c2d(residual), None, 256)
+    else:
+        C.gemm(a, b, out, False, False, EPI_F32 if out_f32 else EPI_BF16, 1.0, None, None, 256)
+    return out
+
+
+def mm_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    if not _ext.use_cuda(a):
+        return a @ b
+    C = _ext.load()
+    a = _c2d(a)
+    b = b.contiguous()
+    out = torch.empty(a.shape[0], b.shape[1], device=a.device, dtype=torch.bfloat16)
+    C.gemm(a, b, out, False, True, EPI_BF16, 1.0, None, None, 256)
+    return out
+
+
+def mm_tn(a: torch.Tensor, b: torch.Tensor, out_f32: bool = False, accumulate_into: torch.Tensor | None = None
+          ) -> torch.Tensor:
+    if not _ext.use_cuda(a):
+        y = a.t() @ b
+        if accumulate_into is not None:
+            accumulate_into += y
+            return accumulate_into
+        return y.float() if out_f32 else y
+    C = _ext.load()
+    a = _c2d(a)
+    b = _c2d(b)
+    if accumulate_into is not None:
+        C.gemm(a, b, accumulate_into, True, True, EPI_ACC_F32, 1.0, None, None, 256)
+        return accumulate_into
+    out = torch.empty(a.shape[1], b.shape[1], device=a.device, dtype=torch.float32 if out_f32 else torch.bfloat16)
+    C.gemm(a, b, out, True, True, EPI_F32 if out_f32 else EPI_BF16, 1.0, None, None, 256)
+    return out
+
+
+def interleave_gate_up(w1: torch.Tensor, w3: torch.Tensor, block: int = 32) -> torch.Tensor:
+    """Stack gate (w1) and up (w3) rows interleaved in blocks of `block` rows:
+    [w1[0:32], w3[0:32], w1[32:64], w3[32:64], ...].  Works on [F, D] or [E, F, D]."""
+    F = w1.shape[-2]
+    assert F % block == 0, "ffn dim must be a multiple of 32"
+    lead = w1.shape[:-2]
+    a = w1.reshape(*lead, F // block, 1, block, w1.shape[-1])
+    b = w3.reshape(*lead, F // block, 1, block, w3.shape[-1])
+    return torch.cat([a, b], dim=-3).reshape(*lead, 2 * F, w1.shape[-1])
+
+
+def split_gate_up(w13: torch.Tensor, block: int = 32) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of :func:`interleave_gate_up`."""
+    F2 = w13.shape[-2]
+    lead = w13.shape[:-2]
+    v = w13.reshape(*lead, F2 // (2 * block), 2, block, w13.shape[-1])
+    return (v[..., 0, :, :].reshape(*lead, F2 // 2, w13.shape[-1]),
+            v[..., 1, :, :].reshape(*lead, F2 // 2, w13.shape[-1]))
+
+
+def deinterleave_cols(h: torch.Tensor, block: int = 32) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split an activation laid out [g(32) u(32) g(32) u(32) ...] along the last dim."""
+    F2 = h.shape[-1]
+    v = h.reshape(*h.shape[:-1], F2 // (2 * block), 2, block)
+    return v[..., 0, :].reshape(*h.shape[:-1], F2 // 2), v[..., 1, :].reshape(*h.shape[:-1], F2 // 2)
+
+
+def interleave_cols(g: torch.Tensor, u: torch.Tensor, block: int = 32) -> torch.Tensor:
+    F = g.shape[-1]
+    a = g.reshape(*g.shape[:-1], F // block, 1, block)
+    b = u.reshape(*u.shape[:-1], F // block, 1, block)
+    return torch.cat([a, b], dim=-2).reshape(*g.shape[:-1], 2 * F)
