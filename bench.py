@@ -1,0 +1,261 @@
+#!/usr/bin/env python
+"""Flagship benchmark: MoE LM pretraining step (forward + backward + AdamW).
+
+Model: 24 layers, d_model 2048, 16-head MLA attention (kv latent 512, rope 64),
+32 routed SwiGLU experts (ffn 1408, top-4) + 1 shared expert, vocab 32000,
+seq 4096, micro-batch 2 sequences per GPU, bf16 compute with fp32 master
+weights and AdamW state, random N(0, 0.02) weights, uniform random token ids.
+Layout on N GPUs: expert parallel over N ranks x data parallel over the same
+N ranks, ZeRO-1 sharded optimiser state for the replicated parameters.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+N > 1 is launched with torch.distributed.run (one rank per GPU, NCCL).  Rank 0
+prints one JSON line.  `value` is the whole-job token throughput measured on
+the device with CUDA events (max over ranks), `e2e` the same metric through the
+public Trainer API including the pinned host->device copy of each step's
+token ids/labels and the device->host read of the loss.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+METRIC = "train tokens/s/box (MoE, EP=8) at 1/2/4/8 B200; decode tokens/s at batch 64"
+MODEL_DESC = ("MoE LM 24L d2048 MLA(16h, kv512, rope64) 32 experts ffn1408 top-4 + 1 shared, vocab 32000 "
+              "(moe_mla_24l)")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--micro-batch", type=int, default=2)
+    ap.add_argument("--preset", default="moe_mla_24l")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-count", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------
+# clocks during the timed region
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, enabled: bool):
+        self.enabled = enabled
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        if not self.enabled:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = list(csv.reader(open(self.path)))
+        os.unlink(self.path)
+        sm, smax, reasons, n_load = [], 0.0, set(), 0
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            if len(r) < 10:
+                continue
+            try:
+                mhz, mx, util = float(r[1]), float(r[2]), float(r[4])
+            except ValueError:
+                continue
+            smax = max(smax, mx)
+            if util >= 50:
+                n_load += 1
+                sm.append(mhz)
+                for nm, v in zip(names, r[6:10]):
+                    if v.lower().startswith("active"):
+                        reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples_under_load": n_load}
+
+
+# ----------------------------------------------------------------------------
+def reference_arm(args):
+    """The reference (installed unmodified under baseline/_ref) cannot run this
+    workload: it has no expert-parallel or distributed path, it truncates every
+    sequence to 128 positions and its MoE layer passes no gradient to experts."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref", "omnicoder")
+        why = ("reference cannot run this config: no expert/data parallel path (torchrun_ep only sets an env var), "
+               "forward truncates sequences to 128 positions, MoE capacity = top_k and experts get no gradient, "
+               "no MLA rope dims")
+        if not os.path.isdir(ref):
+            why = "reference not installed under baseline/_ref; " + why
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+# ----------------------------------------------------------------------------
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from omnicoder.config import TrainConfig, get_preset
+    from omnicoder.models.lm import build_model
+    from omnicoder.ops import _ext
+    from omnicoder.training.engine import Trainer, synthetic_batch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world and not (args.gpus == 1 and world == 1):
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torch.distributed.run")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    parallel = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        from omnicoder.parallel.expert_data import ExpertDataParallel
+        parallel = ExpertDataParallel(dist.group.WORLD)
+
+    cfg = get_preset(args.preset)
+    tcfg = TrainConfig(lr=3e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch, seq_len=args.seq,
+                       grad_clip=1.0, weight_decay=0.1, betas=(0.9, 0.95))
+    model = build_model(cfg, device=dev, seed=1234, ep=parallel) if parallel is not None else \
+        build_model(cfg, device=dev, seed=1234)
+    trainer = Trainer(model, tcfg, parallel)
+    _ext.load()
+
+    B, S, V = args.micro_batch, args.seq, cfg.vocab_size
+    n_steps = args.warmup + args.steps
+    dev_batches = [synthetic_batch(B, S, V, seed=rank, step=i, device=dev) for i in range(n_steps)]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-timed region --------------------------------------------------
+    for i in range(args.warmup):
+        trainer.step(*dev_batches[i], assume_all_valid=True)
+    torch.cuda.synchronize()
+    _ext.check_status()
+    clocks = ClockSampler(local == 0)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    last = None
+    for i in range(args.steps):
+        last = trainer.step(*dev_batches[args.warmup + i], assume_all_valid=True)
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    _ext.check_status()
+    loss_val = float(last.loss.item())
+    tokens_step = B * S * world
+    value = tokens_step / (ms / 1000.0)
+    del dev_batches
+
+    # ---- end-to-end through the public API --------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        host = [synthetic_batch(B, S, V, seed=rank + 7, step=i, pin=True) for i in range(args.steps + 1)]
+        trainer.step(host[0][0].to(dev, non_blocking=True), host[0][1].to(dev, non_blocking=True))
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(1, args.steps + 1):
+            ids = host[i][0].to(dev, non_blocking=True)
+            lab = host[i][1].to(dev, non_blocking=True)
+            st = trainer.step(ids, lab)
+            _ = st.loss.item()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ems = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t.item())
+        bi = host[1][0].numel() * host[1][0].element_size() + host[1][1].numel() * host[1][1].element_size()
+        e2e = {"value": tokens_step / (ems / 1000.0), "unit": "tokens/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4, "note": "per rank bytes; loss read back each step"}
+
+    # ---- launch count of this repo's kernels (one extra, untimed, profiled step) ----
+    launches = None
+    if not args.no_count:
+        from torch.profiler import ProfilerActivity, profile
+        b = synthetic_batch(B, S, V, seed=rank + 11, step=0, device=dev)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            trainer.step(*b, assume_all_valid=True)
+            torch.cuda.synchronize()
+        ours = other = 0
+        for ev in prof.events():
+            if ev.device_type is not None and str(ev.device_type).endswith("CUDA") and ev.name:
+                if "omni::" in ev.name:
+                    ours += 1
+                elif not ev.name.startswith(("Memcpy", "Memset")):
+                    other += 1
+        launches = {"ours_per_step": ours, "other_per_step": other}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init N(0,0.02))",
+            "config": {"model": MODEL_DESC, "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": S,
+                       "parallelism": f"ep{world}xdp{world}" + (" zero1" if world > 1 else ""),
+                       "optimizer": "AdamW fp32 master, grad clip 1.0",
+                       "l2": "working set (14.6 GB bf16 weights, 8192 tokens/GPU of activations) >> 126 MB L2"},
+            "loss": loss_val, "e2e": e2e,
+            "gpu_launches": (launches["ours_per_step"] * args.steps) if launches else None,
+            "launches_per_step": launches, "clocks": clk, "impl": "ours",
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -25,8 +25,8 @@ import torch
 import torch.nn as nn
 
 from ..config import ModelConfig
-from ..ops import (RopeTable, apply_rope, attention, embedding, layer_norm, linear, lm_head_cross_entropy, moe_ffn,
-                   rms_norm, swiglu_mlp)
+from ..ops import (RopeTable, apply_rope, attention, embedding, layer_norm, linear, linear_rope, lm_head_cross_entropy,
+                   moe_ffn, rms_norm, swiglu_mlp)
 from ..ops.gemm import interleave_gate_up, split_gate_up
 
 
@@ -74,8 +74,8 @@ class GQAttention(nn.Module):
 
     def qkv(self, y, rope: RopeTable, positions):
         T = y.shape[0]
-        qkv = linear(y, self.wqkv).view(T, self.H + 2 * self.Hk, self.hd)
-        qkv = apply_rope(qkv, rope, positions, heads=self.H + self.Hk, interleaved=self.cfg.attn.rope_interleaved)
+        qkv = linear_rope(y, self.wqkv, rope, positions, self.hd, self.H + self.Hk,
+                          interleaved=self.cfg.attn.rope_interleaved).view(T, self.H + 2 * self.Hk, self.hd)
         q = qkv[:, :self.H]
         k = qkv[:, self.H:self.H + self.Hk]
         v = qkv[:, self.H + self.Hk:]
@@ -106,16 +106,16 @@ class MLAttention(nn.Module):
     def latent(self, y, rope: RopeTable, positions):
         """Compressed KV of the tokens: (normalised latent c [T, r], rotated rope key [T, dr])."""
         T = y.shape[0]
-        kva = linear(y, self.wkv_a)
+        kva = linear_rope(y, self.wkv_a, rope, positions, self.r + self.dr, 1, off=self.r,
+                          interleaved=self.cfg.attn.rope_interleaved)
         c = rms_norm(kva[:, :self.r].contiguous(), self.kv_norm, self.cfg.norm_eps)
-        kr = kva[:, self.r:].contiguous().view(T, 1, self.dr)
-        kr = apply_rope(kr, rope, positions, interleaved=self.cfg.attn.rope_interleaved).view(T, self.dr)
+        kr = kva[:, self.r:].contiguous()
         return c, kr
 
     def qkv(self, y, rope: RopeTable, positions):
         T = y.shape[0]
-        q = linear(y, self.wq).view(T, self.H, self.dn + self.dr)
-        q = apply_rope(q, rope, positions, off=self.dn, interleaved=self.cfg.attn.rope_interleaved)
+        q = linear_rope(y, self.wq, rope, positions, self.dn + self.dr, self.H, off=self.dn,
+                        interleaved=self.cfg.attn.rope_interleaved).view(T, self.H, self.dn + self.dr)
         c, kr = self.latent(y, rope, positions)
         kv = linear(c, self.wkv_b).view(T, self.H, self.dn + self.dv)
         return q, kv[:, :, :self.dn], kv[:, :, self.dn:], kr

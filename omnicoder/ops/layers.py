@@ -207,6 +207,51 @@ def apply_rope(x: torch.Tensor, table: RopeTable, positions: torch.Tensor | None
 
 
 # ----------------------------------------------------------------------------
+# Linear + RoPE: y = rope(x W^T) on `rope_heads` heads of `head_dim` at [off, off+rot)
+# ----------------------------------------------------------------------------
+class _LinearRopeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, table, pos, head_dim, rope_heads, off, interleaved):
+        C = _ext.load()
+        x2 = _flat(x).contiguous()
+        y = mm_nt(x2, w)
+        T = y.shape[0]
+        nh = y.shape[1] // head_dim
+        C.rope(y, table.cs, pos, 0, 1, T, rope_heads, y.stride(0), head_dim, off, table.rot, interleaved, 1.0)
+        ctx.save_for_backward(x2, w, pos)
+        ctx.cfg = (table, head_dim, rope_heads, off, interleaved)
+        ctx.xshape = x.shape
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, pos = ctx.saved_tensors
+        table, head_dim, rope_heads, off, interleaved = ctx.cfg
+        C = _ext.load()
+        d = dy.contiguous().clone()
+        T = d.shape[0]
+        C.rope(d, table.cs, pos, 0, 1, T, rope_heads, d.stride(0), head_dim, off, table.rot, interleaved, -1.0)
+        dx = mm_nn(d, w).view(*ctx.xshape[:-1], w.shape[1]) if ctx.needs_input_grad[0] else None
+        dw = mm_tn(d, x2) if ctx.needs_input_grad[1] else None
+        return dx, dw, None, None, None, None, None, None
+
+
+def linear_rope(x: torch.Tensor, w: torch.Tensor, table: RopeTable, positions: torch.Tensor, head_dim: int,
+                rope_heads: int, off: int = 0, interleaved: bool = False) -> torch.Tensor:
+    """y = x @ w.T viewed as [T, heads, head_dim]; dims [off, off+rot) of the first
+    `rope_heads` heads are rotated by the position of each token.  Returns [T, heads*head_dim]."""
+    if not x.is_cuda:
+        y = F.linear(_flat(x), w)
+        T = y.shape[0]
+        nh = y.shape[1] // head_dim
+        return apply_rope(y.view(T, nh, head_dim), table, positions, off=off, interleaved=interleaved,
+                          heads=rope_heads).reshape(T, nh * head_dim)
+    table.to(x.device)
+    pos = positions.to(device=x.device, dtype=torch.int32).contiguous()
+    return _LinearRopeFn.apply(x, w, table, pos, head_dim, rope_heads, off, interleaved)
+
+
+# ----------------------------------------------------------------------------
 # Embedding
 # ----------------------------------------------------------------------------
 class _EmbeddingFn(torch.autograd.Function):
@@ -274,5 +319,5 @@ def swiglu_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, residual: t
     return _SwiGLUMLPFn.apply(x, w13, w2, residual)
 
 
-__all__ = ["linear", "rms_norm", "layer_norm", "RopeTable", "apply_rope", "embedding", "swiglu_mlp",
+__all__ = ["linear", "linear_rope", "rms_norm", "layer_norm", "RopeTable", "apply_rope", "embedding", "swiglu_mlp",
            "interleave_cols", "deinterleave_cols"]
