@@ -1,0 +1,279 @@
+"""Batched text generation: prefill + KV-cache decode, sampling, speculative decoding.
+
+Public API (same entry point as the reference, src/omnicoder/inference/generate.py:692):
+
+    generate(model, input_ids, max_new_tokens, temperature=0.8, top_k=40, top_p=0.9,
+             draft_model=None, speculative_draft_len=0, kvq="none", window_size=0,
+             return_stats=False, eos_id=None, seed=None)
+
+Differences from the reference, by design:
+  * batched (B >= 1) prefill of the whole prompt (the reference feeds only the last
+    prompt token, with B == 1);
+  * temperature <= 0 means greedy decoding (the reference clamps temperature to >= 0.2);
+  * speculative decoding verifies all draft tokens in one target forward and accepts
+    them by rejection sampling (exact-match when greedy), so the output distribution
+    is the target's; the reference accepts by a verifier-probability threshold and
+    re-feeds accepted tokens one at a time (generate.py:2925-3048);
+  * `kvq="int8"` stores the cache as int8 with per-token (MLA) / per-head-per-token
+    (MHA/GQA) scales.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from .kv_cache import KVCache
+
+
+# ----------------------------------------------------------------------------
+# Sampling
+# ----------------------------------------------------------------------------
+def _filter_logits(logits: torch.Tensor, top_k: int, top_p: float) -> torch.Tensor:
+    logits = torch.where(torch.isfinite(logits), logits, torch.full_like(logits, float("-inf")))
+    if top_k and top_k > 0 and top_k < logits.shape[-1]:
+        kth = torch.topk(logits, top_k, dim=-1).values[..., -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    if top_p is not None and 0.0 < top_p < 1.0:
+        sorted_logits, idx = torch.sort(logits, dim=-1, descending=True)
+        probs = torch.softmax(sorted_logits, dim=-1)
+        cum = probs.cumsum(-1)
+        remove = cum - probs > top_p
+        sorted_logits = sorted_logits.masked_fill(remove, float("-inf"))
+        logits = torch.full_like(logits, float("-inf")).scatter(-1, idx, sorted_logits)
+    return logits
+
+
+def sampling_probs(logits: torch.Tensor, temperature: float, top_k: int = 0, top_p: float = 1.0) -> torch.Tensor:
+    """The distribution that sample_next_token draws from (fp32 [..., V])."""
+    logits = logits.float()
+    if temperature <= 0:
+        return torch.nn.functional.one_hot(logits.argmax(-1), logits.shape[-1]).float()
+    return torch.softmax(_filter_logits(logits / temperature, top_k, top_p), dim=-1)
+
+
+def sample_next_token(logits: torch.Tensor, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0,
+                      generator: torch.Generator | None = None) -> torch.Tensor:
+    """logits [..., V] -> token ids [...]; greedy when temperature <= 0."""
+    if temperature <= 0:
+        return logits.argmax(-1)
+    p = sampling_probs(logits, temperature, top_k, top_p)
+    flat = p.reshape(-1, p.shape[-1])
+    return torch.multinomial(flat, 1, generator=generator).view(p.shape[:-1])
+
+
+@dataclass
+class GenStats:
+    prompt_tokens: int = 0
+    new_tokens: int = 0
+    prefill_s: float = 0.0
+    decode_s: float = 0.0
+    steps: int = 0
+    accepted_draft_tokens: int = 0
+    proposed_draft_tokens: int = 0
+    step_times_s: list = field(default_factory=list)
+
+    @property
+    def decode_tokens_per_s(self) -> float:
+        return self.new_tokens / self.decode_s if self.decode_s > 0 else 0.0
+
+    def as_dict(self):
+        d = {k: v for k, v in self.__dict__.items() if k != "step_times_s"}
+        d["decode_tokens_per_s"] = self.decode_tokens_per_s
+        if self.step_times_s:
+            st = sorted(self.step_times_s)
+            d["p50_step_s"] = st[len(st) // 2]
+        if self.proposed_draft_tokens:
+            d["acceptance_rate"] = self.accepted_draft_tokens / self.proposed_draft_tokens
+        return d
+
+
+def _sync(t: torch.Tensor):
+    if t.is_cuda:
+        torch.cuda.synchronize(t.device)
+
+
+# ----------------------------------------------------------------------------
+@torch.no_grad()
+def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: float = 0.8, top_k: int = 40,
+             top_p: float = 0.9, draft_model=None, speculative_draft_len: int = 0, kvq: str = "none",
+             window_size: int = 0, return_stats: bool = False, eos_id: int | None = None, seed: int | None = None,
+             max_len: int | None = None, **_unused):
+    """Generate `max_new_tokens` tokens after `input_ids` [B, S] (or [S]).  Returns
+    [B, S + max_new_tokens] (and GenStats with return_stats)."""
+    model.eval()
+    squeeze = input_ids.dim() == 1
+    ids = input_ids[None] if squeeze else input_ids
+    B, S = ids.shape
+    dev = ids.device
+    cfg = model.cfg
+    if window_size:
+        cfg.attn.window = window_size
+    kv_dtype = "int8" if kvq in ("int8", "u8") else "bf16"
+    L = max_len or (S + max_new_tokens + max(0, speculative_draft_len) + 2)
+    gen = None
+    if seed is not None:
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+    stats = GenStats(prompt_tokens=B * S)
+    if draft_model is not None and speculative_draft_len > 0:
+        out = _speculative(model, draft_model, ids, max_new_tokens, speculative_draft_len, temperature, top_k, top_p,
+                           kv_dtype, L, gen, stats, eos_id)
+    else:
+        cache = KVCache(cfg, B, L, dev, dtype=model.embed.dtype, kv_dtype=kv_dtype)
+        t0 = time.perf_counter()
+        logits = model.forward_cached(ids, cache, prefill=True, last_only=True)[:, -1]
+        tok = sample_next_token(logits, temperature, top_k, top_p, gen)
+        _sync(tok)
+        stats.prefill_s = time.perf_counter() - t0
+        toks = [tok]
+        done = torch.zeros(B, dtype=torch.bool, device=dev)
+        t1 = time.perf_counter()
+        for _ in range(max_new_tokens - 1):
+            ts = time.perf_counter()
+            logits = model.forward_cached(tok[:, None], cache)[:, -1]
+            tok = sample_next_token(logits, temperature, top_k, top_p, gen)
+            if eos_id is not None:
+                done |= tok == eos_id
+                tok = torch.where(done, torch.full_like(tok, eos_id), tok)
+            toks.append(tok)
+            stats.steps += 1
+            if return_stats:
+                _sync(tok)
+                stats.step_times_s.append(time.perf_counter() - ts)
+        _sync(tok)
+        stats.decode_s = time.perf_counter() - t1
+        stats.new_tokens = B * (max_new_tokens - 1)
+        out = torch.cat([ids, torch.stack(toks, dim=1)], dim=1)
+    out = out[0] if squeeze else out
+    return (out, stats) if return_stats else out
+
+
+def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_dtype, L, gen, stats, eos_id):
+    """Draft proposes k tokens autoregressively; the target scores all k+1 positions
+    in one forward; tokens are accepted left to right with probability
+    min(1, p_target/p_draft) (always, when greedy and equal); the first rejection
+    is replaced by a sample from normalize(max(0, p_target - p_draft)) and, if all
+    k are accepted, a bonus token comes from the target's last position.  Both
+    caches are then rolled back per sequence to the accepted length."""
+    B, S = ids.shape
+    dev = ids.device
+    tcache = KVCache(target.cfg, B, L, dev, dtype=target.embed.dtype, kv_dtype=kv_dtype)
+    dcache = KVCache(draft.cfg, B, L, dev, dtype=draft.embed.dtype, kv_dtype="bf16")
+    t0 = time.perf_counter()
+    if S > 1:
+        target.forward_cached(ids[:, :-1], tcache, prefill=True, last_only=True)
+        draft.forward_cached(ids[:, :-1], dcache, prefill=True, last_only=True)
+    last = ids[:, -1]
+    _sync(last)
+    stats.prefill_s = time.perf_counter() - t0
+    produced = [[] for _ in range(B)]
+    t1 = time.perf_counter()
+    ar = torch.arange(B, device=dev)
+    while min(len(p) for p in produced) < max_new:
+        ts = time.perf_counter()
+        base_t = tcache.lengths.clone()
+        base_d = dcache.lengths.clone()
+        cur = last
+        d_tok, d_prob = [], []
+        for _ in range(k):
+            dl = draft.forward_cached(cur[:, None], dcache)[:, -1]
+            pd = sampling_probs(dl, temperature, top_k, top_p)
+            nxt = pd.argmax(-1) if temperature <= 0 else torch.multinomial(pd, 1, generator=gen).squeeze(1)
+            d_tok.append(nxt)
+            d_prob.append(pd)
+            cur = nxt
+        d_tok_t = torch.stack(d_tok, dim=1)                          # [B, k]
+        tl = target.forward_cached(torch.cat([last[:, None], d_tok_t], dim=1), tcache)   # [B, k+1, V]
+        pt = sampling_probs(tl, temperature, top_k, top_p)           # [B, k+1, V]
+        pd_all = torch.stack(d_prob, dim=1)                          # [B, k, V]
+        pt_d = pt[:, :k].gather(-1, d_tok_t[..., None]).squeeze(-1)
+        pd_d = pd_all.gather(-1, d_tok_t[..., None]).squeeze(-1)
+        if temperature <= 0:
+            acc = pt_d > 0.5
+        else:
+            u = torch.rand(B, k, device=dev, generator=gen)
+            acc = u < torch.clamp(pt_d / pd_d.clamp_min(1e-20), max=1.0)
+        n_acc = torch.cumprod(acc.int(), dim=1).sum(1)               # accepted prefix length [B]
+        # correction / bonus token at position n_acc
+        p_next = pt[ar, n_acc]                                       # [B, V]
+        resid = torch.clamp(p_next - torch.cat([pd_all, torch.zeros_like(pd_all[:, :1])], 1)[ar, n_acc], min=0)
+        use_resid = n_acc < k
+        q = torch.where(use_resid[:, None], resid, p_next)
+        q = q / q.sum(-1, keepdim=True).clamp_min(1e-20)
+        extra = q.argmax(-1) if temperature <= 0 else torch.multinomial(q, 1, generator=gen).squeeze(1)
+        # draft cache lacks the k-th draft token when everything was accepted: catch up
+        draft.forward_cached(d_tok_t[:, -1:], dcache)
+        tcache.rollback(base_t + n_acc + 1)
+        dcache.rollback(base_d + n_acc + 1)
+        n_list = n_acc.tolist()
+        d_list = d_tok_t.tolist()
+        e_list = extra.tolist()
+        for b in range(B):
+            produced[b].extend(d_list[b][:n_list[b]] + [e_list[b]])
+        stats.accepted_draft_tokens += int(sum(n_list))
+        stats.proposed_draft_tokens += B * k
+        stats.steps += 1
+        last = extra
+        _sync(last)
+        stats.step_times_s.append(time.perf_counter() - ts)
+    stats.decode_s = time.perf_counter() - t1
+    stats.new_tokens = B * max_new
+    out = torch.tensor([p[:max_new] for p in produced], device=dev, dtype=ids.dtype)
+    return torch.cat([ids, out], dim=1)
+
+
+# ----------------------------------------------------------------------------
+# CLI (python -m omnicoder.inference.generate)
+# ----------------------------------------------------------------------------
+def main(argv=None):
+    from ..config import get_preset
+    from ..models.lm import build_model
+    from ..training.checkpoint import maybe_load_checkpoint
+    from ..training.tokenizer import get_tokenizer
+
+    ap = argparse.ArgumentParser(description="omnicoder text generation")
+    ap.add_argument("--prompt", default="def fibonacci(n):")
+    ap.add_argument("--preset", default="tiny_moe")
+    ap.add_argument("--ckpt", default=None)
+    ap.add_argument("--max_new_tokens", type=int, default=64)
+    ap.add_argument("--temperature", type=float, default=0.8)
+    ap.add_argument("--top_k", type=int, default=40)
+    ap.add_argument("--top_p", type=float, default=0.9)
+    ap.add_argument("--kvq", default="none", choices=["none", "int8", "u8"])
+    ap.add_argument("--window_size", type=int, default=0)
+    ap.add_argument("--draft_preset", default=None)
+    ap.add_argument("--draft_ckpt", default=None)
+    ap.add_argument("--speculative_draft_len", type=int, default=0)
+    ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--json", action="store_true")
+    a = ap.parse_args(argv)
+    cfg = get_preset(a.preset)
+    model = build_model(cfg, device=a.device)
+    if a.ckpt:
+        maybe_load_checkpoint(model, a.ckpt)
+    tok = get_tokenizer(cfg.vocab_size)
+    ids = torch.tensor([tok.encode(a.prompt)], device=a.device)
+    draft = None
+    if a.draft_preset:
+        draft = build_model(get_preset(a.draft_preset), device=a.device)
+        if a.draft_ckpt:
+            maybe_load_checkpoint(draft, a.draft_ckpt)
+    out, st = generate(model, ids, a.max_new_tokens, a.temperature, a.top_k, a.top_p, draft_model=draft,
+                       speculative_draft_len=a.speculative_draft_len, kvq=a.kvq, window_size=a.window_size,
+                       return_stats=True, seed=a.seed)
+    text = tok.decode(out[0, ids.shape[1]:].tolist())
+    if a.json:
+        print(json.dumps({"text": text, "stats": st.as_dict()}))
+    else:
+        print(text)
+        print(json.dumps(st.as_dict()), file=sys.stderr)
+
+
+if __name__ == "__main__":
+    main()

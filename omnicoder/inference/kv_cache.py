@@ -1,0 +1,123 @@
+"""Key/value cache of the spec model family for batched generation.
+
+Per layer:
+  * MHA / GQA: keys and values [B, L, Hk, D] (bf16) or int8 with one fp32
+    scale per (sequence, position, head).
+  * MLA: the compressed latent [B, L, r + dr] = (normalised kv latent c,
+    rotated rope key) shared by all heads (bf16) or int8 with one fp32 scale
+    per (sequence, position).  Decoding attends over this latent directly
+    (absorbed up-projections, see OmniLM.prepare_inference).
+
+`lengths[b]` counts the cached positions of sequence b; writes go to
+positions lengths[b] .. lengths[b]+T_new-1.  Quantisation is symmetric:
+q = round(x / s), s = max|x| / 127 over the quantised group (the reference
+quantises per group of 64 with min/max zero points, src/omnicoder/modeling/
+quant/kv_cache.py:108-257; the per-head per-token symmetric scale keeps the
+dequantisation a single multiply inside the attention kernel).
+"""
+from __future__ import annotations
+
+import torch
+
+from ..config import ModelConfig
+
+
+def quantize_int8(x: torch.Tensor, dim: int = -1) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric int8 with one scale per slice along `dim` (reduced)."""
+    amax = x.float().abs().amax(dim=dim, keepdim=True).clamp_min(1e-8)
+    s = amax / 127.0
+    q = torch.round(x.float() / s).clamp_(-127, 127).to(torch.int8)
+    return q, s.squeeze(dim)
+
+
+def dequantize_int8(q: torch.Tensor, s: torch.Tensor, dim: int = -1, dtype=torch.float32) -> torch.Tensor:
+    return (q.float() * s.unsqueeze(dim)).to(dtype)
+
+
+class KVCache:
+    def __init__(self, cfg: ModelConfig, batch: int, max_len: int, device, dtype=None, kv_dtype: str = "bf16"):
+        if dtype is None:
+            dtype = torch.bfloat16 if str(device).startswith("cuda") else torch.float32
+        self.cfg, self.batch, self.max_len, self.device, self.dtype = cfg, batch, max_len, torch.device(device), dtype
+        assert kv_dtype in ("bf16", "int8"), kv_dtype
+        self.kv_dtype = kv_dtype
+        self.mla = cfg.attn.kind == "mla"
+        self.lengths = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.k, self.v, self.ks, self.vs = [], [], [], []
+        store = torch.int8 if kv_dtype == "int8" else dtype
+        for _ in range(cfg.n_layers):
+            if self.mla:
+                w = cfg.attn.kv_lora_rank + cfg.attn.qk_rope_dim
+                self.k.append(torch.zeros(batch, max_len, w, dtype=store, device=device))
+                self.v.append(None)
+                self.ks.append(torch.zeros(batch, max_len, dtype=torch.float32, device=device) if kv_dtype == "int8" else None)
+                self.vs.append(None)
+            else:
+                Hk, D = cfg.n_kv_heads, cfg.head_dim
+                self.k.append(torch.zeros(batch, max_len, Hk, D, dtype=store, device=device))
+                self.v.append(torch.zeros(batch, max_len, Hk, D, dtype=store, device=device))
+                if kv_dtype == "int8":
+                    self.ks.append(torch.zeros(batch, max_len, Hk, dtype=torch.float32, device=device))
+                    self.vs.append(torch.zeros(batch, max_len, Hk, dtype=torch.float32, device=device))
+                else:
+                    self.ks.append(None)
+                    self.vs.append(None)
+
+    # ------------------------------------------------------------------
+    def positions(self, t_new: int) -> torch.Tensor:
+        """[B, t_new] absolute positions of the next t_new tokens."""
+        return self.lengths.long()[:, None] + torch.arange(t_new, device=self.device)[None, :]
+
+    def write(self, layer: int, pos: torch.Tensor, k: torch.Tensor, v: torch.Tensor | None = None):
+        """Store new entries at positions pos [B, T]; k [B, T, ...] (MLA: latent [B, T, r+dr])."""
+        B, T = pos.shape
+        bidx = torch.arange(B, device=self.device)[:, None].expand(B, T)
+        if self.kv_dtype == "int8":
+            if self.mla:
+                q, s = quantize_int8(k, -1)
+                self.k[layer][bidx, pos] = q
+                self.ks[layer][bidx, pos] = s
+            else:
+                q, s = quantize_int8(k, -1)
+                self.k[layer][bidx, pos] = q
+                self.ks[layer][bidx, pos] = s
+                q, s = quantize_int8(v, -1)
+                self.v[layer][bidx, pos] = q
+                self.vs[layer][bidx, pos] = s
+        else:
+            self.k[layer][bidx, pos] = k.to(self.k[layer].dtype)
+            if v is not None:
+                self.v[layer][bidx, pos] = v.to(self.v[layer].dtype)
+
+    def advance(self, t_new: int):
+        self.lengths += t_new
+
+    def rollback(self, new_lengths: torch.Tensor):
+        """Forget positions >= new_lengths[b] (speculative decoding rejection)."""
+        self.lengths.copy_(new_lengths.to(self.lengths.dtype))
+
+    def reorder(self, index: torch.Tensor):
+        """Keep / permute sequences (beam search or finished-sequence compaction)."""
+        for lst in (self.k, self.v, self.ks, self.vs):
+            for i, t in enumerate(lst):
+                if t is not None:
+                    lst[i] = t.index_select(0, index)
+        self.lengths = self.lengths.index_select(0, index)
+        self.batch = int(index.numel())
+
+    def layer_kv(self, layer: int, dtype=None):
+        """Dequantised (k, v) of a layer (MLA: latent, None)."""
+        dtype = dtype or self.dtype
+        if self.kv_dtype == "int8":
+            k = dequantize_int8(self.k[layer], self.ks[layer], -1, dtype)
+            v = None if self.v[layer] is None else dequantize_int8(self.v[layer], self.vs[layer], -1, dtype)
+            return k, v
+        return self.k[layer], self.v[layer]
+
+    def nbytes(self) -> int:
+        n = 0
+        for lst in (self.k, self.v, self.ks, self.vs):
+            for t in lst:
+                if t is not None:
+                    n += t.numel() * t.element_size()
+        return n

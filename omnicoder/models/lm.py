@@ -27,6 +27,7 @@ import torch.nn as nn
 from ..config import ModelConfig
 from ..ops import (RopeTable, apply_rope, attention, embedding, layer_norm, linear, linear_rope, lm_head_cross_entropy,
                    moe_ffn, rms_norm, swiglu_mlp)
+from ..ops.decode import decode_attention
 from ..ops.gemm import interleave_gate_up, split_gate_up
 
 
@@ -86,6 +87,19 @@ class GQAttention(nn.Module):
         o = attention(q, k, v, kr, seq=seq, causal=True, window=self.cfg.attn.window)
         return linear(o.reshape(y.shape[0], -1), self.wo, residual=h)
 
+    def forward_cached(self, y, h, rope, pos, cache, layer: int, prefill: bool):
+        """New tokens y [B*Tn, D] at positions pos [B, Tn] against the cache."""
+        B, Tn = pos.shape
+        q, k, v, _ = self.qkv(y, rope, pos.reshape(-1))
+        cache.write(layer, pos, k.reshape(B, Tn, self.Hk, self.hd), v.reshape(B, Tn, self.Hk, self.hd))
+        if prefill and y.is_cuda and Tn % 128 == 0:
+            o = attention(q, k, v, None, seq=Tn, causal=True, window=self.cfg.attn.window)
+        else:
+            kv_len = cache.lengths + Tn
+            o = decode_attention(q.reshape(B, Tn, self.H, self.hd), cache.k[layer], cache.v[layer], pos, kv_len,
+                                 window=self.cfg.attn.window, k_scale=cache.ks[layer], v_scale=cache.vs[layer])
+        return linear(o.reshape(B * Tn, -1), self.wo, residual=h)
+
 
 class MLAttention(nn.Module):
     """Multi-head latent attention: keys/values come from a low-rank latent
@@ -112,19 +126,59 @@ class MLAttention(nn.Module):
         kr = kva[:, self.r:].contiguous()
         return c, kr
 
-    def qkv(self, y, rope: RopeTable, positions):
+    def qkv_latent(self, y, rope: RopeTable, positions):
+        """(q, k_nope view, v view, rope key, latent c) of tokens y."""
         T = y.shape[0]
         q = linear_rope(y, self.wq, rope, positions, self.dn + self.dr, self.H, off=self.dn,
                         interleaved=self.cfg.attn.rope_interleaved).view(T, self.H, self.dn + self.dr)
         c, kr = self.latent(y, rope, positions)
         kv = linear(c, self.wkv_b).view(T, self.H, self.dn + self.dv)
-        return q, kv[:, :, :self.dn], kv[:, :, self.dn:], kr
+        return q, kv[:, :, :self.dn], kv[:, :, self.dn:], kr, c
+
+    def qkv(self, y, rope: RopeTable, positions):
+        return self.qkv_latent(y, rope, positions)[:4]
 
     def forward(self, y, h, rope, positions, seq):
         q, k, v, kr = self.qkv(y, rope, positions)
         o = attention(q, k, v, kr, seq=seq, causal=True, window=self.cfg.attn.window,
                       scale=1.0 / math.sqrt(self.dn + self.dr))
         return linear(o.reshape(y.shape[0], -1), self.wo, residual=h)
+
+    @torch.no_grad()
+    def prepare_inference(self):
+        """Absorb the latent up-projections into the query and output projections:
+        q_lat[h] = W_uk[h]^T q_nope[h] and out = sum_h Wo_h W_uv[h] o_lat[h], so decoding
+        attends over the compressed latent cache directly."""
+        H, dn, dr, dv, r = self.H, self.dn, self.dr, self.dv, self.r
+        D = self.wq.shape[1]
+        wkv_b = self.wkv_b.float().view(H, dn + dv, r)
+        w_uk, w_uv = wkv_b[:, :dn], wkv_b[:, dn:]
+        wq = self.wq.float().view(H, dn + dr, D)
+        wq_lat = torch.einsum("hnr,hnd->hrd", w_uk, wq[:, :dn])
+        self.wq_abs = torch.cat([wq_lat, wq[:, dn:]], dim=1).reshape(H * (r + dr), D).to(self.wq.dtype).contiguous()
+        wo = self.wo.float().view(D, H, dv)
+        self.wo_abs = torch.einsum("dhv,hvr->dhr", wo, w_uv).reshape(D, H * r).to(self.wo.dtype).contiguous()
+
+    def forward_cached(self, y, h, rope, pos, cache, layer: int, prefill: bool):
+        B, Tn = pos.shape
+        flat = pos.reshape(-1)
+        if prefill and y.is_cuda and Tn % 128 == 0:
+            q, k, v, kr, c = self.qkv_latent(y, rope, flat)
+            cache.write(layer, pos, torch.cat([c, kr], dim=-1).view(B, Tn, -1))
+            o = attention(q, k, v, kr, seq=Tn, causal=True, window=self.cfg.attn.window,
+                          scale=1.0 / math.sqrt(self.dn + self.dr))
+            return linear(o.reshape(B * Tn, -1), self.wo, residual=h)
+        if getattr(self, "wq_abs", None) is None:
+            self.prepare_inference()
+        r, dr = self.r, self.dr
+        qa = linear_rope(y, self.wq_abs, rope, flat, r + dr, self.H, off=r,
+                         interleaved=self.cfg.attn.rope_interleaved).view(B, Tn, self.H, r + dr)
+        c, kr = self.latent(y, rope, flat)
+        cache.write(layer, pos, torch.cat([c, kr], dim=-1).view(B, Tn, r + dr))
+        kv_len = cache.lengths + Tn
+        o = decode_attention(qa, cache.k[layer], None, pos, kv_len, window=self.cfg.attn.window,
+                             scale=1.0 / math.sqrt(self.dn + self.dr), k_scale=cache.ks[layer], latent_v_dim=r)
+        return linear(o.reshape(B * Tn, -1), self.wo_abs, residual=h)
 
 
 class DenseFFN(nn.Module):
@@ -169,6 +223,10 @@ class Block(nn.Module):
     def forward(self, h, rope, positions, seq):
         h = self.attn(self.attn_norm(h), h, rope, positions, seq)
         return self.ffn(self.ffn_norm(h), h)
+
+    def forward_cached(self, h, rope, pos, cache, layer: int, prefill: bool):
+        h = self.attn.forward_cached(self.attn_norm(h), h, rope, pos, cache, layer, prefill)
+        return self.ffn(self.ffn_norm(h), h)[0]
 
 
 class OmniLM(nn.Module):
@@ -238,6 +296,30 @@ class OmniLM(nn.Module):
         return out
 
     # ------------------------------------------------------------------
+    @torch.no_grad()
+    def forward_cached(self, ids: torch.Tensor, cache, prefill: bool = False, last_only: bool = False):
+        """Process new tokens ids [B, Tn] against `cache` (appending them) and return
+        logits [B, Tn, V] (or [B, 1, V] with last_only).  `prefill=True` asserts the
+        cache is empty, which lets long prompts use the flash-attention kernels."""
+        B, Tn = ids.shape
+        if ids.is_cuda:
+            self.rope.to(ids.device)
+        pos = cache.positions(Tn)
+        h = embedding(ids.reshape(-1), self.embed)
+        for i, blk in enumerate(self.blocks):
+            h = blk.forward_cached(h, self.rope, pos, cache, i, prefill)
+        cache.advance(Tn)
+        y = self.norm_f(h).view(B, Tn, -1)
+        if last_only:
+            y = y[:, -1:]
+        return linear(y.reshape(-1, y.shape[-1]), self.head_weight).float().view(B, y.shape[1], -1)
+
+    def prepare_inference(self):
+        for b in self.blocks:
+            if isinstance(b.attn, MLAttention):
+                b.attn.prepare_inference()
+        return self
+
     def export_state_dict(self) -> dict[str, torch.Tensor]:
         """state_dict with SwiGLU gate/up split into separate `w1`/`w3` tensors."""
         sd = {}
