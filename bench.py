@@ -46,6 +46,8 @@ def parse_args():
     ap.add_argument("--preset", default="moe_mla_24l")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-count", action="store_true")
+    ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel exchange: fused peer-memory kernels or NCCL all_to_all (baseline)")
     return ap.parse_args()
 
 
@@ -141,13 +143,16 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torch.distributed.run")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    cfg = get_preset(args.preset)
     parallel = None
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         from omnicoder.parallel.expert_data import ExpertDataParallel
-        parallel = ExpertDataParallel(dist.group.WORLD)
+        # exchange arena: x, y, dy, dx receive slabs (+ routing metadata) of every MoE layer of a step
+        rows = int(args.micro_batch * args.seq * cfg.moe.top_k * 1.3) + cfg.moe.n_experts * 128
+        arena = cfg.n_layers * rows * (4 * cfg.d_model * 2 + 16)
+        parallel = ExpertDataParallel(dist.group.WORLD, transport=args.ep_transport, arena_bytes=arena)
 
-    cfg = get_preset(args.preset)
     tcfg = TrainConfig(lr=3e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch, seq_len=args.seq,
                        grad_clip=1.0, weight_decay=0.1, betas=(0.9, 0.95))
     model = build_model(cfg, device=dev, seed=1234, ep=parallel) if parallel is not None else \
@@ -245,6 +250,7 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init N(0,0.02))",
             "config": {"model": MODEL_DESC, "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": S,
                        "parallelism": f"ep{world}xdp{world}" + (" zero1" if world > 1 else ""),
+                       "ep_transport": args.ep_transport if world > 1 else None,
                        "optimizer": "AdamW fp32 master, grad clip 1.0",
                        "l2": "working set (14.6 GB bf16 weights, 8192 tokens/GPU of activations) >> 126 MB L2"},
             "loss": loss_val, "e2e": e2e,

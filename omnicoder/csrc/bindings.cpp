@@ -235,4 +235,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped_k", &omni::gemm_grouped_k, py::arg("A"), py::arg("B"), py::arg("offsets"), py::arg("C"),
         py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("block_n") = 256);
   omni::register_kernels(m);
+  omni::register_ep(m);
 }

@@ -1,0 +1,107 @@
+// Tensor-level bindings of the expert-parallel exchange kernels (ep_comm.cu).
+// Peer addresses arrive as Python ints (device pointers of peer-mapped
+// symmetric memory, valid in this process) with the row capacity of each.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "ep_comm.h"
+
+namespace omni {
+
+namespace {
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+EpPeers make_peers(const std::vector<int64_t>& ptrs, const std::vector<int64_t>& rows) {
+  TORCH_CHECK(ptrs.size() <= (size_t)kEpMaxRanks, "expert parallel: at most ", kEpMaxRanks, " ranks");
+  TORCH_CHECK(rows.empty() || rows.size() == ptrs.size(), "expert parallel: rows per rank");
+  EpPeers p;
+  for (int i = 0; i < kEpMaxRanks; ++i) {
+    p.ptr[i] = i < (int)ptrs.size() ? (unsigned long long)ptrs[i] : 0ull;
+    p.rows[i] = (i < (int)rows.size()) ? (int)rows[i] : 0;
+  }
+  return p;
+}
+
+void check(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == dt && t.is_contiguous(), name, ": wrong device/dtype/layout");
+}
+}  // namespace
+
+at::Tensor ep_dispatch_t(const at::Tensor& x, const at::Tensor& idx, const at::Tensor& pos, const at::Tensor& loc_off,
+                         const at::Tensor& dst_base, const at::Tensor& keep_lim, const at::Tensor& wts,
+                         const std::vector<int64_t>& x_ptrs, const std::vector<int64_t>& meta_ptrs,
+                         const std::vector<int64_t>& rows, int64_t El, int64_t me) {
+  check(x, at::kBFloat16, "x");
+  check(idx, at::kInt, "idx");
+  check(pos, at::kInt, "pos");
+  check(wts, at::kFloat, "wts");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t T = idx.size(0), K = idx.size(1), D = x.size(1), E = dst_base.numel();
+  TORCH_CHECK(D % 8 == 0, "ep_dispatch: D % 8");
+  auto slot = at::empty({T, K}, idx.options());
+  ep_dispatch(x.data_ptr(), idx.data_ptr<int>(), pos.data_ptr<int>(), loc_off.data_ptr<int>(),
+              dst_base.data_ptr<int>(), keep_lim.data_ptr<int>(), wts.data_ptr<float>(), make_peers(x_ptrs, rows),
+              make_peers(meta_ptrs, rows), slot.data_ptr<int>(), (int)T, (int)K, (int)E, (int)El, (int)D, (int)me,
+              stream());
+  return slot;
+}
+
+void ep_push_t(const at::Tensor& src, const at::Tensor& slot, const at::Tensor& idx, const std::vector<int64_t>& ptrs,
+               const std::vector<int64_t>& rows, int64_t El) {
+  check(src, at::kBFloat16, "src");
+  const c10::cuda::CUDAGuard g(src.device());
+  ep_push(src.data_ptr(), slot.data_ptr<int>(), idx.data_ptr<int>(), make_peers(ptrs, rows), (int)slot.size(0),
+          (int)slot.size(1), (int)El, (int)src.size(1), stream());
+}
+
+at::Tensor ep_combine_t(const at::Tensor& slot, const at::Tensor& idx, const c10::optional<at::Tensor>& w,
+                        const std::vector<int64_t>& ptrs, const std::vector<int64_t>& rows, int64_t El, int64_t D,
+                        const c10::optional<at::Tensor>& add) {
+  check(slot, at::kInt, "slot");
+  const c10::cuda::CUDAGuard g(slot.device());
+  const int64_t T = slot.size(0), K = slot.size(1);
+  TORCH_CHECK(K <= 16, "ep_combine: top-k <= 16");
+  auto out = at::empty({T, D}, slot.options().dtype(at::kBFloat16));
+  if (add.has_value()) check(*add, at::kBFloat16, "add");
+  if (w.has_value()) check(*w, at::kFloat, "w");
+  ep_combine(slot.data_ptr<int>(), idx.data_ptr<int>(), w.has_value() ? w->data_ptr<float>() : nullptr,
+             make_peers(ptrs, rows), add.has_value() ? add->data_ptr() : nullptr, out.data_ptr(), (int)T, (int)K,
+             (int)El, (int)D, stream());
+  return out;
+}
+
+void ep_owner_bwd_t(at::Tensor& dy, const at::Tensor& y, const at::Tensor& meta, const at::Tensor& offsets,
+                    const at::Tensor& kept, const std::vector<int64_t>& dw_ptrs, const std::vector<int64_t>& dw_rows) {
+  check(dy, at::kBFloat16, "dy");
+  check(y, at::kBFloat16, "y");
+  const c10::cuda::CUDAGuard g(dy.device());
+  const int64_t El = kept.numel();
+  TORCH_CHECK(El <= kEpMaxRanks * 32, "ep_owner_bwd: too many local experts");
+  ep_owner_bwd(dy.data_ptr(), y.data_ptr(), meta.data_ptr(), offsets.data_ptr<int>(), kept.data_ptr<int>(), (int)El,
+               make_peers(dw_ptrs, dw_rows), (int)dy.size(0), (int)dy.size(1), stream());
+}
+
+void ep_pad_rows_t(at::Tensor& x, const c10::optional<at::Tensor>& meta, const at::Tensor& offsets,
+                   const at::Tensor& kept) {
+  check(x, at::kBFloat16, "x");
+  const c10::cuda::CUDAGuard g(x.device());
+  ep_pad_rows(x.data_ptr(), meta.has_value() ? meta->data_ptr() : nullptr, offsets.data_ptr<int>(),
+              kept.data_ptr<int>(), (int)kept.numel(), (int)x.size(0), (int)x.size(1), stream());
+}
+
+void ep_barrier_t(const std::vector<int64_t>& sig_ptrs, int64_t me, int64_t epoch, int64_t device) {
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  ep_barrier(make_peers(sig_ptrs, {}), (int)me, (int)sig_ptrs.size(), (unsigned)(epoch & 0xffffffffll), stream());
+}
+
+void register_ep(pybind11::module_& m) {
+  m.def("ep_dispatch", &ep_dispatch_t);
+  m.def("ep_push", &ep_push_t);
+  m.def("ep_combine", &ep_combine_t);
+  m.def("ep_owner_bwd", &ep_owner_bwd_t);
+  m.def("ep_pad_rows", &ep_pad_rows_t);
+  m.def("ep_barrier", &ep_barrier_t);
+}
+
+}  // namespace omni

@@ -1,0 +1,293 @@
+// Expert-parallel dispatch / combine over NVLink 5 peer memory (sm_100a).
+//
+// Every rank owns E / N experts.  Each rank's receive region lives in a
+// symmetric (peer-mapped) allocation, so these kernels move tokens with plain
+// loads and stores to other GPUs' memory over NVSwitch, fused with the work
+// around the exchange:
+//   ep_dispatch   router permutation + all-to-all: each (token, k) pair is
+//                 written straight into its slot of the owner's expert-major,
+//                 128-row padded receive slab (the layout the grouped tcgen05
+//                 GEMM consumes), with its routing weight and origin.
+//   ep_combine    all-to-all back + weighted sum + residual/shared-expert add:
+//                 each token pulls its k expert outputs from the owners.
+//   ep_owner_bwd  combine backward on the owner: routing-weight gradient
+//                 <dout, y> (written back to the source rank) and dout * w.
+// No TMA and no multicast is used here; ep_barrier orders the phases with
+// release/acquire flags at system scope and a bounded wait (status word on
+// timeout, never a trap).
+//
+// The reference has no expert parallelism: its launcher only sets an
+// environment variable (src/omnicoder/tools/torchrun_ep.py:36-38) and the MoE
+// layer keeps every expert on every rank (src/omnicoder/modeling/moe_layer.py).
+#include <algorithm>
+
+#include "common.cuh"
+#include "ep_comm.h"
+#include "kernels.h"
+
+namespace omni {
+
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+constexpr int kWarps = 8;
+
+__device__ __forceinline__ void acc_add8(float* acc, const uint4& v, float w) {
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    acc[2 * j] += w * bf16_lo(q[j]);
+    acc[2 * j + 1] += w * bf16_hi(q[j]);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float* a) {
+  uint4 o;
+  o.x = pack_bf16x2(a[0], a[1]);
+  o.y = pack_bf16x2(a[2], a[3]);
+  o.z = pack_bf16x2(a[4], a[5]);
+  o.w = pack_bf16x2(a[6], a[7]);
+  return o;
+}
+
+__global__ void ep_dispatch_kernel(const bf16* __restrict__ x, const int* __restrict__ idx,
+                                   const int* __restrict__ pos, const int* __restrict__ loc_off,
+                                   const int* __restrict__ dst_base, const int* __restrict__ keep_lim,
+                                   const float* __restrict__ wts, EpPeers xr, EpPeers meta, int* __restrict__ slot,
+                                   int TK, int K, int E, int El, int D, int me, StatusBlock* st) {
+  const int lane = threadIdx.x & 31;
+  for (int i = blockIdx.x * kWarps + (threadIdx.x >> 5); i < TK; i += gridDim.x * kWarps) {
+    const int e = idx[i];
+    const int p = pos[i];
+    int row = -1, owner = 0;
+    if (e >= 0 && e < E && p >= 0) {
+      const int lr = p - loc_off[e];
+      if (lr >= 0 && lr < keep_lim[e]) {
+        owner = e / El;
+        row = dst_base[e] + lr;
+        if (row >= xr.rows[owner]) {
+          if (lane == 0) report_error(st, STATUS_BAD_INDEX, row);
+          row = -1;
+        }
+      }
+    } else if (lane == 0 && (e < 0 || e >= E)) {
+      report_error(st, STATUS_BAD_INDEX, e);
+    }
+    if (lane == 0) slot[i] = row;
+    if (row < 0) continue;
+    const bf16* src = x + (long long)(i / K) * D;
+    bf16* dst = reinterpret_cast<bf16*>(xr.ptr[owner]) + (long long)row * D;
+    for (int c = lane * 8; c < D; c += 256)
+      *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+    if (lane == 0 && meta.ptr[owner] != 0ull) {
+      int4 m = make_int4(__float_as_int(wts[i]), me, i, 0);
+      reinterpret_cast<int4*>(meta.ptr[owner])[row] = m;
+    }
+  }
+}
+
+__global__ void ep_push_kernel(const bf16* __restrict__ src, const int* __restrict__ slot,
+                               const int* __restrict__ idx, EpPeers dst, int TK, int K, int El, int D,
+                               StatusBlock* st) {
+  const int lane = threadIdx.x & 31;
+  for (int i = blockIdx.x * kWarps + (threadIdx.x >> 5); i < TK; i += gridDim.x * kWarps) {
+    const int row = slot[i];
+    if (row < 0) continue;
+    const int owner = idx[i] / El;
+    if (owner < 0 || owner >= kEpMaxRanks || row >= dst.rows[owner]) {
+      if (lane == 0) report_error(st, STATUS_BAD_INDEX, row);
+      continue;
+    }
+    const bf16* s = src + (long long)(i / K) * D;
+    bf16* d = reinterpret_cast<bf16*>(dst.ptr[owner]) + (long long)row * D;
+    for (int c = lane * 8; c < D; c += 256)
+      *reinterpret_cast<uint4*>(d + c) = *reinterpret_cast<const uint4*>(s + c);
+  }
+}
+
+// One warp per token; the k remote rows of a 256-column chunk are loaded
+// before they are accumulated so that up to 8 NVLink loads are in flight per lane.
+template <int KMAX>
+__global__ void ep_combine_kernel(const int* __restrict__ slot, const int* __restrict__ idx,
+                                  const float* __restrict__ w, EpPeers y, const bf16* __restrict__ add,
+                                  bf16* __restrict__ out, int T, int K, int El, int D) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const bf16* rows[KMAX];
+  float wk[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    rows[k] = nullptr;
+    wk[k] = 0.f;
+    if (k < K) {
+      const int s = slot[(long long)t * K + k];
+      if (s >= 0) {
+        const int owner = idx[(long long)t * K + k] / El;
+        if (owner >= 0 && owner < kEpMaxRanks && s < y.rows[owner]) {
+          rows[k] = reinterpret_cast<const bf16*>(y.ptr[owner]) + (long long)s * D;
+          wk[k] = w != nullptr ? w[(long long)t * K + k] : 1.f;
+        }
+      }
+    }
+  }
+  for (int c = lane * 8; c < D; c += 256) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (add != nullptr) acc_add8(acc, *reinterpret_cast<const uint4*>(add + (long long)t * D + c), 1.f);
+    uint4 v[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k)
+      if (rows[k] != nullptr) v[k] = *reinterpret_cast<const uint4*>(rows[k] + c);
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k)
+      if (rows[k] != nullptr) acc_add8(acc, v[k], wk[k]);
+    *reinterpret_cast<uint4*>(out + (long long)t * D + c) = pack8(acc);
+  }
+}
+
+__device__ __forceinline__ int group_of(const int* off, int G, int r) {
+  int g = 0;
+  while (g + 1 < G && off[g + 1] <= r) ++g;
+  return g;
+}
+
+__global__ void ep_owner_bwd_kernel(bf16* __restrict__ dy, const bf16* __restrict__ y, const int4* __restrict__ meta,
+                                    const int* __restrict__ offsets, const int* __restrict__ kept, int El, EpPeers dw,
+                                    int rows, int D, StatusBlock* st) {
+  __shared__ int s_off[kEpMaxRanks * 32 + 1];
+  __shared__ int s_kept[kEpMaxRanks * 32];
+  for (int g = threadIdx.x; g <= El; g += blockDim.x) s_off[g] = offsets[g];
+  for (int g = threadIdx.x; g < El; g += blockDim.x) s_kept[g] = kept[g];
+  __syncthreads();
+  const int total = min(rows, s_off[El]);
+  const int lane = threadIdx.x & 31;
+  for (int r = blockIdx.x * kWarps + (threadIdx.x >> 5); r < total; r += gridDim.x * kWarps) {
+    const int g = group_of(s_off, El, r);
+    bf16* d = dy + (long long)r * D;
+    if (r - s_off[g] >= s_kept[g]) {
+      for (int c = lane * 8; c < D; c += 256) *reinterpret_cast<uint4*>(d + c) = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const int4 m = meta[r];
+    const float wr = __int_as_float(m.x);
+    const bf16* yr = y + (long long)r * D;
+    float dot = 0.f;
+    for (int c = lane * 8; c < D; c += 256) {
+      uint4 dv = *reinterpret_cast<const uint4*>(d + c);
+      uint4 yv = *reinterpret_cast<const uint4*>(yr + c);
+      const uint32_t* dq = reinterpret_cast<const uint32_t*>(&dv);
+      const uint32_t* yq = reinterpret_cast<const uint32_t*>(&yv);
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float d0 = bf16_lo(dq[j]), d1 = bf16_hi(dq[j]);
+        dot += d0 * bf16_lo(yq[j]) + d1 * bf16_hi(yq[j]);
+        o[2 * j] = d0 * wr;
+        o[2 * j + 1] = d1 * wr;
+      }
+      *reinterpret_cast<uint4*>(d + c) = pack8(o);
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) {
+      const int src = m.y, pair = m.z;
+      if (src >= 0 && src < kEpMaxRanks && pair >= 0 && pair < dw.rows[src])
+        reinterpret_cast<float*>(dw.ptr[src])[pair] = dot;
+      else
+        report_error(st, STATUS_BAD_INDEX, pair);
+    }
+  }
+}
+
+__global__ void ep_pad_rows_kernel(bf16* __restrict__ x, int4* __restrict__ meta, const int* __restrict__ offsets,
+                                   const int* __restrict__ kept, int El, int rows, int D) {
+  // one block per local expert group: zero rows [off + kept, next off)
+  const int g = blockIdx.x;
+  if (g >= El) return;
+  const int r0 = offsets[g] + kept[g];
+  const int r1 = min(offsets[g + 1], rows);
+  const int lane = threadIdx.x & 31;
+  for (int r = r0 + (threadIdx.x >> 5); r < r1; r += kWarps) {
+    bf16* d = x + (long long)r * D;
+    for (int c = lane * 8; c < D; c += 256) *reinterpret_cast<uint4*>(d + c) = make_uint4(0, 0, 0, 0);
+    if (meta != nullptr && lane == 0) meta[r] = make_int4(0, -1, -1, 0);
+  }
+}
+
+__global__ void ep_barrier_kernel(EpPeers sig, int me, int n, unsigned epoch, StatusBlock* st) {
+  const int t = threadIdx.x;
+  if (t >= n) return;
+  // release: everything this GPU wrote before this kernel (previous kernels on
+  // the stream, including stores to peers) is visible before the flag.
+  __threadfence_system();
+  unsigned* peer_flag = reinterpret_cast<unsigned*>(sig.ptr[t]) + me;
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer_flag), "r"(epoch) : "memory");
+  const unsigned* mine = reinterpret_cast<const unsigned*>(sig.ptr[me]) + t;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+    if ((int)(v - epoch) >= 0) break;
+    if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) {
+      report_error(st, STATUS_TIMEOUT_PEER_FLAG, t);
+      break;
+    }
+  }
+  __threadfence_system();
+}
+
+int grid_for(long long work_warps) {
+  long long b = (work_warps + kWarps - 1) / kWarps;
+  return (int)std::max(1ll, std::min(b, 148ll * 16));
+}
+
+}  // namespace
+
+void ep_dispatch(const void* x, const int* idx, const int* pos, const int* loc_off, const int* dst_base,
+                 const int* keep_lim, const float* wts, const EpPeers& xr, const EpPeers& meta, int* slot, int T,
+                 int K, int E, int El, int D, int me, cudaStream_t s) {
+  const int TK = T * K;
+  if (TK == 0) return;
+  ep_dispatch_kernel<<<grid_for(TK), kWarps * 32, 0, s>>>((const bf16*)x, idx, pos, loc_off, dst_base, keep_lim,
+                                                          wts, xr, meta, slot, TK, K, E, El, D, me,
+                                                          (StatusBlock*)status_ptr());
+}
+
+void ep_push(const void* src, const int* slot, const int* idx, const EpPeers& dst, int T, int K, int El, int D,
+             cudaStream_t s) {
+  const int TK = T * K;
+  if (TK == 0) return;
+  ep_push_kernel<<<grid_for(TK), kWarps * 32, 0, s>>>((const bf16*)src, slot, idx, dst, TK, K, El, D,
+                                                      (StatusBlock*)status_ptr());
+}
+
+void ep_combine(const int* slot, const int* idx, const float* w, const EpPeers& y, const void* add, void* out, int T,
+                int K, int El, int D, cudaStream_t s) {
+  if (T == 0) return;
+  const int grid = (T + kWarps - 1) / kWarps;
+  if (K <= 4)
+    ep_combine_kernel<4><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D);
+  else if (K <= 8)
+    ep_combine_kernel<8><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D);
+  else
+    ep_combine_kernel<16><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D);
+}
+
+void ep_owner_bwd(void* dy, const void* y, const void* meta, const int* offsets, const int* kept, int El,
+                  const EpPeers& dw, int rows, int D, cudaStream_t s) {
+  if (rows == 0) return;
+  ep_owner_bwd_kernel<<<grid_for(rows), kWarps * 32, 0, s>>>((bf16*)dy, (const bf16*)y, (const int4*)meta, offsets,
+                                                              kept, El, dw, rows, D, (StatusBlock*)status_ptr());
+}
+
+void ep_pad_rows(void* x, void* meta, const int* offsets, const int* kept, int El, int rows, int D, cudaStream_t s) {
+  if (El == 0) return;
+  ep_pad_rows_kernel<<<El, kWarps * 32, 0, s>>>((bf16*)x, (int4*)meta, offsets, kept, El, rows, D);
+}
+
+void ep_barrier(const EpPeers& sig, int me, int n, unsigned epoch, cudaStream_t s) {
+  ep_barrier_kernel<<<1, 32, 0, s>>>(sig, me, n, epoch, (StatusBlock*)status_ptr());
+}
+
+}  // namespace omni

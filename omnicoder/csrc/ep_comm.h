@@ -1,0 +1,41 @@
+// Expert-parallel token exchange over NVLink peer memory (see ep_comm.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace omni {
+
+constexpr int kEpMaxRanks = 8;
+
+// Per-rank device addresses (valid in this process: peer-mapped symmetric
+// memory) and the row capacity of each rank's region.
+struct EpPeers {
+  unsigned long long ptr[kEpMaxRanks];
+  int rows[kEpMaxRanks];
+};
+
+// Push every kept (token, k) pair's row of x [T, D] into row
+// dst_base[e] + (pos - loc_off[e]) of its owner's receive region (owner = e / El);
+// meta (optional) receives {w bits, source rank, pair index, 0} per row.
+// slot[pair] = destination row, -1 when dropped (capacity) or invalid.
+void ep_dispatch(const void* x, const int* idx, const int* pos, const int* loc_off, const int* dst_base,
+                 const int* keep_lim, const float* wts, const EpPeers& xr, const EpPeers& meta, int* slot, int T,
+                 int K, int E, int El, int D, int me, cudaStream_t s);
+// Push rows of src [T, D] along a slot table computed by ep_dispatch.
+void ep_push(const void* src, const int* slot, const int* idx, const EpPeers& dst, int T, int K, int El, int D,
+             cudaStream_t s);
+// out[t] = add[t] + sum_k w[t,k] * Y_owner[slot[t,k]] (w == nullptr: weight 1); peer loads.
+void ep_combine(const int* slot, const int* idx, const float* w, const EpPeers& y, const void* add, void* out, int T,
+                int K, int El, int D, cudaStream_t s);
+// Owner side of the combine backward, over the local receive rows:
+//   dot = <dy[r], y[r]> -> written to dw_src_rank[pair] (peer store);  dy[r] *= w[r];
+// padding rows (beyond kept[g] in each 128-padded group) are zeroed.
+void ep_owner_bwd(void* dy, const void* y, const void* meta, const int* offsets, const int* kept, int El,
+                  const EpPeers& dw, int rows, int D, cudaStream_t s);
+// Zero the padding rows of a receive region (and mark their meta invalid).
+void ep_pad_rows(void* x, void* meta, const int* offsets, const int* kept, int El, int rows, int D, cudaStream_t s);
+// Signal every rank and wait until every rank has signalled `epoch` (bounded wait).
+void ep_barrier(const EpPeers& sig, int me, int n, unsigned epoch, cudaStream_t s);
+
+}  // namespace omni

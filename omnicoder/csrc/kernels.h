@@ -13,6 +13,7 @@ namespace omni {
 
 void* status_ptr();
 void register_kernels(pybind11::module_& m);
+void register_ep(pybind11::module_& m);
 
 // ---- normalisation -------------------------------------------------------
 // y = rmsnorm(x (+ r)) * w ; h = x + r is written when r != nullptr.

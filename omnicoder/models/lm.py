@@ -192,14 +192,24 @@ class DenseFFN(nn.Module):
 
 
 class MoEFFN(nn.Module):
-    def __init__(self, cfg: ModelConfig):
+    """Routed SwiGLU experts (+ shared experts).  With an expert-parallel layout
+    (`ep`, see omnicoder.parallel.expert_data) this rank holds experts
+    [lo, hi) of the group; the full stack is still drawn from the RNG so that
+    every layout initialises identically to the single-device model."""
+
+    def __init__(self, cfg: ModelConfig, ep=None):
         super().__init__()
         m = cfg.moe
         D = cfg.d_model
         self.cfg = cfg
+        self.ep = ep
         self.router = _init(_empty(m.n_experts, D), cfg.init_std)
+        lo, hi = ep.expert_slice(m.n_experts) if ep is not None else (0, m.n_experts)
         self.w13 = _init(_empty(m.n_experts, 2 * m.ffn_dim, D), cfg.init_std)
         self.w2 = _init(_empty(m.n_experts, D, m.ffn_dim), cfg.init_std)
+        if ep is not None:
+            self.w13 = nn.Parameter(self.w13.data[lo:hi].clone())
+            self.w2 = nn.Parameter(self.w2.data[lo:hi].clone())
         self.shared = DenseFFN(D, m.ffn_dim * m.n_shared_experts, cfg.init_std) if m.n_shared_experts > 0 else None
         self.aux_grad_scale = 1.0
 
@@ -207,18 +217,25 @@ class MoEFFN(nn.Module):
         m = self.cfg.moe
         T = y.shape[0]
         base = self.shared(y, h)[0] if self.shared is not None else h
+        if self.ep is not None:
+            from ..parallel.expert import ep_moe_ffn
+            world = self.ep.world
+            out, aux = ep_moe_ffn(y, self.router, self.w13, self.w2, m.top_k, self.ep.ep, m.capacity(T * world),
+                                  m.renorm_topk, m.aux_loss_alpha, m.z_loss_beta, add=base,
+                                  aux_grad_scale=self.aux_grad_scale)
+            return out, aux
         out, aux = moe_ffn(y, self.router, self.w13, self.w2, m.top_k, m.capacity(T), m.renorm_topk,
                            m.aux_loss_alpha, m.z_loss_beta, add=base, aux_grad_scale=self.aux_grad_scale)
         return out, aux
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: ModelConfig, layer: int):
+    def __init__(self, cfg: ModelConfig, layer: int, ep=None):
         super().__init__()
         self.attn_norm = Norm(cfg.d_model, cfg.norm, cfg.norm_eps)
         self.attn = MLAttention(cfg) if cfg.attn.kind == "mla" else GQAttention(cfg)
         self.ffn_norm = Norm(cfg.d_model, cfg.norm, cfg.norm_eps)
-        self.ffn = MoEFFN(cfg) if cfg.is_moe_layer(layer) else DenseFFN(cfg.d_model, cfg.ffn_dim, cfg.init_std)
+        self.ffn = MoEFFN(cfg, ep) if cfg.is_moe_layer(layer) else DenseFFN(cfg.d_model, cfg.ffn_dim, cfg.init_std)
 
     def forward(self, h, rope, positions, seq):
         h = self.attn(self.attn_norm(h), h, rope, positions, seq)
@@ -234,12 +251,12 @@ class OmniLM(nn.Module):
     `loss` (CE + auxiliary), `ce`, `aux` and, without labels, `logits` of the last
     position (or all positions with `all_logits=True`)."""
 
-    def __init__(self, cfg: ModelConfig):
+    def __init__(self, cfg: ModelConfig, ep=None):
         super().__init__()
         self.cfg = cfg
         D, V = cfg.d_model, cfg.vocab_size
         self.embed = _init(_empty(V, D), cfg.init_std)
-        self.blocks = nn.ModuleList([Block(cfg, i) for i in range(cfg.n_layers)])
+        self.blocks = nn.ModuleList([Block(cfg, i, ep) for i in range(cfg.n_layers)])
         self.norm_f = Norm(D, cfg.norm, cfg.norm_eps)
         self.lm_head = None if cfg.tie_embeddings else _init(_empty(V, D), cfg.init_std)
         self.mtp_heads = nn.ParameterList([_init(_empty(V, D), cfg.init_std) for _ in range(cfg.mtp_heads)])
@@ -344,9 +361,11 @@ class OmniLM(nn.Module):
         return self.load_state_dict(merged, strict=strict)
 
 
-def build_model(cfg: ModelConfig, device="cpu", dtype=None, seed: int | None = 0) -> OmniLM:
+def build_model(cfg: ModelConfig, device="cpu", dtype=None, seed: int | None = 0, ep=None) -> OmniLM:
     """Random-init model N(0, init_std) created directly on `device` (bf16 on CUDA,
-    fp32 on CPU by default)."""
+    fp32 on CPU by default).  `ep`: an expert-parallel layout
+    (omnicoder.parallel.expert_data.ExpertDataParallel) -- the model then holds
+    only this rank's routed experts."""
     global _FACTORY
     if seed is not None:
         torch.manual_seed(seed)
@@ -357,7 +376,7 @@ def build_model(cfg: ModelConfig, device="cpu", dtype=None, seed: int | None = 0
     old = _FACTORY
     _FACTORY = {"device": torch.device(device), "dtype": dtype}
     try:
-        m = OmniLM(cfg)
+        m = OmniLM(cfg, ep)
     finally:
         _FACTORY = old
     m.rope.to(device)

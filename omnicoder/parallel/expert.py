@@ -1,0 +1,312 @@
+"""Expert parallelism: routed experts sharded over the ranks of a group.
+
+Rank r owns experts [r * El, (r + 1) * El) (El = E / world).  Each rank routes
+its own tokens; every (token, k) pair travels to the owner of its expert,
+is processed by the owner's grouped SwiGLU GEMMs and travels back to be
+combined with the routing weight.
+
+Receive layout (identical on every rank, computed from the all-gathered
+per-(source, expert) counts C[s, e]):
+  owner r holds its El experts back to back; expert e's segment holds the
+  kept rows of source 0, then source 1, ... in token order, padded to a
+  multiple of 128 rows (the grouped tcgen05 GEMM's tile height).
+With a capacity (tokens per expert, over the whole group) the first
+`capacity` pairs of each expert in (source rank, token) order are kept --
+the same pairs a single process keeps for the concatenated batch.
+
+Two transports implement the same layout:
+  * "p2p" (CUDA): the sm_100a kernels of ep_comm.cu over a symmetric
+    peer-mapped arena: dispatch fused with the permutation (peer stores),
+    combine fused with the weighted sum (peer loads), owner-side routing-weight
+    gradient, device barriers with bounded waits.
+  * "nccl" / CPU: torch.distributed.all_to_all_single with plain PyTorch
+    expert math -- the NCCL + cuBLAS baseline on GPUs and the gloo path of the
+    CPU tests.
+
+The reference has no expert parallelism (its EP launcher only sets an
+environment variable that the MoE layer in use never reads:
+src/omnicoder/tools/torchrun_ep.py:36-38, src/omnicoder/modeling/moe_layer.py).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from ..ops import _ext
+from ..ops.gemm import EPI_BF16, EPI_SWIGLU, EPI_SWIGLU_BWD, deinterleave_cols, mm_nn, mm_nt, mm_tn
+from ..ops.moe import cap_rows_for, route_torch
+
+
+# ----------------------------------------------------------------------------
+# Layout (host, numpy): identical on every rank
+# ----------------------------------------------------------------------------
+@dataclass
+class EPLayout:
+    kept: np.ndarray          # [N, E] rows of source s kept for expert e
+    dst_base: np.ndarray      # [E] first row of this rank's pairs inside expert e's segment (on its owner)
+    keep_lim: np.ndarray      # [E] pairs of this rank kept per expert
+    offs_local: np.ndarray    # [El + 1] padded segment offsets of this rank's receive buffer
+    kept_local: np.ndarray    # [El] rows (before padding) of each local expert
+    rows: list                # [N] padded receive rows of every rank
+    pairs: list               # [N] T_s * K of every rank (size of its routing-weight gradient)
+
+
+def ep_layout(C: np.ndarray, me: int, El: int, capacity: int = 0) -> EPLayout:
+    C = np.asarray(C, dtype=np.int64)
+    N, E = C.shape
+    before = np.cumsum(C, axis=0) - C                         # rows of earlier sources, per expert
+    if capacity > 0:
+        kept = np.clip(np.minimum(C, capacity - before), 0, None)
+    else:
+        kept = C.copy()
+    seg = kept.sum(0)                                         # [E]
+    seg_pad = ((seg + 127) // 128 * 128).reshape(N, El)
+    seg_base = (np.cumsum(seg_pad, axis=1) - seg_pad).reshape(E)
+    kept_before = np.cumsum(kept, axis=0) - kept
+    dst_base = seg_base + kept_before[me]
+    offs_local = np.concatenate([[0], np.cumsum(seg_pad[me])])
+    return EPLayout(kept=kept, dst_base=dst_base, keep_lim=kept[me].copy(), offs_local=offs_local,
+                    kept_local=seg.reshape(N, El)[me].copy(), rows=[int(x) for x in seg_pad.sum(1)],
+                    pairs=[int(x) for x in C.sum(1)])
+
+
+def local_ranks(idx: torch.Tensor, E: int) -> torch.Tensor:
+    """Rank of each (token, k) pair among this rank's pairs of the same expert, in token order."""
+    flat = idx.reshape(-1).long()
+    onehot = F.one_hot(flat, E)
+    return (onehot.cumsum(0) - 1).gather(1, flat.unsqueeze(1)).squeeze(1).view_as(idx)
+
+
+# ----------------------------------------------------------------------------
+# Context
+# ----------------------------------------------------------------------------
+class EPContext:
+    """Expert-parallel group of one process: rank, world, transport, arena."""
+
+    def __init__(self, group=None, transport: str = "auto", device=None, arena_bytes: int = 1 << 30):
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        self.device = torch.device(device) if device is not None else (
+            torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
+        if transport == "auto":
+            transport = "p2p" if self.device.type == "cuda" else "nccl"
+        self.transport = transport
+        self.arena = None
+        self._arena_bytes = arena_bytes
+        self.stats = {"host_syncs": 0}
+
+    def experts_of(self, E: int) -> tuple[int, int]:
+        if E % self.world:
+            raise ValueError(f"{E} experts do not divide over {self.world} expert-parallel ranks")
+        El = E // self.world
+        return self.rank * El, (self.rank + 1) * El
+
+    def ensure_arena(self):
+        if self.arena is None:
+            from .symm import SymmArena
+            self.arena = SymmArena(self.group, self.device, self._arena_bytes)
+        return self.arena
+
+    def begin_step(self):
+        """Start of a micro-step: every rank has finished reading the previous
+        step's regions (device barrier) before they are handed out again."""
+        if self.arena is not None:
+            self.arena.barrier()
+            self.arena.reset()
+
+    def all_gather_counts(self, counts: torch.Tensor) -> np.ndarray:
+        """[E] int32 per rank -> host [N, E] (one small collective + one host sync)."""
+        out = [torch.empty_like(counts) for _ in range(self.world)]
+        dist.all_gather(out, counts.contiguous(), group=self.group)
+        self.stats["host_syncs"] += 1
+        return torch.stack(out).cpu().numpy()
+
+
+# ----------------------------------------------------------------------------
+# p2p transport (CUDA, fused kernels over the symmetric arena)
+# ----------------------------------------------------------------------------
+def _i32(dev, *arrays) -> list[torch.Tensor]:
+    """Upload int32 arrays with one host->device copy."""
+    flat = np.concatenate([np.asarray(a, dtype=np.int32).ravel() for a in arrays])
+    t = torch.from_numpy(flat).pin_memory().to(dev, non_blocking=True)
+    out, o = [], 0
+    for a in arrays:
+        n = int(np.asarray(a).size)
+        out.append(t[o:o + n])
+        o += n
+    return out
+
+
+class _EPMoEP2P(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta, gs):
+        C = _ext.load()
+        arena = ep.ensure_arena()
+        x = x.contiguous()
+        T, D = x.shape
+        E = router_w.shape[0]
+        El = w13.shape[0]
+        F2 = w13.shape[1]
+        me = ep.rank
+        logits = mm_nt(x, router_w, out_f32=True)
+        idx, wts, probs = C.router_topk(logits, k, renorm)
+        counts, loc_off, pos, _ = C.moe_plan(idx, E, 0, cap_rows_for(T, k, E, 0))
+        lay = ep_layout(ep.all_gather_counts(counts), me, El, capacity)
+        rows = [max(r, 128) for r in lay.rows]
+        dst_base, keep_lim, offs_local, kept_local = _i32(x.device, lay.dst_base, lay.keep_lim, lay.offs_local,
+                                                           lay.kept_local)
+        rx = arena.alloc([r * D * 2 for r in rows])
+        rmeta = arena.alloc([r * 16 for r in rows])
+        slot = C.ep_dispatch(x, idx, pos, loc_off, dst_base, keep_lim, wts, rx.ptrs, rmeta.ptrs, rows, El, me)
+        R = rows[me]
+        x_recv = rx.view(torch.bfloat16, R, D)
+        meta = rmeta.view(torch.int32, R, 4)
+        C.ep_pad_rows(x_recv, meta, offs_local, kept_local)
+        arena.barrier()                                       # all pairs have landed
+        act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)
+        H = torch.empty(R, F2, device=x.device, dtype=torch.bfloat16)
+        C.gemm_grouped_m(x_recv, w13, offs_local, act, False, EPI_SWIGLU, 1.0, None, H, 256, R)
+        ry = arena.alloc([r * D * 2 for r in rows])
+        y_recv = ry.view(torch.bfloat16, R, D)
+        C.gemm_grouped_m(act, w2, offs_local, y_recv, False, EPI_BF16, 1.0, None, None, 256, R)
+        arena.barrier()                                       # every owner's outputs are ready
+        out = C.ep_combine(slot, idx, wts, ry.ptrs, rows, El, D, None if add is None else add.contiguous())
+        ctx.save_for_backward(x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, offs_local, kept_local,
+                              x_recv, meta, H, act, y_recv)
+        ctx.ep, ctx.ry, ctx.rows, ctx.lay = ep, ry, rows, lay
+        ctx.cfg = (k, renorm, aux_alpha, z_beta, gs, add is not None)
+        aux = x.new_zeros((), dtype=torch.float32)
+        if aux_alpha > 0:
+            aux = aux + aux_alpha * E * ((counts.float() / (T * k)) * probs.mean(0)).sum()
+        if z_beta > 0:
+            lse = torch.logsumexp(logits, dim=-1)
+            aux = aux + z_beta * (lse * lse).mean()
+        ctx.mark_non_differentiable(aux)
+        return out, aux
+
+    @staticmethod
+    def backward(ctx, dout, daux):
+        (x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, offs_local, kept_local, x_recv, meta, H, act,
+         y_recv) = ctx.saved_tensors
+        k, renorm, aux_alpha, z_beta, gs, has_add = ctx.cfg
+        ep, rows, lay = ctx.ep, ctx.rows, ctx.lay
+        arena = ep.arena
+        C = _ext.load()
+        T, D = x.shape
+        El = w13.shape[0]
+        R = rows[ep.rank]
+        dout = dout.contiguous()
+        rdy = arena.alloc([r * D * 2 for r in rows])
+        rdw = arena.alloc([max(p, 1) * 4 for p in lay.pairs])
+        dwts = rdw.view(torch.float32, T, k)
+        dwts.zero_()                                          # dropped pairs keep a zero gradient
+        C.ep_push(dout, slot, idx, rdy.ptrs, rows, El)
+        arena.barrier()                                       # all output gradients have landed
+        dy_recv = rdy.view(torch.bfloat16, R, D)
+        C.ep_owner_bwd(dy_recv, y_recv, meta, offs_local, kept_local, rdw.ptrs, [max(p, 1) for p in lay.pairs])
+        dH = torch.empty_like(H)
+        C.gemm_grouped_m(dy_recv, w2, offs_local, dH, True, EPI_SWIGLU_BWD, 1.0, H, None, 256, R)
+        dw2 = torch.empty_like(w2)
+        C.gemm_grouped_k(dy_recv, act, offs_local, dw2, EPI_BF16, 1.0, 256)
+        rdx = arena.alloc([r * D * 2 for r in rows])
+        dx_recv = rdx.view(torch.bfloat16, R, D)
+        C.gemm_grouped_m(dH, w13, offs_local, dx_recv, True, EPI_BF16, 1.0, None, None, 256, R)
+        dw13 = torch.empty_like(w13)
+        C.gemm_grouped_k(dH, x_recv, offs_local, dw13, EPI_BF16, 1.0, 256)
+        arena.barrier()                                       # input gradients and weight gradients are ready
+        dlogits, _ = C.router_bwd(logits, probs, idx, dwts, counts, renorm, aux_alpha * gs, z_beta * gs)
+        dx_router = mm_nn(dlogits, router_w)
+        dx = C.ep_combine(slot, idx, None, rdx.ptrs, rows, El, D, dx_router)
+        drouter = mm_tn(dlogits, x)
+        return (dx, drouter, dw13, dw2, (dout if has_add else None), None, None, None, None, None, None, None)
+
+
+# ----------------------------------------------------------------------------
+# all_to_all transport (NCCL baseline on CUDA, gloo on CPU): autograd through torch ops
+# ----------------------------------------------------------------------------
+class _A2A(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, send, recv, group):
+        ctx.send, ctx.recv, ctx.group = send, recv, group
+        out = x.new_empty((sum(recv),) + tuple(x.shape[1:]))
+        dist.all_to_all_single(out, x.contiguous(), recv, send, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        out = g.new_empty((sum(ctx.send),) + tuple(g.shape[1:]))
+        dist.all_to_all_single(out, g.contiguous(), ctx.send, ctx.recv, group=ctx.group)
+        return out, None, None, None
+
+
+def _a2a_meta(t: torch.Tensor, send, recv, group) -> torch.Tensor:
+    out = t.new_empty((sum(recv),) + tuple(t.shape[1:]))
+    dist.all_to_all_single(out, t.contiguous(), recv, send, group=group)
+    return out
+
+
+def _ep_moe_a2a(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta):
+    T, D = x.shape
+    E = router_w.shape[0]
+    El = w13.shape[0]
+    N, me = ep.world, ep.rank
+    logits = x.float() @ router_w.float().t()
+    idx, w, probs = route_torch(logits, k, renorm)
+    counts = torch.bincount(idx.reshape(-1), minlength=E).to(torch.int32)
+    lay = ep_layout(ep.all_gather_counts(counts), me, El, capacity)
+    lr = local_ranks(idx, E)
+    flat_e = idx.reshape(-1)
+    keep_lim = torch.as_tensor(lay.keep_lim, device=x.device)
+    dst_base = torch.as_tensor(lay.dst_base, device=x.device)
+    keep = lr.reshape(-1) < keep_lim[flat_e]
+    pair = torch.nonzero(keep).squeeze(1)
+    e_k = flat_e[pair]
+    owner = e_k // El
+    row = dst_base[e_k] + lr.reshape(-1)[pair]
+    order = torch.argsort(owner * (1 << 40) + row)          # by owner, then destination row
+    pair, owner, row = pair[order], owner[order], row[order]
+    send = torch.bincount(owner, minlength=N).tolist()
+    recv_counts = lay.kept[:, me * El:(me + 1) * El].sum(1)
+    recv = [int(c) for c in recv_counts]
+    xs = x.index_select(0, pair // k)
+    xr = _A2A.apply(xs, send, recv, ep.group)
+    rr = _a2a_meta(row, send, recv, ep.group).long()
+    R = lay.rows[me]
+    x_recv = x.new_zeros(R, D).index_copy(0, rr, xr)
+    segs = []
+    for el in range(El):
+        a, b = int(lay.offs_local[el]), int(lay.offs_local[el + 1])
+        h = x_recv[a:b] @ w13[el].t()
+        g, u = deinterleave_cols(h)
+        segs.append((F.silu(g.float()) * u.float()).to(x.dtype) @ w2[el].t())
+    y_recv = torch.cat(segs, 0) if segs else x.new_zeros(0, D)
+    yb = _A2A.apply(y_recv.index_select(0, rr), recv, send, ep.group)
+    wk = w.reshape(-1)[pair].unsqueeze(1)
+    out = torch.zeros(T, D, dtype=torch.float32, device=x.device).index_add(0, pair // k, yb.float() * wk)
+    if add is not None:
+        out = out + add.float()
+    aux = x.new_zeros((), dtype=torch.float32)
+    if aux_alpha > 0:
+        f = (counts.float() / (T * k)).detach()
+        aux = aux + aux_alpha * E * (f * probs.mean(0)).sum()
+    if z_beta > 0:
+        lse = torch.logsumexp(logits, dim=-1)
+        aux = aux + z_beta * (lse * lse).mean()
+    return out.to(x.dtype), aux
+
+
+def ep_moe_ffn(x: torch.Tensor, router_w: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, k: int, ep: EPContext,
+               capacity: int = 0, renorm: bool = True, aux_alpha: float = 0.0, z_beta: float = 0.0,
+               add: torch.Tensor | None = None, aux_grad_scale: float = 1.0):
+    """Expert-parallel routed SwiGLU FFN.  x [T, D] local tokens; router_w [E, D]
+    (replicated); w13 [El, 2F, D] / w2 [El, D, F] this rank's experts.  `capacity`
+    is the per-expert limit over the whole group (0: dropless)."""
+    if ep.transport == "p2p" and x.is_cuda:
+        return _EPMoEP2P.apply(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta,
+                               aux_grad_scale)
+    return _ep_moe_a2a(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta)

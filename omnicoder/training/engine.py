@@ -55,9 +55,9 @@ class Trainer:
         chunks_ids = ids.chunk(accum, dim=0)
         chunks_lab = labels.chunk(accum, dim=0)
         loss_sum = ce_sum = aux_sum = None
-        for ci, cl in zip(chunks_ids, chunks_lab):
+        for mi, (ci, cl) in enumerate(zip(chunks_ids, chunks_lab)):
             if self.parallel is not None:
-                self.parallel.before_backward(self.model)
+                self.parallel.before_forward(mi, len(chunks_ids))
             out = self.model(ci, labels=cl, assume_all_valid=assume_all_valid)
             loss = out["loss"] / accum
             loss.backward()

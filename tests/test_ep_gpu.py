@@ -1,0 +1,193 @@
+"""Expert-parallel MoE layer over NVLink peer memory on 2 GPUs (one process per
+GPU, NCCL for the plumbing): output, input gradient, router gradient and the
+local experts' weight gradients of the fused p2p kernels must match the
+single-GPU fused MoE layer on the concatenated tokens; the all_to_all (NCCL)
+transport must agree as well.  A full expert x data parallel training step must
+give the same loss as one GPU on the whole batch.
+
+Runs as child processes with NVLS off; every device wait in the kernels is
+bounded and a timeout shows up in the device status word checked here."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _close(a, b, tol):
+    a, b = a.float(), b.float()
+    err = (a - b).abs().max().item()
+    ref = b.abs().max().item() + 1e-6
+    return err / ref < tol, err / ref
+
+
+def _layer_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    out = {}
+    try:
+        from omnicoder.ops import _ext, moe_ffn
+        from omnicoder.parallel.expert import EPContext, ep_moe_ffn
+
+        C = _ext.load()
+        T, D, E, F, K = 1024, 512, 8, 256, 2
+        g = torch.Generator(device="cpu").manual_seed(7)
+        xs = (torch.randn(world * T, D, generator=g) * 0.5).to(dev, torch.bfloat16)
+        wr = (torch.randn(E, D, generator=g) * 0.05).to(dev, torch.bfloat16)
+        w13 = (torch.randn(E, 2 * F, D, generator=g) * 0.05).to(dev, torch.bfloat16)
+        w2 = (torch.randn(E, D, F, generator=g) * 0.05).to(dev, torch.bfloat16)
+        dys = (torch.randn(world * T, D, generator=g) * 0.1).to(dev, torch.bfloat16)
+        El = E // world
+        lo, hi = rank * El, (rank + 1) * El
+        for cap in (0, 300):
+            # single-GPU reference on all tokens
+            xa = xs.clone().requires_grad_(True)
+            ra = wr.clone().requires_grad_(True)
+            a13 = w13.clone().requires_grad_(True)
+            a2 = w2.clone().requires_grad_(True)
+            ya, _ = moe_ffn(xa, ra, a13, a2, K, cap, True)
+            ya.backward(dys)
+            for transport in ("p2p", "nccl"):
+                ep = EPContext(dist.group.WORLD, transport=transport, device=dev, arena_bytes=64 << 20)
+                xb = xs[rank * T:(rank + 1) * T].clone().requires_grad_(True)
+                rb = wr.clone().requires_grad_(True)
+                b13 = w13[lo:hi].clone().requires_grad_(True)
+                b2 = w2[lo:hi].clone().requires_grad_(True)
+                ep.begin_step()
+                yb, _ = ep_moe_ffn(xb, rb, b13, b2, K, ep, capacity=cap, renorm=True)
+                yb.backward(dys[rank * T:(rank + 1) * T])
+                torch.cuda.synchronize()
+                code = C.status()[0]
+                C.status_reset()
+                # the router gradient of one rank covers its tokens only: sum over ranks
+                drb = rb.grad.float().clone()
+                dist.all_reduce(drb)
+                sl = slice(rank * T, (rank + 1) * T)
+                out[(cap, transport)] = {
+                    "status": code,
+                    "y": _close(yb, ya[sl], 2e-2),
+                    "dx": _close(xb.grad, xa.grad[sl], 3e-2),
+                    "drouter": _close(drb, ra.grad, 3e-2),
+                    "dw13": _close(b13.grad, a13.grad[lo:hi], 3e-2),
+                    "dw2": _close(b2.grad, a2.grad[lo:hi], 3e-2),
+                }
+        q.put((rank, out))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _step_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig, TrainConfig
+        from omnicoder.models.lm import build_model
+        from omnicoder.ops import _ext
+        from omnicoder.parallel.expert_data import ExpertDataParallel
+        from omnicoder.training.engine import Trainer, synthetic_batch
+
+        cfg = ModelConfig(name="ep_step", vocab_size=4096, d_model=512, n_layers=2, n_heads=4, ffn_dim=512,
+                          tie_embeddings=False, max_seq_len=512,
+                          attn=AttentionConfig(kind="mla", kv_lora_rank=256, qk_rope_dim=64, qk_nope_dim=128,
+                                               v_head_dim=128),
+                          moe=MoEConfig(n_experts=8, top_k=2, ffn_dim=256, n_shared_experts=1, aux_loss_alpha=0.0))
+        tc = TrainConfig(lr=1e-3, warmup_steps=0, max_steps=10, grad_clip=1.0)
+        ids, lab = synthetic_batch(2 * world, 256, cfg.vocab_size, seed=3, step=0, device=dev)
+        ref = build_model(cfg, device=dev, seed=0)
+        rt = Trainer(ref, tc)
+        ref_losses = [float(rt.step(ids, lab).loss) for _ in range(3)]
+        del rt, ref
+        par = ExpertDataParallel(dist.group.WORLD, arena_bytes=64 << 20)
+        model = build_model(cfg, device=dev, seed=0, ep=par)
+        tr = Trainer(model, tc, par)
+        mine = ids.chunk(world)[rank], lab.chunk(world)[rank]
+        losses = []
+        for _ in range(3):
+            l = tr.step(*mine).loss.detach().float()
+            dist.all_reduce(l)
+            losses.append(float(l) / world)
+        torch.cuda.synchronize()
+        C = _ext.load()
+        code = C.status()[0]
+        C.status_reset()
+        q.put((rank, {"ref": ref_losses, "ep": losses, "status": code}))
+    except Exception as e:
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(target, world=2, timeout=600):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, v = q.get(timeout=timeout)
+            res[r] = v
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return res
+
+
+def _need_gpus(n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+
+
+def test_ep_layer_p2p_matches_single_gpu():
+    _need_gpus(2)
+    res = _run(_layer_worker)
+    for rank, out in res.items():
+        assert isinstance(out, dict), out
+        for key, checks in out.items():
+            assert checks["status"] == 0, (rank, key, checks)
+            for name, (ok, err) in ((k, v) for k, v in checks.items() if k != "status"):
+                assert ok, (rank, key, name, err)
+
+
+def test_ep_dp_train_step_matches_single_gpu():
+    _need_gpus(2)
+    res = _run(_step_worker)
+    for rank, out in res.items():
+        assert isinstance(out, dict), out
+        assert out["status"] == 0
+        for a, b in zip(out["ref"], out["ep"]):
+            assert abs(a - b) < 2e-2 * max(1.0, abs(a)), out
