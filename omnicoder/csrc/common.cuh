@@ -2,7 +2,7 @@
 //
 // Everything here is hand-written inline PTX for Blackwell (sm_100a):
 //   * mbarrier init / arrive / expect_tx / bounded try_wait
-//   * TMA tiled loads (cp.async.bulk.tensor, never with .multicast::cluster)
+//   * TMA tiled loads (cp.async.bulk.tensor, single-CTA destination only)
 //   * tcgen05: TMEM alloc/dealloc, mma (kind::f16), commit, ld, fences
 //   * UMMA shared-memory and instruction descriptors
 //

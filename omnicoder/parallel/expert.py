@@ -177,7 +177,11 @@ class _EPMoEP2P(torch.autograd.Function):
         arena.barrier()                                       # every owner's outputs are ready
         out = C.ep_combine(slot, idx, wts, ry.ptrs, rows, El, D, None if add is None else add.contiguous())
         ctx.save_for_backward(x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, offs_local, kept_local,
-                              x_recv, meta, H, act, y_recv)
+                              H, act)
+        # arena regions are views of one shared buffer (one autograd version counter for all
+        # of them), so they are kept on ctx instead of going through save_for_backward; the
+        # arena is not recycled before this backward has run (reset at the next micro-step)
+        ctx.x_recv, ctx.meta, ctx.y_recv = x_recv, meta, y_recv
         ctx.ep, ctx.ry, ctx.rows, ctx.lay = ep, ry, rows, lay
         ctx.cfg = (k, renorm, aux_alpha, z_beta, gs, add is not None)
         aux = x.new_zeros((), dtype=torch.float32)
@@ -191,8 +195,9 @@ class _EPMoEP2P(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout, daux):
-        (x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, offs_local, kept_local, x_recv, meta, H, act,
-         y_recv) = ctx.saved_tensors
+        (x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, offs_local, kept_local, H,
+         act) = ctx.saved_tensors
+        x_recv, meta, y_recv = ctx.x_recv, ctx.meta, ctx.y_recv
         k, renorm, aux_alpha, z_beta, gs, has_add = ctx.cfg
         ep, rows, lay = ctx.ep, ctx.rows, ctx.lay
         arena = ep.arena
