@@ -88,4 +88,15 @@ void router_bwd(const float* logits, const float* probs, const int* idx, const f
                 void* dlogits, int T, int E, int K, bool renorm, float aux_alpha, float z_beta, float* aux_out,
                 cudaStream_t s);
 
+// ---- decode attention ----------------------------------------------------------
+// Split-KV attention of new tokens against a (bf16 or int8) KV cache; see
+// decode_sm100.cu for the layouts.  v == nullptr: MLA latent cache (the value
+// is the first DV dims of each key row).  workspace: decode_workspace_floats().
+int decode_splits(int B, int Hk, int max_len);
+size_t decode_workspace_floats(int B, int Hk, int splits, int DV);
+void attn_decode(const void* q, const void* k, const void* v, const float* ks, const float* vs, bool int8_kv,
+                 const int* q_pos, const int* kv_len, void* out, float* workspace, int B, int Tn, int H, int Hk,
+                 int L, int DQ, int DV, long long k_b, long long k_l, long long v_b, long long v_l, long long s_b,
+                 long long s_l, int window, float scale, int splits, cudaStream_t s);
+
 }  // namespace omni

@@ -333,6 +333,60 @@ std::vector<at::Tensor> attn_bwd_t(const at::Tensor& q, const at::Tensor& k, con
   return {dq, dk, dv};
 }
 
+// ---- decode attention --------------------------------------------------------
+at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::optional<at::Tensor>& v,
+                         const c10::optional<at::Tensor>& ks, const c10::optional<at::Tensor>& vs,
+                         const at::Tensor& q_pos, const at::Tensor& kv_len, int64_t window, double scale,
+                         int64_t latent_v_dim) {
+  check_bf16(q, "q");
+  check_i32(q_pos, "q_pos");
+  check_i32(kv_len, "kv_len");
+  TORCH_CHECK(q.dim() == 4, "attn_decode: q must be [B, Tn, H, D]");
+  const c10::cuda::CUDAGuard g(q.device());
+  const int64_t B = q.size(0), Tn = q.size(1), H = q.size(2), DQ = q.size(3);
+  const bool int8_kv = k.scalar_type() == at::kChar;
+  TORCH_CHECK(int8_kv || k.scalar_type() == at::kBFloat16, "attn_decode: cache must be bf16 or int8");
+  TORCH_CHECK(k.is_cuda() && k.stride(-1) == 1, "attn_decode: cache rows must be contiguous");
+  int64_t Hk, DV, L = k.size(1);
+  long long v_b = 0, v_l = 0;
+  if (!v.has_value()) {
+    TORCH_CHECK(k.dim() == 3 && k.size(2) == DQ && latent_v_dim > 0 && latent_v_dim <= DQ,
+                "attn_decode: latent cache [B, L, DQ] with 0 < latent_v_dim <= DQ");
+    Hk = 1;
+    DV = latent_v_dim;
+  } else {
+    TORCH_CHECK(k.dim() == 4 && k.size(3) == DQ && k.stride(2) == DQ, "attn_decode: k [B, L, Hk, D]");
+    TORCH_CHECK(v->dim() == 4 && v->scalar_type() == k.scalar_type() && v->stride(-1) == 1 &&
+                    v->stride(2) == v->size(3) && v->size(2) == k.size(2),
+                "attn_decode: v [B, L, Hk, Dv]");
+    Hk = k.size(2);
+    DV = v->size(3);
+    v_b = v->stride(0);
+    v_l = v->stride(1);
+  }
+  TORCH_CHECK(H % Hk == 0, "attn_decode: heads must be a multiple of kv heads");
+  long long s_b = 0, s_l = 0;
+  if (int8_kv) {
+    TORCH_CHECK(ks.has_value() && ks->scalar_type() == at::kFloat && ks->is_cuda(), "attn_decode: int8 needs k scales");
+    s_b = ks->stride(0);
+    s_l = ks->stride(1);
+    if (v.has_value()) {
+      TORCH_CHECK(vs.has_value() && vs->stride(0) == s_b && vs->stride(1) == s_l, "attn_decode: v scales");
+    }
+  }
+  const int splits = decode_splits((int)B, (int)Hk, (int)L);
+  auto ws = at::empty({(int64_t)decode_workspace_floats((int)B, (int)Hk, splits, (int)DV)},
+                      q.options().dtype(at::kFloat));
+  auto out = at::empty({B, Tn, H, DV}, q.options());
+  attn_decode(q.data_ptr(), k.data_ptr(), v.has_value() ? v->data_ptr() : nullptr,
+              int8_kv ? ks->data_ptr<float>() : nullptr,
+              (int8_kv && vs.has_value()) ? vs->data_ptr<float>() : nullptr, int8_kv, q_pos.data_ptr<int>(),
+              kv_len.data_ptr<int>(), out.data_ptr(), ws.data_ptr<float>(), (int)B, (int)Tn, (int)H, (int)Hk, (int)L,
+              (int)DQ, (int)DV, k.stride(0), k.stride(1), v_b, v_l, s_b, s_l, (int)window, (float)scale, splits,
+              stream());
+  return out;
+}
+
 void register_kernels(pybind11::module_& m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd_t, py::arg("x"), py::arg("res"), py::arg("w"), py::arg("eps"));
   m.def("rmsnorm_bwd", &rmsnorm_bwd_t, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dres"));
@@ -356,6 +410,9 @@ void register_kernels(pybind11::module_& m) {
   m.def("moe_combine_bwd", &moe_combine_bwd_t);
   m.def("moe_scatter_add", &moe_scatter_add_t);
   m.def("router_bwd", &router_bwd_t);
+  m.def("attn_decode", &attn_decode_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_scale"),
+        py::arg("v_scale"), py::arg("q_pos"), py::arg("kv_len"), py::arg("window"), py::arg("scale"),
+        py::arg("latent_v_dim"));
   m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_rope"), py::arg("seq"),
         py::arg("causal"), py::arg("window"), py::arg("scale"));
   m.def("attn_bwd", &attn_bwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_rope"), py::arg("o"),

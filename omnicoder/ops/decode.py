@@ -59,5 +59,13 @@ def decode_attention(q, k, v, q_pos, kv_len, *, window=0, scale=None, k_scale=No
                                       v_scale=v_scale, latent_v_dim=latent_v_dim)
     C = _ext.load()
     sc = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
-    return C.attn_decode(q.contiguous(), k, v, k_scale, v_scale, q_pos.to(torch.int32).contiguous(),
-                         kv_len.to(torch.int32).contiguous(), window, sc, latent_v_dim)
+    B, Tn, H, _ = q.shape
+    G = H if latent_v_dim else H // k.shape[2]
+    step = max(1, 64 // G)                 # the kernel holds <= 64 query rows of one kv group
+    qp = q_pos.to(torch.int32)
+    kl = kv_len.to(torch.int32).contiguous()
+    if Tn <= step:
+        return C.attn_decode(q.contiguous(), k, v, k_scale, v_scale, qp.contiguous(), kl, window, sc, latent_v_dim)
+    outs = [C.attn_decode(q[:, t:t + step].contiguous(), k, v, k_scale, v_scale, qp[:, t:t + step].contiguous(), kl,
+                          window, sc, latent_v_dim) for t in range(0, Tn, step)]
+    return torch.cat(outs, dim=1)
