@@ -2,12 +2,19 @@
 PyTorch profiler; shares are what matters, the bench number comes from bench.py).
 
     python -m omnicoder.benchmarks.profile_step [--preset moe_mla_24l] [--layers 4] [--seq 4096] [--mb 2]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        -m omnicoder.benchmarks.profile_step ...      # expert x data parallel; rank 0 reports
+
+Kernels on NCCL's streams overlap the compute stream, so their share is an
+upper bound of what they cost.
 """
 from __future__ import annotations
 
 import argparse
 import collections
+import datetime
 import json
+import os
 import re
 
 import torch
@@ -29,7 +36,9 @@ def family(name: str) -> str:
     for key in ("attn_fwd_kernel", "attn_dkdv_kernel", "attn_dq_kernel", "attn_delta_kernel", "rmsnorm_fwd",
                 "rmsnorm_bwd", "rope_kernel", "embedding_fwd", "embedding_bwd", "ce_kernel", "adamw_kernel",
                 "sq_norm_kernel", "router_topk", "router_bwd", "plan_count", "plan_scan", "plan_assign",
-                "moe_gather", "moe_combine_bwd", "moe_combine_kernel", "moe_scatter_add"):
+                "moe_gather", "moe_combine_bwd", "moe_combine_kernel", "moe_scatter_add", "ep_dispatch",
+                "ep_push", "ep_combine", "ep_owner_bwd", "ep_pad_rows", "ep_barrier", "decode_split",
+                "decode_combine", "nccl"):
         if key in n:
             return key
     return "torch:" + n[:60]
@@ -46,10 +55,22 @@ def main():
     cfg = get_preset(args.preset)
     if args.layers:
         cfg.n_layers = args.layers
-    dev = torch.device("cuda", 0)
-    model = build_model(cfg, device=dev, seed=0)
-    trainer = Trainer(model, TrainConfig(lr=3e-4, warmup_steps=10, max_steps=100, grad_clip=1.0))
-    batches = [synthetic_batch(args.mb, args.seq, cfg.vocab_size, 0, i, device=dev) for i in range(4)]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    par = None
+    if world > 1:
+        import torch.distributed as dist
+
+        from omnicoder.parallel.expert_data import ExpertDataParallel
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        rows = int(args.mb * args.seq * cfg.moe.top_k * 1.3) + cfg.moe.n_experts * 128
+        par = ExpertDataParallel(dist.group.WORLD, arena_bytes=cfg.n_layers * rows * (4 * cfg.d_model * 2 + 16))
+    model = build_model(cfg, device=dev, seed=0, ep=par) if par is not None else build_model(cfg, device=dev, seed=0)
+    trainer = Trainer(model, TrainConfig(lr=3e-4, warmup_steps=10, max_steps=100, grad_clip=1.0), par)
+    batches = [synthetic_batch(args.mb, args.seq, cfg.vocab_size, rank, i, device=dev) for i in range(4)]
     for b in batches[:3]:
         trainer.step(*b, assume_all_valid=True)
     torch.cuda.synchronize()
@@ -69,6 +90,12 @@ def main():
         agg[f][1] += us / 1000.0
         total += us / 1000.0
     rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+        if rank != 0:
+            return
     print(f"{'kernel family':60s} {'count':>6s} {'ms':>9s} {'share':>7s}")
     for name, (cnt, ms) in rows:
         print(f"{name:60s} {cnt:6d} {ms:9.3f} {100 * ms / total:6.1f}%")
