@@ -99,4 +99,13 @@ void attn_decode(const void* q, const void* k, const void* v, const float* ks, c
                  int L, int DQ, int DV, long long k_b, long long k_l, long long v_b, long long v_l, long long s_b,
                  long long s_l, int window, float scale, int splits, cudaStream_t s);
 
+// ---- int4 weight-only linear ----------------------------------------------------
+// y[M, N] = x[M, K] (bf16) . dequant(w)^T, w packed [N, ldw] bytes (two nibbles per
+// byte, low first), value = (q - offset) * scale[n].  M <= 8.
+void int4_gemv(const void* x, const uint8_t* w, const float* scale, void* y, int M, int N, int K, int ldw,
+               float offset, cudaStream_t s);
+// out[N, K] (bf16) = (q - offset) * scale[n]
+void int4_dequant(const uint8_t* w, const float* scale, void* out, int N, int K, int ldw, float offset,
+                  cudaStream_t s);
+
 }  // namespace omni

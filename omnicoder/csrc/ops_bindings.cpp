@@ -387,6 +387,33 @@ at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::op
   return out;
 }
 
+// ---- int4 weight-only linear ----------------------------------------------------
+at::Tensor int4_gemv_t(const at::Tensor& x, const at::Tensor& w, const at::Tensor& scale, double offset) {
+  check_bf16(x, "x");
+  check_f32(scale, "scale");
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kByte && w.is_contiguous() && w.dim() == 2, "int4: packed uint8 [N, ldw]");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0), ldw = w.size(1);
+  TORCH_CHECK(M <= 8, "int4_gemv: at most 8 rows (use int4_dequant + gemm)");
+  TORCH_CHECK(K % 8 == 0 && 2 * ldw >= K && ldw % 16 == 0, "int4_gemv: K % 8 == 0, rows padded to 32 bytes");
+  TORCH_CHECK(scale.numel() == N, "int4_gemv: one scale per row");
+  auto y = at::empty({M, N}, x.options());
+  int4_gemv(x.data_ptr(), w.data_ptr<uint8_t>(), scale.data_ptr<float>(), y.data_ptr(), (int)M, (int)N, (int)K, (int)ldw,
+            (float)offset, stream());
+  return y;
+}
+
+at::Tensor int4_dequant_t(const at::Tensor& w, const at::Tensor& scale, int64_t K, double offset) {
+  check_f32(scale, "scale");
+  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kByte && w.is_contiguous() && w.dim() == 2, "int4: packed uint8 [N, ldw]");
+  TORCH_CHECK(K % 8 == 0 && 2 * w.size(1) >= K && w.size(1) % 4 == 0, "int4_dequant: K % 8 == 0");
+  const c10::cuda::CUDAGuard g(w.device());
+  auto out = at::empty({w.size(0), K}, w.options().dtype(at::kBFloat16));
+  int4_dequant(w.data_ptr<uint8_t>(), scale.data_ptr<float>(), out.data_ptr(), (int)w.size(0), (int)K, (int)w.size(1),
+               (float)offset, stream());
+  return out;
+}
+
 void register_kernels(pybind11::module_& m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd_t, py::arg("x"), py::arg("res"), py::arg("w"), py::arg("eps"));
   m.def("rmsnorm_bwd", &rmsnorm_bwd_t, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dres"));
@@ -410,6 +437,8 @@ void register_kernels(pybind11::module_& m) {
   m.def("moe_combine_bwd", &moe_combine_bwd_t);
   m.def("moe_scatter_add", &moe_scatter_add_t);
   m.def("router_bwd", &router_bwd_t);
+  m.def("int4_gemv", &int4_gemv_t, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("offset"));
+  m.def("int4_dequant", &int4_dequant_t, py::arg("w"), py::arg("scale"), py::arg("K"), py::arg("offset"));
   m.def("attn_decode", &attn_decode_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_scale"),
         py::arg("v_scale"), py::arg("q_pos"), py::arg("kv_len"), py::arg("window"), py::arg("scale"),
         py::arg("latent_v_dim"));
