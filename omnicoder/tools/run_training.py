@@ -1,0 +1,100 @@
+"""Training orchestrator: ``python -m omnicoder.tools.run_training``.
+
+Runs the stages of a training plan as child processes with a time budget each
+(reference src/omnicoder/tools/run_training.py:102-1366: stage planning from a
+minute budget, `run_with_timeout`, resume by skipping finished stages, optional
+expert-parallel launch).  Stages here: `pretrain` (spec LM), `draft` (small
+draft model for speculative decoding), `export` (ONNX decode step).  Each stage
+writes a marker file when it finishes; a rerun skips finished stages unless
+--force is given.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+
+def run_with_timeout(cmd: list[str], timeout_s: float, env=None) -> int:
+    """Run `cmd`; on timeout terminate its process group and return 124."""
+    p = subprocess.Popen(cmd, env=env, start_new_session=True)
+    try:
+        return p.wait(timeout=timeout_s if timeout_s > 0 else None)
+    except subprocess.TimeoutExpired:
+        import signal
+        os.killpg(p.pid, signal.SIGTERM)
+        try:
+            p.wait(timeout=30)
+        except subprocess.TimeoutExpired:
+            os.killpg(p.pid, signal.SIGKILL)
+        return 124
+
+
+def plan(budget_minutes: float, steps_per_minute: float, stages: list[str]) -> dict:
+    """Split the budget: 80 % pretrain, 15 % draft, 5 % export."""
+    share = {"pretrain": 0.8, "draft": 0.15, "export": 0.05}
+    tot = sum(share[s] for s in stages) or 1.0
+    return {s: {"minutes": budget_minutes * share[s] / tot,
+                "steps": max(1, int(budget_minutes * share[s] / tot * steps_per_minute))} for s in stages}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out_dir", default="weights")
+    ap.add_argument("--data", default="synthetic")
+    ap.add_argument("--budget_minutes", type=float, default=10.0)
+    ap.add_argument("--steps_per_minute", type=float, default=60.0)
+    ap.add_argument("--stages", default="pretrain,draft")
+    ap.add_argument("--preset", default="tiny_moe")
+    ap.add_argument("--draft_preset", default="draft_2l")
+    ap.add_argument("--seq_len", type=int, default=256)
+    ap.add_argument("--batch_size", type=int, default=4)
+    ap.add_argument("--devices", default="", help="comma list of cuda devices: expert-parallel launch when > 1")
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--dry_run", action="store_true")
+    a = ap.parse_args(argv)
+    os.makedirs(a.out_dir, exist_ok=True)
+    stages = [s for s in a.stages.split(",") if s]
+    p = plan(a.budget_minutes, a.steps_per_minute, stages)
+    results = {}
+    for s in stages:
+        marker = os.path.join(a.out_dir, f".stage_{s}.done")
+        if os.path.exists(marker) and not a.force:
+            results[s] = "skipped (done)"
+            continue
+        if s in ("pretrain", "draft"):
+            preset = a.preset if s == "pretrain" else a.draft_preset
+            args = ["--data", a.data, "--preset", preset, "--seq_len", str(a.seq_len), "--batch_size",
+                    str(a.batch_size), "--steps", str(p[s]["steps"]), "--out", os.path.join(a.out_dir, f"{s}.pt"),
+                    "--state_out", os.path.join(a.out_dir, f"{s}_state.pt"),
+                    "--log_file", os.path.join(a.out_dir, f"{s}_log.jsonl")]
+            devs = [d for d in a.devices.split(",") if d]
+            if len(devs) > 1:
+                cmd = [sys.executable, "-m", "omnicoder.tools.torchrun_ep", "--script", "omnicoder.training.pretrain",
+                       "--devices", ",".join(devs), "--"] + args
+            else:
+                cmd = [sys.executable, "-m", "omnicoder.training.pretrain"] + args
+        elif s == "export":
+            cmd = [sys.executable, "-m", "omnicoder.export.onnx_export", "--ckpt", os.path.join(a.out_dir, "pretrain.pt"),
+                   "--out", os.path.join(a.out_dir, "decode_step.onnx")]
+        else:
+            raise SystemExit(f"unknown stage {s}")
+        if a.dry_run:
+            print(" ".join(cmd))
+            continue
+        t0 = time.time()
+        rc = run_with_timeout(cmd, p[s]["minutes"] * 60 * 1.5 + 60)
+        results[s] = {"rc": rc, "seconds": round(time.time() - t0, 1)}
+        if rc == 0:
+            open(marker, "w").close()
+        else:
+            break
+    print(json.dumps({"plan": p, "results": results}, indent=1))
+    return 0 if all(not isinstance(v, dict) or v["rc"] == 0 for v in results.values()) else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,51 @@
+"""Entry points: pretrain (single process, resume, text folder), the expert-parallel
+launcher with 2 CPU ranks (gloo), the training orchestrator, generate CLI."""
+import json
+import os
+import subprocess
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _run(args, timeout=600):
+    env = dict(os.environ, PYTHONPATH=ROOT, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, "-m"] + args, cwd=ROOT, env=env, capture_output=True, text=True,
+                       timeout=timeout)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    return r.stdout
+
+
+def test_pretrain_text_folder_and_resume(tmp_path):
+    d = tmp_path / "data"
+    d.mkdir()
+    (d / "a.txt").write_text("the quick brown fox jumps over the lazy dog. " * 40)
+    out, st, log = tmp_path / "m.pt", tmp_path / "s.pt", tmp_path / "log.jsonl"
+    common = ["--preset", "tiny_moe", "--seq_len", "32", "--batch_size", "2", "--log_interval", "1", "--device", "cpu",
+              "--out", str(out), "--state_out", str(st), "--log_file", str(log)]
+    _run(["omnicoder.training.pretrain", "--data", str(d), "--steps", "2"] + common)
+    assert out.exists() and st.exists()
+    ck = torch.load(out, weights_only=False)
+    assert ck["step"] == 2 and any(k.endswith(".w1") for k in ck["model"])
+    _run(["omnicoder.training.pretrain", "--data", str(d), "--steps", "3", "--resume_ckpt", str(out)] + common)
+    recs = [json.loads(l) for l in log.read_text().splitlines()]
+    assert [r["step"] for r in recs] == [1, 2, 3]          # the resumed run continues at step 3
+
+
+def test_torchrun_ep_two_cpu_ranks(tmp_path):
+    out = _run(["omnicoder.tools.torchrun_ep", "--devices", "cpu,cpu", "--script", "omnicoder.training.pretrain", "--",
+                "--device", "cpu", "--data", "synthetic", "--preset", "tiny_moe", "--seq_len", "32", "--batch_size", "2",
+                "--steps", "2", "--log_interval", "1", "--out", str(tmp_path / "m.pt"), "--state_out",
+                str(tmp_path / "s.pt"), "--log_file", str(tmp_path / "l.jsonl")], timeout=900)
+    assert "step 2/2" in out
+    ck = torch.load(tmp_path / "m.pt", weights_only=False)
+    # rank 0 gathered every rank's experts into one consolidated checkpoint
+    assert ck["model"]["blocks.0.ffn.w1"].shape[0] == 4
+    assert (tmp_path / "s.pt.rank0").exists() and (tmp_path / "s.pt.rank1").exists()
+
+
+def test_run_training_plan_dry_run():
+    out = _run(["omnicoder.tools.run_training", "--dry_run", "--budget_minutes", "1", "--stages", "pretrain,draft,export"])
+    assert "omnicoder.training.pretrain" in out and "onnx_export" in out
