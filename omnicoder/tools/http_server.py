@@ -1,0 +1,142 @@
+"""HTTP serving: ``python -m omnicoder.tools.http_server --preset tiny_moe [--ckpt ...]``.
+
+Endpoints (reference src/omnicoder/tools/http_server.py:147-1339):
+  GET  /health                -> {"status": "ok", model info}
+  POST /generate/text         {"prompt", "max_new_tokens", "temperature", "top_k", "top_p", "seed"}
+  POST /generate/unified      {"modality": "text", ...} (text only; other modalities need
+                               external diffusion weights -> 501)
+  POST /generate/image|video  -> 501 (the reference calls external diffusers pipelines)
+
+Unlike the reference (one request at a time per process), concurrent requests
+are batched: a collector task takes up to `max_batch` queued requests that
+share a prompt length and sampling settings and runs them as one batched
+prefill + KV-cache decode.
+"""
+from __future__ import annotations
+
+import argparse
+import asyncio
+import time
+
+import torch
+
+from ..inference.generate import generate
+from ..training.tokenizer import get_tokenizer
+
+
+_REQ = None
+
+
+def _request_model():
+    """The request body model, built on first use (pydantic is only needed for serving)."""
+    global _REQ
+    if _REQ is None:
+        from pydantic import create_model
+        _REQ = create_model("TextReq", prompt=(str, ...), max_new_tokens=(int, 64), temperature=(float, 0.0),
+                            top_k=(int, 0), top_p=(float, 1.0), seed=(int | None, None), modality=(str, "text"))
+    return _REQ
+
+
+def create_app(model, tokenizer=None, max_batch: int = 16, batch_window_s: float = 0.005):
+    from fastapi import FastAPI, HTTPException
+    TextReq = _request_model()
+
+    tok = tokenizer or get_tokenizer(model.cfg.vocab_size)
+    dev = next(model.parameters()).device
+    app = FastAPI(title="omnicoder")
+    state = {"queue": None, "served": 0, "batches": 0}
+
+    async def collector():
+        q = state["queue"]
+        while True:
+            first = await q.get()
+            group = [first]
+            t_end = time.monotonic() + batch_window_s
+            while len(group) < max_batch:
+                timeout = t_end - time.monotonic()
+                if timeout <= 0:
+                    break
+                try:
+                    group.append(await asyncio.wait_for(q.get(), timeout))
+                except asyncio.TimeoutError:
+                    break
+            buckets: dict = {}
+            for item in group:
+                r, ids, fut = item
+                key = (ids.shape[1], r.max_new_tokens, r.temperature, r.top_k, r.top_p, r.seed)
+                buckets.setdefault(key, []).append(item)
+            for key, items in buckets.items():
+                r0 = items[0][0]
+                ids = torch.cat([it[1] for it in items]).to(dev)
+                try:
+                    out = await asyncio.to_thread(generate, model, ids, r0.max_new_tokens, r0.temperature, r0.top_k,
+                                                  r0.top_p, seed=r0.seed)
+                    state["batches"] += 1
+                    for i, (_, pid, fut) in enumerate(items):
+                        fut.set_result(tok.decode(out[i, pid.shape[1]:].tolist()))
+                except Exception as e:  # report to every waiting request
+                    for _, _, fut in items:
+                        if not fut.done():
+                            fut.set_exception(e)
+
+    @app.on_event("startup")
+    async def _start():
+        state["queue"] = asyncio.Queue()
+        state["task"] = asyncio.create_task(collector())
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok", "model": model.cfg.name, "device": str(dev), "served": state["served"],
+                "batches": state["batches"]}
+
+    async def _text(r):
+        ids = torch.tensor([tok.encode(r.prompt) or [0]])
+        fut = asyncio.get_running_loop().create_future()
+        await state["queue"].put((r, ids, fut))
+        text = await fut
+        state["served"] += 1
+        return {"text": text, "prompt_tokens": int(ids.shape[1]), "new_tokens": r.max_new_tokens}
+
+    async def gen_text(r):
+        return await _text(r)
+
+    async def gen_unified(r):
+        if r.modality != "text":
+            raise HTTPException(501, f"modality {r.modality!r} needs external generation weights")
+        return await _text(r)
+
+    gen_text.__annotations__ = {"r": TextReq}
+    gen_unified.__annotations__ = {"r": TextReq}
+    app.post("/generate/text")(gen_text)
+    app.post("/generate/unified")(gen_unified)
+
+    @app.post("/generate/image")
+    async def gen_image():
+        raise HTTPException(501, "image generation needs external diffusion pipeline weights")
+
+    @app.post("/generate/video")
+    async def gen_video():
+        raise HTTPException(501, "video generation needs external diffusion pipeline weights")
+
+    return app
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="tiny_moe")
+    ap.add_argument("--ckpt", default=None)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    ap.add_argument("--max_batch", type=int, default=16)
+    a = ap.parse_args(argv)
+    from ..config import get_preset
+    from ..inference.builders import load_model
+    from ..models.lm import build_model
+    model = load_model(a.ckpt, a.device, preset=a.preset)[0] if a.ckpt else build_model(get_preset(a.preset), a.device)
+    import uvicorn
+    uvicorn.run(create_app(model.eval(), max_batch=a.max_batch), host=a.host, port=a.port)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,90 @@
+"""Inference-side tools: throughput benchmark, kNN-LM cache, batched HTTP
+server, GGUF round trip, ONNX decode-step wrappers (numerics vs the models'
+own decode paths)."""
+import json
+
+import torch
+
+from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig, get_preset
+from omnicoder.models.lm import build_model
+
+
+def _tiny():
+    cfg = ModelConfig(name="t", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=128,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2), moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=64))
+    return cfg, build_model(cfg, device="cpu", seed=0).eval()
+
+
+def test_benchmarks_run():
+    from omnicoder.inference.benchmark import bench_tokens_per_second, decode_benchmark
+    cfg, m = _tiny()
+    assert bench_tokens_per_second(m, seq_len=8, gen_tokens=4) > 0
+    r = decode_benchmark(m, batch=3, prompt_len=8, gen_tokens=5)
+    assert r["decode_tokens_per_s"] > 0 and r["p50_tpot_ms"] > 0
+
+
+def test_knn_cache_blend():
+    from omnicoder.inference.knn_cache import KNNCache
+    c = KNNCache(dim=8, k=2, lam=0.5)
+    h = torch.randn(10, 8)
+    c.add(h, torch.arange(10))
+    p = c.query(h[3:4], 20)
+    assert int(p.argmax()) == 3 and abs(float(p.sum()) - 1) < 1e-5
+    lp = c.blend(torch.zeros(1, 20), h[3:4])
+    assert int(lp.argmax()) == 3
+
+
+def test_http_server_batches_requests():
+    from fastapi.testclient import TestClient
+
+    from omnicoder.tools.http_server import create_app
+    cfg, m = _tiny()
+    with TestClient(create_app(m, max_batch=4, batch_window_s=0.05)) as cli:
+        assert cli.get("/health").json()["status"] == "ok"
+        import concurrent.futures as cf
+        with cf.ThreadPoolExecutor(4) as ex:
+            outs = list(ex.map(lambda p: cli.post("/generate/text", json={"prompt": p, "max_new_tokens": 3}).json(),
+                               ["abcd", "efgh", "ijkl", "mnop"]))
+        assert all("text" in o for o in outs)
+        h = cli.get("/health").json()
+        assert h["served"] == 4 and h["batches"] < 4                  # at least two requests shared a batch
+        assert cli.post("/generate/image", json={}).status_code == 501
+
+
+def test_gguf_roundtrip(tmp_path):
+    from omnicoder.export.gguf import export_model_gguf, read_gguf
+    cfg, m = _tiny()
+    p = tmp_path / "m.gguf"
+    export_model_gguf(m, str(p), dtype="bf16")
+    meta, ts = read_gguf(str(p))
+    assert meta["general.architecture"] == "omnicoder" and json.loads(meta["omnicoder.config"])["d_model"] == 64
+    sd = m.export_state_dict()
+    for k, v in sd.items():
+        assert torch.allclose(ts[k].float(), v.float(), atol=1e-2, rtol=1e-2), k
+
+
+def test_onnx_decode_step_wrappers():
+    from omnicoder.export.onnx_export import DecodeStepWrapper, io_names
+    from omnicoder.inference.kv_cache import KVCache
+    from omnicoder.models.compat import OmniTransformer
+    # compat family: same tensors as the model's own decode path
+    cm = OmniTransformer(vocab_size=100, n_layers=2, d_model=32, n_heads=4, mlp_dim=64, n_experts=2, top_k=1,
+                         max_seq_len=64, kv_latent_dim=8).eval()
+    w = DecodeStepWrapper(cm)
+    ids = torch.tensor([[5]])
+    cache = [torch.randn(1, 4, 16, 8) for _ in range(4)]
+    out = w(ids, *cache)
+    ref = cm(ids, past_kv=[(cache[0], cache[1]), (cache[2], cache[3])], use_cache=True)
+    assert torch.allclose(out[0], ref[0]) and len(out) == 5
+    assert io_names(2)[0] == ["input_ids", "k_lat_0", "v_lat_0", "k_lat_1", "v_lat_1"]
+    # spec family (GQA): one step equals forward_cached
+    cfg, m = _tiny()
+    kv = KVCache(cfg, 1, 32, "cpu")
+    prompt = torch.tensor([[1, 2, 3]])
+    m.forward_cached(prompt, kv, prefill=True)
+    want = m.forward_cached(torch.tensor([[7]]), kv)
+    kv2 = KVCache(cfg, 1, 32, "cpu")
+    m.forward_cached(prompt, kv2, prefill=True)
+    flat = [t for l in range(cfg.n_layers) for t in (kv2.k[l], kv2.v[l])]
+    got = DecodeStepWrapper(m)(torch.tensor([[7]]), torch.tensor(3), *flat)
+    assert torch.allclose(got[0], want, atol=1e-4)
