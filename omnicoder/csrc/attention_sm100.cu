@@ -116,12 +116,10 @@ struct FwdSmem {
   static constexpr int kQ = NQC * kSubTile;
   static constexpr int kK = NQC * kSubTile;
   static constexpr int kV = kTile * DV * 2;
-  static constexpr int kP = kTile * kTile * 2;
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + kQ;           // 2 stages
-  static constexpr int kOffV = kOffK + 2 * kK;
-  static constexpr int kOffP = kOffV + kV;
-  static constexpr int kOffBar = kOffP + kP;
+  static constexpr int kOffV = kOffK + 2 * kK;       // 2 stages (P lives in tensor memory)
+  static constexpr int kOffBar = kOffV + 2 * kV;
   static constexpr int kBytes = kOffBar + 256 + 1024;
 };
 
@@ -138,19 +136,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sQ = smem + L::kOffQ;
   uint8_t* sK = smem + L::kOffK;
   uint8_t* sV = smem + L::kOffV;
-  uint8_t* sP = smem + L::kOffP;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;   // [2]
-  uint64_t* s_empty = bars + 9;  // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_empty = bars + 11; // [2]  S/P stage free again (P.V of the stage's tile completed)
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_done = bars + 14;
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / kTile;
@@ -168,11 +165,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&s_empty[i], 1);
     }
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
     mbar_init(p_full, 4);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
@@ -186,6 +183,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // TMEM: S stages at columns [0, 128) and [128, 256) (fp32); P of a tile is written as
+  // bf16 pairs over the first 64 columns of its own S stage; O at [256, 256 + DV).
   const uint32_t tS0 = tmem, tO = tmem + 256;
 
   if (warp == 0) {
@@ -204,13 +203,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int c = 0; c < NKC; ++c) tma_load_3d(dK + c * kSubTile, &tmK, &k_full[s], c * 64, hk, kt0);
         if (ROPE) tma_load_2d(dK + NKC * kSubTile, &tmKR, &k_full[s], 0, kt0);
-        if (!mbar_wait(v_empty, (jj & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
-        mbar_arrive_expect_tx(v_full, L::kV);
+        if (!mbar_wait(&v_empty[s], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) { ok = false; break; }
+        uint8_t* dV = sV + s * L::kV;
+        mbar_arrive_expect_tx(&v_full[s], L::kV);
 #pragma unroll
         for (int half = 0; half < 2; ++half)
 #pragma unroll
           for (int c = 0; c < VCH; ++c)
-            tma_load_3d(sV + (half * VCH + c) * 8192, &tmV, v_full, c * 64, hk, kt0 + half * 64);
+            tma_load_3d(dV + (half * VCH + c) * 8192, &tmV, &v_full[s], c * 64, hk, kt0 + half * 64);
       }
     }
   } else if (warp == 1) {
@@ -237,20 +237,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
       if (ok && n > 0) ok = issue_s(0);
       for (int jj = 0; jj < n && ok; ++jj) {
+        const int s = jj & 1;
+        const uint32_t u = jj >> 1;
         if (jj + 1 < n && !issue_s(jj + 1)) { ok = false; break; }
         if (!mbar_wait(p_full, jj & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-        if (!mbar_wait(v_full, jj & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(&v_full[s], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP), va = smem_u32(sV);
+        const uint32_t va = smem_u32(sV + s * L::kV);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kSubTile + (kk & 3) * 32;
           const uint32_t boff = (kk >> 2) * (VCH * 8192) + (kk & 3) * 2048;
-          tc_mma_f16(tO, umma_desc_sw128(pa + aoff, 16, 1024), umma_desc_sw128(va + boff, 8192, 1024), idesc_o,
-                     (jj > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tO, tS0 + s * 128 + kk * 8, umma_desc_sw128(va + boff, 8192, 1024), idesc_o,
+                        (jj > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(o_done);
-        tc_commit(v_empty);
+        tc_commit(&v_empty[s]);
+        tc_commit(&s_empty[s]);
       }
       tc_commit(drain);
       mbar_wait(drain, 0, p.status, STATUS_TIMEOUT_DRAIN);
@@ -272,22 +274,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS0 + s * 128 + c * 32 + lane_off, x + c * 32);
       tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[s]);
       const int kpos0 = (j_lo + jj) * kTile;
       const bool need_mask = (p.causal && kpos0 + kTile - 1 > qpos0) ||
                              (p.window > 0 && kpos0 <= qpos0 + kTile - 1 - p.window);
       float mt = -INFINITY;
+      if (need_mask) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = x[c] * p.scale_log2;
-        if (need_mask) {
+        for (int c = 0; c < 128; ++c) {
+          float v = x[c] * p.scale_log2;
           const int kp = kpos0 + c;
           if ((p.causal && kp > qpos) || (p.window > 0 && kp <= qpos - p.window)) v = -INFINITY;
+          x[c] = v;
+          mt = fmaxf(mt, v);
         }
-        x[c] = v;
-        mt = fmaxf(mt, v);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          x[c] *= p.scale_log2;
+          mt = fmaxf(mt, x[c]);
+        }
       }
       const float m_new = fmaxf(m, mt);
       const bool need = m_new > m + 8.0f;
@@ -299,18 +304,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float m_use = (m == -INFINITY) ? 0.f : m;
       float sum = 0.f;
+      uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        x[c] = exp2f(x[c] - m_use);
-        sum += x[c];
+      for (int c = 0; c < 64; ++c) {
+        const float e0 = exp2f(x[2 * c] - m_use), e1 = exp2f(x[2 * c + 1] - m_use);
+        sum += e0 + e1;
+        pk[c] = pack_bf16x2(e0, e1);
       }
       l = l * alpha + sum;
-      if (jj > 0) {
+      // P (bf16) over the first 64 columns of this tile's S stage (S already in registers)
+      tmem_st32_u32(tS0 + s * 128 + lane_off, pk);
+      tmem_st32_u32(tS0 + s * 128 + 32 + lane_off, pk + 32);
+      if (jj > 0 && warp_need) {
+        // O must hold P.V of the previous tile before it is rescaled
         if (!mbar_wait(o_done, (jj - 1) & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
-      }
-      store_row_sw128(sP, r, x);
-      if (jj > 0 && warp_need) {
 #pragma unroll
         for (int c = 0; c < DV / 32; ++c) {
           float o[32];
@@ -320,9 +328,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
           tmem_st32(tO + c * 32 + lane_off, o);
         }
-        tc_wait_st();
       }
-      fence_proxy_async_smem();
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
