@@ -144,10 +144,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* v_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;   // [2]
   uint64_t* s_empty = bars + 11; // [2]  S/P stage free again (P.V of the stage's tile completed)
-  uint64_t* p_full = bars + 13;
-  uint64_t* o_done = bars + 14;
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* p_full = bars + 13;   // [2] per S/P stage, so the softmax can never run two phases ahead
+  uint64_t* o_done = bars + 15;
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / kTile;
@@ -169,8 +169,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 1);
+      mbar_init(&p_full[i], 4);
     }
-    mbar_init(p_full, 4);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int s = jj & 1;
         const uint32_t u = jj >> 1;
         if (jj + 1 < n && !issue_s(jj + 1)) { ok = false; break; }
-        if (!mbar_wait(p_full, jj & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
+        if (!mbar_wait(&p_full[s], u & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         if (!mbar_wait(&v_full[s], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
         tc_fence_after();
         const uint32_t va = smem_u32(sV + s * L::kV);
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[s]);
     }
     if (ok && n > 0 && mbar_wait(o_done, (n - 1) & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) {
       tc_fence_after();
@@ -363,28 +363,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // ===========================================================================
 template <int DQ, int DV>
 struct DkdvSmem {
+  static constexpr int BQ = 64;                    // query rows per iteration
   static constexpr int NQC = DQ / 64;
-  static constexpr int kK = NQC * kSubTile;
-  static constexpr int kV = (DV / 64) * kSubTile;
-  static constexpr int kQ = NQC * kSubTile;
-  static constexpr int kDO = (DV / 64) * kSubTile;
-  static constexpr int kP = 2 * kSubTile;
+  static constexpr int kK = NQC * kSubTile;        // [128 kv x DQ]
+  static constexpr int kV = (DV / 64) * kSubTile;  // [128 kv x DV]
+  static constexpr int kQ = NQC * 8192;            // [64 q x DQ] (64-row sub-tiles)
+  static constexpr int kDO = (DV / 64) * 8192;     // [64 q x DV]
+  static constexpr int kVec = 2 * BQ * 4;          // lse[64], delta[64]
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kK;
-  static constexpr int kOffQ = kOffV + kV;
-  static constexpr int kOffDO = kOffQ + kQ;
-  static constexpr int kOffP = kOffDO + kDO;
-  static constexpr int kOffVec = kOffP + kP;      // lse[128], delta[128] floats
-  static constexpr int kOffBar = kOffVec + 1024;
+  static constexpr int kOffQ = kOffV + kV;         // 2 stages
+  static constexpr int kOffDO = kOffQ + 2 * kQ;    // 2 stages
+  static constexpr int kOffPT = kOffDO + 2 * kDO;  // P^T [128 kv x 64 q] bf16
+  static constexpr int kOffDS = kOffPT + kSubTile; // dS^T [128 kv x 64 q] bf16
+  static constexpr int kOffVec = kOffDS + kSubTile;  // 2 stages of lse/delta
+  static constexpr int kOffBar = kOffVec + 2 * kVec;
   static constexpr int kBytes = kOffBar + 256 + 1024;
 };
 
+// CTA = (kv tile of 128 rows, kv head, sequence); loops over query tiles of 64
+// rows (and over the query heads of a GQA group).  Q/dO (with the tile's lse and
+// delta, fetched by bulk copies on the same barrier) are double buffered so the
+// next tile streams in while this one computes; S^T is double buffered in TMEM
+// so K Q^T of the next tile runs during this tile's softmax.
+//   TMEM columns: S^T[2] = [0, 64), [64, 128); dP^T = [128, 192);
+//                 dV = [192, 192 + DV); dK = [192 + DV, 192 + DV + DQ)
 template <int DQ, int DV, bool ROPE>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmKR, const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmDO, AttnArgs p) {
   using L = DkdvSmem<DQ, DV>;
+  constexpr int BQ = L::BQ;
   constexpr int NQC = L::NQC;
   constexpr int NKC = ROPE ? NQC - 1 : NQC;
   constexpr int VCH = DV / 64;
@@ -394,52 +404,54 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sV = smem + L::kOffV;
   uint8_t* sQ = smem + L::kOffQ;
   uint8_t* sDO = smem + L::kOffDO;
-  uint8_t* sP = smem + L::kOffP;
-  float* s_lse = reinterpret_cast<float*>(smem + L::kOffVec);
-  float* s_delta = s_lse + 128;
+  uint8_t* sPT = smem + L::kOffPT;
+  uint8_t* sDS = smem + L::kOffDS;
+  float* sVec = reinterpret_cast<float*>(smem + L::kOffVec);  // [stage][lse 64 | delta 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;
-  uint64_t* q_empty = bars + 2;
-  uint64_t* do_full = bars + 3;
-  uint64_t* do_empty = bars + 4;
-  uint64_t* s_full = bars + 5;
-  uint64_t* sp_ready = bars + 6;   // count 4
-  uint64_t* dp_full = bars + 7;
-  uint64_t* sdp_empty = bars + 8;  // count 4
-  uint64_t* ds_ready = bars + 9;   // count 4
-  uint64_t* pds_free = bars + 10;
-  uint64_t* acc_done = bars + 11;
-  uint64_t* vec_full = bars + 12;   // count 128: lse/delta of the q tile are in smem
-  uint64_t* vec_empty = bars + 13;  // count 128: every softmax thread is done with them
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* q_full = bars + 1;    // [2] Q + lse/delta
+  uint64_t* q_empty = bars + 3;   // [2]
+  uint64_t* do_full = bars + 5;   // [2]
+  uint64_t* do_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_empty = bars + 11;  // [2] count 4
+  uint64_t* pt_ready = bars + 13; // count 4
+  uint64_t* pt_free = bars + 14;
+  uint64_t* dp_full = bars + 15;
+  uint64_t* dp_empty = bars + 16; // count 4
+  uint64_t* ds_ready = bars + 17; // count 4
+  uint64_t* ds_free = bars + 18;
+  uint64_t* acc_done = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
   const int warp = warp_id(), lane = lane_id();
-  const int nqt = p.S / kTile;
+  const int nqt = p.S / BQ;
   const int kt = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int G = p.H / p.Hk;
   const int kpos0 = kt * kTile;
   const int kt0 = b * p.S + kpos0;
-  const int i_lo = p.causal ? kt : 0;
-  const int i_hi = p.window > 0 ? min(nqt - 1, (kpos0 + kTile - 1 + p.window - 1) / kTile) : nqt - 1;
+  const int i_lo = p.causal ? kpos0 / BQ : 0;
+  const int i_hi = p.window > 0 ? min(nqt - 1, (kpos0 + kTile - 1 + p.window - 1) / BQ) : nqt - 1;
   const int nq = max(0, i_hi - i_lo + 1);
-  const int n = nq * G;  // iterations: (g, i) with i fastest
+  const int n = nq * G;  // iterations (g, i), i fastest
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
-    mbar_init(do_full, 1);
-    mbar_init(do_empty, 1);
-    mbar_init(s_full, 1);
-    mbar_init(sp_ready, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&do_full[i], 1);
+      mbar_init(&do_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    mbar_init(pt_ready, 4);
+    mbar_init(pt_free, 1);
     mbar_init(dp_full, 1);
-    mbar_init(sdp_empty, 4);
+    mbar_init(dp_empty, 4);
     mbar_init(ds_ready, 4);
-    mbar_init(pds_free, 1);
+    mbar_init(ds_free, 1);
     mbar_init(acc_done, 1);
-    mbar_init(vec_full, 128);
-    mbar_init(vec_empty, 128);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -450,7 +462,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tSdP = tmem, tdV = tmem + 128, tdK = tmem + 256;
+  const uint32_t tS0 = tmem, tdP = tmem + 128, tdV = tmem + 192, tdK = tmem + 192 + DV;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -463,66 +475,77 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int it = 0; it < n; ++it) {
         const int g = it / nq, i = i_lo + it % nq;
         const int hq = hk * G + g;
-        const int qt0 = b * p.S + i * kTile;
-        if (!mbar_wait(q_empty, (it & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
-        mbar_arrive_expect_tx(q_full, L::kQ);
+        const int qrow0 = b * p.S + i * BQ;
+        const int st = it & 1;
+        const uint32_t u = it >> 1;
+        if (!mbar_wait(&q_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
+        mbar_arrive_expect_tx(&q_full[st], L::kQ + L::kVec);
 #pragma unroll
-        for (int c = 0; c < NQC; ++c) tma_load_3d(sQ + c * kSubTile, &tmQ, q_full, c * 64, hq, qt0);
-        if (!mbar_wait(do_empty, (it & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
-        mbar_arrive_expect_tx(do_full, L::kDO);
+        for (int c = 0; c < NQC; ++c) tma_load_3d(sQ + st * L::kQ + c * 8192, &tmQ, &q_full[st], c * 64, hq, qrow0);
+        const long long vidx = (long long)hq * p.T + qrow0;
+        bulk_load(sVec + st * 2 * BQ, p.lse + vidx, BQ * 4, &q_full[st]);
+        bulk_load(sVec + st * 2 * BQ + BQ, p.delta + vidx, BQ * 4, &q_full[st]);
+        if (!mbar_wait(&do_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
+        mbar_arrive_expect_tx(&do_full[st], L::kDO);
 #pragma unroll
-        for (int c = 0; c < VCH; ++c) tma_load_3d(sDO + c * kSubTile, &tmDO, do_full, c * 64, hq, qt0);
+        for (int c = 0; c < VCH; ++c) tma_load_3d(sDO + st * L::kDO + c * 8192, &tmDO, &do_full[st], c * 64, hq, qrow0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc_s = umma_idesc_f16(128, 128, false, false, true);    // K Q^T, V dO^T
-      constexpr uint32_t idesc_dv = umma_idesc_f16(128, DV, false, true, true);     // P^T dO
-      constexpr uint32_t idesc_dk = umma_idesc_f16(128, DQ, false, true, true);     // dS^T Q
+      constexpr uint32_t idesc_s = umma_idesc_f16(128, BQ, false, false, true);    // K Q^T, V dO^T
+      constexpr uint32_t idesc_dv = umma_idesc_f16(128, DV, false, true, true);    // P^T dO
+      constexpr uint32_t idesc_dk = umma_idesc_f16(128, DQ, false, true, true);    // dS^T Q
       bool ok = mbar_wait(kv_full, 0, p.status, STATUS_TIMEOUT_TMA_FULL);
-      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), qa = smem_u32(sQ), da = smem_u32(sDO),
-                     pa = smem_u32(sP);
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sPT), dsa = smem_u32(sDS);
+      auto issue_s = [&](int it) -> bool {
+        const int st = it & 1;
+        const uint32_t u = it >> 1;
+        if (!mbar_wait(&q_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) return false;
+        if (!mbar_wait(&s_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) return false;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sQ + st * L::kQ);
+#pragma unroll
+        for (int kk = 0; kk < DQ / 16; ++kk)
+          tc_mma_f16(tS0 + st * 64, umma_desc_sw128(ka + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
+                     umma_desc_sw128(qa + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[st]);
+        return true;
+      };
+      if (ok && n > 0) ok = issue_s(0);
       for (int it = 0; it < n && ok; ++it) {
+        const int st = it & 1;
+        const uint32_t u = it >> 1;
         const uint32_t ph = it & 1;
-        if (!mbar_wait(q_full, ph, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
-        if (!mbar_wait(sdp_empty, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) { ok = false; break; }
+        if (it + 1 < n && !issue_s(it + 1)) { ok = false; break; }
+        // dP^T = V dO^T
+        if (!mbar_wait(&do_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(dp_empty, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t da = smem_u32(sDO + st * L::kDO), qa = smem_u32(sQ + st * L::kQ);
 #pragma unroll
-        for (int kk = 0; kk < DQ / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSubTile + (kk & 3) * 32;
-          tc_mma_f16(tSdP, umma_desc_sw128(ka + off, 16, 1024), umma_desc_sw128(qa + off, 16, 1024), idesc_s,
-                     kk > 0 ? 1u : 0u);
-        }
-        tc_commit(s_full);
-        if (!mbar_wait(sp_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-        if (!mbar_wait(do_full, ph, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < DV / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSubTile + (kk & 3) * 32;
-          tc_mma_f16(tSdP, umma_desc_sw128(va + off, 16, 1024), umma_desc_sw128(da + off, 16, 1024), idesc_s,
-                     kk > 0 ? 1u : 0u);
-        }
-        // dV += P^T dO   (dO tile read as MN-major: d contiguous, q rows at 128 B)
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kSubTile + (kk & 3) * 32;
-          tc_mma_f16(tdV, umma_desc_sw128(pa + aoff, 16, 1024), umma_desc_sw128(da + kk * 2048, kSubTile, 1024),
-                     idesc_dv, (it > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < DV / 16; ++kk)
+          tc_mma_f16(tdP, umma_desc_sw128(va + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
+                     umma_desc_sw128(da + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         tc_commit(dp_full);
-        tc_commit(do_empty);
+        // dV += P^T dO  (dO read as MN-major: DV contiguous, 64-row sub-tiles)
+        if (!mbar_wait(pt_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          tc_mma_f16(tdV, umma_desc_sw128(pa + kk * 32, 16, 1024), umma_desc_sw128(da + kk * 2048, 8192, 1024),
+                     idesc_dv, (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(pt_free);
+        tc_commit(&do_empty[st]);
+        // dK += dS^T Q  (Q read as MN-major)
         if (!mbar_wait(ds_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
-        // dK += dS^T Q   (Q tile read as MN-major)
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kSubTile + (kk & 3) * 32;
-          tc_mma_f16(tdK, umma_desc_sw128(pa + aoff, 16, 1024), umma_desc_sw128(qa + kk * 2048, kSubTile, 1024),
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          tc_mma_f16(tdK, umma_desc_sw128(dsa + kk * 32, 16, 1024), umma_desc_sw128(qa + kk * 2048, 8192, 1024),
                      idesc_dk, (it > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(q_empty);
-        tc_commit(pds_free);
+        tc_commit(ds_free);
+        tc_commit(&q_empty[st]);
       }
       tc_commit(acc_done);
       mbar_wait(acc_done, 0, p.status, STATUS_TIMEOUT_DRAIN);
@@ -530,62 +553,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else {
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // kv row
-    const int sm_tid = threadIdx.x - 64;
     const int kpos = kpos0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
     for (int it = 0; it < n; ++it) {
-      const int g = it / nq, i = i_lo + it % nq;
-      const int hq = hk * G + g;
-      const int qpos0 = i * kTile;
+      const int i = i_lo + it % nq;
+      const int qpos0 = i * BQ;
+      const int st = it & 1;
+      const uint32_t u = it >> 1;
       const uint32_t ph = it & 1;
-      // previous readers of s_lse/s_delta are done -> refill -> wait for all writers
-      if (!mbar_wait(vec_empty, ph ^ 1, p.status, STATUS_TIMEOUT_OTHER)) { ok = false; break; }
-      {
-        const long long idx = (long long)hq * p.T + b * p.S + qpos0 + sm_tid;
-        s_lse[sm_tid] = p.lse[idx] * kLog2e;
-        s_delta[sm_tid] = p.delta[idx];
-      }
-      mbar_arrive(vec_full);
-      if (!mbar_wait(vec_full, ph, p.status, STATUS_TIMEOUT_OTHER)) { ok = false; break; }
-      if (!mbar_wait(s_full, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
+      // lse / delta of this tile arrived with Q (make the bulk-copy writes visible here)
+      if (!mbar_wait(&q_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
+      if (!mbar_wait(&s_full[st], u & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
       tc_fence_after();
-      if (it > 0 && !mbar_wait(pds_free, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-      float P[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tSdP + c * 32 + lane_off, P + c * 32);
+      float P[BQ];
+      tmem_ld32(tS0 + st * 64 + lane_off, P);
+      tmem_ld32(tS0 + st * 64 + 32 + lane_off, P + 32);
       tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[st]);
+      const float* lse = sVec + st * 2 * BQ;
+      const float* delta = lse + BQ;
       const bool need_mask = (p.causal && kpos0 + kTile - 1 > qpos0) ||
-                             (p.window > 0 && kpos0 <= qpos0 + kTile - 1 - p.window);
+                             (p.window > 0 && kpos0 <= qpos0 + BQ - 1 - p.window);
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = exp2f(P[c] * p.scale_log2 - s_lse[c]);
+      for (int c = 0; c < BQ; ++c) {
+        float v = exp2f(P[c] * p.scale_log2 - lse[c] * kLog2e);
         if (need_mask) {
           const int qp = qpos0 + c;
           if ((p.causal && kpos > qp) || (p.window > 0 && kpos <= qp - p.window)) v = 0.f;
         }
         P[c] = v;
       }
-      store_row_sw128(sP, r, P);
+      // P^T buffer free once dV of the previous tile has read it
+      if (it > 0 && !mbar_wait(pt_free, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
+      store_chunk32_sw128(sPT, r, 0, P);
+      store_chunk32_sw128(sPT, r, 1, P + 32);
       fence_proxy_async_smem();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(sp_ready);
+      if (lane == 0) mbar_arrive(pt_ready);
       if (!mbar_wait(dp_full, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float d[32];
-        tmem_ld32(tSdP + c * 32 + lane_off, d);
-        tc_wait_ld();
-#pragma unroll
-        for (int k = 0; k < 32; ++k) d[k] = P[c * 32 + k] * (d[k] - s_delta[c * 32 + k]) * p.scale;
-        store_chunk32_sw128(sP, r, c, d);
-      }
-      mbar_arrive(vec_empty);
+      float d[BQ];
+      tmem_ld32(tdP + lane_off, d);
+      tmem_ld32(tdP + 32 + lane_off, d + 32);
+      tc_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(sdp_empty);
+      if (lane == 0) mbar_arrive(dp_empty);
+#pragma unroll
+      for (int c = 0; c < BQ; ++c) d[c] = P[c] * (d[c] - delta[c]) * p.scale;
+      if (it > 0 && !mbar_wait(ds_free, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
+      store_chunk32_sw128(sDS, r, 0, d);
+      store_chunk32_sw128(sDS, r, 1, d + 32);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
@@ -644,27 +665,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // ===========================================================================
 template <int DQ, int DV>
 struct DqSmem {
+  static constexpr int BK = 64;                      // key rows per iteration
   static constexpr int NQC = DQ / 64;
-  static constexpr int kQ = NQC * kSubTile;
-  static constexpr int kDO = (DV / 64) * kSubTile;
-  static constexpr int kK = NQC * kSubTile;
-  static constexpr int kV = (DV / 64) * kSubTile;
-  static constexpr int kS = 2 * kSubTile;
+  static constexpr int kQ = NQC * kSubTile;          // [128 q x DQ]
+  static constexpr int kDO = (DV / 64) * kSubTile;   // [128 q x DV]
+  static constexpr int kK = NQC * 8192;              // [64 kv x DQ] (64-row sub-tiles)
+  static constexpr int kV = (DV / 64) * 8192;        // [64 kv x DV]
   static constexpr int kOffQ = 0;
   static constexpr int kOffDO = kOffQ + kQ;
-  static constexpr int kOffK = kOffDO + kDO;
-  static constexpr int kOffV = kOffK + kK;
-  static constexpr int kOffS = kOffV + kV;
-  static constexpr int kOffBar = kOffS + kS;
+  static constexpr int kOffK = kOffDO + kDO;         // 2 stages
+  static constexpr int kOffV = kOffK + 2 * kK;       // 2 stages
+  static constexpr int kOffS = kOffV + 2 * kV;       // 2 stages of dS [128 q x 64 kv] bf16
+  static constexpr int kOffBar = kOffS + 2 * kSubTile;
   static constexpr int kBytes = kOffBar + 256 + 1024;
 };
 
+// CTA = (query tile of 128 rows, head, sequence); loops over key tiles of 64 rows.
+// K/V tiles, the S / dP accumulators (TMEM) and dS (shared memory) are all double
+// buffered: the next tile's loads and S = Q K^T, dP = dO V^T run while this
+// tile's dS is formed, and dQ += dS K of this tile follows.
+//   TMEM columns: S[2] = [0, 128), dP[2] = [128, 256), dQ = [256, 256 + DQ)
 template <int DQ, int DV, bool ROPE>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmKR, const __grid_constant__ CUtensorMap tmV,
                    const __grid_constant__ CUtensorMap tmDO, AttnArgs p) {
   using L = DqSmem<DQ, DV>;
+  constexpr int BK = L::BK;
   constexpr int NQC = L::NQC;
   constexpr int NKC = ROPE ? NQC - 1 : NQC;
   constexpr int VCH = DV / 64;
@@ -677,14 +704,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sS = smem + L::kOffS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 2;
-  uint64_t* sdp_full = bars + 3;
-  uint64_t* sdp_empty = bars + 4;  // count 4
-  uint64_t* ds_ready = bars + 5;   // count 4
-  uint64_t* ds_free = bars + 6;
-  uint64_t* acc_done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* kv_full = bars + 1;    // [2]
+  uint64_t* kv_empty = bars + 3;   // [2]
+  uint64_t* sdp_full = bars + 5;   // [2]
+  uint64_t* sdp_empty = bars + 7;  // [2] count 4
+  uint64_t* ds_ready = bars + 9;   // [2] count 4, per dS stage
+  uint64_t* ds_free = bars + 11;   // [2]
+  uint64_t* acc_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / kTile;
@@ -693,18 +720,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int hk = h / (p.H / p.Hk);
   const int t0 = b * p.S + qt * kTile;
   const int qpos0 = qt * kTile;
-  const int j_hi = p.causal ? qt : nqt - 1;
-  const int j_lo = p.window > 0 ? max(0, qpos0 - p.window + 1) / kTile : 0;
+  const int nkt = p.S / BK;
+  const int j_hi = p.causal ? (qpos0 + kTile - 1) / BK : nkt - 1;
+  const int j_lo = p.window > 0 ? max(0, qpos0 - p.window + 1) / BK : 0;
   const int n = j_hi - j_lo + 1;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(kv_full, 1);
-    mbar_init(kv_empty, 1);
-    mbar_init(sdp_full, 1);
-    mbar_init(sdp_empty, 4);
-    mbar_init(ds_ready, 4);
-    mbar_init(ds_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&sdp_empty[i], 4);
+      mbar_init(&ds_free[i], 1);
+      mbar_init(&ds_ready[i], 4);
+    }
     mbar_init(acc_done, 1);
     fence_barrier_init();
   }
@@ -716,7 +746,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tdP = tmem + 128, tdQ = tmem + 256;
+  const uint32_t tS0 = tmem, tdP0 = tmem + 128, tdQ = tmem + 256;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -726,52 +756,58 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < VCH; ++c) tma_load_3d(sDO + c * kSubTile, &tmDO, q_full, c * 64, h, t0);
       for (int jj = 0; jj < n; ++jj) {
-        const int kt0 = b * p.S + (j_lo + jj) * kTile;
-        if (!mbar_wait(kv_empty, (jj & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
-        mbar_arrive_expect_tx(kv_full, L::kK + L::kV);
+        const int kt0 = b * p.S + (j_lo + jj) * BK;
+        const int st = jj & 1;
+        const uint32_t u = jj >> 1;
+        if (!mbar_wait(&kv_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
+        mbar_arrive_expect_tx(&kv_full[st], L::kK + L::kV);
+        uint8_t* dK = sK + st * L::kK;
+        uint8_t* dV = sV + st * L::kV;
 #pragma unroll
-        for (int c = 0; c < NKC; ++c) tma_load_3d(sK + c * kSubTile, &tmK, kv_full, c * 64, hk, kt0);
-        if (ROPE) tma_load_2d(sK + NKC * kSubTile, &tmKR, kv_full, 0, kt0);
+        for (int c = 0; c < NKC; ++c) tma_load_3d(dK + c * 8192, &tmK, &kv_full[st], c * 64, hk, kt0);
+        if (ROPE) tma_load_2d(dK + NKC * 8192, &tmKR, &kv_full[st], 0, kt0);
 #pragma unroll
-        for (int c = 0; c < VCH; ++c) tma_load_3d(sV + c * kSubTile, &tmV, kv_full, c * 64, hk, kt0);
+        for (int c = 0; c < VCH; ++c) tma_load_3d(dV + c * 8192, &tmV, &kv_full[st], c * 64, hk, kt0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc_s = umma_idesc_f16(128, 128, false, false, true);
+      constexpr uint32_t idesc_s = umma_idesc_f16(128, BK, false, false, true);
       constexpr uint32_t idesc_dq = umma_idesc_f16(128, DQ, false, true, true);
       bool ok = mbar_wait(q_full, 0, p.status, STATUS_TIMEOUT_TMA_FULL);
-      const uint32_t qa = smem_u32(sQ), da = smem_u32(sDO), ka = smem_u32(sK), va = smem_u32(sV),
-                     sa = smem_u32(sS);
+      const uint32_t qa = smem_u32(sQ), da = smem_u32(sDO);
+      auto issue_sdp = [&](int jj) -> bool {
+        const int st = jj & 1;
+        const uint32_t u = jj >> 1;
+        if (!mbar_wait(&kv_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) return false;
+        if (!mbar_wait(&sdp_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sK + st * L::kK), va = smem_u32(sV + st * L::kV);
+#pragma unroll
+        for (int kk = 0; kk < DQ / 16; ++kk)
+          tc_mma_f16(tS0 + st * 64, umma_desc_sw128(qa + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
+                     umma_desc_sw128(ka + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk)
+          tc_mma_f16(tdP0 + st * 64, umma_desc_sw128(da + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
+                     umma_desc_sw128(va + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+        tc_commit(&sdp_full[st]);
+        return true;
+      };
+      if (ok && n > 0) ok = issue_sdp(0);
       for (int jj = 0; jj < n && ok; ++jj) {
-        const uint32_t ph = jj & 1;
-        if (!mbar_wait(kv_full, ph, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
-        if (!mbar_wait(sdp_empty, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) { ok = false; break; }
+        const int st = jj & 1;
+        if (jj + 1 < n && !issue_sdp(jj + 1)) { ok = false; break; }
+        if (!mbar_wait(&ds_ready[st], (jj >> 1) & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
+        // dQ += dS K   (K tile read as MN-major: d contiguous, 64-row sub-tiles)
+        const uint32_t sa = smem_u32(sS + st * kSubTile), ka = smem_u32(sK + st * L::kK);
 #pragma unroll
-        for (int kk = 0; kk < DQ / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSubTile + (kk & 3) * 32;
-          tc_mma_f16(tS, umma_desc_sw128(qa + off, 16, 1024), umma_desc_sw128(ka + off, 16, 1024), idesc_s,
-                     kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < DV / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSubTile + (kk & 3) * 32;
-          tc_mma_f16(tdP, umma_desc_sw128(da + off, 16, 1024), umma_desc_sw128(va + off, 16, 1024), idesc_s,
-                     kk > 0 ? 1u : 0u);
-        }
-        tc_commit(sdp_full);
-        if (!mbar_wait(ds_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-        tc_fence_after();
-        // dQ += dS K   (K tile read as MN-major: d contiguous, kv rows at 128 B)
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * kSubTile + (kk & 3) * 32;
-          tc_mma_f16(tdQ, umma_desc_sw128(sa + aoff, 16, 1024), umma_desc_sw128(ka + kk * 2048, kSubTile, 1024),
+        for (int kk = 0; kk < BK / 16; ++kk)
+          tc_mma_f16(tdQ, umma_desc_sw128(sa + kk * 32, 16, 1024), umma_desc_sw128(ka + kk * 2048, 8192, 1024),
                      idesc_dq, (jj > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(kv_empty);
-        tc_commit(ds_free);
+        tc_commit(&kv_empty[st]);
+        tc_commit(&ds_free[st]);
       }
       tc_commit(acc_done);
       mbar_wait(acc_done, 0, p.status, STATUS_TIMEOUT_DRAIN);
@@ -786,36 +822,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float dlt = p.delta[li];
     bool ok = true;
     for (int jj = 0; jj < n; ++jj) {
-      const uint32_t ph = jj & 1;
-      const int kpos0 = (j_lo + jj) * kTile;
-      if (!mbar_wait(sdp_full, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
+      const int st = jj & 1;
+      const uint32_t u = jj >> 1;
+      const int kpos0 = (j_lo + jj) * BK;
+      if (!mbar_wait(&sdp_full[st], u & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
       tc_fence_after();
-      if (jj > 0 && !mbar_wait(ds_free, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-      const bool need_mask = (p.causal && kpos0 + kTile - 1 > qpos0) ||
-                             (p.window > 0 && kpos0 <= qpos0 + kTile - 1 - p.window);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float s[32], d[32];
-        tmem_ld32(tS + c * 32 + lane_off, s);
-        tmem_ld32(tdP + c * 32 + lane_off, d);
-        tc_wait_ld();
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          float pv = exp2f(s[k] * p.scale_log2 - lse2);
-          if (need_mask) {
-            const int kp = kpos0 + c * 32 + k;
-            if ((p.causal && kp > qpos) || (p.window > 0 && kp <= qpos - p.window)) pv = 0.f;
-          }
-          d[k] = pv * (d[k] - dlt) * p.scale;
-        }
-        store_chunk32_sw128(sS, r, c, d);
-      }
+      float sv[BK], d[BK];
+      tmem_ld32(tS0 + st * 64 + lane_off, sv);
+      tmem_ld32(tS0 + st * 64 + 32 + lane_off, sv + 32);
+      tmem_ld32(tdP0 + st * 64 + lane_off, d);
+      tmem_ld32(tdP0 + st * 64 + 32 + lane_off, d + 32);
+      tc_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(sdp_empty);
+      if (lane == 0) mbar_arrive(&sdp_empty[st]);
+      const bool need_mask = (p.causal && kpos0 + BK - 1 > qpos0) ||
+                             (p.window > 0 && kpos0 <= qpos0 + kTile - 1 - p.window);
+#pragma unroll
+      for (int k = 0; k < BK; ++k) {
+        float pv = exp2f(sv[k] * p.scale_log2 - lse2);
+        if (need_mask) {
+          const int kp = kpos0 + k;
+          if ((p.causal && kp > qpos) || (p.window > 0 && kp <= qpos - p.window)) pv = 0.f;
+        }
+        d[k] = pv * (d[k] - dlt) * p.scale;
+      }
+      // this dS buffer was last read by dQ two tiles ago
+      if (jj >= 2 && !mbar_wait(&ds_free[st], ((u - 1) & 1), p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
+      store_chunk32_sw128(sS + st * kSubTile, r, 0, d);
+      store_chunk32_sw128(sS + st * kSubTile, r, 1, d + 32);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ds_ready);
+      if (lane == 0) mbar_arrive(&ds_ready[st]);
     }
     if (ok && n > 0 && mbar_wait(acc_done, 0, p.status, STATUS_TIMEOUT_TMEM_FULL)) {
       tc_fence_after();
@@ -867,10 +905,10 @@ static CUtensorMap map_heads(const void* base, int d, int heads, int T, long lon
   return make_tmap_bf16(base, 3, dims, str, box, what);
 }
 
-static CUtensorMap map_rope(const void* base, int T, long long row, const char* what) {
+static CUtensorMap map_rope(const void* base, int T, long long row, const char* what, int box_rows = 128) {
   uint64_t dims[2] = {64, (uint64_t)T};
   uint64_t str[1] = {(uint64_t)row * 2};
-  uint32_t box[2] = {64, 128};
+  uint32_t box[2] = {64, (uint32_t)box_rows};
   return make_tmap_bf16(base, 2, dims, str, box, what);
 }
 
@@ -939,17 +977,22 @@ static void bwd_impl(const AttnTensors& a, const void* o, const float* lse, cons
   p.status = (StatusBlock*)status;
   {
     using L = DkdvSmem<DQ, DV>;
+    CUtensorMap tq64 = map_heads(a.q, DQ, a.H, a.T, a.q_row, a.q_head, L::BQ, "attention q (64-row tiles)");
+    CUtensorMap tdo64 = map_heads(dO, DV, a.H, a.T, (long long)a.H * DV, DV, L::BQ, "attention dO (64-row tiles)");
     auto kern = attn_dkdv_kernel<DQ, DV, ROPE>;
     set_smem(kern, L::kBytes);
     dim3 grid(a.S / kTile, a.Hk, a.T / a.S);
-    kern<<<grid, kAttnThreads, L::kBytes, s>>>(tq, tk, tkr, tv, tdo, p);
+    kern<<<grid, kAttnThreads, L::kBytes, s>>>(tq64, tk, tkr, tv, tdo64, p);
   }
   {
     using L = DqSmem<DQ, DV>;
+    CUtensorMap tk64 = map_heads(a.k, DK, a.Hk, a.T, a.k_row, a.k_head, L::BK, "attention k (64-row tiles)");
+    CUtensorMap tkr64 = ROPE ? map_rope(a.kr, a.T, a.kr_row, "attention k_rope (64-row tiles)", L::BK) : tk64;
+    CUtensorMap tv64 = map_heads(a.v, DV, a.Hk, a.T, a.v_row, a.v_head, L::BK, "attention v (64-row tiles)");
     auto kern = attn_dq_kernel<DQ, DV, ROPE>;
     set_smem(kern, L::kBytes);
     dim3 grid(a.S / kTile, a.H, a.T / a.S);
-    kern<<<grid, kAttnThreads, L::kBytes, s>>>(tq, tk, tkr, tv, tdo, p);
+    kern<<<grid, kAttnThreads, L::kBytes, s>>>(tq, tk64, tkr64, tv64, tdo, p);
   }
 }
 
