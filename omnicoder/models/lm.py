@@ -62,16 +62,35 @@ class Norm(nn.Module):
         return rms_norm(x, self.weight, self.eps)
 
 
-class GQAttention(nn.Module):
-    """MHA (n_kv_heads == n_heads) or GQA with a fused QKV projection."""
+def _tp_param(t: torch.Tensor) -> nn.Parameter:
+    p = nn.Parameter(t.contiguous())
+    p.tp_sharded = True
+    return p
 
-    def __init__(self, cfg: ModelConfig):
+
+class GQAttention(nn.Module):
+    """MHA (n_kv_heads == n_heads) or GQA with a fused QKV projection.  With a
+    tensor-parallel context (`tp`, omnicoder.parallel.tensor) this rank holds
+    n_heads / N query heads and n_kv_heads / N kv heads; the block input is its
+    token shard (sequence parallel) and is all-gathered before the projection,
+    the output projection's partial sums are reduce-scattered back."""
+
+    def __init__(self, cfg: ModelConfig, tp=None):
         super().__init__()
         self.cfg = cfg
+        self.tp = tp
         D, H, Hk, hd = cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim
         self.H, self.Hk, self.hd = H, Hk, hd
         self.wqkv = _init(_empty((H + 2 * Hk) * hd, D), cfg.init_std)
         self.wo = _init(_empty(D, H * hd), cfg.init_std)
+        if tp is not None:
+            h0, h1 = tp.shard(H, "query heads")
+            k0, k1 = tp.shard(Hk, "kv heads")
+            w = self.wqkv.data
+            self.wqkv = _tp_param(torch.cat([w[h0 * hd:h1 * hd], w[(H + k0) * hd:(H + k1) * hd],
+                                             w[(H + Hk + k0) * hd:(H + Hk + k1) * hd]]))
+            self.wo = _tp_param(self.wo.data[:, h0 * hd:h1 * hd])
+            self.H, self.Hk = h1 - h0, k1 - k0
 
     def qkv(self, y, rope: RopeTable, positions):
         T = y.shape[0]
@@ -83,6 +102,12 @@ class GQAttention(nn.Module):
         return q, k, v, None
 
     def forward(self, y, h, rope, positions, seq):
+        if self.tp is not None:
+            from ..parallel.tensor import all_gather_seq, reduce_scatter_seq
+            yf = all_gather_seq(y, self.tp)
+            q, k, v, kr = self.qkv(yf, rope, positions)
+            o = attention(q, k, v, kr, seq=seq, causal=True, window=self.cfg.attn.window)
+            return reduce_scatter_seq(linear(o.reshape(yf.shape[0], -1), self.wo), self.tp) + h
         q, k, v, kr = self.qkv(y, rope, positions)
         o = attention(q, k, v, kr, seq=seq, causal=True, window=self.cfg.attn.window)
         return linear(o.reshape(y.shape[0], -1), self.wo, residual=h)
@@ -182,12 +207,25 @@ class MLAttention(nn.Module):
 
 
 class DenseFFN(nn.Module):
-    def __init__(self, D: int, F: int, std: float):
+    """SwiGLU MLP.  With `tp` this rank holds F / N hidden features (a contiguous
+    slice of the 32-row interleaved gate/up rows) and runs sequence parallel."""
+
+    def __init__(self, D: int, F: int, std: float, tp=None):
         super().__init__()
+        self.tp = tp
         self.w13 = _init(_empty(2 * F, D), std)
         self.w2 = _init(_empty(D, F), std)
+        if tp is not None:
+            f0, f1 = tp.shard(F, "ffn dim")
+            if (f1 - f0) % 32:
+                raise ValueError("tensor-parallel ffn shards must be multiples of 32 features")
+            self.w13 = _tp_param(self.w13.data[2 * f0:2 * f1])
+            self.w2 = _tp_param(self.w2.data[:, f0:f1])
 
     def forward(self, y, h):
+        if self.tp is not None:
+            from ..parallel.tensor import all_gather_seq, reduce_scatter_seq
+            return reduce_scatter_seq(swiglu_mlp(all_gather_seq(y, self.tp), self.w13, self.w2), self.tp) + h, None
         return swiglu_mlp(y, self.w13, self.w2, residual=h), None
 
 
@@ -230,12 +268,14 @@ class MoEFFN(nn.Module):
 
 
 class Block(nn.Module):
-    def __init__(self, cfg: ModelConfig, layer: int, ep=None):
+    def __init__(self, cfg: ModelConfig, layer: int, ep=None, tp=None):
         super().__init__()
+        if tp is not None and (cfg.attn.kind == "mla" or cfg.is_moe_layer(layer)):
+            raise NotImplementedError("tensor parallelism covers dense GQA/MHA blocks; use expert parallelism for MoE")
         self.attn_norm = Norm(cfg.d_model, cfg.norm, cfg.norm_eps)
-        self.attn = MLAttention(cfg) if cfg.attn.kind == "mla" else GQAttention(cfg)
+        self.attn = MLAttention(cfg) if cfg.attn.kind == "mla" else GQAttention(cfg, tp)
         self.ffn_norm = Norm(cfg.d_model, cfg.norm, cfg.norm_eps)
-        self.ffn = MoEFFN(cfg, ep) if cfg.is_moe_layer(layer) else DenseFFN(cfg.d_model, cfg.ffn_dim, cfg.init_std)
+        self.ffn = MoEFFN(cfg, ep) if cfg.is_moe_layer(layer) else DenseFFN(cfg.d_model, cfg.ffn_dim, cfg.init_std, tp)
 
     def forward(self, h, rope, positions, seq):
         h = self.attn(self.attn_norm(h), h, rope, positions, seq)
@@ -251,12 +291,13 @@ class OmniLM(nn.Module):
     `loss` (CE + auxiliary), `ce`, `aux` and, without labels, `logits` of the last
     position (or all positions with `all_logits=True`)."""
 
-    def __init__(self, cfg: ModelConfig, ep=None):
+    def __init__(self, cfg: ModelConfig, ep=None, tp=None):
         super().__init__()
         self.cfg = cfg
+        self.tp = tp
         D, V = cfg.d_model, cfg.vocab_size
         self.embed = _init(_empty(V, D), cfg.init_std)
-        self.blocks = nn.ModuleList([Block(cfg, i, ep) for i in range(cfg.n_layers)])
+        self.blocks = nn.ModuleList([Block(cfg, i, ep, tp) for i in range(cfg.n_layers)])
         self.norm_f = Norm(D, cfg.norm, cfg.norm_eps)
         self.lm_head = None if cfg.tie_embeddings else _init(_empty(V, D), cfg.init_std)
         self.mtp_heads = nn.ParameterList([_init(_empty(V, D), cfg.init_std) for _ in range(cfg.mtp_heads)])
@@ -279,7 +320,11 @@ class OmniLM(nn.Module):
         B, S = ids.shape
         if ids.is_cuda:
             self.rope.to(ids.device)
-        h = embedding(ids.reshape(-1), self.embed)
+        flat = ids.reshape(-1)
+        if self.tp is not None:                       # sequence parallel: this rank's token shard
+            from ..parallel.tensor import scatter_seq
+            flat = scatter_seq(flat, self.tp)
+        h = embedding(flat, self.embed)
         if positions is None:
             positions = torch.arange(S, device=ids.device).repeat(B)
         aux_total = None
@@ -293,6 +338,9 @@ class OmniLM(nn.Module):
                 assume_all_valid: bool = False):
         y, aux = self.hidden(ids)
         out = {}
+        if labels is not None and self.tp is not None:
+            from ..parallel.tensor import scatter_seq
+            labels = scatter_seq(labels.reshape(-1), self.tp)
         if labels is not None:
             ce = lm_head_cross_entropy(y, self.head_weight, labels, assume_all_valid=assume_all_valid)
             loss = ce
@@ -361,7 +409,7 @@ class OmniLM(nn.Module):
         return self.load_state_dict(merged, strict=strict)
 
 
-def build_model(cfg: ModelConfig, device="cpu", dtype=None, seed: int | None = 0, ep=None) -> OmniLM:
+def build_model(cfg: ModelConfig, device="cpu", dtype=None, seed: int | None = 0, ep=None, tp=None) -> OmniLM:
     """Random-init model N(0, init_std) created directly on `device` (bf16 on CUDA,
     fp32 on CPU by default).  `ep`: an expert-parallel layout
     (omnicoder.parallel.expert_data.ExpertDataParallel) -- the model then holds
@@ -376,7 +424,7 @@ def build_model(cfg: ModelConfig, device="cpu", dtype=None, seed: int | None = 0
     old = _FACTORY
     _FACTORY = {"device": torch.device(device), "dtype": dtype}
     try:
-        m = OmniLM(cfg, ep)
+        m = OmniLM(cfg, ep, getattr(tp, "tp", tp))
     finally:
         _FACTORY = old
     m.rope.to(device)

@@ -1,0 +1,65 @@
+"""1F1B pipeline over 2 CPU stages (gloo point-to-point): the loss and the
+updated parameters of each stage must equal one process on the same batch."""
+import os
+import socket
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from omnicoder.config import AttentionConfig, ModelConfig, TrainConfig
+
+
+def _cfg():
+    return ModelConfig(name="pp_test", vocab_size=300, d_model=64, n_layers=4, n_heads=4, ffn_dim=128,
+                       tie_embeddings=False, max_seq_len=64, attn=AttentionConfig(kind="gqa", n_kv_heads=2))
+
+
+def _tc():
+    return TrainConfig(lr=1e-3, warmup_steps=0, max_steps=10, grad_clip=0.5, weight_decay=0.1, eps=1e-6,
+                       betas=(0.9, 0.95))
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from omnicoder.models.lm import build_model
+        from omnicoder.parallel.pipeline import PipelineTrainer
+        from omnicoder.training.engine import Trainer
+
+        g = torch.Generator().manual_seed(9)
+        ids = torch.randint(0, 300, (8, 16), generator=g)
+        lab = torch.randint(0, 300, (8, 16), generator=g)
+        ref = build_model(_cfg(), device="cpu", seed=0)
+        rt = Trainer(ref, _tc())
+        ref_losses = [float(rt.step(ids, lab).loss) for _ in range(2)]
+        m = build_model(_cfg(), device="cpu", seed=0)
+        pt = PipelineTrainer(m, _tc(), n_micro=4)
+        losses = [float(pt.step(ids, lab)) for _ in range(2)]
+        rsd = ref.state_dict()
+        names = {id(p): n for n, p in m.named_parameters()}
+        worst = max(float((p - rsd[names[id(p)]]).abs().max()) for p in pt.stage.parameters())
+        q.put((rank, ref_losses, losses, worst))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_pipeline_1f1b_matches_single_process():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ref, got, worst in res:
+        for a, b in zip(ref, got):
+            assert abs(a - b) < 1e-4, (rank, ref, got)
+        assert worst < 1e-4, (rank, worst)
