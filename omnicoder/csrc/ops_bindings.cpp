@@ -414,6 +414,29 @@ at::Tensor int4_dequant_t(const at::Tensor& w, const at::Tensor& scale, int64_t 
   return out;
 }
 
+// ---- Gaussian splatting ------------------------------------------------------
+std::vector<at::Tensor> gsplat_forward_t(const at::Tensor& u, const at::Tensor& v, const at::Tensor& sx,
+                                         const at::Tensor& sy, const at::Tensor& opa, const at::Tensor& rgb,
+                                         const c10::optional<at::Tensor>& z, int64_t H, int64_t W, int64_t k) {
+  for (const at::Tensor* t : {&u, &v, &sx, &sy, &opa, &rgb}) check_f32(*t, "gsplat input");
+  const c10::cuda::CUDAGuard g(u.device());
+  const int64_t B = u.size(0), N = u.size(1);
+  TORCH_CHECK(rgb.numel() == B * N * 3 && opa.numel() == B * N, "gsplat: shapes");
+  auto acc = at::empty({B, 5, H, W}, u.options());
+  auto out = at::empty({B, 3, H, W}, u.options());
+  at::Tensor depth;
+  if (z.has_value()) {
+    check_f32(*z, "z");
+    depth = at::empty({B, 1, H, W}, u.options());
+  }
+  gsplat_forward(u.data_ptr<float>(), v.data_ptr<float>(), sx.data_ptr<float>(), sy.data_ptr<float>(),
+                 opa.data_ptr<float>(), rgb.data_ptr<float>(), z.has_value() ? z->data_ptr<float>() : nullptr,
+                 acc.data_ptr<float>(), out.data_ptr<float>(), z.has_value() ? depth.data_ptr<float>() : nullptr,
+                 (int)B, (int)N, (int)H, (int)W, (int)k, stream());
+  if (z.has_value()) return {out, depth};
+  return {out};
+}
+
 void register_kernels(pybind11::module_& m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd_t, py::arg("x"), py::arg("res"), py::arg("w"), py::arg("eps"));
   m.def("rmsnorm_bwd", &rmsnorm_bwd_t, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dres"));
@@ -437,6 +460,7 @@ void register_kernels(pybind11::module_& m) {
   m.def("moe_combine_bwd", &moe_combine_bwd_t);
   m.def("moe_scatter_add", &moe_scatter_add_t);
   m.def("router_bwd", &router_bwd_t);
+  m.def("gsplat_forward", &gsplat_forward_t);
   m.def("int4_gemv", &int4_gemv_t, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("offset"));
   m.def("int4_dequant", &int4_dequant_t, py::arg("w"), py::arg("scale"), py::arg("K"), py::arg("offset"));
   m.def("attn_decode", &attn_decode_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_scale"),

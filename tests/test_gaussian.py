@@ -1,0 +1,77 @@
+"""Gaussian splatting: the vectorised CPU formulation against a per-tap loop,
+gradients on CPU, and the CUDA splat kernel against the CPU formulation."""
+import pytest
+import torch
+
+from omnicoder.models.gaussian import GaussianSplatRenderer2D, GaussianSplatRenderer3D
+
+
+
+def _scene(B=2, N=300, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    pos = torch.randn(B, N, 3, generator=g) * 0.5 + torch.tensor([0.0, 0.0, 4.0])
+    cov_diag = torch.rand(B, N, 3, generator=g) * 0.01 + 0.001
+    rgb = torch.rand(B, N, 3, generator=g)
+    opa = torch.rand(B, N, 1, generator=g)
+    K = torch.tensor([[60.0, 0, 32], [0, 60.0, 24], [0, 0, 1]]).expand(B, 3, 3).contiguous()
+    R = torch.eye(3).expand(B, 3, 3).contiguous()
+    t = torch.zeros(B, 3)
+    return pos, cov_diag, rgb, opa, K, R, t
+
+
+def _brute_force(u, v, sx, sy, opa, rgb, z, H, W, k):
+    """Per-tap loop of the splat formulation (independent of the vectorised code)."""
+    B, N = u.shape
+    num = torch.zeros(B, 3, H, W, dtype=torch.float64)
+    den = torch.zeros(B, H, W, dtype=torch.float64)
+    dep = torch.zeros(B, H, W, dtype=torch.float64)
+    for b in range(B):
+        for n in range(N):
+            for oy in range(-(k // 2), k // 2 + 1):
+                for ox in range(-(k // 2), k // 2 + 1):
+                    px = round(float(u[b, n]) + ox * float(sx[b, n]))
+                    py = round(float(v[b, n]) + oy * float(sy[b, n]))
+                    if not (0 <= px < W and 0 <= py < H):
+                        continue
+                    gx, gy = ox / max(float(sx[b, n]), 1e-6), oy / max(float(sy[b, n]), 1e-6)
+                    a = float(opa[b, n]) * torch.exp(torch.tensor(-0.5 * (gx * gx + gy * gy), dtype=torch.float64))
+                    num[b, :, py, px] += a * rgb[b, n].double()
+                    den[b, py, px] += a
+                    if z is not None:
+                        dep[b, py, px] += a * float(z[b, n])
+    dc = den.clamp_min(1e-6)
+    return (num / dc[:, None]).float(), (dep / dc)[:, None].float()
+
+
+def test_matches_brute_force_formulation():
+    # the reference's renderers cannot serve as the oracle: its 3D renderer raises a shape
+    # error for every input tried and its 2D renderer reshapes a [pixels, 3] buffer into
+    # [3, H, W]; this checks the documented formulation with a per-tap loop instead
+    from omnicoder.models.gaussian import project_gaussians, splat_torch
+    pos, cd, rgb, opa, K, R, t = _scene(B=1, N=12)
+    u, v, z, sx, sy = project_gaussians(pos, None, cd, rgb, K, R, t)
+    sx, sy = sx * 40, sy * 40                     # visible footprints on a 48 x 64 image
+    want_rgb, want_d = _brute_force(u, v, sx, sy, opa.reshape(1, -1), rgb, z, 48, 64, 5)
+    got_rgb, got_d = splat_torch(u, v, sx, sy, opa.reshape(1, -1), rgb, z, 48, 64, 5)
+    assert torch.allclose(got_rgb, want_rgb, atol=1e-5) and torch.allclose(got_d, want_d, atol=1e-4)
+    g2 = GaussianSplatRenderer2D(5)(torch.stack([u, v], -1), torch.stack([sx * sx, sy * sy], -1), rgb, opa, (48, 64))
+    assert torch.allclose(g2, want_rgb, atol=1e-5)
+
+
+def test_gradients_flow_on_cpu():
+    pos, cd, rgb, opa, K, R, t = _scene(B=1, N=50)
+    rgb.requires_grad_(True)
+    opa.requires_grad_(True)
+    out, _ = GaussianSplatRenderer3D(7)(pos, None, cd, rgb, opa, K, R, t, (48, 64))
+    out.sum().backward()
+    assert rgb.grad is not None and opa.grad is not None
+
+
+@pytest.mark.gpu
+def test_cuda_kernel_matches_cpu():
+    pos, cd, rgb, opa, K, R, t = _scene(B=2, N=5000)
+    ref_rgb, ref_d = GaussianSplatRenderer3D(11)(pos, None, cd, rgb, opa, K, R, t, (96, 128))
+    with torch.no_grad():
+        args = [x.cuda() for x in (pos, cd, rgb, opa, K, R, t)]
+        out_rgb, out_d = GaussianSplatRenderer3D(11)(args[0], None, *args[1:], (96, 128))
+    assert torch.allclose(out_rgb.cpu(), ref_rgb, atol=1e-4) and torch.allclose(out_d.cpu(), ref_d, atol=1e-3)
