@@ -4,9 +4,11 @@
 //   k      [B, L, Hk, DQ]  bf16 or int8 (+ fp32 scale per (b, pos, kv head))
 //   v      [B, L, Hk, DV]  bf16 or int8 (+ scale); MLA latent cache: v == nullptr,
 //                          the value is the first DV dims of each key row
-//   q_pos  [B, Tn] absolute positions; kv_len [B] valid cache length.
-// Key p is visible to query (b, t) when p < kv_len[b], p <= q_pos[b, t] and,
-// with a window, p > q_pos[b, t] - window.
+//   q_pos  [B, Tn] absolute positions; kv_len [B] number of cached tokens.
+// Token position p lives in cache row sink_rows + p and is visible to query
+// (b, t) when p < kv_len[b], p <= q_pos[b, t] and, with a window,
+// p > q_pos[b, t] - window.  Rows [0, n_sink) hold compressed memory of tokens
+// that left the window and are visible to every query.
 //
 // Kernel 1 (grid = B x Hk x splits, 256 threads): the CTA keeps the R = Tn * G
 // query rows of one KV group (G = H / Hk heads; MLA: all heads share the
@@ -52,6 +54,7 @@ struct DecArgs {
   float* part_o;  // [B, Hk, splits, R, DV]
   float* part_ml;  // [B, Hk, splits, R, 2]
   int B, Tn, H, Hk, L, DQ, DV, window, splits;
+  int sink_rows, n_sink;          // cache rows reserved before the tokens / how many of them are valid
   long long k_b, k_l, v_b, v_l;  // element strides of the caches (batch, position); head stride = DQ / DV
   long long s_b, s_l;            // scale strides (batch, position); head stride 1
   float scale;
@@ -168,10 +171,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_split_kernel(DecArgs a)
     sL[tid] = 0.f;
   }
   // ---- key range of this split ----------------------------------------------
+  // key tiles: first the always-visible memory rows [0, n_sink), then the token rows
+  // sink_rows + [lo, hi) that the window and causality allow
   const int len = a.kv_len[b];
   const int hi = min(len, pmax + 1);
   const int lo = a.window > 0 ? max(0, pmin - a.window + 1) : 0;
-  const int ntiles_all = hi > lo ? (hi - lo + kKT - 1) / kKT : 0;
+  const int nsk = (a.n_sink + kKT - 1) / kKT;
+  const int ntiles_all = nsk + (hi > lo ? (hi - lo + kKT - 1) / kKT : 0);
   const int per = (ntiles_all + a.splits - 1) / a.splits;
   const int t0 = split * per, t1 = min(ntiles_all, t0 + per);
 
@@ -184,8 +190,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_split_kernel(DecArgs a)
 #pragma unroll
   for (int i = 0; i < kPvRows; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
+  auto row_of = [&](int tile) { return tile < nsk ? tile * kKT : a.sink_rows + lo + (tile - nsk) * kKT; };
   auto issue = [&](int tile, int buf) {
-    const int p0 = lo + tile * kKT;
+    const int p0 = row_of(tile);
     KV* dk = sK + buf * (kKT * DQ);
     const int kchunks = DQ * (int)sizeof(KV) / 16;
     for (int i = tid; i < kKT * kchunks; i += kDecThreads) {
@@ -218,7 +225,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_split_kernel(DecArgs a)
       cp_async_wait_all();
     }
     __syncthreads();
-    const int p0 = lo + tile * kKT;
+    const int p0 = row_of(tile);
+    const bool sink_tile = tile < nsk;
     const KV* tK = sK + buf * (kKT * DQ);
     // ---- scores: thread = (key kk, rows rgs, rgs+8, ...) ---------------------
     {
@@ -244,7 +252,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_split_kernel(DecArgs a)
         const int r = rgs + 8 * i;
         if (r < R) {
           const int qp = sPos[r];
-          const bool ok = p < len && p <= qp && (a.window <= 0 || p > qp - a.window);
+          const int tp = p - a.sink_rows;
+          const bool ok = sink_tile ? (p < a.n_sink)
+                                    : (tp < len && tp <= qp && (a.window <= 0 || tp > qp - a.window));
           sP[r * kKT + kk] = ok ? s[i] * ksc * a.scale : -INFINITY;
         }
       }
@@ -384,7 +394,7 @@ size_t decode_workspace_floats(int B, int Hk, int splits, int DV) {
 void attn_decode(const void* q, const void* k, const void* v, const float* ks, const float* vs, bool int8_kv,
                  const int* q_pos, const int* kv_len, void* out, float* workspace, int B, int Tn, int H, int Hk,
                  int L, int DQ, int DV, long long k_b, long long k_l, long long v_b, long long v_l, long long s_b,
-                 long long s_l, int window, float scale, int splits, cudaStream_t s) {
+                 long long s_l, int window, float scale, int splits, int sink_rows, int n_sink, cudaStream_t s) {
   const bool latent = v == nullptr;
   const int G = H / Hk;
   if (Tn * G > kMaxRows) throw std::runtime_error("attn_decode: Tn * heads-per-kv-group must be <= 64");
@@ -415,6 +425,8 @@ void attn_decode(const void* q, const void* k, const void* v, const float* ks, c
   a.DV = DV;
   a.window = window;
   a.splits = splits;
+  a.sink_rows = sink_rows;
+  a.n_sink = n_sink;
   a.k_b = k_b;
   a.k_l = k_l;
   a.v_b = v_b;

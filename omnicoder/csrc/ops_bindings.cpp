@@ -337,7 +337,7 @@ std::vector<at::Tensor> attn_bwd_t(const at::Tensor& q, const at::Tensor& k, con
 at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::optional<at::Tensor>& v,
                          const c10::optional<at::Tensor>& ks, const c10::optional<at::Tensor>& vs,
                          const at::Tensor& q_pos, const at::Tensor& kv_len, int64_t window, double scale,
-                         int64_t latent_v_dim) {
+                         int64_t latent_v_dim, int64_t sink_rows, int64_t n_sink) {
   check_bf16(q, "q");
   check_i32(q_pos, "q_pos");
   check_i32(kv_len, "kv_len");
@@ -365,6 +365,7 @@ at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::op
     v_l = v->stride(1);
   }
   TORCH_CHECK(H % Hk == 0, "attn_decode: heads must be a multiple of kv heads");
+  TORCH_CHECK(0 <= n_sink && n_sink <= sink_rows && sink_rows <= L, "attn_decode: memory rows");
   long long s_b = 0, s_l = 0;
   if (int8_kv) {
     TORCH_CHECK(ks.has_value() && ks->scalar_type() == at::kFloat && ks->is_cuda(), "attn_decode: int8 needs k scales");
@@ -383,7 +384,7 @@ at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::op
               (int8_kv && vs.has_value()) ? vs->data_ptr<float>() : nullptr, int8_kv, q_pos.data_ptr<int>(),
               kv_len.data_ptr<int>(), out.data_ptr(), ws.data_ptr<float>(), (int)B, (int)Tn, (int)H, (int)Hk, (int)L,
               (int)DQ, (int)DV, k.stride(0), k.stride(1), v_b, v_l, s_b, s_l, (int)window, (float)scale, splits,
-              stream());
+              (int)sink_rows, (int)n_sink, stream());
   return out;
 }
 
@@ -465,7 +466,7 @@ void register_kernels(pybind11::module_& m) {
   m.def("int4_dequant", &int4_dequant_t, py::arg("w"), py::arg("scale"), py::arg("K"), py::arg("offset"));
   m.def("attn_decode", &attn_decode_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_scale"),
         py::arg("v_scale"), py::arg("q_pos"), py::arg("kv_len"), py::arg("window"), py::arg("scale"),
-        py::arg("latent_v_dim"));
+        py::arg("latent_v_dim"), py::arg("sink_rows") = 0, py::arg("n_sink") = 0);
   m.def("attn_fwd", &attn_fwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_rope"), py::arg("seq"),
         py::arg("causal"), py::arg("window"), py::arg("scale"));
   m.def("attn_bwd", &attn_bwd_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_rope"), py::arg("o"),

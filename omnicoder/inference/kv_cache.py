@@ -9,7 +9,12 @@ Per layer:
     (absorbed up-projections, see OmniLM.prepare_inference).
 
 `lengths[b]` counts the cached positions of sequence b; writes go to
-positions lengths[b] .. lengths[b]+T_new-1.  Quantisation is symmetric:
+positions lengths[b] .. lengths[b]+T_new-1, stored at cache rows
+`sink + position`.  With `cfg.attn.mem_slots` = M > 0 the first M rows hold
+compressed memory: `compress_memory()` summarises the tokens that fell out of
+the attention window into M segment means (the reference's CompressiveKV
+segment pooling, src/omnicoder/modeling/memory.py:77-178, without its learned
+gates), which every later query attends to.  Quantisation is symmetric:
 q = round(x / s), s = max|x| / 127 over the quantised group (the reference
 quantises per group of 64 with min/max zero points, src/omnicoder/modeling/
 quant/kv_cache.py:108-257; the per-head per-token symmetric scale keeps the
@@ -42,9 +47,12 @@ class KVCache:
         assert kv_dtype in ("bf16", "int8"), kv_dtype
         self.kv_dtype = kv_dtype
         self.mla = cfg.attn.kind == "mla"
+        self.sink = int(cfg.attn.mem_slots)          # rows reserved for compressed memory
+        self.n_mem = 0                                # rows of memory currently valid
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=device)
         self.k, self.v, self.ks, self.vs = [], [], [], []
         store = torch.int8 if kv_dtype == "int8" else dtype
+        max_len = max_len + self.sink
         for _ in range(cfg.n_layers):
             if self.mla:
                 w = cfg.attn.kv_lora_rank + cfg.attn.qk_rope_dim
@@ -71,6 +79,7 @@ class KVCache:
     def write(self, layer: int, pos: torch.Tensor, k: torch.Tensor, v: torch.Tensor | None = None):
         """Store new entries at positions pos [B, T]; k [B, T, ...] (MLA: latent [B, T, r+dr])."""
         B, T = pos.shape
+        pos = pos + self.sink
         bidx = torch.arange(B, device=self.device)[:, None].expand(B, T)
         if self.kv_dtype == "int8":
             if self.mla:
@@ -89,6 +98,34 @@ class KVCache:
             if v is not None:
                 self.v[layer][bidx, pos] = v.to(self.v[layer].dtype)
 
+    @torch.no_grad()
+    def compress_memory(self, window: int) -> int:
+        """Fill the memory rows with segment means of the tokens older than the window
+        (positions [0, min(lengths) - window)); returns the number of valid memory rows."""
+        M = self.sink
+        n_old = int(self.lengths.min()) - window
+        if M == 0 or n_old <= 0:
+            self.n_mem = 0
+            return 0
+        bounds = [(i * n_old) // M for i in range(M + 1)]
+        for layer in range(self.cfg.n_layers):
+            for store, scale in ((self.k, self.ks), (self.v, self.vs)):
+                t = store[layer]
+                if t is None:
+                    continue
+                rows = t[:, M:M + n_old].float()
+                if scale[layer] is not None:
+                    rows = rows * scale[layer][:, M:M + n_old].unsqueeze(-1)
+                segs = torch.stack([rows[:, a:max(b, a + 1)].mean(1) for a, b in zip(bounds[:-1], bounds[1:])], 1)
+                if scale[layer] is not None:
+                    q, sc = quantize_int8(segs, -1)
+                    t[:, :M] = q
+                    scale[layer][:, :M] = sc
+                else:
+                    t[:, :M] = segs.to(t.dtype)
+        self.n_mem = M
+        return M
+
     def advance(self, t_new: int):
         self.lengths += t_new
 
@@ -104,6 +141,16 @@ class KVCache:
                     lst[i] = t.index_select(0, index)
         self.lengths = self.lengths.index_select(0, index)
         self.batch = int(index.numel())
+
+    def view(self, b0: int, b1: int) -> "KVCache":
+        """A cache over sequences [b0, b1) that shares this cache's storage (for chunked prefill)."""
+        v = object.__new__(KVCache)
+        v.__dict__.update(self.__dict__)
+        v.batch = b1 - b0
+        v.lengths = self.lengths[b0:b1]
+        for name in ("k", "v", "ks", "vs"):
+            setattr(v, name, [None if t is None else t[b0:b1] for t in getattr(self, name)])
+        return v
 
     def layer_kv(self, layer: int, dtype=None):
         """Dequantised (k, v) of a layer (MLA: latent, None)."""

@@ -122,7 +122,8 @@ class GQAttention(nn.Module):
         else:
             kv_len = cache.lengths + Tn
             o = decode_attention(q.reshape(B, Tn, self.H, self.hd), cache.k[layer], cache.v[layer], pos, kv_len,
-                                 window=self.cfg.attn.window, k_scale=cache.ks[layer], v_scale=cache.vs[layer])
+                                 window=self.cfg.attn.window, k_scale=cache.ks[layer], v_scale=cache.vs[layer],
+                                 sink_rows=cache.sink, n_sink=cache.n_mem)
         return linear(o.reshape(B * Tn, -1), self.wo, residual=h)
 
 
@@ -202,7 +203,8 @@ class MLAttention(nn.Module):
         cache.write(layer, pos, torch.cat([c, kr], dim=-1).view(B, Tn, r + dr))
         kv_len = cache.lengths + Tn
         o = decode_attention(qa, cache.k[layer], None, pos, kv_len, window=self.cfg.attn.window,
-                             scale=1.0 / math.sqrt(self.dn + self.dr), k_scale=cache.ks[layer], latent_v_dim=r)
+                             scale=1.0 / math.sqrt(self.dn + self.dr), k_scale=cache.ks[layer], latent_v_dim=r,
+                             sink_rows=cache.sink, n_sink=cache.n_mem)
         return linear(o.reshape(B * Tn, -1), self.wo_abs, residual=h)
 
 

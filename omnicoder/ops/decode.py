@@ -25,8 +25,9 @@ from . import _ext
 
 
 def decode_attention_torch(q, k, v, q_pos, kv_len, *, window=0, scale=None, k_scale=None, v_scale=None,
-                           latent_v_dim=0):
-    """k: [B, L, Hk, D] (or latent [B, L, D] when latent_v_dim > 0); scales dequantise int8 caches."""
+                           latent_v_dim=0, sink_rows=0, n_sink=0):
+    """k: [B, L, Hk, D] (or latent [B, L, D] when latent_v_dim > 0); scales dequantise int8 caches.
+    Token position p is cache row sink_rows + p; rows [0, n_sink) are memory every query sees."""
     B, Tn, H, Dq = q.shape
     sc = scale if scale is not None else 1.0 / math.sqrt(Dq)
     if latent_v_dim:
@@ -42,21 +43,26 @@ def decode_attention_torch(q, k, v, q_pos, kv_len, *, window=0, scale=None, k_sc
     vv = vf.permute(0, 2, 1, 3).repeat_interleave(rep, dim=1)
     qq = q.float().permute(0, 2, 1, 3)                           # [B, H, Tn, D]
     s = torch.matmul(qq, kk.transpose(-1, -2)) * sc              # [B, H, Tn, L]
-    p = torch.arange(L, device=q.device)
+    rows = torch.arange(L, device=q.device)
+    p = rows - sink_rows
     qp = q_pos[:, None, :, None]
-    mask = (p[None, None, None, :] > qp) | (p[None, None, None, :] >= kv_len[:, None, None, None])
+    mask = (p[None, None, None, :] > qp) | (p[None, None, None, :] >= kv_len[:, None, None, None]) | \
+        (p[None, None, None, :] < 0)
     if window > 0:
         mask |= p[None, None, None, :] <= qp - window
+    if n_sink > 0:
+        mask &= ~(rows < n_sink)[None, None, None, :]
     s = s.masked_fill(mask, float("-inf"))
     o = torch.matmul(torch.softmax(s, -1), vv)                   # [B, H, Tn, Dv]
     return o.permute(0, 2, 1, 3).to(q.dtype)
 
 
 def decode_attention(q, k, v, q_pos, kv_len, *, window=0, scale=None, k_scale=None, v_scale=None,
-                     latent_v_dim=0):
+                     latent_v_dim=0, sink_rows=0, n_sink=0):
     if not q.is_cuda:
         return decode_attention_torch(q, k, v, q_pos, kv_len, window=window, scale=scale, k_scale=k_scale,
-                                      v_scale=v_scale, latent_v_dim=latent_v_dim)
+                                      v_scale=v_scale, latent_v_dim=latent_v_dim, sink_rows=sink_rows,
+                                      n_sink=n_sink)
     C = _ext.load()
     sc = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     B, Tn, H, _ = q.shape
@@ -65,7 +71,8 @@ def decode_attention(q, k, v, q_pos, kv_len, *, window=0, scale=None, k_scale=No
     qp = q_pos.to(torch.int32)
     kl = kv_len.to(torch.int32).contiguous()
     if Tn <= step:
-        return C.attn_decode(q.contiguous(), k, v, k_scale, v_scale, qp.contiguous(), kl, window, sc, latent_v_dim)
+        return C.attn_decode(q.contiguous(), k, v, k_scale, v_scale, qp.contiguous(), kl, window, sc, latent_v_dim,
+                             sink_rows, n_sink)
     outs = [C.attn_decode(q[:, t:t + step].contiguous(), k, v, k_scale, v_scale, qp[:, t:t + step].contiguous(), kl,
-                          window, sc, latent_v_dim) for t in range(0, Tn, step)]
+                          window, sc, latent_v_dim, sink_rows, n_sink) for t in range(0, Tn, step)]
     return torch.cat(outs, dim=1)

@@ -92,3 +92,26 @@ def test_generate_greedy_cuda_runs():
     out = generate(model, prompt, 8, temperature=0.0)
     assert out.shape == (4, 24)
     assert torch.equal(out[:, :16], prompt)
+
+
+@pytest.mark.parametrize("int8", [False, True])
+def test_decode_with_memory_rows(int8):
+    """Cache rows [0, n_sink) are visible to every query; token p lives at row sink_rows + p."""
+    from omnicoder.inference.kv_cache import quantize_int8
+    from omnicoder.ops.decode import decode_attention, decode_attention_torch
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cpu").manual_seed(1)
+    B, Tn, H, DQ, DV, S, L = 4, 2, 16, 576, 512, 64, 600
+    q = torch.randn(B, Tn, H, DQ, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(B, S + L, DQ, generator=g).to(dev, torch.bfloat16)
+    kv_len = torch.tensor([300, 599, 450, 120], dtype=torch.int32, device=dev)
+    q_pos = (kv_len[:, None] - Tn + torch.arange(Tn, device=dev)[None]).to(torch.int32)
+    ks = None
+    if int8:
+        k, ks = quantize_int8(k, -1)
+    kw = dict(window=128, scale=1.0 / math.sqrt(DQ), k_scale=ks, latent_v_dim=DV, sink_rows=S, n_sink=60)
+    out = decode_attention(q, k, None, q_pos, kv_len, **kw)
+    ref = decode_attention_torch(q.float(), k, None, q_pos.long(), kv_len.long(), **kw)
+    torch.cuda.synchronize()
+    assert (out.float() - ref.float()).abs().max().item() < 2e-2 * max(1.0, ref.abs().max().item())

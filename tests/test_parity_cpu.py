@@ -71,3 +71,33 @@ def test_batched_decode_equals_full_forward():
     inc = torch.cat([pre] + steps, dim=1)
     full = model(ids[:, :40], all_logits=True)["logits"]
     assert torch.allclose(inc, full, atol=1e-4, rtol=0)
+
+
+def test_windowed_decode_and_memory_slots():
+    """Sliding-window decode equals the windowed full forward; compressed memory rows
+    (segment means of tokens older than the window) are attended after compression."""
+    from omnicoder.config import AttentionConfig, ModelConfig
+    from omnicoder.inference.kv_cache import KVCache
+    from omnicoder.models.lm import build_model
+
+    cfg = ModelConfig(name="win", vocab_size=200, d_model=32, n_layers=2, n_heads=4, ffn_dim=64, max_seq_len=128,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2, window=8))
+    m = build_model(cfg, seed=0).eval()
+    ids = torch.randint(0, 200, (2, 40), generator=torch.Generator().manual_seed(3))
+    full = m(ids, all_logits=True)["logits"]
+    cache = KVCache(cfg, 2, 64, "cpu")
+    pre = m.forward_cached(ids[:, :20], cache, prefill=True)
+    steps = [m.forward_cached(ids[:, i:i + 1], cache) for i in range(20, 40)]
+    assert torch.allclose(torch.cat([pre] + steps, 1), full, atol=1e-4)
+    # with 4 memory rows
+    cfg.attn.mem_slots = 4
+    cache = KVCache(cfg, 2, 64, "cpu")
+    m.forward_cached(ids[:, :32], cache, prefill=True)
+    assert cache.compress_memory(window=8) == 4
+    k_rows = cache.k[0][:, 4:4 + 24].float()
+    assert torch.allclose(cache.k[0][:, 0], k_rows[:, :6].mean(1), atol=1e-6)
+    with_mem = m.forward_cached(ids[:, 32:33], cache)
+    cache.n_mem = 0
+    cache.lengths -= 1
+    without = m.forward_cached(ids[:, 32:33], cache)
+    assert torch.isfinite(with_mem).all() and not torch.allclose(with_mem, without)
