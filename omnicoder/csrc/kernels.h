@@ -91,15 +91,22 @@ void router_bwd(const float* logits, const float* probs, const int* idx, const f
 // ---- decode attention ----------------------------------------------------------
 // Split-KV attention of new tokens against a (bf16 or int8) KV cache; see
 // decode_sm100.cu for the layouts.  v == nullptr: MLA latent cache (the value
-// is the first DV dims of each key row).  workspace: decode_workspace_floats().
+// is the first DV dims of each key row).  workspace: decode_plan().ws_floats.
 // Token position t lives in cache row sink_rows + t; rows [0, n_sink) are
 // compressed-memory rows every query attends to.
-int decode_splits(int B, int Hk, int max_len);
-size_t decode_workspace_floats(int B, int Hk, int splits, int DV);
+struct DecodePlan {
+  bool tc;           // tensor-core kernel (MLA latent caches of supported dims)
+  int rg, groups;    // query rows per CTA, row groups
+  int splits;        // key-range splits per sequence
+  int rstride;       // rows per (sequence, kv head, split) slab of the workspace
+  size_t ws_floats;  // workspace size
+};
+DecodePlan decode_plan(int B, int Tn, int H, int Hk, int L, int DQ, int DV, bool latent, int window, int sink_rows);
 void attn_decode(const void* q, const void* k, const void* v, const float* ks, const float* vs, bool int8_kv,
                  const int* q_pos, const int* kv_len, void* out, float* workspace, int B, int Tn, int H, int Hk,
                  int L, int DQ, int DV, long long k_b, long long k_l, long long v_b, long long v_l, long long s_b,
-                 long long s_l, int window, float scale, int splits, int sink_rows, int n_sink, cudaStream_t s);
+                 long long s_l, int window, float scale, const DecodePlan& plan, int sink_rows, int n_sink,
+                 void* status, cudaStream_t s);
 
 // ---- int4 weight-only linear ----------------------------------------------------
 // y[M, N] = x[M, K] (bf16) . dequant(w)^T, w packed [N, ldw] bytes (two nibbles per

@@ -375,16 +375,16 @@ at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::op
       TORCH_CHECK(vs.has_value() && vs->stride(0) == s_b && vs->stride(1) == s_l, "attn_decode: v scales");
     }
   }
-  const int splits = decode_splits((int)B, (int)Hk, (int)L);
-  auto ws = at::empty({(int64_t)decode_workspace_floats((int)B, (int)Hk, splits, (int)DV)},
-                      q.options().dtype(at::kFloat));
+  const DecodePlan pl = decode_plan((int)B, (int)Tn, (int)H, (int)Hk, (int)L, (int)DQ, (int)DV, !v.has_value(),
+                                    (int)window, (int)sink_rows);
+  auto ws = at::empty({(int64_t)pl.ws_floats}, q.options().dtype(at::kFloat));
   auto out = at::empty({B, Tn, H, DV}, q.options());
   attn_decode(q.data_ptr(), k.data_ptr(), v.has_value() ? v->data_ptr() : nullptr,
               int8_kv ? ks->data_ptr<float>() : nullptr,
               (int8_kv && vs.has_value()) ? vs->data_ptr<float>() : nullptr, int8_kv, q_pos.data_ptr<int>(),
               kv_len.data_ptr<int>(), out.data_ptr(), ws.data_ptr<float>(), (int)B, (int)Tn, (int)H, (int)Hk, (int)L,
-              (int)DQ, (int)DV, k.stride(0), k.stride(1), v_b, v_l, s_b, s_l, (int)window, (float)scale, splits,
-              (int)sink_rows, (int)n_sink, stream());
+              (int)DQ, (int)DV, k.stride(0), k.stride(1), v_b, v_l, s_b, s_l, (int)window, (float)scale, pl,
+              (int)sink_rows, (int)n_sink, status_ptr(), stream());
   return out;
 }
 
@@ -464,6 +464,9 @@ void register_kernels(pybind11::module_& m) {
   m.def("gsplat_forward", &gsplat_forward_t);
   m.def("int4_gemv", &int4_gemv_t, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("offset"));
   m.def("int4_dequant", &int4_dequant_t, py::arg("w"), py::arg("scale"), py::arg("K"), py::arg("offset"));
+  m.def("decode_rows_limit", [](int64_t DQ, int64_t DV, bool latent, int64_t Hk) -> int64_t {
+    return (latent && Hk == 1 && decode_plan(1, 1, 1, 1, 1, (int)DQ, (int)DV, true, 0, 0).tc) ? (1 << 20) : 64;
+  }, "query rows (tokens x heads per kv group) one decode call takes");
   m.def("attn_decode", &attn_decode_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_scale"),
         py::arg("v_scale"), py::arg("q_pos"), py::arg("kv_len"), py::arg("window"), py::arg("scale"),
         py::arg("latent_v_dim"), py::arg("sink_rows") = 0, py::arg("n_sink") = 0);

@@ -12,8 +12,11 @@ MHA/GQA: keys/values [B, L, Hk, D].  MLA (absorbed): the latent cache
 and the value (first r dims); the output is the latent o [B, Tn, H, r] that the
 absorbed output projection consumes.
 
-CUDA: split-KV decode kernel over bf16 or int8 (per-token / per-head scaled)
-caches.  CPU: dense masked softmax (the oracle).
+CUDA: MLA latent caches of the model sizes (576/512, 320/256) run a tcgen05
+kernel (keys on the MMA M side, query rows on N, any number of query rows);
+other layouts run the split-KV CUDA-core kernel (<= 64 query rows per call).
+Both take bf16 or int8 (per-token / per-head scaled) caches.  CPU: dense
+masked softmax (the oracle).
 """
 from __future__ import annotations
 
@@ -66,8 +69,10 @@ def decode_attention(q, k, v, q_pos, kv_len, *, window=0, scale=None, k_scale=No
     C = _ext.load()
     sc = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     B, Tn, H, _ = q.shape
-    G = H if latent_v_dim else H // k.shape[2]
-    step = max(1, 64 // G)                 # the kernel holds <= 64 query rows of one kv group
+    Hk = 1 if latent_v_dim else k.shape[2]
+    G = H // Hk
+    step = max(1, C.decode_rows_limit(q.shape[-1], latent_v_dim or (v.shape[-1] if v is not None else 0),
+                                      bool(latent_v_dim), Hk) // G)   # query rows one call takes
     qp = q_pos.to(torch.int32)
     kl = kv_len.to(torch.int32).contiguous()
     if Tn <= step:
