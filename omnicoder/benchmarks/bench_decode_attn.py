@@ -28,31 +28,41 @@ def main(argv=None):
     ap.add_argument("--mem", type=int, default=64)
     ap.add_argument("--kv", default="int8", choices=["int8", "bf16"])
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--mha", type=int, default=0, metavar="KV_HEADS",
+                    help="MHA / GQA cache with this many kv heads (head dim --head-dim) instead of the MLA latent")
+    ap.add_argument("--head-dim", type=int, default=128)
     a = ap.parse_args(argv)
     from omnicoder.inference.kv_cache import quantize_int8
     from omnicoder.ops import _ext
     from omnicoder.ops.decode import decode_attention
     dev = torch.device("cuda")
-    B, Tn, H, DQ, DV = a.batch, a.tn, a.heads, 576, 512
+    B, Tn, H = a.batch, a.tn, a.heads
+    DQ, DV = (a.head_dim, a.head_dim) if a.mha else (576, 512)
     L = a.mem + a.ctx + Tn
     g = torch.Generator(device="cpu").manual_seed(0)
     q = torch.randn(B, Tn, H, DQ, generator=g).to(dev, torch.bfloat16)
-    k = torch.randn(B, L, DQ, device=dev, dtype=torch.bfloat16)
-    ks = None
+    v = vs = ks = None
+    if a.mha:
+        k = torch.randn(B, L, a.mha, DQ, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(B, L, a.mha, DV, device=dev, dtype=torch.bfloat16)
+    else:
+        k = torch.randn(B, L, DQ, device=dev, dtype=torch.bfloat16)
     if a.kv == "int8":
         k, ks = quantize_int8(k, -1)
+        if v is not None:
+            v, vs = quantize_int8(v, -1)
     kv_len = torch.full((B,), a.ctx + Tn, dtype=torch.int32, device=dev)
     q_pos = (kv_len[:, None] - Tn + torch.arange(Tn, device=dev)[None, :]).to(torch.int32)
-    kw = dict(window=a.window, scale=1.0 / math.sqrt(DQ), k_scale=ks, latent_v_dim=DV, sink_rows=a.mem,
-              n_sink=a.mem)
+    kw = dict(window=a.window, scale=1.0 / math.sqrt(DQ), k_scale=ks, v_scale=vs, latent_v_dim=0 if a.mha else DV,
+              sink_rows=a.mem, n_sink=a.mem)
     for _ in range(3):
-        decode_attention(q, k, None, q_pos, kv_len, **kw)
+        decode_attention(q, k, v, q_pos, kv_len, **kw)
     torch.cuda.synchronize()
     times = []
     for _ in range(a.iters):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        decode_attention(q, k, None, q_pos, kv_len, **kw)
+        decode_attention(q, k, v, q_pos, kv_len, **kw)
         e1.record()
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
@@ -60,8 +70,10 @@ def main(argv=None):
     times.sort()
     ms = times[len(times) // 2]
     rows = (min(a.ctx + Tn, a.window + Tn - 1) if a.window else a.ctx + Tn) + a.mem
-    nbytes = B * rows * DQ * (1 if a.kv == "int8" else 2) + (B * rows * 4 if a.kv == "int8" else 0)
-    print(json.dumps({"kernel": "decode attention (MLA latent)", "batch": B, "tn": Tn, "heads": H, "ctx": a.ctx,
+    row_bytes = (a.mha * (DQ + DV) if a.mha else DQ) * (1 if a.kv == "int8" else 2)
+    row_bytes += (4 * (2 * a.mha if a.mha else 1)) if a.kv == "int8" else 0
+    nbytes = B * rows * row_bytes
+    print(json.dumps({"kernel": f"decode attention ({'MHA/GQA %d kv heads x %d' % (a.mha, DQ) if a.mha else 'MLA latent'})", "batch": B, "tn": Tn, "heads": H, "ctx": a.ctx,
                       "window": a.window, "mem": a.mem, "kv": a.kv, "ms": ms,
                       "gbs": nbytes / ms / 1e6, "bytes": nbytes}))
 

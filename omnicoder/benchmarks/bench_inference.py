@@ -37,6 +37,7 @@ def main(argv=None):
     ap.add_argument("--spec", type=int, default=0, help="draft tokens per step (0: plain decode)")
     ap.add_argument("--prefill_chunk", type=int, default=4, help="sequences per prefill call")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (quick runs only)")
+    ap.add_argument("--no-graphs", dest="graphs", action="store_false", help="run decode steps eagerly")
     ap.add_argument("--json", default=None)
     a = ap.parse_args(argv)
     dev = torch.device("cuda")
@@ -77,26 +78,33 @@ def main(argv=None):
     prefill_s = e0.elapsed_time(e1) / 1000.0
     # ---- decode: the remaining gen - 1 tokens ---------------------------------------
     step_ms, produced, accepted, proposed = [], 1, 0, 0
+    fwd_t = lambda ids: model.forward_cached(ids, cache)
+    fwd_d = (lambda ids: draft.forward_cached(ids, dcache)) if draft is not None else None
+    if a.graphs:
+        from omnicoder.inference.graphs import GraphedStep
+        fwd_t = GraphedStep(model, cache, 1 if draft is None else a.spec + 1)
+        if draft is not None:
+            fwd_d = GraphedStep(draft, dcache, 1)
     with torch.no_grad():
         while produced < a.gen:
             s0, s1 = ev(), ev()
             s0.record()
             if draft is None:
-                last = model.forward_cached(last[:, None], cache)[:, -1].argmax(-1)
+                last = fwd_t(last[:, None])[:, -1].argmax(-1)
                 n_new = 1
             else:
                 base_t, base_d = cache.lengths.clone(), dcache.lengths.clone()
                 cur, props = last, []
                 for _ in range(a.spec):
-                    cur = draft.forward_cached(cur[:, None], dcache)[:, -1].argmax(-1)
+                    cur = fwd_d(cur[:, None])[:, -1].argmax(-1)
                     props.append(cur)
                 props = torch.stack(props, 1)                                    # [B, k] proposals
-                tgt = model.forward_cached(torch.cat([last[:, None], props], 1), cache).argmax(-1)  # [B, k+1]
+                tgt = fwd_t(torch.cat([last[:, None], props], 1)).argmax(-1)  # [B, k+1]
                 n_acc = torch.cumprod((tgt[:, :a.spec] == props).int(), 1).sum(1)
                 # lock-step batch: keep the prefix every sequence accepted, then the target's token
                 m = int(n_acc.min())
                 if m == a.spec:
-                    draft.forward_cached(props[:, -1:], dcache)
+                    fwd_d(props[:, -1:])
                 cache.rollback(base_t + m + 1)
                 dcache.rollback(base_d + m + 1)
                 last = tgt[:, m]
@@ -119,7 +127,7 @@ def main(argv=None):
         "p50_step_ms": statistics.median(step_ms),
         "p50_tpot_ms": statistics.median(step_ms) * len(step_ms) / max(1, produced - 1),
         "memory_rows": n_mem, "kv_cache_gb": cache.nbytes() / 1e9,
-        "draft_acceptance": (accepted / proposed) if proposed else None,
+        "draft_acceptance": (accepted / proposed) if proposed else None, "cuda_graphs": a.graphs,
         "data": "synthetic (uniform random prompts, random-init N(0,0.02) weights)", "dtype": "bf16 weights",
     }
     print(json.dumps(res))

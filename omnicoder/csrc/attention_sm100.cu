@@ -923,7 +923,7 @@ static void check_shapes(const AttnTensors& a) {
 
 template <typename K>
 static void set_smem(K kern, int bytes) {
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  ensure_smem_attr(reinterpret_cast<const void*>(kern), bytes);
 }
 
 template <int DQ, int DV, bool ROPE>

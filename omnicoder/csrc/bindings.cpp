@@ -8,6 +8,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -52,6 +54,42 @@ static cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().strea
 // ---------------------------------------------------------------------------
 // GEMM
 // ---------------------------------------------------------------------------
+// Row count up to which dense GEMMs with K-major operands take the few-row
+// (swap-AB) kernel; OMNI_SKINNY_MAX_ROWS overrides it (0 disables).
+static int g_skinny_rows = -1;
+static int skinny_rows() {
+  if (g_skinny_rows < 0) {
+    const char* e = std::getenv("OMNI_SKINNY_MAX_ROWS");
+    g_skinny_rows = e ? std::max(0, std::min(std::atoi(e), kSkinnyMaxRows)) : 128;
+  }
+  return g_skinny_rows;
+}
+void set_skinny_rows(int64_t n) { g_skinny_rows = (int)std::max<int64_t>(0, std::min<int64_t>(n, kSkinnyMaxRows)); }
+
+static void run_skinny(const at::Tensor& A, const at::Tensor& B, const int* offsets, int G, int rows, int N, int K,
+                       long long w_group_stride, at::Tensor& C, int epilogue, double alpha,
+                       const c10::optional<at::Tensor>& R) {
+  auto acc = at::empty({(int64_t)rows, (int64_t)N}, A.options().dtype(at::kFloat));
+  C10_CUDA_CHECK(cudaMemsetAsync(acc.data_ptr<float>(), 0, (size_t)rows * N * sizeof(float), cur_stream()));
+  SkinnyDesc sd;
+  sd.M = rows;
+  sd.N = N;
+  sd.K = K;
+  sd.G = G;
+  sd.offsets = offsets;
+  sd.X = A.data_ptr();
+  sd.ldx = A.stride(0);
+  sd.W = B.data_ptr();
+  sd.ldw = B.stride(-2);
+  sd.w_group_stride = w_group_stride;
+  sd.acc = acc.data_ptr<float>();
+  sd.status = status_ptr();
+  skinny_gemm_launch(sd, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  skinny_finalize(acc.data_ptr<float>(), rows, N, epilogue, (float)alpha, C.data_ptr(), C.stride(0),
+                  R.has_value() ? R->data_ptr() : nullptr, R.has_value() ? R->stride(0) : 0, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 // Dense: C = alpha * op(A) op(B)^T.
 //   a_mn=false: A [M,K]; a_mn=true: A [K,M].  b_mn=false: B [N,K]; b_mn=true: B [K,N].
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn, int64_t epilogue,
@@ -115,9 +153,41 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
     }
   }
   if (epilogue == EPI_SWIGLU_BWD) TORCH_CHECK(N % 32 == 0, "gemm swiglu bwd: N must be a multiple of 32");
+  const bool skinny_epi = epilogue == EPI_STORE_BF16 || epilogue == EPI_STORE_F32 || epilogue == EPI_ADD_BF16 ||
+                          (epilogue == EPI_SWIGLU && !H.has_value());
+  if (!a_mn && !b_mn && skinny_epi && M <= skinny_rows()) {
+    run_skinny(A, B, nullptr, 1, (int)M, (int)N, (int)K, 0, C, (int)epilogue, alpha, R);
+    return;
+  }
   d.status = status_ptr();
   gemm_sm100_launch(d, cur_stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Few-row grouped GEMM: group g owns rows [offsets[g], offsets[g+1]) of A (at most
+// `rows` rows in all, any alignment); B is [G, N, K].  Epilogues: bf16 store or
+// SwiGLU (C then has N/2 columns).
+void gemm_skinny_grouped(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor& C,
+                         int64_t epilogue, double alpha, int64_t rows) {
+  CHECK_CUDA_T(A);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_BF16(C);
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(C);
+  TORCH_CHECK(B.dim() == 3 && B.is_contiguous(), "gemm_skinny_grouped: B must be a contiguous [G, N, K] stack");
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda() && offsets.numel() == B.size(0) + 1,
+              "gemm_skinny_grouped: offsets must be int32 [G+1] on the device");
+  TORCH_CHECK(epilogue == EPI_STORE_BF16 || epilogue == EPI_SWIGLU, "gemm_skinny_grouped: bf16 or swiglu epilogue");
+  const int64_t K = A.size(1), N = B.size(1);
+  TORCH_CHECK(B.size(2) == K && K % 8 == 0, "gemm_skinny_grouped: reduction dims");
+  TORCH_CHECK(rows >= 0 && rows <= A.size(0) && rows <= C.size(0), "gemm_skinny_grouped: rows");
+  TORCH_CHECK(C.size(1) == (epilogue == EPI_SWIGLU ? N / 2 : N), "gemm_skinny_grouped: output columns");
+  if (epilogue == EPI_SWIGLU) TORCH_CHECK(N % 64 == 0, "gemm_skinny_grouped: swiglu needs N % 64 == 0");
+  const c10::cuda::CUDAGuard guard(A.device());
+  if (rows == 0) return;
+  run_skinny(A, B, offsets.data_ptr<int>(), (int)B.size(0), (int)rows, (int)N, (int)K, B.stride(0), C,
+             (int)epilogue, alpha, c10::nullopt);
 }
 
 // Grouped-M: rows of A ([rows, K], K-major) segmented by offsets [G+1];
@@ -229,6 +299,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &omni::gemm, "tcgen05 GEMM", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
         py::arg("H") = py::none(), py::arg("block_n") = 256);
+  m.def("gemm_skinny_grouped", &omni::gemm_skinny_grouped, py::arg("A"), py::arg("B"), py::arg("offsets"),
+        py::arg("C"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("rows") = 0);
+  m.def("set_skinny_rows", &omni::set_skinny_rows, "rows up to which dense GEMMs use the few-row kernel (0: off)");
   m.def("gemm_grouped_m", &omni::gemm_grouped_m, py::arg("A"), py::arg("B"), py::arg("offsets"), py::arg("C"),
         py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
         py::arg("H") = py::none(), py::arg("block_n") = 256, py::arg("max_rows_hint") = 0);

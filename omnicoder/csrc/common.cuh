@@ -11,6 +11,9 @@
 // `omni_status_t`) and the role that timed out leaves its loop; the host reads
 // the status word after the stream synchronises and raises.  Nothing here traps.
 #pragma once
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include <cstdint>
 #include <cuda.h>
@@ -19,6 +22,23 @@
 #include <cuda_runtime.h>
 
 namespace omni {
+
+// Raise a kernel's dynamic shared-memory limit when a launch needs more than was
+// set before on this device (kernels whose smem depends on runtime dims get the
+// largest size seen).  Setting it on every launch would also put a non-stream
+// API call inside CUDA-graph captures of decode steps.
+inline void ensure_smem_attr(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> limit;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  int& cur = limit[{func, dev}];
+  if (bytes > cur) {
+    cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cur = bytes;
+  }
+}
 
 // ---------------------------------------------------------------------------
 // Status word

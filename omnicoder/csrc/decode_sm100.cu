@@ -881,7 +881,7 @@ template <typename KV, int DQ, int DV, int RG>
 void launch_tc(const DecArgs& a, int groups, StatusBlock* st, cudaStream_t s) {
   auto kern = decode_mla_tc_kernel<KV, DQ, DV, RG>;
   constexpr int smem = TcSmem<DQ, RG>::kBytes;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   kern<<<dim3(groups, a.splits, a.B), kTcThreads, smem, s>>>(a, st);
 }
 
@@ -894,6 +894,310 @@ bool dispatch_tc_dims(const DecArgs& a, int groups, StatusBlock* st, cudaStream_
 
 bool tc_dims_supported(int DQ, int DV) { return (DQ == 576 && DV == 512) || (DQ == 320 && DV == 256); }
 
+// ===========================================================================
+// Few-row path (MHA / GQA caches with at most 16 query rows per KV head, e.g.
+// one decode token of an MHA model): the op is a pair of GEMVs over the cache
+// and must run at HBM bandwidth, so every thread works on keys in both phases.
+// CTA = (sequence, kv head, split), 256 threads, tiles of 64 keys staged by
+// cp.async (double buffered, rows padded by 16 bytes):
+//   scores : 4 threads per key, each a quarter of the head dim for all rows,
+//            combined by two shuffles;
+//   softmax: one warp per row (online max / sum in shared memory);
+//   P.V    : thread = (2 value dims, key group); the groups are summed once at
+//            the end.
+// ===========================================================================
+constexpr int kGvThreads = 256;
+constexpr int kGvKeys = 64;
+constexpr int kGvMaxRows = 16;
+
+struct GvLayout {
+  int kRow, vRow, offQ, offK, offV, offS, offKs, offVs, offM, offL, offA, offPos, bytes;
+};
+
+__host__ __device__ inline GvLayout gv_layout(int DQ, int DV, int kv_bytes) {
+  GvLayout L;
+  L.kRow = DQ * kv_bytes + 16;
+  L.vRow = DV * kv_bytes + 16;
+  L.offQ = 0;                                                   // float [16][DQ]
+  L.offK = L.offQ + kGvMaxRows * DQ * 4;                        // [2][64][kRow]
+  L.offV = L.offK + 2 * kGvKeys * L.kRow;                       // [2][64][vRow]
+  L.offS = L.offV + 2 * kGvKeys * L.vRow;                       // float [16][64]
+  L.offKs = L.offS + kGvMaxRows * kGvKeys * 4;                  // float [2][64]
+  L.offVs = L.offKs + 2 * kGvKeys * 4;                          // float [2][64]
+  L.offM = L.offVs + 2 * kGvKeys * 4;
+  L.offL = L.offM + kGvMaxRows * 4;
+  L.offA = L.offL + kGvMaxRows * 4;
+  L.offPos = L.offA + kGvMaxRows * 4;
+  L.bytes = L.offPos + kGvMaxRows * 4;
+  return L;
+}
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+
+// 16 bytes of cache elements -> floats (8 for bf16, 16 for int8)
+__device__ __forceinline__ void unpack16(const bf16*, const uint4 w, float* f) {
+  const uint32_t* x = reinterpret_cast<const uint32_t*>(&w);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = bf16_lo(x[j]);
+    f[2 * j + 1] = bf16_hi(x[j]);
+  }
+}
+__device__ __forceinline__ void unpack16(const int8_t*, const uint4 w, float* f) {
+  const uint32_t* x = reinterpret_cast<const uint32_t*>(&w);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[4 * j] = (float)(signed char)(x[j] & 0xff);
+    f[4 * j + 1] = (float)(signed char)((x[j] >> 8) & 0xff);
+    f[4 * j + 2] = (float)(signed char)((x[j] >> 16) & 0xff);
+    f[4 * j + 3] = (float)(signed char)((x[j] >> 24) & 0xff);
+  }
+}
+
+template <typename KV, int RMAX>
+__global__ void __launch_bounds__(kGvThreads) decode_gemv_kernel(DecArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int PC = 16 / (int)sizeof(KV);  // elements per 16-byte chunk
+  constexpr float kLog2e = 1.4426950408889634f;
+  constexpr float kLn2 = 0.6931471805599453f;
+  const int b = blockIdx.x, g = blockIdx.y, split = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = a.H / a.Hk, R = a.Tn * G;
+  const int DQ = a.DQ, DV = a.DV;
+  const GvLayout Ly = gv_layout(DQ, DV, (int)sizeof(KV));
+  float* sQ = reinterpret_cast<float*>(smem + Ly.offQ);
+  uint8_t* sK = smem + Ly.offK;
+  uint8_t* sV = smem + Ly.offV;
+  float* sS = reinterpret_cast<float*>(smem + Ly.offS);
+  float* sKs = reinterpret_cast<float*>(smem + Ly.offKs);
+  float* sVs = reinterpret_cast<float*>(smem + Ly.offVs);
+  float* sM = reinterpret_cast<float*>(smem + Ly.offM);
+  float* sL = reinterpret_cast<float*>(smem + Ly.offL);
+  float* sA = reinterpret_cast<float*>(smem + Ly.offA);
+  int* sPos = reinterpret_cast<int*>(smem + Ly.offPos);
+
+  for (int i = tid; i < R * DQ; i += kGvThreads) {
+    const int r = i / DQ, d = i % DQ;
+    const int t = r / G, h = g * G + r % G;
+    sQ[r * DQ + d] = __bfloat162float(a.q[(((long long)b * a.Tn + t) * a.H + h) * DQ + d]);
+  }
+  int pmin = 0x7fffffff, pmax = -1;
+  for (int t = 0; t < a.Tn; ++t) {
+    const int p = a.q_pos[b * a.Tn + t];
+    pmin = min(pmin, p);
+    pmax = max(pmax, p);
+  }
+  if (tid < R) {
+    sPos[tid] = a.q_pos[b * a.Tn + tid / G];
+    sM[tid] = -INFINITY;
+    sL[tid] = 0.f;
+  }
+  const int len = a.kv_len[b];
+  const int hi = min(len, pmax + 1);
+  const int lo = a.window > 0 ? max(0, pmin - a.window + 1) : 0;
+  const int nsk = (a.n_sink + kGvKeys - 1) / kGvKeys;
+  const int ntiles = nsk + (hi > lo ? (hi - lo + kGvKeys - 1) / kGvKeys : 0);
+  const int per = (ntiles + a.splits - 1) / a.splits;
+  const int t0 = min(ntiles, split * per), t1 = min(ntiles, t0 + per);
+  auto row_of = [&](int tile) { return tile < nsk ? tile * kGvKeys : a.sink_rows + lo + (tile - nsk) * kGvKeys; };
+
+  // copy assignment (fixed for the whole loop): thread -> (key kk, 16-byte chunk c) pairs
+  const int kch = DQ * (int)sizeof(KV) / 16, vch = DV * (int)sizeof(KV) / 16;
+  const int k_per = kGvKeys * kch / kGvThreads, v_per = kGvKeys * vch / kGvThreads;  // exact (dims checked)
+  const int k_kk0 = tid / kch, k_c = tid % kch, k_step = kGvThreads / kch;
+  const int v_kk0 = tid / vch, v_c = tid % vch, v_step = kGvThreads / vch;
+  const uint8_t* kbase = reinterpret_cast<const uint8_t*>(a.k) +
+                         ((long long)b * a.k_b + (long long)g * DQ) * (long long)sizeof(KV) + k_c * 16;
+  const uint8_t* vbase = reinterpret_cast<const uint8_t*>(a.v) +
+                         ((long long)b * a.v_b + (long long)g * DV) * (long long)sizeof(KV) + v_c * 16;
+  auto issue = [&](int tile, int buf) {
+    const int p0 = row_of(tile);
+    for (int j = 0; j < k_per; ++j) {
+      const int kk = k_kk0 + j * k_step;
+      const int p = min(p0 + kk, a.L - 1);
+      cp_async16(sK + (buf * kGvKeys + kk) * Ly.kRow + k_c * 16, kbase + (long long)p * a.k_l * (long long)sizeof(KV));
+    }
+    for (int j = 0; j < v_per; ++j) {
+      const int kk = v_kk0 + j * v_step;
+      const int p = min(p0 + kk, a.L - 1);
+      cp_async16(sV + (buf * kGvKeys + kk) * Ly.vRow + v_c * 16, vbase + (long long)p * a.v_l * (long long)sizeof(KV));
+    }
+    if (a.ks != nullptr && tid < kGvKeys) {
+      const int p = min(p0 + tid, a.L - 1);
+      cp_async4(sKs + buf * kGvKeys + tid, a.ks + (long long)b * a.s_b + (long long)p * a.s_l + g);
+      cp_async4(sVs + buf * kGvKeys + tid, a.vs + (long long)b * a.s_b + (long long)p * a.s_l + g);
+    }
+    cp_async_commit();
+  };
+
+  // P.V mapping: thread = (value dims 2*d2, 2*d2+1; key group kg)
+  const int nd2 = DV / 2;
+  const int nkg = kGvThreads / nd2;
+  const int d2 = tid % nd2, kg = tid / nd2;
+  const int kpg = kGvKeys / nkg;
+  float acc[RMAX][2];
+#pragma unroll
+  for (int r = 0; r < RMAX; ++r) acc[r][0] = acc[r][1] = 0.f;
+
+  __syncthreads();
+  if (t0 < t1) issue(t0, 0);
+  for (int tile = t0; tile < t1; ++tile) {
+    const int buf = (tile - t0) & 1;
+    if (tile + 1 < t1) {
+      issue(tile + 1, buf ^ 1);
+      cp_async_wait_one();
+    } else {
+      cp_async_wait_all();
+    }
+    __syncthreads();
+    const int p0 = row_of(tile);
+    const bool sink_tile = tile < nsk;
+    // ---- scores -------------------------------------------------------------------
+    {
+      const int key = tid >> 2, part = tid & 3;
+      const int n_el = DQ / 4;
+      const KV* krow = reinterpret_cast<const KV*>(sK + (buf * kGvKeys + key) * Ly.kRow) + part * n_el;
+      float sc[RMAX];
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) sc[r] = 0.f;
+      for (int c = 0; c < n_el; c += PC) {
+        float kf[PC];
+        unpack16(krow, *reinterpret_cast<const uint4*>(krow + c), kf);
+        const float* qb = sQ + part * n_el + c;
+#pragma unroll
+        for (int r = 0; r < RMAX; ++r) {
+          if (r < R) {
+            float acc_r = 0.f;
+#pragma unroll
+            for (int e = 0; e < PC; e += 4) {
+              const float4 qv = *reinterpret_cast<const float4*>(qb + r * DQ + e);
+              acc_r += kf[e] * qv.x + kf[e + 1] * qv.y + kf[e + 2] * qv.z + kf[e + 3] * qv.w;
+            }
+            sc[r] += acc_r;
+          }
+        }
+      }
+      const int p = p0 + key;
+      const int tp = p - a.sink_rows;
+      const float mul = a.scale * kLog2e * (a.ks != nullptr ? sKs[buf * kGvKeys + key] : 1.f);
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) {
+        if (r < R) {
+          float v = sc[r];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          const int qp = sPos[r];
+          const bool vis = sink_tile ? (p < a.n_sink) : (tp < len && tp <= qp && (a.window <= 0 || tp > qp - a.window));
+          if (part == 0) sS[r * kGvKeys + key] = vis ? v * mul : -INFINITY;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- online softmax, one warp per row ----------------------------------------------
+    for (int r = warp; r < R; r += kGvThreads / 32) {
+      const float x0 = sS[r * kGvKeys + lane], x1 = sS[r * kGvKeys + lane + 32];
+      const float mold = sM[r];
+      const float mnew = fmaxf(mold, warp_max(fmaxf(x0, x1)));
+      const float e0 = mnew == -INFINITY ? 0.f : fast_exp2(x0 - mnew);
+      const float e1 = mnew == -INFINITY ? 0.f : fast_exp2(x1 - mnew);
+      const float sum = warp_sum(e0 + e1);
+      const float vs0 = a.vs != nullptr ? sVs[buf * kGvKeys + lane] : 1.f;
+      const float vs1 = a.vs != nullptr ? sVs[buf * kGvKeys + lane + 32] : 1.f;
+      sS[r * kGvKeys + lane] = e0 * vs0;
+      sS[r * kGvKeys + lane + 32] = e1 * vs1;
+      if (lane == 0) {
+        const float alpha = mold == -INFINITY ? 0.f : fast_exp2(mold - mnew);
+        sA[r] = alpha;
+        sL[r] = sL[r] * alpha + sum;
+        sM[r] = mnew;
+      }
+    }
+    __syncthreads();
+    // ---- O = O * alpha + P V ---------------------------------------------------------
+#pragma unroll
+    for (int r = 0; r < RMAX; ++r) {
+      if (r < R) {
+        const float al = sA[r];
+        acc[r][0] *= al;
+        acc[r][1] *= al;
+      }
+    }
+    for (int j = 0; j < kpg; ++j) {
+      const int key = kg * kpg + j;
+      const KV* vrow = reinterpret_cast<const KV*>(sV + (buf * kGvKeys + key) * Ly.vRow);
+      float v0, v1;
+      if (sizeof(KV) == 2) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(vrow + 2 * d2);
+        v0 = bf16_lo(w);
+        v1 = bf16_hi(w);
+      } else {
+        const uint16_t w = *reinterpret_cast<const uint16_t*>(vrow + 2 * d2);
+        v0 = (float)(signed char)(w & 0xff);
+        v1 = (float)(signed char)(w >> 8);
+      }
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) {
+        if (r < R) {
+          const float pr = sS[r * kGvKeys + key];
+          acc[r][0] += pr * v0;
+          acc[r][1] += pr * v1;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // ---- sum the key groups (shared memory reused), write the split's partials ----------
+  float* red = reinterpret_cast<float*>(smem + Ly.offK);  // [nkg][R][DV] <= 8 * 16 * 256 floats
+#pragma unroll
+  for (int r = 0; r < RMAX; ++r) {
+    if (r < R) {
+      red[(kg * R + r) * DV + 2 * d2] = acc[r][0];
+      red[(kg * R + r) * DV + 2 * d2 + 1] = acc[r][1];
+    }
+  }
+  __syncthreads();
+  const long long base = (((long long)b * a.Hk + g) * a.splits + split) * R;
+  for (int i = tid; i < R * DV; i += kGvThreads) {
+    const int r = i / DV, d = i % DV;
+    float o = 0.f;
+    for (int q = 0; q < nkg; ++q) o += red[(q * R + r) * DV + d];
+    a.part_o[(base + r) * DV + d] = o;
+  }
+  if (tid < R) {
+    a.part_ml[(base + tid) * 2] = sM[tid] == -INFINITY ? -INFINITY : sM[tid] * kLn2;
+    a.part_ml[(base + tid) * 2 + 1] = sL[tid];
+  }
+}
+
+template <typename KV, int RMAX>
+void launch_gemv_r(const DecArgs& a, int smem, cudaStream_t s) {
+  auto kern = decode_gemv_kernel<KV, RMAX>;
+  ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
+  kern<<<dim3(a.B, a.Hk, a.splits), kGvThreads, smem, s>>>(a);
+}
+template <typename KV>
+void launch_gemv(const DecArgs& a, int smem, cudaStream_t s) {
+  const int R = a.Tn * (a.H / a.Hk);
+  if (R <= 1) launch_gemv_r<KV, 1>(a, smem, s);
+  else if (R <= 2) launch_gemv_r<KV, 2>(a, smem, s);
+  else if (R <= 4) launch_gemv_r<KV, 4>(a, smem, s);
+  else if (R <= 8) launch_gemv_r<KV, 8>(a, smem, s);
+  else launch_gemv_r<KV, 16>(a, smem, s);
+}
+
+bool gemv_dims_supported(int DQ, int DV, int kv_bytes) {
+  if (DQ % 32 != 0 || DV % 64 != 0 || DQ > 256 || DV > 256) return false;
+  if ((DQ / 4) % (16 / kv_bytes) != 0) return false;        // whole 16-byte chunks per quarter row
+  if (kGvKeys % (kGvThreads / (DV / 2)) != 0) return false;   // key groups divide the tile
+  const int kch = DQ * kv_bytes / 16, vch = DV * kv_bytes / 16;
+  if (kGvThreads % kch != 0 || kGvThreads % vch != 0) return false;  // whole keys per copy pass
+  const GvLayout L = gv_layout(DQ, DV, kv_bytes);
+  return L.bytes <= 227 * 1024 && (kGvThreads / (DV / 2)) * kGvMaxRows * DV * 4 <= 2 * kGvKeys * L.kRow +
+                                                                                      2 * kGvKeys * L.vRow;
+}
+
 int decode_smem_bytes(int DQ, int DV, int kv_bytes, bool latent) {
   return kMaxRows * DQ * 2 + 2 * kKT * DQ * kv_bytes + (latent ? 0 : 2 * kKT * DV * kv_bytes) +
          (kMaxRows * kKT + 3 * kMaxRows) * 4 + kMaxRows * 4 + 128;
@@ -902,17 +1206,35 @@ int decode_smem_bytes(int DQ, int DV, int kv_bytes, bool latent) {
 template <typename KV, bool LATENT>
 void launch_split(const DecArgs& a, dim3 grid, int smem, cudaStream_t s) {
   auto kern = decode_split_kernel<KV, LATENT>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  ensure_smem_attr(reinterpret_cast<const void*>(kern), smem);
   kern<<<grid, kDecThreads, smem, s>>>(a);
 }
 
 }  // namespace
 
-DecodePlan decode_plan(int B, int Tn, int H, int Hk, int L, int DQ, int DV, bool latent, int window, int sink_rows) {
+DecodePlan decode_plan(int B, int Tn, int H, int Hk, int L, int DQ, int DV, bool latent, int window, int sink_rows,
+                       int kv_bytes) {
   DecodePlan pl;
   const int R = Tn * (H / Hk);
   pl.tc = latent && Hk == 1 && tc_dims_supported(DQ, DV);
-  if (pl.tc) {
+  pl.gemv = !pl.tc && !latent && R <= kGvMaxRows && gemv_dims_supported(DQ, DV, kv_bytes);
+  if (pl.gemv) {
+    pl.rg = R;
+    pl.groups = 1;
+    pl.rstride = R;
+    const int tokens = window > 0 ? std::min(L - sink_rows, window + Tn) : L - sink_rows;
+    const int tiles = (sink_rows + kGvKeys - 1) / kGvKeys + std::max(1, (tokens + kGvKeys - 1) / kGvKeys);
+    const int per_sm = std::max(1, std::min(8, (227 * 1024) / gv_layout(DQ, DV, kv_bytes).bytes));
+    const int slots = 148 * per_sm;
+    const int ctas = B * Hk;
+    long best = -1;
+    pl.splits = 1;
+    for (int sp = 1; sp <= std::min(64, tiles); ++sp) {
+      const long waves = ((long)ctas * sp + slots - 1) / slots;
+      const long cost = waves * ((tiles + sp - 1) / sp + 2);
+      if (best < 0 || cost < best) { best = cost; pl.splits = sp; }
+    }
+  } else if (pl.tc) {
     pl.rg = 16;  // 16 query rows per CTA keep the prefetch registers and softmax state spill-free
     pl.groups = (R + pl.rg - 1) / pl.rg;
     pl.rstride = R;
@@ -948,7 +1270,7 @@ void attn_decode(const void* q, const void* k, const void* v, const float* ks, c
                  void* status, cudaStream_t s) {
   const bool latent = v == nullptr;
   const int G = H / Hk;
-  if (!pl.tc) {
+  if (!pl.tc && !pl.gemv) {
     if (Tn * G > kMaxRows) throw std::runtime_error("attn_decode: Tn * heads-per-kv-group must be <= 64");
     if (DQ % 16 != 0 || DV % 4 != 0 || DV > 4 * kDecThreads) throw std::runtime_error("attn_decode: head dims");
     if ((DV / 4 < kDecThreads) && (kDecThreads % (DV / 4) != 0))
@@ -990,6 +1312,12 @@ void attn_decode(const void* q, const void* k, const void* v, const float* ks, c
     bool done;
     done = int8_kv ? dispatch_tc_dims<int8_t, 16>(a, pl.groups, st, s) : dispatch_tc_dims<bf16, 16>(a, pl.groups, st, s);
     if (!done) throw std::runtime_error("attn_decode: no tensor-core kernel for these dims");
+  } else if (pl.gemv) {
+    const int smem = gv_layout(DQ, DV, int8_kv ? 1 : 2).bytes;
+    if (int8_kv)
+      launch_gemv<int8_t>(a, smem, s);
+    else
+      launch_gemv<bf16>(a, smem, s);
   } else {
     const dim3 grid(B, Hk, pl.splits);
     const int smem = decode_smem_bytes(DQ, DV, int8_kv ? 1 : 2, latent);

@@ -495,8 +495,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // rank-2 or rank-3 bf16 tensor map with 128-byte swizzle.  dims[0] is the
 // contiguous dimension; strides are in bytes for dims 1.. .
-static CUtensorMap make_tmap(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-                             const uint32_t* box) {
+CUtensorMap make_tmap_bf16_sw128(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                                 const uint32_t* box) {
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
     throw std::runtime_error("omnicoder gemm: operand base address must be 16-byte aligned");
   for (int i = 0; i + 1 < rank; ++i)
@@ -517,7 +517,7 @@ static CUtensorMap make_tmap(const void* base, int rank, const uint64_t* dims, c
   return m;
 }
 
-static int num_sms() {
+int num_sms() {
   static int n = 0;
   if (n == 0) {
     int dev;
@@ -531,11 +531,7 @@ template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
 static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
   using C_ = Cfg<BN>;
   auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, MODE>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::kSmemBytes);
-    attr_set = true;
-  }
+  ensure_smem_attr(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
   // A operand tensor map.
   CUtensorMap tmA, tmB;
   {
@@ -543,12 +539,12 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
       uint64_t dims[2] = {(uint64_t)d.K_extent_a, (uint64_t)d.rows_a};
       uint64_t str[1] = {(uint64_t)d.lda * 2};
       uint32_t box[2] = {64, 128};
-      tmA = make_tmap(d.A, 2, dims, str, box);
+      tmA = make_tmap_bf16_sw128(d.A, 2, dims, str, box);
     } else {      // A stored [K, M] with row stride lda
       uint64_t dims[2] = {(uint64_t)d.M, (uint64_t)d.K_extent_a};
       uint64_t str[1] = {(uint64_t)d.lda * 2};
       uint32_t box[2] = {64, 64};
-      tmA = make_tmap(d.A, 2, dims, str, box);
+      tmA = make_tmap_bf16_sw128(d.A, 2, dims, str, box);
     }
   }
   {
@@ -557,24 +553,24 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
         uint64_t dims[3] = {(uint64_t)d.K, (uint64_t)d.N, (uint64_t)d.num_groups};
         uint64_t str[2] = {(uint64_t)d.ldb * 2, (uint64_t)d.b_group_stride * 2};
         uint32_t box[3] = {64, (uint32_t)BN, 1};
-        tmB = make_tmap(d.B, 3, dims, str, box);
+        tmB = make_tmap_bf16_sw128(d.B, 3, dims, str, box);
       } else {
         uint64_t dims[2] = {(uint64_t)d.K_extent_b, (uint64_t)d.N};
         uint64_t str[1] = {(uint64_t)d.ldb * 2};
         uint32_t box[2] = {64, (uint32_t)BN};
-        tmB = make_tmap(d.B, 2, dims, str, box);
+        tmB = make_tmap_bf16_sw128(d.B, 2, dims, str, box);
       }
     } else {      // B stored [K, N]
       if (MODE == GEMM_GROUPED_M) {
         uint64_t dims[3] = {(uint64_t)d.N, (uint64_t)d.K, (uint64_t)d.num_groups};
         uint64_t str[2] = {(uint64_t)d.ldb * 2, (uint64_t)d.b_group_stride * 2};
         uint32_t box[3] = {64, 64, 1};
-        tmB = make_tmap(d.B, 3, dims, str, box);
+        tmB = make_tmap_bf16_sw128(d.B, 3, dims, str, box);
       } else {
         uint64_t dims[2] = {(uint64_t)d.N, (uint64_t)d.K_extent_b};
         uint64_t str[1] = {(uint64_t)d.ldb * 2};
         uint32_t box[2] = {64, 64};
-        tmB = make_tmap(d.B, 2, dims, str, box);
+        tmB = make_tmap_bf16_sw128(d.B, 2, dims, str, box);
       }
     }
   }

@@ -1,5 +1,6 @@
 // Host interface of the tcgen05 GEMM (see gemm_sm100.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace omni {
@@ -50,5 +51,37 @@ struct GemmDesc {
 
 // Launch on `stream`.  Throws std::runtime_error on an invalid description.
 void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream);
+
+// rank-2 or rank-3 bf16 tensor map with 128-byte swizzle (dims[0] contiguous,
+// byte strides for dims 1..).  Throws on misaligned bases or strides.
+CUtensorMap make_tmap_bf16_sw128(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                                 const uint32_t* box);
+int num_sms();
+
+// ---- few-row GEMM (decode, speculative verification) --------------------------
+// Y[rows, N] = X[rows, K] W[N, K]^T for at most kSkinnyMaxRows rows per group
+// (swap-AB on the tensor core: weight rows on the MMA M side, tokens on N).
+// Grouped: group g owns rows [offsets[g], offsets[g+1]) of X and weight W[g]
+// (W is [G, N, K]); dense: G = 1, offsets = nullptr, rows = M.  Partial sums
+// are added into acc [rows, N] fp32 (zeroed by the caller); skinny_finalize
+// applies the epilogue.
+constexpr int kSkinnyMaxRows = 256;
+struct SkinnyDesc {
+  int M = 0;            // rows of X (upper bound of offsets[G] when grouped)
+  int N = 0, K = 0, G = 1;
+  const int* offsets = nullptr;
+  const void* X = nullptr;
+  long long ldx = 0;
+  const void* W = nullptr;
+  long long ldw = 0;
+  long long w_group_stride = 0;
+  float* acc = nullptr;
+  void* status = nullptr;
+};
+void skinny_gemm_launch(const SkinnyDesc& d, cudaStream_t stream);
+// out[r, :] = epilogue(acc[r, :]) for r < rows: EPI_STORE_BF16 / EPI_STORE_F32 /
+// EPI_ADD_BF16 (+ R) / EPI_SWIGLU (acc gate/up interleaved by 32 -> N/2 columns).
+void skinny_finalize(const float* acc, int rows, int N, int epilogue, float alpha, void* out, long long ldo,
+                     const void* R, long long ldr, cudaStream_t stream);
 
 }  // namespace omni

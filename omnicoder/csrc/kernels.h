@@ -69,7 +69,7 @@ void router_topk(const float* logits, int* idx, float* wts, float* probs, int T,
 //   (token*K + k of each permuted row, -1 for padding).  capacity <= 0: no drop.
 // workspace: int32 of size (E * nblocks) * 2 where nblocks = ceil(T*K/1024).
 void moe_permute_plan(const int* idx, int T, int K, int E, int capacity, int* counts, int* offsets, int* pos,
-                      int* src, int cap_rows, int* workspace, cudaStream_t s);
+                      int* src, int cap_rows, int* workspace, cudaStream_t s, int align = 128);
 // X_perm[r] = X[src[r]/K] for valid rows, zero for padding rows r < cap_rows.
 void moe_gather(const void* x, const int* src, void* x_perm, int cap_rows, int K, int dim, const int* offsets,
                 int E, cudaStream_t s);
@@ -88,6 +88,13 @@ void router_bwd(const float* logits, const float* probs, const int* idx, const f
                 void* dlogits, int T, int E, int K, bool renorm, float aux_alpha, float z_beta, float* aux_out,
                 cudaStream_t s);
 
+// ---- KV-cache append ---------------------------------------------------------
+// src [B, T, G, D] bf16 -> dst rows row_offset + pos[b, t] of [B, L, G, D]
+// (bf16 copy, or int8 with one fp32 scale per (b, row, g)); see kv_write.cu.
+void kv_cache_write(const void* src, const long long* pos, void* dst, float* scale, bool int8, int B, int T, int G,
+                    int D, long long d_b, long long d_l, long long s_b, long long s_l, int row_offset, int L,
+                    cudaStream_t s);
+
 // ---- decode attention ----------------------------------------------------------
 // Split-KV attention of new tokens against a (bf16 or int8) KV cache; see
 // decode_sm100.cu for the layouts.  v == nullptr: MLA latent cache (the value
@@ -96,12 +103,14 @@ void router_bwd(const float* logits, const float* probs, const int* idx, const f
 // compressed-memory rows every query attends to.
 struct DecodePlan {
   bool tc;           // tensor-core kernel (MLA latent caches of supported dims)
+  bool gemv;         // few-row kernel (MHA / GQA with <= 16 query rows per kv head)
   int rg, groups;    // query rows per CTA, row groups
   int splits;        // key-range splits per sequence
   int rstride;       // rows per (sequence, kv head, split) slab of the workspace
   size_t ws_floats;  // workspace size
 };
-DecodePlan decode_plan(int B, int Tn, int H, int Hk, int L, int DQ, int DV, bool latent, int window, int sink_rows);
+DecodePlan decode_plan(int B, int Tn, int H, int Hk, int L, int DQ, int DV, bool latent, int window, int sink_rows,
+                       int kv_bytes);
 void attn_decode(const void* q, const void* k, const void* v, const float* ks, const float* vs, bool int8_kv,
                  const int* q_pos, const int* kv_len, void* out, float* workspace, int B, int Tn, int H, int Hk,
                  int L, int DQ, int DV, long long k_b, long long k_l, long long v_b, long long v_l, long long s_b,

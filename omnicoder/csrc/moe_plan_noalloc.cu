@@ -15,7 +15,7 @@ namespace omni {
 // Kernels defined in moe_route.cu (same launch geometry is used below).
 __global__ void plan_count_kernel(const int* idx, int N, int E, int* blk_cnt, StatusBlock* st);
 __global__ void plan_scan_kernel(int nblocks, int E, int capacity, const int* blk_cnt, int* blk_base, int* counts,
-                                 int* offsets, int* src, int cap_rows);
+                                 int* offsets, int* src, int cap_rows, int align);
 __global__ void plan_assign_kernel(const int* idx, int N, int E, int capacity, const int* blk_base,
                                    const int* offsets, int* pos, int* src, int cap_rows, StatusBlock* st);
 }  // namespace omni
@@ -83,7 +83,8 @@ extern "C" int omni_moe_permute_plan_noalloc(const int* idx, int T, int K, int E
     return OMNI_NOALLOC_OK;
   }
   omni::plan_count_kernel<<<nblocks, kThreads, 0, s>>>(idx, N, E, blk_cnt, nullptr);
-  omni::plan_scan_kernel<<<1, 256, 0, s>>>(nblocks, E, capacity, blk_cnt, blk_base, counts, offsets, src, cap_rows);
+  omni::plan_scan_kernel<<<1, 256, 0, s>>>(nblocks, E, capacity, blk_cnt, blk_base, counts, offsets, src, cap_rows,
+                                           128);
   omni::plan_assign_kernel<<<nblocks, kThreads, 0, s>>>(idx, N, E, capacity, blk_base, offsets, pos, src, cap_rows,
                                                         nullptr);
   if (cudaGetLastError() != cudaSuccess) return OMNI_NOALLOC_LAUNCH_FAILED;

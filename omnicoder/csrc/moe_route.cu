@@ -1,7 +1,7 @@
 // MoE routing kernels (sm_100a): softmax top-k router, deterministic
-// expert-major permutation with 128-row padded segments (the layout the
-// grouped tcgen05 GEMM consumes), gather, weighted combine and their
-// backward passes.
+// expert-major permutation with segments padded to 128 rows (the layout the
+// grouped tile GEMM consumes; align = 1 packs them for the few-row GEMM of a
+// decode step), gather, weighted combine and their backward passes.
 //
 // Behaviour of the reference being replaced: moe_scatter.fused_dispatch
 // (src/omnicoder/modeling/kernels/moe_scatter.py:315-912) stable-sorts the N*K
@@ -123,7 +123,7 @@ __global__ void plan_count_kernel(const int* __restrict__ idx, int N, int E, int
 
 __global__ void plan_scan_kernel(int nblocks, int E, int capacity, const int* __restrict__ blk_cnt,
                                  int* __restrict__ blk_base, int* __restrict__ counts, int* __restrict__ offsets,
-                                 int* __restrict__ src, int cap_rows) {
+                                 int* __restrict__ src, int cap_rows, int align) {
   __shared__ int kept[kRouteMaxE];
   __shared__ int off[kRouteMaxE + 1];
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -141,7 +141,7 @@ __global__ void plan_scan_kernel(int nblocks, int E, int capacity, const int* __
     for (int e = 0; e < E; ++e) {
       off[e] = o;
       offsets[e] = o;
-      o += (kept[e] + 127) / 128 * 128;
+      o += (kept[e] + align - 1) / align * align;
     }
     off[E] = o;
     offsets[E] = o;
@@ -203,7 +203,7 @@ __global__ void plan_assign_kernel(const int* __restrict__ idx, int N, int E, in
 }
 
 void moe_permute_plan(const int* idx, int T, int K, int E, int capacity, int* counts, int* offsets, int* pos,
-                      int* src, int cap_rows, int* workspace, cudaStream_t s) {
+                      int* src, int cap_rows, int* workspace, cudaStream_t s, int align) {
   const int N = T * K;
   const int nblocks = (N + kPlanPairsPerBlock - 1) / kPlanPairsPerBlock;
   if (nblocks == 0) {
@@ -215,7 +215,7 @@ void moe_permute_plan(const int* idx, int T, int K, int E, int capacity, int* co
   int* blk_cnt = workspace;
   int* blk_base = workspace + nblocks * E;
   plan_count_kernel<<<nblocks, kPlanThreads, 0, s>>>(idx, N, E, blk_cnt, st);
-  plan_scan_kernel<<<1, 256, 0, s>>>(nblocks, E, capacity, blk_cnt, blk_base, counts, offsets, src, cap_rows);
+  plan_scan_kernel<<<1, 256, 0, s>>>(nblocks, E, capacity, blk_cnt, blk_base, counts, offsets, src, cap_rows, align);
   plan_assign_kernel<<<nblocks, kPlanThreads, 0, s>>>(idx, N, E, capacity, blk_base, offsets, pos, src, cap_rows, st);
 }
 
@@ -244,49 +244,52 @@ void moe_gather(const void* x, const int* src, void* x_perm, int cap_rows, int K
   moe_gather_kernel<<<148 * 8, 256, 0, s>>>((const bf16*)x, src, (bf16*)x_perm, cap_rows, K, dim, offsets, E);
 }
 
+// One thread per (token, 8 columns): every load is independent, so even a
+// decode batch of a few tokens spreads over many SMs.
 __global__ void moe_combine_kernel(const bf16* __restrict__ y, const int* __restrict__ pos,
                                    const float* __restrict__ w, const bf16* __restrict__ add, bf16* __restrict__ out,
                                    int T, int K, int dim) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  for (int c = lane * 8; c < dim; c += 256) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (add != nullptr) {
-      uint4 v = *reinterpret_cast<const uint4*>(add + (long long)t * dim + c);
-      const uint32_t* q = reinterpret_cast<const uint32_t*>(&v);
+  const int chunks = dim / 8;
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i >= (long long)T * chunks) return;
+  const int t = (int)(i / chunks);
+  const int c = (int)(i - (long long)t * chunks) * 8;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (add != nullptr) {
+    uint4 v = *reinterpret_cast<const uint4*>(add + (long long)t * dim + c);
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc[2 * j] = bf16_lo(q[j]);
-        acc[2 * j + 1] = bf16_hi(q[j]);
-      }
+    for (int j = 0; j < 4; ++j) {
+      acc[2 * j] = bf16_lo(q[j]);
+      acc[2 * j + 1] = bf16_hi(q[j]);
     }
-    for (int k = 0; k < K; ++k) {
-      const int p = pos[(long long)t * K + k];
-      if (p < 0) continue;
-      const float wk = w[(long long)t * K + k];
-      uint4 v = *reinterpret_cast<const uint4*>(y + (long long)p * dim + c);
-      const uint32_t* q = reinterpret_cast<const uint32_t*>(&v);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc[2 * j] += wk * bf16_lo(q[j]);
-        acc[2 * j + 1] += wk * bf16_hi(q[j]);
-      }
-    }
-    uint4 o;
-    o.x = pack_bf16x2(acc[0], acc[1]);
-    o.y = pack_bf16x2(acc[2], acc[3]);
-    o.z = pack_bf16x2(acc[4], acc[5]);
-    o.w = pack_bf16x2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(out + (long long)t * dim + c) = o;
   }
+  for (int k = 0; k < K; ++k) {
+    const int p = __ldg(pos + (long long)t * K + k);
+    if (p < 0) continue;
+    const float wk = __ldg(w + (long long)t * K + k);
+    uint4 v = *reinterpret_cast<const uint4*>(y + (long long)p * dim + c);
+    const uint32_t* q = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[2 * j] += wk * bf16_lo(q[j]);
+      acc[2 * j + 1] += wk * bf16_hi(q[j]);
+    }
+  }
+  uint4 o;
+  o.x = pack_bf16x2(acc[0], acc[1]);
+  o.y = pack_bf16x2(acc[2], acc[3]);
+  o.z = pack_bf16x2(acc[4], acc[5]);
+  o.w = pack_bf16x2(acc[6], acc[7]);
+  *reinterpret_cast<uint4*>(out + (long long)t * dim + c) = o;
 }
 
 void moe_combine(const void* y_perm, const int* pos, const float* w, const void* add, void* out, int T, int K,
                  int dim, cudaStream_t s) {
-  const int warps = 8;
-  moe_combine_kernel<<<(T + warps - 1) / warps, warps * 32, 0, s>>>((const bf16*)y_perm, pos, w, (const bf16*)add,
-                                                                    (bf16*)out, T, K, dim);
+  const long long work = (long long)T * (dim / 8);
+  if (work == 0) return;
+  moe_combine_kernel<<<(unsigned)((work + 255) / 256), 256, 0, s>>>((const bf16*)y_perm, pos, w, (const bf16*)add,
+                                                                  (bf16*)out, T, K, dim);
 }
 
 __global__ void moe_combine_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ y,

@@ -193,11 +193,13 @@ std::vector<at::Tensor> router_topk_t(const at::Tensor& logits, int64_t k, bool 
 }
 
 // Returns counts[E], offsets[E+1], pos[T*K], src[cap_rows].
-std::vector<at::Tensor> moe_plan_t(const at::Tensor& idx, int64_t E, int64_t capacity, int64_t cap_rows) {
+std::vector<at::Tensor> moe_plan_t(const at::Tensor& idx, int64_t E, int64_t capacity, int64_t cap_rows,
+                                   int64_t align) {
   check_i32(idx, "idx");
   const c10::cuda::CUDAGuard g(idx.device());
   const int64_t T = idx.size(0), K = idx.size(1);
   TORCH_CHECK(E <= 256, "moe_plan: E <= 256");
+  TORCH_CHECK(align >= 1, "moe_plan: align >= 1");
   auto o = idx.options();
   auto counts = at::empty({E}, o);
   auto offsets = at::empty({E + 1}, o);
@@ -207,7 +209,7 @@ std::vector<at::Tensor> moe_plan_t(const at::Tensor& idx, int64_t E, int64_t cap
   auto ws = at::empty({std::max<int64_t>(1, 2 * nblocks * E)}, o);
   moe_permute_plan(idx.data_ptr<int>(), (int)T, (int)K, (int)E, (int)capacity, counts.data_ptr<int>(),
                    offsets.data_ptr<int>(), pos.data_ptr<int>(), src.data_ptr<int>(), (int)cap_rows,
-                   ws.data_ptr<int>(), stream());
+                   ws.data_ptr<int>(), stream(), (int)align);
   return {counts, offsets, pos, src};
 }
 
@@ -226,6 +228,7 @@ at::Tensor moe_combine_t(const at::Tensor& y_perm, const at::Tensor& pos, const 
   check_f32(w, "w");
   const c10::cuda::CUDAGuard g(y_perm.device());
   const int64_t T = pos.size(0), K = pos.size(1), dim = y_perm.size(1);
+  TORCH_CHECK(dim % 8 == 0, "moe_combine: dim % 8");
   auto out = at::empty({T, dim}, y_perm.options());
   if (add.has_value()) check_bf16(*add, "add");
   moe_combine(y_perm.data_ptr(), pos.data_ptr<int>(), w.data_ptr<float>(), opt_ptr<void>(add), out.data_ptr(),
@@ -376,7 +379,7 @@ at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::op
     }
   }
   const DecodePlan pl = decode_plan((int)B, (int)Tn, (int)H, (int)Hk, (int)L, (int)DQ, (int)DV, !v.has_value(),
-                                    (int)window, (int)sink_rows);
+                                    (int)window, (int)sink_rows, int8_kv ? 1 : 2);
   auto ws = at::empty({(int64_t)pl.ws_floats}, q.options().dtype(at::kFloat));
   auto out = at::empty({B, Tn, H, DV}, q.options());
   attn_decode(q.data_ptr(), k.data_ptr(), v.has_value() ? v->data_ptr() : nullptr,
@@ -386,6 +389,35 @@ at::Tensor attn_decode_t(const at::Tensor& q, const at::Tensor& k, const c10::op
               (int)DQ, (int)DV, k.stride(0), k.stride(1), v_b, v_l, s_b, s_l, (int)window, (float)scale, pl,
               (int)sink_rows, (int)n_sink, status_ptr(), stream());
   return out;
+}
+
+// ---- KV-cache append ---------------------------------------------------------------
+void kv_cache_write_t(const at::Tensor& src, const at::Tensor& pos, at::Tensor& dst,
+                      const c10::optional<at::Tensor>& scale, int64_t row_offset) {
+  check_bf16(src, "src");
+  TORCH_CHECK(src.dim() == 4 && src.is_contiguous(), "kv_cache_write: src must be a contiguous [B, T, G, D]");
+  TORCH_CHECK(pos.scalar_type() == at::kLong && pos.is_contiguous() && pos.dim() == 2, "kv_cache_write: pos int64 [B, T]");
+  const int64_t B = src.size(0), T = src.size(1), G = src.size(2), D = src.size(3);
+  TORCH_CHECK(pos.size(0) == B && pos.size(1) == T, "kv_cache_write: pos shape");
+  TORCH_CHECK(D <= 1024, "kv_cache_write: D <= 1024");
+  TORCH_CHECK(dst.is_cuda() && dst.size(0) == B && dst.numel() == B * dst.size(1) * G * D && dst.stride(-1) == 1,
+              "kv_cache_write: dst [B, L, G, D] with contiguous rows");
+  const int64_t d_b = dst.stride(0), d_l = dst.stride(1);
+  TORCH_CHECK(d_l >= G * D, "kv_cache_write: dst row stride");
+  const bool int8 = dst.scalar_type() == at::kChar;
+  int64_t s_b = 0, s_l = 0;
+  if (int8) {
+    TORCH_CHECK(scale.has_value() && scale->scalar_type() == at::kFloat && scale->stride(-1) == 1,
+                "kv_cache_write: int8 cache needs fp32 scales");
+    s_b = scale->stride(0);
+    s_l = scale->stride(1);
+  } else {
+    TORCH_CHECK(dst.scalar_type() == at::kBFloat16 && D % 8 == 0, "kv_cache_write: bf16 cache with D % 8 == 0");
+  }
+  const c10::cuda::CUDAGuard g(src.device());
+  kv_cache_write(src.data_ptr(), reinterpret_cast<const long long*>(pos.data_ptr<int64_t>()), dst.data_ptr(), int8 ? scale->data_ptr<float>() : nullptr,
+                 int8, (int)B, (int)T, (int)G, (int)D, d_b, d_l, s_b, s_l, (int)row_offset, (int)dst.size(1),
+                 stream());
 }
 
 // ---- int4 weight-only linear ----------------------------------------------------
@@ -455,7 +487,10 @@ void register_kernels(pybind11::module_& m) {
         py::arg("norm_sq"), py::arg("max_norm"));
   m.def("sq_norm", &sq_norm_t);
   m.def("router_topk", &router_topk_t);
-  m.def("moe_plan", &moe_plan_t);
+  m.def("kv_cache_write", &kv_cache_write_t, py::arg("src"), py::arg("pos"), py::arg("dst"), py::arg("scale"),
+        py::arg("row_offset"));
+  m.def("moe_plan", &moe_plan_t, py::arg("idx"), py::arg("E"), py::arg("capacity"), py::arg("cap_rows"),
+        py::arg("align") = 128);
   m.def("moe_gather", &moe_gather_t);
   m.def("moe_combine", &moe_combine_t);
   m.def("moe_combine_bwd", &moe_combine_bwd_t);
@@ -465,7 +500,7 @@ void register_kernels(pybind11::module_& m) {
   m.def("int4_gemv", &int4_gemv_t, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("offset"));
   m.def("int4_dequant", &int4_dequant_t, py::arg("w"), py::arg("scale"), py::arg("K"), py::arg("offset"));
   m.def("decode_rows_limit", [](int64_t DQ, int64_t DV, bool latent, int64_t Hk) -> int64_t {
-    return (latent && Hk == 1 && decode_plan(1, 1, 1, 1, 1, (int)DQ, (int)DV, true, 0, 0).tc) ? (1 << 20) : 64;
+    return (latent && Hk == 1 && decode_plan(1, 1, 1, 1, 1, (int)DQ, (int)DV, true, 0, 0, 2).tc) ? (1 << 20) : 64;
   }, "query rows (tokens x heads per kv group) one decode call takes");
   m.def("attn_decode", &attn_decode_t, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("k_scale"),
         py::arg("v_scale"), py::arg("q_pos"), py::arg("kv_len"), py::arg("window"), py::arg("scale"),

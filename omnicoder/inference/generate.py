@@ -102,9 +102,11 @@ def _sync(t: torch.Tensor):
 def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: float = 0.8, top_k: int = 40,
              top_p: float = 0.9, draft_model=None, speculative_draft_len: int = 0, kvq: str = "none",
              window_size: int = 0, return_stats: bool = False, eos_id: int | None = None, seed: int | None = None,
-             max_len: int | None = None, **_unused):
+             max_len: int | None = None, cuda_graph: bool = True, **_unused):
     """Generate `max_new_tokens` tokens after `input_ids` [B, S] (or [S]).  Returns
-    [B, S + max_new_tokens] (and GenStats with return_stats)."""
+    [B, S + max_new_tokens] (and GenStats with return_stats).  On CUDA the
+    decode step is captured once as a CUDA graph (`cuda_graph=False` runs it
+    eagerly)."""
     model.eval()
     squeeze = input_ids.dim() == 1
     ids = input_ids[None] if squeeze else input_ids
@@ -132,10 +134,14 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         stats.prefill_s = time.perf_counter() - t0
         toks = [tok]
         done = torch.zeros(B, dtype=torch.bool, device=dev)
+        step = None
+        if cuda_graph and dev.type == "cuda" and max_new_tokens > 2:
+            from .graphs import GraphedStep
+            step = GraphedStep(model, cache)
         t1 = time.perf_counter()
         for _ in range(max_new_tokens - 1):
             ts = time.perf_counter()
-            logits = model.forward_cached(tok[:, None], cache)[:, -1]
+            logits = (step(tok[:, None]) if step is not None else model.forward_cached(tok[:, None], cache))[:, -1]
             tok = sample_next_token(logits, temperature, top_k, top_p, gen)
             if eos_id is not None:
                 done |= tok == eos_id

@@ -79,6 +79,18 @@ class KVCache:
     def write(self, layer: int, pos: torch.Tensor, k: torch.Tensor, v: torch.Tensor | None = None):
         """Store new entries at positions pos [B, T]; k [B, T, ...] (MLA: latent [B, T, r+dr])."""
         B, T = pos.shape
+        if k.is_cuda and self.k[layer].dtype in (torch.int8, torch.bfloat16):
+            from ..ops import _ext
+            C = _ext.load()
+            p = pos.to(torch.int64).contiguous()
+            if self.mla:
+                C.kv_cache_write(k.reshape(B, T, 1, -1).to(torch.bfloat16).contiguous(), p, self.k[layer],
+                                 self.ks[layer], self.sink)
+            else:
+                C.kv_cache_write(k.to(torch.bfloat16).contiguous(), p, self.k[layer], self.ks[layer], self.sink)
+                if v is not None:
+                    C.kv_cache_write(v.to(torch.bfloat16).contiguous(), p, self.v[layer], self.vs[layer], self.sink)
+            return
         pos = pos + self.sink
         bidx = torch.arange(B, device=self.device)[:, None].expand(B, T)
         if self.kv_dtype == "int8":

@@ -289,7 +289,9 @@ class _SwiGLUMLPFn(torch.autograd.Function):
         T = x2.shape[0]
         F2 = w13.shape[0]
         act = torch.empty(T, F2 // 2, device=x.device, dtype=torch.bfloat16)
-        H = torch.empty(T, F2, device=x.device, dtype=torch.bfloat16)
+        # the pre-activation is kept only for backward (without it, few-row calls take the
+        # swap-AB kernel)
+        H = torch.empty(T, F2, device=x.device, dtype=torch.bfloat16) if any(ctx.needs_input_grad) else None
         C.gemm(x2, w13, act, False, False, EPI_SWIGLU, 1.0, None, H, 256)
         y = mm_nt(act, w2, residual=None if residual is None else _flat(residual).contiguous())
         ctx.save_for_backward(x2, w13, w2, H, act)
@@ -316,6 +318,14 @@ def swiglu_mlp(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, residual: t
         g, u = deinterleave_cols(h)
         y = F.linear(F.silu(g) * u, w2)
         return y if residual is None else y + residual
+    if not torch.is_grad_enabled():
+        # inference: no pre-activation is kept, so few-row calls take the swap-AB kernel
+        C = _ext.load()
+        x2 = _flat(x).contiguous()
+        act = torch.empty(x2.shape[0], w13.shape[0] // 2, device=x.device, dtype=torch.bfloat16)
+        C.gemm(x2, w13, act, False, False, EPI_SWIGLU, 1.0, None, None, 256)
+        y = mm_nt(act, w2, residual=None if residual is None else _flat(residual).contiguous())
+        return y.view(*x.shape[:-1], w2.shape[0])
     return _SwiGLUMLPFn.apply(x, w13, w2, residual)
 
 

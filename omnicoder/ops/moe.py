@@ -141,6 +141,45 @@ class _MoEFn(torch.autograd.Function):
         return dx, drouter, dw13, dw2, (dout if has_add else None), None, None, None, None, None, None
 
 
+SKINNY_MAX_PAIRS = 256   # token-expert pairs up to which inference uses the few-row expert GEMM
+
+
+def _moe_infer(x, router_w, w13, w2, add, k, capacity, renorm):
+    """Forward only (no autograd state).  Up to SKINNY_MAX_PAIRS routed pairs the
+    permutation is packed (no 128-row padding) and both expert GEMMs run the
+    few-row swap-AB kernel, which streams each expert's weights once whatever
+    its token count; larger batches use the tile GEMM without storing the
+    SwiGLU pre-activation."""
+    C = _ext.load()
+    x = x.contiguous()
+    T, D = x.shape
+    E = router_w.shape[0]
+    F2 = w13.shape[1]
+    logits = mm_nt(x, router_w, out_f32=True)
+    idx, wts, _ = C.router_topk(logits, k, renorm)
+    n = T * k
+    dev = x.device
+    if n <= SKINNY_MAX_PAIRS:
+        counts, offsets, pos, src = C.moe_plan(idx, E, capacity, n, 1)
+        x_perm = torch.empty(n, D, device=dev, dtype=torch.bfloat16)
+        C.moe_gather(x, src, x_perm, k, offsets)
+        act = torch.empty(n, F2 // 2, device=dev, dtype=torch.bfloat16)
+        C.gemm_skinny_grouped(x_perm, w13, offsets, act, EPI_SWIGLU, 1.0, n)
+        y_perm = torch.empty(n, D, device=dev, dtype=torch.bfloat16)
+        C.gemm_skinny_grouped(act, w2, offsets, y_perm, EPI_BF16, 1.0, n)
+    else:
+        rows = cap_rows_for(T, k, E, capacity)
+        counts, offsets, pos, src = C.moe_plan(idx, E, capacity, rows)
+        x_perm = torch.empty(rows, D, device=dev, dtype=torch.bfloat16)
+        C.moe_gather(x, src, x_perm, k, offsets)
+        act = torch.empty(rows, F2 // 2, device=dev, dtype=torch.bfloat16)
+        C.gemm_grouped_m(x_perm, w13, offsets, act, False, EPI_SWIGLU, 1.0, None, None, 256, rows)
+        y_perm = torch.empty(rows, D, device=dev, dtype=torch.bfloat16)
+        C.gemm_grouped_m(act, w2, offsets, y_perm, False, EPI_BF16, 1.0, None, None, 256, rows)
+    out = C.moe_combine(y_perm, pos, wts, None if add is None else add.contiguous())
+    return out, x.new_zeros((), dtype=torch.float32)
+
+
 def moe_ffn(x: torch.Tensor, router_w: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, k: int,
             capacity: int = 0, renorm: bool = True, aux_alpha: float = 0.0, z_beta: float = 0.0,
             add: torch.Tensor | None = None, aux_grad_scale: float = 1.0):
@@ -152,4 +191,6 @@ def moe_ffn(x: torch.Tensor, router_w: torch.Tensor, w13: torch.Tensor, w2: torc
     differentiable scalar the caller adds to the loss."""
     if not x.is_cuda:
         return moe_ffn_torch(x, router_w, w13, w2, k, capacity, renorm, aux_alpha, z_beta, add)
+    if not (torch.is_grad_enabled() and any(t.requires_grad for t in (x, router_w, w13, w2))):
+        return _moe_infer(x, router_w, w13, w2, add, k, capacity, renorm)
     return _MoEFn.apply(x, router_w, w13, w2, add, k, capacity, renorm, aux_alpha, z_beta, aux_grad_scale)

@@ -115,3 +115,97 @@ def test_decode_with_memory_rows(int8):
     ref = decode_attention_torch(q.float(), k, None, q_pos.long(), kv_len.long(), **kw)
     torch.cuda.synchronize()
     assert (out.float() - ref.float()).abs().max().item() < 2e-2 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("int8", [False, True])
+@pytest.mark.parametrize("Tn,H,Hk,D", [(1, 8, 8, 128), (2, 8, 2, 64), (4, 16, 4, 128)])
+def test_decode_mha_memory_rows_and_window(int8, Tn, H, Hk, D):
+    """Few-row (GEMV) kernel: MHA / GQA caches with memory rows, a window and ragged lengths."""
+    from omnicoder.inference.kv_cache import quantize_int8
+    from omnicoder.ops.decode import decode_attention, decode_attention_torch
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cpu").manual_seed(2)
+    B, S, L = 5, 16, 700
+    q = torch.randn(B, Tn, H, D, generator=g).to(dev, torch.bfloat16)
+    k = torch.randn(B, S + L, Hk, D, generator=g).to(dev, torch.bfloat16)
+    v = torch.randn(B, S + L, Hk, D, generator=g).to(dev, torch.bfloat16)
+    kv_len = torch.tensor([699, 300, 64, 5 + Tn, 513], dtype=torch.int32, device=dev)
+    q_pos = (kv_len[:, None] - Tn + torch.arange(Tn, device=dev)[None]).to(torch.int32)
+    ks = vs = None
+    if int8:
+        k, ks = quantize_int8(k, -1)
+        v, vs = quantize_int8(v, -1)
+    kw = dict(window=200, scale=1.0 / math.sqrt(D), k_scale=ks, v_scale=vs, sink_rows=S, n_sink=12)
+    out = decode_attention(q, k, v, q_pos, kv_len, **kw)
+    ref = decode_attention_torch(q.float(), k, v, q_pos.long(), kv_len.long(), **kw)
+    torch.cuda.synchronize()
+    assert (out.float() - ref.float()).abs().max().item() < 2e-2 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("mla", [True, False])
+@pytest.mark.parametrize("kv", ["int8", "bf16"])
+def test_kv_cache_write_kernel_matches_torch(mla, kv):
+    """The fused append kernel writes the rows and scales quantize_int8 + index_put would."""
+    from omnicoder.inference.kv_cache import quantize_int8
+    from omnicoder.ops import _ext
+    C = _ext.load()
+    dev = torch.device("cuda")
+    torch.manual_seed(0)
+    B, T, L, sink = 3, 5, 40, 4
+    shape = (B, T, 1, 576) if mla else (B, T, 4, 128)
+    src = torch.randn(*shape, device=dev).to(torch.bfloat16)
+    pos = torch.tensor([[0, 1, 2, 3, 4], [7, 8, 9, 10, 11], [30, 31, 32, 33, 34]], device=dev)
+    G, D = shape[2], shape[3]
+    dt = torch.int8 if kv == "int8" else torch.bfloat16
+    dst = torch.zeros(B, L, G, D, device=dev, dtype=dt)
+    sc = torch.zeros(B, L, G, device=dev) if kv == "int8" else None
+    C.kv_cache_write(src, pos, dst, sc, sink)
+    rows = pos + sink
+    b = torch.arange(B, device=dev)[:, None].expand(B, T)
+    if kv == "int8":
+        q, s = quantize_int8(src, -1)
+        assert torch.equal(dst[b, rows], q)
+        assert torch.allclose(sc[b, rows], s, rtol=1e-6, atol=0)
+    else:
+        assert torch.equal(dst[b, rows], src)
+    mask = torch.ones(B, L, dtype=torch.bool, device=dev)
+    mask[b, rows] = False
+    assert (dst[mask] == 0).all()
+
+
+def test_graphed_decode_matches_eager():
+    """A decode step replayed from a CUDA graph produces the eager step's logits and cache."""
+    from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig
+    from omnicoder.inference.graphs import GraphedStep
+    from omnicoder.inference.kv_cache import KVCache
+    from omnicoder.models.lm import build_model
+    dev = torch.device("cuda")
+    attn = AttentionConfig(kind="mla", kv_lora_rank=512, qk_rope_dim=64, qk_nope_dim=64, v_head_dim=128,
+                           window=64, mem_slots=8)
+    cfg = ModelConfig(name="g", vocab_size=1000, d_model=512, n_layers=2, n_heads=16, ffn_dim=1024,
+                      tie_embeddings=True, max_seq_len=512, attn=attn,
+                      moe=MoEConfig(n_experts=8, top_k=2, ffn_dim=256, n_shared_experts=1))
+    m = build_model(cfg, device=dev, seed=0).eval().prepare_inference()
+    B = 4
+    ids = torch.randint(0, 1000, (B, 128), device=dev)
+    caches = []
+    for _ in range(2):
+        c = KVCache(cfg, B, 160, dev, kv_dtype="int8")
+        with torch.no_grad():
+            m.forward_cached(ids, c, prefill=True, last_only=True)
+        c.compress_memory(64)
+        caches.append(c)
+    step = GraphedStep(m, caches[1])
+    tok = ids[:, -1]
+    for _ in range(4):
+        with torch.no_grad():
+            le = m.forward_cached(tok[:, None], caches[0])
+        lg = step(tok[:, None])
+        torch.cuda.synchronize()
+        # split-K partial sums of the few-row GEMM are added with fp32 atomics, so two runs
+        # may differ in the last bf16 bit of an activation
+        assert (le - lg).abs().max().item() < 2e-2 * max(1.0, le.abs().max().item())
+        assert torch.equal(caches[0].lengths, caches[1].lengths)
+        tok = le[:, -1].argmax(-1)
+    assert (caches[0].k[0].float() - caches[1].k[0].float()).abs().max().item() <= 2
