@@ -699,6 +699,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_mla_tc_kernel(DecArgs a,
     constexpr uint32_t idesc_s = umma_idesc_f16(128, RG, false, false, !I8);
     constexpr uint32_t idesc_o = umma_idesc_f16(128, RG, true, false, !I8);
     const uint32_t ka = smem_u32(sK), qa = smem_u32(sQ), pa = smem_u32(sP);
+    // base descriptors; an operand at byte offset `off` is base + (off >> 4) (the 14-bit
+    // start-address field cannot carry for shared-memory addresses)
+    const uint64_t dK = umma_desc_sw128(ka, 16, 1024), dQ = umma_desc_sw128(qa, 16, 1024);
+    const uint64_t dV = umma_desc_sw128(ka, kTcKeys * 128, 1024), dP = umma_desc_sw128(pa, 16, 1024);
     for (int it = 0; it < nt; ++it) {
       const int tile = t0 + it;
       if (issuer && ok) {
@@ -713,7 +717,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_mla_tc_kernel(DecArgs a,
           for (int k4 = 0; k4 < 4; ++k4) {
             const uint32_t koff = c * (kTcKeys * 128) + k4 * 32;
             const uint32_t qoff = c * (RG * 128) + k4 * 32;
-            tc_mma_f16(tS + k4 * RG, umma_desc_sw128(ka + koff, 16, 1024), umma_desc_sw128(qa + qoff, 16, 1024),
+            tc_mma_f16(tS + k4 * RG, dK + (koff >> 4), dQ + (qoff >> 4),
                        idesc_s, i > 0 ? 1u : 0u);
           }
           if (i < NROPE) tc_commit(&chunk_free[c]);  // rope chunks: free once the scores are done
@@ -820,8 +824,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) decode_mla_tc_kernel(DecArgs a,
             for (int kk = 0; kk < kTcKeys / 16; ++kk) {
               const uint32_t aoff = (2 * j) * (kTcKeys * 128) + kk * 2048;
               const uint32_t poff = (kk >> 2) * (RG * 128) + (kk & 3) * 32;
-              tc_mma_f16(tO + j * RG, umma_desc_sw128(ka + aoff, kTcKeys * 128, 1024),
-                         umma_desc_sw128(pa + poff, 16, 1024), idesc_o, (it > 0 || kk > 0) ? 1u : 0u);
+              tc_mma_f16(tO + j * RG, dV + (aoff >> 4), dP + (poff >> 4), idesc_o, (it > 0 || kk > 0) ? 1u : 0u);
             }
             tc_commit(&chunk_free[2 * j]);
             tc_commit(&chunk_free[2 * j + 1]);
