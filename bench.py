@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--no-count", action="store_true")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel exchange: fused peer-memory kernels or NCCL all_to_all (baseline)")
+    ap.add_argument("--no-decode", action="store_true", help="skip the batch-64 long-context decode measurement")
+    ap.add_argument("--decode-gen", type=int, default=512)
     return ap.parse_args()
 
 
@@ -120,6 +122,64 @@ def reference_arm(args):
         if not os.path.isdir(ref):
             why = "reference not installed under baseline/_ref; " + why
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+# ----------------------------------------------------------------------------
+def decode_phase(args, dev, world, rank, barrier):
+    """Batch-64 long-context decode (the metric's second half): every GPU serves its own
+    64 sequences with a full replica of the long-context MoE model (24L d2048 MLA, 32
+    experts top-4, window 4096 + 64 memory rows, int8 KV), 8192-token random prompts,
+    greedy generation.  Device-timed: the decode steps (CUDA graphs), max over ranks.
+    End to end: the public generate() call, prompts copied from pinned host memory and
+    the generated ids read back, timed around the whole call."""
+    import torch
+    import torch.distributed as dist
+
+    from omnicoder.benchmarks.bench_inference import run
+    from omnicoder.config import get_preset
+    from omnicoder.inference.generate import generate
+    from omnicoder.models.lm import build_model
+
+    res = run(batch=64, prompt=8192, gen=args.decode_gen, kv="int8", seed=rank, device=dev)
+    dec_s = (res["decode_steps"] and 64 * (args.decode_gen - 1) / res["decode_tokens_per_s"])
+    pre_s = res["prefill_s"]
+    torch.cuda.empty_cache()
+    # ---- end to end through generate() ------------------------------------------------------
+    cfg = get_preset("longctx_moe")
+    model = build_model(cfg, device=dev, seed=rank).eval().prepare_inference()
+    g = torch.Generator().manual_seed(rank + 100)
+    prompts = torch.randint(0, cfg.vocab_size, (64, 8192), generator=g).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    out = generate(model, prompts.to(dev, non_blocking=True), args.decode_gen, temperature=0.0, top_k=0, top_p=1.0,
+                   kvq="int8")
+    host = out.cpu()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_s = e0.elapsed_time(e1) / 1000.0
+    barrier()
+    t = torch.tensor([dec_s, pre_s, e2e_s], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dec_s, pre_s, e2e_s = [float(x) for x in t.tolist()]
+    gen_tokens = 64 * (args.decode_gen - 1)
+    del model
+    torch.cuda.empty_cache()
+    return {
+        "metric": "decode tokens/s at batch 64 (long-context MoE inference)", "value": world * gen_tokens / dec_s,
+        "unit": "tokens/s", "per_gpu_batch": 64, "prompt": 8192, "gen": args.decode_gen, "kv": "int8",
+        "window": 4096, "memory_rows": res["memory_rows"], "p50_tpot_ms": res["p50_tpot_ms"],
+        "prefill_tokens_per_s": world * 64 * 8192 / pre_s, "cuda_graphs": True,
+        "parallelism": f"{world} replica(s), one per GPU (13 GB of weights each)",
+        "model": res["model"], "data": "synthetic (uniform random prompts, random-init N(0,0.02))",
+        "e2e": {"value": world * 64 * args.decode_gen / e2e_s, "unit": "generated tokens/s (prefill + decode)",
+                "s": e2e_s, "h2d_bytes_per_step": prompts.numel() * prompts.element_size(),
+                "d2h_bytes_per_step": host.numel() * host.element_size(),
+                "note": "one generate() call per rank: prompts H2D from pinned memory, ids D2H"},
+    }
 
 
 # ----------------------------------------------------------------------------
@@ -243,6 +303,14 @@ def main():
                     other += 1
         launches = {"ours_per_step": ours, "other_per_step": other}
 
+    decode = None
+    if not args.no_decode:
+        del trainer, model, last
+        import gc
+        gc.collect()
+        torch.cuda.empty_cache()
+        decode = decode_phase(args, dev, world, rank, barrier)
+
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -255,7 +323,7 @@ def main():
                        "l2": "working set (14.6 GB bf16 weights, 8192 tokens/GPU of activations) >> 126 MB L2"},
             "loss": loss_val, "e2e": e2e,
             "gpu_launches": (launches["ours_per_step"] * args.steps) if launches else None,
-            "launches_per_step": launches, "clocks": clk, "impl": "ours",
+            "launches_per_step": launches, "clocks": clk, "impl": "ours", "decode": decode,
         }
         print(json.dumps(out), flush=True)
     if world > 1:

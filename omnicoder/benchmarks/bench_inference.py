@@ -26,6 +26,102 @@ from omnicoder.models.lm import build_model
 from omnicoder.ops import _ext
 
 
+def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, gen=512, kv="int8", spec=0,
+        prefill_chunk=4, layers=0, graphs=True, seed=0, device=None):
+    """One long-context batched generation; returns the result dict (device-timed with CUDA events)."""
+    dev = device or torch.device("cuda")
+    _ext.load()
+    cfg = get_preset(preset)
+    if layers:
+        cfg.n_layers = layers
+    cfg.max_seq_len = max(cfg.max_seq_len, prompt + gen + spec + 1)
+    model = build_model(cfg, device=dev, seed=seed).eval().prepare_inference()
+    draft = None
+    if spec > 0:
+        dcfg = get_preset(draft_preset)
+        dcfg.vocab_size = cfg.vocab_size
+        dcfg.max_seq_len = cfg.max_seq_len
+        draft = build_model(dcfg, device=dev, seed=seed + 1).eval()
+    g = torch.Generator().manual_seed(seed)
+    prompts = torch.randint(0, cfg.vocab_size, (batch, prompt), generator=g).to(dev)
+    L = prompt + gen + spec + 1
+    cache = KVCache(cfg, batch, L, dev, kv_dtype=kv)
+    dcache = KVCache(draft.cfg, batch, L, dev) if draft is not None else None
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    # ---- prefill: the whole prompt, in chunks of sequences; its last logits give token 1
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    e0.record()
+    first = []
+    with torch.no_grad():
+        for b0 in range(0, batch, prefill_chunk):
+            b1 = min(batch, b0 + prefill_chunk)
+            lg = model.forward_cached(prompts[b0:b1], cache.view(b0, b1), prefill=True, last_only=True)
+            first.append(lg[:, -1].argmax(-1))
+            if draft is not None:
+                draft.forward_cached(prompts[b0:b1], dcache.view(b0, b1), prefill=True, last_only=True)
+        n_mem = cache.compress_memory(cfg.attn.window) if cfg.attn.window else 0
+        last = torch.cat(first)
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_s = e0.elapsed_time(e1) / 1000.0
+    # ---- decode: the remaining gen - 1 tokens ---------------------------------------
+    step_ms, produced, accepted, proposed = [], 1, 0, 0
+    fwd_t = lambda ids: model.forward_cached(ids, cache)
+    fwd_d = (lambda ids: draft.forward_cached(ids, dcache)) if draft is not None else None
+    if graphs:
+        from omnicoder.inference.graphs import GraphedStep
+        fwd_t = GraphedStep(model, cache, 1 if draft is None else spec + 1)
+        if draft is not None:
+            fwd_d = GraphedStep(draft, dcache, 1)
+    with torch.no_grad():
+        while produced < gen:
+            s0, s1 = ev(), ev()
+            s0.record()
+            if draft is None:
+                last = fwd_t(last[:, None])[:, -1].argmax(-1)
+                n_new = 1
+            else:
+                base_t, base_d = cache.lengths.clone(), dcache.lengths.clone()
+                cur, props = last, []
+                for _ in range(spec):
+                    cur = fwd_d(cur[:, None])[:, -1].argmax(-1)
+                    props.append(cur)
+                props = torch.stack(props, 1)                                    # [B, k] proposals
+                tgt = fwd_t(torch.cat([last[:, None], props], 1)).argmax(-1)  # [B, k+1]
+                n_acc = torch.cumprod((tgt[:, :spec] == props).int(), 1).sum(1)
+                # lock-step batch: keep the prefix every sequence accepted, then the target's token
+                m = int(n_acc.min())
+                if m == spec:
+                    fwd_d(props[:, -1:])
+                cache.rollback(base_t + m + 1)
+                dcache.rollback(base_d + m + 1)
+                last = tgt[:, m]
+                accepted += int(n_acc.sum())
+                proposed += batch * spec
+                n_new = m + 1
+            s1.record()
+            s1.synchronize()
+            step_ms.append(s0.elapsed_time(s1))
+            produced += n_new
+    _ext.check_status()
+    decode_s = sum(step_ms) / 1000.0
+    res = {
+        "metric": "long-context MoE inference (prefill tokens/s, decode tokens/s, p50 TPOT)",
+        "model": f"{cfg.name}: {cfg.n_layers}L d{cfg.d_model} MLA kv{cfg.attn.kv_lora_rank} {cfg.moe.n_experts} experts "
+                 f"top-{cfg.moe.top_k}, window {cfg.attn.window} + {cfg.attn.mem_slots} memory rows",
+        "batch": batch, "prompt": prompt, "gen": gen, "kv": kv, "spec_tokens": spec,
+        "prefill_tokens_per_s": batch * prompt / prefill_s, "prefill_s": prefill_s,
+        "decode_tokens_per_s": batch * (produced - 1) / decode_s, "decode_steps": len(step_ms),
+        "p50_step_ms": statistics.median(step_ms),
+        "p50_tpot_ms": statistics.median(step_ms) * len(step_ms) / max(1, produced - 1),
+        "memory_rows": n_mem, "kv_cache_gb": cache.nbytes() / 1e9,
+        "draft_acceptance": (accepted / proposed) if proposed else None, "cuda_graphs": graphs,
+        "data": "synthetic (uniform random prompts, random-init N(0,0.02) weights)", "dtype": "bf16 weights",
+    }
+    return res
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="longctx_moe")
@@ -40,96 +136,7 @@ def main(argv=None):
     ap.add_argument("--no-graphs", dest="graphs", action="store_false", help="run decode steps eagerly")
     ap.add_argument("--json", default=None)
     a = ap.parse_args(argv)
-    dev = torch.device("cuda")
-    C = _ext.load()
-    cfg = get_preset(a.preset)
-    if a.layers:
-        cfg.n_layers = a.layers
-    cfg.max_seq_len = max(cfg.max_seq_len, a.prompt + a.gen + a.spec + 1)
-    model = build_model(cfg, device=dev, seed=0).eval().prepare_inference()
-    draft = None
-    if a.spec > 0:
-        dcfg = get_preset(a.draft)
-        dcfg.vocab_size = cfg.vocab_size
-        dcfg.max_seq_len = cfg.max_seq_len
-        draft = build_model(dcfg, device=dev, seed=1).eval()
-    g = torch.Generator().manual_seed(0)
-    prompts = torch.randint(0, cfg.vocab_size, (a.batch, a.prompt), generator=g).to(dev)
-    L = a.prompt + a.gen + a.spec + 1
-    cache = KVCache(cfg, a.batch, L, dev, kv_dtype=a.kv)
-    dcache = KVCache(draft.cfg, a.batch, L, dev) if draft is not None else None
-    ev = lambda: torch.cuda.Event(enable_timing=True)
-    # ---- prefill: the whole prompt, in chunks of sequences; its last logits give token 1
-    torch.cuda.synchronize()
-    e0, e1 = ev(), ev()
-    e0.record()
-    first = []
-    with torch.no_grad():
-        for b0 in range(0, a.batch, a.prefill_chunk):
-            b1 = min(a.batch, b0 + a.prefill_chunk)
-            lg = model.forward_cached(prompts[b0:b1], cache.view(b0, b1), prefill=True, last_only=True)
-            first.append(lg[:, -1].argmax(-1))
-            if draft is not None:
-                draft.forward_cached(prompts[b0:b1], dcache.view(b0, b1), prefill=True, last_only=True)
-        n_mem = cache.compress_memory(cfg.attn.window) if cfg.attn.window else 0
-        last = torch.cat(first)
-    e1.record()
-    torch.cuda.synchronize()
-    prefill_s = e0.elapsed_time(e1) / 1000.0
-    # ---- decode: the remaining gen - 1 tokens ---------------------------------------
-    step_ms, produced, accepted, proposed = [], 1, 0, 0
-    fwd_t = lambda ids: model.forward_cached(ids, cache)
-    fwd_d = (lambda ids: draft.forward_cached(ids, dcache)) if draft is not None else None
-    if a.graphs:
-        from omnicoder.inference.graphs import GraphedStep
-        fwd_t = GraphedStep(model, cache, 1 if draft is None else a.spec + 1)
-        if draft is not None:
-            fwd_d = GraphedStep(draft, dcache, 1)
-    with torch.no_grad():
-        while produced < a.gen:
-            s0, s1 = ev(), ev()
-            s0.record()
-            if draft is None:
-                last = fwd_t(last[:, None])[:, -1].argmax(-1)
-                n_new = 1
-            else:
-                base_t, base_d = cache.lengths.clone(), dcache.lengths.clone()
-                cur, props = last, []
-                for _ in range(a.spec):
-                    cur = fwd_d(cur[:, None])[:, -1].argmax(-1)
-                    props.append(cur)
-                props = torch.stack(props, 1)                                    # [B, k] proposals
-                tgt = fwd_t(torch.cat([last[:, None], props], 1)).argmax(-1)  # [B, k+1]
-                n_acc = torch.cumprod((tgt[:, :a.spec] == props).int(), 1).sum(1)
-                # lock-step batch: keep the prefix every sequence accepted, then the target's token
-                m = int(n_acc.min())
-                if m == a.spec:
-                    fwd_d(props[:, -1:])
-                cache.rollback(base_t + m + 1)
-                dcache.rollback(base_d + m + 1)
-                last = tgt[:, m]
-                accepted += int(n_acc.sum())
-                proposed += a.batch * a.spec
-                n_new = m + 1
-            s1.record()
-            s1.synchronize()
-            step_ms.append(s0.elapsed_time(s1))
-            produced += n_new
-    _ext.check_status()
-    decode_s = sum(step_ms) / 1000.0
-    res = {
-        "metric": "long-context MoE inference (prefill tokens/s, decode tokens/s, p50 TPOT)",
-        "model": f"{cfg.name}: {cfg.n_layers}L d{cfg.d_model} MLA kv{cfg.attn.kv_lora_rank} {cfg.moe.n_experts} experts "
-                 f"top-{cfg.moe.top_k}, window {cfg.attn.window} + {cfg.attn.mem_slots} memory rows",
-        "batch": a.batch, "prompt": a.prompt, "gen": a.gen, "kv": a.kv, "spec_tokens": a.spec,
-        "prefill_tokens_per_s": a.batch * a.prompt / prefill_s, "prefill_s": prefill_s,
-        "decode_tokens_per_s": a.batch * (produced - 1) / decode_s, "decode_steps": len(step_ms),
-        "p50_step_ms": statistics.median(step_ms),
-        "p50_tpot_ms": statistics.median(step_ms) * len(step_ms) / max(1, produced - 1),
-        "memory_rows": n_mem, "kv_cache_gb": cache.nbytes() / 1e9,
-        "draft_acceptance": (accepted / proposed) if proposed else None, "cuda_graphs": a.graphs,
-        "data": "synthetic (uniform random prompts, random-init N(0,0.02) weights)", "dtype": "bf16 weights",
-    }
+    res = run(a.preset, a.draft, a.batch, a.prompt, a.gen, a.kv, a.spec, a.prefill_chunk, a.layers, a.graphs)
     print(json.dumps(res))
     if a.json:
         with open(a.json, "w") as f:

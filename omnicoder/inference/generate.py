@@ -92,6 +92,26 @@ class GenStats:
         return d
 
 
+PREFILL_TOKENS = 32768   # tokens per prefill call (whole sequences; bounds the activation memory)
+
+
+def _prefill(model, ids: torch.Tensor, cache) -> torch.Tensor:
+    """Run the prompt through the model in chunks of whole sequences and return the
+    last-position logits [B, V].  With memory rows and a window, the tokens that left
+    the window are then summarised into the memory rows."""
+    B, S = ids.shape
+    step = max(1, PREFILL_TOKENS // max(1, S))
+    out = []
+    for b0 in range(0, B, step):
+        b1 = min(B, b0 + step)
+        view = cache.view(b0, b1) if (b0, b1) != (0, B) else cache
+        out.append(model.forward_cached(ids[b0:b1], view, prefill=True, last_only=True)[:, -1])
+    cfg = model.cfg
+    if getattr(cfg.attn, "mem_slots", 0) and cfg.attn.window:
+        cache.compress_memory(cfg.attn.window)
+    return torch.cat(out) if len(out) > 1 else out[0]
+
+
 def _sync(t: torch.Tensor):
     if t.is_cuda:
         torch.cuda.synchronize(t.device)
@@ -128,7 +148,7 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
     else:
         cache = KVCache(cfg, B, L, dev, dtype=model.embed.dtype, kv_dtype=kv_dtype)
         t0 = time.perf_counter()
-        logits = model.forward_cached(ids, cache, prefill=True, last_only=True)[:, -1]
+        logits = _prefill(model, ids, cache)
         tok = sample_next_token(logits, temperature, top_k, top_p, gen)
         _sync(tok)
         stats.prefill_s = time.perf_counter() - t0
