@@ -44,6 +44,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kTile = 128;
 constexpr int kAttnThreads = 192;
+// backward kernels: producer warp, MMA warp and 8 softmax warps (two per TMEM lane
+// quadrant, each taking half of the 64 columns of a tile)
+constexpr int kBwdThreads = 320;
+constexpr int kBwdSoftmaxWarps = 8;
 constexpr int kSubTile = 16384;  // one [128 rows x 64 bf16] swizzled sub-tile
 
 struct AttnArgs {
@@ -85,19 +89,6 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* tile, int r, const floa
   }
 }
 
-__device__ __forceinline__ void store_chunk32_sw128(uint8_t* tile, int r, int c32, const float* v) {
-  // columns [32*c32, 32*c32+32) of row r
-  const int sub = c32 >> 1;
-  const int ch0 = (c32 & 1) * 4;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float* x = v + q * 8;
-    uint4 w = make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]),
-                         pack_bf16x2(x[6], x[7]));
-    const int ch = ch0 + q;
-    *reinterpret_cast<uint4*>(tile + sub * kSubTile + r * 128 + ((ch ^ (r & 7)) << 4)) = w;
-  }
-}
 
 __device__ __forceinline__ void store_global_row(bf16* dst, const float* v, int n, float mul) {
   for (int q = 0; q < n / 8; ++q) {
@@ -374,9 +365,7 @@ struct DkdvSmem {
   static constexpr int kOffV = kOffK + kK;
   static constexpr int kOffQ = kOffV + kV;         // 2 stages
   static constexpr int kOffDO = kOffQ + 2 * kQ;    // 2 stages
-  static constexpr int kOffPT = kOffDO + 2 * kDO;  // P^T [128 kv x 64 q] bf16
-  static constexpr int kOffDS = kOffPT + kSubTile; // dS^T [128 kv x 64 q] bf16
-  static constexpr int kOffVec = kOffDS + kSubTile;  // 2 stages of lse/delta
+  static constexpr int kOffVec = kOffDO + 2 * kDO;  // 2 stages of lse/delta
   static constexpr int kOffBar = kOffVec + 2 * kVec;
   static constexpr int kBytes = kOffBar + 256 + 1024;
 };
@@ -385,11 +374,15 @@ struct DkdvSmem {
 // rows (and over the query heads of a GQA group).  Q/dO (with the tile's lse and
 // delta, fetched by bulk copies on the same barrier) are double buffered so the
 // next tile streams in while this one computes; S^T is double buffered in TMEM
-// so K Q^T of the next tile runs during this tile's softmax.
-//   TMEM columns: S^T[2] = [0, 64), [64, 128); dP^T = [128, 192);
+// so K Q^T of the next tile runs during this tile's softmax.  P^T and dS^T (bf16)
+// are written over the two halves of their S^T stage and feed their MMAs
+// (dV += P^T dO, dK += dS^T Q) straight from tensor memory: thread r holds row r
+// of both, which is the A-operand layout.  dP^T is released as soon as the
+// softmax has read it, so the next tile's V dO^T does not wait for dK.
+//   TMEM columns: S^T -> [P^T | dS^T] [2] = [0, 64), [64, 128); dP^T = [128, 192);
 //                 dV = [192, 192 + DV); dK = [192 + DV, 192 + DV + DQ)
 template <int DQ, int DV, bool ROPE>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmKR, const __grid_constant__ CUtensorMap tmV,
                      const __grid_constant__ CUtensorMap tmDO, AttnArgs p) {
@@ -404,8 +397,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sV = smem + L::kOffV;
   uint8_t* sQ = smem + L::kOffQ;
   uint8_t* sDO = smem + L::kOffDO;
-  uint8_t* sPT = smem + L::kOffPT;
-  uint8_t* sDS = smem + L::kOffDS;
   float* sVec = reinterpret_cast<float*>(smem + L::kOffVec);  // [stage][lse 64 | delta 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* kv_full = bars + 0;
@@ -414,15 +405,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* do_full = bars + 5;   // [2]
   uint64_t* do_empty = bars + 7;  // [2]
   uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* s_empty = bars + 11;  // [2] count 4
-  uint64_t* pt_ready = bars + 13; // count 4
-  uint64_t* pt_free = bars + 14;
-  uint64_t* dp_full = bars + 15;
-  uint64_t* dp_empty = bars + 16; // count 4
-  uint64_t* ds_ready = bars + 17; // count 4
-  uint64_t* ds_free = bars + 18;
-  uint64_t* acc_done = bars + 19;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* s_empty = bars + 11;  // [2] S^T / P^T / dS^T stage free (commit after dK read dS^T)
+  uint64_t* pt_ready = bars + 13; // one arrival per softmax warp
+  uint64_t* dp_full = bars + 14;
+  uint64_t* dp_empty = bars + 15; // one arrival per softmax warp: dP^T read
+  uint64_t* ds_ready = bars + 16; // one arrival per softmax warp
+  uint64_t* acc_done = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / BQ;
@@ -443,14 +432,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&do_full[i], 1);
       mbar_init(&do_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&s_empty[i], 1);
     }
-    mbar_init(pt_ready, 4);
-    mbar_init(pt_free, 1);
+    mbar_init(pt_ready, kBwdSoftmaxWarps);
     mbar_init(dp_full, 1);
-    mbar_init(dp_empty, 4);
-    mbar_init(ds_ready, 4);
-    mbar_init(ds_free, 1);
+    mbar_init(dp_empty, kBwdSoftmaxWarps);
+    mbar_init(ds_ready, kBwdSoftmaxWarps);
     mbar_init(acc_done, 1);
     fence_barrier_init();
   }
@@ -497,7 +484,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       constexpr uint32_t idesc_dv = umma_idesc_f16(128, DV, false, true, true);    // P^T dO
       constexpr uint32_t idesc_dk = umma_idesc_f16(128, DQ, false, true, true);    // dS^T Q
       bool ok = mbar_wait(kv_full, 0, p.status, STATUS_TIMEOUT_TMA_FULL);
-      const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sPT), dsa = smem_u32(sDS);
+      const uint32_t ka = smem_u32(sK), va = smem_u32(sV);
       auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
         const uint32_t u = it >> 1;
@@ -528,23 +515,22 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tc_mma_f16(tdP, umma_desc_sw128(va + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
                      umma_desc_sw128(da + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         tc_commit(dp_full);
-        // dV += P^T dO  (dO read as MN-major: DV contiguous, 64-row sub-tiles)
+        // dV += P^T dO  (P^T from tensor memory; dO read as MN-major: DV contiguous, 64-row sub-tiles)
         if (!mbar_wait(pt_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          tc_mma_f16(tdV, umma_desc_sw128(pa + kk * 32, 16, 1024), umma_desc_sw128(da + kk * 2048, 8192, 1024),
-                     idesc_dv, (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(pt_free);
+          tc_mma_f16_ts(tdV, tS0 + st * 64 + kk * 8, umma_desc_sw128(da + kk * 2048, 8192, 1024), idesc_dv,
+                        (it > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&do_empty[st]);
-        // dK += dS^T Q  (Q read as MN-major)
+        // dK += dS^T Q  (dS^T from tensor memory; Q read as MN-major)
         if (!mbar_wait(ds_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          tc_mma_f16(tdK, umma_desc_sw128(dsa + kk * 32, 16, 1024), umma_desc_sw128(qa + kk * 2048, 8192, 1024),
-                     idesc_dk, (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(ds_free);
+          tc_mma_f16_ts(tdK, tS0 + st * 64 + 32 + kk * 8, umma_desc_sw128(qa + kk * 2048, 8192, 1024), idesc_dk,
+                        (it > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&s_empty[st]);
         tc_commit(&q_empty[st]);
       }
       tc_commit(acc_done);
@@ -552,13 +538,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;   // columns [32 * half, 32 * half + 32) of each tile
     const int r = quarter * 32 + lane;  // kv row
     const int kpos = kpos0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
     for (int it = 0; it < n; ++it) {
       const int i = i_lo + it % nq;
-      const int qpos0 = i * BQ;
+      const int qpos0 = i * BQ + half * 32;
       const int st = it & 1;
       const uint32_t u = it >> 1;
       const uint32_t ph = it & 1;
@@ -566,89 +553,99 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!mbar_wait(&q_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
       if (!mbar_wait(&s_full[st], u & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
       tc_fence_after();
-      float P[BQ];
-      tmem_ld32(tS0 + st * 64 + lane_off, P);
-      tmem_ld32(tS0 + st * 64 + 32 + lane_off, P + 32);
+      float P[32];
+      tmem_ld32(tS0 + st * 64 + half * 32 + lane_off, P);
       tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[st]);
-      const float* lse = sVec + st * 2 * BQ;
+      const float* lse = sVec + st * 2 * BQ + half * 32;
       const float* delta = lse + BQ;
       const bool need_mask = (p.causal && kpos0 + kTile - 1 > qpos0) ||
-                             (p.window > 0 && kpos0 <= qpos0 + BQ - 1 - p.window);
+                             (p.window > 0 && kpos0 <= qpos0 + 31 - p.window);
 #pragma unroll
-      for (int c = 0; c < BQ; ++c) {
-        float v = exp2f(P[c] * p.scale_log2 - lse[c] * kLog2e);
+      for (int c = 0; c < 32; ++c) {
+        float v = fast_exp2(P[c] * p.scale_log2 - lse[c] * kLog2e);
         if (need_mask) {
           const int qp = qpos0 + c;
           if ((p.causal && kpos > qp) || (p.window > 0 && kpos <= qp - p.window)) v = 0.f;
         }
         P[c] = v;
       }
-      // P^T buffer free once dV of the previous tile has read it
-      if (it > 0 && !mbar_wait(pt_free, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-      store_chunk32_sw128(sPT, r, 0, P);
-      store_chunk32_sw128(sPT, r, 1, P + 32);
-      fence_proxy_async_smem();
+      {
+        // P^T (bf16) into the first half of this S^T stage: the A operand of dV += P^T dO
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) pk[c] = pack_bf16x2(P[2 * c], P[2 * c + 1]);
+        tmem_st16_u32(tS0 + st * 64 + half * 16 + lane_off, pk);
+        tc_wait_st();
+      }
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pt_ready);
       if (!mbar_wait(dp_full, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
       tc_fence_after();
-      float d[BQ];
-      tmem_ld32(tdP + lane_off, d);
-      tmem_ld32(tdP + 32 + lane_off, d + 32);
+      float d[32];
+      tmem_ld32(tdP + half * 32 + lane_off, d);
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dp_empty);
+      {
+        // dS^T (bf16) into the second half of this S^T stage: the A operand of dK += dS^T Q
+        uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < BQ; ++c) d[c] = P[c] * (d[c] - delta[c]) * p.scale;
-      if (it > 0 && !mbar_wait(ds_free, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-      store_chunk32_sw128(sDS, r, 0, d);
-      store_chunk32_sw128(sDS, r, 1, d + 32);
-      fence_proxy_async_smem();
+        for (int c = 0; c < 16; ++c)
+          pk[c] = pack_bf16x2(P[2 * c] * (d[2 * c] - delta[2 * c]) * p.scale,
+                              P[2 * c + 1] * (d[2 * c + 1] - delta[2 * c + 1]) * p.scale);
+        tmem_st16_u32(tS0 + st * 64 + 32 + half * 16 + lane_off, pk);
+        tc_wait_st();
+      }
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(ds_ready);
     }
     if (ok && n > 0 && mbar_wait(acc_done, 0, p.status, STATUS_TIMEOUT_TMEM_FULL)) {
       tc_fence_after();
       const long long t = kt0 + r;
-      bf16* dv = p.dv + t * p.dv_row + (long long)hk * p.dv_head;
+      if (half == 0) {
+        bf16* dv = p.dv + t * p.dv_row + (long long)hk * p.dv_head;
 #pragma unroll
-      for (int c = 0; c < DV / 32; ++c) {
-        float v[32];
-        tmem_ld32(tdV + c * 32 + lane_off, v);
-        tc_wait_ld();
-        store_global_row(dv + c * 32, v, 32, 1.f);
-      }
-      bf16* dk = p.dk + t * p.dk_row + (long long)hk * p.dk_head;
-#pragma unroll
-      for (int c = 0; c < NKC * 2; ++c) {
-        float v[32];
-        tmem_ld32(tdK + c * 32 + lane_off, v);
-        tc_wait_ld();
-        store_global_row(dk + c * 32, v, 32, 1.f);
-      }
-      if (ROPE) {
-        bf16* dkr = p.dkr + t * p.dkr_row + (long long)hk * p.dkr_head;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < DV / 32; ++c) {
           float v[32];
-          tmem_ld32(tdK + NKC * 64 + c * 32 + lane_off, v);
+          tmem_ld32(tdV + c * 32 + lane_off, v);
           tc_wait_ld();
-          store_global_row(dkr + c * 32, v, 32, 1.f);
+          store_global_row(dv + c * 32, v, 32, 1.f);
+        }
+      } else {
+        bf16* dk = p.dk + t * p.dk_row + (long long)hk * p.dk_head;
+#pragma unroll
+        for (int c = 0; c < NKC * 2; ++c) {
+          float v[32];
+          tmem_ld32(tdK + c * 32 + lane_off, v);
+          tc_wait_ld();
+          store_global_row(dk + c * 32, v, 32, 1.f);
+        }
+        if (ROPE) {
+          bf16* dkr = p.dkr + t * p.dkr_row + (long long)hk * p.dkr_head;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float v[32];
+            tmem_ld32(tdK + NKC * 64 + c * 32 + lane_off, v);
+            tc_wait_ld();
+            store_global_row(dkr + c * 32, v, 32, 1.f);
+          }
         }
       }
     } else if (n == 0) {
       // no query attends to this kv tile: zero gradients
       const long long t = kt0 + r;
       float z[32] = {0};
-      for (int c = 0; c < DV / 32; ++c) store_global_row(p.dv + t * p.dv_row + (long long)hk * p.dv_head + c * 32, z, 32, 1.f);
-      for (int c = 0; c < NKC * 2; ++c) store_global_row(p.dk + t * p.dk_row + (long long)hk * p.dk_head + c * 32, z, 32, 1.f);
-      if (ROPE)
-        for (int c = 0; c < 2; ++c)
-          store_global_row(p.dkr + t * p.dkr_row + (long long)hk * p.dkr_head + c * 32, z, 32, 1.f);
+      if (half == 0) {
+        for (int c = 0; c < DV / 32; ++c) store_global_row(p.dv + t * p.dv_row + (long long)hk * p.dv_head + c * 32, z, 32, 1.f);
+      } else {
+        for (int c = 0; c < NKC * 2; ++c) store_global_row(p.dk + t * p.dk_row + (long long)hk * p.dk_head + c * 32, z, 32, 1.f);
+        if (ROPE)
+          for (int c = 0; c < 2; ++c)
+            store_global_row(p.dkr + t * p.dkr_row + (long long)hk * p.dkr_head + c * 32, z, 32, 1.f);
+      }
     }
   }
   __syncwarp();
@@ -675,18 +672,18 @@ struct DqSmem {
   static constexpr int kOffDO = kOffQ + kQ;
   static constexpr int kOffK = kOffDO + kDO;         // 2 stages
   static constexpr int kOffV = kOffK + 2 * kK;       // 2 stages
-  static constexpr int kOffS = kOffV + 2 * kV;       // 2 stages of dS [128 q x 64 kv] bf16
-  static constexpr int kOffBar = kOffS + 2 * kSubTile;
+  static constexpr int kOffBar = kOffV + 2 * kV;
   static constexpr int kBytes = kOffBar + 256 + 1024;
 };
 
 // CTA = (query tile of 128 rows, head, sequence); loops over key tiles of 64 rows.
-// K/V tiles, the S / dP accumulators (TMEM) and dS (shared memory) are all double
-// buffered: the next tile's loads and S = Q K^T, dP = dO V^T run while this
-// tile's dS is formed, and dQ += dS K of this tile follows.
-//   TMEM columns: S[2] = [0, 128), dP[2] = [128, 256), dQ = [256, 256 + DQ)
+// K/V tiles and the S / dP accumulators (TMEM) are double buffered: the next
+// tile's loads and S = Q K^T, dP = dO V^T run while this tile's dS is formed,
+// and dQ += dS K of this tile follows.  dS (bf16) is written over its dP stage
+// and read by the MMA from tensor memory (thread = query row = A-operand row).
+//   TMEM columns: S[2] = [0, 128), dP / dS [2] = [128, 256), dQ = [256, 256 + DQ)
 template <int DQ, int DV, bool ROPE>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmKR, const __grid_constant__ CUtensorMap tmV,
                    const __grid_constant__ CUtensorMap tmDO, AttnArgs p) {
@@ -701,17 +698,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sDO = smem + L::kOffDO;
   uint8_t* sK = smem + L::kOffK;
   uint8_t* sV = smem + L::kOffV;
-  uint8_t* sS = smem + L::kOffS;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;    // [2]
   uint64_t* kv_empty = bars + 3;   // [2]
   uint64_t* sdp_full = bars + 5;   // [2]
-  uint64_t* sdp_empty = bars + 7;  // [2] count 4
-  uint64_t* ds_ready = bars + 9;   // [2] count 4, per dS stage
-  uint64_t* ds_free = bars + 11;   // [2]
-  uint64_t* acc_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* sdp_empty = bars + 7;  // [2] S / dP(dS) stage free (commit after dQ read dS)
+  uint64_t* ds_ready = bars + 9;   // [2] one arrival per softmax warp, per dS stage
+  uint64_t* acc_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / kTile;
@@ -731,9 +726,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&sdp_full[i], 1);
-      mbar_init(&sdp_empty[i], 4);
-      mbar_init(&ds_free[i], 1);
-      mbar_init(&ds_ready[i], 4);
+      mbar_init(&sdp_empty[i], 1);
+      mbar_init(&ds_ready[i], kBwdSoftmaxWarps);
     }
     mbar_init(acc_done, 1);
     fence_barrier_init();
@@ -800,20 +794,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (jj + 1 < n && !issue_sdp(jj + 1)) { ok = false; break; }
         if (!mbar_wait(&ds_ready[st], (jj >> 1) & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
-        // dQ += dS K   (K tile read as MN-major: d contiguous, 64-row sub-tiles)
-        const uint32_t sa = smem_u32(sS + st * kSubTile), ka = smem_u32(sK + st * L::kK);
+        // dQ += dS K   (dS from tensor memory; K tile read as MN-major: d contiguous, 64-row sub-tiles)
+        const uint32_t ka = smem_u32(sK + st * L::kK);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
-          tc_mma_f16(tdQ, umma_desc_sw128(sa + kk * 32, 16, 1024), umma_desc_sw128(ka + kk * 2048, 8192, 1024),
-                     idesc_dq, (jj > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16_ts(tdQ, tdP0 + st * 64 + kk * 8, umma_desc_sw128(ka + kk * 2048, 8192, 1024), idesc_dq,
+                        (jj > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&kv_empty[st]);
-        tc_commit(&ds_free[st]);
+        tc_commit(&sdp_empty[st]);
       }
       tc_commit(acc_done);
       mbar_wait(acc_done, 0, p.status, STATUS_TIMEOUT_DRAIN);
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;   // key columns [32 * half, 32 * half + 32) of each tile
     const int r = quarter * 32 + lane;
     const int qpos = qpos0 + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -824,42 +819,42 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int jj = 0; jj < n; ++jj) {
       const int st = jj & 1;
       const uint32_t u = jj >> 1;
-      const int kpos0 = (j_lo + jj) * BK;
+      const int kpos0 = (j_lo + jj) * BK + half * 32;
       if (!mbar_wait(&sdp_full[st], u & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
       tc_fence_after();
-      float sv[BK], d[BK];
-      tmem_ld32(tS0 + st * 64 + lane_off, sv);
-      tmem_ld32(tS0 + st * 64 + 32 + lane_off, sv + 32);
-      tmem_ld32(tdP0 + st * 64 + lane_off, d);
-      tmem_ld32(tdP0 + st * 64 + 32 + lane_off, d + 32);
+      float sv[32], d[32];
+      tmem_ld32(tS0 + st * 64 + half * 32 + lane_off, sv);
+      tmem_ld32(tdP0 + st * 64 + half * 32 + lane_off, d);
       tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sdp_empty[st]);
-      const bool need_mask = (p.causal && kpos0 + BK - 1 > qpos0) ||
+      const bool need_mask = (p.causal && kpos0 + 31 > qpos0) ||
                              (p.window > 0 && kpos0 <= qpos0 + kTile - 1 - p.window);
 #pragma unroll
-      for (int k = 0; k < BK; ++k) {
-        float pv = exp2f(sv[k] * p.scale_log2 - lse2);
+      for (int k = 0; k < 32; ++k) {
+        float pv = fast_exp2(sv[k] * p.scale_log2 - lse2);
         if (need_mask) {
           const int kp = kpos0 + k;
           if ((p.causal && kp > qpos) || (p.window > 0 && kp <= qpos - p.window)) pv = 0.f;
         }
         d[k] = pv * (d[k] - dlt) * p.scale;
       }
-      // this dS buffer was last read by dQ two tiles ago
-      if (jj >= 2 && !mbar_wait(&ds_free[st], ((u - 1) & 1), p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-      store_chunk32_sw128(sS + st * kSubTile, r, 0, d);
-      store_chunk32_sw128(sS + st * kSubTile, r, 1, d + 32);
-      fence_proxy_async_smem();
+      {
+        // dS (bf16) into this dP stage (first 32 columns): the A operand of dQ += dS K
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) pk[c] = pack_bf16x2(d[2 * c], d[2 * c + 1]);
+        tmem_st16_u32(tdP0 + st * 64 + half * 16 + lane_off, pk);
+        tc_wait_st();
+      }
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_ready[st]);
     }
     if (ok && n > 0 && mbar_wait(acc_done, 0, p.status, STATUS_TIMEOUT_TMEM_FULL)) {
       tc_fence_after();
       bf16* dst = p.dq + (long long)(t0 + r) * p.dq_row + (long long)h * p.dq_head;
+      constexpr int CH = DQ / 64;  // 32-column chunks per half
 #pragma unroll
-      for (int c = 0; c < DQ / 32; ++c) {
+      for (int c = half * CH; c < (half + 1) * CH; ++c) {
         float v[32];
         tmem_ld32(tdQ + c * 32 + lane_off, v);
         tc_wait_ld();
@@ -982,7 +977,7 @@ static void bwd_impl(const AttnTensors& a, const void* o, const float* lse, cons
     auto kern = attn_dkdv_kernel<DQ, DV, ROPE>;
     set_smem(kern, L::kBytes);
     dim3 grid(a.S / kTile, a.Hk, a.T / a.S);
-    kern<<<grid, kAttnThreads, L::kBytes, s>>>(tq64, tk, tkr, tv, tdo64, p);
+    kern<<<grid, kBwdThreads, L::kBytes, s>>>(tq64, tk, tkr, tv, tdo64, p);
   }
   {
     using L = DqSmem<DQ, DV>;
@@ -992,7 +987,7 @@ static void bwd_impl(const AttnTensors& a, const void* o, const float* lse, cons
     auto kern = attn_dq_kernel<DQ, DV, ROPE>;
     set_smem(kern, L::kBytes);
     dim3 grid(a.S / kTile, a.H, a.T / a.S);
-    kern<<<grid, kAttnThreads, L::kBytes, s>>>(tq, tk64, tkr64, tv64, tdo, p);
+    kern<<<grid, kBwdThreads, L::kBytes, s>>>(tq, tk64, tkr64, tv64, tdo, p);
   }
 }
 
