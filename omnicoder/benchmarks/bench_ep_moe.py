@@ -13,6 +13,10 @@ with CUDA events (max over ranks) around forward + backward of one layer;
 inputs (>= 67 MB) and expert weights exceed L2 only together, so L2 is
 flushed before every timed iteration.
 
+Transports: p2p (fused NVLink exchange, bf16 expert GEMMs), p2p_fp8 (the same
+exchange with block-scaled fp8 forward expert GEMMs: 1 x 128 activation and
+128 x 128 weight scales; backward with the bf16 weights), nccl (baseline).
+
 Roofline of the fused path per rank: the slower of (expert GEMM FLOPs of
 forward + backward at the measured sustained bf16 peak) and (bytes that must
 cross NVLink at 770 GB/s per direction: dispatch rows, combine rows, their
@@ -41,7 +45,8 @@ def main(argv=None):
     ap.add_argument("--cf", type=float, default=1.25)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--transports", default="p2p,nccl")
+    ap.add_argument("--transports", default="p2p,p2p_fp8,nccl",
+                    help="p2p (bf16 expert GEMMs), p2p_fp8 (block-scaled fp8 forward expert GEMMs), nccl")
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -66,7 +71,11 @@ def main(argv=None):
     rows = int(T * k * a.cf * 1.1) + E * 128
     results = {}
     for tr in a.transports.split(","):
-        ep = EPContext(dist.group.WORLD, transport=tr, device=dev, arena_bytes=rows * (4 * D * 2 + 16))
+        fp8 = tr == "p2p_fp8"
+        ep = EPContext(dist.group.WORLD, transport="p2p" if fp8 else tr, device=dev,
+                       arena_bytes=rows * (4 * D * 2 + 16))
+        if fp8:
+            ep.set_fp8_weights(w13, w2)   # once per optimiser step in training; outside the timed region
 
         def step():
             ep.begin_step()

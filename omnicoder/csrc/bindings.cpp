@@ -247,6 +247,84 @@ void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---------------------------------------------------------------------------
+// Block-scaled fp8 (1 x 128 activation scales, 128 x 128 weight scales)
+// ---------------------------------------------------------------------------
+std::vector<at::Tensor> fp8_quant_act_t(const at::Tensor& x) {
+  CHECK_CUDA_T(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  TORCH_CHECK(x.dim() == 2 && x.size(1) % 128 == 0, "fp8_quant_act: x [M, K] with K % 128 == 0");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t M = x.size(0), K = x.size(1), Mp = (M + 127) / 128 * 128;
+  auto xq = at::empty({M, K}, x.options().dtype(at::kFloat8_e4m3fn));
+  auto sx = at::empty({K / 128, Mp}, x.options().dtype(at::kFloat));
+  fp8_quant_act(x.data_ptr(), x.stride(0), (int)M, (int)K, xq.data_ptr(), sx.data_ptr<float>(), Mp, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {xq, sx};
+}
+
+std::vector<at::Tensor> fp8_quant_weight_t(const at::Tensor& w) {
+  CHECK_CUDA_T(w);
+  CHECK_BF16(w);
+  TORCH_CHECK(w.is_contiguous() && (w.dim() == 2 || w.dim() == 3), "fp8_quant_weight: contiguous [N, K] or [G, N, K]");
+  const c10::cuda::CUDAGuard guard(w.device());
+  const int64_t G = w.dim() == 3 ? w.size(0) : 1, N = w.size(-2), K = w.size(-1);
+  TORCH_CHECK(K % 128 == 0, "fp8_quant_weight: K % 128 == 0");
+  auto wq = at::empty_like(w, w.options().dtype(at::kFloat8_e4m3fn));
+  auto sw = at::empty({G, (N + 127) / 128, K / 128}, w.options().dtype(at::kFloat));
+  fp8_quant_weight(w.data_ptr(), (int)G, (int)N, (int)K, wq.data_ptr(), sw.data_ptr<float>(), cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {wq, sw};
+}
+
+// C [M, N] bf16 = fp8 GEMM; grouped when offsets is given (wq [G, N, K], offsets int32 [G+1],
+// multiples of 128, rows = allocated rows of xq).
+void fp8_gemm_t(const at::Tensor& xq, const at::Tensor& sx, const at::Tensor& wq, const at::Tensor& sw, at::Tensor& C,
+                const c10::optional<at::Tensor>& offsets, int64_t max_rows) {
+  CHECK_CUDA_T(xq);
+  TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn,
+              "fp8_gemm: e4m3 operands");
+  TORCH_CHECK(sx.scalar_type() == at::kFloat && sw.scalar_type() == at::kFloat && sx.is_contiguous() &&
+                  sw.is_contiguous(), "fp8_gemm: fp32 contiguous scales");
+  CHECK_BF16(C);
+  CHECK_ROWMAJOR(C);
+  CHECK_ROWMAJOR(xq);
+  TORCH_CHECK(wq.is_contiguous(), "fp8_gemm: contiguous weights");
+  const c10::cuda::CUDAGuard guard(xq.device());
+  Fp8GemmDesc d;
+  d.M = (int)xq.size(0);
+  d.K = (int)xq.size(1);
+  d.N = (int)wq.size(-2);
+  TORCH_CHECK(wq.size(-1) == d.K && d.K % 128 == 0, "fp8_gemm: K mismatch or K % 128 != 0");
+  TORCH_CHECK(sx.dim() == 2 && sx.size(0) == d.K / 128 && sx.size(1) >= (d.M + 127) / 128 * 128,
+              "fp8_gemm: sx [K/128, >= M rounded up to 128]");
+  TORCH_CHECK(C.size(0) == d.M && C.size(1) == d.N && C.stride(0) % 8 == 0, "fp8_gemm: C [M, N], row stride % 8");
+  d.X = xq.data_ptr();
+  d.ldx = xq.stride(0);
+  d.sx = sx.data_ptr<float>();
+  d.ldsx = sx.size(1);
+  d.W = wq.data_ptr();
+  d.ldw = d.K;
+  d.sw = sw.data_ptr<float>();
+  d.C = C.data_ptr();
+  d.ldc = C.stride(0);
+  if (offsets.has_value()) {
+    TORCH_CHECK(wq.dim() == 3 && offsets->scalar_type() == at::kInt && offsets->numel() == wq.size(0) + 1,
+                "fp8_gemm: grouped needs wq [G, N, K] and int32 offsets [G+1]");
+    d.G = (int)wq.size(0);
+    d.offsets = offsets->data_ptr<int>();
+    d.w_group_stride = (long long)d.N * d.K;
+    d.max_rows_hint = (int)max_rows;
+    TORCH_CHECK(sw.numel() == (long long)d.G * ((d.N + 127) / 128) * (d.K / 128), "fp8_gemm: sw shape");
+  } else {
+    TORCH_CHECK(sw.numel() == (long long)((d.N + 127) / 128) * (d.K / 128), "fp8_gemm: sw shape");
+  }
+  d.status = status_ptr();
+  fp8_gemm_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Grouped-K: C[g] (M x N) = alpha * A[rows_g]^T B[rows_g] with A [rows, M], B [rows, N].
 void gemm_grouped_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor& C,
                     int64_t epilogue, double alpha, int64_t block_n) {
@@ -299,6 +377,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &omni::gemm, "tcgen05 GEMM", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
         py::arg("H") = py::none(), py::arg("block_n") = 256);
+  m.def("fp8_quant_act", &omni::fp8_quant_act_t, "bf16 [M, K] -> (e4m3 [M, K], fp32 scales [K/128, M padded to 128])");
+  m.def("fp8_quant_weight", &omni::fp8_quant_weight_t, "bf16 [(G,) N, K] -> (e4m3, fp32 scales [G, N/128, K/128])");
+  m.def("fp8_gemm", &omni::fp8_gemm_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"), py::arg("C"),
+        py::arg("offsets") = py::none(), py::arg("max_rows") = 0);
   m.def("gemm_skinny_grouped", &omni::gemm_skinny_grouped, py::arg("A"), py::arg("B"), py::arg("offsets"),
         py::arg("C"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("rows") = 0);
   m.def("set_skinny_rows", &omni::set_skinny_rows, "rows up to which dense GEMMs use the few-row kernel (0: off)");

@@ -495,8 +495,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // rank-2 or rank-3 bf16 tensor map with 128-byte swizzle.  dims[0] is the
 // contiguous dimension; strides are in bytes for dims 1.. .
+static CUtensorMap make_tmap_sw128(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                                   const uint64_t* strides_bytes, const uint32_t* box);
+
 CUtensorMap make_tmap_bf16_sw128(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                                  const uint32_t* box) {
+  return make_tmap_sw128(base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, dims, strides_bytes, box);
+}
+
+CUtensorMap make_tmap_u8_sw128(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                               const uint32_t* box) {
+  return make_tmap_sw128(base, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, dims, strides_bytes, box);
+}
+
+static CUtensorMap make_tmap_sw128(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                                   const uint64_t* strides_bytes, const uint32_t* box) {
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
     throw std::runtime_error("omnicoder gemm: operand base address must be 16-byte aligned");
   for (int i = 0; i + 1 < rank; ++i)
@@ -510,7 +523,7 @@ CUtensorMap make_tmap_bf16_sw128(const void* base, int rank, const uint64_t* dim
     b[i] = box[i];
   }
   for (int i = 0; i + 1 < rank; ++i) s[i] = strides_bytes[i];
-  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s, b, es,
+  CUresult r = encode_fn()(&m, dtype, rank, const_cast<void*>(base), d, s, b, es,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("omnicoder gemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");

@@ -56,7 +56,38 @@ void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream);
 // byte strides for dims 1..).  Throws on misaligned bases or strides.
 CUtensorMap make_tmap_bf16_sw128(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
                                  const uint32_t* box);
+// Same for byte-sized elements (fp8 operands).
+CUtensorMap make_tmap_u8_sw128(const void* base, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+                               const uint32_t* box);
 int num_sms();
+
+// ---- block-scaled fp8 GEMM (gemm_fp8.cu) ----------------------------------------
+// C[M, N] (bf16) = sum over 128-wide K blocks kb of (Xq[M, kb] . Wq[N, kb]^T) * sx[kb][m] * sw[g][n / 128][kb]
+// Xq, Wq: e4m3, K-major ([rows, K] row-major, K % 128 == 0).  sx: fp32 [K/128][ldsx] (ldsx >= M rounded
+// up to 128; one scale per row and 128-column block).  sw: fp32 [G][ceil(N/128)][K/128] (one scale per
+// 128 x 128 weight block).  Grouped-M: group g owns rows [offsets[g], offsets[g+1]) of X (multiples of
+// 128, device array) and weight Wq[g] ([G, N, K]).
+struct Fp8GemmDesc {
+  int M = 0, N = 0, K = 0, G = 1;
+  const int* offsets = nullptr;  // grouped-M when non-null
+  int max_rows_hint = 0;
+  const void* X = nullptr;
+  long long ldx = 0;
+  const float* sx = nullptr;
+  long long ldsx = 0;
+  const void* W = nullptr;
+  long long ldw = 0;
+  long long w_group_stride = 0;
+  const float* sw = nullptr;
+  void* C = nullptr;
+  long long ldc = 0;
+  void* status = nullptr;
+};
+void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream);
+// x [M, K] bf16 -> xq e4m3 [M, K], sx fp32 [K/128][ldsx] (rows >= M zero-filled up to ldsx)
+void fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sx, long long ldsx, cudaStream_t s);
+// w [G, N, K] bf16 -> wq e4m3, sw fp32 [G][ceil(N/128)][K/128]
+void fp8_quant_weight(const void* w, int G, int N, int K, void* wq, float* sw, cudaStream_t s);
 
 // ---- few-row GEMM (decode, speculative verification) --------------------------
 // Y[rows, N] = X[rows, K] W[N, K]^T for at most kSkinnyMaxRows rows per group

@@ -99,6 +99,16 @@ class EPContext:
         self.arena = None
         self._arena_bytes = arena_bytes
         self.stats = {"host_syncs": 0}
+        # id(bf16 expert weight) -> (e4m3 weight, fp32 128x128 block scales): when both expert
+        # weights of a layer are present, its forward expert GEMMs run in block-scaled fp8
+        self.fp8_weights: dict = {}
+
+    def set_fp8_weights(self, *weights):
+        """Quantise the given expert weight stacks ([El, N, K] bf16) for the fp8 forward path
+        (call again after every optimiser step)."""
+        from ..ops.fp8 import quantize_weight
+        for w in weights:
+            self.fp8_weights[id(w)] = quantize_weight(w.detach())
 
     def experts_of(self, E: int) -> tuple[int, int]:
         if E % self.world:
@@ -168,12 +178,24 @@ class _EPMoEP2P(torch.autograd.Function):
         meta = rmeta.view(torch.int32, R, 4)
         C.ep_pad_rows(x_recv, meta, offs_local, kept_local)
         arena.barrier()                                       # all pairs have landed
-        act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)
-        H = torch.empty(R, F2, device=x.device, dtype=torch.bfloat16)
-        C.gemm_grouped_m(x_recv, w13, offs_local, act, False, EPI_SWIGLU, 1.0, None, H, 256, R)
         ry = arena.alloc([r * D * 2 for r in rows])
         y_recv = ry.view(torch.bfloat16, R, D)
-        C.gemm_grouped_m(act, w2, offs_local, y_recv, False, EPI_BF16, 1.0, None, None, 256, R)
+        q13 = ep.fp8_weights.get(id(w13)) if ep.fp8_weights else None
+        q2 = ep.fp8_weights.get(id(w2)) if ep.fp8_weights else None
+        if q13 is not None and q2 is not None:
+            # block-scaled fp8 expert GEMMs (weights quantised once per optimiser step by the
+            # caller; activations per 1 x 128 block here); backward uses the bf16 weights
+            from ..ops.fp8 import fp8_grouped_mm, quantize_act
+            H = fp8_grouped_mm(x_recv, q13[0], q13[1], offs_local, R)
+            g, u = deinterleave_cols(H)
+            act = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
+            aq, sa = quantize_act(act)
+            C.fp8_gemm(aq, sa, q2[0], q2[1].reshape(-1), y_recv, offs_local, R)
+        else:
+            act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)
+            H = torch.empty(R, F2, device=x.device, dtype=torch.bfloat16)
+            C.gemm_grouped_m(x_recv, w13, offs_local, act, False, EPI_SWIGLU, 1.0, None, H, 256, R)
+            C.gemm_grouped_m(act, w2, offs_local, y_recv, False, EPI_BF16, 1.0, None, None, 256, R)
         arena.barrier()                                       # every owner's outputs are ready
         out = C.ep_combine(slot, idx, wts, ry.ptrs, rows, El, D, None if add is None else add.contiguous())
         ctx.save_for_backward(x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, offs_local, kept_local,

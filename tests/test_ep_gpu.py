@@ -88,6 +88,18 @@ def _layer_worker(rank, world, port, q):
                     "dw13": _close(b13.grad, a13.grad[lo:hi], 3e-2),
                     "dw2": _close(b2.grad, a2.grad[lo:hi], 3e-2),
                 }
+            if cap == 0:
+                # block-scaled fp8 forward expert GEMMs: output within fp8 precision of bf16
+                ep = EPContext(dist.group.WORLD, transport="p2p", device=dev, arena_bytes=64 << 20)
+                b13, b2 = w13[lo:hi].contiguous(), w2[lo:hi].contiguous()
+                ep.set_fp8_weights(b13, b2)
+                ep.begin_step()
+                with torch.no_grad():
+                    yq, _ = ep_moe_ffn(xs[rank * T:(rank + 1) * T], wr, b13, b2, K, ep, capacity=0, renorm=True)
+                torch.cuda.synchronize()
+                code = C.status()[0]
+                C.status_reset()
+                out[("fp8", "p2p")] = {"status": code, "y": _close(yq, ya[rank * T:(rank + 1) * T], 8e-2)}
         q.put((rank, out))
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e)))
