@@ -325,6 +325,123 @@ void fp8_gemm_t(const at::Tensor& xq, const at::Tensor& sx, const at::Tensor& wq
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel fused collectives over peer memory
+// ---------------------------------------------------------------------------
+// C [nsrc * src_rows, N] = gather_r(A_r) . B^T: rank r's row block A_r ([src_rows, K] bf16, row stride of
+// a_local) is read straight from its buffer (peer_a[r], mapped in this process) by the GEMM's loads.
+void gemm_ag(const at::Tensor& a_local, const std::vector<int64_t>& peer_a, int64_t me, const at::Tensor& B,
+             at::Tensor& C, bool b_mn, int64_t epilogue, double alpha, const c10::optional<at::Tensor>& H,
+             int64_t block_n) {
+  CHECK_BF16(a_local);
+  CHECK_BF16(B);
+  CHECK_BF16(C);
+  CHECK_ROWMAJOR(a_local);
+  CHECK_ROWMAJOR(B);
+  CHECK_ROWMAJOR(C);
+  const int64_t nsrc = (int64_t)peer_a.size(), src_rows = a_local.size(0), K = a_local.size(1);
+  TORCH_CHECK(nsrc >= 1 && nsrc <= GEMM_MAX_PEERS && me >= 0 && me < nsrc, "gemm_ag: ranks");
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  TORCH_CHECK((b_mn ? B.size(0) : B.size(1)) == K, "gemm_ag: reduction dims differ");
+  TORCH_CHECK(C.size(0) == nsrc * src_rows && C.size(1) == (epilogue == EPI_SWIGLU ? N / 2 : N), "gemm_ag: C shape");
+  const c10::cuda::CUDAGuard guard(a_local.device());
+  GemmDesc d;
+  d.mode = GEMM_AG;
+  d.epilogue = (int)epilogue;
+  d.block_n = (int)block_n;
+  d.b_mn_major = b_mn;
+  d.M = (int)(nsrc * src_rows);
+  d.N = (int)N;
+  d.K = (int)K;
+  d.lda = a_local.stride(0);
+  d.K_extent_a = K;
+  d.rows_a = src_rows;
+  d.B = B.data_ptr();
+  d.ldb = B.stride(0);
+  d.K_extent_b = K;
+  d.C = C.data_ptr();
+  d.ldc = C.stride(0);
+  d.alpha = (float)alpha;
+  d.nsrc = (int)nsrc;
+  d.me = (int)me;
+  d.src_rows = (int)src_rows;
+  for (int r = 0; r < nsrc; ++r) d.peer_a[r] = reinterpret_cast<const void*>(peer_a[r]);
+  if (epilogue == EPI_SWIGLU && H.has_value()) {
+    CHECK_BF16(H.value());
+    TORCH_CHECK(H->size(0) == d.M && H->size(1) == N, "gemm_ag swiglu: H shape");
+    d.H = H->data_ptr();
+    d.ldh = H->stride(0);
+  }
+  d.status = status_ptr();
+  gemm_sm100_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Partial products A . B^T (A [nsrc * src_rows, K]) stored tile by tile into the row owners' staging
+// buffers: rows of rank r go to peer_c[r] + (me * src_rows + local row) * ldc (bf16).
+void gemm_rs(const at::Tensor& A, const at::Tensor& B, const std::vector<int64_t>& peer_c, int64_t src_rows,
+             int64_t ldc, int64_t me, bool b_mn, int64_t block_n) {
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_ROWMAJOR(A);
+  CHECK_ROWMAJOR(B);
+  const int64_t nsrc = (int64_t)peer_c.size(), M = A.size(0), K = A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  TORCH_CHECK(nsrc >= 1 && nsrc <= GEMM_MAX_PEERS && M == nsrc * src_rows && me >= 0 && me < nsrc, "gemm_rs: rows");
+  TORCH_CHECK((b_mn ? B.size(0) : B.size(1)) == K && ldc >= N && ldc % 8 == 0, "gemm_rs: dims");
+  const c10::cuda::CUDAGuard guard(A.device());
+  GemmDesc d;
+  d.mode = GEMM_DENSE;
+  d.epilogue = EPI_PEER_BF16;
+  d.block_n = (int)block_n;
+  d.b_mn_major = b_mn;
+  d.M = (int)M;
+  d.N = (int)N;
+  d.K = (int)K;
+  d.A = A.data_ptr();
+  d.lda = A.stride(0);
+  d.rows_a = M;
+  d.K_extent_a = K;
+  d.B = B.data_ptr();
+  d.ldb = B.stride(0);
+  d.K_extent_b = K;
+  d.ldc = ldc;
+  d.nsrc = (int)nsrc;
+  d.me = (int)me;
+  d.src_rows = (int)src_rows;
+  for (int r = 0; r < nsrc; ++r) d.peer_c[r] = reinterpret_cast<void*>(peer_c[r]);
+  d.status = status_ptr();
+  gemm_sm100_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// dst (contiguous bytes) <- nbytes at device address src (a peer's buffer mapped in this process), on the
+// current stream (copy engine over NVLink).
+void peer_copy(at::Tensor& dst, int64_t src, int64_t nbytes) {
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous() && dst.numel() * dst.element_size() >= nbytes, "peer_copy: dst");
+  const c10::cuda::CUDAGuard guard(dst.device());
+  C10_CUDA_CHECK(cudaMemcpyAsync(dst.data_ptr(), reinterpret_cast<const void*>(src), (size_t)nbytes,
+                                 cudaMemcpyDeviceToDevice, cur_stream()));
+}
+
+void tp_reduce(const at::Tensor& staging, at::Tensor& out, const c10::optional<at::Tensor>& residual) {
+  CHECK_BF16(staging);
+  CHECK_BF16(out);
+  TORCH_CHECK(staging.dim() == 3 && staging.stride(-1) == 1, "tp_reduce: staging [nsrc, rows, D]");
+  const int64_t nsrc = staging.size(0), rows = staging.size(1), D = staging.size(2);
+  TORCH_CHECK(staging.stride(0) == rows * staging.stride(1), "tp_reduce: slots must be packed");
+  TORCH_CHECK(out.size(0) == rows && out.size(1) == D && out.stride(-1) == 1, "tp_reduce: out [rows, D]");
+  if (residual.has_value()) {
+    CHECK_BF16(residual.value());
+    TORCH_CHECK(residual->size(0) == rows && residual->size(1) == D && residual->stride(-1) == 1, "tp_reduce: residual");
+  }
+  const c10::cuda::CUDAGuard guard(staging.device());
+  tp_reduce_slots(staging.data_ptr(), (int)nsrc, (int)rows, (int)D, staging.stride(1),
+                  residual.has_value() ? residual->data_ptr() : nullptr, residual.has_value() ? residual->stride(0) : 0,
+                  out.data_ptr(), out.stride(0), cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Grouped-K: C[g] (M x N) = alpha * A[rows_g]^T B[rows_g] with A [rows, M], B [rows, N].
 void gemm_grouped_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor& C,
                     int64_t epilogue, double alpha, int64_t block_n) {
@@ -377,6 +494,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &omni::gemm, "tcgen05 GEMM", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn"),
         py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
         py::arg("H") = py::none(), py::arg("block_n") = 256);
+  m.def("gemm_ag", &omni::gemm_ag, py::arg("a_local"), py::arg("peer_a"), py::arg("me"), py::arg("B"), py::arg("C"),
+        py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("H") = py::none(),
+        py::arg("block_n") = 256);
+  m.def("gemm_rs", &omni::gemm_rs, py::arg("A"), py::arg("B"), py::arg("peer_c"), py::arg("src_rows"), py::arg("ldc"),
+        py::arg("me"), py::arg("b_mn"), py::arg("block_n") = 256);
+  m.def("peer_copy", &omni::peer_copy, py::arg("dst"), py::arg("src"), py::arg("nbytes"));
+  m.def("tp_reduce", &omni::tp_reduce, py::arg("staging"), py::arg("out"), py::arg("residual") = py::none());
   m.def("fp8_quant_act", &omni::fp8_quant_act_t, "bf16 [M, K] -> (e4m3 [M, K], fp32 scales [K/128, M padded to 128])");
   m.def("fp8_quant_weight", &omni::fp8_quant_weight_t, "bf16 [(G,) N, K] -> (e4m3, fp32 scales [G, N/128, K/128])");
   m.def("fp8_gemm", &omni::fp8_gemm_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"), py::arg("C"),

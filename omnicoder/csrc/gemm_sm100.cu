@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstring>
 #include <stdexcept>
 #include <string>
 
@@ -59,6 +60,14 @@ struct GemmArgs {
   long long ldh;
   float alpha;
   StatusBlock* status;
+  int nsrc, me, src_rows;
+  int mt_rot;                      // dense raster: rotate the M tiles so a rank starts on its own rows
+  void* peer_c[GEMM_MAX_PEERS];
+};
+
+// Per-source tensor maps of A (GEMM_AG mode; unused otherwise).
+struct AgMaps {
+  CUtensorMap m[GEMM_MAX_PEERS];
 };
 
 template <int BN>
@@ -79,7 +88,7 @@ struct TileInfo {
 template <int BN, int MODE>
 __device__ __forceinline__ int total_tiles(const GemmArgs& p, const int* s_off) {
   const int num_n = (p.N + BN - 1) / BN;
-  if (MODE == GEMM_DENSE) return ((p.M + kBM - 1) / kBM) * num_n;
+  if (MODE == GEMM_DENSE || MODE == GEMM_AG) return ((p.M + kBM - 1) / kBM) * num_n;
   if (MODE == GEMM_GROUPED_M) return (s_off[p.num_groups] / kBM) * num_n;
   return p.num_groups * ((p.M + kBM - 1) / kBM) * num_n;
 }
@@ -88,7 +97,7 @@ template <int BN, int MODE>
 __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, int t, const int* s_off) {
   TileInfo ti;
   const int num_n = (p.N + BN - 1) / BN;
-  if (MODE == GEMM_DENSE) {
+  if (MODE == GEMM_DENSE || MODE == GEMM_AG) {
     // Grouped raster: 8 M-tiles share each sweep over N for L2 reuse of B.
     const int num_m = (p.M + kBM - 1) / kBM;
     constexpr int GM = 8;
@@ -97,7 +106,7 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, int t, const in
     const int first_m = grp * GM;
     const int gsize = min(num_m - first_m, GM);
     const int r = t - grp * per_group;
-    ti.m0 = (first_m + r % gsize) * kBM;
+    ti.m0 = ((first_m + r % gsize + p.mt_rot) % num_m) * kBM;
     ti.n0 = (r / gsize) * BN;
     ti.g = 0;
     ti.k0 = 0;
@@ -172,6 +181,24 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& p, int row, int col,
       }
     } else {
       for (int j = 0; j < ncols; ++j) C[j] = __float2bfloat16(o[j]);
+    }
+  } else if (EPI == EPI_PEER_BF16) {
+    // partial sums of a row owned by rank `owner` go to slot `me` of that rank's staging buffer
+    const int owner = row / p.src_rows;
+    __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.peer_c[owner]) +
+                       ((long long)p.me * p.src_rows + (row - owner * p.src_rows)) * p.ldc + col;
+    if (ncols == 32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(v[q * 8 + 0] * p.alpha, v[q * 8 + 1] * p.alpha);
+        w.y = pack_bf16x2(v[q * 8 + 2] * p.alpha, v[q * 8 + 3] * p.alpha);
+        w.z = pack_bf16x2(v[q * 8 + 4] * p.alpha, v[q * 8 + 5] * p.alpha);
+        w.w = pack_bf16x2(v[q * 8 + 6] * p.alpha, v[q * 8 + 7] * p.alpha);
+        *reinterpret_cast<uint4*>(C + q * 8) = w;
+      }
+    } else {
+      for (int j = 0; j < ncols; ++j) C[j] = __float2bfloat16(v[j] * p.alpha);
     }
   } else if (EPI == EPI_STORE_F32 || EPI == EPI_ACCUM_F32) {
     float* C = reinterpret_cast<float*>(p.C) + (long long)g * p.c_group_stride + (long long)row * p.ldc + col;
@@ -283,7 +310,7 @@ __device__ __forceinline__ void store_swiglu_bwd(const GemmArgs& p, int row, int
 template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      GemmArgs p) {
+                      const __grid_constant__ AgMaps ag, GemmArgs p) {
   using C_ = Cfg<BN>;
   constexpr int S = C_::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -315,7 +342,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
+    if (MODE == GEMM_AG) {
+      for (int r = 0; r < p.nsrc; ++r) tma_prefetch_desc(&ag.m[r]);
+    } else {
+      tma_prefetch_desc(&tmA);
+    }
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
@@ -345,7 +376,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sB = sA + C_::kStageA;
           mbar_arrive_expect_tx(&full_bar[stage], C_::kStageBytes);
           const int k = ti.k0 + kb * kBK;
-          if (!A_MN) {
+          if (MODE == GEMM_AG) {
+            // rows of source rank `src`, read from its buffer (over NVLink for a peer)
+            const int src = ti.m0 / p.src_rows;
+            tma_load_2d(sA, &ag.m[src], &full_bar[stage], k, ti.m0 - src * p.src_rows);
+          } else if (!A_MN) {
             tma_load_2d(sA, &tmA, &full_bar[stage], k, ti.m0);
           } else {
 #pragma unroll
@@ -545,9 +580,19 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
   using C_ = Cfg<BN>;
   auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, MODE>;
   ensure_smem_attr(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
-  // A operand tensor map.
+  // A operand tensor map(s).
   CUtensorMap tmA, tmB;
-  {
+  AgMaps ag;
+  memset(&ag, 0, sizeof(ag));
+  memset(&tmA, 0, sizeof(tmA));
+  if (MODE == GEMM_AG) {
+    for (int r = 0; r < d.nsrc; ++r) {
+      uint64_t dims[2] = {(uint64_t)d.K_extent_a, (uint64_t)d.src_rows};
+      uint64_t str[1] = {(uint64_t)d.lda * 2};
+      uint32_t box[2] = {64, 128};
+      ag.m[r] = make_tmap_bf16_sw128(d.peer_a[r], 2, dims, str, box);
+    }
+  } else {
     if (!A_MN) {  // A stored [rowsA, K] with row stride lda
       uint64_t dims[2] = {(uint64_t)d.K_extent_a, (uint64_t)d.rows_a};
       uint64_t str[1] = {(uint64_t)d.lda * 2};
@@ -602,8 +647,18 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
   p.ldh = d.ldh;
   p.alpha = d.alpha;
   p.status = reinterpret_cast<StatusBlock*>(d.status);
+  p.nsrc = d.nsrc;
+  p.me = d.me;
+  p.src_rows = d.src_rows > 0 ? d.src_rows : 1;
+  p.mt_rot = 0;
+  for (int r = 0; r < GEMM_MAX_PEERS; ++r) p.peer_c[r] = d.peer_c[r];
+  if (MODE == GEMM_AG) {
+    p.mt_rot = d.me * (d.src_rows / kBM);               // start on this rank's own rows
+  } else if (EPI == EPI_PEER_BF16) {
+    p.mt_rot = ((d.me + 1) % d.nsrc) * (d.src_rows / kBM);  // peers' rows first, own rows last
+  }
   int grid = num_sms();
-  if (MODE == GEMM_DENSE) {
+  if (MODE == GEMM_DENSE || MODE == GEMM_AG) {
     const int tiles = ((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
     grid = tiles < grid ? tiles : grid;
   } else if (MODE == GEMM_GROUPED_K) {
@@ -614,7 +669,7 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
     grid = tiles < grid ? tiles : grid;
   }
   if (grid < 1) grid = 1;
-  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(tmA, tmB, p);
+  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(tmA, tmB, ag, p);
 }
 
 template <bool A_MN, bool B_MN, int EPI, int MODE>
@@ -629,6 +684,8 @@ static void dispatch_bn(const GemmDesc& d, cudaStream_t s) {
 // rejected so the number of kernel instantiations stays small.
 template <bool A_MN, bool B_MN, int EPI, int MODE>
 constexpr bool combo_supported() {
+  if (MODE == GEMM_AG) return !A_MN && (EPI == EPI_STORE_BF16 || (EPI == EPI_SWIGLU && !B_MN));
+  if (EPI == EPI_PEER_BF16) return !A_MN && MODE == GEMM_DENSE;
   if (EPI == EPI_SWIGLU) return !A_MN && !B_MN && MODE != GEMM_GROUPED_K;
   if (EPI == EPI_SWIGLU_BWD) return !A_MN && B_MN && MODE != GEMM_GROUPED_K;
   if (EPI == EPI_ADD_BF16) return !A_MN && MODE == GEMM_DENSE;
@@ -655,11 +712,57 @@ static void dispatch_epi(const GemmDesc& d, cudaStream_t s) {
     case EPI_ADD_BF16: dispatch_checked<A_MN, B_MN, EPI_ADD_BF16, MODE>(d, s); break;
     case EPI_SWIGLU: dispatch_checked<A_MN, B_MN, EPI_SWIGLU, MODE>(d, s); break;
     case EPI_SWIGLU_BWD: dispatch_checked<A_MN, B_MN, EPI_SWIGLU_BWD, MODE>(d, s); break;
+    case EPI_PEER_BF16: dispatch_checked<A_MN, B_MN, EPI_PEER_BF16, MODE>(d, s); break;
     default: throw std::runtime_error("omnicoder gemm: unknown epilogue");
   }
 }
 
+// out[r, :] = sum over slots s of staging[s, r, :] (+ residual[r, :]), fp32 sums, bf16 out; one thread per
+// 8 columns.  The second half of a fused GEMM -> reduce-scatter: every rank stored its partial rows here.
+__global__ void tp_reduce_kernel(const __nv_bfloat16* __restrict__ st, int nsrc, int rows, int D, long long ld,
+                                 const __nv_bfloat16* __restrict__ res, long long ldr, __nv_bfloat16* __restrict__ out,
+                                 long long ldo) {
+  const int chunks = D / 8;
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * chunks) return;
+  const int r = (int)(i / chunks), c = (int)(i - (long long)r * chunks) * 8;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int s = 0; s < nsrc; ++s) {
+    const uint4 v = *reinterpret_cast<const uint4*>(st + ((long long)s * rows + r) * ld + c);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[2 * j] += bf16_lo(w[j]);
+      acc[2 * j + 1] += bf16_hi(w[j]);
+    }
+  }
+  if (res != nullptr) {
+    const uint4 v = *reinterpret_cast<const uint4*>(res + (long long)r * ldr + c);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[2 * j] += bf16_lo(w[j]);
+      acc[2 * j + 1] += bf16_hi(w[j]);
+    }
+  }
+  *reinterpret_cast<uint4*>(out + (long long)r * ldo + c) =
+      make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                 pack_bf16x2(acc[6], acc[7]));
+}
+
+void tp_reduce_slots(const void* staging, int nsrc, int rows, int D, long long ld, const void* residual,
+                     long long ldr, void* out, long long ldo, cudaStream_t s) {
+  if (D % 8 != 0) throw std::runtime_error("tp reduce: D % 8");
+  const long long work = (long long)rows * (D / 8);
+  if (work == 0) return;
+  tp_reduce_kernel<<<(unsigned)((work + 255) / 256), 256, 0, s>>>(
+      (const __nv_bfloat16*)staging, nsrc, rows, D, ld, (const __nv_bfloat16*)residual, ldr, (__nv_bfloat16*)out, ldo);
+}
+
 void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream) {
+  if (d.epilogue == EPI_PEER_BF16 &&
+      (d.nsrc < 1 || d.nsrc > GEMM_MAX_PEERS || d.src_rows <= 0 || d.src_rows % kBM != 0 || d.M != d.nsrc * d.src_rows))
+    throw std::runtime_error("omnicoder gemm: peer-store epilogue needs M = ranks x src_rows, src_rows % 128 == 0");
   if (d.num_groups > GEMM_MAX_GROUPS) throw std::runtime_error("omnicoder gemm: too many groups");
   if (d.K % 8 != 0 && !(d.mode == GEMM_GROUPED_K)) throw std::runtime_error("omnicoder gemm: K must be a multiple of 8");
   const int combo = (d.a_mn_major ? 2 : 0) | (d.b_mn_major ? 1 : 0);
@@ -674,6 +777,14 @@ void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream) {
       if (combo == 0) dispatch_epi<false, false, GEMM_GROUPED_M>(d, stream);
       else if (combo == 1) dispatch_epi<false, true, GEMM_GROUPED_M>(d, stream);
       else throw std::runtime_error("omnicoder gemm: unsupported major combination (grouped-M)");
+      break;
+    case GEMM_AG:
+      if (d.nsrc < 1 || d.nsrc > GEMM_MAX_PEERS || d.src_rows <= 0 || d.src_rows % kBM != 0 ||
+          d.M != d.nsrc * d.src_rows)
+        throw std::runtime_error("omnicoder gemm: all-gather mode needs M = ranks x src_rows, src_rows % 128 == 0");
+      if (combo == 0) dispatch_epi<false, false, GEMM_AG>(d, stream);
+      else if (combo == 1) dispatch_epi<false, true, GEMM_AG>(d, stream);
+      else throw std::runtime_error("omnicoder gemm: unsupported major combination (all-gather)");
       break;
     case GEMM_GROUPED_K:
       if (combo == 3) dispatch_epi<true, true, GEMM_GROUPED_K>(d, stream);

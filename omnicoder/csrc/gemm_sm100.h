@@ -5,7 +5,12 @@
 
 namespace omni {
 
-enum GemmMode : int { GEMM_DENSE = 0, GEMM_GROUPED_M = 1, GEMM_GROUPED_K = 2 };
+enum GemmMode : int {
+  GEMM_DENSE = 0,
+  GEMM_GROUPED_M = 1,
+  GEMM_GROUPED_K = 2,
+  GEMM_AG = 3,  // dense, rows [r*src_rows, (r+1)*src_rows) of A read from source r's buffer (peer memory)
+};
 
 enum GemmEpi : int {
   EPI_STORE_BF16 = 0,  // C(bf16) = alpha * acc
@@ -14,7 +19,11 @@ enum GemmEpi : int {
   EPI_ADD_BF16 = 3,    // C(bf16) = alpha * acc + R(bf16)   (R may alias C)
   EPI_SWIGLU = 4,      // acc = [gate|up] interleaved by 32; C = silu(gate)*up (bf16, N/2 cols); H = acc (bf16)
   EPI_SWIGLU_BWD = 5,  // acc = dAct; R = saved H; C = dH (bf16, 2N cols, interleaved by 32)
+  EPI_PEER_BF16 = 6,   // bf16 partial tile stored into its row owner's staging buffer (peer memory):
+                       // row -> owner r = row / src_rows, slot me: peer_c[r] + (me*src_rows + row%src_rows)*ldc
 };
+
+constexpr int GEMM_MAX_PEERS = 8;
 
 constexpr int GEMM_MAX_GROUPS = 256;
 
@@ -47,10 +56,20 @@ struct GemmDesc {
   long long ldh = 0;
   float alpha = 1.0f;
   void* status = nullptr;  // omni::StatusBlock*
+  // tensor-parallel fused collectives (GEMM_AG mode / EPI_PEER_BF16 epilogue)
+  int nsrc = 0;                              // ranks in the group
+  int me = 0;                                // this rank
+  int src_rows = 0;                          // rows per rank (multiple of 128)
+  const void* peer_a[GEMM_MAX_PEERS] = {};   // GEMM_AG: each rank's A row block ([src_rows, K], stride lda)
+  void* peer_c[GEMM_MAX_PEERS] = {};         // EPI_PEER_BF16: each rank's staging buffer
 };
 
 // Launch on `stream`.  Throws std::runtime_error on an invalid description.
 void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream);
+
+// out[r, :] = sum_s staging[s, r, :] (+ residual[r, :]) — the local half of a fused GEMM -> reduce-scatter.
+void tp_reduce_slots(const void* staging, int nsrc, int rows, int D, long long ld, const void* residual,
+                     long long ldr, void* out, long long ldo, cudaStream_t s);
 
 // rank-2 or rank-3 bf16 tensor map with 128-byte swizzle (dims[0] contiguous,
 // byte strides for dims 1..).  Throws on misaligned bases or strides.

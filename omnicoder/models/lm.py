@@ -102,6 +102,17 @@ class GQAttention(nn.Module):
         return q, k, v, None
 
     def forward(self, y, h, rope, positions, seq):
+        if self.tp is not None and getattr(self.tp, "transport", "nccl") == "p2p":
+            # fused collectives: the QKV GEMM gathers the token shards with its own loads, the output
+            # projection's epilogue reduce-scatters its partial tiles (parallel/tensor.py)
+            from ..parallel.tensor import tp_linear_ag, tp_linear_rs
+            T = y.shape[0] * self.tp.world
+            qkv = tp_linear_ag(y, self.wqkv, self.tp).view(T, self.H + 2 * self.Hk, self.hd)
+            qkv = apply_rope(qkv, rope, positions, off=0, interleaved=self.cfg.attn.rope_interleaved,
+                             heads=self.H + self.Hk)
+            q, k, v = qkv[:, :self.H], qkv[:, self.H:self.H + self.Hk], qkv[:, self.H + self.Hk:]
+            o = attention(q, k, v, None, seq=seq, causal=True, window=self.cfg.attn.window)
+            return tp_linear_rs(o.reshape(T, -1), self.wo, self.tp, residual=h)
         if self.tp is not None:
             from ..parallel.tensor import all_gather_seq, reduce_scatter_seq
             yf = all_gather_seq(y, self.tp)
@@ -225,6 +236,9 @@ class DenseFFN(nn.Module):
             self.w2 = _tp_param(self.w2.data[:, f0:f1])
 
     def forward(self, y, h):
+        if self.tp is not None and getattr(self.tp, "transport", "nccl") == "p2p":
+            from ..parallel.tensor import tp_swiglu_mlp
+            return tp_swiglu_mlp(y, self.w13, self.w2, self.tp, residual=h), None
         if self.tp is not None:
             from ..parallel.tensor import all_gather_seq, reduce_scatter_seq
             return reduce_scatter_seq(swiglu_mlp(all_gather_seq(y, self.tp), self.w13, self.w2), self.tp) + h, None

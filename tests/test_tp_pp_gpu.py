@@ -1,6 +1,9 @@
 """Tensor parallel (+ sequence parallel) and 1F1B pipeline training on 2 GPUs
-(NCCL, one process per GPU): the group-mean loss of three steps must track one
-GPU training the same model on the same batch (bf16 tolerance)."""
+(one process per GPU): the group-mean loss of three steps must track one GPU
+training the same model on the same batch (bf16 tolerance).  Tensor parallel
+runs with NCCL collectives and with the fused peer-memory collectives
+(all-gather inside the consuming GEMM's loads, reduce-scatter in the producing
+GEMM's epilogue)."""
 import os
 import socket
 
@@ -36,9 +39,9 @@ def _worker(rank, world, port, mode, q):
         rt = Trainer(ref, tc)
         ref_l = [float(rt.step(ids, lab).loss) for _ in range(3)]
         del rt, ref
-        if mode == "tp":
+        if mode in ("tp", "tp_p2p"):
             from omnicoder.parallel.tensor import TensorParallel
-            par = TensorParallel(dist.group.WORLD)
+            par = TensorParallel(dist.group.WORLD, transport="p2p" if mode == "tp_p2p" else "nccl")
             m = build_model(_cfg(), device=dev, seed=0, tp=par)
             tr = Trainer(m, tc, par)
             got = []
@@ -87,7 +90,7 @@ def _run(mode, world=2):
     return res
 
 
-@pytest.mark.parametrize("mode", ["tp", "pp"])
+@pytest.mark.parametrize("mode", ["tp", "tp_p2p", "pp"])
 def test_tp_and_pp_track_single_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
