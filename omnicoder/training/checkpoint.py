@@ -152,3 +152,64 @@ def load_best_or_latest(model: torch.nn.Module, directory_or_path: str) -> str |
         return None
     maybe_load_checkpoint(model, p)
     return p
+
+
+# ----------------------------------------------------------------------------
+# sidecars, manifest, best-weights registry (reference src/omnicoder/utils/
+# checkpoint.py:12-224 save_with_sidecar, model_manifest.py, best_weights.py)
+# ----------------------------------------------------------------------------
+def save_with_sidecar(path: str, model: torch.nn.Module, meta: dict | None = None, vocab=None) -> None:
+    """state_dict (CPU copy, atomic) + `<path>.meta.json` (config, parameter count, user meta)
+    + optional `<path>.vocab.json` (the unified-vocabulary sidecar)."""
+    import json
+    sd = {k: v.detach().cpu() for k, v in model.state_dict().items()}
+    _atomic_save({"model": sd, "config": getattr(model, "cfg").to_dict() if hasattr(model, "cfg") else None}, path)
+    info = {"params": int(sum(v.numel() for v in sd.values())), "keys": len(sd)}
+    if hasattr(model, "cfg"):
+        info["config"] = model.cfg.to_dict()
+    info.update(meta or {})
+    with open(path + ".meta.json", "w") as f:
+        json.dump(info, f, indent=1)
+    if vocab is not None:
+        vocab.save(path + ".vocab.json")
+
+
+def write_manifest(directory: str) -> dict:
+    """manifest.json of every checkpoint file in `directory` (bytes, mtime, meta if present)."""
+    import json
+    out = {}
+    for f in sorted(os.listdir(directory)):
+        p = os.path.join(directory, f)
+        if f.endswith((".pt", ".pth")) and os.path.isfile(p):
+            e = {"bytes": os.path.getsize(p), "mtime": os.path.getmtime(p)}
+            if os.path.exists(p + ".meta.json"):
+                e["meta"] = json.load(open(p + ".meta.json"))
+            out[f] = e
+    with open(os.path.join(directory, "manifest.json"), "w") as fh:
+        json.dump(out, fh, indent=1)
+    return out
+
+
+class BestWeightsRegistry:
+    """Tracks the best checkpoint per task in a JSON file: register(task, path, metric)."""
+
+    def __init__(self, path: str, higher_is_better: bool = True):
+        import json
+        self.path, self.hib = path, higher_is_better
+        self.data = json.load(open(path)) if os.path.exists(path) else {}
+
+    def register(self, task: str, ckpt: str, metric: float) -> bool:
+        import json
+        cur = self.data.get(task)
+        better = cur is None or (metric > cur["metric"] if self.hib else metric < cur["metric"])
+        if better:
+            self.data[task] = {"path": ckpt, "metric": float(metric)}
+            tmp = self.path + ".tmp"
+            with open(tmp, "w") as f:
+                json.dump(self.data, f, indent=1)
+            os.replace(tmp, self.path)
+        return better
+
+    def best(self, task: str) -> str | None:
+        e = self.data.get(task)
+        return e["path"] if e else None

@@ -97,3 +97,103 @@ def batches(source, batch: int, shuffle_seed: int = 0, pin: bool = True) -> Iter
         if len(order) < batch:
             xs, ys = zip(*(source[j % len(source)] for j in range(batch)))
             yield torch.stack(xs), torch.stack(ys)
+
+
+# ----------------------------------------------------------------------------
+# Data module with noise options, JSONL pair datasets, weighted mixture engine
+# (reference src/omnicoder/training/data/*.py: DataModule, KD / VL / VQA JSONL
+# datasets, DataEngine)
+# ----------------------------------------------------------------------------
+class DataModule:
+    """Batches from a token source with optional input noise: `drop_p` replaces tokens by
+    `mask_id`, `replace_p` by uniform random ids (labels keep the clean tokens)."""
+
+    def __init__(self, source, batch: int, vocab: int, drop_p: float = 0.0, replace_p: float = 0.0,
+                 mask_id: int = 0, seed: int = 0):
+        self.it = batches(source, batch, shuffle_seed=seed, pin=False)
+        self.vocab, self.drop_p, self.replace_p, self.mask_id = vocab, drop_p, replace_p, mask_id
+        self.g = torch.Generator().manual_seed(seed)
+
+    def __iter__(self):
+        return self
+
+    def __next__(self):
+        ids, lab = next(self.it)
+        if self.drop_p > 0 or self.replace_p > 0:
+            ids = ids.clone()
+            u = torch.rand(ids.shape, generator=self.g)
+            ids[u < self.drop_p] = self.mask_id
+            rep = (u >= self.drop_p) & (u < self.drop_p + self.replace_p)
+            ids[rep] = torch.randint(0, self.vocab, (int(rep.sum()),), generator=self.g)
+        return ids, lab
+
+
+class JsonlPairs:
+    """{"prompt": ..., "response": ...} lines (KD / SFT pairs) -> (ids, labels) with the prompt
+    masked out of the labels; `tokenize(str) -> list[int]`."""
+
+    def __init__(self, path: str, tokenize, seq_len: int, prompt_key: str = "prompt", response_key: str = "response"):
+        import json
+        self.items = []
+        for line in open(path, encoding="utf-8"):
+            line = line.strip()
+            if not line:
+                continue
+            d = json.loads(line)
+            p, r = tokenize(d[prompt_key]), tokenize(d[response_key])
+            ids = (p + r)[:seq_len + 1]
+            lab = ([-100] * len(p) + r)[:seq_len + 1]
+            pad = seq_len + 1 - len(ids)
+            self.items.append((torch.tensor(ids + [0] * pad), torch.tensor(lab + [-100] * pad)))
+
+    def __len__(self):
+        return len(self.items)
+
+    def __getitem__(self, i):
+        ids, lab = self.items[i]
+        return ids[:-1], lab[1:]
+
+
+class ImageTextJsonl:
+    """{"image": path, "text": caption} lines -> (image tensor [3, S, S] in [-1, 1], token ids)."""
+
+    def __init__(self, path: str, tokenize, image_size: int = 224, root: str | None = None):
+        import json
+        import os
+        self.rows = [json.loads(l) for l in open(path, encoding="utf-8") if l.strip()]
+        self.tok, self.size = tokenize, image_size
+        self.root = root or os.path.dirname(os.path.abspath(path))
+
+    def __len__(self):
+        return len(self.rows)
+
+    def __getitem__(self, i):
+        import os
+
+        import numpy as np
+        from PIL import Image
+        r = self.rows[i]
+        img = Image.open(os.path.join(self.root, r["image"])).convert("RGB").resize((self.size, self.size))
+        x = torch.from_numpy(np.asarray(img, dtype=np.float32) / 127.5 - 1.0).permute(2, 0, 1)
+        return x, torch.tensor(self.tok(r["text"]))
+
+
+class DataEngine:
+    """Weighted mixture of iterators: each draw picks source i with probability w_i / sum(w)."""
+
+    def __init__(self, sources: dict, weights: dict, seed: int = 0):
+        self.names = list(sources)
+        self.its = {k: iter(v) for k, v in sources.items()}
+        w = torch.tensor([float(weights.get(k, 1.0)) for k in self.names])
+        self.p = w / w.sum()
+        self.g = torch.Generator().manual_seed(seed)
+        self.counts = {k: 0 for k in self.names}
+
+    def __iter__(self):
+        return self
+
+    def __next__(self):
+        i = int(torch.multinomial(self.p, 1, generator=self.g))
+        k = self.names[i]
+        self.counts[k] += 1
+        return k, next(self.its[k])

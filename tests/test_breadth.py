@@ -1,0 +1,286 @@
+"""CPU tests of the multimodal VQ-VAEs and aligners, the multimodal / verifier trainers,
+data mixtures, inference tools and retrieval memory, graph-of-thoughts and SFB
+reasoning, GPTQ / AWQ quantisation, the mobile package round trip, tensor helpers
+and checkpoint sidecars."""
+import json
+import os
+
+import pytest
+import torch
+
+
+def _tiny_lm(vocab=64):
+    from omnicoder.config import AttentionConfig, ModelConfig
+    from omnicoder.models.lm import build_model
+    return build_model(ModelConfig(vocab_size=vocab, d_model=32, n_layers=1, n_heads=4, ffn_dim=64, max_seq_len=64,
+                                   attn=AttentionConfig(kind="mha")), seed=0)
+
+
+# ---------------------------------------------------------------------------- multimodal
+def test_image_vqvae_codes_and_training_reduce_loss():
+    from omnicoder.multimodal.vqvae import ImageVQVAE
+    from omnicoder.training.multimodal import train_vq
+    torch.manual_seed(0)
+    m = ImageVQVAE(width=16, levels=2, code_dim=8, codebook_size=32)
+    img = torch.rand(2, 3, 16, 16) * 2 - 1
+    codes = m.encode(img)
+    assert codes.shape == (2, 4, 4) and codes.dtype == torch.long and int(codes.max()) < 32
+    assert m.decode(codes).shape == img.shape
+    losses = train_vq(m, iter(lambda: img, None), steps=30, lr=3e-3)
+    assert losses[-1] < losses[0]
+
+
+def test_video_and_audio_vq_shapes():
+    from omnicoder.multimodal.vqvae import AudioVQ, MelVocoder, VideoVQVAE
+    torch.manual_seed(0)
+    v = VideoVQVAE(width=16, levels=2, code_dim=8, codebook_size=16)
+    vid = torch.rand(1, 3, 3, 16, 16)
+    rec, codes, loss = v(vid)
+    assert rec.shape == vid.shape and codes.shape == (1, 3, 4, 4) and loss.dim() == 0
+    assert v.decode(codes).shape == vid.shape
+    a = AudioVQ(n_mels=16, dim=32, code_dim=8, codebook_size=16)
+    wav = torch.randn(2, 4000)
+    c = a.encode(wav)
+    assert c.dim() == 2 and c.shape[0] == 2 and int(c.max()) < 16
+    voc = MelVocoder(n_mels=16, width=32, ups=(4, 2))
+    assert voc(torch.randn(2, 10, 16)).shape == (2, 10 * voc.hop)
+
+
+def test_cross_modal_alignment_learns_pairing():
+    from omnicoder.multimodal.aligner import CrossModalVerifier
+    from omnicoder.training.multimodal import train_alignment
+    torch.manual_seed(0)
+    W = torch.randn(24, 16)
+
+    def pairs():
+        while True:
+            t = torch.randn(8, 16)
+            yield t, t @ W.t() + 0.01 * torch.randn(8, 24)
+    ver = CrossModalVerifier({"text": 16, "image": 24}, shared=32)
+    losses = train_alignment(ver, pairs(), steps=60, lr=1e-2)
+    assert losses[-1] < 0.5 * losses[0]
+    t, i = next(pairs())
+    s = torch.stack([ver.score("text", t[k:k + 1].expand(8, -1), "image", i) for k in range(8)])
+    assert (s.argmax(1) == torch.arange(8)).float().mean() >= 0.75
+
+
+def test_grounding_segmentation_and_av_offset():
+    from omnicoder.multimodal.aligner import GroundingHead, SegmentationHead, av_offset
+    g = GroundingHead(32)
+    box = g(torch.randn(2, 5, 32), torch.randn(2, 16, 32))
+    assert box.shape == (2, 4) and bool(((box >= 0) & (box <= 1)).all())
+    seg = SegmentationHead(32, n_classes=3)(torch.randn(2, 16, 32), grid=4, image_size=32)
+    assert seg.shape == (2, 3, 32, 32)
+    torch.manual_seed(0)
+    video = torch.randn(40, 8)
+    audio = torch.roll(video, shifts=-3, dims=0)          # audio frame t matches video frame t + 3
+    assert av_offset(audio, video, max_lag=6) == 3
+
+
+def test_vl_pretrain_step_and_verifier_head():
+    from omnicoder.multimodal.composer import MultimodalComposer
+    from omnicoder.multimodal.vocab import VocabSidecar
+    from omnicoder.training.multimodal import VerifierHead, train_verifier_head, vl_pretrain_step
+    lm = _tiny_lm(vocab=64)
+    comp = MultimodalComposer(32, layout=VocabSidecar([0, 31], [32, 47], [48, 55], [56, 63]))
+    opt = torch.optim.AdamW(lm.parameters(), lr=1e-3)
+    loss = vl_pretrain_step(lm, comp, opt, torch.randint(0, 16, (2, 2, 2)), torch.randint(0, 32, (2, 9)))
+    assert loss > 0
+    head = VerifierHead(32)
+    g = torch.Generator().manual_seed(0)
+
+    def batches():
+        while True:
+            ids = torch.randint(0, 32, (8, 6), generator=g)
+            yield ids, (ids[:, -1] < 16).long()
+    ls = train_verifier_head(lm, head, batches(), steps=40, lr=1e-2)
+    assert sum(ls[-5:]) < sum(ls[:5])
+
+
+# ---------------------------------------------------------------------------- data
+def test_data_module_noise_and_mixture(tmp_path):
+    from omnicoder.training.data import DataEngine, DataModule, JsonlPairs, SyntheticTokens, TokenStream
+    src = TokenStream(torch.arange(1, 2001) % 97 + 1, seq_len=16)
+    dm = DataModule(src, batch=4, vocab=97, drop_p=0.5, seed=0)
+    ids, lab = next(dm)
+    assert ids.shape == (4, 16) and (ids == 0).float().mean() > 0.3 and (lab != 0).all()
+    p = tmp_path / "pairs.jsonl"
+    p.write_text("\n".join(json.dumps({"prompt": "ab", "response": "cde"}) for _ in range(3)))
+    ds = JsonlPairs(str(p), lambda s: [ord(c) for c in s], seq_len=8)
+    x, y = ds[0]
+    assert x.tolist()[:5] == [97, 98, 99, 100, 101] and y.tolist()[:4] == [-100, 99, 100, 101]
+    eng = DataEngine({"a": iter(int, 1), "b": iter(int, 1)}, {"a": 3.0, "b": 1.0}, seed=0)
+    for _ in range(400):
+        next(eng)
+    assert 250 < eng.counts["a"] < 350
+
+
+# ---------------------------------------------------------------------------- inference tools
+def test_tool_registry_and_router():
+    from omnicoder.inference.tools import ToolRegistry, UnifiedRouter, safe_eval_arith
+    assert safe_eval_arith("2*(3+4)**2 - 1") == 97
+    with pytest.raises(ValueError):
+        safe_eval_arith("__import__('os')")
+    reg = ToolRegistry()
+    reg.register("upper", str.upper)
+    out = reg.run_calls("x <tool>calc(6*7)</tool> y <tool>upper('hi')</tool> <tool>nope(1)</tool>")
+    assert "<result>42</result>" in out and "<result>HI</result>" in out and "unknown tool" in out
+    r = UnifiedRouter()
+    r.register("text", lambda q: "T")
+    r.register("image", lambda q: "I")
+    assert r({"prompt": "x"}) == "T" and r({"path": "cat.PNG"}) == "I"
+    with pytest.raises(KeyError):
+        r({"modality": "audio"})
+
+
+def test_estimate_memory_counts_parameters():
+    from omnicoder.inference.tools import estimate_memory
+    lm = _tiny_lm(vocab=64)
+    est = estimate_memory(lm.cfg, batch=2, seq=128, kv_dtype="int8", training=True)
+    n = sum(p.numel() for p in lm.parameters())
+    assert abs(est["params"] - n) / n < 0.05, (est["params"], n)
+    assert est["kv_cache_bytes"] > 0 and est["total_bytes"] > est["weights_bytes"]
+
+
+def test_retrieval_and_semantic_memory():
+    from omnicoder.inference.retrieval_memory import ExternalRetrievalMemory, SemanticMemory, retrieval_prefix
+    mem = ExternalRetrievalMemory()
+    mem.add(["the capital of France is Paris", "python lists have append", "rust uses ownership"])
+    assert "Paris" in mem.search("what is the capital of France", k=1)[0][0]
+    ids = retrieval_prefix(mem, "python append", lambda s: [len(w) for w in s.split()], k=1, sep=[0])
+    assert ids[-1] == 0 and len(ids) == 5
+    sm = SemanticMemory(half_life=2.0)
+    sm.put("a", 1)
+    for i in range(10):
+        sm.put(f"x{i}", i)
+    assert sm.relevance("a") < 0.1
+    assert sm.get("x9") == 9 and sm.top(1) == ["x9"]
+    assert sm.forget(0.05) >= 1 and "a" not in sm.facts
+
+
+# ---------------------------------------------------------------------------- reasoning
+def test_graph_of_thoughts_and_bfs():
+    from omnicoder.reasoning.graph_of_thoughts import AdaptiveGraphOfThoughts, latent_bfs, reflect
+    target = 23
+    got = AdaptiveGraphOfThoughts(propose=lambda s: [s + 1, s * 2, s + 5], score=lambda s: -abs(target - s),
+                                  is_final=lambda s: s == target, beam=3, max_rounds=10)
+    assert got.run(1).state == target
+    path = latent_bfs(1, lambda s: [("+1", s + 1), ("*2", s * 2)] if s < 100 else [], lambda s: s == 10)
+    assert path is not None and len(path) == 4             # 1 -> 2 -> 4 -> 5 -> 10
+    ans, rounds = reflect(lambda p: "ok" if "feedback" in p else "bad",
+                          lambda p, a: (a == "ok", "try again"), "q")
+    assert ans == "ok" and rounds == 1
+
+
+def test_omega_controller_hysteresis():
+    from omnicoder.reasoning.graph_of_thoughts import OmegaController
+    oc = OmegaController()
+    flat, sharp = torch.full((1, 100), 0.01), torch.nn.functional.one_hot(torch.tensor([3]), 100).float()
+    assert oc.knobs(flat)["search"] and oc.mode == "explore"
+    mid = torch.softmax(torch.randn(1, 100) * 2.0, -1)
+    if oc.normalized_entropy(mid) > oc.low:
+        assert oc.knobs(mid)["search"]                     # hysteresis: stays exploring
+    assert not oc.knobs(sharp)["search"] and oc.mode == "normal"
+
+
+def test_certificates():
+    from omnicoder.reasoning.graph_of_thoughts import verify_certificate
+    assert verify_certificate("42", {"kind": "numeric", "value": 42})
+    assert not verify_certificate("41", {"kind": "numeric", "value": 42})
+    assert verify_certificate(12, {"kind": "python", "check": "assert answer % 3 == 0"})
+    assert not verify_certificate(13, {"kind": "python", "check": "assert answer % 3 == 0"})
+
+
+def test_sfb_factorize_spn_bias_arbiter():
+    from omnicoder.reasoning.sfb import ProofMarginArbiter, compile_factor_graph, cross_bias, factorize
+    fs = factorize("1. compute 3 + 4\n2. implement a python function\n3. who wrote Hamlet?")
+    assert [f["kind"] for f in fs] == ["math", "code", "retrieval"]
+    spn = compile_factor_graph({"a": [0, 1], "b": [0, 1]},
+                               [(("a",), lambda a: 0.3 if a else 0.7), (("a", "b"), lambda a, b: 0.9 if a == b else 0.1)])
+    m = spn.marginal("b", [0, 1])
+    assert abs(m[1] - (0.3 * 0.9 + 0.7 * 0.1)) < 1e-9
+    assert abs(spn.marginal("a", [0, 1], {"b": 1})[1] - 0.27 / 0.34) < 1e-9
+    p1, p2 = torch.tensor([0.7, 0.1, 0.1, 0.1]), torch.tensor([0.1, 0.7, 0.1, 0.1])
+    b = cross_bias([p1, p2], [3.0, 1.0])
+    assert int(b.argmax()) == 0 and torch.allclose(torch.softmax(b, -1), 0.75 * p1 + 0.25 * p2, atol=1e-5)
+    arb = ProofMarginArbiter(0.1)
+    assert arb.choose([{"answer": "x", "score": 0.9}, {"answer": "y", "score": 0.85}]) is None
+    assert arb.choose([{"answer": "x", "score": 0.5, "verified": True}, {"answer": "y", "score": 0.9}]) == "x"
+
+
+# ---------------------------------------------------------------------------- export / quantisation
+def test_gptq_beats_rtn_on_calibration_data():
+    from omnicoder.export.quantize import gptq_quantize, rtn_quantize
+    torch.manual_seed(0)
+    W = torch.randn(64, 256)
+    X = torch.randn(512, 256) @ torch.randn(256, 256) * 0.2       # correlated activations
+    q, s, Wg = gptq_quantize(W, X, bits=4, group=128)
+    _, _, Wr = rtn_quantize(W, bits=4, group=128)
+    assert q.dtype == torch.int8 and int(q.abs().max()) <= 7 and s.shape == (64, 2)
+    assert torch.allclose(Wg, (q.float().view(64, 2, 128) * s[..., None]).view(64, 256), atol=1e-5)
+    eg = (X @ (W - Wg).t()).pow(2).mean()
+    er = (X @ (W - Wr).t()).pow(2).mean()
+    assert eg < 0.8 * er, (eg, er)
+
+
+def test_awq_scales_do_not_hurt():
+    from omnicoder.export.quantize import awq_scales, rtn_quantize
+    torch.manual_seed(0)
+    W = torch.randn(32, 128)
+    X = torch.randn(256, 128) * torch.linspace(0.05, 5.0, 128)      # a few salient channels
+    s, Ws = awq_scales(W, X, bits=4, group=64)
+    _, _, Wq = rtn_quantize(Ws, 4, 64)
+    _, _, Wr = rtn_quantize(W, 4, 64)
+    ea = (X @ W.t() - (X / s) @ Wq.t()).pow(2).mean()
+    er = (X @ (W - Wr).t()).pow(2).mean()
+    assert ea <= er * 1.0001
+
+
+def test_mobile_package_round_trip(tmp_path):
+    from omnicoder.export.mobile_packager import load_package, package_model
+    lm = _tiny_lm(vocab=64).eval()
+    man = package_model(lm, str(tmp_path / "pkg"))
+    assert "weights_int4.pt" in man["files"] and "vocab.json" in man["files"]
+    m2 = load_package(str(tmp_path / "pkg")).eval()
+    ids = torch.randint(0, 64, (1, 12))
+    with torch.no_grad():
+        a = lm(ids, all_logits=True)["logits"].float()
+        b = m2(ids, all_logits=True)["logits"].float()
+    assert (a - b).abs().max() < 0.25 * a.abs().max()
+    (tmp_path / "pkg" / "config.json").write_text("{}")
+    with pytest.raises(ValueError):
+        load_package(str(tmp_path / "pkg"))
+
+
+# ---------------------------------------------------------------------------- utilities
+def test_torchutils(tmp_path):
+    from omnicoder.utils.torchutils import (guard_shape, safe_concat, safe_copy_into, safe_make_contiguous,
+                                            safe_new_like, safe_torch_save)
+    t = torch.ones(2, 3)
+    assert safe_new_like(t, fill=2.0).sum() == 12
+    with pytest.raises(ValueError):
+        safe_copy_into(torch.zeros(3), t)
+    assert safe_concat([t, None, torch.zeros(0, 3), t.double()]).dtype == torch.float64
+    assert safe_make_contiguous(t.t()).is_contiguous()
+    guard_shape(t, (2, None))
+    with pytest.raises(ValueError):
+        guard_shape(t, (3, None), "x")
+    p = str(tmp_path / "a" / "x.pt")
+    safe_torch_save({"t": t}, p)
+    assert torch.equal(torch.load(p)["t"], t) and os.listdir(tmp_path / "a") == ["x.pt"]
+
+
+def test_checkpoint_sidecar_manifest_registry(tmp_path):
+    from omnicoder.multimodal.vocab import VocabSidecar
+    from omnicoder.training.checkpoint import BestWeightsRegistry, save_with_sidecar, write_manifest
+    lm = _tiny_lm()
+    p = str(tmp_path / "m.pt")
+    save_with_sidecar(p, lm, meta={"step": 7}, vocab=VocabSidecar.from_config(text_vocab=64))
+    meta = json.load(open(p + ".meta.json"))
+    assert meta["step"] == 7 and meta["params"] == sum(v.numel() for v in lm.state_dict().values())
+    assert os.path.exists(p + ".vocab.json")
+    assert "m.pt" in write_manifest(str(tmp_path))
+    reg = BestWeightsRegistry(str(tmp_path / "best.json"))
+    assert reg.register("code", "a.pt", 0.5) and not reg.register("code", "b.pt", 0.4)
+    assert reg.register("code", "c.pt", 0.6)
+    assert BestWeightsRegistry(str(tmp_path / "best.json")).best("code") == "c.pt"
