@@ -26,6 +26,7 @@ SHAPES = [
     ("o_proj_dx", 8192, 2048, 2048, "dx"),
     ("o_proj_dw", 8192, 2048, 2048, "dw"),
     ("lm_head_dx", 8192, 2048, 32000, "dx"),
+    ("expert_w13_dw_grouped", 2816, 2048, 32768, "dw_grouped"),   # 32 experts x 1024 rows
 ]
 
 
@@ -48,6 +49,16 @@ def run(shape):
         ours = lambda: C.gemm(a, b, out, False, True, EPI_BF16, 1.0, None, None, 256)
         ref = lambda: torch.matmul(a, b)
         flops = 2 * M * N * K
+    elif kind == "dw_grouped":
+        # per expert g: dW[g] [M, N] = A_g^T B_g over the expert's rows (K = all rows of 32 experts)
+        G = 32
+        a = torch.randn(K, M, device="cuda").to(torch.bfloat16)
+        b = torch.randn(K, N, device="cuda").to(torch.bfloat16)
+        offs = torch.arange(0, K + 1, K // G, device="cuda", dtype=torch.int32)
+        out = torch.empty(G, M, N, device="cuda", dtype=torch.bfloat16)
+        ours = lambda: C.gemm_grouped_k(a, b, offs, out, EPI_BF16, 1.0, 256)
+        ref = lambda: torch.bmm(a.view(G, K // G, M).transpose(1, 2), b.view(G, K // G, N))
+        flops = 2 * M * N * K
     else:  # dw: dW[N,K] = dY[M,N]^T X[M,K]
         dy = torch.randn(M, N, device="cuda").to(torch.bfloat16)
         out = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
@@ -55,10 +66,16 @@ def run(shape):
         ref = lambda: torch.matmul(dy.t(), a)
         flops = 2 * M * N * K
     t_ours = time_fn(ours)
+    C.set_gemm_pair(False)           # the one-CTA 128-row tile kernel, for comparison
+    try:
+        t_single = time_fn(ours)
+    finally:
+        C.set_gemm_pair(True)
     t_ref = time_fn(ref)
     _ext.check_status()
-    return {"name": name, "M": M, "N": N, "K": K, "kind": kind, "ms": t_ours, "cublas_ms": t_ref,
-            "tflops": flops / t_ours / 1e9, "cublas_tflops": flops / t_ref / 1e9, "speedup": t_ref / t_ours}
+    return {"name": name, "M": M, "N": N, "K": K, "kind": kind, "ms": t_ours, "single_cta_ms": t_single,
+            "cublas_ms": t_ref, "tflops": flops / t_ours / 1e9, "single_cta_tflops": flops / t_single / 1e9,
+            "cublas_tflops": flops / t_ref / 1e9, "speedup": t_ref / t_ours}
 
 
 def main():
@@ -73,7 +90,7 @@ def main():
         r = run(s)
         rows.append(r)
         print(f"{r['name']:24s} M={r['M']:6d} N={r['N']:6d} K={r['K']:6d}  ours {r['ms']:8.3f} ms "
-              f"{r['tflops']:7.1f} TF/s | cuBLAS {r['cublas_ms']:8.3f} ms {r['cublas_tflops']:7.1f} TF/s | x{r['speedup']:.2f}",
+              f"{r['tflops']:7.1f} TF/s (one-CTA tiles {r['single_cta_tflops']:7.1f}) | cuBLAS {r['cublas_ms']:8.3f} ms {r['cublas_tflops']:7.1f} TF/s | x{r['speedup']:.2f}",
               flush=True)
     if args.json:
         with open(args.json, "w") as f:

@@ -508,6 +508,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_skinny_grouped", &omni::gemm_skinny_grouped, py::arg("A"), py::arg("B"), py::arg("offsets"),
         py::arg("C"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("rows") = 0);
   m.def("set_skinny_rows", &omni::set_skinny_rows, "rows up to which dense GEMMs use the few-row kernel (0: off)");
+  m.def("set_gemm_pair", &omni::set_gemm_pair, "use CTA-pair (cta_group::2) 256-row tiles for large dense / grouped-K GEMMs");
+  m.def("gemm_pair_enabled", &omni::gemm_pair_enabled);
   m.def("gemm_grouped_m", &omni::gemm_grouped_m, py::arg("A"), py::arg("B"), py::arg("offsets"), py::arg("C"),
         py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
         py::arg("H") = py::none(), py::arg("block_n") = 256, py::arg("max_rows_hint") = 0);

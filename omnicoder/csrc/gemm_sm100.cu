@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -70,12 +71,17 @@ struct AgMaps {
   CUtensorMap m[GEMM_MAX_PEERS];
 };
 
-template <int BN>
+// PAIR: a cluster of two CTAs computes one (2*128) x BN tile with cta_group::2 MMAs;
+// each CTA stages its 128 rows of A and BN/2 rows of B, so per SM the shared-memory
+// operand traffic per FLOP drops by a third against the one-CTA 128 x BN tile.
+template <int BN, bool PAIR = false>
 struct Cfg {
+  static constexpr int kTM = PAIR ? 2 * kBM : kBM;  // rows of C per tile
+  static constexpr int kBNc = PAIR ? BN / 2 : BN;  // rows of B staged by one CTA
   static constexpr int kStageA = kBM * kBK * 2;    // 16 KB
-  static constexpr int kStageB = BN * kBK * 2;     // 32 KB at BN=256
+  static constexpr int kStageB = kBNc * kBK * 2;   // 32 KB at BN=256 (16 KB per CTA of a pair)
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kStages = PAIR ? 6 : (BN >= 256 ? 4 : 6);
   static constexpr int kTmemCols = 2 * BN;         // double-buffered accumulator
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -85,28 +91,28 @@ struct TileInfo {
   int m_limit;  // rows >= m_limit are not stored
 };
 
-template <int BN, int MODE>
+template <int BN, int MODE, int TM = kBM>
 __device__ __forceinline__ int total_tiles(const GemmArgs& p, const int* s_off) {
   const int num_n = (p.N + BN - 1) / BN;
-  if (MODE == GEMM_DENSE || MODE == GEMM_AG) return ((p.M + kBM - 1) / kBM) * num_n;
+  if (MODE == GEMM_DENSE || MODE == GEMM_AG) return ((p.M + TM - 1) / TM) * num_n;
   if (MODE == GEMM_GROUPED_M) return (s_off[p.num_groups] / kBM) * num_n;
-  return p.num_groups * ((p.M + kBM - 1) / kBM) * num_n;
+  return p.num_groups * ((p.M + TM - 1) / TM) * num_n;
 }
 
-template <int BN, int MODE>
+template <int BN, int MODE, int TM = kBM>
 __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, int t, const int* s_off) {
   TileInfo ti;
   const int num_n = (p.N + BN - 1) / BN;
   if (MODE == GEMM_DENSE || MODE == GEMM_AG) {
     // Grouped raster: 8 M-tiles share each sweep over N for L2 reuse of B.
-    const int num_m = (p.M + kBM - 1) / kBM;
+    const int num_m = (p.M + TM - 1) / TM;
     constexpr int GM = 8;
     const int per_group = GM * num_n;
     const int grp = t / per_group;
     const int first_m = grp * GM;
     const int gsize = min(num_m - first_m, GM);
     const int r = t - grp * per_group;
-    ti.m0 = ((first_m + r % gsize + p.mt_rot) % num_m) * kBM;
+    ti.m0 = ((first_m + r % gsize + p.mt_rot) % num_m) * TM;
     ti.n0 = (r / gsize) * BN;
     ti.g = 0;
     ti.k0 = 0;
@@ -123,12 +129,12 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& p, int t, const in
     ti.num_kb = (p.K + kBK - 1) / kBK;
     ti.m_limit = s_off[g + 1];
   } else {
-    const int num_m = (p.M + kBM - 1) / kBM;
+    const int num_m = (p.M + TM - 1) / TM;
     const int per_g = num_m * num_n;
     const int g = t / per_g;
     const int r = t - g * per_g;
     ti.g = g;
-    ti.m0 = (r / num_n) * kBM;
+    ti.m0 = (r / num_n) * TM;
     ti.n0 = (r % num_n) * BN;
     ti.k0 = s_off[g];
     ti.num_kb = (s_off[g + 1] - s_off[g]) / kBK;
@@ -307,12 +313,13 @@ __device__ __forceinline__ void store_swiglu_bwd(const GemmArgs& p, int row, int
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ AgMaps ag, GemmArgs p) {
-  using C_ = Cfg<BN>;
+  using C_ = Cfg<BN, PAIR>;
   constexpr int S = C_::kStages;
+  constexpr int TM = C_::kTM;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * C_::kStageBytes);
@@ -325,6 +332,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
+  // A pair is two consecutive CTAs of one cluster; rank 0 (the leader) issues the MMAs
+  // and owns the barriers that the MMAs wait on.
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = crank == 0u;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (MODE != GEMM_DENSE) {
     for (int i = threadIdx.x; i <= p.num_groups; i += kThreads) s_off[i] = p.group_offsets[i];
@@ -336,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 4);
+      mbar_init(&tempty_bar[b], PAIR ? 8 : 4);  // every epilogue warp of the tile's CTAs
     }
     mbar_init(drain_bar, 1);
     fence_barrier_init();
@@ -350,14 +363,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C_::kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, C_::kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C_::kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync_all(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int ntiles = total_tiles<BN, MODE>(p, s_off);
+  const int ntiles = total_tiles<BN, MODE, TM>(p, s_off);
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -365,8 +383,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const TileInfo ti = tile_info<BN, MODE>(p, t, s_off);
+      for (int t = tile0; t < ntiles && ok; t += tile_step) {
+        const TileInfo ti = tile_info<BN, MODE, TM>(p, t, s_off);
+        const int am0 = ti.m0 + (int)crank * kBM;         // this CTA's rows of A
+        const int bn0 = ti.n0 + (int)crank * C_::kBNc;    // this CTA's rows of B
         for (int kb = 0; kb < ti.num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) {
             ok = false;
@@ -374,30 +394,50 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sA = smem + stage * C_::kStageBytes;
           uint8_t* sB = sA + C_::kStageA;
-          mbar_arrive_expect_tx(&full_bar[stage], C_::kStageBytes);
           const int k = ti.k0 + kb * kBK;
-          if (MODE == GEMM_AG) {
-            // rows of source rank `src`, read from its buffer (over NVLink for a peer)
-            const int src = ti.m0 / p.src_rows;
-            tma_load_2d(sA, &ag.m[src], &full_bar[stage], k, ti.m0 - src * p.src_rows);
-          } else if (!A_MN) {
-            tma_load_2d(sA, &tmA, &full_bar[stage], k, ti.m0);
-          } else {
+          if constexpr (PAIR) {
+            // both CTAs' bytes complete on the leader's barrier
+            const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * C_::kStageBytes);
+            if (!A_MN) {
+              tma_load_2d_pair(sA, &tmA, bar, k, am0);
+            } else {
 #pragma unroll
-            for (int i = 0; i < kBM / 64; ++i) tma_load_2d(sA + i * kSwizzleChunk, &tmA, &full_bar[stage], ti.m0 + 64 * i, k);
-          }
-          if (!B_MN) {
-            if (MODE == GEMM_GROUPED_M)
-              tma_load_3d(sB, &tmB, &full_bar[stage], k, ti.n0, ti.g);
-            else
-              tma_load_2d(sB, &tmB, &full_bar[stage], k, ti.n0);
-          } else {
+              for (int i = 0; i < kBM / 64; ++i) tma_load_2d_pair(sA + i * kSwizzleChunk, &tmA, bar, am0 + 64 * i, k);
+            }
+            if (!B_MN) {
+              tma_load_2d_pair(sB, &tmB, bar, k, bn0);
+            } else {
 #pragma unroll
-            for (int i = 0; i < BN / 64; ++i) {
+              for (int i = 0; i < C_::kBNc / 64; ++i)
+                tma_load_2d_pair(sB + i * kSwizzleChunk, &tmB, bar, bn0 + 64 * i, k);
+            }
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], C_::kStageBytes);
+            if (MODE == GEMM_AG) {
+              // rows of source rank `src`, read from its buffer (over NVLink for a peer)
+              const int src = ti.m0 / p.src_rows;
+              tma_load_2d(sA, &ag.m[src], &full_bar[stage], k, ti.m0 - src * p.src_rows);
+            } else if (!A_MN) {
+              tma_load_2d(sA, &tmA, &full_bar[stage], k, ti.m0);
+            } else {
+#pragma unroll
+              for (int i = 0; i < kBM / 64; ++i)
+                tma_load_2d(sA + i * kSwizzleChunk, &tmA, &full_bar[stage], ti.m0 + 64 * i, k);
+            }
+            if (!B_MN) {
               if (MODE == GEMM_GROUPED_M)
-                tma_load_3d(sB + i * kSwizzleChunk, &tmB, &full_bar[stage], ti.n0 + 64 * i, k, ti.g);
+                tma_load_3d(sB, &tmB, &full_bar[stage], k, ti.n0, ti.g);
               else
-                tma_load_2d(sB + i * kSwizzleChunk, &tmB, &full_bar[stage], ti.n0 + 64 * i, k);
+                tma_load_2d(sB, &tmB, &full_bar[stage], k, ti.n0);
+            } else {
+#pragma unroll
+              for (int i = 0; i < BN / 64; ++i) {
+                if (MODE == GEMM_GROUPED_M)
+                  tma_load_3d(sB + i * kSwizzleChunk, &tmB, &full_bar[stage], ti.n0 + 64 * i, k, ti.g);
+                else
+                  tma_load_2d(sB + i * kSwizzleChunk, &tmB, &full_bar[stage], ti.n0 + 64 * i, k);
+              }
             }
           }
           if (++stage == S) {
@@ -409,15 +449,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer --------------------------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(kBM, BN, A_MN, B_MN, true);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = umma_idesc_f16(TM, BN, A_MN, B_MN, true);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const TileInfo ti = tile_info<BN, MODE>(p, t, s_off);
+      for (int t = tile0; t < ntiles && ok; t += tile_step) {
+        const TileInfo ti = tile_info<BN, MODE, TM>(p, t, s_off);
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) break;
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
@@ -435,33 +475,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         : umma_desc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? umma_desc_sw128(b_addr + kk * 2048, kSwizzleChunk, 1024)
                                         : umma_desc_sw128(b_addr + kk * 32, 16, 1024);
-            tc_mma_f16(tmem_d, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              tc_mma_f16_pair(tmem_d, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            else
+              tc_mma_f16(tmem_d, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
-          tc_commit(&empty_bar[stage]);
+          if constexpr (PAIR) tc_commit_pair(&empty_bar[stage], 0x3); else tc_commit(&empty_bar[stage]);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull_bar[acc]);
+        if constexpr (PAIR) tc_commit_pair(&tfull_bar[acc], 0x3); else tc_commit(&tfull_bar[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
         }
       }
       // Drain: wait for every MMA this thread issued before TMEM is released.
-      tc_commit(drain_bar);
+      if constexpr (PAIR) tc_commit_pair(drain_bar, 0x1); else tc_commit(drain_bar);
       mbar_wait(drain_bar, 0, p.status, STATUS_TIMEOUT_DRAIN);
     }
   } else {
     // ------------------------------ Epilogue ----------------------------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = quarter * 32 + lane;
+    const int row_in_tile = (int)crank * kBM + quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const TileInfo ti = tile_info<BN, MODE>(p, t, s_off);
+    for (int t = tile0; t < ntiles; t += tile_step) {
+      const TileInfo ti = tile_info<BN, MODE, TM>(p, t, s_off);
       if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, STATUS_TIMEOUT_TMEM_FULL)) break;
       tc_fence_after();
       const int row = ti.m0 + row_in_tile;
@@ -495,7 +538,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (lane == 0) {
+        if (PAIR && !leader)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+        else
+          mbar_arrive(&tempty_bar[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -505,10 +553,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  // A pair stays resident until the leader's MMAs (which read the peer's shared memory
+  // and write its tensor memory) have drained.
+  if constexpr (PAIR) cluster_sync_all(); else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C_::kTmemCols);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C_::kTmemCols); else tmem_dealloc(tmem_base, C_::kTmemCols);
   }
 }
 
@@ -575,10 +625,10 @@ int num_sms() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE, bool PAIR = false>
 static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
-  using C_ = Cfg<BN>;
-  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, MODE>;
+  using C_ = Cfg<BN, PAIR>;
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, MODE, PAIR>;
   ensure_smem_attr(reinterpret_cast<const void*>(kern), C_::kSmemBytes);
   // A operand tensor map(s).
   CUtensorMap tmA, tmB;
@@ -615,7 +665,7 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
       } else {
         uint64_t dims[2] = {(uint64_t)d.K_extent_b, (uint64_t)d.N};
         uint64_t str[1] = {(uint64_t)d.ldb * 2};
-        uint32_t box[2] = {64, (uint32_t)BN};
+        uint32_t box[2] = {64, (uint32_t)C_::kBNc};
         tmB = make_tmap_bf16_sw128(d.B, 2, dims, str, box);
       }
     } else {      // B stored [K, N]
@@ -657,27 +707,94 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
   } else if (EPI == EPI_PEER_BF16) {
     p.mt_rot = ((d.me + 1) % d.nsrc) * (d.src_rows / kBM);  // peers' rows first, own rows last
   }
+  constexpr int TM = C_::kTM;
+  // persistent grid: one CTA (pair) per SM (pair of SMs), no more than there are tiles
   int grid = num_sms();
+  if constexpr (PAIR) {
+    static int max_pairs = 0;  // co-resident clusters of two for this kernel
+    if (max_pairs == 0) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(2 * num_sms());
+      q.blockDim = dim3(kThreads);
+      q.dynamicSmemBytes = C_::kSmemBytes;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 2;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n < 1) {
+        (void)cudaGetLastError();
+        n = num_sms() / 2;
+      }
+      max_pairs = n;
+    }
+    grid = max_pairs;
+  }
   if (MODE == GEMM_DENSE || MODE == GEMM_AG) {
-    const int tiles = ((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
+    const int tiles = ((d.M + TM - 1) / TM) * ((d.N + BN - 1) / BN);
     grid = tiles < grid ? tiles : grid;
   } else if (MODE == GEMM_GROUPED_K) {
-    const int tiles = d.num_groups * ((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
+    const int tiles = d.num_groups * ((d.M + TM - 1) / TM) * ((d.N + BN - 1) / BN);
     grid = tiles < grid ? tiles : grid;
   } else if (d.max_rows_hint > 0) {
     const int tiles = (d.max_rows_hint / kBM) * ((d.N + BN - 1) / BN);
     grid = tiles < grid ? tiles : grid;
   }
   if (grid < 1) grid = 1;
-  kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(tmA, tmB, ag, p);
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C_::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, ag, p);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("omnicoder gemm: pair launch failed: ") + cudaGetErrorString(e));
+  } else {
+    kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(tmA, tmB, ag, p);
+  }
+}
+
+// CTA-pair tiles are used for large dense and grouped-K problems (and can be switched off
+// with set_gemm_pair(false), or OMNI_GEMM_PAIR=0, for comparisons).
+static int g_pair_mode = -1;  // -1: read the environment on first use
+void set_gemm_pair(bool on) { g_pair_mode = on ? 1 : 0; }
+bool gemm_pair_enabled() {
+  if (g_pair_mode < 0) {
+    const char* e = getenv("OMNI_GEMM_PAIR");
+    g_pair_mode = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return g_pair_mode == 1;
+}
+
+template <int EPI, int MODE>
+constexpr bool pair_supported() {
+  return (MODE == GEMM_DENSE || MODE == GEMM_GROUPED_K) && EPI != EPI_PEER_BF16;
 }
 
 template <bool A_MN, bool B_MN, int EPI, int MODE>
 static void dispatch_bn(const GemmDesc& d, cudaStream_t s) {
-  if (d.block_n == 128)
+  if (d.block_n == 128) {
     launch_impl<128, A_MN, B_MN, EPI, MODE>(d, s);
-  else
-    launch_impl<256, A_MN, B_MN, EPI, MODE>(d, s);
+    return;
+  }
+  if constexpr (pair_supported<EPI, MODE>()) {
+    const bool pair = d.pair == 1 || (d.pair < 0 && gemm_pair_enabled() && d.M > kBM);
+    if (pair) {
+      launch_impl<256, A_MN, B_MN, EPI, MODE, true>(d, s);
+      return;
+    }
+  }
+  launch_impl<256, A_MN, B_MN, EPI, MODE>(d, s);
 }
 
 // Epilogue / layout combinations that training actually uses; others are

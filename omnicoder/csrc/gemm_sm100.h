@@ -31,6 +31,7 @@ struct GemmDesc {
   int mode = GEMM_DENSE;
   int epilogue = EPI_STORE_BF16;
   int block_n = 256;  // 128 or 256
+  int pair = -1;      // CTA-pair (cta_group::2) 256-row tiles: -1 automatic, 0 off, 1 on (block_n 256 only)
   bool a_mn_major = false;
   bool b_mn_major = false;
   int M = 0, N = 0, K = 0;
@@ -66,6 +67,10 @@ struct GemmDesc {
 
 // Launch on `stream`.  Throws std::runtime_error on an invalid description.
 void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream);
+
+// Process-wide switch of the automatic CTA-pair choice (default on unless OMNI_GEMM_PAIR=0).
+void set_gemm_pair(bool on);
+bool gemm_pair_enabled();
 
 // out[r, :] = sum_s staging[s, r, :] (+ residual[r, :]) — the local half of a fused GEMM -> reduce-scatter.
 void tp_reduce_slots(const void* staging, int nsrc, int rows, int D, long long ld, const void* residual,

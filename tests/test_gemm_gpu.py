@@ -150,3 +150,47 @@ def test_grouped_k(cuda_ext):
             assert C[g].abs().max().item() == 0.0
         else:
             assert _rel(C[g], ref) < 1e-2, g
+
+
+@pytest.mark.parametrize("layout", ["kk", "k_mn", "mn_mn"])
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 256), (384, 768, 640), (1000, 264, 136)])
+def test_cta_pair_tiles_match_single_cta(cuda_ext, layout, M, N, K):
+    """256-row CTA-pair tiles (cta_group::2) give the one-CTA kernel's result, including
+    ragged M / N / K edges and more tiles than co-resident pairs."""
+    torch.manual_seed(7)
+    a_mn, b_mn = {"kk": (False, False), "k_mn": (False, True), "mn_mn": (True, True)}[layout]
+    A = _mk(K, M) if a_mn else _mk(M, K)
+    B = _mk(K, N) if b_mn else _mk(N, K)
+    f32 = layout != "k_mn"                  # the (K, MN) layout has bf16 epilogues only
+    out = []
+    try:
+        for pair in (False, True):
+            cuda_ext.set_gemm_pair(pair)
+            C = torch.empty(M, N, device="cuda", dtype=torch.float32 if f32 else torch.bfloat16)
+            cuda_ext.gemm(A, B, C, a_mn, b_mn, EPI_F32 if f32 else EPI_BF16, 1.0, None, None, 256)
+            out.append(C)
+    finally:
+        cuda_ext.set_gemm_pair(True)
+    ref = (A.float().T if a_mn else A.float()) @ (B.float() if b_mn else B.float().T)
+    assert _rel(out[1], ref) < (2e-3 if f32 else 1e-2)
+    assert _rel(out[1], out[0]) < (1e-5 if f32 else 1e-2)
+
+
+def test_cta_pair_grouped_k(cuda_ext):
+    torch.manual_seed(8)
+    G, M, N = 3, 640, 512
+    counts = [384, 0, 1000]
+    off = _offsets(counts)
+    rows = off[-1]
+    A = torch.zeros(rows, M, device="cuda", dtype=torch.bfloat16)
+    B = torch.zeros(rows, N, device="cuda", dtype=torch.bfloat16)
+    for g in range(G):
+        A[off[g]:off[g] + counts[g]] = _mk(counts[g], M)
+        B[off[g]:off[g] + counts[g]] = _mk(counts[g], N)
+    offs = torch.tensor(off, device="cuda", dtype=torch.int32)
+    assert cuda_ext.gemm_pair_enabled()
+    C = torch.full((G, M, N), 3.0, device="cuda", dtype=torch.float32)
+    cuda_ext.gemm_grouped_k(A, B, offs, C, EPI_F32, 1.0, 256)
+    for g in range(G):
+        ref = A[off[g]:off[g + 1]].float().T @ B[off[g]:off[g + 1]].float()
+        assert _rel(C[g], ref) < 2e-3 if counts[g] else C[g].abs().max().item() == 0.0
