@@ -230,6 +230,7 @@ void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   d.max_rows_hint = (int)max_rows_hint;
   d.C = C.data_ptr();
   d.ldc = C.stride(0);
+  d.rows_c = C.size(0);
   d.alpha = (float)alpha;
   CHECK_BF16(C);
   CHECK_ROWMAJOR(C);

@@ -64,6 +64,8 @@ struct GemmArgs {
   int nsrc, me, src_rows;
   int mt_rot;                      // dense raster: rotate the M tiles so a rank starts on its own rows
   void* peer_c[GEMM_MAX_PEERS];
+  int tma_c;                       // bf16 / SwiGLU outputs leave through shared memory + TMA stores
+  int rows_c;                      // rows of C (per group in grouped-K mode)
 };
 
 // Per-source tensor maps of A (GEMM_AG mode; unused otherwise).
@@ -83,7 +85,50 @@ struct Cfg {
   static constexpr int kStageBytes = kStageA + kStageB;
   static constexpr int kStages = PAIR ? 6 : (BN >= 256 ? 4 : 6);
   static constexpr int kTmemCols = 2 * BN;         // double-buffered accumulator
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  // epilogue staging: two [32 rows x 128 B] swizzled boxes per epilogue warp
+  static constexpr int kEpiBox = 4096;
+  static constexpr int kEpiBytes = 4 * 2 * kEpiBox;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+// Epilogue staging of one warp: its 32 accumulator rows, 64 bf16 columns at a time, are
+// written into a 128B-swizzled [32 x 128 B] box in shared memory (conflict-free: lane r
+// writes 16-byte chunk q of its row at chunk q ^ (r & 7)) and leave with one TMA store,
+// so global memory sees whole 128-byte row segments instead of one 16-byte piece per row.
+struct EpiStage {
+  uint8_t* base;  // two 4 KB boxes, 1024-byte aligned
+  int cur;
+  // Next free box (the store issued two boxes ago has finished reading it).
+  __device__ __forceinline__ uint8_t* acquire(int lane) {
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    return base + cur * 4096;
+  }
+  // Row `lane` of the box: 8 chunks of 8 bf16 (packed pairs).
+  __device__ __forceinline__ static void put_row(uint8_t* box, int lane, const uint32_t* w) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<uint4*>(box + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+          make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  }
+  __device__ __forceinline__ void issue_2d(int lane, const CUtensorMap* m, int x, int y) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(m, base + cur * 4096, x, y);
+      bulk_commit_group();
+    }
+    cur ^= 1;
+  }
+  __device__ __forceinline__ void issue_3d(int lane, const CUtensorMap* m, int x, int y, int z) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(m, base + cur * 4096, x, y, z);
+      bulk_commit_group();
+    }
+    cur ^= 1;
+  }
 };
 
 struct TileInfo {
@@ -316,13 +361,16 @@ __device__ __forceinline__ void store_swiglu_bwd(const GemmArgs& p, int row, int
 template <int BN, bool A_MN, bool B_MN, int EPI, int MODE, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ AgMaps ag, GemmArgs p) {
+                      const __grid_constant__ AgMaps ag, const __grid_constant__ CUtensorMap tmC,
+                      const __grid_constant__ CUtensorMap tmH, GemmArgs p) {
   using C_ = Cfg<BN, PAIR>;
   constexpr int S = C_::kStages;
   constexpr int TM = C_::kTM;
+  constexpr bool kTmaEpi = EPI == EPI_STORE_BF16 || EPI == EPI_SWIGLU;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * C_::kStageBytes);
+  uint8_t* epi_smem = smem + S * C_::kStageBytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + C_::kEpiBytes);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;  // [2]
@@ -361,6 +409,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmA);
     }
     tma_prefetch_desc(&tmB);
+    if (kTmaEpi && p.tma_c) {
+      tma_prefetch_desc(&tmC);
+      if (EPI == EPI_SWIGLU && p.H != nullptr) tma_prefetch_desc(&tmH);
+    }
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -501,6 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------ Epilogue ----------------------------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = (int)crank * kBM + quarter * 32 + lane;
+    EpiStage stg{epi_smem + (warp - 2) * 2 * C_::kEpiBox, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = tile0; t < ntiles; t += tile_step) {
@@ -511,7 +564,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < ti.m_limit;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(quarter * 32) << 16);
       const bool zero = ti.num_kb == 0;
-      if (EPI == EPI_SWIGLU) {
+      const int y0 = ti.m0 + (int)crank * kBM + quarter * 32;  // first row of this warp's 32
+      if (kTmaEpi && p.tma_c) {
+        // whole-box stores; a box that starts past the last row or column is skipped, one
+        // that overhangs is clipped by the tensor map
+        const bool rows_ok = y0 < p.rows_c && y0 < ti.m_limit;
+        if (EPI == EPI_STORE_BF16) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; ++c) {
+            float v[64];
+            tmem_ld32(tbase + c * 64, v);
+            tmem_ld32(tbase + c * 64 + 32, v + 32);
+            tc_wait_ld();
+            const int x = ti.n0 + c * 64;
+            if (!rows_ok || x >= p.N) continue;
+            uint32_t w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = zero ? 0u : pack_bf16x2(v[2 * j] * p.alpha, v[2 * j + 1] * p.alpha);
+            uint8_t* box = stg.acquire(lane);
+            EpiStage::put_row(box, lane, w);
+            if (MODE == GEMM_GROUPED_K)
+              stg.issue_3d(lane, &tmC, x, y0, ti.g);
+            else
+              stg.issue_2d(lane, &tmC, x, y0);
+          }
+        } else {
+          // SwiGLU: two 64-column accumulator blocks (gate 32 | up 32 each) make 64 activation
+          // columns; the raw blocks are the saved pre-activation H
+#pragma unroll 1
+          for (int c = 0; c < BN / 64; c += 2) {
+            uint32_t act[32];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float gt[32], up[32];
+              tmem_ld32(tbase + (c + h) * 64, gt);
+              tmem_ld32(tbase + (c + h) * 64 + 32, up);
+              tc_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                act[16 * h + j] = pack_bf16x2(silu_f(gt[2 * j]) * up[2 * j], silu_f(gt[2 * j + 1]) * up[2 * j + 1]);
+              const int xh = ti.n0 + (c + h) * 64;
+              if (p.H != nullptr && rows_ok && xh < p.N) {
+                uint32_t w[32];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  w[j] = pack_bf16x2(gt[2 * j], gt[2 * j + 1]);
+                  w[16 + j] = pack_bf16x2(up[2 * j], up[2 * j + 1]);
+                }
+                uint8_t* box = stg.acquire(lane);
+                EpiStage::put_row(box, lane, w);
+                stg.issue_2d(lane, &tmH, xh, y0);
+              }
+            }
+            const int xa = (ti.n0 + c * 64) >> 1;
+            if (rows_ok && 2 * xa < p.N) {
+              uint8_t* box = stg.acquire(lane);
+              EpiStage::put_row(box, lane, act);
+              stg.issue_2d(lane, &tmC, xa, y0);
+            }
+          }
+        }
+      } else if (EPI == EPI_SWIGLU) {
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
           float gt[32], up[32];
@@ -549,6 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (kTmaEpi && p.tma_c && lane == 0) bulk_wait_group_all();
   }
 
   __syncwarp();
@@ -682,7 +796,47 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
       }
     }
   }
+  // Output tensor maps for the shared-memory + TMA-store epilogue (bf16 outputs whose base
+  // and row stride are 16-byte aligned; otherwise the epilogue stores rows directly).
+  constexpr bool kTmaEpi = EPI == EPI_STORE_BF16 || EPI == EPI_SWIGLU;
+  CUtensorMap tmC, tmH;
+  memset(&tmC, 0, sizeof(tmC));
+  memset(&tmH, 0, sizeof(tmH));
+  const long long rows_c = d.rows_c > 0 ? d.rows_c : d.M;
+  int tma_c = 0;
+  static const bool tma_epi_on = [] {
+    const char* e = getenv("OMNI_GEMM_TMA_EPI");  // "0": rows stored directly from registers
+    return !(e != nullptr && e[0] == '0');
+  }();
+  if (kTmaEpi && tma_epi_on) {
+    auto al16 = [](const void* ptr, long long ld) {
+      return ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && (ld * 2) % 16 == 0;
+    };
+    const long long cols_c = EPI == EPI_SWIGLU ? d.N / 2 : d.N;
+    bool ok = al16(d.C, d.ldc) && (MODE != GEMM_GROUPED_K || (d.c_group_stride * 2) % 16 == 0);
+    if (EPI == EPI_SWIGLU && d.H != nullptr) ok = ok && al16(d.H, d.ldh);
+    if (ok) {
+      uint32_t box[3] = {64, 32, 1};
+      if (MODE == GEMM_GROUPED_K) {
+        uint64_t dims[3] = {(uint64_t)cols_c, (uint64_t)rows_c, (uint64_t)d.num_groups};
+        uint64_t str[2] = {(uint64_t)d.ldc * 2, (uint64_t)d.c_group_stride * 2};
+        tmC = make_tmap_bf16_sw128(d.C, 3, dims, str, box);
+      } else {
+        uint64_t dims[2] = {(uint64_t)cols_c, (uint64_t)rows_c};
+        uint64_t str[1] = {(uint64_t)d.ldc * 2};
+        tmC = make_tmap_bf16_sw128(d.C, 2, dims, str, box);
+        if (EPI == EPI_SWIGLU && d.H != nullptr) {
+          uint64_t hd[2] = {(uint64_t)d.N, (uint64_t)rows_c};
+          uint64_t hs[1] = {(uint64_t)d.ldh * 2};
+          tmH = make_tmap_bf16_sw128(d.H, 2, hd, hs, box);
+        }
+      }
+      tma_c = 1;
+    }
+  }
   GemmArgs p;
+  p.tma_c = tma_c;
+  p.rows_c = (int)rows_c;
   p.M = d.M;
   p.N = d.N;
   p.K = d.K;
@@ -757,10 +911,10 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, ag, p);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, ag, tmC, tmH, p);
     if (e != cudaSuccess) throw std::runtime_error(std::string("omnicoder gemm: pair launch failed: ") + cudaGetErrorString(e));
   } else {
-    kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(tmA, tmB, ag, p);
+    kern<<<grid, kThreads, C_::kSmemBytes, stream>>>(tmA, tmB, ag, tmC, tmH, p);
   }
 }
 
@@ -877,6 +1031,20 @@ void tp_reduce_slots(const void* staging, int nsrc, int rows, int D, long long l
 }
 
 void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream) {
+  // The epilogues move 16-byte vectors (or 16-byte-aligned TMA boxes): every output / residual
+  // row must start on a 16-byte boundary.
+  {
+    const int c_elem = (d.epilogue == EPI_STORE_F32 || d.epilogue == EPI_ACCUM_F32) ? 4 : 2;
+    auto aligned = [](const void* ptr, long long ld, int elem) {
+      return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && (ld * elem) % 16 == 0);
+    };
+    if (d.epilogue != EPI_PEER_BF16 && !aligned(d.C, d.ldc, c_elem))
+      throw std::runtime_error("omnicoder gemm: output base and row stride must be 16-byte aligned");
+    if (d.mode == GEMM_GROUPED_K && (d.c_group_stride * c_elem) % 16 != 0)
+      throw std::runtime_error("omnicoder gemm: output group stride must be 16-byte aligned");
+    if (!aligned(d.R, d.ldr, 2) || !aligned(d.H, d.ldh, 2))
+      throw std::runtime_error("omnicoder gemm: residual / pre-activation rows must be 16-byte aligned");
+  }
   if (d.epilogue == EPI_PEER_BF16 &&
       (d.nsrc < 1 || d.nsrc > GEMM_MAX_PEERS || d.src_rows <= 0 || d.src_rows % kBM != 0 || d.M != d.nsrc * d.src_rows))
     throw std::runtime_error("omnicoder gemm: peer-store epilogue needs M = ranks x src_rows, src_rows % 128 == 0");

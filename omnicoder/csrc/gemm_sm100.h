@@ -50,6 +50,7 @@ struct GemmDesc {
   int max_rows_hint = 0;               // grouped-M: upper bound on total rows (0 = unknown)
   void* C = nullptr;
   long long ldc = 0;
+  long long rows_c = 0;  // rows of C (0: M); grouped-M outputs are as tall as A
   long long c_group_stride = 0;
   const void* R = nullptr;
   long long ldr = 0;
@@ -105,6 +106,7 @@ struct Fp8GemmDesc {
   const float* sw = nullptr;
   void* C = nullptr;
   long long ldc = 0;
+  long long rows_c = 0;  // rows of C (0: M); grouped-M outputs are as tall as A
   void* status = nullptr;
 };
 void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream);

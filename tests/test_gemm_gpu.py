@@ -194,3 +194,43 @@ def test_cta_pair_grouped_k(cuda_ext):
     for g in range(G):
         ref = A[off[g]:off[g + 1]].float().T @ B[off[g]:off[g + 1]].float()
         assert _rel(C[g], ref) < 2e-3 if counts[g] else C[g].abs().max().item() == 0.0
+
+
+@pytest.mark.parametrize("ldc_pad", [0, 8])
+def test_bf16_epilogue_strided_output(cuda_ext, ldc_pad):
+    """bf16 outputs leave through shared memory + TMA stores into a strided view; columns
+    past N stay untouched."""
+    torch.manual_seed(9)
+    M, N, K = 640, 320, 512
+    A, B = _mk(M, K), _mk(N, K)
+    full = torch.full((M, N + ldc_pad), 5.0, device="cuda", dtype=torch.bfloat16)
+    C = full[:, :N]
+    cuda_ext.gemm(A, B, C, False, False, EPI_BF16, 1.0, None, None, 256)
+    assert _rel(C, A.float() @ B.float().T) < 1e-2
+    if ldc_pad:
+        assert (full[:, N:] == 5.0).all()
+
+
+def test_unaligned_output_rows_are_rejected(cuda_ext):
+    """An output whose rows do not start on 16-byte boundaries is refused on the host
+    (the epilogue writes 16-byte vectors); nothing is launched."""
+    A, B = _mk(256, 64), _mk(320, 64)
+    C = torch.zeros(256, 325, device="cuda", dtype=torch.bfloat16)[:, :320]
+    with pytest.raises(RuntimeError, match="16-byte"):
+        cuda_ext.gemm(A, B, C, False, False, EPI_BF16, 1.0, None, None, 256)
+    torch.cuda.synchronize()
+
+
+def test_swiglu_epilogue_partial_tile(cuda_ext):
+    """SwiGLU outputs (activation and saved pre-activation) on a tile that overhangs N and M."""
+    torch.manual_seed(10)
+    T, D, F = 200, 256, 96                  # 2F = 192 accumulator columns: one partial 256-wide tile
+    x = _mk(T, D)
+    w1, w3 = _mk(F, D, scale=0.05), _mk(F, D, scale=0.05)
+    w13 = _interleave(w1, w3)
+    act = torch.empty(T, F, device="cuda", dtype=torch.bfloat16)
+    H = torch.empty(T, 2 * F, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(x, w13, act, False, False, EPI_SWIGLU, 1.0, None, H, 256)
+    ref = torch.nn.functional.silu(x.float() @ w1.float().T) * (x.float() @ w3.float().T)
+    assert _rel(act, ref) < 2e-2
+    assert _rel(H, x.float() @ w13.float().T) < 1e-2
