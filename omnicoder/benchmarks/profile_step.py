@@ -27,11 +27,12 @@ from omnicoder.training.engine import Trainer, synthetic_batch
 def family(name: str) -> str:
     n = name
     if "gemm_sm100_kernel" in n:
-        mode = re.search(r"gemm_sm100_kernel<(\d+), (\w+), (\w+), (\d+), (\d+)>", n)
+        mode = re.search(r"gemm_sm100_kernel<(\d+), (\w+), (\w+), (\d+), (\d+)(?:, (\w+))?>", n)
         if mode:
-            bn, amn, bmn, epi, md = mode.groups()
-            kind = {"0": "dense", "1": "grouped_m", "2": "grouped_k"}[md]
-            return f"gemm[{kind} a_mn={amn[0]} b_mn={bmn[0]} epi={epi} bn={bn}]"
+            bn, amn, bmn, epi, md, pair = mode.groups()
+            kind = {"0": "dense", "1": "grouped_m", "2": "grouped_k", "3": "allgather"}[md]
+            pair = " pair" if pair == "true" else ""
+            return f"gemm[{kind} a_mn={amn[0]} b_mn={bmn[0]} epi={epi} bn={bn}{pair}]"
         return "gemm"
     for key in ("attn_fwd_kernel", "attn_dkdv_kernel", "attn_dq_kernel", "attn_delta_kernel", "rmsnorm_fwd",
                 "rmsnorm_bwd", "rope_kernel", "embedding_fwd", "embedding_bwd", "ce_kernel", "adamw_kernel",

@@ -167,6 +167,13 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* desc, ui
       : "memory");
 }
 
+// Bring a tile of a tensor into L2 (no shared memory, no completion to wait for).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* desc, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(desc)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 // Tiled bulk store shared -> global, tracked by this thread's bulk async-group.
 // The box is clipped at the tensor's bounds; callers never start one at a negative
 // coordinate.
@@ -483,6 +490,6 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 }  // namespace omni

@@ -367,6 +367,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int S = C_::kStages;
   constexpr int TM = C_::kTM;
   constexpr bool kTmaEpi = EPI == EPI_STORE_BF16 || EPI == EPI_SWIGLU;
+  // epilogues with a bf16 side input (residual R, or the saved SwiGLU pre-activation H)
+  constexpr bool kTmaIn = EPI == EPI_ADD_BF16 || EPI == EPI_SWIGLU_BWD;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi_smem = smem + S * C_::kStageBytes;
@@ -375,7 +377,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull_bar = empty_bar + S;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;  // [2]
   uint64_t* drain_bar = tempty_bar + 2;  // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* in_bar = drain_bar + 1;      // [4 warps x 2 boxes] side-input (residual / H) box loads
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(in_bar + 8);
   __shared__ int s_off[GEMM_MAX_GROUPS + 1];
 
   const int warp = warp_id();
@@ -400,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty_bar[b], PAIR ? 8 : 4);  // every epilogue warp of the tile's CTAs
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(&in_bar[i], 1);
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -409,9 +413,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmA);
     }
     tma_prefetch_desc(&tmB);
-    if (kTmaEpi && p.tma_c) {
+    if ((kTmaEpi || kTmaIn) && p.tma_c) {
       tma_prefetch_desc(&tmC);
-      if (EPI == EPI_SWIGLU && p.H != nullptr) tma_prefetch_desc(&tmH);
+      if ((EPI == EPI_SWIGLU && p.H != nullptr) || kTmaIn) tma_prefetch_desc(&tmH);
     }
   }
   if (warp == 1) {
@@ -554,18 +558,105 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = (int)crank * kBM + quarter * 32 + lane;
     EpiStage stg{epi_smem + (warp - 2) * 2 * C_::kEpiBox, 0};
+    uint64_t* wbar = in_bar + (warp - 2) * 2;  // this warp's two box-load barriers
+    uint32_t in_phase = 0;                     // bit b: parity of box b's next load completion
+    int in_box = 0;                            // box of the next side-input chunk
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = tile0; t < ntiles; t += tile_step) {
       const TileInfo ti = tile_info<BN, MODE, TM>(p, t, s_off);
+      const int y0 = ti.m0 + (int)crank * kBM + quarter * 32;  // first row of this warp's 32
+      // Side-input epilogue, one box (32 rows x 64 bf16 columns) per chunk: the box of R (or
+      // H) is loaded by TMA into shared memory one chunk ahead, combined with the
+      // accumulator in place and stored back out with TMA.  The residual chunk is 64
+      // accumulator columns; the SwiGLU-backward chunk is 32 dAct columns, whose H / dH
+      // columns (gate 32 | up 32) fill one box.  The whole tile's side input is requested
+      // into L2, and the first box into shared memory, before the accumulator is ready.
+      constexpr int kChunk = EPI == EPI_SWIGLU_BWD ? 32 : 64;
+      int nvalid = 0;
+      if (kTmaIn && p.tma_c && y0 < p.rows_c && y0 < ti.m_limit && ti.n0 < p.N)
+        nvalid = min(BN / kChunk, (p.N - ti.n0 + kChunk - 1) / kChunk);
+      auto box_x = [&](int c) { return EPI == EPI_SWIGLU_BWD ? 2 * (ti.n0 + c * kChunk) : ti.n0 + c * kChunk; };
+      auto load_box = [&](int c, int b) {
+        if (lane == 0) {
+          bulk_wait_group_read<0>();  // the store that last used this box has read it
+          mbar_arrive_expect_tx(&wbar[b], C_::kEpiBox);
+          tma_load_2d(stg.base + b * C_::kEpiBox, &tmH, &wbar[b], box_x(c), y0);
+        }
+        __syncwarp();
+      };
+      if (kTmaIn && nvalid > 0) {
+        if (lane == 0)
+          for (int c = 1; c < nvalid; ++c) tma_prefetch_l2_2d(&tmH, box_x(c), y0);
+        load_box(0, in_box);
+      }
       if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, STATUS_TIMEOUT_TMEM_FULL)) break;
       tc_fence_after();
       const int row = ti.m0 + row_in_tile;
       const bool row_ok = row < ti.m_limit;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(quarter * 32) << 16);
       const bool zero = ti.num_kb == 0;
-      const int y0 = ti.m0 + (int)crank * kBM + quarter * 32;  // first row of this warp's 32
-      if (kTmaEpi && p.tma_c) {
+      if (kTmaIn && p.tma_c) {
+#pragma unroll 1
+        for (int c = 0; c < nvalid; ++c) {
+          const int b = (in_box + c) & 1;
+          if (c + 1 < nvalid) load_box(c + 1, b ^ 1);
+          float v[kChunk];
+          tmem_ld32(tbase + c * kChunk, v);
+          if constexpr (kChunk == 64) tmem_ld32(tbase + c * kChunk + 32, v + 32);
+          tc_wait_ld();
+          if (!mbar_wait(&wbar[b], (in_phase >> b) & 1u, p.status, STATUS_TIMEOUT_TMA_FULL)) break;
+          in_phase ^= 1u << b;
+          uint8_t* box = stg.base + b * C_::kEpiBox + lane * 128;
+          uint32_t w[32];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 r4 = *reinterpret_cast<const uint4*>(box + ((q ^ (lane & 7)) << 4));
+            w[4 * q] = r4.x;
+            w[4 * q + 1] = r4.y;
+            w[4 * q + 2] = r4.z;
+            w[4 * q + 3] = r4.w;
+          }
+          if (EPI == EPI_ADD_BF16) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float a0 = zero ? 0.f : v[2 * j] * p.alpha, a1 = zero ? 0.f : v[2 * j + 1] * p.alpha;
+              w[j] = pack_bf16x2(a0 + bf16_lo(w[j]), a1 + bf16_hi(w[j]));
+            }
+          } else {
+            // w[0..16) = gate (32 values), w[16..32) = up; out: dgate | dup
+            uint32_t o[32];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float r[2], sgl[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const float g = h ? bf16_hi(w[j]) : bf16_lo(w[j]);
+                const float u = h ? bf16_hi(w[16 + j]) : bf16_lo(w[16 + j]);
+                const float d = zero ? 0.f : v[2 * j + h] * p.alpha;
+                const float sg = __fdividef(1.0f, 1.0f + __expf(-g));
+                sgl[h] = d * g * sg;                              // d/du
+                r[h] = d * u * (sg * (1.0f + g * (1.0f - sg)));  // d/dg
+              }
+              o[j] = pack_bf16x2(r[0], r[1]);
+              o[16 + j] = pack_bf16x2(sgl[0], sgl[1]);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = o[j];
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4*>(box + ((q ^ (lane & 7)) << 4)) =
+                make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stg.base + b * C_::kEpiBox, box_x(c), y0);
+            bulk_commit_group();
+          }
+        }
+        in_box = (in_box + nvalid) & 1;
+      } else if (kTmaEpi && p.tma_c) {
         // whole-box stores; a box that starts past the last row or column is skipped, one
         // that overhangs is clipped by the tensor map
         const bool rows_ok = y0 < p.rows_c && y0 < ti.m_limit;
@@ -662,7 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
-    if (kTmaEpi && p.tma_c && lane == 0) bulk_wait_group_all();
+    if ((kTmaEpi || kTmaIn) && p.tma_c && lane == 0) bulk_wait_group_all();
   }
 
   __syncwarp();
@@ -799,6 +890,7 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
   // Output tensor maps for the shared-memory + TMA-store epilogue (bf16 outputs whose base
   // and row stride are 16-byte aligned; otherwise the epilogue stores rows directly).
   constexpr bool kTmaEpi = EPI == EPI_STORE_BF16 || EPI == EPI_SWIGLU;
+  constexpr bool kTmaIn = EPI == EPI_ADD_BF16 || EPI == EPI_SWIGLU_BWD;
   CUtensorMap tmC, tmH;
   memset(&tmC, 0, sizeof(tmC));
   memset(&tmH, 0, sizeof(tmH));
@@ -808,6 +900,17 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
     const char* e = getenv("OMNI_GEMM_TMA_EPI");  // "0": rows stored directly from registers
     return !(e != nullptr && e[0] == '0');
   }();
+  if (kTmaIn && tma_epi_on && MODE != GEMM_GROUPED_K && d.R != nullptr) {
+    // side-input epilogues: R / H read and C written as [rows, cols] bf16 boxes
+    const long long cols = EPI == EPI_SWIGLU_BWD ? 2LL * d.N : d.N;
+    uint32_t box[2] = {64, 32};
+    uint64_t cd[2] = {(uint64_t)cols, (uint64_t)rows_c};
+    uint64_t cs[1] = {(uint64_t)d.ldc * 2};
+    uint64_t rs[1] = {(uint64_t)d.ldr * 2};
+    tmC = make_tmap_bf16_sw128(d.C, 2, cd, cs, box);
+    tmH = make_tmap_bf16_sw128(d.R, 2, cd, rs, box);
+    tma_c = 1;
+  }
   if (kTmaEpi && tma_epi_on) {
     auto al16 = [](const void* ptr, long long ld) {
       return ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && (ld * 2) % 16 == 0;

@@ -234,3 +234,45 @@ def test_swiglu_epilogue_partial_tile(cuda_ext):
     ref = torch.nn.functional.silu(x.float() @ w1.float().T) * (x.float() @ w3.float().T)
     assert _rel(act, ref) < 2e-2
     assert _rel(H, x.float() @ w13.float().T) < 1e-2
+
+
+@pytest.mark.parametrize("inplace", [False, True])
+def test_residual_epilogue_ragged(cuda_ext, inplace):
+    """Residual epilogue (R boxes loaded by TMA one chunk ahead) on tiles overhanging M and N."""
+    torch.manual_seed(11)
+    M, N, K = 300, 200, 256
+    A, B, R = _mk(M, K), _mk(N, K), _mk(M, N)
+    ref = A.float() @ B.float().T + R.float()
+    C = R.clone() if inplace else torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm(A, B, C, False, False, EPI_ADD, 1.0, C if inplace else R, None, 256)
+    assert _rel(C, ref) < 1e-2
+
+
+def test_grouped_m_swiglu_bwd(cuda_ext):
+    """SwiGLU-backward epilogue of the grouped expert GEMM (H boxes loaded by TMA)."""
+    torch.manual_seed(12)
+    G, D, F = 3, 256, 192
+    counts = [130, 0, 256]
+    off = _offsets(counts)
+    rows = off[-1]
+    dy = torch.zeros(rows, D, device="cuda", dtype=torch.bfloat16)
+    H = torch.zeros(rows, 2 * F, device="cuda", dtype=torch.bfloat16)
+    for g in range(G):
+        dy[off[g]:off[g] + counts[g]] = _mk(counts[g], D)
+        H[off[g]:off[g] + counts[g]] = _mk(counts[g], 2 * F)
+    w2 = _mk(G, D, F, scale=0.05)                          # [G, K = D, N = F]
+    offs = torch.tensor(off, device="cuda", dtype=torch.int32)
+    dH = torch.zeros(rows, 2 * F, device="cuda", dtype=torch.bfloat16)
+    cuda_ext.gemm_grouped_m(dy, w2, offs, dH, True, EPI_SWIGLU_BWD, 1.0, H, None, 256, rows)
+    for g in range(G):
+        if counts[g] == 0:
+            continue
+        sl = slice(off[g], off[g] + counts[g])
+        da = dy[sl].float() @ w2[g].float()
+        Hf = H[sl].float().view(-1, F // 32, 2, 32)
+        gg, uu = Hf[:, :, 0].reshape(-1, F), Hf[:, :, 1].reshape(-1, F)
+        sg = torch.sigmoid(gg)
+        dg = da * uu * sg * (1 + gg * (1 - sg))
+        du = da * gg * sg
+        ref = torch.stack([dg.view(-1, F // 32, 32), du.view(-1, F // 32, 32)], 2).reshape(-1, 2 * F)
+        assert _rel(dH[sl], ref) < 2e-2, g
