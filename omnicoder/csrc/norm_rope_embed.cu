@@ -134,8 +134,85 @@ __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ x, const bf16* __res
   for (int i = threadIdx.x; i < dim; i += blockDim.x) atomicAdd(&dw[i], s_dw[i]);
 }
 
+// Same, for dim = NC * 256 <= 2048: each warp accumulates dw for its rows in its own
+// shared-memory row (lane owns columns lane*8 + 256k, so no atomics), and the block sums its
+// warps' rows once at the end (the general kernel above does a shared-memory atomic per
+// element).
+template <int NC>
+__global__ void __launch_bounds__(128) rmsnorm_bwd_warp_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                               const float* __restrict__ rstd, const bf16* __restrict__ dy,
+                                                               const bf16* __restrict__ dres, bf16* __restrict__ dx,
+                                                               float* __restrict__ dw, int rows) {
+  constexpr int dim = NC * 256;
+  constexpr int kWarps = 4;
+  __shared__ __align__(16) float s_acc[kWarps][dim];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int i = lane * 4; i < dim; i += 128) *reinterpret_cast<float4*>(&s_acc[warp][i]) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
+  for (int row = blockIdx.x * kWarps + warp; row < rows; row += gridDim.x * kWarps) {
+    const long long base = (long long)row * dim + lane * 8;
+    const float rs = rstd[row];
+    float dot = 0.f;
+#pragma unroll 2
+    for (int k = 0; k < NC; ++k) {
+      float wv[8], xh[8], g[8];
+      load8(w + k * 256 + lane * 8, wv);
+      load8(x + base + k * 256, xh);
+      load8(dy + base + k * 256, g);
+      float4* a = reinterpret_cast<float4*>(&s_acc[warp][k * 256 + lane * 8]);
+      float4 a0 = a[0], a1 = a[1];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xh[i] *= rs;
+        dot += xh[i] * wv[i] * g[i];
+      }
+      a0.x += g[0] * xh[0]; a0.y += g[1] * xh[1]; a0.z += g[2] * xh[2]; a0.w += g[3] * xh[3];
+      a1.x += g[4] * xh[4]; a1.y += g[5] * xh[5]; a1.z += g[6] * xh[6]; a1.w += g[7] * xh[7];
+      a[0] = a0;
+      a[1] = a1;
+    }
+    dot = warp_sum(dot) / (float)dim;
+#pragma unroll 2
+    for (int k = 0; k < NC; ++k) {  // second pass over the row: its 4 KB are still in L1
+      float wv[8], xh[8], g[8], o[8];
+      load8(w + k * 256 + lane * 8, wv);
+      load8(x + base + k * 256, xh);
+      load8(dy + base + k * 256, g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = rs * (wv[i] * g[i] - xh[i] * rs * dot);
+      if (dres != nullptr) {
+        float e[8];
+        load8(dres + base + k * 256, e);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] += e[i];
+      }
+      store8(dx + base + k * 256, o);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int v = 0; v < kWarps; ++v) t += s_acc[v][i];
+    atomicAdd(&dw[i], t);
+  }
+}
+
 void rmsnorm_bwd(const void* x, const void* w, const float* rstd, const void* dy, const void* dres, void* dx,
                  float* dw, int rows, int dim, cudaStream_t s) {
+  if (dim == 512 || dim == 1024 || dim == 2048) {
+    int grid = (rows + 3) / 4;
+    if (grid > 148 * 6) grid = 148 * 6;
+    auto launch = [&](auto kern) {
+      kern<<<grid, 128, 0, s>>>((const bf16*)x, (const bf16*)w, rstd, (const bf16*)dy, (const bf16*)dres, (bf16*)dx,
+                                dw, rows);
+    };
+    if (dim == 512) launch(rmsnorm_bwd_warp_kernel<2>);
+    else if (dim == 1024) launch(rmsnorm_bwd_warp_kernel<4>);
+    else launch(rmsnorm_bwd_warp_kernel<8>);
+    return;
+  }
   const int warps = 8;
   int grid = (rows + warps - 1) / warps;
   if (grid > 148 * 4) grid = 148 * 4;

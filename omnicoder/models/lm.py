@@ -25,8 +25,8 @@ import torch
 import torch.nn as nn
 
 from ..config import ModelConfig
-from ..ops import (RopeTable, apply_rope, attention, embedding, layer_norm, linear, linear_rope, lm_head_cross_entropy,
-                   moe_ffn, rms_norm, swiglu_mlp)
+from ..ops import (RopeTable, apply_rope, attention, attention_kv, embedding, layer_norm, linear, linear_rope,
+                   lm_head_cross_entropy, moe_ffn, rms_norm, split_norm, swiglu_mlp)
 from ..ops.decode import decode_attention
 from ..ops.gemm import interleave_gate_up, split_gate_up
 
@@ -156,12 +156,9 @@ class MLAttention(nn.Module):
 
     def latent(self, y, rope: RopeTable, positions):
         """Compressed KV of the tokens: (normalised latent c [T, r], rotated rope key [T, dr])."""
-        T = y.shape[0]
         kva = linear_rope(y, self.wkv_a, rope, positions, self.r + self.dr, 1, off=self.r,
                           interleaved=self.cfg.attn.rope_interleaved)
-        c = rms_norm(kva[:, :self.r].contiguous(), self.kv_norm, self.cfg.norm_eps)
-        kr = kva[:, self.r:].contiguous()
-        return c, kr
+        return split_norm(kva, self.kv_norm, self.r, self.cfg.norm_eps)
 
     def qkv_latent(self, y, rope: RopeTable, positions):
         """(q, k_nope view, v view, rope key, latent c) of tokens y."""
@@ -176,10 +173,14 @@ class MLAttention(nn.Module):
         return self.qkv_latent(y, rope, positions)[:4]
 
     def forward(self, y, h, rope, positions, seq):
-        q, k, v, kr = self.qkv(y, rope, positions)
-        o = attention(q, k, v, kr, seq=seq, causal=True, window=self.cfg.attn.window,
-                      scale=1.0 / math.sqrt(self.dn + self.dr))
-        return linear(o.reshape(y.shape[0], -1), self.wo, residual=h)
+        T = y.shape[0]
+        q = linear_rope(y, self.wq, rope, positions, self.dn + self.dr, self.H, off=self.dn,
+                        interleaved=self.cfg.attn.rope_interleaved).view(T, self.H, self.dn + self.dr)
+        c, kr = self.latent(y, rope, positions)
+        kv = linear(c, self.wkv_b).view(T, self.H, self.dn + self.dv)
+        o = attention_kv(q, kv, self.dn, kr, seq=seq, causal=True, window=self.cfg.attn.window,
+                         scale=1.0 / math.sqrt(self.dn + self.dr))
+        return linear(o.reshape(T, -1), self.wo, residual=h)
 
     @torch.no_grad()
     def prepare_inference(self):

@@ -97,6 +97,41 @@ class _FlashAttnFn(torch.autograd.Function):
         return grads[0], grads[1], grads[2], dk_rope, None, None, None, None
 
 
+class _FlashAttnKVFn(torch.autograd.Function):
+    """Attention whose keys and values are the two column blocks of one tensor kv
+    [T, Hk, dk + dv] (the MLA key/value up-projection).  Backward writes dK and dV
+    straight into one gradient of kv, so autograd adds no zero-filled slice gradients."""
+
+    @staticmethod
+    def forward(ctx, q, kv, dk, k_rope, seq, causal, window, scale):
+        C = _ext.load()
+        k, v = kv[:, :, :dk], kv[:, :, dk:]
+        o, lse = C.attn_fwd(q, k, v, k_rope, seq, causal, window, scale)
+        ctx.save_for_backward(q, kv, k_rope if k_rope is not None else torch.empty(0, device=q.device), o, lse)
+        ctx.has_rope = k_rope is not None
+        ctx.cfg = (dk, seq, causal, window, scale)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, kv, k_rope, o, lse = ctx.saved_tensors
+        dk, seq, causal, window, scale = ctx.cfg
+        C = _ext.load()
+        dkv = torch.empty_like(kv)
+        grads = C.attn_bwd(q, kv[:, :, :dk], kv[:, :, dk:], k_rope if ctx.has_rope else None, o, lse, do.contiguous(),
+                           seq, causal, window, scale, None, dkv[:, :, :dk], dkv[:, :, dk:])
+        return grads[0], dkv, None, (grads[3] if ctx.has_rope else None), None, None, None, None
+
+
+def attention_kv(q: torch.Tensor, kv: torch.Tensor, dk: int, k_rope: torch.Tensor | None = None, *, seq: int,
+                 causal: bool = True, window: int = 0, scale: float | None = None) -> torch.Tensor:
+    """attention(q, kv[..., :dk], kv[..., dk:], k_rope) with a single gradient for kv."""
+    sc = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not q.is_cuda:
+        return attention_torch(q, kv[:, :, :dk], kv[:, :, dk:], k_rope, seq=seq, causal=causal, window=window, scale=sc)
+    return _FlashAttnKVFn.apply(q, kv, dk, k_rope, seq, causal, window, sc)
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_rope: torch.Tensor | None = None, *, seq: int,
               causal: bool = True, window: int = 0, scale: float | None = None, mem_k=None, mem_v=None):
     sc = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])

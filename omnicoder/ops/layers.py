@@ -85,6 +85,37 @@ class _RMSNormFn(torch.autograd.Function):
         return dx, dwt, None, None
 
 
+class _SplitNormFn(torch.autograd.Function):
+    """(rms_norm(x[:, :n]) * w, x[:, n:]) of x [T, n + m] with one gradient for x."""
+
+    @staticmethod
+    def forward(ctx, x, w, n, eps):
+        C = _ext.load()
+        xa = x[:, :n].contiguous()
+        y, rstd = C.rmsnorm_fwd(xa, None, w, eps)
+        ctx.save_for_backward(xa, w, rstd)
+        ctx.m = x.shape[1] - n
+        return y, x[:, n:].contiguous()
+
+    @staticmethod
+    def backward(ctx, dy, dtail):
+        xa, w, rstd = ctx.saved_tensors
+        C = _ext.load()
+        if dy is None:
+            dy = torch.zeros_like(xa)
+        dx, dw = C.rmsnorm_bwd(xa, w, rstd, dy.contiguous(), None)
+        if dtail is None:
+            dtail = torch.zeros(xa.shape[0], ctx.m, device=xa.device, dtype=xa.dtype)
+        return torch.cat([dx, dtail], dim=1), dw.to(w.dtype), None, None
+
+
+def split_norm(x: torch.Tensor, w: torch.Tensor, n: int, eps: float = 1e-6):
+    """(RMSNorm of the first n columns of x, the remaining columns), both contiguous."""
+    if not x.is_cuda:
+        return rms_norm(x[:, :n], w, eps), x[:, n:]
+    return _SplitNormFn.apply(x, w, n, eps)
+
+
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, residual: torch.Tensor | None = None):
     """RMSNorm(x (+ residual)) * w.  With `residual` returns (y, h) where h = x + residual."""
     if not x.is_cuda:

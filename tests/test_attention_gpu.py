@@ -54,3 +54,25 @@ def test_attention_fwd_bwd(cuda_ext, name, B, S, H, Hk, Dk, Dr, Dv, window):
     assert _rel(v.grad, vf.grad) < 3e-2, "dv"
     if kr is not None:
         assert _rel(kr.grad, krf.grad) < 3e-2, "dk_rope"
+
+
+def test_attention_kv_single_gradient_matches_views():
+    """attention_kv (keys/values as column blocks of one tensor, one gradient buffer) gives
+    the gradients of attention() on the two views."""
+    from omnicoder.ops import attention, attention_kv
+    torch.manual_seed(3)
+    T, H, dn, dr, dv, seq = 512, 4, 128, 64, 128, 256
+    q = (torch.randn(T, H, dn + dr, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_()
+    kv = (torch.randn(T, H, dn + dv, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_()
+    kr = (torch.randn(T, dr, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_()
+    g = torch.randn(T, H, dv, device="cuda").to(torch.bfloat16)
+    o1 = attention_kv(q, kv, dn, kr, seq=seq, causal=True)
+    o1.backward(g)
+    grads1 = [t.grad.clone() for t in (q, kv, kr)]
+    for t in (q, kv, kr):
+        t.grad = None
+    o2 = attention(q, kv[:, :, :dn], kv[:, :, dn:], kr, seq=seq, causal=True)
+    o2.backward(g)
+    assert torch.equal(o1, o2)
+    for a, t in zip(grads1, (q, kv, kr)):
+        assert torch.equal(a, t.grad)

@@ -14,11 +14,12 @@ def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-6)).item()
 
 
-def test_rmsnorm_residual_fwd_bwd(cuda_ext):
+@pytest.mark.parametrize("rows,dim", [(300, 512), (1000, 2048), (77, 1024), (64, 384)])
+def test_rmsnorm_residual_fwd_bwd(cuda_ext, rows, dim):
     torch.manual_seed(0)
-    x = torch.randn(300, 512, device="cuda").to(torch.bfloat16).requires_grad_()
-    r = torch.randn(300, 512, device="cuda").to(torch.bfloat16).requires_grad_()
-    w = (1 + 0.1 * torch.randn(512, device="cuda")).to(torch.bfloat16).requires_grad_()
+    x = torch.randn(rows, dim, device="cuda").to(torch.bfloat16).requires_grad_()
+    r = torch.randn(rows, dim, device="cuda").to(torch.bfloat16).requires_grad_()
+    w = (1 + 0.1 * torch.randn(dim, device="cuda")).to(torch.bfloat16).requires_grad_()
     y, h = ops.rms_norm(x, w, 1e-6, residual=r)
     xf, rf, wf = (t.detach().float().requires_grad_() for t in (x, r, w))
     hf = xf + rf
