@@ -27,7 +27,7 @@ from omnicoder.ops import _ext
 
 
 def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, gen=512, kv="int8", spec=0,
-        prefill_chunk=4, layers=0, graphs=True, seed=0, device=None):
+        prefill_chunk=4, layers=0, graphs=True, seed=0, device=None, profile_steps=0):
     """One long-context batched generation; returns the result dict (device-timed with CUDA events)."""
     dev = device or torch.device("cuda")
     _ext.load()
@@ -105,6 +105,7 @@ def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, ge
             step_ms.append(s0.elapsed_time(s1))
             produced += n_new
     _ext.check_status()
+    breakdown = _profile_decode(fwd_t, last, profile_steps) if profile_steps and draft is None else None
     decode_s = sum(step_ms) / 1000.0
     res = {
         "metric": "long-context MoE inference (prefill tokens/s, decode tokens/s, p50 TPOT)",
@@ -117,9 +118,28 @@ def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, ge
         "p50_tpot_ms": statistics.median(step_ms) * len(step_ms) / max(1, produced - 1),
         "memory_rows": n_mem, "kv_cache_gb": cache.nbytes() / 1e9,
         "draft_acceptance": (accepted / proposed) if proposed else None, "cuda_graphs": graphs,
+        "decode_kernel_breakdown_ms_per_step": breakdown,
         "data": "synthetic (uniform random prompts, random-init N(0,0.02) weights)", "dtype": "bf16 weights",
     }
     return res
+
+
+def _profile_decode(step, last, n):
+    """Kernel time per family over n more decode steps (PyTorch profiler; shares, not a bench number)."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    from omnicoder.benchmarks.profile_step import family
+    with torch.no_grad(), profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            last = step(last[:, None])[:, -1].argmax(-1)
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(float)
+    for e in prof.events():
+        if e.device_type is not None and str(e.device_type).endswith("CUDA"):
+            agg[family(e.name)] += (e.device_time_total if hasattr(e, "device_time_total") else e.cuda_time_total) / 1e3
+    return {k: round(v / n, 4) for k, v in sorted(agg.items(), key=lambda kv: -kv[1])}
 
 
 def main(argv=None):
@@ -135,8 +155,10 @@ def main(argv=None):
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (quick runs only)")
     ap.add_argument("--no-graphs", dest="graphs", action="store_false", help="run decode steps eagerly")
     ap.add_argument("--json", default=None)
+    ap.add_argument("--profile", type=int, default=0, help="profile this many extra decode steps (kernel shares)")
     a = ap.parse_args(argv)
-    res = run(a.preset, a.draft, a.batch, a.prompt, a.gen, a.kv, a.spec, a.prefill_chunk, a.layers, a.graphs)
+    res = run(a.preset, a.draft, a.batch, a.prompt, a.gen, a.kv, a.spec, a.prefill_chunk, a.layers, a.graphs,
+              profile_steps=a.profile)
     print(json.dumps(res))
     if a.json:
         with open(a.json, "w") as f:

@@ -39,7 +39,8 @@ def family(name: str) -> str:
                 "sq_norm_kernel", "router_topk", "router_bwd", "plan_count", "plan_scan", "plan_assign",
                 "moe_gather", "moe_combine_bwd", "moe_combine_kernel", "moe_scatter_add", "ep_dispatch",
                 "ep_push", "ep_combine", "ep_owner_bwd", "ep_pad_rows", "ep_barrier", "decode_split",
-                "decode_combine", "nccl"):
+                "decode_combine", "decode_mla_tc", "decode_gemv", "skinny_gemm", "skinny_finalize", "kv_cache_write",
+                "kv_write", "moe_plan", "int4", "nccl"):
         if key in n:
             return key
     return "torch:" + n[:60]

@@ -69,8 +69,6 @@ void set_skinny_rows(int64_t n) { g_skinny_rows = (int)std::max<int64_t>(0, std:
 static void run_skinny(const at::Tensor& A, const at::Tensor& B, const int* offsets, int G, int rows, int N, int K,
                        long long w_group_stride, at::Tensor& C, int epilogue, double alpha,
                        const c10::optional<at::Tensor>& R) {
-  auto acc = at::empty({(int64_t)rows, (int64_t)N}, A.options().dtype(at::kFloat));
-  C10_CUDA_CHECK(cudaMemsetAsync(acc.data_ptr<float>(), 0, (size_t)rows * N * sizeof(float), cur_stream()));
   SkinnyDesc sd;
   sd.M = rows;
   sd.N = N;
@@ -82,8 +80,21 @@ static void run_skinny(const at::Tensor& A, const at::Tensor& B, const int* offs
   sd.W = B.data_ptr();
   sd.ldw = B.stride(-2);
   sd.w_group_stride = w_group_stride;
-  sd.acc = acc.data_ptr<float>();
   sd.status = status_ptr();
+  if ((epilogue == EPI_STORE_BF16 || epilogue == EPI_SWIGLU) && C.scalar_type() == at::kBFloat16 &&
+      skinny_ksplit(sd) == 1) {
+    // every output tile is computed by one CTA: the epilogue writes C itself
+    sd.out = C.data_ptr();
+    sd.ldo = C.stride(0);
+    sd.epilogue = epilogue;
+    sd.alpha = (float)alpha;
+    skinny_gemm_launch(sd, cur_stream());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  auto acc = at::empty({(int64_t)rows, (int64_t)N}, A.options().dtype(at::kFloat));
+  C10_CUDA_CHECK(cudaMemsetAsync(acc.data_ptr<float>(), 0, (size_t)rows * N * sizeof(float), cur_stream()));
+  sd.acc = acc.data_ptr<float>();
   skinny_gemm_launch(sd, cur_stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   skinny_finalize(acc.data_ptr<float>(), rows, N, epilogue, (float)alpha, C.data_ptr(), C.stride(0),

@@ -47,7 +47,29 @@ struct SkArgs {
   const int* offsets;
   float* acc;
   StatusBlock* status;
+  // direct epilogue (no K split): bf16 out = alpha * acc, or SwiGLU of the gate|up rows
+  int direct, epi;
+  float alpha;
+  bf16* out;
+  long long ldo;
 };
+
+// AND of `v` over the 128 epilogue threads (named barrier 1), so that they all take the
+// same branch afterwards and none is left waiting at the barrier.
+__device__ __forceinline__ bool all_epilogue(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 struct SkWork {
   int g, rt, kb0, kb1, row0, rows;
@@ -171,6 +193,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     // --------------------------------- epilogue ---------------------------------
     const int q = warp & 3;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    __shared__ float s_up[2][16][32];  // SwiGLU: up values of the current 16 tokens, per 64-row block
     int tile = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
@@ -181,9 +204,43 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const int nx = (min(kSkRows, w.rows - c0) + 15) / 16;
         const int a = tile & 1;
         bool got = mbar_wait(&tfull[a], (tile >> 1) & 1, p.status, STATUS_TIMEOUT_TMEM_FULL);
-        got = __all_sync(0xffffffffu, got);  // tcgen05.ld is warp-collective
+        got = all_epilogue(got);  // tcgen05.ld is warp-collective; the direct epilogue syncs all 4 warps
         if (!got) { ok = false; break; }
         tc_fence_after();
+        if (p.direct) {
+          for (int j = 0; j < nx; ++j) {
+            float v[16];
+            tmem_ld16(tmem + a * kSkRows + j * 16 + lane_off, v);
+            tc_wait_ld();
+            const int t0 = c0 + j * 16;
+            if (p.epi == EPI_SWIGLU) {
+              // weight rows of the tile: [gate 32 | up 32] x 2; warp q holds block q >> 1, gate if q even
+              if (q & 1) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) s_up[q >> 1][i][lane] = v[i] * p.alpha;
+              }
+              epilogue_bar();
+              if (!(q & 1)) {
+                const int col = w.rt * 64 + (q >> 1) * 32 + lane;
+                if (col < p.N / 2) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i)
+                    if (t0 + i < w.rows)
+                      p.out[(long long)(w.row0 + t0 + i) * p.ldo + col] =
+                          __float2bfloat16(silu_f(v[i] * p.alpha) * s_up[q >> 1][i][lane]);
+                }
+              }
+              epilogue_bar();
+            } else if (n < p.N) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (t0 + i < w.rows) p.out[(long long)(w.row0 + t0 + i) * p.ldo + n] = __float2bfloat16(v[i] * p.alpha);
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&tempty[a]);
+          continue;
+        }
         for (int j = 0; j < nx; ++j) {
           float v[16];
           tmem_ld16(tmem + a * kSkRows + j * 16 + lane_off, v);
@@ -235,6 +292,17 @@ __global__ void skinny_finalize_kernel(const float* __restrict__ acc, int rows, 
 
 }  // namespace
 
+int skinny_ksplit(const SkinnyDesc& d) {
+  const int nt = (d.N + 127) / 128;
+  const int nkb = (d.K + 63) / 64;
+  const int base = (d.offsets != nullptr ? d.G : 1) * nt;
+  const int sms = num_sms();
+  int ks = (2 * sms + base - 1) / base;
+  ks = std::max(1, std::min(ks, std::max(1, nkb / 4)));
+  const int kb_per = (nkb + ks - 1) / ks;
+  return (nkb + kb_per - 1) / kb_per;
+}
+
 void skinny_gemm_launch(const SkinnyDesc& d, cudaStream_t stream) {
   if (d.M <= 0 || d.N <= 0) return;
   if (d.K <= 0 || d.K % 8 != 0) throw std::runtime_error("skinny gemm: K must be a positive multiple of 8");
@@ -258,6 +326,11 @@ void skinny_gemm_launch(const SkinnyDesc& d, cudaStream_t stream) {
     tmX = make_tmap_bf16_sw128(d.X, 2, dims, str, box);
   }
   SkArgs p;
+  p.direct = 0;
+  p.epi = d.epilogue;
+  p.alpha = d.alpha;
+  p.out = reinterpret_cast<bf16*>(d.out);
+  p.ldo = d.ldo;
   p.M = d.M;
   p.N = d.N;
   p.K = d.K;
@@ -269,10 +342,14 @@ void skinny_gemm_launch(const SkinnyDesc& d, cudaStream_t stream) {
   const int nkb = (d.K + 63) / 64;
   const int sms = num_sms();
   const int base = p.G * p.nt;
-  int ks = (2 * sms + base - 1) / base;
-  ks = std::max(1, std::min(ks, std::max(1, nkb / 4)));
+  const int ks = skinny_ksplit(d);
   p.kb_per = (nkb + ks - 1) / ks;
   p.ksplit = (nkb + p.kb_per - 1) / p.kb_per;
+  if (d.out != nullptr) {
+    if (p.ksplit != 1 || !(d.epilogue == EPI_STORE_BF16 || d.epilogue == EPI_SWIGLU))
+      throw std::runtime_error("skinny gemm: direct output needs an unsplit K and a bf16 / SwiGLU epilogue");
+    p.direct = 1;
+  }
   const int units = base * p.ksplit;
   const int grid = std::min(units, sms);
   if (grouped) {

@@ -134,7 +134,15 @@ struct SkinnyDesc {
   long long w_group_stride = 0;
   float* acc = nullptr;
   void* status = nullptr;
+  // direct output (only when skinny_ksplit(d) == 1): bf16 out [rows, N] = alpha * X W^T, or the
+  // SwiGLU activation [rows, N/2] of 32-interleaved gate|up rows; acc is then unused
+  void* out = nullptr;
+  long long ldo = 0;
+  int epilogue = EPI_STORE_BF16;
+  float alpha = 1.0f;
 };
+// Number of K splits the launch will use (1: the output can be written directly).
+int skinny_ksplit(const SkinnyDesc& d);
 void skinny_gemm_launch(const SkinnyDesc& d, cudaStream_t stream);
 // out[r, :] = epilogue(acc[r, :]) for r < rows: EPI_STORE_BF16 / EPI_STORE_F32 /
 // EPI_ADD_BF16 (+ R) / EPI_SWIGLU (acc gate/up interleaved by 32 -> N/2 columns).
