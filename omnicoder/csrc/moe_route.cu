@@ -26,20 +26,15 @@ constexpr int kPlanThreads = 256;
 // ---------------------------------------------------------------------------
 // Router: softmax over E logits, top-k, optional renormalisation (one warp per token)
 // ---------------------------------------------------------------------------
-__global__ void router_topk_kernel(const float* __restrict__ logits, int* __restrict__ idx, float* __restrict__ wts,
-                                   float* __restrict__ probs, int T, int E, int K, bool renorm) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  float p[kRouteMaxE / 32];
+// p[j] = logit of expert lane + 32 j on entry (-inf where e >= E); softmax over the E logits,
+// then the top K by repeated warp argmax (ties -> lowest expert id), optionally renormalised.
+__device__ __forceinline__ void router_select(float (&p)[kRouteMaxE / 32], int t, int lane, int E, int K,
+                                              bool renorm, int* __restrict__ idx, float* __restrict__ wts,
+                                              float* __restrict__ probs) {
   const int per = (E + 31) / 32;
   float m = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kRouteMaxE / 32; ++j) {
-    const int e = lane + 32 * j;
-    p[j] = (j < per && e < E) ? logits[(long long)t * E + e] : -INFINITY;
-    m = fmaxf(m, p[j]);
-  }
+  for (int j = 0; j < kRouteMaxE / 32; ++j) m = fmaxf(m, p[j]);
   m = warp_max(m);
   float s = 0.f;
 #pragma unroll
@@ -53,9 +48,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int* __rest
   for (int j = 0; j < kRouteMaxE / 32; ++j) {
     p[j] *= inv;
     const int e = lane + 32 * j;
-    if (j < per && e < E) probs[(long long)t * E + e] = p[j];
+    if (probs != nullptr && j < per && e < E) probs[(long long)t * E + e] = p[j];
   }
-  // top-k by repeated warp argmax (ties -> lowest expert id)
   float sel_w[kRouteMaxK];
   int sel_e[kRouteMaxK];
   float wsum = 0.f;
@@ -93,6 +87,21 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int* __rest
       wts[(long long)t * K + k] = sel_w[k] * r;
     }
   }
+}
+
+__global__ void router_topk_kernel(const float* __restrict__ logits, int* __restrict__ idx, float* __restrict__ wts,
+                                   float* __restrict__ probs, int T, int E, int K, bool renorm) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  float p[kRouteMaxE / 32];
+  const int per = (E + 31) / 32;
+#pragma unroll
+  for (int j = 0; j < kRouteMaxE / 32; ++j) {
+    const int e = lane + 32 * j;
+    p[j] = (j < per && e < E) ? logits[(long long)t * E + e] : -INFINITY;
+  }
+  router_select(p, t, lane, E, K, renorm, idx, wts, probs);
 }
 
 void router_topk(const float* logits, int* idx, float* wts, float* probs, int T, int E, int K, bool renorm,
@@ -202,6 +211,71 @@ __global__ void plan_assign_kernel(const int* __restrict__ idx, int N, int E, in
   }
 }
 
+// The whole plan in one CTA when every pair fits one block (decode steps): the same
+// token-order ranks as count -> scan -> assign, in one launch.
+__global__ void __launch_bounds__(kPlanPairsPerBlock) plan_small_kernel(
+    const int* __restrict__ idx, int N, int E, int capacity, int* __restrict__ counts, int* __restrict__ offsets,
+    int* __restrict__ pos, int* __restrict__ src, int cap_rows, int align, StatusBlock* st) {
+  __shared__ int wcnt[kPlanPairsPerBlock / 32][kRouteMaxE];
+  __shared__ int kept[kRouteMaxE];
+  __shared__ int off[kRouteMaxE + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kPlanPairsPerBlock / 32;
+  for (int i = threadIdx.x; i < kWarps * kRouteMaxE; i += blockDim.x) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  const int i = threadIdx.x;
+  const bool active = i < N;
+  int e = active ? idx[i] : -1;
+  if (active && (e < 0 || e >= E)) {
+    report_error(st, STATUS_BAD_INDEX, e);
+    e = -1;
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, e);
+  const int rank_w = __popc(peers & ((1u << lane) - 1u));
+  if (e >= 0 && rank_w == 0) wcnt[warp][e] = __popc(peers);
+  __syncthreads();
+  for (int x = threadIdx.x; x < E; x += blockDim.x) {
+    int tot = 0;
+    for (int w = 0; w < kWarps; ++w) tot += wcnt[w][x];
+    counts[x] = tot;
+    kept[x] = capacity > 0 ? min(tot, capacity) : tot;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int o = 0;
+    for (int x = 0; x < E; ++x) {
+      off[x] = o;
+      offsets[x] = o;
+      o += (kept[x] + align - 1) / align * align;
+    }
+    off[E] = o;
+    offsets[E] = o;
+  }
+  __syncthreads();
+  for (int x = 0; x < E; ++x)
+    for (int r = off[x] + kept[x] + threadIdx.x; r < min(off[x + 1], cap_rows); r += blockDim.x) src[r] = -1;
+  if (active) {
+    if (e < 0) {
+      pos[i] = -1;
+    } else {
+      int r = rank_w;
+      for (int w = 0; w < warp; ++w) r += wcnt[w][e];
+      if (r < kept[e]) {
+        const int row = off[e] + r;
+        if (row < cap_rows) {
+          pos[i] = row;
+          src[row] = i;
+        } else {
+          pos[i] = -1;
+          report_error(st, STATUS_BAD_INDEX, row);
+        }
+      } else {
+        pos[i] = -1;
+      }
+    }
+  }
+}
+
 void moe_permute_plan(const int* idx, int T, int K, int E, int capacity, int* counts, int* offsets, int* pos,
                       int* src, int cap_rows, int* workspace, cudaStream_t s, int align) {
   const int N = T * K;
@@ -209,6 +283,11 @@ void moe_permute_plan(const int* idx, int T, int K, int E, int capacity, int* co
   if (nblocks == 0) {
     cudaMemsetAsync(counts, 0, E * sizeof(int), s);
     cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int), s);
+    return;
+  }
+  if (nblocks == 1) {
+    plan_small_kernel<<<1, kPlanPairsPerBlock, 0, s>>>(idx, N, E, capacity, counts, offsets, pos, src, cap_rows,
+                                                       align, (StatusBlock*)status_ptr());
     return;
   }
   StatusBlock* st = (StatusBlock*)status_ptr();

@@ -133,3 +133,36 @@ def test_swiglu_mlp_matches_oracle(cuda_ext):
     xs = [t.detach().float().requires_grad_() for t in (x, w13, w2, res)]
     yr = ops.swiglu_mlp(*[t.cpu() for t in xs[:3]], residual=xs[3].cpu())
     assert _rel(y, yr) < 2e-2
+
+
+def _plan_reference(idx, E, capacity, align):
+    """Token-order ranks inside each expert, kept while rank < capacity, segments padded to align."""
+    flat = idx.flatten().tolist()
+    seen = [0] * E
+    ranks = []
+    for e in flat:
+        ranks.append(seen[e])
+        seen[e] += 1
+    kept = [min(c, capacity) if capacity > 0 else c for c in seen]
+    offsets = [0]
+    for e in range(E):
+        offsets.append(offsets[-1] + (kept[e] + align - 1) // align * align)
+    pos = [offsets[e] + r if r < kept[e] else -1 for e, r in zip(flat, ranks)]
+    src = [-1] * offsets[-1]
+    for i, p in enumerate(pos):
+        if p >= 0:
+            src[p] = i
+    return seen, offsets, pos, src
+
+
+@pytest.mark.parametrize("T,K,E,cap,align", [(64, 4, 32, 0, 1), (200, 4, 32, 20, 1), (100, 6, 64, 0, 128), (5, 2, 8, 1, 128)])
+def test_small_permutation_plan_matches_reference(cuda_ext, T, K, E, cap, align):
+    """T * K <= 1024 pairs: the one-CTA plan kernel gives the stable token-order permutation."""
+    g = torch.Generator().manual_seed(T + E)
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).to(torch.int32).cuda()
+    counts_r, offsets_r, pos_r, src_r = _plan_reference(idx.cpu(), E, cap, align)
+    rows = offsets_r[-1]
+    counts, offsets, pos, src = cuda_ext.moe_plan(idx, E, cap, rows, align)
+    torch.cuda.synchronize()
+    assert counts.tolist() == counts_r and offsets.tolist() == offsets_r
+    assert pos.flatten().tolist() == pos_r and src.tolist() == src_r
