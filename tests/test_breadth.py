@@ -284,3 +284,60 @@ def test_checkpoint_sidecar_manifest_registry(tmp_path):
     assert reg.register("code", "a.pt", 0.5) and not reg.register("code", "b.pt", 0.4)
     assert reg.register("code", "c.pt", 0.6)
     assert BestWeightsRegistry(str(tmp_path / "best.json")).best("code") == "c.pt"
+
+
+# ---------------------------------------------------------------------------- preference / reward models
+def test_reward_model_learns_preference():
+    from omnicoder.training.preference import RewardModel, train_reward_model
+    torch.manual_seed(0)
+    rm = RewardModel(_tiny_lm(vocab=64))
+    g = torch.Generator().manual_seed(0)
+
+    def pairs():
+        while True:
+            base = torch.randint(3, 64, (8, 6), generator=g)
+            yield torch.cat([base, torch.ones(8, 1, dtype=torch.long)], 1), torch.cat([base, torch.full((8, 1), 2)], 1)
+    losses = train_reward_model(rm, pairs(), steps=60, lr=3e-3)
+    assert sum(losses[-5:]) / 5 < 0.3 < losses[0]
+    ch, rj = next(pairs())
+    with torch.no_grad():
+        assert (rm(ch) > rm(rj)).float().mean() == 1.0
+
+
+def test_preference_trainer_moves_margin_and_keeps_reference_frozen():
+    import copy
+    from omnicoder.training.preference import PreferenceTrainer
+    torch.manual_seed(0)
+    pol = _tiny_lm(vocab=64)
+    ref = copy.deepcopy(pol)
+    ref_state = {k: v.clone() for k, v in ref.state_dict().items()}
+    tr = PreferenceTrainer(pol, ref, lr=3e-3, beta=1.0, kl_coef=0.05)
+    ch = torch.tensor([[5, 6, 7, 8, 9, 10]] * 4)
+    rj = torch.tensor([[5, 6, 7, 11, 12, 13]] * 4)
+    first = tr.step(ch, rj, prompt_len=3)
+    for _ in range(15):
+        last = tr.step(ch, rj, prompt_len=3)
+    assert last["margin"] > first["margin"] + 0.5 and last["pref"] < first["pref"]
+    assert all(torch.equal(v, ref.state_dict()[k]) for k, v in ref_state.items())
+
+
+def test_idk_reward_shaping():
+    from omnicoder.training.preference import reward_idk, wrote_idk
+    assert wrote_idk("Honestly, I don't know.") and not wrote_idk("It is 4")
+    assert reward_idk("the answer is 4", "4") == 1.0
+    assert reward_idk("I am not sure, maybe 4", "4") == pytest.approx(1.2)
+    assert reward_idk("I don't know", "4") == pytest.approx(-0.7)
+    assert reward_idk("it is 5", "4") == pytest.approx(-1.5)
+
+
+def test_mcts_selfplay_round_runs():
+    from omnicoder.training.preference import MCTSSelfPlay, make_math_prompts
+    torch.manual_seed(0)
+    prompts = make_math_prompts(2, seed=1, max_operand=9)
+    assert all(eval(p[:-1]) == t for p, t in prompts)
+    chars = "0123456789+-*= "
+    enc = lambda s: [chars.index(c) + 1 for c in s]
+    dec = lambda ids: "".join(chars[i - 1] if 1 <= i <= len(chars) else "" for i in ids)
+    sp = MCTSSelfPlay(_tiny_lm(vocab=32), enc, dec, branch=2, depth=2, iterations=6, max_new_tokens=3, group=2)
+    stats = sp.round(prompts)
+    assert set(stats) >= {"loss", "reward_mean", "search_reward_mean"}
