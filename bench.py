@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--no-count", action="store_true")
     ap.add_argument("--ep-transport", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel exchange: fused peer-memory kernels or NCCL all_to_all (baseline)")
+    ap.add_argument("--zero-transport", default="nccl", choices=["nccl", "p2p"],
+                    help="data-parallel ZeRO-1: NCCL collectives, or the fused peer-memory optimiser kernels")
     ap.add_argument("--no-decode", action="store_true", help="skip the batch-64 long-context decode measurement")
     ap.add_argument("--decode-gen", type=int, default=512)
     return ap.parse_args()
@@ -211,7 +213,8 @@ def main():
         # exchange arena: x, y, dy, dx receive slabs (+ routing metadata) of every MoE layer of a step
         rows = int(args.micro_batch * args.seq * cfg.moe.top_k * 1.3) + cfg.moe.n_experts * 128
         arena = cfg.n_layers * rows * (4 * cfg.d_model * 2 + 16)
-        parallel = ExpertDataParallel(dist.group.WORLD, transport=args.ep_transport, arena_bytes=arena)
+        parallel = ExpertDataParallel(dist.group.WORLD, transport=args.ep_transport, arena_bytes=arena,
+                                      zero_transport=args.zero_transport)
 
     tcfg = TrainConfig(lr=3e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch, seq_len=args.seq,
                        grad_clip=1.0, weight_decay=0.1, betas=(0.9, 0.95))
@@ -319,6 +322,7 @@ def main():
             "config": {"model": MODEL_DESC, "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": S,
                        "parallelism": f"ep{world}xdp{world}" + (" zero1" if world > 1 else ""),
                        "ep_transport": args.ep_transport if world > 1 else None,
+                       "zero_transport": args.zero_transport if world > 1 else None,
                        "optimizer": "AdamW fp32 master, grad clip 1.0",
                        "l2": "working set (14.6 GB bf16 weights, 8192 tokens/GPU of activations) >> 126 MB L2"},
             "loss": loss_val, "e2e": e2e,

@@ -95,6 +95,30 @@ void ep_barrier_t(const std::vector<int64_t>& sig_ptrs, int64_t me, int64_t epoc
   ep_barrier(make_peers(sig_ptrs, {}), (int)me, (int)sig_ptrs.size(), (unsigned)(epoch & 0xffffffffll), stream());
 }
 
+void zero_rs_t(const std::vector<int64_t>& g_ptrs, int64_t lo, int64_t n, double scale, at::Tensor& out,
+               const c10::optional<at::Tensor>& norm_sq) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() >= n,
+              "zero_rs: fp32 shard output");
+  TORCH_CHECK(lo % 8 == 0, "zero_rs: shard offset must be a multiple of 8 elements");
+  const c10::cuda::CUDAGuard gd(out.device());
+  zero_rs(make_peers(g_ptrs, {}), (int)g_ptrs.size(), lo, n, (float)scale, out.data_ptr<float>(),
+          norm_sq.has_value() ? norm_sq->data_ptr<float>() : nullptr, stream());
+}
+
+void zero_adamw_push_t(at::Tensor& p, at::Tensor& m, at::Tensor& v, const at::Tensor& g,
+                       const std::vector<int64_t>& dst_ptrs, int64_t lo, double lr, double b1, double b2, double eps,
+                       double wd, int64_t step, const c10::optional<at::Tensor>& norm_sq, double max_norm) {
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&p, &m, &v, &g})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == p.numel(),
+                "zero_adamw_push: fp32 master / moments / gradient shards of one size");
+  TORCH_CHECK(lo % 8 == 0, "zero_adamw_push: shard offset must be a multiple of 8 elements");
+  const c10::cuda::CUDAGuard gd(p.device());
+  zero_adamw_push(p.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), g.data_ptr<float>(),
+                  make_peers(dst_ptrs, {}), (int)dst_ptrs.size(), lo, p.numel(), (float)lr, (float)b1, (float)b2,
+                  (float)eps, (float)wd, (int)step, norm_sq.has_value() ? norm_sq->data_ptr<float>() : nullptr,
+                  (float)max_norm, stream());
+}
+
 void register_ep(pybind11::module_& m) {
   m.def("ep_dispatch", &ep_dispatch_t);
   m.def("ep_push", &ep_push_t);
@@ -102,6 +126,11 @@ void register_ep(pybind11::module_& m) {
   m.def("ep_owner_bwd", &ep_owner_bwd_t);
   m.def("ep_pad_rows", &ep_pad_rows_t);
   m.def("ep_barrier", &ep_barrier_t);
+  m.def("zero_rs", &zero_rs_t, py::arg("g_ptrs"), py::arg("lo"), py::arg("n"), py::arg("scale"), py::arg("out"),
+        py::arg("norm_sq") = py::none());
+  m.def("zero_adamw_push", &zero_adamw_push_t, py::arg("p"), py::arg("m"), py::arg("v"), py::arg("g"),
+        py::arg("dst_ptrs"), py::arg("lo"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"),
+        py::arg("step"), py::arg("norm_sq") = py::none(), py::arg("max_norm") = 0.0);
 }
 
 }  // namespace omni

@@ -38,4 +38,14 @@ void ep_pad_rows(void* x, void* meta, const int* offsets, const int* kept, int E
 // Signal every rank and wait until every rank has signalled `epoch` (bounded wait).
 void ep_barrier(const EpPeers& sig, int me, int n, unsigned epoch, cudaStream_t s);
 
+// ZeRO-1 step over peer memory (zero_p2p.cu): reduce-scatter of rank-local bf16 gradient
+// buckets g.ptr[r] into this rank's fp32 shard out[0, n) = scale * sum_r g_r[lo + i] (+ its
+// squared norm into *norm_sq), and the AdamW update of that shard whose bf16 result is stored
+// into every rank's parameter bucket dst.ptr[r] at [lo, lo + n).  lo must be a multiple of 8.
+void zero_rs(const EpPeers& g, int world, long long lo, long long n, float scale, float* out, float* norm_sq,
+             cudaStream_t s);
+void zero_adamw_push(float* p, float* m, float* v, const float* g, const EpPeers& dst, int world, long long lo,
+                     long long n, float lr, float b1, float b2, float eps, float wd, int step, const float* norm_sq,
+                     float max_norm, cudaStream_t s);
+
 }  // namespace omni

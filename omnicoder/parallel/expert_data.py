@@ -27,8 +27,12 @@ from .zero import ZeroAdamW
 
 class ExpertDataParallel:
     def __init__(self, group=None, transport: str = "auto", bucket_bytes: int = 128 << 20,
-                 arena_bytes: int = 1 << 30):
+                 arena_bytes: int = 1 << 30, zero_transport: str = "nccl"):
+        """zero_transport: "nccl" (reduce-scatter / all-gather collectives) or "p2p" (the
+        reduce-scatter and the updated-weight all-gather fused into the optimiser kernels over
+        peer memory, see omnicoder.parallel.zero)."""
         self.group = group if group is not None else dist.group.WORLD
+        self.zero_transport = zero_transport
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
         self.ep = EPContext(self.group, transport=transport, arena_bytes=arena_bytes)
@@ -55,7 +59,8 @@ class ExpertDataParallel:
         dense = [p for p in model.parameters() if id(p) not in eid]
         self.opt = ZeroAdamW(dense, experts, self.group, lr=tcfg.lr, betas=tuple(tcfg.betas), eps=tcfg.eps,
                              weight_decay=tcfg.weight_decay, max_grad_norm=tcfg.grad_clip,
-                             bucket_bytes=self.bucket_bytes, expert_grad_scale=1.0 / self.world)
+                             bucket_bytes=self.bucket_bytes, expert_grad_scale=1.0 / self.world,
+                             transport=self.zero_transport)
         return self.opt
 
     def before_forward(self, micro: int, n_micro: int):

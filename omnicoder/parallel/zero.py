@@ -18,7 +18,17 @@ step with the same global-norm clip (the squared norm of every shard and every
 expert gradient is summed over the group on the device, no host sync).
 
 Weight decay skips 1-D parameters (norm weights); those live in their own
-buckets.  The update rule is torch.optim.AdamW's, the optimiser of the
+buckets.
+
+transport="p2p" (CUDA, one process per GPU of an NVLink box) keeps every bucket's
+gradients and bf16 parameters in peer-mapped symmetric memory and replaces the
+NCCL collectives and the separate norm / update kernels: when a bucket's last
+gradient arrives, a side stream runs a device barrier over the group and the
+fused reduce-scatter (each rank sums its shard straight from every rank's
+bucket, scales it and accumulates its squared norm); step() then all-reduces
+the one clip-norm scalar and runs the fused AdamW update, which stores the new
+bf16 shard into every rank's parameter bucket (the all-gather), followed by a
+closing device barrier.  The update rule is torch.optim.AdamW's, the optimiser of the
 reference trainer (src/omnicoder/training/pretrain.py:582); the reference has
 no sharded optimiser or gradient synchronisation at all.
 """
@@ -33,7 +43,7 @@ from ..ops import _ext
 
 
 class _Bucket:
-    def __init__(self, params, world, rank, device, dtype, decay):
+    def __init__(self, params, world, rank, device, dtype, decay, symm=None):
         self.params = params
         self.decay = decay
         n = sum(p.numel() for p in params)
@@ -41,8 +51,18 @@ class _Bucket:
         self.n_pad = max(quantum, (n + quantum - 1) // quantum * quantum)
         self.shard = self.n_pad // world
         self.lo = rank * self.shard
-        self.flat_p = torch.zeros(self.n_pad, device=device, dtype=dtype)
-        self.flat_g = torch.zeros(self.n_pad, device=device, dtype=dtype)
+        if symm is None:
+            self.flat_p = torch.zeros(self.n_pad, device=device, dtype=dtype)
+            self.flat_g = torch.zeros(self.n_pad, device=device, dtype=dtype)
+        else:
+            # peer-mapped: [flat_p | flat_g], every rank's copy addressable from this process
+            region = symm.alloc([2 * self.n_pad * 2] * world)
+            both = region.view(dtype, 2 * self.n_pad)
+            both.zero_()
+            self.flat_p, self.flat_g = both[:self.n_pad], both[self.n_pad:]
+            self.p_ptrs = list(region.ptrs)
+            self.g_ptrs = [ptr + self.n_pad * 2 for ptr in region.ptrs]
+            self.shard_gf = torch.zeros(self.shard, device=device, dtype=torch.float32)
         self.offset = {}
         o = 0
         with torch.no_grad():
@@ -62,10 +82,14 @@ class _Bucket:
 
 class ZeroAdamW:
     def __init__(self, dense_params, expert_params, group=None, lr=1e-3, betas=(0.9, 0.999), eps=1e-8,
-                 weight_decay=0.0, max_grad_norm=0.0, bucket_bytes: int = 128 << 20, expert_grad_scale: float = 1.0):
+                 weight_decay=0.0, max_grad_norm=0.0, bucket_bytes: int = 128 << 20, expert_grad_scale: float = 1.0,
+                 transport: str = "nccl"):
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"unknown ZeRO transport {transport!r}")
+        self.p2p = transport == "p2p"
         self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay
         self.max_grad_norm = max_grad_norm
         self.expert_grad_scale = expert_grad_scale
@@ -74,6 +98,14 @@ class ZeroAdamW:
         self.device = dense[0].device if dense else (expert_params[0].device if expert_params else torch.device("cpu"))
         self.cuda = self.device.type == "cuda"
         dtype = dense[0].dtype if dense else torch.float32
+        if self.p2p and not self.cuda:
+            raise ValueError("the peer-memory ZeRO transport needs CUDA tensors")
+        self.symm = None
+        if self.p2p:
+            from .symm import SymmArena
+            total = sum(p.numel() for p in dense) * 4 + 8 * 4096
+            self.symm = SymmArena(self.group, self.device, chunk_bytes=total)   # bucket storage + barrier flags
+            self.side = torch.cuda.Stream(self.device)
         self.buckets: list[_Bucket] = []
         for decay in (True, False):
             group_ps = [p for p in reversed(dense) if (p.dim() > 1) == decay]
@@ -82,10 +114,10 @@ class ZeroAdamW:
                 cur.append(p)
                 nbytes += p.numel() * p.element_size()
                 if nbytes >= bucket_bytes:
-                    self.buckets.append(_Bucket(cur, self.world, self.rank, self.device, dtype, decay))
+                    self.buckets.append(_Bucket(cur, self.world, self.rank, self.device, dtype, decay, self.symm))
                     cur, nbytes = [], 0
             if cur:
-                self.buckets.append(_Bucket(cur, self.world, self.rank, self.device, dtype, decay))
+                self.buckets.append(_Bucket(cur, self.world, self.rank, self.device, dtype, decay, self.symm))
         self._bucket_of = {p: b for b in self.buckets for p in b.params}
         # every rank starts from rank 0's replica
         for b in self.buckets:
@@ -125,6 +157,17 @@ class ZeroAdamW:
             self._launch(b)
 
     def _launch(self, b: _Bucket):
+        if self.p2p:
+            # every rank's bucket gradient is complete -> sum this rank's shard from all of them
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.side):
+                self.side.wait_event(ev)
+                self.symm.barrier()
+                _ext.load().zero_rs(b.g_ptrs, b.lo, b.shard, 1.0 / self.world, b.shard_gf,
+                                    self._norm if self.max_grad_norm > 0 else None)
+            b.work = True
+            return
         b.work = dist.reduce_scatter_tensor(b.shard_g, b.flat_g, group=self.group, async_op=True)
 
     def zero_grad(self, set_to_none: bool = True):
@@ -137,6 +180,8 @@ class ZeroAdamW:
         if lr is not None:
             self.lr = lr
         self.step_count += 1
+        if self.p2p:
+            return self._step_p2p()
         for b in self.buckets:
             if b.work is None:            # some parameters of the bucket received no gradient this step
                 for p in b.params:
@@ -197,6 +242,43 @@ class ZeroAdamW:
         for b in self.buckets:
             dist.all_gather_into_tensor(b.flat_p, b.flat_p[b.lo:b.lo + b.shard].clone() if not self.cuda
                                         else b.flat_p[b.lo:b.lo + b.shard], group=self.group)
+
+    def _step_p2p(self):
+        C = _ext.load()
+        cur = torch.cuda.current_stream(self.device)
+        for b in self.buckets:
+            if b.work is None:            # some parameters of the bucket received no gradient this step
+                for p in b.params:
+                    if p not in b.got:
+                        o = b.offset[p]
+                        b.flat_g[o:o + p.numel()].zero_()
+                self._launch(b)
+        cur.wait_stream(self.side)
+        for b in self.buckets:
+            b.work = None
+            b.ready = 0
+            b.got = set()
+        t = self.step_count
+        b1, b2 = self.betas
+        norm = None
+        if self.max_grad_norm > 0:
+            for p in self.experts:
+                if p.grad is not None:
+                    C.sq_norm(p.grad.to(torch.bfloat16).contiguous(), self.expert_grad_scale, self._norm)
+            dist.all_reduce(self._norm, group=self.group)
+            norm = self._norm
+        for b in self.buckets:
+            C.zero_adamw_push(b.master, b.m, b.v, b.shard_gf, b.p_ptrs, b.lo, self.lr, b1, b2, self.eps,
+                              self.wd if b.decay else 0.0, t, norm, self.max_grad_norm)
+        for p, st in zip(self.experts, self.estate):
+            if p.grad is None:
+                continue
+            C.adamw(st["master"], st["m"], st["v"], p.grad.to(torch.bfloat16).contiguous(), p.data, self.lr, b1,
+                    b2, self.eps, self.wd if p.dim() > 1 else 0.0, t, self.expert_grad_scale, norm,
+                    self.max_grad_norm)
+        self.symm.barrier()               # every rank's parameter bucket is complete before the next forward
+        if self.max_grad_norm > 0:
+            self._norm.zero_()            # the next step's reduce-scatters accumulate into it
 
     # ------------------------------------------------------------------
     def state_dict(self) -> dict:
