@@ -59,6 +59,24 @@ void adamw_step(float* p, float* m, float* v, const void* g, void* p_bf16, long 
                 float max_norm, cudaStream_t s);
 // *out += sum(g^2) * scale^2 over a bf16 vector (for global-norm clipping).
 void sq_norm_accum(const void* g, long long n, float scale, float* out, cudaStream_t s);
+// Many small tensors per launch (one block each): AdamW update / squared-norm accumulation.
+constexpr int kMultiItems = 48;
+struct AdamwItem {
+  float* p;
+  float* m;
+  float* v;
+  const void* g;  // bf16 gradient
+  void* pb;       // bf16 parameter copy (or nullptr)
+  long long n;
+  float wd;
+};
+struct AdamwMulti {
+  AdamwItem item[kMultiItems];
+  int count;
+};
+void adamw_multi(const AdamwMulti& t, float lr, float b1, float b2, float eps, float bc1, float bc2, float grad_scale,
+                 const float* norm_sq, float max_norm, cudaStream_t s);
+void sq_norm_multi(const AdamwMulti& t, float scale, float* out, cudaStream_t s);
 
 // ---- MoE routing -------------------------------------------------------------
 // Softmax over E router logits (fp32 [T, E]), top-k, optional renormalisation.

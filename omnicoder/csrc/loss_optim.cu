@@ -226,4 +226,61 @@ void sq_norm_accum(const void* g, long long n, float scale, float* out, cudaStre
   sq_norm_kernel<<<(int)blocks, 256, 0, s>>>((const bf16*)g, n, scale, out);
 }
 
+// ---------------------------------------------------------------------------
+// Multi-tensor forms for many small parameters (norm weights, routers): one block
+// per tensor, up to kMultiItems tensors per launch, the table passed by value.
+// Same arithmetic as adamw_kernel / sq_norm_kernel (scalar loop, fp32).
+// ---------------------------------------------------------------------------
+__global__ void adamw_multi_kernel(AdamwMulti t, float lr, float b1, float b2, float eps, float bc1, float bc2,
+                                   float grad_scale, const float* __restrict__ norm_sq, float max_norm) {
+  if ((int)blockIdx.x >= t.count) return;
+  const AdamwItem it = t.item[blockIdx.x];
+  float clip = 1.f;
+  if (max_norm > 0.f && norm_sq != nullptr) clip = fminf(1.f, max_norm / (sqrtf(*norm_sq) + 1e-6f));
+  const float gs = grad_scale * clip;
+  const float step = lr / bc1;
+  const float inv_sqrt_bc2 = rsqrtf(bc2);
+  const float decay = 1.f - lr * it.wd;
+  const bf16* g = reinterpret_cast<const bf16*>(it.g);
+  bf16* pb = reinterpret_cast<bf16*>(it.pb);
+  for (long long i = threadIdx.x; i < it.n; i += blockDim.x) {
+    const float gf = __bfloat162float(g[i]) * gs;
+    it.m[i] = b1 * it.m[i] + (1.f - b1) * gf;
+    it.v[i] = b2 * it.v[i] + (1.f - b2) * gf * gf;
+    it.p[i] = it.p[i] * decay - step * it.m[i] / (sqrtf(it.v[i]) * inv_sqrt_bc2 + eps);
+    if (pb != nullptr) pb[i] = __float2bfloat16(it.p[i]);
+  }
+}
+
+__global__ void sq_norm_multi_kernel(AdamwMulti t, float scale, float* out) {
+  __shared__ float sh[32];
+  if ((int)blockIdx.x >= t.count) return;
+  const AdamwItem it = t.item[blockIdx.x];
+  const bf16* g = reinterpret_cast<const bf16*>(it.g);
+  float acc = 0.f;
+  for (long long i = threadIdx.x; i < it.n; i += blockDim.x) {
+    const float a = __bfloat162float(g[i]);
+    acc += a * a;
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    acc = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    acc = warp_sum(acc);
+    if (threadIdx.x == 0) atomicAdd(out, acc * scale * scale);
+  }
+}
+
+void adamw_multi(const AdamwMulti& t, float lr, float b1, float b2, float eps, float bc1, float bc2, float grad_scale,
+                 const float* norm_sq, float max_norm, cudaStream_t s) {
+  if (t.count <= 0) return;
+  adamw_multi_kernel<<<t.count, 256, 0, s>>>(t, lr, b1, b2, eps, bc1, bc2, grad_scale, norm_sq, max_norm);
+}
+
+void sq_norm_multi(const AdamwMulti& t, float scale, float* out, cudaStream_t s) {
+  if (t.count <= 0) return;
+  sq_norm_multi_kernel<<<t.count, 256, 0, s>>>(t, scale, out);
+}
+
 }  // namespace omni

@@ -171,6 +171,63 @@ void adamw_t(at::Tensor& p, at::Tensor& m, at::Tensor& v, const at::Tensor& g, c
              (float)grad_scale, opt_ptr<float>(norm_sq), (float)max_norm, stream());
 }
 
+// Lists of small tensors: one launch per kMultiItems tensors.
+void adamw_multi_t(const std::vector<at::Tensor>& p, const std::vector<at::Tensor>& m, const std::vector<at::Tensor>& v,
+                   const std::vector<at::Tensor>& g, const std::vector<c10::optional<at::Tensor>>& pb,
+                   const std::vector<double>& wd, double lr, double b1, double b2, double eps, int64_t step,
+                   double grad_scale, const c10::optional<at::Tensor>& norm_sq, double max_norm) {
+  const size_t n = p.size();
+  TORCH_CHECK(m.size() == n && v.size() == n && g.size() == n && pb.size() == n && wd.size() == n,
+              "adamw_multi: list lengths");
+  if (n == 0) return;
+  const c10::cuda::CUDAGuard gd(p[0].device());
+  const double bc1 = 1.0 - std::pow(b1, (double)step);
+  const double bc2 = 1.0 - std::pow(b2, (double)step);
+  AdamwMulti t;
+  t.count = 0;
+  for (size_t i = 0; i < n; ++i) {
+    check_f32(p[i], "p");
+    check_f32(m[i], "m");
+    check_f32(v[i], "v");
+    check_bf16(g[i], "g");
+    TORCH_CHECK(p[i].is_contiguous() && m[i].is_contiguous() && v[i].is_contiguous() && g[i].is_contiguous() &&
+                    g[i].numel() == p[i].numel() && m[i].numel() == p[i].numel() && v[i].numel() == p[i].numel(),
+                "adamw_multi: contiguous tensors of one size per item");
+    if (pb[i].has_value()) check_bf16(*pb[i], "p_bf16");
+    AdamwItem& it = t.item[t.count++];
+    it.p = p[i].data_ptr<float>();
+    it.m = m[i].data_ptr<float>();
+    it.v = v[i].data_ptr<float>();
+    it.g = g[i].data_ptr();
+    it.pb = pb[i].has_value() ? pb[i]->data_ptr() : nullptr;
+    it.n = p[i].numel();
+    it.wd = (float)wd[i];
+    if (t.count == kMultiItems || i + 1 == n) {
+      adamw_multi(t, (float)lr, (float)b1, (float)b2, (float)eps, (float)bc1, (float)bc2, (float)grad_scale,
+                  opt_ptr<float>(norm_sq), (float)max_norm, stream());
+      t.count = 0;
+    }
+  }
+}
+
+void sq_norm_multi_t(const std::vector<at::Tensor>& g, double scale, at::Tensor& out) {
+  if (g.empty()) return;
+  check_f32(out, "out");
+  const c10::cuda::CUDAGuard gd(out.device());
+  AdamwMulti t;
+  t.count = 0;
+  for (size_t i = 0; i < g.size(); ++i) {
+    check_bf16(g[i], "g");
+    TORCH_CHECK(g[i].is_contiguous(), "sq_norm_multi: contiguous gradients");
+    AdamwItem& it = t.item[t.count++];
+    it = AdamwItem{nullptr, nullptr, nullptr, g[i].data_ptr(), nullptr, g[i].numel(), 0.f};
+    if (t.count == kMultiItems || i + 1 == g.size()) {
+      sq_norm_multi(t, (float)scale, out.data_ptr<float>(), stream());
+      t.count = 0;
+    }
+  }
+}
+
 void sq_norm_t(const at::Tensor& g, double scale, at::Tensor& out) {
   check_bf16(g, "g");
   check_f32(out, "out");
@@ -486,6 +543,10 @@ void register_kernels(pybind11::module_& m) {
         py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"), py::arg("step"), py::arg("grad_scale"),
         py::arg("norm_sq"), py::arg("max_norm"));
   m.def("sq_norm", &sq_norm_t);
+  m.def("adamw_multi", &adamw_multi_t, py::arg("p"), py::arg("m"), py::arg("v"), py::arg("g"), py::arg("p_bf16"),
+        py::arg("wd"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("step"),
+        py::arg("grad_scale"), py::arg("norm_sq") = py::none(), py::arg("max_norm") = 0.0);
+  m.def("sq_norm_multi", &sq_norm_multi_t);
   m.def("router_topk", &router_topk_t);
   m.def("kv_cache_write", &kv_cache_write_t, py::arg("src"), py::arg("pos"), py::arg("dst"), py::arg("scale"),
         py::arg("row_offset"));

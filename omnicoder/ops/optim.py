@@ -19,6 +19,8 @@ from . import _ext
 
 
 class FusedAdamW:
+    SMALL = 1 << 20   # elements: parameters up to this size are updated by the multi-tensor kernels
+
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, max_grad_norm: float = 0.0, no_decay_1d: bool = True):
         self.params = [p for p in params if p.requires_grad]
@@ -56,24 +58,35 @@ class FusedAdamW:
         cuda = len(self.params) > 0 and self.params[0].is_cuda
         if cuda:
             C = _ext.load()
+            grads = {i: (p.grad if p.grad.dtype == torch.bfloat16 else p.grad.to(torch.bfloat16)).contiguous()
+                     for i, p in enumerate(self.params) if p.grad is not None}
+            # parameters up to SMALL elements (norm weights, routers) go through the multi-tensor
+            # kernels, a few launches for all of them instead of two per parameter
+            small = [i for i in grads if self.params[i].numel() <= self.SMALL]
+            large = [i for i in grads if self.params[i].numel() > self.SMALL]
             norm = None
             if self.max_grad_norm > 0:
                 if self._norm is None:
                     self._norm = torch.zeros(1, device=self.params[0].device, dtype=torch.float32)
                 self._norm.zero_()
-                for p in self.params:
-                    if p.grad is not None:
-                        C.sq_norm(p.grad.to(torch.bfloat16).contiguous(), grad_scale, self._norm)
+                C.sq_norm_multi([grads[i] for i in small], grad_scale, self._norm)
+                for i in large:
+                    C.sq_norm(grads[i], grad_scale, self._norm)
                 norm = self._norm
-            for i, p in enumerate(self.params):
-                if p.grad is None:
-                    continue
-                st = self.state[i]
-                g = p.grad if p.grad.dtype == torch.bfloat16 else p.grad.to(torch.bfloat16)
+            if small:
+                pbs = [self.params[i].data if self.params[i].dtype == torch.bfloat16 else None for i in small]
+                C.adamw_multi([self.state[i]["master"] for i in small], [self.state[i]["m"] for i in small],
+                              [self.state[i]["v"] for i in small], [grads[i] for i in small], pbs,
+                              [self._wd(self.params[i]) for i in small], self.lr, b1, b2, self.eps, t, grad_scale,
+                              norm, self.max_grad_norm)
+            for i in large:
+                p, st = self.params[i], self.state[i]
                 pb = p.data if p.dtype == torch.bfloat16 else None
-                C.adamw(st["master"], st["m"], st["v"], g.contiguous(), pb, self.lr, b1, b2, self.eps, self._wd(p), t,
+                C.adamw(st["master"], st["m"], st["v"], grads[i], pb, self.lr, b1, b2, self.eps, self._wd(p), t,
                         grad_scale, norm, self.max_grad_norm)
-                if pb is None and p.data.data_ptr() != st["master"].data_ptr():
+            for i in grads:
+                p, st = self.params[i], self.state[i]
+                if p.dtype != torch.bfloat16 and p.data.data_ptr() != st["master"].data_ptr():
                     p.data.copy_(st["master"])
             return
         # CPU reference (identical update rule, fp32)

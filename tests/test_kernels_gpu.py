@@ -166,3 +166,26 @@ def test_small_permutation_plan_matches_reference(cuda_ext, T, K, E, cap, align)
     torch.cuda.synchronize()
     assert counts.tolist() == counts_r and offsets.tolist() == offsets_r
     assert pos.flatten().tolist() == pos_r and src.tolist() == src_r
+
+
+def test_adamw_multi_tensor_with_clip_matches_torch(cuda_ext):
+    """Many small parameters (multi-tensor kernels) and large ones (one launch each), with the
+    device-side global-norm clip, against torch.optim.AdamW + clip_grad_norm_."""
+    torch.manual_seed(7)
+    shapes = [(2048,), (33,), (512, 300), (1 << 20 | 8,), (64, 2048), (7,)] + [(2048,)] * 60
+    ps = [torch.nn.Parameter(torch.randn(s, device="cuda").to(torch.bfloat16)) for s in shapes]
+    refs = [torch.nn.Parameter(p.detach().float().clone()) for p in ps]
+    opt = ops.FusedAdamW(ps, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=0.5)
+    topt = torch.optim.AdamW([{"params": [r for r in refs if r.dim() > 1], "weight_decay": 0.1},
+                              {"params": [r for r in refs if r.dim() <= 1], "weight_decay": 0.0}],
+                             lr=1e-2, betas=(0.9, 0.95))
+    for _ in range(3):
+        for p, r in zip(ps, refs):
+            g = torch.randn(p.shape, device="cuda").to(torch.bfloat16)
+            p.grad, r.grad = g, g.float()
+        opt.step()
+        torch.nn.utils.clip_grad_norm_(refs, 0.5)
+        topt.step()
+    for i, r in enumerate(refs):
+        assert _rel(opt.state[i]["master"], r.detach()) < 1e-4, i
+        assert _rel(ps[i], r.detach()) < 1e-2, i
