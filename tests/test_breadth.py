@@ -7,6 +7,7 @@ import os
 
 import pytest
 import torch
+import torch.nn.functional as F
 
 
 def _tiny_lm(vocab=64):
@@ -341,3 +342,62 @@ def test_mcts_selfplay_round_runs():
     sp = MCTSSelfPlay(_tiny_lm(vocab=32), enc, dec, branch=2, depth=2, iterations=6, max_new_tokens=3, group=2)
     stats = sp.round(prompts)
     assert set(stats) >= {"loss", "reward_mean", "search_reward_mean"}
+
+
+def test_video_encoder_and_temporal_mixer():
+    from omnicoder.multimodal.video import TemporalMixer, VideoEncoder
+    torch.manual_seed(0)
+    enc = VideoEncoder(image_size=32, patch=8, dim=32, depth=1, heads=2, temporal_kernel=3)
+    feats, pooled = enc(torch.randn(2, 5, 3, 32, 32))
+    assert feats.shape == (2, 5, 32) and pooled.shape == (2, 32)
+    assert torch.allclose(pooled, feats.mean(1))
+    mix = TemporalMixer(8, kernel_size=3)
+    x = torch.randn(1, 9, 8)
+    y0 = mix(x)
+    x2 = x.clone()
+    x2[:, 8] += 1.0                                   # a change at t=8 reaches only t=7, 8 (kernel 3)
+    diff = (mix(x2) - y0).abs().amax(-1)[0]
+    assert diff[:7].max() == 0 and diff[7:].min() > 0
+
+
+def test_voxel_head_and_ortho_renderer():
+    from omnicoder.multimodal.video import OrthoRenderer, VoxelLatentHead
+    torch.manual_seed(0)
+    vox = VoxelLatentHead(16, depth=4, height=8, width=8, hidden=32)(torch.randn(2, 7, 16))
+    assert vox.shape == (2, 4, 8, 8)
+    r = OrthoRenderer(depth=4, out_h=16, out_w=16)
+    img = r(vox)
+    assert img.shape == (2, 3, 16, 16) and img.min() >= 0 and img.max() <= 1
+    # a fully opaque front slice shows only its own colour
+    opaque = torch.full((1, 4, 16, 16), -30.0)
+    opaque[:, 0] = 30.0
+    out = r(opaque)
+    assert torch.allclose(out[0, :, 8, 8], torch.sigmoid(r.color[0]), atol=1e-4)
+    assert torch.allclose(r(torch.full((1, 4, 16, 16), -30.0)), torch.zeros(1, 3, 16, 16), atol=1e-6)
+
+
+def test_latent_refiner_and_interpolator():
+    from omnicoder.multimodal.video import LatentInterpolator, LatentRefiner
+    torch.manual_seed(0)
+    ref = LatentRefiner(16)
+    with torch.no_grad():
+        ref.gate.zero_()
+    x = torch.randn(3, 16)
+    assert torch.equal(ref(x), x)                     # gate 0 is the identity
+    assert LatentRefiner(16, temporal=True)(torch.randn(2, 6, 16)).shape == (2, 6, 16)
+    with pytest.raises(ValueError):
+        ref(torch.randn(2, 2, 2, 16))
+    interp = LatentInterpolator(8, hidden=32)
+    z0, z1 = torch.randn(2, 3, 8), torch.randn(2, 3, 8)
+    out = interp(z0, z1, steps=5)
+    assert out.shape == (2, 5, 3, 8)
+    opt = torch.optim.Adam(interp.parameters(), lr=1e-2)
+    tau = torch.linspace(0, 1, 5).view(1, 5, 1, 1)
+    target = z0.unsqueeze(1) * (1 - tau) + z1.unsqueeze(1) * tau
+    first = float(F.mse_loss(interp(z0, z1, 5), target))
+    for _ in range(200):
+        loss = F.mse_loss(interp(z0, z1, 5), target)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+    assert float(loss) < 0.2 * first
