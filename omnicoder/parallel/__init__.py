@@ -1,2 +1,2 @@
 """Parallel layouts: expert parallelism over NVLink peer memory, ZeRO-1 data
-parallelism, tensor/sequence and pipeline parallelism."""
+parallelism, tensor/sequence, context (all-to-all over heads) and pipeline parallelism."""
