@@ -1,8 +1,9 @@
 """Inference-side tools: throughput benchmark, kNN-LM cache, batched HTTP
 server, GGUF round trip, ONNX decode-step wrappers (numerics vs the models'
-own decode paths)."""
+own decode paths), decode-step session runner with KV quantisation and paging."""
 import json
 
+import pytest
 import torch
 
 from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig, get_preset
@@ -88,3 +89,54 @@ def test_onnx_decode_step_wrappers():
     flat = [t for l in range(cfg.n_layers) for t in (kv2.k[l], kv2.v[l])]
     got = DecodeStepWrapper(m)(torch.tensor([[7]]), torch.tensor(3), *flat)
     assert torch.allclose(got[0], want, atol=1e-4)
+
+
+def test_decode_runner_matches_generate():
+    import numpy as np
+    from omnicoder.inference.generate import generate
+    from omnicoder.inference.runtimes import DecodeRunner, TorchStepSession, bench_decode
+    cfg, m = _tiny()
+    prompt = torch.tensor([[4, 9, 17, 3]])
+    want = generate(m, prompt, 6, temperature=0.0)
+    sess = TorchStepSession(m, max_len=32)
+    got = DecodeRunner(sess).generate(prompt.numpy(), 6)
+    assert np.array_equal(got, want.numpy())
+    q = DecodeRunner(sess, kv_quant="u8", group=16).generate(prompt.numpy(), 6)
+    assert q.shape == got.shape and (q[:, :5] == got[:, :5]).all()
+    assert bench_decode(sess, cfg.vocab_size, prompt_len=3, gen_tokens=3) > 0
+
+
+def test_decode_runner_compat_window_and_sampling():
+    import numpy as np
+    from omnicoder.inference.runtimes import DecodeRunner, TorchStepSession, cache_layout
+    from omnicoder.models.compat import OmniTransformer
+    torch.manual_seed(0)
+    cm = OmniTransformer(vocab_size=100, n_layers=2, d_model=32, n_heads=4, mlp_dim=64, n_experts=2, top_k=1,
+                         max_seq_len=64, kv_latent_dim=8).eval()
+    sess = TorchStepSession(cm)
+    tok, pos, layers, outs = cache_layout(sess)
+    assert tok == "input_ids" and pos is None and layers[0][2] == (1, 4, 16, 8) and outs[0] == "logits"
+    r = DecodeRunner(sess, logit_bias={7: 1e4})
+    out = r.generate(np.array([[1, 2, 3]]), 4, temperature=0.7, top_k=5, top_p=0.9, seed=1)
+    assert out.shape == (1, 7) and (out[0, 3:] == 7).all()         # the bias dominates sampling
+
+
+def test_lru_kv_pager_counts():
+    from omnicoder.inference.runtimes import LRUKVPager, PagingConfig
+    p = LRUKVPager(PagingConfig(n_layers=2, page_len=4, max_pages_ram=4, prefetch_ahead=1))
+    for pos in range(16):
+        p.access(pos)
+    s = p.stats()
+    assert s["misses"] == 2 and s["hits"] == 30 and s["prefetch_hits"] == 6 and s["resident_pages"] == 4
+    small = LRUKVPager(PagingConfig(n_layers=2, page_len=4, max_pages_ram=2, prefetch_ahead=1))
+    for pos in range(8):
+        small.access(pos)
+    assert small.stats()["misses"] > 2                              # prefetches evict the pages in use
+
+
+def test_onnx_session_needs_onnxruntime():
+    from omnicoder.inference import runtimes
+    if runtimes.providers():
+        pytest.skip("onnxruntime is installed")
+    with pytest.raises(RuntimeError, match="onnxruntime"):
+        runtimes.open_session("missing.onnx")
