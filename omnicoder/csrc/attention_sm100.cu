@@ -139,6 +139,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* o_done = bars + 15;
   uint64_t* drain = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  // Completes once, after the last P.V: o_done completes once per tile, and when
+  // the softmax warps finish the last tile it may still be two completions short
+  // (only P.V of tile n-3 is ordered before S of tile n-1), where a parity wait
+  // on o_done could not tell phase n-1 from phase n-3.
+  uint64_t* o_last = bars + 18;
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / kTile;
@@ -163,6 +168,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&p_full[i], 4);
     }
     mbar_init(o_done, 1);
+    mbar_init(o_last, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
   }
@@ -245,6 +251,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_commit(&v_empty[s]);
         tc_commit(&s_empty[s]);
       }
+      if (ok && n > 0) tc_commit(o_last);
       tc_commit(drain);
       mbar_wait(drain, 0, p.status, STATUS_TIMEOUT_DRAIN);
     }
@@ -325,7 +332,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[s]);
     }
-    if (ok && n > 0 && mbar_wait(o_done, (n - 1) & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) {
+    if (ok && n > 0 && mbar_wait(o_last, 0, p.status, STATUS_TIMEOUT_TMEM_FULL)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       bf16* dst = p.o + (long long)(t0 + r) * p.o_row + (long long)h * p.o_head;

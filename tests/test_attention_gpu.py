@@ -24,8 +24,9 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("name,B,S,H,Hk,Dk,Dr,Dv,window", CASES)
-def test_attention_fwd_bwd(cuda_ext, name, B, S, H, Hk, Dk, Dr, Dv, window):
+def test_attention_fwd_bwd(cuda_ext, name, B, S, H, Hk, Dk, Dr, Dv, window, causal):
     torch.manual_seed(0)
     T = B * S
     Dq = Dk + Dr
@@ -37,8 +38,8 @@ def test_attention_fwd_bwd(cuda_ext, name, B, S, H, Hk, Dk, Dr, Dv, window):
     v = kv[:, :, Dk:].detach().requires_grad_()
     kr = torch.randn(T, Dr, device=dev).to(torch.bfloat16).requires_grad_() if Dr else None
     scale = 1.0 / math.sqrt(Dq)
-    o = attention(q, k, v, kr, seq=S, causal=True, window=window, scale=scale)
-    ref = attention_torch(q.float(), k.float(), v.float(), None if kr is None else kr.float(), seq=S, causal=True,
+    o = attention(q, k, v, kr, seq=S, causal=causal, window=window, scale=scale)
+    ref = attention_torch(q.float(), k.float(), v.float(), None if kr is None else kr.float(), seq=S, causal=causal,
                           window=window, scale=scale)
     assert _rel(o, ref) < 2e-2, "forward"
     do = torch.randn_like(o)
@@ -47,7 +48,7 @@ def test_attention_fwd_bwd(cuda_ext, name, B, S, H, Hk, Dk, Dr, Dv, window):
     kf = k.detach().float().requires_grad_()
     vf = v.detach().float().requires_grad_()
     krf = kr.detach().float().requires_grad_() if kr is not None else None
-    r = attention_torch(qf, kf, vf, krf, seq=S, causal=True, window=window, scale=scale)
+    r = attention_torch(qf, kf, vf, krf, seq=S, causal=causal, window=window, scale=scale)
     r.backward(do.float())
     assert _rel(q.grad, qf.grad) < 3e-2, "dq"
     assert _rel(k.grad, kf.grad) < 3e-2, "dk"
