@@ -19,6 +19,16 @@ def _c2d(t: torch.Tensor) -> torch.Tensor:
     return t if (t.dim() == 2 and t.stride(-1) == 1) else t.reshape(-1, t.shape[-1]).contiguous()
 
 
+def _pad_to8(t: torch.Tensor, dim: int) -> torch.Tensor:
+    """Zero-pad `dim` (a reduction dim) up to a multiple of 8: the tcgen05 GEMM takes K in
+    16-byte steps, and zero rows / columns add nothing to the product."""
+    k = t.shape[dim]
+    if k % 8 == 0:
+        return t
+    pad = [0, 0] * (t.dim() - 1 - dim) + [0, 8 - k % 8]
+    return torch.nn.functional.pad(t, pad).contiguous()
+
+
 def mm_nt(a: torch.Tensor, b: torch.Tensor, residual: torch.Tensor | None = None, out_f32: bool = False,
           out: torch.Tensor | None = None) -> torch.Tensor:
     if not _ext.use_cuda(a):
@@ -27,8 +37,8 @@ def mm_nt(a: torch.Tensor, b: torch.Tensor, residual: torch.Tensor | None = None
             y = y + residual
         return y.float() if out_f32 else y
     C = _ext.load()
-    a = _c2d(a)
-    b = b.contiguous()
+    a = _pad_to8(_c2d(a), 1)
+    b = _pad_to8(b.contiguous(), 1)
     M, N = a.shape[0], b.shape[0]
     if out is None:
         out = torch.empty(M, N, device=a.device, dtype=torch.float32 if out_f32 else torch.bfloat16)
@@ -43,8 +53,8 @@ def mm_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     if not _ext.use_cuda(a):
         return a @ b
     C = _ext.load()
-    a = _c2d(a)
-    b = b.contiguous()
+    a = _pad_to8(_c2d(a), 1)
+    b = _pad_to8(b.contiguous(), 0)
     out = torch.empty(a.shape[0], b.shape[1], device=a.device, dtype=torch.bfloat16)
     C.gemm(a, b, out, False, True, EPI_BF16, 1.0, None, None, 256)
     return out
@@ -59,8 +69,8 @@ def mm_tn(a: torch.Tensor, b: torch.Tensor, out_f32: bool = False, accumulate_in
             return accumulate_into
         return y.float() if out_f32 else y
     C = _ext.load()
-    a = _c2d(a)
-    b = _c2d(b)
+    a = _pad_to8(_c2d(a), 0)
+    b = _pad_to8(_c2d(b), 0)
     if accumulate_into is not None:
         C.gemm(a, b, accumulate_into, True, True, EPI_ACC_F32, 1.0, None, None, 256)
         return accumulate_into

@@ -69,6 +69,10 @@ def parse_args(argv=None):
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--tokenizer", default=None, help="local Hugging Face tokenizer directory (default: bytes)")
     ap.add_argument("--ep_transport", default="auto", choices=["auto", "p2p", "nccl"])
+    ap.add_argument("--pg_timeout", type=float, default=600.0, help="process-group timeout (s)")
+    ap.add_argument("--heartbeat_timeout", type=float, default=0.0,
+                    help="multi-rank: check every rank's heartbeat before each step, naming a rank that left, "
+                         "died or stalled for this many seconds (0: off)")
     return ap.parse_args(argv)
 
 
@@ -110,7 +114,7 @@ def main(argv=None):
     if a.capacity_factor is not None:
         cfg.moe.capacity_factor = a.capacity_factor
     if world > 1:
-        dist.init_process_group("nccl" if dev.type == "cuda" else "gloo", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl" if dev.type == "cuda" else "gloo", timeout=datetime.timedelta(seconds=a.pg_timeout),
                                 device_id=dev if dev.type == "cuda" else None)
         from ..parallel.expert_data import ExpertDataParallel
         par = ExpertDataParallel(dist.group.WORLD, transport=a.ep_transport)
@@ -141,10 +145,33 @@ def main(argv=None):
         os.makedirs(os.path.dirname(os.path.abspath(a.log_file)) or ".", exist_ok=True)
     ev0 = torch.cuda.Event(enable_timing=True) if dev.type == "cuda" else None
     ev1 = torch.cuda.Event(enable_timing=True) if dev.type == "cuda" else None
-    t_last, tok_acc = time.time(), 0
     if ev0 is not None:
         ev0.record()
+    from ..parallel.health import FaultInjector, Heartbeat
+    hb = Heartbeat(timeout=a.heartbeat_timeout).start() if (world > 1 and a.heartbeat_timeout > 0) else None
+    inj = FaultInjector.from_env()
+    try:
+        _train_loop(a, trainer, model, it, dev, world, rank, start, state_path, log, ev0, ev1, hb, inj)
+    except Exception as e:
+        if hb is not None:
+            hb.leave(f"{type(e).__name__}: {e}")
+        raise
+    if hb is not None:
+        hb.stop()
+    _save(model, trainer, a, world, rank, state_path, a.steps)
+    if log is not None:
+        log.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _train_loop(a, trainer, model, it, dev, world, rank, start, state_path, log, ev0, ev1, hb, inj):
+    t_last, tok_acc = time.time(), 0
     for step in range(start, a.steps):
+        inj.at_step(rank, step, hb)
+        if hb is not None:
+            hb.check(step)
         ids, lab = next(it)
         st = trainer.step(ids.to(dev, non_blocking=True), lab.to(dev, non_blocking=True))
         tok_acc += ids.numel() * world
@@ -173,12 +200,6 @@ def main(argv=None):
                     log.flush()
         if a.save_interval and (step + 1) % a.save_interval == 0:
             _save(model, trainer, a, world, rank, state_path, step + 1)
-    _save(model, trainer, a, world, rank, state_path, a.steps)
-    if log is not None:
-        log.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
 
 
 def _save(model, trainer, a, world, rank, state_path, step):

@@ -1,0 +1,76 @@
+"""Edge shapes and determinism of the sm_100a kernels (no sanitizer is available on
+the GPUs, so these stand in for it together with the device status word that
+every test checks): the routed MoE FFN with one token, with every token sent to
+the same two experts (six experts receive none) and with capacity overflow,
+against the fp32 oracle; and bitwise-repeatable forward passes of the GEMM,
+flash attention and MoE inference path."""
+import pytest
+import torch
+
+from omnicoder import ops
+from omnicoder.ops.gemm import interleave_gate_up
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-6)).item()
+
+
+def _moe_inputs(T, skew: bool, D=256, E=8, Fd=128, seed=11):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(T, D, generator=g)
+    rw = 0.1 * torch.randn(E, D, generator=g)
+    if skew:                        # every token's top-2 experts are 3 and 5
+        x[:, 0] = 4.0 + x[:, 0].abs()
+        rw[:, 0] = 0.0
+        rw[3, 0], rw[5, 0] = 2.0, 1.6
+    w1 = 0.05 * torch.randn(E, Fd, D, generator=g)
+    w3 = 0.05 * torch.randn(E, Fd, D, generator=g)
+    w13 = interleave_gate_up(w1, w3)
+    w2 = 0.05 * torch.randn(E, D, Fd, generator=g)
+    add = torch.randn(T, D, generator=g)
+    return [t.cuda().to(torch.bfloat16).requires_grad_() for t in (x, rw, w13, w2, add)]
+
+
+@pytest.mark.parametrize("name,T,skew,capacity", [
+    ("one_token", 1, False, 0),
+    ("two_experts_only", 256, True, 0),
+    ("capacity_overflow", 256, True, 40),
+])
+def test_moe_edge_cases_match_oracle(cuda_ext, name, T, skew, capacity):
+    K = 2
+    x, rw, w13, w2, add = _moe_inputs(T, skew)
+    out, aux = ops.moe_ffn(x, rw, w13, w2, K, capacity, True, 0.01, 0.001, add=add)
+    xs = [t.detach().float().requires_grad_() for t in (x, rw, w13, w2, add)]
+    ref, aux_ref = ops.moe_ffn_torch(xs[0], xs[1], xs[2], xs[3], K, capacity, True, 0.01, 0.001, add=xs[4])
+    assert torch.isfinite(out.float()).all()
+    assert _rel(out, ref) < 2e-2, name
+    assert abs(aux.item() - aux_ref.item()) < 1e-3 * max(1.0, abs(aux_ref.item()))
+    dout = torch.randn_like(out)
+    out.backward(dout)
+    (ref * dout.float()).sum().add(aux_ref).backward()
+    for got, want, what in zip((x, rw, w13, w2, add), xs, ("x", "router", "w13", "w2", "add")):
+        assert torch.isfinite(got.grad.float()).all(), what
+        assert _rel(got.grad, want.grad) < 5e-2, f"{name}: {what}"
+    if skew and capacity == 0:      # experts without tokens get exactly zero weight gradients
+        idle = [e for e in range(8) if e not in (3, 5)]
+        assert w13.grad[idle].abs().max().item() == 0.0 and w2.grad[idle].abs().max().item() == 0.0
+
+
+def test_forward_kernels_are_bitwise_repeatable(cuda_ext):
+    torch.manual_seed(3)
+    x = torch.randn(512, 1024, device="cuda").to(torch.bfloat16)
+    w = (0.03 * torch.randn(768, 1024, device="cuda")).to(torch.bfloat16)
+    assert torch.equal(ops.linear(x, w), ops.linear(x, w))
+    q = torch.randn(512, 4, 128, device="cuda").to(torch.bfloat16)
+    k = torch.randn(512, 2, 128, device="cuda").to(torch.bfloat16)
+    v = torch.randn(512, 2, 128, device="cuda").to(torch.bfloat16)
+    a1 = ops.attention(q, k, v, seq=256, causal=True)
+    a2 = ops.attention(q, k, v, seq=256, causal=True)
+    assert torch.equal(a1, a2)
+    xm, rw, w13, w2, _ = (t.detach() for t in _moe_inputs(300, False))
+    with torch.no_grad():
+        m1, _ = ops.moe_ffn(xm, rw, w13, w2, 2, 0, True)
+        m2, _ = ops.moe_ffn(xm, rw, w13, w2, 2, 0, True)
+    assert torch.equal(m1, m2)
