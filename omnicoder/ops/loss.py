@@ -27,7 +27,7 @@ class _HeadCEFn(torch.autograd.Function):
         lab = labels.reshape(-1).contiguous().long()
         T = h2.shape[0]
         if assume_all_valid:
-            n_valid = torch.tensor(float(T), device=h.device)
+            n_valid = torch.full((), float(T), device=h.device)   # a fill kernel, no host copy
             scale = 1.0 / T
         else:
             lab = torch.where(lab == ignore_index, torch.full_like(lab, -1), lab)

@@ -6,6 +6,13 @@ expert-parallel x data-parallel layout of :mod:`omnicoder.parallel` (experts
 sharded over the EP group, dense parameters replicated with ZeRO-1 sharded
 AdamW state); without one it is the single-device trainer.
 
+`cuda_graph=True` (single device, grad_accum 1): after `graph_warmup` eager
+steps, forward + backward is captured once as a CUDA graph and replayed every
+step (the batch is copied into static input buffers; the gradients are static
+tensors the replay overwrites, so they are not reset between steps); the
+optimiser runs eagerly after the replay, with the learning rate of the step.
+A capture that fails leaves the trainer in eager mode (`graph_error` says why).
+
 The reference trainer's step (src/omnicoder/training/pretrain.py:915-952:
 scaled backward, optimizer.step, zero_grad) has no gradient synchronisation at
 all; it runs in a single process.
@@ -32,11 +39,17 @@ class StepStats:
 
 
 class Trainer:
-    def __init__(self, model: OmniLM, tcfg: TrainConfig, parallel=None):
+    def __init__(self, model: OmniLM, tcfg: TrainConfig, parallel=None, cuda_graph: bool = False,
+                 graph_warmup: int = 2):
         self.model = model
         self.tcfg = tcfg
         self.parallel = parallel
         self.step_idx = 0
+        self.cuda_graph = cuda_graph and parallel is None and max(1, tcfg.grad_accum) == 1
+        self.graph_warmup = graph_warmup
+        self._graph = None
+        self._graph_key = None
+        self.graph_error: str | None = None
         if parallel is not None:
             self.opt = parallel.make_optimizer(model, tcfg)
         else:
@@ -51,6 +64,14 @@ class Trainer:
     def step(self, ids: torch.Tensor, labels: torch.Tensor, assume_all_valid: bool = False) -> StepStats:
         """One optimiser step over micro-batches `ids`/`labels` [B, S] (split into
         grad_accum chunks along the batch)."""
+        if self.cuda_graph and ids.is_cuda:
+            key = (tuple(ids.shape), tuple(labels.shape), bool(assume_all_valid))
+            if self._graph is None and self.step_idx >= self.graph_warmup:
+                self._capture(ids, labels, assume_all_valid, key)
+            if self._graph is not None and key == self._graph_key:
+                return self._graph_step(ids, labels)
+            if self._graph is not None:              # eager step beside the graph: fresh gradients
+                self.opt.zero_grad(set_to_none=True)
         accum = max(1, self.tcfg.grad_accum)
         chunks_ids = ids.chunk(accum, dim=0)
         chunks_lab = labels.chunk(accum, dim=0)
@@ -73,6 +94,46 @@ class Trainer:
         self.opt.zero_grad(set_to_none=True)
         self.step_idx += 1
         return StepStats(loss_sum / accum, ce_sum / accum, aux_sum / accum, ids.numel(), lr)
+
+    # ------------------------------------------------------------------
+    def _capture(self, ids, labels, assume_all_valid, key):
+        self._static_ids, self._static_lab = ids.clone(), labels.clone()
+        self.opt.zero_grad(set_to_none=True)
+        dev = ids.device
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        try:
+            with torch.cuda.stream(side):        # lazy setup outside the capture; no optimiser step
+                out = self.model(self._static_ids, labels=self._static_lab, assume_all_valid=assume_all_valid)
+                out["loss"].backward()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            del out
+            self.opt.zero_grad(set_to_none=True)
+            torch.cuda.synchronize(dev)
+            torch.cuda.empty_cache()             # the graph's private pool replaces the eager steps' cache
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = self.model(self._static_ids, labels=self._static_lab, assume_all_valid=assume_all_valid)
+                out["loss"].backward()
+        except Exception as e:                   # stay eager
+            self.cuda_graph, self.graph_error = False, f"{type(e).__name__}: {e}"
+            self.opt.zero_grad(set_to_none=True)
+            return
+        self._graph, self._graph_key = g, key
+        self._static_out = (out["loss"].detach(), out["ce"].detach(), out["aux"].detach())
+        self._static_grads = [(p, p.grad) for p in self.model.parameters() if p.grad is not None]
+
+    def _graph_step(self, ids, labels) -> StepStats:
+        self._static_ids.copy_(ids, non_blocking=True)
+        self._static_lab.copy_(labels, non_blocking=True)
+        self._graph.replay()
+        for p, g in self._static_grads:              # the replay wrote these tensors
+            p.grad = g
+        lr = self.lr_at(self.step_idx)
+        self.opt.step(lr=lr)
+        self.step_idx += 1
+        loss, ce, aux = (t.clone() for t in self._static_out)
+        return StepStats(loss, ce, aux, ids.numel(), lr)
 
     # ------------------------------------------------------------------
     def state_dict(self) -> dict:

@@ -3,7 +3,8 @@ the GPUs, so these stand in for it together with the device status word that
 every test checks): the routed MoE FFN with one token, with every token sent to
 the same two experts (six experts receive none) and with capacity overflow,
 against the fp32 oracle; and bitwise-repeatable forward passes of the GEMM,
-flash attention and MoE inference path."""
+flash attention and MoE inference path; and the CUDA-graph training step against
+the eager one."""
 import pytest
 import torch
 
@@ -74,3 +75,48 @@ def test_forward_kernels_are_bitwise_repeatable(cuda_ext):
         m1, _ = ops.moe_ffn(xm, rw, w13, w2, 2, 0, True)
         m2, _ = ops.moe_ffn(xm, rw, w13, w2, 2, 0, True)
     assert torch.equal(m1, m2)
+
+
+def test_cuda_graph_training_step_matches_eager(cuda_ext):
+    """Trainer(cuda_graph=True) replays forward + backward as a CUDA graph after two eager
+    steps; losses and weights must follow the eager trainer's from the same start."""
+    from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig, TrainConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.engine import Trainer, synthetic_batch
+
+    cfg = ModelConfig(name="graph", vocab_size=4096, d_model=512, n_layers=2, n_heads=4, ffn_dim=512,
+                      tie_embeddings=False, max_seq_len=512,
+                      attn=AttentionConfig(kind="mla", kv_lora_rank=256, qk_rope_dim=64, qk_nope_dim=128,
+                                           v_head_dim=128),
+                      moe=MoEConfig(n_experts=8, top_k=2, ffn_dim=256, n_shared_experts=1))
+    tc = TrainConfig(lr=1e-3, warmup_steps=2, max_steps=20, grad_clip=1.0)
+    eager = Trainer(build_model(cfg, device="cuda", seed=0), tc)
+    eager2 = Trainer(build_model(cfg, device="cuda", seed=0), tc)
+    graph = Trainer(build_model(cfg, device="cuda", seed=0), tc, cuda_graph=True, graph_warmup=2)
+    le, lg = [], []
+    for step in range(6):
+        ids, labels = synthetic_batch(2, 256, cfg.vocab_size, seed=0, step=step, device="cuda")
+        le.append(float(eager.step(ids, labels, assume_all_valid=True).loss))
+        eager2.step(ids, labels, assume_all_valid=True)
+        lg.append(float(graph.step(ids, labels, assume_all_valid=True).loss))
+    assert graph._graph is not None, graph.graph_error
+    for a, b in zip(le, lg):
+        assert abs(a - b) < 2e-3 * abs(a), (le, lg)
+
+    def dist(m1, m2):   # global relative distance of all weights
+        num = sum(float((p.float() - q.float()).pow(2).sum()) for p, q in zip(m1.parameters(), m2.parameters()))
+        den = sum(float(q.float().pow(2).sum()) for q in m2.parameters())
+        return (num / den) ** 0.5
+
+    # the MoE backward accumulates with atomics, so two eager runs already drift apart a little
+    # (Adam turns tiny gradient differences of near-zero gradients into full-size updates)
+    noise = dist(eager2.model, eager.model)
+    assert dist(graph.model, eager.model) <= 3 * noise + 2e-3, (dist(graph.model, eager.model), noise)
+    # an eager step beside the graph (other flag), then back to the graph
+    ids, labels = synthetic_batch(2, 256, cfg.vocab_size, seed=0, step=6, device="cuda")
+    a = float(eager.step(ids, labels).loss)
+    b = float(graph.step(ids, labels).loss)
+    ids, labels = synthetic_batch(2, 256, cfg.vocab_size, seed=0, step=7, device="cuda")
+    c = float(eager.step(ids, labels, assume_all_valid=True).loss)
+    d = float(graph.step(ids, labels, assume_all_valid=True).loss)
+    assert abs(a - b) < 2e-3 * abs(a) and abs(c - d) < 2e-3 * abs(c), (a, b, c, d)
