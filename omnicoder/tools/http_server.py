@@ -3,9 +3,12 @@
 Endpoints (reference src/omnicoder/tools/http_server.py:147-1339):
   GET  /health                -> {"status": "ok", model info}
   POST /generate/text         {"prompt", "max_new_tokens", "temperature", "top_k", "top_p", "seed"}
-  POST /generate/unified      {"modality": "text", ...} (text only; other modalities need
-                               external diffusion weights -> 501)
-  POST /generate/image|video  -> 501 (the reference calls external diffusers pipelines)
+  POST /generate/unified      {"modality": "text", ...} (text only -> 501 for other modalities)
+  POST /generate/image|video  {"prompt", "grid_h", "grid_w", "frames", "temperature", "top_k", "seed"}
+                              -> {"shape", "layout", "pixels_b64"}: the model samples image / video
+                              code tokens of the unified vocabulary and a VQ-VAE decoder renders
+                              them (the reference calls external diffusion pipelines instead);
+                              501 when the app was built without decoders
 
 Unlike the reference (one request at a time per process), concurrent requests
 are batched: a collector task takes up to `max_batch` queued requests that
@@ -32,14 +35,20 @@ def _request_model():
     global _REQ
     if _REQ is None:
         from pydantic import create_model
-        _REQ = create_model("TextReq", prompt=(str, ...), max_new_tokens=(int, 64), temperature=(float, 0.0),
-                            top_k=(int, 0), top_p=(float, 1.0), seed=(int | None, None), modality=(str, "text"))
+        _REQ = (create_model("TextReq", prompt=(str, ...), max_new_tokens=(int, 64), temperature=(float, 0.0),
+                             top_k=(int, 0), top_p=(float, 1.0), seed=(int | None, None), modality=(str, "text")),
+                create_model("MediaReq", prompt=(str, ...), grid_h=(int, 8), grid_w=(int, 8), frames=(int, 4),
+                             temperature=(float, 1.0), top_k=(int, 0), seed=(int | None, None)))
     return _REQ
 
 
-def create_app(model, tokenizer=None, max_batch: int = 16, batch_window_s: float = 0.005):
+def create_app(model, tokenizer=None, max_batch: int = 16, batch_window_s: float = 0.005, image_vq=None,
+               video_vq=None, vocab=None):
+    """`image_vq` / `video_vq` (VQ-VAE decoders) and `vocab` (the unified vocabulary layout) enable
+    /generate/image and /generate/video: the model samples code tokens of that modality and the
+    decoder renders them; the response carries uint8 pixels (base64) and their shape."""
     from fastapi import FastAPI, HTTPException
-    TextReq = _request_model()
+    TextReq, MediaReq = _request_model()
 
     tok = tokenizer or get_tokenizer(model.cfg.vocab_size)
     dev = next(model.parameters()).device
@@ -110,13 +119,36 @@ def create_app(model, tokenizer=None, max_batch: int = 16, batch_window_s: float
     app.post("/generate/text")(gen_text)
     app.post("/generate/unified")(gen_unified)
 
-    @app.post("/generate/image")
-    async def gen_image():
-        raise HTTPException(501, "image generation needs external diffusion pipeline weights")
+    def _media(r, kind):
+        import base64
+        from ..multimodal.generation import generate_image, generate_video
+        vq = image_vq if kind == "image" else video_vq
+        if vq is None or vocab is None:
+            raise HTTPException(501, f"{kind} generation needs a {kind} VQ decoder and the unified vocabulary "
+                                     "layout (create_app(image_vq=..., video_vq=..., vocab=...))")
+        ids = torch.tensor([tok.encode(r.prompt) or [0]], device=dev)
+        gen = None
+        if r.seed is not None:
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(r.seed)
+        kw = dict(grid=(r.grid_h, r.grid_w), temperature=r.temperature, top_k=r.top_k, generator=gen)
+        out = (generate_image(model, vq, ids, vocab, **kw) if kind == "image"
+               else generate_video(model, vq, ids, vocab, frames=r.frames, **kw))[0]
+        pix = (out * 255).round().to(torch.uint8).cpu().contiguous()
+        state["served"] += 1
+        return {"shape": list(pix.shape), "layout": "CHW" if kind == "image" else "TCHW",
+                "pixels_b64": base64.b64encode(pix.numpy().tobytes()).decode()}
 
-    @app.post("/generate/video")
-    async def gen_video():
-        raise HTTPException(501, "video generation needs external diffusion pipeline weights")
+    async def gen_image(r):
+        return _media(r, "image")
+
+    async def gen_video(r):
+        return _media(r, "video")
+
+    gen_image.__annotations__ = {"r": MediaReq}
+    gen_video.__annotations__ = {"r": MediaReq}
+    app.post("/generate/image")(gen_image)
+    app.post("/generate/video")(gen_video)
 
     return app
 

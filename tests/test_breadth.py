@@ -401,3 +401,47 @@ def test_latent_refiner_and_interpolator():
         loss.backward()
         opt.step()
     assert float(loss) < 0.2 * first
+
+
+def _mm_setup():
+    from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.multimodal.vocab import VocabSidecar
+    cfg = ModelConfig(name="mm", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=256,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2), moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=64))
+    return build_model(cfg, device="cpu", seed=0).eval(), VocabSidecar([0, 99], [100, 163], [164, 227], [228, 291])
+
+
+def test_generate_codes_in_range_and_greedy():
+    from omnicoder.multimodal.generation import generate_codes
+    m, _ = _mm_setup()
+    prompt = torch.tensor([[5, 6, 7]])
+    codes = generate_codes(m, prompt, 100, 64, 6, temperature=0.0)
+    assert codes.shape == (1, 6) and codes.min() >= 0 and codes.max() < 64
+    ids = prompt
+    for c in codes[0].tolist():                          # greedy equals argmax over the range, step by step
+        with torch.no_grad():
+            logits = m(ids)["logits"][0, -1]
+        assert int(logits[100:164].argmax()) == c
+        ids = torch.cat([ids, torch.tensor([[100 + c]])], 1)
+    with pytest.raises(ValueError):
+        generate_codes(m, prompt, 280, 64, 2)
+
+
+def test_http_image_and_video_endpoints():
+    import base64
+    from fastapi.testclient import TestClient
+    from omnicoder.multimodal.vqvae import ImageVQVAE, VideoVQVAE
+    from omnicoder.tools.http_server import create_app
+    m, voc = _mm_setup()
+    torch.manual_seed(0)
+    iv = ImageVQVAE(width=8, levels=2, code_dim=8, codebook_size=64)
+    vv = VideoVQVAE(width=8, levels=2, code_dim=8, codebook_size=64)
+    with TestClient(create_app(m, image_vq=iv, video_vq=vv, vocab=voc)) as cli:
+        r = cli.post("/generate/image", json={"prompt": "a cat", "grid_h": 3, "grid_w": 2, "seed": 1}).json()
+        assert r["shape"] == [3, 12, 8] and len(base64.b64decode(r["pixels_b64"])) == 3 * 12 * 8
+        v = cli.post("/generate/video", json={"prompt": "waves", "grid_h": 2, "grid_w": 2, "frames": 3,
+                                              "temperature": 0.0}).json()
+        assert v["shape"] == [3, 3, 8, 8] and v["layout"] == "TCHW"
+    with TestClient(create_app(m)) as cli:
+        assert cli.post("/generate/image", json={"prompt": "x"}).status_code == 501

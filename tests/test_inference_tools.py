@@ -49,7 +49,7 @@ def test_http_server_batches_requests():
         assert all("text" in o for o in outs)
         h = cli.get("/health").json()
         assert h["served"] == 4 and h["batches"] < 4                  # at least two requests shared a batch
-        assert cli.post("/generate/image", json={}).status_code == 501
+        assert cli.post("/generate/image", json={"prompt": "x"}).status_code == 501   # no decoder given
 
 
 def test_gguf_roundtrip(tmp_path):
