@@ -19,16 +19,20 @@ from .encoders import PatchEncoder
 
 
 class TemporalMixer(nn.Module):
-    def __init__(self, d_model: int, kernel_size: int = 5, expansion: int = 2):
+    """causal=True pads only the past side, so the output at frame t sees frames <= t."""
+
+    def __init__(self, d_model: int, kernel_size: int = 5, expansion: int = 2, causal: bool = False):
         super().__init__()
         hidden = d_model * expansion
         self.inp = nn.Linear(d_model, 2 * hidden, bias=False)
-        self.conv = nn.Conv1d(hidden, hidden, kernel_size, padding=kernel_size // 2, groups=hidden)
+        self.conv = nn.Conv1d(hidden, hidden, kernel_size, groups=hidden)
         self.out = nn.Linear(hidden, d_model, bias=False)
+        k = kernel_size
+        self.pad = (k - 1, 0) if causal else (k // 2, k - 1 - k // 2)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         a, b = self.inp(x).chunk(2, dim=-1)
-        y = self.conv((a * F.gelu(b)).transpose(1, 2)).transpose(1, 2)
+        y = self.conv(F.pad((a * F.gelu(b)).transpose(1, 2), self.pad)).transpose(1, 2)
         return self.out(y)
 
 

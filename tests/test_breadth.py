@@ -445,3 +445,54 @@ def test_http_image_and_video_endpoints():
         assert v["shape"] == [3, 3, 8, 8] and v["layout"] == "TCHW"
     with TestClient(create_app(m)) as cli:
         assert cli.post("/generate/image", json={"prompt": "x"}).status_code == 501
+
+
+def test_btm_merge_round_robin_and_mean():
+    from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.multimodal_tasks import btm_merge
+    cfg = ModelConfig(name="b", vocab_size=300, d_model=64, n_layers=1, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2), moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=64))
+    d0, d1, st = (build_model(cfg, device="cpu", seed=s) for s in (1, 2, 3))
+    rep = btm_merge(st, [d0, d1])
+    w, a, b = st.state_dict()["blocks.0.ffn.w13"], d0.state_dict()["blocks.0.ffn.w13"], d1.state_dict()["blocks.0.ffn.w13"]
+    assert torch.equal(w[0], a[0]) and torch.equal(w[1], b[0]) and torch.equal(w[2], a[1]) and torch.equal(w[3], b[1])
+    q = st.state_dict()["blocks.0.attn.wqkv"]
+    torch.testing.assert_close(q.float(), (d0.state_dict()["blocks.0.attn.wqkv"].float()
+                                            + d1.state_dict()["blocks.0.attn.wqkv"].float()) / 2)
+    assert rep["blocks.0.ffn.w2"] == "experts round-robin" and rep["embed"] == "mean of 2"
+
+
+def test_latent3d_video_sr_policy_trainers_reduce_loss():
+    from omnicoder.multimodal.video import OrthoRenderer, TemporalMixer, VoxelLatentHead
+    from omnicoder.training import multimodal_tasks as mt
+    torch.manual_seed(0)
+    m, _ = _mm_setup()
+    ids = torch.randint(0, 100, (2, 8))
+    target = torch.zeros(2, 3, 16, 16)
+    target[:, 0, 4:12, 4:12] = 1.0
+    l3 = mt.train_latent3d(m, VoxelLatentHead(64, depth=4, height=8, width=8, hidden=32),
+                           OrthoRenderer(depth=4, out_h=16, out_w=16), iter(lambda: (ids, target), None), 60, lr=3e-2)
+    assert l3[-1] < 0.5 * l3[0]
+    mix = TemporalMixer(8, kernel_size=3, causal=True)
+    x = torch.randn(1, 9, 8)
+    x2 = x.clone()
+    x2[:, 5] += 1.0
+    assert torch.equal(mix(x)[:, :5], mix(x2)[:, :5])               # causal: the past ignores frame 5
+    t = torch.arange(12).float()
+    clip = torch.stack([torch.sin(0.5 * t + p) for p in range(8)], -1)[None]
+    lv = mt.train_video_temporal(mix, iter(lambda: clip, None), 150, lr=1e-2, smoothness=0.01)
+    assert lv[-1] < 0.3 * lv[0]
+    hr = torch.rand(2, 3, 16, 16)
+    lr_img = F.avg_pool2d(hr, 2)
+    ls = mt.train_super_resolution(mt.SuperResolver(2, width=16, depth=2), iter(lambda: (lr_img, hr), None), 80,
+                                   lr=3e-3)
+    assert ls[-1] < ls[0]
+    r = mt.retention_targets(10, 4)
+    assert r[-4:].eq(1).all() and r[0] == 0 and bool((r[1:6] > r[:5]).all())
+    lp = mt.train_policy_head(m, torch.nn.Linear(64, 1), iter(lambda: ids, None), 60, lr=3e-2,
+                              target_fn=lambda i: mt.retention_targets(i.shape[1], 3).expand(i.shape))
+    assert lp[-1] < lp[0]
+    p, q = torch.randn(2, 3, 8, 8), torch.randn(2, 3, 8, 8)
+    assert float(mt.recon_loss(p, q, "huber")) > 0 and float(mt.recon_loss(p, p, "mae")) == 0
+    assert float(mt.recon_loss(p, q, "feature", features=torch.nn.Conv2d(3, 4, 3))) > 0
