@@ -496,3 +496,50 @@ def test_latent3d_video_sr_policy_trainers_reduce_loss():
     p, q = torch.randn(2, 3, 8, 8), torch.randn(2, 3, 8, 8)
     assert float(mt.recon_loss(p, q, "huber")) > 0 and float(mt.recon_loss(p, p, "mae")) == 0
     assert float(mt.recon_loss(p, q, "feature", features=torch.nn.Conv2d(3, 4, 3))) > 0
+
+
+def test_vector_index_exact_ivf_and_text_retriever():
+    from omnicoder.retrieval.vector_index import IVFIndex, TextRetriever, VectorIndex
+    torch.manual_seed(0)
+    x = torch.randn(1000, 32)
+    q = torch.randn(5, 32)
+    for metric in ("cosine", "ip", "l2"):
+        idx = VectorIndex(32, metric, chunk=300)
+        idx.add(x)
+        s, i = idx.search(q, 4)
+        if metric == "l2":
+            want = torch.cdist(q, x).topk(4, largest=False).indices
+        else:
+            xx = F.normalize(x, dim=1) if metric == "cosine" else x
+            qq = F.normalize(q, dim=1) if metric == "cosine" else q
+            want = (qq @ xx.t()).topk(4).indices
+        assert torch.equal(i, want), metric
+    ivf = IVFIndex(32, n_lists=16, nprobe=16)                 # probing every list is exact
+    ivf.add(x)
+    _, ii = ivf.search(q, 4)
+    assert torch.equal(ii, (F.normalize(q, dim=1) @ F.normalize(x, dim=1).t()).topk(4).indices)
+    docs = ["the cat sat on the mat " * 3, "gpu kernels use tensor memory and tma loads " * 3,
+            "rivers flow into the sea " * 3]
+    tr = TextRetriever(docs, dim=512, chunk_words=16, stride=12)
+    assert "tensor" in tr.search("tensor memory kernels", k=1)[0].text
+
+
+def test_media_metrics():
+    from omnicoder.eval import media_metrics as mm
+    assert mm.word_error_rate("the cat sat", "the cat sat") == 0
+    assert mm.word_error_rate("the cat sat down", "the bat sat") == pytest.approx(0.5)
+    assert mm.bleu(["the cat is on the mat"], [["the cat is on the mat"]]) == pytest.approx(1.0)
+    assert 0 < mm.bleu(["the cat is on a mat today"], [["the cat is on the mat"]]) < 1
+    assert mm.exact_match_accuracy([("Paris.", "paris"), ("4", "5")]) == 0.5
+    torch.manual_seed(0)
+    a = torch.rand(2, 3, 32, 32)
+    assert mm.psnr(a, a) == float("inf") and mm.ssim(a, a) == pytest.approx(1.0, abs=1e-5)
+    noisy = (a + 0.1 * torch.randn_like(a)).clamp(0, 1)
+    assert 15 < mm.psnr(noisy, a) < 30 and mm.ssim(noisy, a) < mm.ssim(a, a)
+    f1, f2 = torch.randn(500, 8), torch.randn(500, 8) + 2.0
+    assert mm.frechet_distance(f1, f1) == pytest.approx(0.0, abs=1e-6)
+    assert mm.frechet_distance(f1, f2) == pytest.approx(32.0, rel=0.15)   # |mu diff|^2 = 8 * 4
+    assert mm.embedding_alignment(f1, f1) == pytest.approx(1.0)
+    assert mm.temporal_consistency(torch.ones(5, 4)) == pytest.approx(1.0)
+    s = torch.randn(1000)
+    assert mm.snr_db(s, s + 0.1 * torch.randn(1000)) == pytest.approx(20.0, abs=1.5)
