@@ -10,9 +10,9 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 
-def _data(rope: bool):
+def _data(rope: bool, world: int = 2):
     g = torch.Generator().manual_seed(3)
-    B, S, H, Hk, Dk, Dv, Dr = 2, 16, 4, 2, 8, 8, 4
+    B, S, H, Hk, Dk, Dv, Dr = 2, 16, 2 * world, world, 8, 8, 4
     T = B * S
     q = torch.randn(T, H, Dk + (Dr if rope else 0), generator=g)
     k = torch.randn(T, Hk, Dk, generator=g)
@@ -36,7 +36,7 @@ def _worker(rank, world, port, q_out):
         worst = 0.0
         for rope in (False, True):
             for window in (0, 5):
-                B, S, q, k, v, kr, dout = _data(rope)
+                B, S, q, k, v, kr, dout = _data(rope, world)
                 full = [t.clone().requires_grad_(True) for t in (q, k, v)] + \
                        ([kr.clone().requires_grad_(True)] if rope else [None])
                 ref = attention_torch(*full[:3], full[3], seq=S, causal=True, window=window)
@@ -64,7 +64,7 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2])
+@pytest.mark.parametrize("world", [2, 4])
 def test_context_parallel_matches_full_attention(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

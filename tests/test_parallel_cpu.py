@@ -77,9 +77,8 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("cf", [0.0, 1.0])
-def test_ep_dp_zero1_matches_single_process(cf):
-    world = 2
+@pytest.mark.parametrize("cf,world", [(0.0, 2), (1.0, 2), (0.0, 4)])
+def test_ep_dp_zero1_matches_single_process(cf, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
