@@ -21,7 +21,7 @@ def pytest_configure(config):
 
 @pytest.fixture(scope="session")
 def cuda_ext():
-    """The compiled extension on a GPU box; skips on CPU-only machines."""
+    """The compiled extension on a machine with a CUDA device; skips on CPU-only machines."""
     import torch
 
     if not torch.cuda.is_available():
