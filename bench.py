@@ -311,6 +311,17 @@ def main():
                     other += 1
         launches = {"ours_per_step": ours, "other_per_step": other}
 
+    from omnicoder.utils.flops import train_flops_per_token
+    fpt = train_flops_per_token(cfg, S)
+    mfu_info = {"train_gflop_per_token": fpt / 1e9, "model_tflops_per_gpu": value * fpt / world / 1e12,
+                "note": "6 x active params + causal attention, per trained token"}
+    try:
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        mfu_info["of_measured_bf16_sustained"] = mfu_info["model_tflops_per_gpu"] / pk["bf16_tflops_sustained"]
+    except (OSError, KeyError, ValueError):
+        pass
+    mfu_info["of_nominal_dense_bf16_2250"] = mfu_info["model_tflops_per_gpu"] / 2250.0
     graph_state = ("forward+backward replayed" if trainer._graph is not None else
                    (f"off ({trainer.graph_error})" if trainer.graph_error else "off"))
     decode = None
@@ -333,7 +344,7 @@ def main():
                        "optimizer": "AdamW fp32 master, grad clip 1.0",
                        "cuda_graph": graph_state,
                        "l2": "working set (14.6 GB bf16 weights, 8192 tokens/GPU of activations) >> 126 MB L2"},
-            "loss": loss_val, "e2e": e2e,
+            "loss": loss_val, "e2e": e2e, "mfu": mfu_info,
             "gpu_launches": (launches["ours_per_step"] * args.steps) if launches else None,
             "launches_per_step": launches, "clocks": clk, "impl": "ours", "decode": decode,
         }

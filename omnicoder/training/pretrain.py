@@ -167,6 +167,7 @@ def main(argv=None):
 
 
 def _train_loop(a, trainer, model, it, dev, world, rank, start, state_path, log, ev0, ev1, hb, inj):
+    from ..utils.flops import train_flops_per_token
     t_last, tok_acc = time.time(), 0
     for step in range(start, a.steps):
         inj.at_step(rank, step, hb)
@@ -189,8 +190,10 @@ def _train_loop(a, trainer, model, it, dev, world, rank, start, state_path, log,
             else:
                 secs = time.time() - t_last
                 t_last = time.time()
+            tps = tok_acc / max(secs, 1e-9)
             rec = {"step": step + 1, "loss": loss, "ce": float(st.ce), "aux": float(st.aux), "lr": st.lr,
-                   "tokens_per_s": tok_acc / max(secs, 1e-9), "time": time.time()}
+                   "tokens_per_s": tps, "model_tflops_per_gpu": tps * train_flops_per_token(model.cfg, a.seq_len)
+                   / world / 1e12, "time": time.time()}
             tok_acc = 0
             if rank == 0:
                 print(f"[pretrain] step {step + 1}/{a.steps} loss {loss:.4f} lr {st.lr:.2e} "

@@ -543,3 +543,17 @@ def test_media_metrics():
     assert mm.temporal_consistency(torch.ones(5, 4)) == pytest.approx(1.0)
     s = torch.randn(1000)
     assert mm.snr_db(s, s + 0.1 * torch.randn(1000)) == pytest.approx(20.0, abs=1.5)
+
+
+def test_train_flops_per_token_by_hand():
+    from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig
+    from omnicoder.utils.flops import active_params_per_token, mfu, train_flops_per_token
+    cfg = ModelConfig(name="f", vocab_size=100, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2),
+                      moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=32, n_shared_experts=1))
+    attn = 64 * 16 * (4 + 2 * 2) + 4 * 16 * 64                 # wqkv + wo
+    ffn = 3 * (3 * 64 * 32) + 4 * 64                           # 2 routed + 1 shared expert, router
+    assert active_params_per_token(cfg) == 2 * (attn + ffn) + 100 * 64
+    fpt = train_flops_per_token(cfg, 32)
+    assert fpt == 6 * active_params_per_token(cfg) + 3 * 2 * 2 * 16 * 4 * (16 + 16)
+    assert mfu(1e12 / fpt, cfg, 32, 1, 1.0) == pytest.approx(1.0)
