@@ -557,3 +557,17 @@ def test_train_flops_per_token_by_hand():
     fpt = train_flops_per_token(cfg, 32)
     assert fpt == 6 * active_params_per_token(cfg) + 3 * 2 * 2 * 16 * 4 * (16 + 16)
     assert mfu(1e12 / fpt, cfg, 32, 1, 1.0) == pytest.approx(1.0)
+
+
+def test_import_changes_no_torch_flags():
+    import subprocess
+    import sys
+    code = ("import torch\n"
+            "f = lambda: (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32,\n"
+            "             torch.get_float32_matmul_precision(), torch.are_deterministic_algorithms_enabled())\n"
+            "a = f()\n"
+            "import omnicoder, omnicoder.ops, omnicoder.models.lm, omnicoder.training.engine, omnicoder.parallel.zero\n"
+            "assert f() == a, (a, f())\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120,
+                       cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    assert r.returncode == 0, r.stderr[-500:]
