@@ -66,6 +66,53 @@ def sample_next_token(logits: torch.Tensor, temperature: float = 0.0, top_k: int
     return torch.multinomial(flat, 1, generator=generator).view(p.shape[:-1])
 
 
+class LogitProcessor:
+    """Penalties and biases applied to the logits before sampling (reference
+    src/omnicoder/inference/generate.py:500-690): CTRL-style repetition penalty (the logit of
+    a token already in the sequence is divided by `repetition_penalty` when positive and
+    multiplied by it when negative), presence / frequency penalties (minus `presence` once a
+    token occurred, minus `frequency` x its count) and an additive per-token bias.  Token
+    counts live on the device ([B, V], updated with scatter_add), so no step reads the host."""
+
+    def __init__(self, batch: int, vocab: int, device, repetition_penalty: float = 1.0, presence_penalty: float = 0.0,
+                 frequency_penalty: float = 0.0, logit_bias: dict | None = None):
+        self.rep, self.pres, self.freq = repetition_penalty, presence_penalty, frequency_penalty
+        self.counts = torch.zeros(batch, vocab, device=device)
+        self.bias = None
+        if logit_bias:
+            self.bias = torch.zeros(vocab, device=device)
+            for t, b in logit_bias.items():
+                self.bias[int(t)] = float(b)
+
+    @property
+    def active(self) -> bool:
+        return self.rep != 1.0 or self.pres != 0.0 or self.freq != 0.0 or self.bias is not None
+
+    def observe(self, ids: torch.Tensor) -> None:
+        ids = ids.reshape(self.counts.shape[0], -1)
+        self.counts.scatter_add_(1, ids, torch.ones_like(ids, dtype=self.counts.dtype))
+
+    def __call__(self, logits: torch.Tensor) -> torch.Tensor:
+        if not self.active:
+            return logits
+        x = logits.float()
+        seen = self.counts > 0
+        if self.rep != 1.0:
+            x = torch.where(seen, torch.where(x > 0, x / self.rep, x * self.rep), x)
+        if self.pres or self.freq:
+            x = x - self.pres * seen.float() - self.freq * self.counts
+        if self.bias is not None:
+            x = x + self.bias
+        return x
+
+
+def load_logit_bias(path: str) -> dict:
+    """JSON object {token id: additive bias}."""
+    import json
+    with open(path) as f:
+        return {int(k): float(v) for k, v in json.load(f).items()}
+
+
 @dataclass
 class GenStats:
     prompt_tokens: int = 0
@@ -122,11 +169,14 @@ def _sync(t: torch.Tensor):
 def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: float = 0.8, top_k: int = 40,
              top_p: float = 0.9, draft_model=None, speculative_draft_len: int = 0, kvq: str = "none",
              window_size: int = 0, return_stats: bool = False, eos_id: int | None = None, seed: int | None = None,
-             max_len: int | None = None, cuda_graph: bool = True, **_unused):
+             max_len: int | None = None, cuda_graph: bool = True, repetition_penalty: float = 1.0,
+             presence_penalty: float = 0.0, frequency_penalty: float = 0.0, logit_bias: dict | None = None,
+             **_unused):
     """Generate `max_new_tokens` tokens after `input_ids` [B, S] (or [S]).  Returns
     [B, S + max_new_tokens] (and GenStats with return_stats).  On CUDA the
     decode step is captured once as a CUDA graph (`cuda_graph=False` runs it
-    eagerly)."""
+    eagerly).  Repetition / presence / frequency penalties and `logit_bias` (LogitProcessor)
+    apply on the plain decode path; speculative decoding samples without them."""
     model.eval()
     squeeze = input_ids.dim() == 1
     ids = input_ids[None] if squeeze else input_ids
@@ -149,7 +199,13 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         cache = KVCache(cfg, B, L, dev, dtype=model.embed.dtype, kv_dtype=kv_dtype)
         t0 = time.perf_counter()
         logits = _prefill(model, ids, cache)
-        tok = sample_next_token(logits, temperature, top_k, top_p, gen)
+        proc = LogitProcessor(B, logits.shape[-1], dev, repetition_penalty, presence_penalty, frequency_penalty,
+                              logit_bias)
+        if proc.active:
+            proc.observe(ids)
+        tok = sample_next_token(proc(logits), temperature, top_k, top_p, gen)
+        if proc.active:
+            proc.observe(tok)
         _sync(tok)
         stats.prefill_s = time.perf_counter() - t0
         toks = [tok]
@@ -162,7 +218,9 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         for _ in range(max_new_tokens - 1):
             ts = time.perf_counter()
             logits = (step(tok[:, None]) if step is not None else model.forward_cached(tok[:, None], cache))[:, -1]
-            tok = sample_next_token(logits, temperature, top_k, top_p, gen)
+            tok = sample_next_token(proc(logits), temperature, top_k, top_p, gen)
+            if proc.active:
+                proc.observe(tok)
             if eos_id is not None:
                 done |= tok == eos_id
                 tok = torch.where(done, torch.full_like(tok, eos_id), tok)
@@ -270,6 +328,10 @@ def main(argv=None):
     ap.add_argument("--temperature", type=float, default=0.8)
     ap.add_argument("--top_k", type=int, default=40)
     ap.add_argument("--top_p", type=float, default=0.9)
+    ap.add_argument("--repetition_penalty", type=float, default=1.0)
+    ap.add_argument("--presence_penalty", type=float, default=0.0)
+    ap.add_argument("--frequency_penalty", type=float, default=0.0)
+    ap.add_argument("--logit_bias_file", default=None, help="JSON {token id: additive bias}")
     ap.add_argument("--kvq", default="none", choices=["none", "int8", "u8"])
     ap.add_argument("--window_size", type=int, default=0)
     ap.add_argument("--draft_preset", default=None)
@@ -291,6 +353,9 @@ def main(argv=None):
         if a.draft_ckpt:
             maybe_load_checkpoint(draft, a.draft_ckpt)
     out, st = generate(model, ids, a.max_new_tokens, a.temperature, a.top_k, a.top_p, draft_model=draft,
+                       repetition_penalty=a.repetition_penalty, presence_penalty=a.presence_penalty,
+                       frequency_penalty=a.frequency_penalty,
+                       logit_bias=load_logit_bias(a.logit_bias_file) if a.logit_bias_file else None,
                        speculative_draft_len=a.speculative_draft_len, kvq=a.kvq, window_size=a.window_size,
                        return_stats=True, seed=a.seed)
     text = tok.decode(out[0, ids.shape[1]:].tolist())

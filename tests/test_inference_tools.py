@@ -140,3 +140,28 @@ def test_onnx_session_needs_onnxruntime():
         pytest.skip("onnxruntime is installed")
     with pytest.raises(RuntimeError, match="onnxruntime"):
         runtimes.open_session("missing.onnx")
+
+
+def test_logit_processor_penalties_and_bias():
+    from omnicoder.inference.generate import LogitProcessor, generate, load_logit_bias
+    p = LogitProcessor(1, 6, "cpu", repetition_penalty=2.0, presence_penalty=0.5, frequency_penalty=0.25,
+                       logit_bias={5: 3.0})
+    p.observe(torch.tensor([[1, 1, 2]]))
+    x = p(torch.tensor([[1.0, 4.0, -2.0, 1.0, 0.0, 0.0]]))
+    want = torch.tensor([[1.0, 4.0 / 2 - 0.5 - 0.5, -2.0 * 2 - 0.5 - 0.25, 1.0, 0.0, 3.0]])
+    torch.testing.assert_close(x, want)
+    assert not LogitProcessor(1, 6, "cpu").active
+    cfg, m = _tiny()
+    prompt = torch.tensor([[3, 4, 5]])
+    out = generate(m, prompt, 12, temperature=0.0, repetition_penalty=1e6, presence_penalty=1e6)
+    new = out[0, 3:].tolist()
+    assert len(set(new)) == len(new) and not set(new) & {3, 4, 5}      # nothing repeats
+    forced = generate(m, prompt, 5, temperature=0.0, logit_bias={42: 1e4})
+    assert (forced[0, 3:] == 42).all()
+
+
+def test_load_logit_bias(tmp_path):
+    from omnicoder.inference.generate import load_logit_bias
+    f = tmp_path / "bias.json"
+    f.write_text(json.dumps({"7": -5, "9": 2.5}))
+    assert load_logit_bias(str(f)) == {7: -5.0, 9: 2.5}
