@@ -2,7 +2,8 @@
 
 Endpoints (reference src/omnicoder/tools/http_server.py:147-1339):
   GET  /health                -> {"status": "ok", model info}
-  POST /generate/text         {"prompt", "max_new_tokens", "temperature", "top_k", "top_p", "seed"}
+  POST /generate/text         {"prompt", "max_new_tokens", "temperature", "top_k", "top_p", "seed",
+                               "repetition_penalty", "presence_penalty", "frequency_penalty"}
   POST /generate/unified      {"modality": "text", ...} (text only -> 501 for other modalities)
   POST /generate/image|video  {"prompt", "grid_h", "grid_w", "frames", "temperature", "top_k", "seed"}
                               -> {"shape", "layout", "pixels_b64"}: the model samples image / video
@@ -36,7 +37,9 @@ def _request_model():
     if _REQ is None:
         from pydantic import create_model
         _REQ = (create_model("TextReq", prompt=(str, ...), max_new_tokens=(int, 64), temperature=(float, 0.0),
-                             top_k=(int, 0), top_p=(float, 1.0), seed=(int | None, None), modality=(str, "text")),
+                             top_k=(int, 0), top_p=(float, 1.0), seed=(int | None, None), modality=(str, "text"),
+                             repetition_penalty=(float, 1.0), presence_penalty=(float, 0.0),
+                             frequency_penalty=(float, 0.0)),
                 create_model("MediaReq", prompt=(str, ...), grid_h=(int, 8), grid_w=(int, 8), frames=(int, 4),
                              temperature=(float, 1.0), top_k=(int, 0), seed=(int | None, None)))
     return _REQ
@@ -72,14 +75,17 @@ def create_app(model, tokenizer=None, max_batch: int = 16, batch_window_s: float
             buckets: dict = {}
             for item in group:
                 r, ids, fut = item
-                key = (ids.shape[1], r.max_new_tokens, r.temperature, r.top_k, r.top_p, r.seed)
+                key = (ids.shape[1], r.max_new_tokens, r.temperature, r.top_k, r.top_p, r.seed,
+                       r.repetition_penalty, r.presence_penalty, r.frequency_penalty)
                 buckets.setdefault(key, []).append(item)
             for key, items in buckets.items():
                 r0 = items[0][0]
                 ids = torch.cat([it[1] for it in items]).to(dev)
                 try:
                     out = await asyncio.to_thread(generate, model, ids, r0.max_new_tokens, r0.temperature, r0.top_k,
-                                                  r0.top_p, seed=r0.seed)
+                                                  r0.top_p, seed=r0.seed, repetition_penalty=r0.repetition_penalty,
+                                                  presence_penalty=r0.presence_penalty,
+                                                  frequency_penalty=r0.frequency_penalty)
                     state["batches"] += 1
                     for i, (_, pid, fut) in enumerate(items):
                         fut.set_result(tok.decode(out[i, pid.shape[1]:].tolist()))
