@@ -70,6 +70,9 @@ def parse_args(argv=None):
     ap.add_argument("--tokenizer", default=None, help="local Hugging Face tokenizer directory (default: bytes)")
     ap.add_argument("--ep_transport", default="auto", choices=["auto", "p2p", "nccl"])
     ap.add_argument("--pg_timeout", type=float, default=600.0, help="process-group timeout (s)")
+    ap.add_argument("--log_expert_load", action="store_true",
+                    help="single process: add per-layer expert load (CV, busiest share) to each log record "
+                         "(one extra no-grad forward per log interval)")
     ap.add_argument("--heartbeat_timeout", type=float, default=0.0,
                     help="multi-rank: check every rank's heartbeat before each step, naming a rank that left, "
                          "died or stalled for this many seconds (0: off)")
@@ -194,6 +197,10 @@ def _train_loop(a, trainer, model, it, dev, world, rank, start, state_path, log,
             rec = {"step": step + 1, "loss": loss, "ce": float(st.ce), "aux": float(st.aux), "lr": st.lr,
                    "tokens_per_s": tps, "model_tflops_per_gpu": tps * train_flops_per_token(model.cfg, a.seq_len)
                    / world / 1e12, "time": time.time()}
+            if a.log_expert_load and world == 1:
+                from ..utils.diagnostics import expert_load
+                el = expert_load(model, ids.to(dev))
+                rec["expert_load_cv"], rec["expert_max_share"] = el["cv"], el["max_share"]
             tok_acc = 0
             if rank == 0:
                 print(f"[pretrain] step {step + 1}/{a.steps} loss {loss:.4f} lr {st.lr:.2e} "

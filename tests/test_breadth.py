@@ -571,3 +571,17 @@ def test_import_changes_no_torch_flags():
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120,
                        cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     assert r.returncode == 0, r.stderr[-500:]
+
+
+def test_expert_load_diagnostic():
+    from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.utils.diagnostics import expert_load
+    cfg = ModelConfig(name="d", vocab_size=200, d_model=64, n_layers=3, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2), moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=32))
+    m = build_model(cfg, device="cpu", seed=0)
+    ids = torch.randint(0, 200, (2, 16))
+    r = expert_load(m, ids)
+    assert r["counts"].shape == (3, 4) and (r["counts"].sum(1) == 2 * 16 * 2).all()
+    assert len(r["cv"]) == 3 and all(0.25 <= s <= 1.0 for s in r["max_share"])
+    assert not m.blocks[0].ffn._forward_pre_hooks                       # hooks removed

@@ -29,9 +29,11 @@ def test_pretrain_text_folder_and_resume(tmp_path):
     assert out.exists() and st.exists()
     ck = torch.load(out, weights_only=False)
     assert ck["step"] == 2 and any(k.endswith(".w1") for k in ck["model"])
-    _run(["omnicoder.training.pretrain", "--data", str(d), "--steps", "3", "--resume_ckpt", str(out)] + common)
+    _run(["omnicoder.training.pretrain", "--data", str(d), "--steps", "3", "--resume_ckpt", str(out),
+          "--log_expert_load"] + common)
     recs = [json.loads(l) for l in log.read_text().splitlines()]
     assert [r["step"] for r in recs] == [1, 2, 3]          # the resumed run continues at step 3
+    assert "expert_load_cv" in recs[-1] and recs[-1]["model_tflops_per_gpu"] > 0
 
 
 def test_torchrun_ep_two_cpu_ranks(tmp_path):
