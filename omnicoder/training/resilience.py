@@ -3,7 +3,8 @@
 CheckpointManager keeps `keep` step checkpoints (model weights + trainer state:
 step, optimiser moments) in one directory, each written to a temporary file
 and renamed into place, so a crash mid-save never leaves a half-written file
-under a checkpoint's name.  `load_latest` tries the newest first and falls
+under a checkpoint's name (`save_async` copies the state to host memory and writes
+on a background thread).  `load_latest` tries the newest first and falls
 back to older ones when a file is unreadable (truncated, corrupted), logging
 each rejected file.
 
@@ -23,6 +24,7 @@ import glob
 import logging
 import os
 import re
+import threading
 from typing import Callable
 
 import torch
@@ -46,17 +48,52 @@ class CheckpointManager:
                  if (m := pat.search(p))]
         return sorted(found)
 
-    def save(self, step: int, model: torch.nn.Module, trainer) -> str:
-        obj = {"step": step, "model": {k: v.detach().cpu() for k, v in model.state_dict().items()},
-               "trainer": _to_cpu(trainer.state_dict())}
+    def _snapshot(self, step, model, trainer) -> dict:
+        # copy=True: for CPU tensors .cpu() would alias the live weights
+        return {"step": step, "model": {k: v.detach().to("cpu", copy=True) for k, v in model.state_dict().items()},
+                "trainer": _to_cpu(trainer.state_dict())}
+
+    def _write(self, step: int, obj: dict) -> str:
         path = self._path(step)
         _atomic_save(obj, path)
         for old in self.steps()[:-self.keep]:
             os.unlink(self._path(old))
         return path
 
+    def save(self, step: int, model: torch.nn.Module, trainer) -> str:
+        self.wait()
+        return self._write(step, self._snapshot(step, model, trainer))
+
+    def save_async(self, step: int, model: torch.nn.Module, trainer) -> None:
+        """Copy the state to host memory now (training may continue and change the device
+        tensors afterwards) and write the file on a background thread; at most one write is in
+        flight (a new save first waits for the previous one)."""
+        self.wait()
+        obj = self._snapshot(step, model, trainer)
+        self._error = None
+
+        def run():
+            try:
+                self._write(step, obj)
+            except Exception as e:          # surfaced by wait()
+                self._error = e
+
+        self._thread = threading.Thread(target=run, name="omnicoder-ckpt", daemon=False)
+        self._thread.start()
+
+    def wait(self) -> None:
+        t = getattr(self, "_thread", None)
+        if t is not None:
+            t.join()
+            self._thread = None
+        err = getattr(self, "_error", None)
+        if err is not None:
+            self._error = None
+            raise err
+
     def load_latest(self, model: torch.nn.Module, trainer) -> int:
         """Load the newest readable checkpoint; returns its step (0 when there is none)."""
+        self.wait()
         for step in reversed(self.steps()):
             path = self._path(step)
             try:
@@ -71,7 +108,7 @@ class CheckpointManager:
 
 def _to_cpu(x):
     if isinstance(x, torch.Tensor):
-        return x.detach().cpu()
+        return x.detach().to("cpu", copy=True)
     if isinstance(x, dict):
         return {k: _to_cpu(v) for k, v in x.items()}
     if isinstance(x, (list, tuple)):

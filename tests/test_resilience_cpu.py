@@ -214,3 +214,25 @@ def test_resume_from_last_good_checkpoint(tmp_path):
     for (n, a), b in zip(ref.model.state_dict().items(), t2.model.state_dict().values()):
         torch.testing.assert_close(a, b, atol=1e-6, rtol=1e-6, msg=n)
     assert mgr.steps() == [4, 6]
+
+
+def test_async_checkpoint_is_a_consistent_snapshot(tmp_path):
+    from omnicoder.training.resilience import CheckpointManager
+    t = _DPTrainer.__new__(_DPTrainer)
+    torch.manual_seed(0)
+    t.model, t.step_idx = nn.Linear(8, 4), 3
+    want = {k: v.clone() for k, v in t.model.state_dict().items()}
+    mgr = CheckpointManager(str(tmp_path), keep=2)
+    mgr.save_async(3, t.model, t)
+    with torch.no_grad():
+        t.model.weight.add_(1.0)                 # training goes on while the file is written
+    mgr.wait()
+    fresh = _DPTrainer.__new__(_DPTrainer)
+    fresh.model, fresh.step_idx = nn.Linear(8, 4), 0
+    assert mgr.load_latest(fresh.model, fresh) == 3 and fresh.step_idx == 3
+    for k, v in fresh.model.state_dict().items():
+        assert torch.equal(v, want[k]), k
+    for s in (4, 5):
+        mgr.save_async(s, t.model, t)
+    mgr.wait()
+    assert mgr.steps() == [4, 5]
