@@ -4,6 +4,7 @@ one batch-64 decode step of the long-context MoE model (24L d2048, MLA latent
 512 + rope 64, 16 heads, 32 experts of ffn 1408, top-4, vocab 32000).
 
     python -m omnicoder.benchmarks.bench_skinny [--json out.json]
+    python -m omnicoder.benchmarks.bench_skinny --grouped-calls 3   # only 3 grouped gate|up calls (for ncu)
 
 L2 is flushed before every timed call, so each call streams its weight matrix
 from HBM; reported GB/s = weight bytes / time.
@@ -33,11 +34,13 @@ DENSE = [
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", default=None)
+    ap.add_argument("--grouped-calls", type=int, default=0,
+                    help="run only this many untimed grouped gate|up calls (a small case for a profiler)")
     a = ap.parse_args(argv)
     C = _ext.load()
     dev = torch.device("cuda")
     res = []
-    for name, M, N, K in DENSE:
+    for name, M, N, K in ([] if a.grouped_calls else DENSE):
         x = torch.randn(M, K, device=dev).to(torch.bfloat16)
         w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
@@ -60,6 +63,12 @@ def main(argv=None):
     w2 = (torch.randn(E, D, F, device=dev) * 0.02).to(torch.bfloat16)
     act = torch.empty(rows, F, device=dev, dtype=torch.bfloat16)
     y = torch.empty(rows, D, device=dev, dtype=torch.bfloat16)
+    if a.grouped_calls:
+        for _ in range(a.grouped_calls):
+            C.gemm_skinny_grouped(x, w13, off, act, EPI_SWIGLU, 1.0, rows)
+        torch.cuda.synchronize()
+        _ext.check_status()
+        return
     t13 = time_fn(lambda: C.gemm_skinny_grouped(x, w13, off, act, EPI_SWIGLU, 1.0, rows))
     t2 = time_fn(lambda: C.gemm_skinny_grouped(act, w2, off, y, EPI_BF16, 1.0, rows))
     # cuBLAS reference of the same work: one matmul per expert

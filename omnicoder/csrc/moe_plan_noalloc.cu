@@ -69,6 +69,8 @@ extern "C" int omni_moe_permute_plan_noalloc(const int* idx, int T, int K, int E
   if ((long long)T * K > (1ll << 30)) return OMNI_NOALLOC_TOO_LARGE;
   const long long need = scratch_ints(T, K, E);
   if (need > OMNI_PLAN_NOALLOC_MAX_INTS) return OMNI_NOALLOC_TOO_LARGE;
+  // an error left by unrelated earlier work is not ours to consume: report it and launch nothing
+  if (cudaPeekAtLastError() != cudaSuccess) return OMNI_NOALLOC_PENDING_ERROR;
   int err = OMNI_NOALLOC_OK;
   int* base = scratch_for_current_device(&err);
   if (base == nullptr) return err;
@@ -82,9 +84,12 @@ extern "C" int omni_moe_permute_plan_noalloc(const int* idx, int T, int K, int E
     if (cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int), s) != cudaSuccess) return OMNI_NOALLOC_LAUNCH_FAILED;
     return OMNI_NOALLOC_OK;
   }
+  // no error was pending above, so an error read after a launch belongs to that launch
   omni::plan_count_kernel<<<nblocks, kThreads, 0, s>>>(idx, N, E, blk_cnt, nullptr);
+  if (cudaGetLastError() != cudaSuccess) return OMNI_NOALLOC_LAUNCH_FAILED;
   omni::plan_scan_kernel<<<1, 256, 0, s>>>(nblocks, E, capacity, blk_cnt, blk_base, counts, offsets, src, cap_rows,
                                            128);
+  if (cudaGetLastError() != cudaSuccess) return OMNI_NOALLOC_LAUNCH_FAILED;
   omni::plan_assign_kernel<<<nblocks, kThreads, 0, s>>>(idx, N, E, capacity, blk_base, offsets, pos, src, cap_rows,
                                                         nullptr);
   if (cudaGetLastError() != cudaSuccess) return OMNI_NOALLOC_LAUNCH_FAILED;

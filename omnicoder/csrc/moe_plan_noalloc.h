@@ -45,7 +45,9 @@ enum {
   OMNI_NOALLOC_TOO_LARGE = 1,    // problem needs more scratch than the static array holds
   OMNI_NOALLOC_BAD_ARGUMENT = 2, // null pointer or size outside the supported range
   OMNI_NOALLOC_SETUP_FAILED = 3, // cudaGetSymbolAddress failed on this device
-  OMNI_NOALLOC_LAUNCH_FAILED = 4 // a kernel launch reported an error
+  OMNI_NOALLOC_LAUNCH_FAILED = 4, // a kernel launch of this call reported an error
+  OMNI_NOALLOC_PENDING_ERROR = 5  // an earlier CUDA error was pending on this thread; nothing was
+                                  // launched and the error is left for its owner to read
 };
 
 // Enqueue the permutation plan on `stream` (a cudaStream_t, may be null for the

@@ -68,18 +68,32 @@ def sample_next_token(logits: torch.Tensor, temperature: float = 0.0, top_k: int
 
 class LogitProcessor:
     """Penalties and biases applied to the logits before sampling (reference
-    src/omnicoder/inference/generate.py:500-690): CTRL-style repetition penalty (the logit of
-    a token already in the sequence is divided by `repetition_penalty` when positive and
-    multiplied by it when negative), presence / frequency penalties (minus `presence` once a
-    token occurred, minus `frequency` x its count) and an additive per-token bias.  Token
-    counts live on the device ([B, V], updated with scatter_add), so no step reads the host."""
+    src/omnicoder/inference/generate.py:500-690 and :2148-2169): CTRL-style repetition penalty
+    (the logit of a token seen in the window is divided by `repetition_penalty` when positive
+    and multiplied by it when negative), presence / frequency penalties (minus `presence` once
+    a token occurred, minus `frequency` x its count) and an additive per-token bias.
+
+    Only the last `window` tokens of each sequence count (default 128, the reference's
+    rep_window); `window=0` counts the whole sequence.  Token counts ([B, V]) and the ring of
+    the window's token ids ([B, window]) live on the device, so no step reads the host."""
 
     def __init__(self, batch: int, vocab: int, device, repetition_penalty: float = 1.0, presence_penalty: float = 0.0,
-                 frequency_penalty: float = 0.0, logit_bias: dict | None = None):
+                 frequency_penalty: float = 0.0, logit_bias: dict | None = None, window: int = 128):
+        if repetition_penalty <= 0:
+            raise ValueError(f"repetition_penalty must be > 0 (got {repetition_penalty})")
+        if window < 0:
+            raise ValueError(f"penalty window must be >= 0 (got {window})")
         self.rep, self.pres, self.freq = repetition_penalty, presence_penalty, frequency_penalty
+        self.vocab = vocab
+        self.window = int(window)
         self.counts = torch.zeros(batch, vocab, device=device)
+        self.ring = torch.full((batch, self.window), -1, dtype=torch.long, device=device) if self.window else None
+        self.head = 0                      # next ring column to overwrite
         self.bias = None
         if logit_bias:
+            bad = [t for t in logit_bias if not 0 <= int(t) < vocab]
+            if bad:
+                raise ValueError(f"logit_bias token ids outside [0, {vocab}): {sorted(bad)[:8]}")
             self.bias = torch.zeros(vocab, device=device)
             for t, b in logit_bias.items():
                 self.bias[int(t)] = float(b)
@@ -89,8 +103,27 @@ class LogitProcessor:
         return self.rep != 1.0 or self.pres != 0.0 or self.freq != 0.0 or self.bias is not None
 
     def observe(self, ids: torch.Tensor) -> None:
-        ids = ids.reshape(self.counts.shape[0], -1)
-        self.counts.scatter_add_(1, ids, torch.ones_like(ids, dtype=self.counts.dtype))
+        """Append the token ids [B, n] (or [B]) of every sequence to the window."""
+        ids = ids.reshape(self.counts.shape[0], -1).long()
+        one = torch.ones_like(ids[:, :1], dtype=self.counts.dtype)
+        if not self.window:
+            self.counts.scatter_add_(1, ids, one.expand_as(ids))
+            return
+        if ids.shape[1] >= self.window:    # the window holds only the newest tokens: rebuild it
+            tail = ids[:, -self.window:]
+            self.counts.zero_()
+            self.counts.scatter_add_(1, tail, one.expand_as(tail))
+            self.ring.copy_(tail)
+            self.head = 0
+            return
+        for j in range(ids.shape[1]):
+            old = self.ring[:, self.head:self.head + 1]
+            # tokens leaving the window (ring slots still -1 subtract nothing)
+            self.counts.scatter_add_(1, old.clamp_min(0), -(old >= 0).to(self.counts.dtype))
+            new = ids[:, j:j + 1]
+            self.counts.scatter_add_(1, new, one)
+            self.ring[:, self.head:self.head + 1] = new
+            self.head = (self.head + 1) % self.window
 
     def __call__(self, logits: torch.Tensor) -> torch.Tensor:
         if not self.active:
@@ -171,12 +204,14 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
              window_size: int = 0, return_stats: bool = False, eos_id: int | None = None, seed: int | None = None,
              max_len: int | None = None, cuda_graph: bool = True, repetition_penalty: float = 1.0,
              presence_penalty: float = 0.0, frequency_penalty: float = 0.0, logit_bias: dict | None = None,
-             **_unused):
+             penalty_window: int = 128):
     """Generate `max_new_tokens` tokens after `input_ids` [B, S] (or [S]).  Returns
     [B, S + max_new_tokens] (and GenStats with return_stats).  On CUDA the
     decode step is captured once as a CUDA graph (`cuda_graph=False` runs it
-    eagerly).  Repetition / presence / frequency penalties and `logit_bias` (LogitProcessor)
-    apply on the plain decode path; speculative decoding samples without them."""
+    eagerly).  Repetition / presence / frequency penalties over the last `penalty_window`
+    tokens (0: the whole sequence) and `logit_bias` (LogitProcessor) apply on the plain decode
+    path; speculative decoding refuses them (its acceptance test needs the unmodified target
+    distribution)."""
     model.eval()
     squeeze = input_ids.dim() == 1
     ids = input_ids[None] if squeeze else input_ids
@@ -193,6 +228,9 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         gen.manual_seed(seed)
     stats = GenStats(prompt_tokens=B * S)
     if draft_model is not None and speculative_draft_len > 0:
+        if repetition_penalty != 1.0 or presence_penalty or frequency_penalty or logit_bias:
+            raise ValueError("speculative decoding samples from the unmodified target distribution: "
+                             "penalties and logit_bias are not applied there")
         out = _speculative(model, draft_model, ids, max_new_tokens, speculative_draft_len, temperature, top_k, top_p,
                            kv_dtype, L, gen, stats, eos_id)
     else:
@@ -200,7 +238,7 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         t0 = time.perf_counter()
         logits = _prefill(model, ids, cache)
         proc = LogitProcessor(B, logits.shape[-1], dev, repetition_penalty, presence_penalty, frequency_penalty,
-                              logit_bias)
+                              logit_bias, window=penalty_window)
         if proc.active:
             proc.observe(ids)
         tok = sample_next_token(proc(logits), temperature, top_k, top_p, gen)

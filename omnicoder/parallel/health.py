@@ -179,14 +179,33 @@ class FaultSpec:
         return spec
 
 
+# kinds that end or freeze a rank's process without unwinding it; on GPU ranks of a
+# multi-rank job they can leave peers waiting on device barriers or leave memory bound
+# to an NVLink multicast object, so they are only armed on CPU (gloo) ranks
+HOST_ONLY_KINDS = ("exit", "hang", "stall")
+
+
 class FaultInjector:
     def __init__(self, specs=None):
         self.specs = list(specs or [])
 
     @classmethod
-    def from_env(cls, var: str = "OMNICODER_FAULT") -> "FaultInjector":
+    def from_env(cls, var: str = "OMNICODER_FAULT", device_type: str = "cpu", world: int = 1) -> "FaultInjector":
+        """Fault specs from `var` ("rank=1,step=3,kind=raise;..."). On a CUDA job with more
+        than one rank only the unwinding kinds (raise, drop) are accepted: an exiting,
+        hanging or stalled GPU rank may be holding peer-mapped (symmetric / multicast)
+        memory or be awaited by peers' device barriers."""
         text = os.environ.get(var, "")
-        return cls([FaultSpec.parse(t) for t in text.split(";") if t.strip()])
+        inj = cls([FaultSpec.parse(t) for t in text.split(";") if t.strip()])
+        inj.check_allowed(device_type, world)
+        return inj
+
+    def check_allowed(self, device_type: str, world: int):
+        if device_type == "cuda" and world > 1:
+            bad = [s.kind for s in self.specs if s.kind in HOST_ONLY_KINDS]
+            if bad:
+                raise ValueError(f"fault kinds {sorted(set(bad))} are only injected on CPU (gloo) ranks; "
+                                 "on multi-rank CUDA jobs use kind=raise or kind=drop")
 
     def _match(self, rank: int, step: int, kinds) -> FaultSpec | None:
         for s in self.specs:

@@ -35,11 +35,14 @@ def _request_model():
     """The request body model, built on first use (pydantic is only needed for serving)."""
     global _REQ
     if _REQ is None:
-        from pydantic import create_model
-        _REQ = (create_model("TextReq", prompt=(str, ...), max_new_tokens=(int, 64), temperature=(float, 0.0),
-                             top_k=(int, 0), top_p=(float, 1.0), seed=(int | None, None), modality=(str, "text"),
-                             repetition_penalty=(float, 1.0), presence_penalty=(float, 0.0),
-                             frequency_penalty=(float, 0.0)),
+        from pydantic import Field, create_model
+        # out-of-range sampling settings are refused with 422 before they reach the sampler
+        # (a repetition penalty <= 0 would divide logits by zero or flip their order)
+        _REQ = (create_model("TextReq", prompt=(str, ...), max_new_tokens=(int, Field(64, ge=1)),
+                             temperature=(float, 0.0), top_k=(int, Field(0, ge=0)),
+                             top_p=(float, Field(1.0, gt=0.0, le=1.0)), seed=(int | None, None),
+                             modality=(str, "text"), repetition_penalty=(float, Field(1.0, gt=0.0)),
+                             presence_penalty=(float, 0.0), frequency_penalty=(float, 0.0)),
                 create_model("MediaReq", prompt=(str, ...), grid_h=(int, 8), grid_w=(int, 8), frames=(int, 4),
                              temperature=(float, 1.0), top_k=(int, 0), seed=(int | None, None)))
     return _REQ

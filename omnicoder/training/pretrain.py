@@ -152,7 +152,7 @@ def main(argv=None):
         ev0.record()
     from ..parallel.health import FaultInjector, Heartbeat
     hb = Heartbeat(timeout=a.heartbeat_timeout).start() if (world > 1 and a.heartbeat_timeout > 0) else None
-    inj = FaultInjector.from_env()
+    inj = FaultInjector.from_env(device_type=dev.type, world=world)
     try:
         _train_loop(a, trainer, model, it, dev, world, rank, start, state_path, log, ev0, ev1, hb, inj)
     except Exception as e:

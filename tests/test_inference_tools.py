@@ -160,6 +160,42 @@ def test_logit_processor_penalties_and_bias():
     assert (forced[0, 3:] == 42).all()
 
 
+def test_logit_processor_window_and_validation():
+    """Only the last `window` tokens are penalised (the reference's rep_window); ids outside
+    the vocabulary and a non-positive repetition penalty are refused."""
+    from omnicoder.inference.generate import LogitProcessor
+    p = LogitProcessor(2, 8, "cpu", frequency_penalty=1.0, window=3)
+    p.observe(torch.tensor([[1, 2, 3, 4, 4], [5, 5, 5, 6, 7]]))      # longer than the window
+    want = torch.zeros(2, 8)
+    want[0, 3], want[0, 4] = 1, 2
+    want[1, 5], want[1, 6], want[1, 7] = 1, 1, 1
+    torch.testing.assert_close(p.counts, want)
+    p.observe(torch.tensor([1, 7]))                                   # one step: the oldest leaves
+    want[0, 3], want[0, 1] = 0, 1
+    want[1, 5], want[1, 7] = 0, 2
+    torch.testing.assert_close(p.counts, want)
+    q = LogitProcessor(1, 8, "cpu", frequency_penalty=1.0, window=4)
+    for t in [1, 2, 1, 3, 1, 4, 5, 6]:
+        q.observe(torch.tensor([t]))
+    assert q.counts[0].tolist() == [0, 1, 0, 0, 1, 1, 1, 0]            # the last four: 1, 4, 5, 6
+    full = LogitProcessor(1, 8, "cpu", frequency_penalty=1.0, window=0)
+    full.observe(torch.tensor([[1, 1, 1, 2]]))
+    assert full.counts[0, 1] == 3
+    with pytest.raises(ValueError):
+        LogitProcessor(1, 8, "cpu", logit_bias={-1: 1.0})
+    with pytest.raises(ValueError):
+        LogitProcessor(1, 8, "cpu", logit_bias={8: 1.0})
+    with pytest.raises(ValueError):
+        LogitProcessor(1, 8, "cpu", repetition_penalty=0.0)
+
+
+def test_generate_rejects_unknown_options():
+    from omnicoder.inference.generate import generate
+    cfg, m = _tiny()
+    with pytest.raises(TypeError):
+        generate(m, torch.tensor([[3, 4, 5]]), 2, temperature=0.0, no_such_option=True)
+
+
 def test_load_logit_bias(tmp_path):
     from omnicoder.inference.generate import load_logit_bias
     f = tmp_path / "bias.json"

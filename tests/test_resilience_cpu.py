@@ -179,6 +179,19 @@ def test_fault_spec_parsing(monkeypatch):
     assert inj.drop(0, 1) and not inj.drop(0, 2) and len(inj.specs) == 2
 
 
+def test_fault_injector_refuses_process_ending_kinds_on_gpu_jobs(monkeypatch):
+    """exit / hang / stall are armed only on CPU ranks; a multi-rank CUDA job accepts raise / drop."""
+    from omnicoder.parallel.health import FaultInjector
+    for kind in ("exit", "hang", "stall"):
+        monkeypatch.setenv("OMNICODER_FAULT_TEST", f"rank=1,step=2,kind={kind}")
+        with pytest.raises(ValueError):
+            FaultInjector.from_env("OMNICODER_FAULT_TEST", device_type="cuda", world=2)
+        assert len(FaultInjector.from_env("OMNICODER_FAULT_TEST", device_type="cpu", world=2).specs) == 1
+        assert len(FaultInjector.from_env("OMNICODER_FAULT_TEST", device_type="cuda", world=1).specs) == 1
+    monkeypatch.setenv("OMNICODER_FAULT_TEST", "rank=1,step=2,kind=raise;rank=0,step=1,kind=drop")
+    assert len(FaultInjector.from_env("OMNICODER_FAULT_TEST", device_type="cuda", world=8).specs) == 2
+
+
 def test_resume_from_last_good_checkpoint(tmp_path):
     """An injected failure at step 5 (checkpoints every 2 steps) and a corrupted newest
     checkpoint: the relaunch resumes from step 2 and ends equal to an uninterrupted run,

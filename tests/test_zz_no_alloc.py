@@ -31,6 +31,8 @@ def _entry():
 
 def _route(T, K, E, seed):
     g = torch.Generator(device="cpu").manual_seed(seed)
+    if T == 0:
+        return torch.empty(0, K, dtype=torch.int32, device="cuda")
     # distinct experts per token, like a top-k router
     idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).to(torch.int32)
     return idx.cuda().contiguous()
@@ -41,21 +43,23 @@ def test_noalloc_plan_matches_allocating_binding(cuda_ext):
 
     f = _entry()
     stream = torch.cuda.current_stream().cuda_stream
-    for call, (T, K, E, cap) in enumerate([(3000, 4, 32, 0), (2500, 6, 64, 300)]):
+    # multi-block problems, then a one-block problem (T*K <= 1024, where the allocating
+    # binding switches to its single-CTA kernel) with a capacity, then no tokens at all
+    for call, (T, K, E, cap) in enumerate([(3000, 4, 32, 0), (2500, 6, 64, 300), (100, 4, 16, 20), (0, 4, 16, 0)]):
         idx = _route(T, K, E, seed=100 + call)
         rows = cap_rows_for(T, K, E, cap)
         ref_counts, ref_offsets, ref_pos, ref_src = cuda_ext.moe_plan(idx, E, cap, rows)
         counts = torch.full((E,), -7, dtype=torch.int32, device="cuda")
         offsets = torch.full((E + 1,), -7, dtype=torch.int32, device="cuda")
-        pos = torch.full((T, K), -7, dtype=torch.int32, device="cuda")
-        src = torch.full((rows,), -7, dtype=torch.int32, device="cuda")
-        rc = f(idx.data_ptr(), T, K, E, cap, counts.data_ptr(), offsets.data_ptr(), pos.data_ptr(), src.data_ptr(),
-               rows, stream)
+        pos = torch.full((max(T, 1), K), -7, dtype=torch.int32, device="cuda")
+        src = torch.full((max(rows, 1),), -7, dtype=torch.int32, device="cuda")
+        rc = f(idx.data_ptr() if T else pos.data_ptr(), T, K, E, cap, counts.data_ptr(), offsets.data_ptr(),
+               pos.data_ptr(), src.data_ptr(), rows, stream)
         assert rc == OK, f"call {call}: return code {rc}"
         torch.cuda.synchronize()
         assert torch.equal(counts, ref_counts), call
         assert torch.equal(offsets, ref_offsets), call
-        assert torch.equal(pos, ref_pos), call
+        assert torch.equal(pos[:T], ref_pos.view(T, K)), call
         used = int(ref_offsets[-1])
         assert torch.equal(src[:used], ref_src[:used]), call
 
