@@ -8,7 +8,7 @@ weights and AdamW state, random N(0, 0.02) weights, uniform random token ids.
 Layout on N GPUs: expert parallel over N ranks x data parallel over the same
 N ranks, ZeRO-1 sharded optimiser state for the replicated parameters.
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference|baseline]
 
 N > 1 is launched with torch.distributed.run (one rank per GPU, NCCL).  Rank 0
 prints one JSON line.  `value` is the whole-job token throughput measured on
@@ -17,6 +17,14 @@ public Trainer API including the pinned host->device copy of each step's
 token ids/labels and the device->host read of the loss.  On one GPU the
 forward + backward of the step is captured once as a CUDA graph and replayed
 (`--cuda-graph off` runs it eagerly); the optimiser step runs after the replay.
+
+Comparison arm: after this package's step, the same process times the plain
+PyTorch + NCCL + cuBLAS build of the same step (omnicoder.baselines.torch_nccl:
+cuBLAS linears, PyTorch SDPA, torch._grouped_mm experts, all_to_all_single
+expert exchange, ZeRO-1 with reduce_scatter_tensor / all_gather_into_tensor and
+fused torch AdamW) on the same data; `vs_baseline` is value / its value and the
+`baseline` object carries its device-timed and end-to-end numbers
+(`--baseline off` skips it; `--impl baseline` runs only that arm).
 """
 from __future__ import annotations
 
@@ -42,7 +50,10 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "baseline"],
+                    help="ours; reference (the unmodified reference package); baseline (plain PyTorch + NCCL)")
+    ap.add_argument("--baseline", default="on", choices=["on", "off"],
+                    help="with --impl ours, also time the plain PyTorch + NCCL build in the same process")
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--micro-batch", type=int, default=2)
     ap.add_argument("--preset", default="moe_mla_24l")
@@ -189,6 +200,115 @@ def decode_phase(args, dev, world, rank, barrier):
 
 
 # ----------------------------------------------------------------------------
+def _barrier_fn(world):
+    import torch.distributed as dist
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+    return barrier
+
+
+def _max_over_ranks(x: float, dev, world) -> float:
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_train_arm(step, args, dev, world, rank, local, B, S, V, with_clocks: bool):
+    """Device-timed training steps and the end-to-end run of one arm.  `step(ids, labels)`
+    returns the step's loss as a device tensor.  Returns (ms per step, loss, e2e dict, clocks)."""
+    import torch
+
+    from omnicoder.training.engine import synthetic_batch
+    barrier = _barrier_fn(world)
+    n_steps = args.warmup + args.steps
+    dev_batches = [synthetic_batch(B, S, V, seed=rank, step=i, device=dev) for i in range(n_steps)]
+    for i in range(args.warmup):
+        step(*dev_batches[i])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(with_clocks and local == 0)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    last = None
+    for i in range(args.steps):
+        last = step(*dev_batches[args.warmup + i])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = _max_over_ranks(t0.elapsed_time(t1) / args.steps, dev, world)
+    loss = float(last.item())
+    del dev_batches
+    e2e = None
+    if not args.no_e2e:
+        # end to end: each step's ids / labels copied from pinned host memory, the loss read back
+        host = [synthetic_batch(B, S, V, seed=rank + 7, step=i, pin=True) for i in range(args.steps + 1)]
+        step(host[0][0].to(dev, non_blocking=True), host[0][1].to(dev, non_blocking=True))
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(1, args.steps + 1):
+            ids = host[i][0].to(dev, non_blocking=True)
+            lab = host[i][1].to(dev, non_blocking=True)
+            _ = step(ids, lab).item()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ems = _max_over_ranks(e0.elapsed_time(e1) / args.steps, dev, world)
+        bi = host[1][0].numel() * host[1][0].element_size() + host[1][1].numel() * host[1][1].element_size()
+        e2e = {"value": B * S * world / (ems / 1000.0), "unit": "tokens/s", "ms_per_step": ems,
+               "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4, "note": "per rank bytes; loss read back each step"}
+    return ms, loss, e2e, clk
+
+
+def baseline_arm(args, cfg, dev, world, rank, local, group):
+    """The plain PyTorch + NCCL + cuBLAS build (omnicoder.baselines.torch_nccl) of the same step."""
+    import torch
+
+    from omnicoder.baselines.torch_nccl import TorchMoELM, TorchTrainer
+    tcfg = _tcfg(args)
+    model = TorchMoELM(cfg, dev, torch.bfloat16, group=group if world > 1 else None, seed=1234)
+    tr = TorchTrainer(model, tcfg, group if world > 1 else None)
+    B, S, V = args.micro_batch, args.seq, cfg.vocab_size
+    ms, loss, e2e, clk = time_train_arm(lambda i, l: tr.step(i, l), args, dev, world, rank, local, B, S, V, True)
+    out = {"impl": "torch_nccl_baseline", "value": B * S * world / (ms / 1000.0), "unit": "tokens/s",
+           "ms_per_step": ms, "loss": loss, "e2e": e2e, "clocks": clk,
+           "what": "plain PyTorch: bf16 F.linear (cuBLAS), F.scaled_dot_product_attention, torch._grouped_mm "
+                   "experts, all_to_all_single expert exchange, ZeRO-1 reduce_scatter_tensor / "
+                   "all_gather_into_tensor with fused torch AdamW on fp32 master shards"}
+    del tr, model
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
+    return out
+
+
+def _tcfg(args):
+    from omnicoder.config import TrainConfig
+    return TrainConfig(lr=3e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch, seq_len=args.seq,
+                       grad_clip=1.0, weight_decay=0.1, betas=(0.9, 0.95))
+
+
+def _config_json(args, world, B, S, extra=None):
+    c = {"model": MODEL_DESC, "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": S,
+         "parallelism": f"ep{world}xdp{world}" + (" zero1" if world > 1 else ""),
+         "optimizer": "AdamW fp32 master, grad clip 1.0",
+         "l2": "working set (14.6 GB bf16 weights, 8192 tokens/GPU of activations) >> 126 MB L2"}
+    c.update(extra or {})
+    return c
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -197,7 +317,7 @@ def main():
     import torch
     import torch.distributed as dist
 
-    from omnicoder.config import TrainConfig, get_preset
+    from omnicoder.config import get_preset
     from omnicoder.models.lm import build_model
     from omnicoder.ops import _ext
     from omnicoder.training.engine import Trainer, synthetic_batch
@@ -210,88 +330,45 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     cfg = get_preset(args.preset)
-    parallel = None
+    B, S, V = args.micro_batch, args.seq, cfg.vocab_size
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    group = dist.group.WORLD if world > 1 else None
+
+    if args.impl == "baseline":
+        base = baseline_arm(args, cfg, dev, world, rank, local, group)
+        if rank == 0:
+            out = {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": world,
+                   "steps": args.steps, "warmup": args.warmup, "ms_per_step": base["ms_per_step"],
+                   "higher_is_better": True, "scaling": "weak", "vs_baseline": 1.0, "dtype": "bf16",
+                   "data": "synthetic (uniform random token ids, random-init N(0,0.02))",
+                   "config": _config_json(args, world, B, S), "loss": base["loss"], "e2e": base["e2e"],
+                   "clocks": base["clocks"], "gpu_launches": 0, "impl": base["impl"], "what": base["what"]}
+            print(json.dumps(out), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    parallel = None
+    if world > 1:
         from omnicoder.parallel.expert_data import ExpertDataParallel
         # exchange arena: x, y, dy, dx receive slabs (+ routing metadata) of every MoE layer of a step
         rows = int(args.micro_batch * args.seq * cfg.moe.top_k * 1.3) + cfg.moe.n_experts * 128
         arena = cfg.n_layers * rows * (4 * cfg.d_model * 2 + 16)
         parallel = ExpertDataParallel(dist.group.WORLD, transport=args.ep_transport, arena_bytes=arena,
                                       zero_transport=args.zero_transport)
-
-    tcfg = TrainConfig(lr=3e-4, warmup_steps=10, max_steps=1000, micro_batch=args.micro_batch, seq_len=args.seq,
-                       grad_clip=1.0, weight_decay=0.1, betas=(0.9, 0.95))
     model = build_model(cfg, device=dev, seed=1234, ep=parallel) if parallel is not None else \
         build_model(cfg, device=dev, seed=1234)
-    trainer = Trainer(model, tcfg, parallel, cuda_graph=(args.cuda_graph == "on" and world == 1))
+    trainer = Trainer(model, _tcfg(args), parallel, cuda_graph=(args.cuda_graph == "on" and world == 1))
     _ext.load()
 
-    B, S, V = args.micro_batch, args.seq, cfg.vocab_size
-    n_steps = args.warmup + args.steps
-    dev_batches = [synthetic_batch(B, S, V, seed=rank, step=i, device=dev) for i in range(n_steps)]
+    def step(ids, lab):
+        return trainer.step(ids, lab, assume_all_valid=True).loss
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    # ---- device-timed region --------------------------------------------------
-    for i in range(args.warmup):
-        trainer.step(*dev_batches[i], assume_all_valid=True)
-    torch.cuda.synchronize()
+    ms, loss_val, e2e, clk = time_train_arm(step, args, dev, world, rank, local, B, S, V, True)
     _ext.check_status()
-    clocks = ClockSampler(local == 0)
-    barrier()
-    torch.cuda.synchronize()
-    clocks.start()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record()
-    last = None
-    for i in range(args.steps):
-        last = trainer.step(*dev_batches[args.warmup + i], assume_all_valid=True)
-    t_end.record()
-    torch.cuda.synchronize()
-    barrier()
-    clk = clocks.stop()
-    ms = t_start.elapsed_time(t_end) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    _ext.check_status()
-    loss_val = float(last.loss.item())
-    tokens_step = B * S * world
-    value = tokens_step / (ms / 1000.0)
-    del dev_batches
-
-    # ---- end-to-end through the public API --------------------------------------
-    e2e = None
-    if not args.no_e2e:
-        host = [synthetic_batch(B, S, V, seed=rank + 7, step=i, pin=True) for i in range(args.steps + 1)]
-        trainer.step(host[0][0].to(dev, non_blocking=True), host[0][1].to(dev, non_blocking=True),
-                     assume_all_valid=True)
-        torch.cuda.synchronize()
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(1, args.steps + 1):
-            ids = host[i][0].to(dev, non_blocking=True)
-            lab = host[i][1].to(dev, non_blocking=True)
-            st = trainer.step(ids, lab, assume_all_valid=True)
-            _ = st.loss.item()
-        e1.record()
-        torch.cuda.synchronize()
-        barrier()
-        ems = e0.elapsed_time(e1) / args.steps
-        if world > 1:
-            t = torch.tensor([ems], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ems = float(t.item())
-        bi = host[1][0].numel() * host[1][0].element_size() + host[1][1].numel() * host[1][1].element_size()
-        e2e = {"value": tokens_step / (ems / 1000.0), "unit": "tokens/s", "ms_per_step": ems,
-               "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4, "note": "per rank bytes; loss read back each step"}
+    value = B * S * world / (ms / 1000.0)
 
     # ---- launch count of this repo's kernels (one extra, untimed, profiled step) ----
     launches = None
@@ -324,29 +401,36 @@ def main():
     mfu_info["of_nominal_dense_bf16_2250"] = mfu_info["model_tflops_per_gpu"] / 2250.0
     graph_state = ("forward+backward replayed" if trainer._graph is not None else
                    (f"off ({trainer.graph_error})" if trainer.graph_error else "off"))
+    ep_stats = dict(parallel.ep.stats) if parallel is not None else None
+    del trainer, model, step
+    import gc
+    gc.collect()
+    torch.cuda.empty_cache()
+
+    base = None
+    if args.baseline == "on":
+        base = baseline_arm(args, cfg, dev, world, rank, local, group)
+        base["ratio"] = value / base["value"]
+        if e2e is not None and base["e2e"] is not None:
+            base["e2e_ratio"] = e2e["value"] / base["e2e"]["value"]
+
     decode = None
     if not args.no_decode:
-        del trainer, model, last
-        import gc
-        gc.collect()
-        torch.cuda.empty_cache()
-        decode = decode_phase(args, dev, world, rank, barrier)
+        decode = decode_phase(args, dev, world, rank, _barrier_fn(world))
 
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init N(0,0.02))",
-            "config": {"model": MODEL_DESC, "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": S,
-                       "parallelism": f"ep{world}xdp{world}" + (" zero1" if world > 1 else ""),
-                       "ep_transport": args.ep_transport if world > 1 else None,
-                       "zero_transport": args.zero_transport if world > 1 else None,
-                       "optimizer": "AdamW fp32 master, grad clip 1.0",
-                       "cuda_graph": graph_state,
-                       "l2": "working set (14.6 GB bf16 weights, 8192 tokens/GPU of activations) >> 126 MB L2"},
+            "vs_baseline": base["ratio"] if base else None, "dtype": "bf16",
+            "data": "synthetic (uniform random token ids, random-init N(0,0.02))",
+            "config": _config_json(args, world, B, S, {
+                "ep_transport": args.ep_transport if world > 1 else None,
+                "zero_transport": args.zero_transport if world > 1 else None, "cuda_graph": graph_state}),
             "loss": loss_val, "e2e": e2e, "mfu": mfu_info,
             "gpu_launches": (launches["ours_per_step"] * args.steps) if launches else None,
-            "launches_per_step": launches, "clocks": clk, "impl": "ours", "decode": decode,
+            "launches_per_step": launches, "clocks": clk, "impl": "ours", "ep_stats": ep_stats,
+            "baseline": base, "decode": decode,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
