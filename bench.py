@@ -14,9 +14,12 @@ N > 1 is launched with torch.distributed.run (one rank per GPU, NCCL).  Rank 0
 prints one JSON line.  `value` is the whole-job token throughput measured on
 the device with CUDA events (max over ranks), `e2e` the same metric through the
 public Trainer API including the pinned host->device copy of each step's
-token ids/labels and the device->host read of the loss.  On one GPU the
-forward + backward of the step is captured once as a CUDA graph and replayed
-(`--cuda-graph off` runs it eagerly); the optimiser step runs after the replay.
+token ids/labels and the device->host read of the loss.  The forward +
+backward of the step is captured once as a CUDA graph and replayed
+(`--cuda-graph off` runs it eagerly); the optimiser step (with the ZeRO-1
+gradient reduce-scatter on several GPUs) runs after the replay.  On several
+GPUs the expert exchange computes its layout on the device (routing counts are
+exchanged through peer memory), so nothing in the step waits for the host.
 
 Comparison arm: after this package's step, the same process times the plain
 PyTorch + NCCL + cuBLAS build of the same step (omnicoder.baselines.torch_nccl:
@@ -65,7 +68,10 @@ def parse_args():
                     help="data-parallel ZeRO-1: NCCL collectives, or the fused peer-memory optimiser kernels")
     ap.add_argument("--no-decode", action="store_true", help="skip the batch-64 long-context decode measurement")
     ap.add_argument("--cuda-graph", default="on", choices=["on", "off"],
-                    help="1 GPU: replay forward + backward of the training step as a CUDA graph")
+                    help="replay forward + backward of the training step as a CUDA graph")
+    ap.add_argument("--ep-buffer-factor", type=float, default=2.0,
+                    help="expert-parallel receive slabs hold this many times the balanced per-expert load "
+                         "(pairs beyond it are dropped and counted in ep_stats)")
     ap.add_argument("--decode-gen", type=int, default=512)
     return ap.parse_args()
 
@@ -353,14 +359,14 @@ def main():
     parallel = None
     if world > 1:
         from omnicoder.parallel.expert_data import ExpertDataParallel
-        # exchange arena: x, y, dy, dx receive slabs (+ routing metadata) of every MoE layer of a step
-        rows = int(args.micro_batch * args.seq * cfg.moe.top_k * 1.3) + cfg.moe.n_experts * 128
-        arena = cfg.n_layers * rows * (4 * cfg.d_model * 2 + 16)
+        # exchange arena: every MoE layer's fixed receive / output slabs (+ routing metadata),
+        # the backward slabs shared by the layers and the count board, in one peer-mapped chunk
+        arena = ExpertDataParallel.arena_bytes_for(cfg, B * S, world, args.ep_buffer_factor)
         parallel = ExpertDataParallel(dist.group.WORLD, transport=args.ep_transport, arena_bytes=arena,
-                                      zero_transport=args.zero_transport)
+                                      zero_transport=args.zero_transport, buffer_factor=args.ep_buffer_factor)
     model = build_model(cfg, device=dev, seed=1234, ep=parallel) if parallel is not None else \
         build_model(cfg, device=dev, seed=1234)
-    trainer = Trainer(model, _tcfg(args), parallel, cuda_graph=(args.cuda_graph == "on" and world == 1))
+    trainer = Trainer(model, _tcfg(args), parallel, cuda_graph=(args.cuda_graph == "on"))
     _ext.load()
 
     def step(ids, lab):
@@ -401,7 +407,11 @@ def main():
     mfu_info["of_nominal_dense_bf16_2250"] = mfu_info["model_tflops_per_gpu"] / 2250.0
     graph_state = ("forward+backward replayed" if trainer._graph is not None else
                    (f"off ({trainer.graph_error})" if trainer.graph_error else "off"))
-    ep_stats = dict(parallel.ep.stats) if parallel is not None else None
+    ep_stats = None
+    if parallel is not None:
+        ep_stats = dict(parallel.ep.stats, layout=parallel.ep.layout,
+                        dropped_pairs_this_rank=parallel.ep.dropped_pairs(),
+                        buffer_factor=parallel.ep.buffer_factor)
     del trainer, model, step
     import gc
     gc.collect()

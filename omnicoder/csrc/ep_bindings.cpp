@@ -95,6 +95,36 @@ void ep_barrier_t(const std::vector<int64_t>& sig_ptrs, int64_t me, int64_t epoc
   ep_barrier(make_peers(sig_ptrs, {}), (int)me, (int)sig_ptrs.size(), (unsigned)(epoch & 0xffffffffll), stream());
 }
 
+void ep_barrier_dev_t(const std::vector<int64_t>& sig_ptrs, int64_t me, at::Tensor& epoch_ctr) {
+  check(epoch_ctr, at::kInt, "epoch_ctr");
+  const c10::cuda::CUDAGuard g(epoch_ctr.device());
+  ep_barrier_dev(make_peers(sig_ptrs, {}), (int)me, (int)sig_ptrs.size(),
+                 reinterpret_cast<unsigned*>(epoch_ctr.data_ptr<int>()), stream());
+}
+
+// -> (dst_base [E], keep_lim [E], offs_local [El + 1], kept_local [El]) written into the given tensors
+void ep_exchange_layout_t(const at::Tensor& counts, const std::vector<int64_t>& board_ptrs,
+                          const std::vector<int64_t>& sig_ptrs, int64_t me, at::Tensor& epoch_ctr, int64_t El,
+                          int64_t capacity, int64_t seg_cap, at::Tensor& dst_base, at::Tensor& keep_lim,
+                          at::Tensor& offs_local, at::Tensor& kept_local, at::Tensor& dropped) {
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&counts, &epoch_ctr, &dst_base, &keep_lim,
+                                                                       &offs_local, &kept_local, &dropped})
+    check(*t, at::kInt, "ep_exchange_layout");
+  const int64_t E = counts.numel();
+  const int64_t n = (int64_t)board_ptrs.size();
+  TORCH_CHECK(E >= 1 && E <= 1024 && El >= 1 && E % El == 0 && E / El == n, "ep_exchange_layout: E = El * ranks");
+  TORCH_CHECK(sig_ptrs.size() == board_ptrs.size(), "ep_exchange_layout: one signal area per rank");
+  TORCH_CHECK(dst_base.numel() == E && keep_lim.numel() == E && offs_local.numel() == El + 1 &&
+                  kept_local.numel() == El && dropped.numel() >= 1,
+              "ep_exchange_layout: output sizes");
+  TORCH_CHECK(seg_cap > 0 && seg_cap % 128 == 0, "ep_exchange_layout: seg_cap must be a positive multiple of 128");
+  const c10::cuda::CUDAGuard g(counts.device());
+  ep_exchange_layout(make_peers(board_ptrs, {}), make_peers(sig_ptrs, {}), (int)me, (int)n,
+                     reinterpret_cast<unsigned*>(epoch_ctr.data_ptr<int>()), counts.data_ptr<int>(), (int)E, (int)El,
+                     (int)capacity, (int)seg_cap, dst_base.data_ptr<int>(), keep_lim.data_ptr<int>(),
+                     offs_local.data_ptr<int>(), kept_local.data_ptr<int>(), dropped.data_ptr<int>(), stream());
+}
+
 void zero_rs_t(const std::vector<int64_t>& g_ptrs, int64_t lo, int64_t n, double scale, at::Tensor& out,
                const c10::optional<at::Tensor>& norm_sq) {
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() >= n,
@@ -126,6 +156,8 @@ void register_ep(pybind11::module_& m) {
   m.def("ep_owner_bwd", &ep_owner_bwd_t);
   m.def("ep_pad_rows", &ep_pad_rows_t);
   m.def("ep_barrier", &ep_barrier_t);
+  m.def("ep_barrier_dev", &ep_barrier_dev_t);
+  m.def("ep_exchange_layout", &ep_exchange_layout_t);
   m.def("zero_rs", &zero_rs_t, py::arg("g_ptrs"), py::arg("lo"), py::arg("n"), py::arg("scale"), py::arg("out"),
         py::arg("norm_sq") = py::none());
   m.def("zero_adamw_push", &zero_adamw_push_t, py::arg("p"), py::arg("m"), py::arg("v"), py::arg("g"),

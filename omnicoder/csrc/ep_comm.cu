@@ -237,6 +237,111 @@ __global__ void ep_barrier_kernel(EpPeers sig, int me, int n, unsigned epoch, St
   __threadfence_system();
 }
 
+// Signal every rank with the next epoch of the device counter and wait (bounded) until every
+// rank has signalled it.  Every rank runs the same sequence of these barriers, so the
+// counters advance in step; the epoch is read on the device, which lets a CUDA graph
+// replay the barrier.  Called by one block: threads [0, n) each serve one peer.
+__device__ __forceinline__ void dev_barrier(const EpPeers& sig, int me, int n, unsigned* epoch_ctr,
+                                            StatusBlock* st) {
+  __shared__ unsigned s_epoch;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_epoch = *reinterpret_cast<volatile unsigned*>(epoch_ctr) + 1u;
+    *reinterpret_cast<volatile unsigned*>(epoch_ctr) = s_epoch;
+  }
+  __syncthreads();
+  const unsigned epoch = s_epoch;
+  const int t = threadIdx.x;
+  if (t < n) {
+    __threadfence_system();
+    unsigned* peer_flag = reinterpret_cast<unsigned*>(sig.ptr[t]) + me;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peer_flag), "r"(epoch) : "memory");
+    const unsigned* mine = reinterpret_cast<const unsigned*>(sig.ptr[me]) + t;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (true) {
+      unsigned v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if ((int)(v - epoch) >= 0) break;
+      if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) {
+        report_error(st, STATUS_TIMEOUT_PEER_FLAG, t);
+        break;
+      }
+    }
+    __threadfence_system();
+  }
+  __syncthreads();
+}
+
+__global__ void ep_barrier_dev_kernel(EpPeers sig, int me, int n, unsigned* epoch_ctr, StatusBlock* st) {
+  dev_barrier(sig, me, n, epoch_ctr, st);
+}
+
+// Routing-count exchange and receive layout, computed on the device by every rank alike.
+// Each rank stores its per-expert pair counts into row `me` of every rank's count board
+// [N][E], passes a device barrier, then derives from the board (C[s][e] = pairs of source s
+// for expert e) the layout that the host used to compute from all-gathered counts:
+//   cap       = min(capacity or inf, seg_cap)          per-expert limit over the group
+//   kept[s,e] = clamp(min(C[s,e], cap - sum_{s'<s} C[s',e]), 0)
+//   seg[e]    = sum_s kept[s,e], padded to 128 rows; segments of one owner back to back
+//   dst_base[e] = base of e's segment + sum_{s<me} kept[s,e];  keep_lim[e] = kept[me,e]
+//   offs_local / kept_local: this rank's El segments
+//   *dropped += this rank's pairs lost to seg_cap (beyond what the capacity alone drops)
+// seg_cap (a multiple of 128) bounds every segment, so each owner's slab holds at most
+// El * seg_cap rows whatever the routing: the slabs are allocated once, and no count has to
+// reach the host.  One block of >= E threads.
+__global__ void ep_exchange_layout_kernel(EpPeers board, EpPeers sig, int me, int n, unsigned* epoch_ctr,
+                                          const int* __restrict__ counts, int E, int El, int capacity, int seg_cap,
+                                          int* __restrict__ dst_base, int* __restrict__ keep_lim,
+                                          int* __restrict__ offs_local, int* __restrict__ kept_local,
+                                          int* __restrict__ dropped, StatusBlock* st) {
+  extern __shared__ int sh[];
+  int* C = sh;                 // [n][E]
+  int* seg_pad = sh + n * E;   // [E]
+  const int e = threadIdx.x;
+  if (e < E) {
+    const int c = counts[e];
+    for (int t = 0; t < n; ++t) reinterpret_cast<volatile int*>(board.ptr[t])[me * E + e] = c;
+  }
+  dev_barrier(sig, me, n, epoch_ctr, st);
+  const volatile int* mine = reinterpret_cast<const volatile int*>(board.ptr[me]);
+  for (int i = threadIdx.x; i < n * E; i += blockDim.x) C[i] = mine[i];
+  __syncthreads();
+  int kept_me = 0, before_me = 0, seg = 0, lost_me = 0;
+  if (e < E) {
+    const int cap = capacity > 0 ? min(capacity, seg_cap) : seg_cap;
+    int before = 0;
+    for (int s = 0; s < n; ++s) {
+      const int c = C[s * E + e];
+      const int k = max(0, min(c, cap - before));
+      if (s < me) before_me += k;
+      if (s == me) {
+        kept_me = k;
+        // pairs lost to the slab bound only (not to the configured capacity)
+        const int k_cap = capacity > 0 ? max(0, min(c, capacity - before)) : c;
+        lost_me = k_cap - k;
+      }
+      seg += k;
+      before += c;
+    }
+    seg_pad[e] = (seg + 127) / 128 * 128;
+  }
+  __syncthreads();
+  if (e < E) {
+    const int owner = e / El;
+    int base = 0;
+    for (int j = owner * El; j < e; ++j) base += seg_pad[j];
+    dst_base[e] = base + before_me;
+    keep_lim[e] = kept_me;
+    if (owner == me) {
+      offs_local[e - me * El] = base;
+      kept_local[e - me * El] = seg;
+      if (e == me * El + El - 1) offs_local[El] = base + seg_pad[e];
+    }
+    if (lost_me > 0 && dropped != nullptr) atomicAdd(dropped, lost_me);
+  }
+}
+
 int grid_for(long long work_warps) {
   long long b = (work_warps + kWarps - 1) / kWarps;
   return (int)std::max(1ll, std::min(b, 148ll * 16));
@@ -284,6 +389,20 @@ void ep_owner_bwd(void* dy, const void* y, const void* meta, const int* offsets,
 void ep_pad_rows(void* x, void* meta, const int* offsets, const int* kept, int El, int rows, int D, cudaStream_t s) {
   if (El == 0) return;
   ep_pad_rows_kernel<<<El, kWarps * 32, 0, s>>>((bf16*)x, (int4*)meta, offsets, kept, El, rows, D);
+}
+
+void ep_barrier_dev(const EpPeers& sig, int me, int n, unsigned* epoch_ctr, cudaStream_t s) {
+  ep_barrier_dev_kernel<<<1, 32, 0, s>>>(sig, me, n, epoch_ctr, (StatusBlock*)status_ptr());
+}
+
+void ep_exchange_layout(const EpPeers& board, const EpPeers& sig, int me, int n, unsigned* epoch_ctr,
+                        const int* counts, int E, int El, int capacity, int seg_cap, int* dst_base, int* keep_lim,
+                        int* offs_local, int* kept_local, int* dropped, cudaStream_t s) {
+  const int threads = std::max(32, (E + 31) / 32 * 32);
+  const size_t smem = (size_t)(n * E + E) * sizeof(int);
+  ep_exchange_layout_kernel<<<1, threads, smem, s>>>(board, sig, me, n, epoch_ctr, counts, E, El, capacity, seg_cap,
+                                                     dst_base, keep_lim, offs_local, kept_local, dropped,
+                                                     (StatusBlock*)status_ptr());
 }
 
 void ep_barrier(const EpPeers& sig, int me, int n, unsigned epoch, cudaStream_t s) {

@@ -37,6 +37,16 @@ void ep_owner_bwd(void* dy, const void* y, const void* meta, const int* offsets,
 void ep_pad_rows(void* x, void* meta, const int* offsets, const int* kept, int El, int rows, int D, cudaStream_t s);
 // Signal every rank and wait until every rank has signalled `epoch` (bounded wait).
 void ep_barrier(const EpPeers& sig, int me, int n, unsigned epoch, cudaStream_t s);
+// Same, with the epoch taken from (and advanced in) the device counter *epoch_ctr, so that a
+// CUDA graph can replay it.
+void ep_barrier_dev(const EpPeers& sig, int me, int n, unsigned* epoch_ctr, cudaStream_t s);
+// Exchange per-expert routing counts [E] through the peer-mapped count boards ([N][E] int32
+// per rank) and compute the receive layout on the device (dst_base / keep_lim [E], this rank's
+// offs_local [El + 1] / kept_local [El]; pairs beyond min(capacity, seg_cap) per expert are
+// dropped and counted into *dropped).  E <= 1024.
+void ep_exchange_layout(const EpPeers& board, const EpPeers& sig, int me, int n, unsigned* epoch_ctr,
+                        const int* counts, int E, int El, int capacity, int seg_cap, int* dst_base, int* keep_lim,
+                        int* offs_local, int* kept_local, int* dropped, cudaStream_t s);
 
 // ZeRO-1 step over peer memory (zero_p2p.cu): reduce-scatter of rank-local bf16 gradient
 // buckets g.ptr[r] into this rank's fp32 shard out[0, n) = scale * sum_r g_r[lo + i] (+ its

@@ -29,6 +29,7 @@ src/omnicoder/tools/torchrun_ep.py:36-38, src/omnicoder/modeling/moe_layer.py).
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import numpy as np
@@ -87,7 +88,19 @@ def local_ranks(idx: torch.Tensor, E: int) -> torch.Tensor:
 class EPContext:
     """Expert-parallel group of one process: rank, world, transport, arena."""
 
-    def __init__(self, group=None, transport: str = "auto", device=None, arena_bytes: int = 1 << 30):
+    def __init__(self, group=None, transport: str = "auto", device=None, arena_bytes: int = 1 << 30,
+                 layout: str = "device", buffer_factor: float = 2.0):
+        """layout (p2p transport): "device" -- routing counts are exchanged and the receive
+        layout is computed on the device; every MoE layer has fixed slabs of
+        El * seg_cap rows (seg_cap = the capacity, or, dropless, buffer_factor x the
+        balanced per-expert load, rounded up to 128), so nothing reaches the host and the
+        step can be captured as a CUDA graph.  Pairs beyond seg_cap per expert are dropped
+        (counted in `dropped_pairs()`).  "host" -- counts are all-gathered to the host once
+        per layer and the slabs are sized exactly (no drop beyond the capacity)."""
+        if layout not in ("device", "host"):
+            raise ValueError(f"unknown expert-parallel layout {layout!r}")
+        self.layout = layout
+        self.buffer_factor = float(buffer_factor)
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
@@ -99,6 +112,11 @@ class EPContext:
         self.arena = None
         self._arena_bytes = arena_bytes
         self.stats = {"host_syncs": 0}
+        self._slots: list = []           # device layout: per MoE call of a step (fixed slabs)
+        self._cursor = 0
+        self._shared = None              # device layout: backward slabs shared by all layers
+        self._tokens = None              # tokens per rank (must be the same on every rank)
+        self._dropped = None
         # id(bf16 expert weight) -> (e4m3 weight, fp32 128x128 block scales): when both expert
         # weights of a layer are present, its forward expert GEMMs run in block-scaled fp8
         self.fp8_weights: dict = {}
@@ -123,11 +141,56 @@ class EPContext:
         return self.arena
 
     def begin_step(self):
-        """Start of a micro-step: every rank has finished reading the previous
-        step's regions (device barrier) before they are handed out again."""
+        """Start of a micro-step.  Host layout: every rank has finished reading the previous
+        step's regions (device barrier) before they are handed out again.  Device layout:
+        the k-th MoE layer of every step reuses the k-th set of slabs; the barriers inside
+        each layer's exchange already order every reuse, so nothing is launched here."""
+        if self.layout == "device" and self.transport == "p2p":
+            self._cursor = 0
+            return
         if self.arena is not None:
             self.arena.barrier()
             self.arena.reset()
+
+    def dropped_pairs(self) -> int:
+        """(token, expert) pairs of this rank dropped by the device layout's slab bound so far
+        (reads the device counter: a host sync; call it outside timed loops)."""
+        return 0 if self._dropped is None else int(self._dropped.item())
+
+    # ---- device layout: fixed slabs ----------------------------------------------------
+    def seg_cap(self, T: int, k: int, E: int, capacity: int) -> int:
+        if capacity > 0:
+            return (capacity + 127) // 128 * 128
+        bal = math.ceil(self.buffer_factor * self.world * T * k / E)
+        return max(128, (bal + 127) // 128 * 128)
+
+    def slot(self, T: int, k: int, E: int, El: int, D: int, capacity: int) -> "_Slot":
+        """Slabs of the next MoE layer of this step (allocated on the first step; every
+        rank allocates the same sizes in the same order)."""
+        if self._tokens is None:
+            t = torch.tensor([T], device=self.device)
+            mx, mn = t.clone(), t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=self.group)
+            dist.all_reduce(mn, op=dist.ReduceOp.MIN, group=self.group)
+            if int(mx.item()) != int(mn.item()):
+                raise ValueError("the device expert-parallel layout needs the same token count on every rank")
+            self._tokens = T
+            self._dropped = torch.zeros(1, dtype=torch.int32, device=self.device)
+        elif T != self._tokens:
+            raise ValueError(f"device expert-parallel layout was set up for {self._tokens} tokens per rank, got {T}")
+        arena = self.ensure_arena()
+        cap = self.seg_cap(T, k, E, capacity)
+        R = El * cap
+        N = self.world
+        if self._shared is None:
+            self._shared = _Shared(arena, N, R, D, T * k, E)
+        if self._cursor == len(self._slots):
+            self._slots.append(_Slot(arena, N, R, D, E, El, cap, self.device))
+        sl = self._slots[self._cursor]
+        if (sl.R, sl.D, sl.E, sl.cap) != (R, D, E, cap):
+            raise ValueError("MoE layers of one step changed shape between steps")
+        self._cursor += 1
+        return sl
 
     def all_gather_counts(self, counts: torch.Tensor) -> np.ndarray:
         """[E] int32 per rank -> host [N, E] (one small collective + one host sync)."""
@@ -135,6 +198,32 @@ class EPContext:
         dist.all_gather(out, counts.contiguous(), group=self.group)
         self.stats["host_syncs"] += 1
         return torch.stack(out).cpu().numpy()
+
+
+class _Slot:
+    """Fixed peer-mapped slabs of one MoE layer (device layout): receive rows x, routing
+    metadata, expert outputs y; plus this rank's device-computed layout tensors."""
+
+    def __init__(self, arena, N, R, D, E, El, cap, device):
+        self.R, self.D, self.E, self.cap = R, D, E, cap
+        self.x = arena.alloc([R * D * 2] * N)
+        self.meta = arena.alloc([R * 16] * N)
+        self.y = arena.alloc([R * D * 2] * N)
+        z = lambda n: torch.zeros(n, dtype=torch.int32, device=device)
+        self.dst_base, self.keep_lim, self.offs_local, self.kept_local = z(E), z(E), z(El + 1), z(El)
+        self.rows = [R] * N
+
+
+class _Shared:
+    """Backward slabs shared by every MoE layer (device layout): output gradients pushed to
+    the owners, input gradients pulled back, routing-weight gradients, the count board."""
+
+    def __init__(self, arena, N, R, D, pairs, E):
+        self.dy = arena.alloc([R * D * 2] * N)
+        self.dx = arena.alloc([R * D * 2] * N)
+        self.dw = arena.alloc([pairs * 4] * N)
+        self.board = arena.alloc([N * E * 4] * N)
+        self.pairs = [pairs] * N
 
 
 # ----------------------------------------------------------------------------
@@ -253,6 +342,103 @@ class _EPMoEP2P(torch.autograd.Function):
         return (dx, drouter, dw13, dw2, (dout if has_add else None), None, None, None, None, None, None, None)
 
 
+class _EPMoEDev(torch.autograd.Function):
+    """p2p transport with the device-computed layout: no host synchronisation anywhere in the
+    layer (forward or backward), fixed slabs, device-epoch barriers -- capturable in a CUDA graph."""
+
+    @staticmethod
+    def forward(ctx, x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta, gs):
+        C = _ext.load()
+        x = x.contiguous()
+        T, D = x.shape
+        E = router_w.shape[0]
+        El = w13.shape[0]
+        F2 = w13.shape[1]
+        me = ep.rank
+        sl = ep.slot(T, k, E, El, D, capacity)
+        sh = ep._shared
+        arena = ep.arena
+        R = sl.R
+        logits = mm_nt(x, router_w, out_f32=True)
+        idx, wts, probs = C.router_topk(logits, k, renorm)
+        counts, loc_off, pos, _ = C.moe_plan(idx, E, 0, cap_rows_for(T, k, E, 0))
+        # counts -> every rank's board, device barrier, layout from the board
+        C.ep_exchange_layout(counts, sh.board.ptrs, arena.sig_ptrs, me, arena.epoch_ctr, El, capacity, sl.cap,
+                             sl.dst_base, sl.keep_lim, sl.offs_local, sl.kept_local, ep._dropped)
+        slot = C.ep_dispatch(x, idx, pos, loc_off, sl.dst_base, sl.keep_lim, wts, sl.x.ptrs, sl.meta.ptrs, sl.rows,
+                             El, me)
+        x_recv = sl.x.view(torch.bfloat16, R, D)
+        meta = sl.meta.view(torch.int32, R, 4)
+        C.ep_pad_rows(x_recv, meta, sl.offs_local, sl.kept_local)
+        arena.barrier()                                       # all pairs have landed
+        y_recv = sl.y.view(torch.bfloat16, R, D)
+        offs_local = sl.offs_local
+        q13 = ep.fp8_weights.get(id(w13)) if ep.fp8_weights else None
+        q2 = ep.fp8_weights.get(id(w2)) if ep.fp8_weights else None
+        if q13 is not None and q2 is not None:
+            from ..ops.fp8 import fp8_grouped_mm, quantize_act
+            H = fp8_grouped_mm(x_recv, q13[0], q13[1], offs_local, R)
+            g, u = deinterleave_cols(H)
+            act = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
+            aq, sa = quantize_act(act)
+            C.fp8_gemm(aq, sa, q2[0], q2[1].reshape(-1), y_recv, offs_local, R)
+        else:
+            act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)
+            H = torch.empty(R, F2, device=x.device, dtype=torch.bfloat16)
+            C.gemm_grouped_m(x_recv, w13, offs_local, act, False, EPI_SWIGLU, 1.0, None, H, 256, R)
+            C.gemm_grouped_m(act, w2, offs_local, y_recv, False, EPI_BF16, 1.0, None, None, 256, R)
+        arena.barrier()                                       # every owner's outputs are ready
+        out = C.ep_combine(slot, idx, wts, sl.y.ptrs, sl.rows, El, D, None if add is None else add.contiguous())
+        ctx.save_for_backward(x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, H, act)
+        # the slabs are views of the shared arena (kept on ctx, not saved tensors); the next
+        # forward of this layer rewrites them only after this backward
+        ctx.ep, ctx.sl = ep, sl
+        ctx.cfg = (k, renorm, aux_alpha, z_beta, gs, add is not None)
+        aux = x.new_zeros((), dtype=torch.float32)
+        if aux_alpha > 0:
+            aux = aux + aux_alpha * E * ((counts.float() / (T * k)) * probs.mean(0)).sum()
+        if z_beta > 0:
+            lse = torch.logsumexp(logits, dim=-1)
+            aux = aux + z_beta * (lse * lse).mean()
+        ctx.mark_non_differentiable(aux)
+        return out, aux
+
+    @staticmethod
+    def backward(ctx, dout, daux):
+        x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, H, act = ctx.saved_tensors
+        k, renorm, aux_alpha, z_beta, gs, has_add = ctx.cfg
+        ep, sl = ctx.ep, ctx.sl
+        sh, arena = ep._shared, ep.arena
+        C = _ext.load()
+        T, D = x.shape
+        El = w13.shape[0]
+        R = sl.R
+        x_recv = sl.x.view(torch.bfloat16, R, D)
+        meta = sl.meta.view(torch.int32, R, 4)
+        y_recv = sl.y.view(torch.bfloat16, R, D)
+        dout = dout.contiguous()
+        dwts = sh.dw.view(torch.float32, T, k)
+        dwts.zero_()                                          # dropped pairs keep a zero gradient
+        C.ep_push(dout, slot, idx, sh.dy.ptrs, sl.rows, El)
+        arena.barrier()                                       # all output gradients have landed
+        dy_recv = sh.dy.view(torch.bfloat16, R, D)
+        C.ep_owner_bwd(dy_recv, y_recv, meta, sl.offs_local, sl.kept_local, sh.dw.ptrs, sh.pairs)
+        dH = torch.empty_like(H)
+        C.gemm_grouped_m(dy_recv, w2, sl.offs_local, dH, True, EPI_SWIGLU_BWD, 1.0, H, None, 256, R)
+        dw2 = torch.empty_like(w2)
+        C.gemm_grouped_k(dy_recv, act, sl.offs_local, dw2, EPI_BF16, 1.0, 256)
+        dx_recv = sh.dx.view(torch.bfloat16, R, D)
+        C.gemm_grouped_m(dH, w13, sl.offs_local, dx_recv, True, EPI_BF16, 1.0, None, None, 256, R)
+        dw13 = torch.empty_like(w13)
+        C.gemm_grouped_k(dH, x_recv, sl.offs_local, dw13, EPI_BF16, 1.0, 256)
+        arena.barrier()                                       # input gradients and weight gradients are ready
+        dlogits, _ = C.router_bwd(logits, probs, idx, dwts, counts, renorm, aux_alpha * gs, z_beta * gs)
+        dx_router = mm_nn(dlogits, router_w)
+        dx = C.ep_combine(slot, idx, None, sh.dx.ptrs, sl.rows, El, D, dx_router)
+        drouter = mm_tn(dlogits, x)
+        return (dx, drouter, dw13, dw2, (dout if has_add else None), None, None, None, None, None, None, None)
+
+
 # ----------------------------------------------------------------------------
 # all_to_all transport (NCCL baseline on CUDA, gloo on CPU): autograd through torch ops
 # ----------------------------------------------------------------------------
@@ -333,6 +519,9 @@ def ep_moe_ffn(x: torch.Tensor, router_w: torch.Tensor, w13: torch.Tensor, w2: t
     """Expert-parallel routed SwiGLU FFN.  x [T, D] local tokens; router_w [E, D]
     (replicated); w13 [El, 2F, D] / w2 [El, D, F] this rank's experts.  `capacity`
     is the per-expert limit over the whole group (0: dropless)."""
+    if ep.transport == "p2p" and x.is_cuda and ep.layout == "device":
+        return _EPMoEDev.apply(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta,
+                               aux_grad_scale)
     if ep.transport == "p2p" and x.is_cuda:
         return _EPMoEP2P.apply(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta,
                                aux_grad_scale)

@@ -27,7 +27,8 @@ from .zero import ZeroAdamW
 
 class ExpertDataParallel:
     def __init__(self, group=None, transport: str = "auto", bucket_bytes: int = 128 << 20,
-                 arena_bytes: int = 1 << 30, zero_transport: str = "nccl"):
+                 arena_bytes: int = 1 << 30, zero_transport: str = "nccl", layout: str = "device",
+                 buffer_factor: float = 2.0):
         """zero_transport: "nccl" (reduce-scatter / all-gather collectives) or "p2p" (the
         reduce-scatter and the updated-weight all-gather fused into the optimiser kernels over
         peer memory, see omnicoder.parallel.zero)."""
@@ -35,9 +36,29 @@ class ExpertDataParallel:
         self.zero_transport = zero_transport
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
-        self.ep = EPContext(self.group, transport=transport, arena_bytes=arena_bytes)
+        self.ep = EPContext(self.group, transport=transport, arena_bytes=arena_bytes, layout=layout,
+                            buffer_factor=buffer_factor)
         self.bucket_bytes = bucket_bytes
         self.opt = None
+
+    @staticmethod
+    def arena_bytes_for(cfg, tokens_per_rank: int, world: int, buffer_factor: float = 2.0) -> int:
+        """Peer-mapped bytes per rank that the device-layout exchange of one step of `cfg` needs
+        (every MoE layer's x / metadata / y slabs, the shared backward slabs, the count board)."""
+        import math
+        m = cfg.moe
+        E, k, D = m.n_experts, m.top_k, cfg.d_model
+        El = E // world
+        if m.capacity_factor > 0:
+            cap = m.capacity(tokens_per_rank * world)
+            seg = (cap + 127) // 128 * 128
+        else:
+            seg = max(128, (math.ceil(buffer_factor * world * tokens_per_rank * k / E) + 127) // 128 * 128)
+        R = El * seg
+        n_moe = sum(1 for i in range(cfg.n_layers) if cfg.is_moe_layer(i))
+        per_layer = 2 * R * D * 2 + R * 16
+        shared = 2 * R * D * 2 + tokens_per_rank * k * 4 + world * E * 4
+        return n_moe * (per_layer + 1024) + shared + (1 << 20)
 
     # ---- model construction -------------------------------------------------
     def expert_slice(self, n_experts: int) -> tuple[int, int]:
@@ -70,6 +91,15 @@ class ExpertDataParallel:
 
     def sync_and_step(self, model, opt, lr: float):
         opt.step(lr=lr)
+
+    def graph_capturable(self) -> bool:
+        """Forward + backward can be captured as one CUDA graph: the expert exchange runs on the
+        device layout (no host synchronisation, fixed slabs, device-epoch barriers)."""
+        return self.ep.transport == "p2p" and self.ep.layout == "device" and self.ep.device.type == "cuda"
+
+    def set_deferred_reduce(self, on: bool):
+        if self.opt is not None:
+            self.opt.defer = on
 
     def all_reduce_mean(self, t: torch.Tensor) -> torch.Tensor:
         t = t.clone()

@@ -14,8 +14,11 @@ new, larger chunk (a collective rendezvous), so the exchange never drops a
 token for lack of buffer space.
 
 ``barrier()`` is the device-side phase separator of the exchange: one tiny
-kernel that signals every peer with a release store and waits (bounded) for
-every peer's signal; a timeout is recorded in the device status word.
+kernel that signals every peer with a release store of the next epoch of a
+device counter and waits (bounded) for every peer's signal; a timeout is
+recorded in the device status word.  Regions can also be kept for the life of
+the arena (``reset`` is then never called): the expert-parallel exchange's
+device-computed layout uses slabs of a fixed worst-case size per layer.
 """
 from __future__ import annotations
 
@@ -80,6 +83,8 @@ class SymmArena:
         self._sig.buf.zero_()
         self.sig_ptrs = self._sig.ptrs
         self.epoch = 0
+        # barrier epochs are counted on the device (so CUDA graphs can replay barriers)
+        self.epoch_ctr = torch.zeros(1, dtype=torch.int32, device=device)
         self.peak = [0] * self.world
         torch.cuda.synchronize(device)
         dist.barrier(group)
@@ -109,9 +114,11 @@ class SymmArena:
         return Region([c.ptrs[r] + offs[r] for r in range(self.world)], sizes, local)
 
     def barrier(self):
-        """Device-side barrier over the group on the current stream (bounded wait)."""
+        """Device-side barrier over the group on the current stream (bounded wait).  The epoch
+        lives in a device counter that every rank advances alike, so the barrier can be captured
+        in a CUDA graph and replayed."""
         self.epoch += 1
-        _ext.load().ep_barrier(self.sig_ptrs, self.rank, self.epoch, self.device.index)
+        _ext.load().ep_barrier_dev(self.sig_ptrs, self.rank, self.epoch_ctr)
 
     def nbytes(self) -> int:
         return sum(c.nbytes for c in self.chunks)

@@ -131,6 +131,10 @@ class ZeroAdamW:
             self.estate.append({"master": master, "m": torch.zeros_like(master), "v": torch.zeros_like(master)})
         self._accumulating = False
         self._first_micro = True
+        # deferred mode (CUDA-graph replay of forward + backward): the hooks only write the
+        # gradients into the buckets (those copies are what a graph captures); step() launches
+        # every bucket's reduction
+        self.defer = False
         self._norm = torch.zeros(1, device=self.device, dtype=torch.float32)
         for p in dense:
             p.register_post_accumulate_grad_hook(self._hook)
@@ -151,6 +155,8 @@ class ZeroAdamW:
         else:
             dst.add_(g)
         p.grad = None
+        if self.defer:
+            return
         b.got.add(p)
         b.ready += 1
         if b.ready == len(b.params) and not self._accumulating:
@@ -180,6 +186,10 @@ class ZeroAdamW:
         if lr is not None:
             self.lr = lr
         self.step_count += 1
+        if self.defer:                    # every bucket was filled by the replayed backward
+            for b in self.buckets:
+                if b.work is None:
+                    self._launch(b)
         if self.p2p:
             return self._step_p2p()
         for b in self.buckets:

@@ -6,7 +6,8 @@ expert-parallel x data-parallel layout of :mod:`omnicoder.parallel` (experts
 sharded over the EP group, dense parameters replicated with ZeRO-1 sharded
 AdamW state); without one it is the single-device trainer.
 
-`cuda_graph=True` (single device, grad_accum 1): after `graph_warmup` eager
+`cuda_graph=True` (grad_accum 1; one device, or an expert x data parallel layout whose
+exchange runs on the device -- see ExpertDataParallel.graph_capturable): after `graph_warmup` eager
 steps, forward + backward is captured once as a CUDA graph and replayed every
 step (the batch is copied into static input buffers; the gradients are static
 tensors the replay overwrites, so they are not reset between steps); the
@@ -45,7 +46,8 @@ class Trainer:
         self.tcfg = tcfg
         self.parallel = parallel
         self.step_idx = 0
-        self.cuda_graph = cuda_graph and parallel is None and max(1, tcfg.grad_accum) == 1
+        self.cuda_graph = (cuda_graph and max(1, tcfg.grad_accum) == 1 and
+                           (parallel is None or getattr(parallel, "graph_capturable", lambda: False)()))
         self.graph_warmup = graph_warmup
         self._graph = None
         self._graph_key = None
@@ -100,10 +102,17 @@ class Trainer:
         self._static_ids, self._static_lab = ids.clone(), labels.clone()
         self.opt.zero_grad(set_to_none=True)
         dev = ids.device
+        par = self.parallel
+        if par is not None:
+            # gradient reductions move out of the backward hooks into opt.step(); the graph
+            # holds only this rank's kernels (device-side exchange and barriers), no NCCL call
+            par.set_deferred_reduce(True)
         side = torch.cuda.Stream(device=dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         try:
             with torch.cuda.stream(side):        # lazy setup outside the capture; no optimiser step
+                if par is not None:
+                    par.before_forward(0, 1)
                 out = self.model(self._static_ids, labels=self._static_lab, assume_all_valid=assume_all_valid)
                 out["loss"].backward()
             torch.cuda.current_stream(dev).wait_stream(side)
@@ -113,10 +122,14 @@ class Trainer:
             torch.cuda.empty_cache()             # the graph's private pool replaces the eager steps' cache
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
+                if par is not None:
+                    par.before_forward(0, 1)
                 out = self.model(self._static_ids, labels=self._static_lab, assume_all_valid=assume_all_valid)
                 out["loss"].backward()
         except Exception as e:                   # stay eager
             self.cuda_graph, self.graph_error = False, f"{type(e).__name__}: {e}"
+            if par is not None:
+                par.set_deferred_reduce(False)
             self.opt.zero_grad(set_to_none=True)
             return
         self._graph, self._graph_key = g, key
@@ -130,7 +143,10 @@ class Trainer:
         for p, g in self._static_grads:              # the replay wrote these tensors
             p.grad = g
         lr = self.lr_at(self.step_idx)
-        self.opt.step(lr=lr)
+        if self.parallel is not None:
+            self.parallel.sync_and_step(self.model, self.opt, lr)
+        else:
+            self.opt.step(lr=lr)
         self.step_idx += 1
         loss, ce, aux = (t.clone() for t in self._static_out)
         return StepStats(loss, ce, aux, ids.numel(), lr)

@@ -56,23 +56,33 @@ def _layer_worker(rank, world, port, q):
         dys = (torch.randn(world * T, D, generator=g) * 0.1).to(dev, torch.bfloat16)
         El = E // world
         lo, hi = rank * El, (rank + 1) * El
-        for cap in (0, 300):
+        # (capacity passed to the layer, capacity of the single-GPU reference, variants):
+        # variant = (name, transport, layout, buffer factor); the device layout with buffer
+        # factor 0.5 bounds every expert at 256 rows, i.e. the reference with capacity 256
+        cases = [(0, 0, [("p2p", "p2p", "device", 2.0), ("p2p_host", "p2p", "host", 2.0),
+                         ("nccl", "nccl", "host", 2.0)]),
+                 (300, 300, [("p2p", "p2p", "device", 2.0), ("p2p_host", "p2p", "host", 2.0),
+                             ("nccl", "nccl", "host", 2.0)]),
+                 (0, 256, [("p2p_bound", "p2p", "device", 0.5)])]
+        for cap, ref_cap, variants in cases:
             # single-GPU reference on all tokens
             xa = xs.clone().requires_grad_(True)
             ra = wr.clone().requires_grad_(True)
             a13 = w13.clone().requires_grad_(True)
             a2 = w2.clone().requires_grad_(True)
-            ya, _ = moe_ffn(xa, ra, a13, a2, K, cap, True)
+            ya, _ = moe_ffn(xa, ra, a13, a2, K, ref_cap, True)
             ya.backward(dys)
-            for transport in ("p2p", "nccl"):
-                ep = EPContext(dist.group.WORLD, transport=transport, device=dev, arena_bytes=64 << 20)
-                xb = xs[rank * T:(rank + 1) * T].clone().requires_grad_(True)
-                rb = wr.clone().requires_grad_(True)
-                b13 = w13[lo:hi].clone().requires_grad_(True)
-                b2 = w2[lo:hi].clone().requires_grad_(True)
-                ep.begin_step()
-                yb, _ = ep_moe_ffn(xb, rb, b13, b2, K, ep, capacity=cap, renorm=True)
-                yb.backward(dys[rank * T:(rank + 1) * T])
+            for name, transport, layout, bf in variants:
+                ep = EPContext(dist.group.WORLD, transport=transport, device=dev, arena_bytes=64 << 20, layout=layout,
+                               buffer_factor=bf)
+                for it in range(2):                   # the second pass reuses the device layout's slabs
+                    xb = xs[rank * T:(rank + 1) * T].clone().requires_grad_(True)
+                    rb = wr.clone().requires_grad_(True)
+                    b13 = w13[lo:hi].clone().requires_grad_(True)
+                    b2 = w2[lo:hi].clone().requires_grad_(True)
+                    ep.begin_step()
+                    yb, _ = ep_moe_ffn(xb, rb, b13, b2, K, ep, capacity=cap, renorm=True)
+                    yb.backward(dys[rank * T:(rank + 1) * T])
                 torch.cuda.synchronize()
                 code = C.status()[0]
                 C.status_reset()
@@ -80,8 +90,10 @@ def _layer_worker(rank, world, port, q):
                 drb = rb.grad.float().clone()
                 dist.all_reduce(drb)
                 sl = slice(rank * T, (rank + 1) * T)
-                out[(cap, transport)] = {
+                out[(cap, name)] = {
                     "status": code,
+                    # pairs beyond the slab bound are dropped (and counted) only in the bounded case
+                    "dropped": ((ep.dropped_pairs() > 0) == (name == "p2p_bound"), ep.dropped_pairs()),
                     "y": _close(yb, ya[sl], 2e-2),
                     "dx": _close(xb.grad, xa.grad[sl], 3e-2),
                     "drouter": _close(drb, ra.grad, 3e-2),
@@ -108,7 +120,7 @@ def _layer_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def _step_worker(rank, world, port, q, zero_transport="nccl"):
+def _step_worker(rank, world, port, q, zero_transport="nccl", graph=False):
     import datetime
 
     import torch.distributed as dist
@@ -134,14 +146,15 @@ def _step_worker(rank, world, port, q, zero_transport="nccl"):
         ids, lab = synthetic_batch(2 * world, 256, cfg.vocab_size, seed=3, step=0, device=dev)
         ref = build_model(cfg, device=dev, seed=0)
         rt = Trainer(ref, tc)
-        ref_losses = [float(rt.step(ids, lab).loss) for _ in range(3)]
+        n = 5 if graph else 3
+        ref_losses = [float(rt.step(ids, lab).loss) for _ in range(n)]
         del rt, ref
         par = ExpertDataParallel(dist.group.WORLD, arena_bytes=64 << 20, zero_transport=zero_transport)
         model = build_model(cfg, device=dev, seed=0, ep=par)
-        tr = Trainer(model, tc, par)
+        tr = Trainer(model, tc, par, cuda_graph=graph, graph_warmup=2)
         mine = ids.chunk(world)[rank], lab.chunk(world)[rank]
         losses = []
-        for _ in range(3):
+        for _ in range(n):
             l = tr.step(*mine).loss.detach().float()
             dist.all_reduce(l)
             losses.append(float(l) / world)
@@ -149,7 +162,8 @@ def _step_worker(rank, world, port, q, zero_transport="nccl"):
         C = _ext.load()
         code = C.status()[0]
         C.status_reset()
-        q.put((rank, {"ref": ref_losses, "ep": losses, "status": code}))
+        q.put((rank, {"ref": ref_losses, "ep": losses, "status": code,
+                      "graphed": tr._graph is not None, "graph_error": tr.graph_error}))
     except Exception as e:
         q.put((rank, repr(e)))
         raise
@@ -159,6 +173,10 @@ def _step_worker(rank, world, port, q, zero_transport="nccl"):
 
 def _step_worker_p2p_zero(rank, world, port, q):
     _step_worker(rank, world, port, q, "p2p")
+
+
+def _step_worker_graph(rank, world, port, q):
+    _step_worker(rank, world, port, q, "nccl", graph=True)
 
 
 def _zero_worker(rank, world, port, q):
@@ -270,5 +288,19 @@ def test_ep_dp_train_step_with_p2p_zero_matches_single_gpu():
     for rank, out in res.items():
         assert isinstance(out, dict), out
         assert out["status"] == 0
+        for a, b in zip(out["ref"], out["ep"]):
+            assert abs(a - b) < 2e-2 * max(1.0, abs(a)), out
+
+
+def test_ep_dp_train_step_cuda_graph_matches_single_gpu():
+    """Forward + backward of the expert x data parallel step captured as one CUDA graph per
+    rank (device-side expert exchange and barriers; ZeRO-1 reductions after the replay): the
+    replayed steps give the single-GPU losses."""
+    _need_gpus(2)
+    res = _run(_step_worker_graph)
+    for rank, out in res.items():
+        assert isinstance(out, dict), out
+        assert out["status"] == 0
+        assert out["graphed"], out["graph_error"]
         for a, b in zip(out["ref"], out["ep"]):
             assert abs(a - b) < 2e-2 * max(1.0, abs(a)), out
