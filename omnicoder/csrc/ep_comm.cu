@@ -281,15 +281,14 @@ __global__ void ep_barrier_dev_kernel(EpPeers sig, int me, int n, unsigned* epoc
 // Each rank stores its per-expert pair counts into row `me` of every rank's count board
 // [N][E], passes a device barrier, then derives from the board (C[s][e] = pairs of source s
 // for expert e) the layout that the host used to compute from all-gathered counts:
-//   cap       = min(capacity or inf, seg_cap)          per-expert limit over the group
-//   kept[s,e] = clamp(min(C[s,e], cap - sum_{s'<s} C[s',e]), 0)
+//   kept[s,e] = clamp(min(C[s,e], cap - sum_{s'<s} C[s',e]), 0)    (cap: the capacity, or none)
 //   seg[e]    = sum_s kept[s,e], padded to 128 rows; segments of one owner back to back
 //   dst_base[e] = base of e's segment + sum_{s<me} kept[s,e];  keep_lim[e] = kept[me,e]
 //   offs_local / kept_local: this rank's El segments
-//   *dropped += this rank's pairs lost to seg_cap (beyond what the capacity alone drops)
-// seg_cap (a multiple of 128) bounds every segment, so each owner's slab holds at most
-// El * seg_cap rows whatever the routing: the slabs are allocated once, and no count has to
-// reach the host.  One block of >= E threads.
+// Each owner's slab holds El * seg_cap rows.  When an owner's padded segments do not fit, each
+// of its experts is limited to seg_cap rows (cap = min(capacity, seg_cap)), which always fits;
+// *dropped counts this rank's pairs lost to that bound (not those the capacity alone drops).
+// The slabs are allocated once and no count reaches the host.  One block of >= E threads.
 __global__ void ep_exchange_layout_kernel(EpPeers board, EpPeers sig, int me, int n, unsigned* epoch_ctr,
                                           const int* __restrict__ counts, int E, int El, int capacity, int seg_cap,
                                           int* __restrict__ dst_base, int* __restrict__ keep_lim,
@@ -307,9 +306,30 @@ __global__ void ep_exchange_layout_kernel(EpPeers board, EpPeers sig, int me, in
   const volatile int* mine = reinterpret_cast<const volatile int*>(board.ptr[me]);
   for (int i = threadIdx.x; i < n * E; i += blockDim.x) C[i] = mine[i];
   __syncthreads();
+  // pass 1: segments under the capacity alone
+  const int cap0 = capacity > 0 ? capacity : 0x3fffffff;
+  if (e < E) {
+    int before = 0, seg = 0;
+    for (int s = 0; s < n; ++s) {
+      const int c = C[s * E + e];
+      seg += max(0, min(c, cap0 - before));
+      before += c;
+    }
+    seg_pad[e] = (seg + 127) / 128 * 128;
+  }
+  __syncthreads();
+  bool bounded = false;
+  if (e < E) {
+    const int owner = e / El;
+    long long total = 0;
+    for (int j = owner * El; j < owner * El + El; ++j) total += seg_pad[j];
+    bounded = total > (long long)El * seg_cap;
+  }
+  __syncthreads();
+  // pass 2: the final per-expert limit
   int kept_me = 0, before_me = 0, seg = 0, lost_me = 0;
   if (e < E) {
-    const int cap = capacity > 0 ? min(capacity, seg_cap) : seg_cap;
+    const int cap = bounded ? min(cap0, seg_cap) : cap0;
     int before = 0;
     for (int s = 0; s < n; ++s) {
       const int c = C[s * E + e];
@@ -317,9 +337,7 @@ __global__ void ep_exchange_layout_kernel(EpPeers board, EpPeers sig, int me, in
       if (s < me) before_me += k;
       if (s == me) {
         kept_me = k;
-        // pairs lost to the slab bound only (not to the configured capacity)
-        const int k_cap = capacity > 0 ? max(0, min(c, capacity - before)) : c;
-        lost_me = k_cap - k;
+        lost_me = max(0, min(c, cap0 - before)) - k;
       }
       seg += k;
       before += c;

@@ -92,11 +92,13 @@ class EPContext:
                  layout: str = "device", buffer_factor: float = 2.0):
         """layout (p2p transport): "device" -- routing counts are exchanged and the receive
         layout is computed on the device; every MoE layer has fixed slabs of
-        El * seg_cap rows (seg_cap = the capacity, or, dropless, buffer_factor x the
+        El * seg_cap rows per rank (seg_cap = the capacity, or, dropless, buffer_factor x the
         balanced per-expert load, rounded up to 128), so nothing reaches the host and the
-        step can be captured as a CUDA graph.  Pairs beyond seg_cap per expert are dropped
-        (counted in `dropped_pairs()`).  "host" -- counts are all-gathered to the host once
-        per layer and the slabs are sized exactly (no drop beyond the capacity)."""
+        step can be captured as a CUDA graph.  Nothing is dropped while an owner's routed
+        rows fit its slab; when they do not, each of its experts keeps at most seg_cap rows
+        (the pairs lost are counted in `dropped_pairs()`).  "host" -- counts are all-gathered
+        to the host once per layer and the slabs are sized exactly (no drop beyond the
+        capacity)."""
         if layout not in ("device", "host"):
             raise ValueError(f"unknown expert-parallel layout {layout!r}")
         self.layout = layout

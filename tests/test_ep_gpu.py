@@ -100,7 +100,7 @@ def _layer_worker(rank, world, port, q):
                     "dw13": _close(b13.grad, a13.grad[lo:hi], 3e-2),
                     "dw2": _close(b2.grad, a2.grad[lo:hi], 3e-2),
                 }
-            if cap == 0:
+            if cap == 0 and ref_cap == 0:
                 # block-scaled fp8 forward expert GEMMs: output within fp8 precision of bf16
                 ep = EPContext(dist.group.WORLD, transport="p2p", device=dev, arena_bytes=64 << 20)
                 b13, b2 = w13[lo:hi].contiguous(), w2[lo:hi].contiguous()
