@@ -34,7 +34,7 @@ def family(name: str) -> str:
             pair = " pair" if pair == "true" else ""
             return f"gemm[{kind} a_mn={amn[0]} b_mn={bmn[0]} epi={epi} bn={bn}{pair}]"
         return "gemm"
-    for key in ("attn_fwd_kernel", "attn_dkdv_kernel", "attn_dq_kernel", "attn_delta_kernel", "rmsnorm_fwd",
+    for key in ("ep_exchange_layout", "attn_fwd_kernel", "attn_dkdv_kernel", "attn_dq_kernel", "attn_delta_kernel", "rmsnorm_fwd",
                 "rmsnorm_bwd", "rope_kernel", "embedding_fwd", "embedding_bwd", "ce_kernel", "adamw_kernel",
                 "sq_norm_kernel", "router_topk", "router_bwd", "plan_count", "plan_scan", "plan_assign",
                 "moe_gather", "moe_combine_bwd", "moe_combine_kernel", "moe_scatter_add", "ep_dispatch",
@@ -53,6 +53,7 @@ def main():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--mb", type=int, default=2)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--cuda-graph", default="on", choices=["on", "off"])
     args = ap.parse_args()
     cfg = get_preset(args.preset)
     if args.layers:
@@ -68,10 +69,11 @@ def main():
 
         from omnicoder.parallel.expert_data import ExpertDataParallel
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-        rows = int(args.mb * args.seq * cfg.moe.top_k * 1.3) + cfg.moe.n_experts * 128
-        par = ExpertDataParallel(dist.group.WORLD, arena_bytes=cfg.n_layers * rows * (4 * cfg.d_model * 2 + 16))
+        par = ExpertDataParallel(dist.group.WORLD,
+                                 arena_bytes=ExpertDataParallel.arena_bytes_for(cfg, args.mb * args.seq, world))
     model = build_model(cfg, device=dev, seed=0, ep=par) if par is not None else build_model(cfg, device=dev, seed=0)
-    trainer = Trainer(model, TrainConfig(lr=3e-4, warmup_steps=10, max_steps=100, grad_clip=1.0), par)
+    trainer = Trainer(model, TrainConfig(lr=3e-4, warmup_steps=10, max_steps=100, grad_clip=1.0), par,
+                      cuda_graph=args.cuda_graph == "on")
     batches = [synthetic_batch(args.mb, args.seq, cfg.vocab_size, rank, i, device=dev) for i in range(4)]
     for b in batches[:3]:
         trainer.step(*b, assume_all_valid=True)

@@ -20,7 +20,8 @@ Two transports implement the same layout:
     combine fused with the weighted sum (peer loads), owner-side routing-weight
     gradient, device barriers with bounded waits.
   * "nccl" / CPU: torch.distributed.all_to_all_single with plain PyTorch
-    expert math -- the NCCL + cuBLAS baseline on GPUs and the gloo path of the
+    expert math (torch._grouped_mm over the local experts, a batched weighted
+    sum) -- the NCCL + cuBLAS comparison path on GPUs and the gloo path of the
     CPU tests.
 
 The reference has no expert parallelism (its EP launcher only sets an
@@ -493,18 +494,17 @@ def _ep_moe_a2a(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z
     rr = _a2a_meta(row, send, recv, ep.group).long()
     R = lay.rows[me]
     x_recv = x.new_zeros(R, D).index_copy(0, rr, xr)
-    segs = []
-    for el in range(El):
-        a, b = int(lay.offs_local[el]), int(lay.offs_local[el + 1])
-        h = x_recv[a:b] @ w13[el].t()
-        g, u = deinterleave_cols(h)
-        segs.append((F.silu(g.float()) * u.float()).to(x.dtype) @ w2[el].t())
-    y_recv = torch.cat(segs, 0) if segs else x.new_zeros(0, D)
+    # one grouped GEMM per projection over the local experts' (128-padded) segments
+    offs = torch.as_tensor(lay.offs_local[1:], dtype=torch.int32, device=x.device)
+    h = torch._grouped_mm(x_recv, w13.transpose(-2, -1), offs=offs)
+    g, u = deinterleave_cols(h)
+    y_recv = torch._grouped_mm(F.silu(g) * u, w2.transpose(-2, -1), offs=offs)
     yb = _A2A.apply(y_recv.index_select(0, rr), recv, send, ep.group)
-    wk = w.reshape(-1)[pair].unsqueeze(1)
-    out = torch.zeros(T, D, dtype=torch.float32, device=x.device).index_add(0, pair // k, yb.float() * wk)
+    # weighted sum of each token's k expert rows (dropped pairs contribute zero rows)
+    yk = x.new_zeros(T * k, D).index_copy(0, pair, yb)
+    out = torch.bmm(w.to(x.dtype).unsqueeze(1), yk.view(T, k, D)).squeeze(1)
     if add is not None:
-        out = out + add.float()
+        out = out + add
     aux = x.new_zeros((), dtype=torch.float32)
     if aux_alpha > 0:
         f = (counts.float() / (T * k)).detach()
@@ -512,7 +512,7 @@ def _ep_moe_a2a(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z
     if z_beta > 0:
         lse = torch.logsumexp(logits, dim=-1)
         aux = aux + z_beta * (lse * lse).mean()
-    return out.to(x.dtype), aux
+    return out, aux
 
 
 def ep_moe_ffn(x: torch.Tensor, router_w: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, k: int, ep: EPContext,
