@@ -368,20 +368,23 @@ struct DkdvSmem {
   static constexpr int kQ = NQC * 8192;            // [64 q x DQ] (64-row sub-tiles)
   static constexpr int kDO = (DV / 64) * 8192;     // [64 q x DV]
   static constexpr int kVec = 2 * BQ * 4;          // lse[64], delta[64]
+  static constexpr int NS = 3;                     // Q / dO / lse-delta ring stages
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kOffK + kK;
-  static constexpr int kOffQ = kOffV + kV;         // 2 stages
-  static constexpr int kOffDO = kOffQ + 2 * kQ;    // 2 stages
-  static constexpr int kOffVec = kOffDO + 2 * kDO;  // 2 stages of lse/delta
-  static constexpr int kOffBar = kOffVec + 2 * kVec;
+  static constexpr int kOffQ = kOffV + kV;           // NS stages
+  static constexpr int kOffDO = kOffQ + NS * kQ;     // NS stages
+  static constexpr int kOffVec = kOffDO + NS * kDO;  // NS stages of lse/delta
+  static constexpr int kOffBar = kOffVec + NS * kVec;
   static constexpr int kBytes = kOffBar + 256 + 1024;
 };
 
 // CTA = (kv tile of 128 rows, kv head, sequence); loops over query tiles of 64
 // rows (and over the query heads of a GQA group).  Q/dO (with the tile's lse and
-// delta, fetched by bulk copies on the same barrier) are double buffered so the
-// next tile streams in while this one computes; S^T is double buffered in TMEM
-// so K Q^T of the next tile runs during this tile's softmax.  P^T and dS^T (bf16)
+// delta, fetched by bulk copies on the same barrier) stream through a 3-stage ring,
+// so a tile's loads start two iterations before its MMAs; S^T is double buffered in
+// TMEM so K Q^T of the next tile runs during this tile's softmax.  The MMA thread
+// issues V dO^T of this tile before K Q^T of the next one: the softmax warps wait for
+// dP^T, while the next S^T is not needed until they finish this tile.  P^T and dS^T (bf16)
 // are written over the two halves of their S^T stage and feed their MMAs
 // (dV += P^T dO, dK += dS^T Q) straight from tensor memory: thread r holds row r
 // of both, which is the A-operand layout.  dP^T is released as soon as the
@@ -406,19 +409,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sDO = smem + L::kOffDO;
   float* sVec = reinterpret_cast<float*>(smem + L::kOffVec);  // [stage][lse 64 | delta 64]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  constexpr int NS = L::NS;
   uint64_t* kv_full = bars + 0;
-  uint64_t* q_full = bars + 1;    // [2] Q + lse/delta
-  uint64_t* q_empty = bars + 3;   // [2]
-  uint64_t* do_full = bars + 5;   // [2]
-  uint64_t* do_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;    // [2]
-  uint64_t* s_empty = bars + 11;  // [2] S^T / P^T / dS^T stage free (commit after dK read dS^T)
-  uint64_t* pt_ready = bars + 13; // one arrival per softmax warp
-  uint64_t* dp_full = bars + 14;
-  uint64_t* dp_empty = bars + 15; // one arrival per softmax warp: dP^T read
-  uint64_t* ds_ready = bars + 16; // one arrival per softmax warp
-  uint64_t* acc_done = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* q_full = bars + 1;    // [NS] Q + lse/delta
+  uint64_t* q_empty = bars + 4;   // [NS]
+  uint64_t* do_full = bars + 7;   // [NS]
+  uint64_t* do_empty = bars + 10; // [NS]
+  uint64_t* s_full = bars + 13;   // [2]
+  uint64_t* s_empty = bars + 15;  // [2] S^T / P^T / dS^T stage free (commit after dK read dS^T)
+  uint64_t* pt_ready = bars + 17; // one arrival per softmax warp
+  uint64_t* dp_full = bars + 18;
+  uint64_t* dp_empty = bars + 19; // one arrival per softmax warp: dP^T read
+  uint64_t* ds_ready = bars + 20; // one arrival per softmax warp
+  uint64_t* acc_done = bars + 21;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / BQ;
@@ -433,11 +437,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&do_full[i], 1);
       mbar_init(&do_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 1);
     }
@@ -470,8 +476,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int g = it / nq, i = i_lo + it % nq;
         const int hq = hk * G + g;
         const int qrow0 = b * p.S + i * BQ;
-        const int st = it & 1;
-        const uint32_t u = it >> 1;
+        const int st = it % NS;
+        const uint32_t u = it / NS;
         if (!mbar_wait(&q_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
         mbar_arrive_expect_tx(&q_full[st], L::kQ + L::kVec);
 #pragma unroll
@@ -493,53 +499,65 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = mbar_wait(kv_full, 0, p.status, STATUS_TIMEOUT_TMA_FULL);
       const uint32_t ka = smem_u32(sK), va = smem_u32(sV);
       auto issue_s = [&](int it) -> bool {
-        const int st = it & 1;
-        const uint32_t u = it >> 1;
-        if (!mbar_wait(&q_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) return false;
-        if (!mbar_wait(&s_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) return false;
+        const int qs = it % NS;                 // Q ring stage
+        const int ts = it & 1;                  // S^T tensor-memory stage
+        if (!mbar_wait(&q_full[qs], (it / NS) & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) return false;
+        if (!mbar_wait(&s_empty[ts], ((it >> 1) & 1) ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) return false;
         tc_fence_after();
-        const uint32_t qa = smem_u32(sQ + st * L::kQ);
+        const uint32_t qa = smem_u32(sQ + qs * L::kQ);
 #pragma unroll
         for (int kk = 0; kk < DQ / 16; ++kk)
-          tc_mma_f16(tS0 + st * 64, umma_desc_sw128(ka + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
+          tc_mma_f16(tS0 + ts * 64, umma_desc_sw128(ka + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
                      umma_desc_sw128(qa + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
-        tc_commit(&s_full[st]);
+        tc_commit(&s_full[ts]);
         return true;
       };
+      // dK += dS^T Q of tile j  (dS^T from tensor memory; Q read as MN-major)
+      auto issue_dk = [&](int j) -> bool {
+        if (!mbar_wait(ds_ready, j & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) return false;
+        tc_fence_after();
+        const int qs = j % NS, ts = j & 1;
+        const uint32_t qa = smem_u32(sQ + qs * L::kQ);
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          tc_mma_f16_ts(tdK, tS0 + ts * 64 + 32 + kk * 8, umma_desc_sw128(qa + kk * 2048, 8192, 1024), idesc_dk,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&s_empty[ts]);
+        tc_commit(&q_empty[qs]);
+        return true;
+      };
+      // Software pipeline, per iteration: dP^T(it), dK(it-1), S^T(it+1), dV(it).  dP^T of a tile
+      // is issued as soon as the softmax warps have read the previous one, ahead of the previous
+      // tile's dK, so it is ready when they finish P^T; S^T(it+1) reuses the tensor-memory stage
+      // of tile it-1 and so follows dK(it-1).
       if (ok && n > 0) ok = issue_s(0);
       for (int it = 0; it < n && ok; ++it) {
-        const int st = it & 1;
-        const uint32_t u = it >> 1;
+        const int qs = it % NS;
+        const uint32_t uq = it / NS;
+        const int ts = it & 1;
         const uint32_t ph = it & 1;
-        if (it + 1 < n && !issue_s(it + 1)) { ok = false; break; }
         // dP^T = V dO^T
-        if (!mbar_wait(&do_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
+        if (!mbar_wait(&do_full[qs], uq & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
         if (!mbar_wait(dp_empty, ph ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t da = smem_u32(sDO + st * L::kDO), qa = smem_u32(sQ + st * L::kQ);
+        const uint32_t da = smem_u32(sDO + qs * L::kDO);
 #pragma unroll
         for (int kk = 0; kk < DV / 16; ++kk)
           tc_mma_f16(tdP, umma_desc_sw128(va + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
                      umma_desc_sw128(da + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
         tc_commit(dp_full);
+        if (it > 0 && !issue_dk(it - 1)) { ok = false; break; }
+        if (it + 1 < n && !issue_s(it + 1)) { ok = false; break; }
         // dV += P^T dO  (P^T from tensor memory; dO read as MN-major: DV contiguous, 64-row sub-tiles)
         if (!mbar_wait(pt_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          tc_mma_f16_ts(tdV, tS0 + st * 64 + kk * 8, umma_desc_sw128(da + kk * 2048, 8192, 1024), idesc_dv,
+          tc_mma_f16_ts(tdV, tS0 + ts * 64 + kk * 8, umma_desc_sw128(da + kk * 2048, 8192, 1024), idesc_dv,
                         (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&do_empty[st]);
-        // dK += dS^T Q  (dS^T from tensor memory; Q read as MN-major)
-        if (!mbar_wait(ds_ready, ph, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk)
-          tc_mma_f16_ts(tdK, tS0 + st * 64 + 32 + kk * 8, umma_desc_sw128(qa + kk * 2048, 8192, 1024), idesc_dk,
-                        (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&s_empty[st]);
-        tc_commit(&q_empty[st]);
+        tc_commit(&do_empty[qs]);
       }
+      if (ok && n > 0) ok = issue_dk(n - 1);
       tc_commit(acc_done);
       mbar_wait(acc_done, 0, p.status, STATUS_TIMEOUT_DRAIN);
     }
@@ -553,17 +571,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int it = 0; it < n; ++it) {
       const int i = i_lo + it % nq;
       const int qpos0 = i * BQ + half * 32;
+      const int qs = it % NS;
       const int st = it & 1;
       const uint32_t u = it >> 1;
       const uint32_t ph = it & 1;
       // lse / delta of this tile arrived with Q (make the bulk-copy writes visible here)
-      if (!mbar_wait(&q_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
+      if (!mbar_wait(&q_full[qs], (it / NS) & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) { ok = false; break; }
       if (!mbar_wait(&s_full[st], u & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
       tc_fence_after();
       float P[32];
       tmem_ld32(tS0 + st * 64 + half * 32 + lane_off, P);
       tc_wait_ld();
-      const float* lse = sVec + st * 2 * BQ + half * 32;
+      const float* lse = sVec + qs * 2 * BQ + half * 32;
       const float* delta = lse + BQ;
       const bool need_mask = (p.causal && kpos0 + kTile - 1 > qpos0) ||
                              (p.window > 0 && kpos0 <= qpos0 + 31 - p.window);
@@ -675,18 +694,20 @@ struct DqSmem {
   static constexpr int kDO = (DV / 64) * kSubTile;   // [128 q x DV]
   static constexpr int kK = NQC * 8192;              // [64 kv x DQ] (64-row sub-tiles)
   static constexpr int kV = (DV / 64) * 8192;        // [64 kv x DV]
+  static constexpr int NS = 3;                       // K / V ring stages
   static constexpr int kOffQ = 0;
   static constexpr int kOffDO = kOffQ + kQ;
-  static constexpr int kOffK = kOffDO + kDO;         // 2 stages
-  static constexpr int kOffV = kOffK + 2 * kK;       // 2 stages
-  static constexpr int kOffBar = kOffV + 2 * kV;
+  static constexpr int kOffK = kOffDO + kDO;         // NS stages
+  static constexpr int kOffV = kOffK + NS * kK;      // NS stages
+  static constexpr int kOffBar = kOffV + NS * kV;
   static constexpr int kBytes = kOffBar + 256 + 1024;
 };
 
 // CTA = (query tile of 128 rows, head, sequence); loops over key tiles of 64 rows.
-// K/V tiles and the S / dP accumulators (TMEM) are double buffered: the next
-// tile's loads and S = Q K^T, dP = dO V^T run while this tile's dS is formed,
-// and dQ += dS K of this tile follows.  dS (bf16) is written over its dP stage
+// K/V tiles stream through a 3-stage ring (a tile's loads start two iterations ahead)
+// and the S / dP accumulators (TMEM) are double buffered: the next tile's
+// S = Q K^T, dP = dO V^T run while this tile's dS is formed, and dQ += dS K of
+// this tile follows.  dS (bf16) is written over its dP stage
 // and read by the MMA from tensor memory (thread = query row = A-operand row).
 //   TMEM columns: S[2] = [0, 128), dP / dS [2] = [128, 256), dQ = [256, 256 + DQ)
 template <int DQ, int DV, bool ROPE>
@@ -706,14 +727,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sK = smem + L::kOffK;
   uint8_t* sV = smem + L::kOffV;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  constexpr int NS = L::NS;
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [2]
-  uint64_t* kv_empty = bars + 3;   // [2]
-  uint64_t* sdp_full = bars + 5;   // [2]
-  uint64_t* sdp_empty = bars + 7;  // [2] S / dP(dS) stage free (commit after dQ read dS)
-  uint64_t* ds_ready = bars + 9;   // [2] one arrival per softmax warp, per dS stage
-  uint64_t* acc_done = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_full = bars + 1;    // [NS]
+  uint64_t* kv_empty = bars + 4;   // [NS]
+  uint64_t* sdp_full = bars + 7;   // [2]
+  uint64_t* sdp_empty = bars + 9;  // [2] S / dP(dS) stage free (commit after dQ read dS)
+  uint64_t* ds_ready = bars + 11;  // [2] one arrival per softmax warp, per dS stage
+  uint64_t* acc_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
 
   const int warp = warp_id(), lane = lane_id();
   const int nqt = p.S / kTile;
@@ -729,9 +751,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NS; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&sdp_full[i], 1);
       mbar_init(&sdp_empty[i], 1);
       mbar_init(&ds_ready[i], kBwdSoftmaxWarps);
@@ -758,8 +782,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int c = 0; c < VCH; ++c) tma_load_3d(sDO + c * kSubTile, &tmDO, q_full, c * 64, h, t0);
       for (int jj = 0; jj < n; ++jj) {
         const int kt0 = b * p.S + (j_lo + jj) * BK;
-        const int st = jj & 1;
-        const uint32_t u = jj >> 1;
+        const int st = jj % NS;
+        const uint32_t u = jj / NS;
         if (!mbar_wait(&kv_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) break;
         mbar_arrive_expect_tx(&kv_full[st], L::kK + L::kV);
         uint8_t* dK = sK + st * L::kK;
@@ -778,12 +802,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = mbar_wait(q_full, 0, p.status, STATUS_TIMEOUT_TMA_FULL);
       const uint32_t qa = smem_u32(sQ), da = smem_u32(sDO);
       auto issue_sdp = [&](int jj) -> bool {
-        const int st = jj & 1;
+        const int ks = jj % NS;                 // K / V ring stage
+        const int st = jj & 1;                  // S / dP tensor-memory stage
         const uint32_t u = jj >> 1;
-        if (!mbar_wait(&kv_full[st], u & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) return false;
+        if (!mbar_wait(&kv_full[ks], (jj / NS) & 1, p.status, STATUS_TIMEOUT_TMA_FULL)) return false;
         if (!mbar_wait(&sdp_empty[st], (u & 1) ^ 1, p.status, STATUS_TIMEOUT_TMEM_EMPTY)) return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(sK + st * L::kK), va = smem_u32(sV + st * L::kV);
+        const uint32_t ka = smem_u32(sK + ks * L::kK), va = smem_u32(sV + ks * L::kV);
 #pragma unroll
         for (int kk = 0; kk < DQ / 16; ++kk)
           tc_mma_f16(tS0 + st * 64, umma_desc_sw128(qa + (kk >> 2) * kSubTile + (kk & 3) * 32, 16, 1024),
@@ -802,12 +827,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!mbar_wait(&ds_ready[st], (jj >> 1) & 1, p.status, STATUS_TIMEOUT_TMEM_FULL)) { ok = false; break; }
         tc_fence_after();
         // dQ += dS K   (dS from tensor memory; K tile read as MN-major: d contiguous, 64-row sub-tiles)
-        const uint32_t ka = smem_u32(sK + st * L::kK);
+        const int ks = jj % NS;
+        const uint32_t ka = smem_u32(sK + ks * L::kK);
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk)
           tc_mma_f16_ts(tdQ, tdP0 + st * 64 + kk * 8, umma_desc_sw128(ka + kk * 2048, 8192, 1024), idesc_dq,
                         (jj > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&kv_empty[st]);
+        tc_commit(&kv_empty[ks]);
         tc_commit(&sdp_empty[st]);
       }
       tc_commit(acc_done);
