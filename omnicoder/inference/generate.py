@@ -155,6 +155,7 @@ class GenStats:
     steps: int = 0
     accepted_draft_tokens: int = 0
     proposed_draft_tokens: int = 0
+    early_exits: int = 0
     step_times_s: list = field(default_factory=list)
 
     @property
@@ -175,21 +176,41 @@ class GenStats:
 PREFILL_TOKENS = 32768   # tokens per prefill call (whole sequences; bounds the activation memory)
 
 
-def _prefill(model, ids: torch.Tensor, cache) -> torch.Tensor:
+def _prefill(model, ids: torch.Tensor, cache, return_hidden: bool = False):
     """Run the prompt through the model in chunks of whole sequences and return the
-    last-position logits [B, V].  With memory rows and a window, the tokens that left
-    the window are then summarised into the memory rows."""
+    last-position logits [B, V] (and final hidden states [B, D] with return_hidden).
+    With memory rows and a window, the tokens that left the window are then summarised
+    into the memory rows."""
     B, S = ids.shape
     step = max(1, PREFILL_TOKENS // max(1, S))
-    out = []
+    out, hid = [], []
     for b0 in range(0, B, step):
         b1 = min(B, b0 + step)
         view = cache.view(b0, b1) if (b0, b1) != (0, B) else cache
-        out.append(model.forward_cached(ids[b0:b1], view, prefill=True, last_only=True)[:, -1])
+        r = model.forward_cached(ids[b0:b1], view, prefill=True, last_only=True, return_hidden=return_hidden)
+        if return_hidden:
+            out.append(r[0][:, -1])
+            hid.append(r[1][:, -1])
+        else:
+            out.append(r[:, -1])
     cfg = model.cfg
     if getattr(cfg.attn, "mem_slots", 0) and cfg.attn.window:
         cache.compress_memory(cfg.attn.window)
-    return torch.cat(out) if len(out) > 1 else out[0]
+    logits = torch.cat(out) if len(out) > 1 else out[0]
+    if return_hidden:
+        return logits, (torch.cat(hid) if len(hid) > 1 else hid[0])
+    return logits
+
+
+@torch.no_grad()
+def prime_kv_with_features(model, feats: torch.Tensor, cache) -> torch.Tensor:
+    """Append feature vectors feats [B, P, D] (e.g. another modality's encoder output, or a
+    summary of text beyond the window) to the cache as if they were token embeddings, so the
+    following tokens attend to them (reference src/omnicoder/inference/generate.py:1381-1403,
+    :3193).  Returns the logits of the last primed position [B, V]."""
+    B, P, _ = feats.shape
+    ids = torch.zeros(B, P, dtype=torch.long, device=feats.device)
+    return model.forward_cached(ids, cache, embeds=feats)[:, -1]
 
 
 def _sync(t: torch.Tensor):
@@ -204,14 +225,34 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
              window_size: int = 0, return_stats: bool = False, eos_id: int | None = None, seed: int | None = None,
              max_len: int | None = None, cuda_graph: bool = True, repetition_penalty: float = 1.0,
              presence_penalty: float = 0.0, frequency_penalty: float = 0.0, logit_bias: dict | None = None,
-             penalty_window: int = 128):
+             penalty_window: int = 128,
+             # decode-time add-ons (omnicoder.inference.addons)
+             knn_cache=None, knn_k: int = 16, knn_lambda: float = 0.2, knn_write_every: int = 8,
+             retrieved_texts: list[str] | None = None, retrieval_bias_alpha: float = 0.0, encode_fn=None,
+             sfb: bool = False, sfb_alpha: float = 1.0, prompt_text: str | None = None,
+             dual_substrate: bool = True, dual_alpha: float = 1.0, dual_beta: float = 1.0,
+             adaptive_moe: bool = False, adaptive_top_k_min: int = 1, adaptive_top_k_max: int = 4,
+             adaptive_conf_floor: float = 0.3, adaptive_layer_ramp: bool = False, adaptive_layer_power: float = 1.0,
+             early_exit: bool = False, early_exit_entropy: float = 0.0, early_exit_mode: str = "entropy",
+             verify_threshold: float = 0.0, compress_kv_slots: int = 0, prefix_embeds: torch.Tensor | None = None):
     """Generate `max_new_tokens` tokens after `input_ids` [B, S] (or [S]).  Returns
     [B, S + max_new_tokens] (and GenStats with return_stats).  On CUDA the
     decode step is captured once as a CUDA graph (`cuda_graph=False` runs it
     eagerly).  Repetition / presence / frequency penalties over the last `penalty_window`
     tokens (0: the whole sequence) and `logit_bias` (LogitProcessor) apply on the plain decode
     path; speculative decoding refuses them (its acceptance test needs the unmodified target
-    distribution)."""
+    distribution).
+
+    Add-ons (omnicoder.inference.addons; plain decode path): kNN-LM blend (`knn_cache`,
+    `knn_k`, `knn_lambda`), retrieval bias (`retrieved_texts`, `retrieval_bias_alpha`,
+    `encode_fn`), structured factor bias (`sfb`, `sfb_alpha`, `prompt_text` or a tokenizer-bound
+    `encode_fn`), dual-substrate blend with the model's byte head when it has one, adaptive
+    expert count (`adaptive_moe` with the `adaptive_*` knobs; decodes eagerly).  Speculative
+    path: `early_exit` skips the draft on confident steps; `verify_threshold` > 0 with a target
+    that has a verifier head accepts draft tokens whose verifier probability reaches the
+    threshold (the reference's policy) instead of by rejection sampling.
+    `compress_kv_slots` sets the number of compressed memory rows; `prefix_embeds` [B, P, D]
+    primes the cache with feature vectors before the prompt."""
     model.eval()
     squeeze = input_ids.dim() == 1
     ids = input_ids[None] if squeeze else input_ids
@@ -220,23 +261,59 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
     cfg = model.cfg
     if window_size:
         cfg.attn.window = window_size
+    if compress_kv_slots:
+        cfg.attn.mem_slots = int(compress_kv_slots)
     kv_dtype = "int8" if kvq in ("int8", "u8") else "bf16"
-    L = max_len or (S + max_new_tokens + max(0, speculative_draft_len) + 2)
+    P = 0 if prefix_embeds is None else int(prefix_embeds.shape[1])
+    L = max_len or (P + S + max_new_tokens + max(0, speculative_draft_len) + 2)
     gen = None
     if seed is not None:
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
     stats = GenStats(prompt_tokens=B * S)
+    from .addons import DecodeAddons, adapt_moe_top_k, clear_moe_top_k, retrieval_vectors, sfb_token_bias
+    addons = DecodeAddons(knn_cache=knn_cache, knn_k=knn_k, knn_lambda=knn_lambda, knn_write_every=knn_write_every,
+                          dual_alpha=dual_alpha,
+                          dual_beta=dual_beta, dual=bool(dual_substrate) and getattr(model, "byte_head", None) is not None)
+    if retrieved_texts and retrieval_bias_alpha > 0:
+        if encode_fn is None:
+            raise ValueError("encode_fn is required when retrieval_bias_alpha > 0 and retrieved_texts are given")
+        addons.retrieval_vecs = retrieval_vectors(model, retrieved_texts, encode_fn)
+        addons.retrieval_alpha = float(retrieval_bias_alpha)
+    if sfb:
+        if encode_fn is None:
+            raise ValueError("sfb needs encode_fn (and prompt_text, or a tokenizer-bound encode_fn)")
+        text = prompt_text
+        if text is None:
+            tok_obj = getattr(encode_fn, "__self__", None)
+            text = tok_obj.decode(ids[0].tolist()) if tok_obj is not None and hasattr(tok_obj, "decode") else ""
+        if retrieved_texts:
+            text = "\n\n".join(retrieved_texts[:5]) + "\n\n" + text
+        addons.sfb_bias = sfb_token_bias(text, encode_fn, cfg.vocab_size, dev)
+        addons.sfb_alpha = float(sfb_alpha)
     if draft_model is not None and speculative_draft_len > 0:
-        if repetition_penalty != 1.0 or presence_penalty or frequency_penalty or logit_bias:
+        if repetition_penalty != 1.0 or presence_penalty or frequency_penalty or logit_bias or addons.active \
+                or adaptive_moe:
             raise ValueError("speculative decoding samples from the unmodified target distribution: "
-                             "penalties and logit_bias are not applied there")
+                             "penalties, logit_bias and the logit add-ons are not applied there")
         out = _speculative(model, draft_model, ids, max_new_tokens, speculative_draft_len, temperature, top_k, top_p,
-                           kv_dtype, L, gen, stats, eos_id)
+                           kv_dtype, L, gen, stats, eos_id, early_exit=(early_exit_mode, early_exit_entropy)
+                           if early_exit else None, verify_threshold=verify_threshold, prefix_embeds=prefix_embeds)
     else:
         cache = KVCache(cfg, B, L, dev, dtype=model.embed.dtype, kv_dtype=kv_dtype)
         t0 = time.perf_counter()
-        logits = _prefill(model, ids, cache)
+        if prefix_embeds is not None:
+            prime_kv_with_features(model, prefix_embeds.to(dev), cache)
+        hidden = None
+        if addons.needs_hidden:
+            logits, hidden = _prefill(model, ids, cache, return_hidden=True)
+        else:
+            logits = _prefill(model, ids, cache)
+        if addons.active:
+            logits = addons.apply(model, logits, hidden)
+        if adaptive_moe:
+            adapt_moe_top_k(model, logits, adaptive_top_k_min, adaptive_top_k_max, adaptive_conf_floor,
+                            adaptive_layer_ramp, adaptive_layer_power)
         proc = LogitProcessor(B, logits.shape[-1], dev, repetition_penalty, presence_penalty, frequency_penalty,
                               logit_bias, window=penalty_window)
         if proc.active:
@@ -249,13 +326,25 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         toks = [tok]
         done = torch.zeros(B, dtype=torch.bool, device=dev)
         step = None
-        if cuda_graph and dev.type == "cuda" and max_new_tokens > 2:
+        if cuda_graph and dev.type == "cuda" and max_new_tokens > 2 and not adaptive_moe:
             from .graphs import GraphedStep
-            step = GraphedStep(model, cache)
+            step = GraphedStep(model, cache, return_hidden=addons.needs_hidden)
         t1 = time.perf_counter()
         for _ in range(max_new_tokens - 1):
             ts = time.perf_counter()
-            logits = (step(tok[:, None]) if step is not None else model.forward_cached(tok[:, None], cache))[:, -1]
+            if step is not None:
+                logits = step(tok[:, None])[:, -1]
+                hidden = step.hidden[:, -1] if step.hidden is not None else None
+            elif addons.needs_hidden:
+                logits, hidden = model.forward_cached(tok[:, None], cache, return_hidden=True)
+                logits, hidden = logits[:, -1], hidden[:, -1]
+            else:
+                logits = model.forward_cached(tok[:, None], cache)[:, -1]
+            if addons.active:
+                logits = addons.apply(model, logits, hidden)
+            if adaptive_moe:
+                adapt_moe_top_k(model, logits, adaptive_top_k_min, adaptive_top_k_max, adaptive_conf_floor,
+                                adaptive_layer_ramp, adaptive_layer_power)
             tok = sample_next_token(proc(logits), temperature, top_k, top_p, gen)
             if proc.active:
                 proc.observe(tok)
@@ -270,23 +359,38 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         _sync(tok)
         stats.decode_s = time.perf_counter() - t1
         stats.new_tokens = B * (max_new_tokens - 1)
+        if adaptive_moe:
+            clear_moe_top_k(model)
         out = torch.cat([ids, torch.stack(toks, dim=1)], dim=1)
     out = out[0] if squeeze else out
     return (out, stats) if return_stats else out
 
 
-def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_dtype, L, gen, stats, eos_id):
+def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_dtype, L, gen, stats, eos_id,
+                 early_exit=None, verify_threshold: float = 0.0, prefix_embeds=None):
     """Draft proposes k tokens autoregressively; the target scores all k+1 positions
     in one forward; tokens are accepted left to right with probability
     min(1, p_target/p_draft) (always, when greedy and equal); the first rejection
     is replaced by a sample from normalize(max(0, p_target - p_draft)) and, if all
     k are accepted, a bonus token comes from the target's last position.  Both
-    caches are then rolled back per sequence to the accepted length."""
+    caches are then rolled back per sequence to the accepted length; every sequence
+    keeps its own accepted length.
+
+    verify_threshold > 0 with a target that has a verifier head: a draft token is accepted
+    while the verifier's probability of it reaches the threshold (reference
+    src/omnicoder/inference/generate.py:2925-3048); the next token then comes from the
+    target distribution at the first unaccepted position.
+    early_exit = (mode, threshold): after a confident step (omnicoder.inference.addons.confident)
+    the next step is a single target step without a draft (reference :2433-2467)."""
+    from .addons import confident
     B, S = ids.shape
     dev = ids.device
     tcache = KVCache(target.cfg, B, L, dev, dtype=target.embed.dtype, kv_dtype=kv_dtype)
     dcache = KVCache(draft.cfg, B, L, dev, dtype=draft.embed.dtype, kv_dtype="bf16")
+    use_verifier = verify_threshold > 0 and getattr(target, "verifier", None) is not None
     t0 = time.perf_counter()
+    if prefix_embeds is not None:                   # the draft has another width: only the target is primed
+        prime_kv_with_features(target, prefix_embeds.to(dev), tcache)
     if S > 1:
         target.forward_cached(ids[:, :-1], tcache, prefill=True, last_only=True)
         draft.forward_cached(ids[:, :-1], dcache, prefill=True, last_only=True)
@@ -296,8 +400,24 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
     produced = [[] for _ in range(B)]
     t1 = time.perf_counter()
     ar = torch.arange(B, device=dev)
+    skip_draft = False
     while min(len(p) for p in produced) < max_new:
         ts = time.perf_counter()
+        if skip_draft:
+            # early exit: one target step, the draft cache follows with the same token
+            tl = target.forward_cached(last[:, None], tcache)[:, -1]
+            draft.forward_cached(last[:, None], dcache)
+            pt = sampling_probs(tl, temperature, top_k, top_p)
+            extra = pt.argmax(-1) if temperature <= 0 else torch.multinomial(pt, 1, generator=gen).squeeze(1)
+            for b, e in enumerate(extra.tolist()):
+                produced[b].append(e)
+            stats.steps += 1
+            stats.early_exits += 1
+            skip_draft = confident(tl, *early_exit)
+            last = extra
+            _sync(last)
+            stats.step_times_s.append(time.perf_counter() - ts)
+            continue
         base_t = tcache.lengths.clone()
         base_d = dcache.lengths.clone()
         cur = last
@@ -310,22 +430,33 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
             d_prob.append(pd)
             cur = nxt
         d_tok_t = torch.stack(d_tok, dim=1)                          # [B, k]
-        tl = target.forward_cached(torch.cat([last[:, None], d_tok_t], dim=1), tcache)   # [B, k+1, V]
+        seq_in = torch.cat([last[:, None], d_tok_t], dim=1)
+        if use_verifier:
+            tl, th = target.forward_cached(seq_in, tcache, return_hidden=True)      # [B, k+1, V], [B, k+1, D]
+        else:
+            tl = target.forward_cached(seq_in, tcache)
         pt = sampling_probs(tl, temperature, top_k, top_p)           # [B, k+1, V]
         pd_all = torch.stack(d_prob, dim=1)                          # [B, k, V]
-        pt_d = pt[:, :k].gather(-1, d_tok_t[..., None]).squeeze(-1)
-        pd_d = pd_all.gather(-1, d_tok_t[..., None]).squeeze(-1)
-        if temperature <= 0:
-            acc = pt_d > 0.5
+        if use_verifier:
+            vl = (th[:, :k].to(target.verifier.dtype) @ target.verifier.t()).float()
+            v_d = torch.softmax(vl, -1).gather(-1, d_tok_t[..., None]).squeeze(-1)
+            acc = v_d >= verify_threshold
         else:
-            u = torch.rand(B, k, device=dev, generator=gen)
-            acc = u < torch.clamp(pt_d / pd_d.clamp_min(1e-20), max=1.0)
+            pt_d = pt[:, :k].gather(-1, d_tok_t[..., None]).squeeze(-1)
+            pd_d = pd_all.gather(-1, d_tok_t[..., None]).squeeze(-1)
+            if temperature <= 0:
+                acc = pt_d > 0.5
+            else:
+                u = torch.rand(B, k, device=dev, generator=gen)
+                acc = u < torch.clamp(pt_d / pd_d.clamp_min(1e-20), max=1.0)
         n_acc = torch.cumprod(acc.int(), dim=1).sum(1)               # accepted prefix length [B]
         # correction / bonus token at position n_acc
         p_next = pt[ar, n_acc]                                       # [B, V]
-        resid = torch.clamp(p_next - torch.cat([pd_all, torch.zeros_like(pd_all[:, :1])], 1)[ar, n_acc], min=0)
-        use_resid = n_acc < k
-        q = torch.where(use_resid[:, None], resid, p_next)
+        if use_verifier:
+            q = p_next
+        else:
+            resid = torch.clamp(p_next - torch.cat([pd_all, torch.zeros_like(pd_all[:, :1])], 1)[ar, n_acc], min=0)
+            q = torch.where((n_acc < k)[:, None], resid, p_next)
         q = q / q.sum(-1, keepdim=True).clamp_min(1e-20)
         extra = q.argmax(-1) if temperature <= 0 else torch.multinomial(q, 1, generator=gen).squeeze(1)
         # draft cache lacks the k-th draft token when everything was accepted: catch up
@@ -340,6 +471,8 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
         stats.accepted_draft_tokens += int(sum(n_list))
         stats.proposed_draft_tokens += B * k
         stats.steps += 1
+        if early_exit is not None:
+            skip_draft = confident(tl[ar, n_acc], *early_exit)
         last = extra
         _sync(last)
         stats.step_times_s.append(time.perf_counter() - ts)
@@ -378,6 +511,28 @@ def main(argv=None):
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--penalty_window", type=int, default=128, help="tokens the penalties look back over (0: all)")
+    ap.add_argument("--eos_id", type=int, default=None)
+    ap.add_argument("--no_cuda_graph", action="store_true", help="decode eagerly instead of replaying a CUDA graph")
+    # add-ons
+    ap.add_argument("--knn_cache", default=None, help="saved kNN-LM cache (KNNCache.save) to blend with")
+    ap.add_argument("--knn_k", type=int, default=16)
+    ap.add_argument("--knn_lambda", type=float, default=0.2)
+    ap.add_argument("--retrieve_texts", default=None, help="file with one retrieved passage per line")
+    ap.add_argument("--retrieval_bias_alpha", type=float, default=0.0)
+    ap.add_argument("--sfb", action="store_true", help="structured factor bias from the factorised prompt")
+    ap.add_argument("--sfb_alpha", type=float, default=1.0)
+    ap.add_argument("--adaptive_moe", action="store_true", help="confidence-driven routed experts per token")
+    ap.add_argument("--adaptive_top_k_min", type=int, default=1)
+    ap.add_argument("--adaptive_top_k_max", type=int, default=4)
+    ap.add_argument("--adaptive_conf_floor", type=float, default=0.3)
+    ap.add_argument("--adaptive_layer_ramp", action="store_true")
+    ap.add_argument("--early_exit", action="store_true", help="skip the speculative draft on confident steps")
+    ap.add_argument("--early_exit_entropy", type=float, default=1.0)
+    ap.add_argument("--early_exit_mode", default="entropy", choices=["entropy", "delta"])
+    ap.add_argument("--verify_threshold", type=float, default=0.0,
+                    help="speculative acceptance by the target's verifier head (0: rejection sampling)")
+    ap.add_argument("--compress_kv_slots", type=int, default=0, help="compressed memory rows of the cache")
     a = ap.parse_args(argv)
     cfg = get_preset(a.preset)
     model = build_model(cfg, device=a.device)
@@ -390,12 +545,28 @@ def main(argv=None):
         draft = build_model(get_preset(a.draft_preset), device=a.device)
         if a.draft_ckpt:
             maybe_load_checkpoint(draft, a.draft_ckpt)
+    knn = None
+    if a.knn_cache:
+        from .knn_cache import KNNCache
+        knn = KNNCache.load(a.knn_cache)
+    texts = None
+    if a.retrieve_texts:
+        with open(a.retrieve_texts) as f:
+            texts = [ln.strip() for ln in f if ln.strip()]
     out, st = generate(model, ids, a.max_new_tokens, a.temperature, a.top_k, a.top_p, draft_model=draft,
                        repetition_penalty=a.repetition_penalty, presence_penalty=a.presence_penalty,
                        frequency_penalty=a.frequency_penalty,
                        logit_bias=load_logit_bias(a.logit_bias_file) if a.logit_bias_file else None,
                        speculative_draft_len=a.speculative_draft_len, kvq=a.kvq, window_size=a.window_size,
-                       return_stats=True, seed=a.seed)
+                       return_stats=True, seed=a.seed, eos_id=a.eos_id, cuda_graph=not a.no_cuda_graph,
+                       penalty_window=a.penalty_window, knn_cache=knn, knn_k=a.knn_k, knn_lambda=a.knn_lambda,
+                       retrieved_texts=texts, retrieval_bias_alpha=a.retrieval_bias_alpha, encode_fn=tok.encode,
+                       sfb=a.sfb, sfb_alpha=a.sfb_alpha, prompt_text=a.prompt, adaptive_moe=a.adaptive_moe,
+                       adaptive_top_k_min=a.adaptive_top_k_min, adaptive_top_k_max=a.adaptive_top_k_max,
+                       adaptive_conf_floor=a.adaptive_conf_floor, adaptive_layer_ramp=a.adaptive_layer_ramp,
+                       early_exit=a.early_exit, early_exit_entropy=a.early_exit_entropy,
+                       early_exit_mode=a.early_exit_mode, verify_threshold=a.verify_threshold,
+                       compress_kv_slots=a.compress_kv_slots)
     text = tok.decode(out[0, ids.shape[1]:].tolist())
     if a.json:
         print(json.dumps({"text": text, "stats": st.as_dict()}))

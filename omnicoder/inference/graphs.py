@@ -21,7 +21,7 @@ import torch
 
 
 class GraphedStep:
-    def __init__(self, model, cache, tokens_per_step: int = 1, warmup: int = 2):
+    def __init__(self, model, cache, tokens_per_step: int = 1, warmup: int = 2, return_hidden: bool = False):
         if not cache.device.type == "cuda":
             raise ValueError("GraphedStep needs a CUDA cache")
         self.model, self.cache = model, cache
@@ -31,17 +31,20 @@ class GraphedStep:
         side.wait_stream(torch.cuda.current_stream(cache.device))
         with torch.cuda.stream(side), torch.no_grad():
             for _ in range(warmup):          # first-call setup (attributes, tensor maps) outside the capture
-                model.forward_cached(self.ids, cache)
+                model.forward_cached(self.ids, cache, return_hidden=return_hidden)
                 cache.rollback(saved)
         torch.cuda.current_stream(cache.device).wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
+        self.hidden = None
         with torch.cuda.graph(self.graph), torch.no_grad():
-            self.logits = model.forward_cached(self.ids, cache)
+            out = model.forward_cached(self.ids, cache, return_hidden=return_hidden)
+        self.logits, self.hidden = out if return_hidden else (out, None)
         # capture records without executing: the cache is as it was before the warm-up
         cache.rollback(saved)
 
     def __call__(self, ids: torch.Tensor) -> torch.Tensor:
-        """ids [B, tokens_per_step] -> logits [B, tokens_per_step, V] (a view of the static output)."""
+        """ids [B, tokens_per_step] -> logits [B, tokens_per_step, V] (a view of the static output;
+        the final hidden states, when captured, are in `self.hidden`)."""
         self.ids.copy_(ids)
         self.graph.replay()
         return self.logits

@@ -267,19 +267,21 @@ class MoEFFN(nn.Module):
             self.w2 = nn.Parameter(self.w2.data[lo:hi].clone())
         self.shared = DenseFFN(D, m.ffn_dim * m.n_shared_experts, cfg.init_std) if m.n_shared_experts > 0 else None
         self.aux_grad_scale = 1.0
+        self.top_k_override: int | None = None   # decode-time adaptive expert count (inference add-on)
 
     def forward(self, y, h):
         m = self.cfg.moe
+        k = self.top_k_override or m.top_k
         T = y.shape[0]
         base = self.shared(y, h)[0] if self.shared is not None else h
         if self.ep is not None:
             from ..parallel.expert import ep_moe_ffn
             world = self.ep.world
-            out, aux = ep_moe_ffn(y, self.router, self.w13, self.w2, m.top_k, self.ep.ep, m.capacity(T * world),
+            out, aux = ep_moe_ffn(y, self.router, self.w13, self.w2, k, self.ep.ep, m.capacity(T * world),
                                   m.renorm_topk, m.aux_loss_alpha, m.z_loss_beta, add=base,
                                   aux_grad_scale=self.aux_grad_scale)
             return out, aux
-        out, aux = moe_ffn(y, self.router, self.w13, self.w2, m.top_k, m.capacity(T), m.renorm_topk,
+        out, aux = moe_ffn(y, self.router, self.w13, self.w2, k, m.capacity(T), m.renorm_topk,
                            m.aux_loss_alpha, m.z_loss_beta, add=base, aux_grad_scale=self.aux_grad_scale)
         return out, aux
 
@@ -379,22 +381,30 @@ class OmniLM(nn.Module):
 
     # ------------------------------------------------------------------
     @torch.no_grad()
-    def forward_cached(self, ids: torch.Tensor, cache, prefill: bool = False, last_only: bool = False):
+    def forward_cached(self, ids: torch.Tensor, cache, prefill: bool = False, last_only: bool = False,
+                       return_hidden: bool = False, embeds: torch.Tensor | None = None):
         """Process new tokens ids [B, Tn] against `cache` (appending them) and return
         logits [B, Tn, V] (or [B, 1, V] with last_only).  `prefill=True` asserts the
-        cache is empty, which lets long prompts use the flash-attention kernels."""
+        cache is empty, which lets long prompts use the flash-attention kernels.
+        `return_hidden`: also return the final normalised hidden states of the same
+        positions ([B, Tn or 1, D]).  `embeds` [B, Tn, D]: input vectors used in place of
+        the token embeddings (priming the cache with features, e.g. another modality's)."""
         B, Tn = ids.shape
         if ids.is_cuda:
             self.rope.to(ids.device)
         pos = cache.positions(Tn)
-        h = embedding(ids.reshape(-1), self.embed)
+        if embeds is not None:
+            h = embeds.reshape(B * Tn, -1).to(self.embed.dtype).contiguous()
+        else:
+            h = embedding(ids.reshape(-1), self.embed)
         for i, blk in enumerate(self.blocks):
             h = blk.forward_cached(h, self.rope, pos, cache, i, prefill)
         cache.advance(Tn)
         y = self.norm_f(h).view(B, Tn, -1)
         if last_only:
             y = y[:, -1:]
-        return linear(y.reshape(-1, y.shape[-1]), self.head_weight).float().view(B, y.shape[1], -1)
+        logits = linear(y.reshape(-1, y.shape[-1]), self.head_weight).float().view(B, y.shape[1], -1)
+        return (logits, y) if return_hidden else logits
 
     def prepare_inference(self):
         for b in self.blocks:

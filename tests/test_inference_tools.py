@@ -201,3 +201,111 @@ def test_load_logit_bias(tmp_path):
     f = tmp_path / "bias.json"
     f.write_text(json.dumps({"7": -5, "9": 2.5}))
     assert load_logit_bias(str(f)) == {7: -5.0, 9: 2.5}
+
+
+# ---- decode-time add-ons of generate() ----------------------------------------------------
+def test_addon_knn_blend_formula_and_generate():
+    from omnicoder.inference.addons import DecodeAddons
+    from omnicoder.inference.generate import generate
+    from omnicoder.inference.knn_cache import KNNCache
+    cfg, m = _tiny()
+    kc = KNNCache(cfg.d_model, k=4)
+    key = torch.randn(1, cfg.d_model)
+    kc.add(key, torch.tensor([42]))
+    ad = DecodeAddons(knn_cache=kc, knn_lambda=0.5, knn_write_every=0)
+    logits = torch.randn(1, cfg.vocab_size)
+    got = ad.apply(m, logits, key + 0.01)
+    want = torch.log(0.5 * torch.softmax(logits, -1) + 0.5 * torch.nn.functional.one_hot(
+        torch.tensor([42]), cfg.vocab_size).float())
+    torch.testing.assert_close(got, want.clamp_min(torch.log(torch.tensor(1e-8))), rtol=1e-5, atol=1e-5)
+    # through generate(): a near-certain kNN distribution forces its token; writes fill the cache
+    kc2 = KNNCache(cfg.d_model, k=1)
+    kc2.add(torch.zeros(1, cfg.d_model), torch.tensor([7]))
+    out = generate(m, torch.tensor([[3, 4, 5]]), 6, temperature=0.0, knn_cache=kc2, knn_lambda=0.999,
+                   knn_write_every=0)
+    assert (out[0, 3:] == 7).all()
+    kc3 = KNNCache(cfg.d_model)
+    generate(m, torch.tensor([[3, 4, 5]]), 10, temperature=0.0, knn_cache=kc3, knn_lambda=0.2, knn_write_every=4)
+    assert len(kc3) == 3                              # steps 0, 4, 8 of 10 (prefill + 9 decode steps)
+
+
+def test_addon_retrieval_bias_matches_definition():
+    from omnicoder.inference.addons import DecodeAddons, retrieval_vectors
+    from omnicoder.inference.generate import generate
+    cfg, m = _tiny()
+    enc = lambda t: [ord(c) % cfg.vocab_size for c in t]
+    r = retrieval_vectors(m, ["abc", "hello world"], enc)
+    assert r.shape == (2, cfg.d_model)
+    torch.testing.assert_close(r[0], m.embed[torch.tensor(enc("abc"))].mean(0))
+    h = torch.randn(2, cfg.d_model)
+    logits = torch.randn(2, cfg.vocab_size)
+    got = DecodeAddons(retrieval_vecs=r, retrieval_alpha=0.7).apply(m, logits, h)
+    w = torch.softmax(h @ r.t() / cfg.d_model ** 0.5, -1)
+    torch.testing.assert_close(got, logits + 0.7 * ((w @ r) @ m.head_weight.t()), rtol=1e-5, atol=1e-5)
+    out = generate(m, torch.tensor([[3, 4, 5]]), 4, temperature=0.0, retrieved_texts=["abc"],
+                   retrieval_bias_alpha=0.5, encode_fn=enc)
+    assert out.shape == (1, 7)
+    with pytest.raises(ValueError):
+        generate(m, torch.tensor([[3, 4, 5]]), 2, retrieved_texts=["abc"], retrieval_bias_alpha=0.5)
+
+
+def test_addon_sfb_bias_prefers_goal_tokens():
+    from omnicoder.inference.addons import sfb_token_bias
+    from omnicoder.inference.generate import generate
+    cfg, m = _tiny()
+    enc = lambda t: [ord(c) % cfg.vocab_size for c in t]
+    b = sfb_token_bias("1. compute xyz\n2. write code qq", enc, cfg.vocab_size, "cpu")
+    goal_tok = set(enc("compute xyz") + enc("write code qq"))
+    inside = b[torch.tensor(sorted(goal_tok))].min()
+    outside = b[torch.tensor([t for t in range(cfg.vocab_size) if t not in goal_tok])].max()
+    assert inside > outside
+    out = generate(m, torch.tensor([[3, 4, 5]]), 4, temperature=0.0, sfb=True, sfb_alpha=50.0,
+                   prompt_text="zzzz", encode_fn=enc)
+    assert set(out[0, 3:].tolist()) <= {ord("z") % cfg.vocab_size}
+
+
+def test_addon_adaptive_moe_top_k():
+    from omnicoder.inference.addons import adapt_moe_top_k, clear_moe_top_k
+    from omnicoder.inference.generate import generate
+    cfg, m = _tiny()
+    flat = torch.zeros(1, cfg.vocab_size)                       # uniform: not confident
+    assert adapt_moe_top_k(m, flat, 1, 3, 0.3) == 3
+    assert all(b.ffn.top_k_override == 3 for b in m.blocks)
+    peaked = torch.full((1, cfg.vocab_size), -1e4)
+    peaked[0, 5] = 0.0
+    assert adapt_moe_top_k(m, peaked, 1, 3, 0.3, layer_ramp=True) == 1
+    clear_moe_top_k(m)
+    assert all(b.ffn.top_k_override is None for b in m.blocks)
+    out = generate(m, torch.tensor([[3, 4, 5]]), 5, temperature=0.0, adaptive_moe=True, adaptive_top_k_min=1,
+                   adaptive_top_k_max=3)
+    assert out.shape == (1, 8) and all(b.ffn.top_k_override is None for b in m.blocks)
+
+
+def test_prefix_embeds_equal_prepended_tokens():
+    """Priming the cache with the embedding vectors of some tokens is the same as prepending them."""
+    from omnicoder.inference.generate import generate
+    cfg, m = _tiny()
+    pre = torch.tensor([[11, 12, 13, 14]])
+    prompt = torch.tensor([[3, 4, 5]])
+    a = generate(m, torch.cat([pre, prompt], 1), 5, temperature=0.0)[:, pre.shape[1]:]
+    b = generate(m, prompt, 5, temperature=0.0, prefix_embeds=m.embed[pre])
+    assert torch.equal(a, b)
+
+
+def test_speculative_verifier_threshold_and_early_exit():
+    from omnicoder.inference.generate import generate
+    cfg = ModelConfig(name="t", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=128,
+                      verifier_head=True, attn=AttentionConfig(kind="gqa", n_kv_heads=2))
+    tgt = build_model(cfg, device="cpu", seed=0).eval()
+    dcfg = ModelConfig(name="d", vocab_size=300, d_model=32, n_layers=1, n_heads=2, ffn_dim=64, max_seq_len=128)
+    drf = build_model(dcfg, device="cpu", seed=1).eval()
+    prompt = torch.tensor([[3, 4, 5], [6, 7, 8]])
+    plain = generate(tgt, prompt, 8, temperature=0.0)
+    # an unreachable verifier threshold accepts nothing: every token comes from the target
+    out, st = generate(tgt, prompt, 8, temperature=0.0, draft_model=drf, speculative_draft_len=3,
+                       verify_threshold=1.5, return_stats=True)
+    assert st.accepted_draft_tokens == 0 and torch.equal(out, plain)
+    # a threshold every step meets: after the first step every step skips the draft
+    out2, st2 = generate(tgt, prompt, 8, temperature=0.0, draft_model=drf, speculative_draft_len=3,
+                         early_exit=True, early_exit_entropy=1e9, return_stats=True)
+    assert torch.equal(out2, plain) and st2.early_exits == st2.steps - 1
