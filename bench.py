@@ -149,12 +149,14 @@ def reference_arm(args):
 
 # ----------------------------------------------------------------------------
 def decode_phase(args, dev, world, rank, barrier):
-    """Batch-64 long-context decode (the metric's second half): every GPU serves its own
-    64 sequences with a full replica of the long-context MoE model (24L d2048 MLA, 32
-    experts top-4, window 4096 + 64 memory rows, int8 KV), 8192-token random prompts,
-    greedy generation.  Device-timed: the decode steps (CUDA graphs), max over ranks.
-    End to end: the public generate() call, prompts copied from pinned host memory and
-    the generated ids read back, timed around the whole call."""
+    """Batch-64 long-context decode (the metric's second half) of the long-context MoE model
+    (24L d2048 MLA, 32 experts top-4, window 4096 + 64 memory rows, int8 KV), 8192-token
+    random prompts, greedy generation.  One GPU: the whole model.  N GPUs: expert parallel
+    (each rank holds 32/N of every layer's experts; tokens reach their experts through the
+    device-side peer-memory exchange) and every GPU serves its own 64 sequences with its own
+    KV cache.  Device-timed: the decode steps (CUDA graphs), max over ranks.  End to end: the
+    public generate() call, prompts copied from pinned host memory and the generated ids read
+    back, timed around the whole call."""
     import torch
     import torch.distributed as dist
 
@@ -163,13 +165,23 @@ def decode_phase(args, dev, world, rank, barrier):
     from omnicoder.inference.generate import generate
     from omnicoder.models.lm import build_model
 
-    res = run(batch=64, prompt=8192, gen=args.decode_gen, kv="int8", seed=rank, device=dev)
+    par = None
+    if world > 1:
+        from omnicoder.parallel.expert_data import ExpertDataParallel
+        c = get_preset("longctx_moe")
+        # inference slabs are shared by the layers: sized for the largest call (4 prompts of prefill)
+        T = 4 * 8192
+        El = c.moe.n_experts // world
+        seg = max(128, (-(-2 * world * T * c.moe.top_k // c.moe.n_experts) + 127) // 128 * 128)
+        R = El * seg
+        par = ExpertDataParallel(dist.group.WORLD, arena_bytes=2 * R * c.d_model * 2 + R * 16 + (64 << 20))
+    res = run(batch=64, prompt=8192, gen=args.decode_gen, kv="int8", seed=rank, device=dev, parallel=par)
     dec_s = (res["decode_steps"] and 64 * (args.decode_gen - 1) / res["decode_tokens_per_s"])
     pre_s = res["prefill_s"]
     torch.cuda.empty_cache()
     # ---- end to end through generate() ------------------------------------------------------
     cfg = get_preset("longctx_moe")
-    model = build_model(cfg, device=dev, seed=rank).eval().prepare_inference()
+    model = build_model(cfg, device=dev, seed=0 if par is not None else rank, ep=par).eval().prepare_inference()
     g = torch.Generator().manual_seed(rank + 100)
     prompts = torch.randint(0, cfg.vocab_size, (64, 8192), generator=g).pin_memory()
     barrier()
@@ -196,7 +208,9 @@ def decode_phase(args, dev, world, rank, barrier):
         "unit": "tokens/s", "per_gpu_batch": 64, "prompt": 8192, "gen": args.decode_gen, "kv": "int8",
         "window": 4096, "memory_rows": res["memory_rows"], "p50_tpot_ms": res["p50_tpot_ms"],
         "prefill_tokens_per_s": world * 64 * 8192 / pre_s, "cuda_graphs": True,
-        "parallelism": f"{world} replica(s), one per GPU (13 GB of weights each)",
+        "parallelism": (f"ep{world}: each GPU holds {32 // world} of the 32 experts of every layer and serves its "
+                        f"own 64 sequences" if world > 1 else "one GPU, whole model (13 GB of weights)"),
+        "expert_parallel": world,
         "model": res["model"], "data": "synthetic (uniform random prompts, random-init N(0,0.02))",
         "e2e": {"value": world * 64 * args.decode_gen / e2e_s, "unit": "generated tokens/s (prefill + decode)",
                 "s": e2e_s, "h2d_bytes_per_step": prompts.numel() * prompts.element_size(),

@@ -27,15 +27,20 @@ from omnicoder.ops import _ext
 
 
 def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, gen=512, kv="int8", spec=0,
-        prefill_chunk=4, layers=0, graphs=True, seed=0, device=None, profile_steps=0):
-    """One long-context batched generation; returns the result dict (device-timed with CUDA events)."""
+        prefill_chunk=4, layers=0, graphs=True, seed=0, device=None, profile_steps=0, parallel=None):
+    """One long-context batched generation; returns the result dict (device-timed with CUDA events).
+    `parallel` (omnicoder.parallel.expert_data.ExpertDataParallel): the routed experts are sharded
+    over its ranks (expert parallel); every rank serves its own `batch` sequences with its own KV
+    cache and all ranks run this function together."""
     dev = device or torch.device("cuda")
     _ext.load()
     cfg = get_preset(preset)
     if layers:
         cfg.n_layers = layers
     cfg.max_seq_len = max(cfg.max_seq_len, prompt + gen + spec + 1)
-    model = build_model(cfg, device=dev, seed=seed).eval().prepare_inference()
+    # expert parallel: every rank builds the same model (its slice of the experts); prompts differ
+    model = build_model(cfg, device=dev, seed=0 if parallel is not None else seed,
+                        ep=parallel).eval().prepare_inference()
     draft = None
     if spec > 0:
         dcfg = get_preset(draft_preset)
@@ -67,6 +72,8 @@ def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, ge
     prefill_s = e0.elapsed_time(e1) / 1000.0
     # ---- decode: the remaining gen - 1 tokens ---------------------------------------
     step_ms, produced, accepted, proposed = [], 1, 0, 0
+    per_seq = torch.ones(batch, dtype=torch.long, device=dev)       # tokens produced per sequence
+    total_new = 0
     fwd_t = lambda ids: model.forward_cached(ids, cache)
     fwd_d = (lambda ids: draft.forward_cached(ids, dcache)) if draft is not None else None
     if graphs:
@@ -75,12 +82,14 @@ def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, ge
         if draft is not None:
             fwd_d = GraphedStep(draft, dcache, 1)
     with torch.no_grad():
+        ar = torch.arange(batch, device=dev)
         while produced < gen:
             s0, s1 = ev(), ev()
             s0.record()
             if draft is None:
                 last = fwd_t(last[:, None])[:, -1].argmax(-1)
                 n_new = 1
+                total_new += batch
             else:
                 base_t, base_d = cache.lengths.clone(), dcache.lengths.clone()
                 cur, props = last, []
@@ -90,16 +99,19 @@ def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, ge
                 props = torch.stack(props, 1)                                    # [B, k] proposals
                 tgt = fwd_t(torch.cat([last[:, None], props], 1)).argmax(-1)  # [B, k+1]
                 n_acc = torch.cumprod((tgt[:, :spec] == props).int(), 1).sum(1)
-                # lock-step batch: keep the prefix every sequence accepted, then the target's token
-                m = int(n_acc.min())
-                if m == spec:
-                    fwd_d(props[:, -1:])
-                cache.rollback(base_t + m + 1)
-                dcache.rollback(base_d + m + 1)
-                last = tgt[:, m]
+                # every sequence keeps its own accepted prefix and the target's next token; both
+                # caches roll back per sequence (the draft first appends its last proposal, which
+                # only fully accepted sequences keep)
+                fwd_d(props[:, -1:])
+                cache.rollback(base_t + n_acc + 1)
+                dcache.rollback(base_d + n_acc + 1)
+                last = tgt[ar, n_acc]
+                gained = torch.minimum(n_acc + 1, (gen - per_seq).clamp_min(0))
+                per_seq += n_acc + 1
                 accepted += int(n_acc.sum())
                 proposed += batch * spec
-                n_new = m + 1
+                total_new += int(gained.sum())
+                n_new = int(per_seq.min()) - produced
             s1.record()
             s1.synchronize()
             step_ms.append(s0.elapsed_time(s1))
@@ -113,11 +125,13 @@ def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, ge
                  f"top-{cfg.moe.top_k}, window {cfg.attn.window} + {cfg.attn.mem_slots} memory rows",
         "batch": batch, "prompt": prompt, "gen": gen, "kv": kv, "spec_tokens": spec,
         "prefill_tokens_per_s": batch * prompt / prefill_s, "prefill_s": prefill_s,
-        "decode_tokens_per_s": batch * (produced - 1) / decode_s, "decode_steps": len(step_ms),
+        "decode_tokens_per_s": total_new / decode_s, "decode_steps": len(step_ms),
         "p50_step_ms": statistics.median(step_ms),
-        "p50_tpot_ms": statistics.median(step_ms) * len(step_ms) / max(1, produced - 1),
+        "p50_tpot_ms": statistics.median(step_ms) * len(step_ms) * batch / max(1, total_new),
+        "expert_parallel": parallel.world if parallel is not None else 1,
         "memory_rows": n_mem, "kv_cache_gb": cache.nbytes() / 1e9,
         "draft_acceptance": (accepted / proposed) if proposed else None, "cuda_graphs": graphs,
+        "speculative_acceptance": "per sequence (own accepted prefix and cache rollback)" if spec else None,
         "decode_kernel_breakdown_ms_per_step": breakdown,
         "data": "synthetic (uniform random prompts, random-init N(0,0.02) weights)", "dtype": "bf16 weights",
     }

@@ -115,10 +115,8 @@ class EPContext:
         self.arena = None
         self._arena_bytes = arena_bytes
         self.stats = {"host_syncs": 0}
-        self._slots: list = []           # device layout: per MoE call of a step (fixed slabs)
+        self._plans: dict = {}           # device layout, per (tokens per rank, training?): fixed slabs
         self._cursor = 0
-        self._shared = None              # device layout: backward slabs shared by all layers
-        self._tokens = None              # tokens per rank (must be the same on every rank)
         self._dropped = None
         # id(bf16 expert weight) -> (e4m3 weight, fp32 128x128 block scales): when both expert
         # weights of a layer are present, its forward expert GEMMs run in block-scaled fp8
@@ -167,33 +165,41 @@ class EPContext:
         bal = math.ceil(self.buffer_factor * self.world * T * k / E)
         return max(128, (bal + 127) // 128 * 128)
 
-    def slot(self, T: int, k: int, E: int, El: int, D: int, capacity: int) -> "_Slot":
-        """Slabs of the next MoE layer of this step (allocated on the first step; every
-        rank allocates the same sizes in the same order)."""
-        if self._tokens is None:
+    def slot(self, T: int, k: int, E: int, El: int, D: int, capacity: int, train: bool):
+        """(slabs of the next MoE layer, shared slabs) for T tokens per rank.  With autograd
+        recording, every MoE layer of a step has its own slabs (its forward's slabs are read by
+        its backward) and the cursor advances; without (inference), one set serves every layer
+        (each layer's barriers order the reuse).  Slabs are allocated on first use; every rank
+        allocates the same sizes in the same order, and every rank must pass the same T (checked
+        once per T with one collective).  `train` must be decided outside autograd.Function.forward,
+        where grad mode is always off."""
+        key = (T, train)
+        plan = self._plans.get(key)
+        if plan is None:
             t = torch.tensor([T], device=self.device)
             mx, mn = t.clone(), t.clone()
             dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=self.group)
             dist.all_reduce(mn, op=dist.ReduceOp.MIN, group=self.group)
             if int(mx.item()) != int(mn.item()):
                 raise ValueError("the device expert-parallel layout needs the same token count on every rank")
-            self._tokens = T
-            self._dropped = torch.zeros(1, dtype=torch.int32, device=self.device)
-        elif T != self._tokens:
-            raise ValueError(f"device expert-parallel layout was set up for {self._tokens} tokens per rank, got {T}")
+            if self._dropped is None:
+                self._dropped = torch.zeros(1, dtype=torch.int32, device=self.device)
+            plan = self._plans[key] = {"slots": [], "shared": None}
         arena = self.ensure_arena()
         cap = self.seg_cap(T, k, E, capacity)
         R = El * cap
         N = self.world
-        if self._shared is None:
-            self._shared = _Shared(arena, N, R, D, T * k, E)
-        if self._cursor == len(self._slots):
-            self._slots.append(_Slot(arena, N, R, D, E, El, cap, self.device))
-        sl = self._slots[self._cursor]
+        if plan["shared"] is None:
+            plan["shared"] = _Shared(arena, N, R, D, T * k, E, backward=train)
+        i = self._cursor if train else 0
+        if i == len(plan["slots"]):
+            plan["slots"].append(_Slot(arena, N, R, D, E, El, cap, self.device))
+        sl = plan["slots"][i]
         if (sl.R, sl.D, sl.E, sl.cap) != (R, D, E, cap):
             raise ValueError("MoE layers of one step changed shape between steps")
-        self._cursor += 1
-        return sl
+        if train:
+            self._cursor += 1
+        return sl, plan["shared"]
 
     def all_gather_counts(self, counts: torch.Tensor) -> np.ndarray:
         """[E] int32 per rank -> host [N, E] (one small collective + one host sync)."""
@@ -218,14 +224,17 @@ class _Slot:
 
 
 class _Shared:
-    """Backward slabs shared by every MoE layer (device layout): output gradients pushed to
-    the owners, input gradients pulled back, routing-weight gradients, the count board."""
+    """Slabs shared by every MoE layer (device layout): the count board and, when training,
+    the backward's output gradients pushed to the owners, input gradients pulled back and
+    routing-weight gradients."""
 
-    def __init__(self, arena, N, R, D, pairs, E):
-        self.dy = arena.alloc([R * D * 2] * N)
-        self.dx = arena.alloc([R * D * 2] * N)
-        self.dw = arena.alloc([pairs * 4] * N)
+    def __init__(self, arena, N, R, D, pairs, E, backward: bool = True):
         self.board = arena.alloc([N * E * 4] * N)
+        self.dy = self.dx = self.dw = None
+        if backward:
+            self.dy = arena.alloc([R * D * 2] * N)
+            self.dx = arena.alloc([R * D * 2] * N)
+            self.dw = arena.alloc([pairs * 4] * N)
         self.pairs = [pairs] * N
 
 
@@ -350,7 +359,7 @@ class _EPMoEDev(torch.autograd.Function):
     layer (forward or backward), fixed slabs, device-epoch barriers -- capturable in a CUDA graph."""
 
     @staticmethod
-    def forward(ctx, x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta, gs):
+    def forward(ctx, x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta, gs, train):
         C = _ext.load()
         x = x.contiguous()
         T, D = x.shape
@@ -358,8 +367,7 @@ class _EPMoEDev(torch.autograd.Function):
         El = w13.shape[0]
         F2 = w13.shape[1]
         me = ep.rank
-        sl = ep.slot(T, k, E, El, D, capacity)
-        sh = ep._shared
+        sl, sh = ep.slot(T, k, E, El, D, capacity, train)
         arena = ep.arena
         R = sl.R
         logits = mm_nt(x, router_w, out_f32=True)
@@ -395,7 +403,7 @@ class _EPMoEDev(torch.autograd.Function):
         ctx.save_for_backward(x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, H, act)
         # the slabs are views of the shared arena (kept on ctx, not saved tensors); the next
         # forward of this layer rewrites them only after this backward
-        ctx.ep, ctx.sl = ep, sl
+        ctx.ep, ctx.sl, ctx.sh = ep, sl, sh
         ctx.cfg = (k, renorm, aux_alpha, z_beta, gs, add is not None)
         aux = x.new_zeros((), dtype=torch.float32)
         if aux_alpha > 0:
@@ -410,8 +418,8 @@ class _EPMoEDev(torch.autograd.Function):
     def backward(ctx, dout, daux):
         x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, H, act = ctx.saved_tensors
         k, renorm, aux_alpha, z_beta, gs, has_add = ctx.cfg
-        ep, sl = ctx.ep, ctx.sl
-        sh, arena = ep._shared, ep.arena
+        ep, sl, sh = ctx.ep, ctx.sl, ctx.sh
+        arena = ep.arena
         C = _ext.load()
         T, D = x.shape
         El = w13.shape[0]
@@ -439,7 +447,7 @@ class _EPMoEDev(torch.autograd.Function):
         dx_router = mm_nn(dlogits, router_w)
         dx = C.ep_combine(slot, idx, None, sh.dx.ptrs, sl.rows, El, D, dx_router)
         drouter = mm_tn(dlogits, x)
-        return (dx, drouter, dw13, dw2, (dout if has_add else None), None, None, None, None, None, None, None)
+        return (dx, drouter, dw13, dw2, (dout if has_add else None), None, None, None, None, None, None, None, None)
 
 
 # ----------------------------------------------------------------------------
@@ -522,8 +530,10 @@ def ep_moe_ffn(x: torch.Tensor, router_w: torch.Tensor, w13: torch.Tensor, w2: t
     (replicated); w13 [El, 2F, D] / w2 [El, D, F] this rank's experts.  `capacity`
     is the per-expert limit over the whole group (0: dropless)."""
     if ep.transport == "p2p" and x.is_cuda and ep.layout == "device":
+        # training (this layer's backward will read its forward slabs) or inference (slabs shared)
+        train = torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, router_w, w13, w2))
         return _EPMoEDev.apply(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta,
-                               aux_grad_scale)
+                               aux_grad_scale, train)
     if ep.transport == "p2p" and x.is_cuda:
         return _EPMoEP2P.apply(x, router_w, w13, w2, add, ep, k, capacity, renorm, aux_alpha, z_beta,
                                aux_grad_scale)

@@ -304,3 +304,70 @@ def test_ep_dp_train_step_cuda_graph_matches_single_gpu():
         assert out["graphed"], out["graph_error"]
         for a, b in zip(out["ref"], out["ep"]):
             assert abs(a - b) < 2e-2 * max(1.0, abs(a)), out
+
+
+def _decode_worker(rank, world, port, q):
+    """Expert-parallel inference (device layout, shared slabs, graphed decode steps) against a
+    full replica of the same weights on this rank's prompts."""
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig
+        from omnicoder.inference.graphs import GraphedStep
+        from omnicoder.inference.kv_cache import KVCache
+        from omnicoder.models.lm import build_model
+        from omnicoder.ops import _ext
+        from omnicoder.parallel.expert_data import ExpertDataParallel
+
+        cfg = ModelConfig(name="ep_dec", vocab_size=4096, d_model=512, n_layers=2, n_heads=4, ffn_dim=512,
+                          tie_embeddings=False, max_seq_len=1024,
+                          attn=AttentionConfig(kind="mla", kv_lora_rank=256, qk_rope_dim=64, qk_nope_dim=128,
+                                               v_head_dim=128),
+                          moe=MoEConfig(n_experts=8, top_k=2, ffn_dim=256, n_shared_experts=1))
+        full = build_model(cfg, device=dev, seed=0).eval().prepare_inference()
+        par = ExpertDataParallel(dist.group.WORLD, arena_bytes=64 << 20)
+        epm = build_model(cfg, device=dev, seed=0, ep=par).eval().prepare_inference()
+        B, S = 8, 256
+        g = torch.Generator().manual_seed(50 + rank)
+        ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g).to(dev)
+        ca = KVCache(cfg, B, S + 16, dev, kv_dtype="int8")
+        cb = KVCache(cfg, B, S + 16, dev, kv_dtype="int8")
+        errs = []
+        with torch.no_grad():
+            la = full.forward_cached(ids, ca, prefill=True, last_only=True)[:, -1]
+            lb = epm.forward_cached(ids, cb, prefill=True, last_only=True)[:, -1]
+            errs.append(_close(lb, la, 3e-2))
+            step = GraphedStep(epm, cb)
+            tok = la.argmax(-1)
+            for _ in range(4):
+                la = full.forward_cached(tok[:, None], ca)[:, -1]
+                lb = step(tok[:, None])[:, -1]
+                errs.append(_close(lb, la, 3e-2))
+                tok = la.argmax(-1)
+        torch.cuda.synchronize()
+        C = _ext.load()
+        code = C.status()[0]
+        C.status_reset()
+        q.put((rank, {"errs": errs, "status": code, "dropped": par.ep.dropped_pairs()}))
+    except Exception as e:
+        q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_inference_prefill_and_graphed_decode_match_replica():
+    _need_gpus(2)
+    res = _run(_decode_worker)
+    for rank, out in res.items():
+        assert isinstance(out, dict), out
+        assert out["status"] == 0 and out["dropped"] == 0, out
+        for ok, err in out["errs"]:
+            assert ok, (rank, out["errs"])
