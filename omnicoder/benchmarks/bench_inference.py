@@ -24,6 +24,7 @@ from omnicoder.config import get_preset
 from omnicoder.inference.kv_cache import KVCache
 from omnicoder.models.lm import build_model
 from omnicoder.ops import _ext
+from omnicoder.ops.spec import spec_verify
 
 
 def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, gen=512, kv="int8", spec=0,
@@ -97,15 +98,15 @@ def run(preset="longctx_moe", draft_preset="draft_2l", batch=64, prompt=8192, ge
                     cur = fwd_d(cur[:, None])[:, -1].argmax(-1)
                     props.append(cur)
                 props = torch.stack(props, 1)                                    # [B, k] proposals
-                tgt = fwd_t(torch.cat([last[:, None], props], 1)).argmax(-1)  # [B, k+1]
-                n_acc = torch.cumprod((tgt[:, :spec] == props).int(), 1).sum(1)
-                # every sequence keeps its own accepted prefix and the target's next token; both
-                # caches roll back per sequence (the draft first appends its last proposal, which
-                # only fully accepted sequences keep)
+                tl = fwd_t(torch.cat([last[:, None], props], 1))                 # [B, k+1, V]
+                # verify kernel: every sequence keeps its own accepted prefix and the target's
+                # next token; both caches roll back per sequence (the draft first appends its last
+                # proposal, which only fully accepted sequences keep)
+                n_acc, last, new_len = spec_verify(tl, None, props, None, base_t, 0.0)
+                n_acc = n_acc.long()
                 fwd_d(props[:, -1:])
-                cache.rollback(base_t + n_acc + 1)
+                cache.rollback(new_len)
                 dcache.rollback(base_d + n_acc + 1)
-                last = tgt[ar, n_acc]
                 gained = torch.minimum(n_acc + 1, (gen - per_seq).clamp_min(0))
                 per_seq += n_acc + 1
                 accepted += int(n_acc.sum())

@@ -28,6 +28,15 @@ void layernorm_fwd(const void* x, const void* w, const void* b, void* y, float* 
 void layernorm_bwd(const void* x, const void* w, const float* mean, const float* rstd, const void* dy, void* dx,
                    float* dw, float* db, int rows, int dim, cudaStream_t s);
 
+// ---- speculative decoding ---------------------------------------------------
+// Verify k draft tokens per sequence: logits [B, K+1, V] fp32 of the target, pdraft [B, K, V]
+// fp32 draft distributions (unused when temperature <= 0), draft [B, K] and next [B] token ids
+// (int64 when draft_i64, else int32), u [B, K+1] uniforms, base_len / new_len [B] cache lengths
+// (int64 when len_i64).  Writes n_acc [B], next, new_len = base_len + n_acc + 1.
+void spec_verify(const float* logits, const float* pdraft, const void* draft, bool draft_i64, const float* u,
+                 const void* base_len, bool len_i64, int B, int K, int V, float temperature, int* n_acc, void* next,
+                 void* new_len, cudaStream_t s);
+
 // ---- rotary embedding ------------------------------------------------------
 // In-place rotation of dims [off, off+rot) of each head of x (bf16).
 // x row t, head h starts at x + t*row_stride + h*head_stride.  Positions are

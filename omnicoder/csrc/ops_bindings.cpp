@@ -527,6 +527,39 @@ std::vector<at::Tensor> gsplat_forward_t(const at::Tensor& u, const at::Tensor& 
   return {out};
 }
 
+// ---- speculative verify ------------------------------------------------------
+// -> (n_acc [B] int32, next [B] (draft dtype), new_len [B] (base_len dtype))
+std::vector<at::Tensor> spec_verify_t(const at::Tensor& logits, const c10::optional<at::Tensor>& pdraft,
+                                      const at::Tensor& draft, const c10::optional<at::Tensor>& u,
+                                      const at::Tensor& base_len, double temperature) {
+  check_f32(logits, "logits");
+  TORCH_CHECK(logits.dim() == 3, "spec_verify: logits [B, K+1, V]");
+  const int64_t B = logits.size(0), K = logits.size(1) - 1, V = logits.size(2);
+  TORCH_CHECK(draft.is_cuda() && draft.is_contiguous() && draft.dim() == 2 && draft.size(0) == B &&
+                  draft.size(1) == K && (draft.scalar_type() == at::kLong || draft.scalar_type() == at::kInt),
+              "spec_verify: draft tokens [B, K] int32/int64");
+  TORCH_CHECK(base_len.is_cuda() && base_len.is_contiguous() && base_len.numel() == B &&
+                  (base_len.scalar_type() == at::kLong || base_len.scalar_type() == at::kInt),
+              "spec_verify: base_len [B] int32/int64");
+  TORCH_CHECK(K >= 0 && V > 0 && V < (1 << 30), "spec_verify: sizes");
+  const bool sample = temperature > 0;
+  if (sample) {
+    TORCH_CHECK(pdraft.has_value() && u.has_value(), "spec_verify: sampling needs draft probabilities and uniforms");
+    check_f32(*pdraft, "pdraft");
+    check_f32(*u, "u");
+    TORCH_CHECK(pdraft->numel() == B * K * V && u->numel() == B * (K + 1), "spec_verify: pdraft [B, K, V], u [B, K+1]");
+  }
+  const c10::cuda::CUDAGuard g(logits.device());
+  auto n_acc = at::empty({B}, logits.options().dtype(at::kInt));
+  auto next = at::empty({B}, draft.options());
+  auto new_len = at::empty_like(base_len);
+  spec_verify(logits.data_ptr<float>(), sample ? pdraft->data_ptr<float>() : nullptr, draft.data_ptr(),
+              draft.scalar_type() == at::kLong, sample ? u->data_ptr<float>() : nullptr, base_len.data_ptr(),
+              base_len.scalar_type() == at::kLong, (int)B, (int)K, (int)V, (float)temperature, n_acc.data_ptr<int>(),
+              next.data_ptr(), new_len.data_ptr(), stream());
+  return {n_acc, next, new_len};
+}
+
 void register_kernels(pybind11::module_& m) {
   m.def("rmsnorm_fwd", &rmsnorm_fwd_t, py::arg("x"), py::arg("res"), py::arg("w"), py::arg("eps"));
   m.def("rmsnorm_bwd", &rmsnorm_bwd_t, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dres"));
@@ -550,6 +583,8 @@ void register_kernels(pybind11::module_& m) {
   m.def("router_topk", &router_topk_t);
   m.def("kv_cache_write", &kv_cache_write_t, py::arg("src"), py::arg("pos"), py::arg("dst"), py::arg("scale"),
         py::arg("row_offset"));
+  m.def("spec_verify", &spec_verify_t, py::arg("logits"), py::arg("pdraft"), py::arg("draft"), py::arg("u"),
+        py::arg("base_len"), py::arg("temperature"));
   m.def("moe_plan", &moe_plan_t, py::arg("idx"), py::arg("E"), py::arg("capacity"), py::arg("cap_rows"),
         py::arg("align") = 128);
   m.def("moe_gather", &moe_gather_t);

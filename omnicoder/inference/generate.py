@@ -382,9 +382,13 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
     target distribution at the first unaccepted position.
     early_exit = (mode, threshold): after a confident step (omnicoder.inference.addons.confident)
     the next step is a single target step without a draft (reference :2433-2467)."""
+    from ..ops.spec import spec_verify
     from .addons import confident
     B, S = ids.shape
     dev = ids.device
+    # unfiltered sampling (or greedy) verifies in the fused kernel (omnicoder/csrc/spec_verify.cu)
+    fused_verify = (not (verify_threshold > 0 and getattr(target, "verifier", None) is not None)
+                    and (temperature <= 0 or ((not top_k or top_k <= 0) and (top_p is None or top_p >= 1.0))))
     tcache = KVCache(target.cfg, B, L, dev, dtype=target.embed.dtype, kv_dtype=kv_dtype)
     dcache = KVCache(draft.cfg, B, L, dev, dtype=draft.embed.dtype, kv_dtype="bf16")
     use_verifier = verify_threshold > 0 and getattr(target, "verifier", None) is not None
@@ -435,8 +439,28 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
             tl, th = target.forward_cached(seq_in, tcache, return_hidden=True)      # [B, k+1, V], [B, k+1, D]
         else:
             tl = target.forward_cached(seq_in, tcache)
-        pt = sampling_probs(tl, temperature, top_k, top_p)           # [B, k+1, V]
         pd_all = torch.stack(d_prob, dim=1)                          # [B, k, V]
+        if fused_verify:
+            # one kernel: per-sequence acceptance, next token and rolled-back cache lengths
+            u = torch.rand(B, k + 1, device=dev, generator=gen) if temperature > 0 else None
+            n_acc, extra, new_len = spec_verify(tl, pd_all if temperature > 0 else None, d_tok_t, u, base_t,
+                                                temperature)
+            draft.forward_cached(d_tok_t[:, -1:], dcache)
+            tcache.rollback(new_len)
+            dcache.rollback(base_d + (n_acc + 1).to(base_d.dtype))
+            n_list, d_list, e_list = n_acc.tolist(), d_tok_t.tolist(), extra.tolist()
+            for b in range(B):
+                produced[b].extend(d_list[b][:n_list[b]] + [e_list[b]])
+            stats.accepted_draft_tokens += int(sum(n_list))
+            stats.proposed_draft_tokens += B * k
+            stats.steps += 1
+            if early_exit is not None:
+                skip_draft = confident(tl[ar, n_acc.long()], *early_exit)
+            last = extra
+            _sync(last)
+            stats.step_times_s.append(time.perf_counter() - ts)
+            continue
+        pt = sampling_probs(tl, temperature, top_k, top_p)           # [B, k+1, V]
         if use_verifier:
             vl = (th[:, :k].to(target.verifier.dtype) @ target.verifier.t()).float()
             v_d = torch.softmax(vl, -1).gather(-1, d_tok_t[..., None]).squeeze(-1)
