@@ -112,3 +112,64 @@ def test_torch_baseline_moe_matches_torch_oracle():
     shared = swiglu_mlp(y, s13, m.s2)
     want, _ = moe_ffn_torch(y, m.router, w13, m.w2, cfg.moe.top_k, 0, True, add=shared)
     torch.testing.assert_close(out, want, rtol=1e-4, atol=1e-5)
+
+
+def _tp_cfg():
+    return ModelConfig(name="tp_base", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128,
+                       tie_embeddings=False, max_seq_len=64, attn=AttentionConfig(kind="gqa", n_kv_heads=2))
+
+
+def _tp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from omnicoder.baselines.torch_tp import TorchDenseTPLM, TorchTPTrainer
+        cfg = _tp_cfg()
+        tc = TrainConfig(lr=1e-3, warmup_steps=0, max_steps=10, grad_clip=1.0, weight_decay=0.1, eps=1e-6,
+                         grad_accum=2)
+        ref = TorchDenseTPLM(cfg, "cpu", None, torch.float32, seed=0)
+        model = TorchDenseTPLM(cfg, "cpu", dist.group.WORLD, torch.float32, seed=1)
+        hd, H, Hk, Fd = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.ffn_dim
+        h0, h1 = rank * H // world, (rank + 1) * H // world
+        k0, k1 = rank * Hk // world, (rank + 1) * Hk // world
+        f0, f1 = rank * Fd // world, (rank + 1) * Fd // world
+        with torch.no_grad():
+            model.embed.copy_(ref.embed)
+            model.head.copy_(ref.head)
+            model.nf.copy_(ref.nf)
+            for a, b in zip(model.blocks, ref.blocks):
+                w = b.wqkv
+                a.wqkv.copy_(torch.cat([w[h0 * hd:h1 * hd], w[(H + k0) * hd:(H + k1) * hd],
+                                        w[(H + Hk + k0) * hd:(H + Hk + k1) * hd]]))
+                a.wo.copy_(b.wo[:, h0 * hd:h1 * hd])
+                a.w13.copy_(torch.cat([b.w13[f0:f1], b.w13[Fd + f0:Fd + f1]]))
+                a.w2.copy_(b.w2[:, f0:f1])
+                a.n1.copy_(b.n1)
+                a.n2.copy_(b.n2)
+        g = torch.Generator().manual_seed(3)
+        ids = torch.randint(0, 300, (2, 32), generator=g)
+        lab = torch.randint(0, 300, (2, 32), generator=g)
+        rt, tr = TorchTPTrainer(ref, tc), TorchTPTrainer(model, tc)
+        out = [(float(rt.step(ids, lab)), float(tr.step(ids, lab))) for _ in range(3)]
+        err = float((model.blocks[0].wo - ref.blocks[0].wo[:, h0 * hd:h1 * hd]).abs().max())
+        q.put((rank, out, err))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_torch_tp_baseline_matches_single_process():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, out, err in res:
+        for a, b in out:
+            assert abs(a - b) < 1e-4, (rank, out)
+        assert out[-1][0] < out[0][0]
+        assert err < 1e-5, (rank, err)
