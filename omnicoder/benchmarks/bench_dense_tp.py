@@ -2,7 +2,7 @@
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
         -m omnicoder.benchmarks.bench_dense_tp [--global-batch 64] [--steps 2 --warmup 1] \\
-        [--transport nccl|p2p] [--arms ours,baseline] [--layers 48]
+        [--transport nccl|p2p] [--arms ours,baseline] [--layers 48] [--pp P]
 
 Model: dense_20b (48 layers, d_model 6144, 48 query / 8 KV heads of 128, SwiGLU 16384,
 vocab 32000), sequence 8192, random N(0, 0.02) weights, uniform random token ids; bf16
@@ -16,6 +16,9 @@ Arms (same data, same step):
             flash attention; "p2p": the fused peer-memory all-gather -> GEMM and GEMM ->
             reduce-scatter collectives);
   baseline  plain PyTorch + NCCL + cuBLAS (omnicoder.baselines.torch_tp).
+`--pp P` runs the second layout instead: P pipeline stages (1F1B over NCCL point-to-point,
+omnicoder.parallel.pipeline) x tensor parallel N / P inside each stage (rank = stage x TP +
+tp rank), the global batch split into micro-batches of one sequence; only this package's arm.
 Device time with CUDA events, max over ranks; tokens/s = global batch x 8192 / step time.
 """
 from __future__ import annotations
@@ -57,6 +60,7 @@ def main(argv=None):
     ap.add_argument("--transport", default="nccl", choices=["nccl", "p2p"])
     ap.add_argument("--arms", default="ours,baseline")
     ap.add_argument("--json", default=None)
+    ap.add_argument("--pp", type=int, default=1, help="pipeline stages (tensor parallel = N / pp inside each)")
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -77,7 +81,27 @@ def main(argv=None):
                        grad_clip=1.0, weight_decay=0.1, betas=(0.9, 0.95))
     ids, lab = synthetic_batch(G, S, cfg.vocab_size, seed=0, step=0, device=dev)   # same data on every rank
     res = {}
-    for arm in a.arms.split(","):
+    if a.pp > 1:
+        from omnicoder.models.lm import build_model
+        from omnicoder.parallel.pipeline import PipelineTrainer
+        from omnicoder.parallel.tensor import TensorParallel
+        T = world // a.pp
+        if T * a.pp != world:
+            raise SystemExit(f"{world} ranks do not split into {a.pp} stages")
+        tp_groups = [dist.new_group(list(range(s_ * T, (s_ + 1) * T))) for s_ in range(a.pp)]
+        pp_groups = [dist.new_group(list(range(t_, world, T))) for t_ in range(T)]
+        stage, t = rank // T, rank % T
+        par = TensorParallel(tp_groups[stage], transport=a.transport) if T > 1 else None
+        model = build_model(cfg, device=dev, seed=1234, tp=par)
+        pt = PipelineTrainer(model, tcfg, group=pp_groups[t], n_micro=G, tp=par)
+        del model
+        gc.collect()
+        torch.cuda.empty_cache()
+        ms, loss = _time(pt.step, ids, lab, a.warmup, a.steps, dev)
+        res["ours"] = {"ms_per_step": ms, "tokens_per_s": G * S / (ms / 1e3), "loss": loss,
+                       "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 1e9}
+        a.arms = ""
+    for arm in [x for x in a.arms.split(",") if x]:
         if arm == "ours":
             from omnicoder.models.lm import build_model
             from omnicoder.parallel.tensor import TensorParallel
@@ -105,7 +129,8 @@ def main(argv=None):
         r["model_tflops_per_gpu"] = r["tokens_per_s"] * fpt / world / 1e12
     if rank == 0:
         out = {"bench": "dense 20B training step, tensor + sequence parallel", "n_gpus": world,
-               "parallelism": f"tp{world}+sp", "transport": a.transport, "model": f"{cfg.name} {cfg.n_layers}L",
+               "parallelism": (f"pp{a.pp}xtp{world // a.pp}+sp" if a.pp > 1 else f"tp{world}+sp"),
+               "transport": a.transport, "model": f"{cfg.name} {cfg.n_layers}L",
                "global_batch": G, "seq_len": S, "dtype": "bf16 (fp32 master weights, AdamW)",
                "data": "synthetic (uniform random token ids, random-init N(0,0.02))",
                "train_gflop_per_token": fpt / 1e9, "arms": res}

@@ -17,6 +17,12 @@ on each other's sends.  The last stage owns the loss (mean over micro-batches);
 Optimiser: FusedAdamW over the stage's parameters with the global-norm clip
 computed over all stages (one all-reduce of the squared norm).
 
+Tensor parallelism inside the stages (`tp`, an omnicoder.parallel.tensor.TensorParallel
+over the stage's ranks, the model built with it): a stage is a TP group, the
+activations crossing stages are the sequence-parallel token shards (rank t of a
+stage exchanges with rank t of the next), replicated gradients are summed over
+the TP group and the clip norm counts each replicated parameter once per stage.
+
 The reference has no pipeline parallelism.
 """
 from __future__ import annotations
@@ -44,31 +50,46 @@ class PipelineStage(torch.nn.Module):
         self.norm_f = model.norm_f if self.last else None
         self.lm_head = model.lm_head if self.last else None
         self.rope = model.rope
+        self.tp = model.tp                      # TPContext of the stage's tensor-parallel group, or None
 
-    def forward(self, x, seq: int):
-        """Stage 0: token ids [b, S] -> hidden; other stages: hidden [b*S, D] -> hidden;
-        last stage returns final normalised hidden states."""
+    def forward(self, x, seq: int, batch: int | None = None):
+        """Stage 0: token ids [b, S] -> hidden; other stages: hidden [b*S (/ TP), D] -> hidden;
+        last stage returns final normalised hidden states (this rank's token shard with TP)."""
         if self.first:
             b, S = x.shape
+            batch = b
             if x.is_cuda:
                 self.rope.to(x.device)
-            h = embedding(x.reshape(-1), self.embed)
+            flat = x.reshape(-1)
+            if self.tp is not None:
+                from .tensor import scatter_seq
+                flat = scatter_seq(flat, self.tp)
+            h = embedding(flat, self.embed)
         else:
             h = x
             if h.is_cuda:
                 self.rope.to(h.device)
-        positions = torch.arange(seq, device=h.device).repeat(h.shape[0] // seq)
+        if batch is None:
+            batch = h.shape[0] // seq
+        positions = torch.arange(seq, device=h.device).repeat(batch)
         for blk in self.blocks:
             h, _ = blk(h, self.rope, positions, seq)
         return self.norm_f(h) if self.last else h
 
 
 class PipelineTrainer:
-    def __init__(self, model: OmniLM, tcfg, group=None, n_micro: int = 4):
+    def __init__(self, model: OmniLM, tcfg, group=None, n_micro: int = 4, tp=None):
+        """`group`: the ranks of this rank's pipeline (one per stage); `tp`: the TensorParallel
+        layout of this rank's stage (the model must have been built with it)."""
         self.group = group if group is not None else dist.group.WORLD
         self.stage_id = dist.get_rank(self.group)
         self.P = dist.get_world_size(self.group)
+        self.tp = tp
+        self.tp_world = tp.world if tp is not None else 1
         self.stage = PipelineStage(model, self.stage_id, self.P)
+        if tp is not None:
+            self.replicated = [p for p in self.stage.parameters() if not getattr(p, "tp_sharded", False)]
+            self.sharded = [p for p in self.stage.parameters() if getattr(p, "tp_sharded", False)]
         self.tcfg, self.n_micro = tcfg, n_micro
         self.opt = FusedAdamW(self.stage.parameters(), lr=tcfg.lr, betas=tuple(tcfg.betas), eps=tcfg.eps,
                               weight_decay=tcfg.weight_decay, max_grad_norm=0.0)
@@ -99,15 +120,21 @@ class PipelineTrainer:
         pending: list = []
         loss_sum = torch.zeros((), device=dev, dtype=torch.float32)
 
+        rows = mb * S // self.tp_world
+
         def fwd(i):
             nonlocal loss_sum
             if st.first:
                 x = ids_m[i]
             else:
-                x = self._recv((mb * S, D), dtype, dev, self.stage_id - 1).requires_grad_(True)
-            out = st(x, S)
+                x = self._recv((rows, D), dtype, dev, self.stage_id - 1).requires_grad_(True)
+            out = st(x, S, mb)
             if st.last:
-                loss = lm_head_cross_entropy(out, st.lm_head, lab_m[i].reshape(-1)) / M
+                lab = lab_m[i].reshape(-1)
+                if self.tp is not None:
+                    from .tensor import scatter_seq
+                    lab = scatter_seq(lab, self.tp.tp)
+                loss = lm_head_cross_entropy(out, st.lm_head, lab) / M
                 loss_sum = loss_sum + loss.detach().float()
                 saved[i] = (x, loss)
             else:
@@ -136,16 +163,35 @@ class PipelineTrainer:
             r.wait()
         # global-norm clip over all stages, then the optimiser step
         scale = 1.0
+        if self.tp is not None:
+            # each TP rank back-propagated the mean loss of its own token shard: sum the replicated
+            # gradients over the stage's group and average everything over it
+            self.tp.replicated, self.tp.sharded = self.replicated, self.sharded
+            self.tp.sync_grads()
+            scale = 1.0 / self.tp_world
         if self.tcfg.grad_clip > 0:
             sq = torch.zeros((), device=dev)
-            for p in st.parameters():
-                if p.grad is not None:
-                    sq += p.grad.float().pow(2).sum()
+            if self.tp is None:
+                for p in st.parameters():
+                    if p.grad is not None:
+                        sq += p.grad.float().pow(2).sum()
+            else:
+                for p in self.sharded:
+                    if p.grad is not None:
+                        sq += p.grad.float().pow(2).sum()
+                dist.all_reduce(sq, group=self.tp.group)
+                for p in self.replicated:
+                    if p.grad is not None:
+                        sq += p.grad.float().pow(2).sum()
             dist.all_reduce(sq, group=self.group)
-            scale = min(1.0, self.tcfg.grad_clip / (float(sq.sqrt()) + 1e-6))
+            norm = float(sq.sqrt()) * scale
+            scale *= min(1.0, self.tcfg.grad_clip / (norm + 1e-6))
         lr = cosine_lr(self.step_idx, self.tcfg.lr, self.tcfg.warmup_steps, self.tcfg.max_steps)
         self.opt.step(lr=lr, grad_scale=scale)
         self.opt.zero_grad()
         self.step_idx += 1
+        if self.tp is not None and st.last:
+            dist.all_reduce(loss_sum, group=self.tp.group)
+            loss_sum = loss_sum / self.tp_world
         dist.broadcast(loss_sum, self._peer(P - 1), group=self.group)
         return loss_sum
