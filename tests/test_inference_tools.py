@@ -309,3 +309,33 @@ def test_speculative_verifier_threshold_and_early_exit():
     out2, st2 = generate(tgt, prompt, 8, temperature=0.0, draft_model=drf, speculative_draft_len=3,
                          early_exit=True, early_exit_entropy=1e9, return_stats=True)
     assert torch.equal(out2, plain) and st2.early_exits == st2.steps - 1
+
+
+def test_onnx_wrapper_mla_prefill_and_decode_match_model():
+    """Spec MLA family through the export wrapper (absorbed latent attention): a T-token prefill
+    graph and the following one-token decode steps give forward_cached's logits."""
+    from omnicoder.export.onnx_export import DecodeStepWrapper, example_inputs, spec_cache_shapes
+    cfg = ModelConfig(name="mla_x", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      attn=AttentionConfig(kind="mla", kv_lora_rank=32, qk_rope_dim=16, qk_nope_dim=16,
+                                           v_head_dim=16),
+                      moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=64, n_shared_experts=1))
+    m = build_model(cfg, device="cpu", seed=0).eval()
+    prompt = torch.tensor([[5, 9, 2, 7, 1, 3], [8, 8, 4, 6, 2, 11]])
+    from omnicoder.inference.kv_cache import KVCache
+    kv = KVCache(cfg, 2, 32, "cpu")
+    want = [m.forward_cached(prompt, kv, prefill=True)]
+    w = DecodeStepWrapper(m)
+    cache = [torch.zeros(s) for s in spec_cache_shapes(cfg, 2, 32)]
+    out = w(prompt, torch.tensor(0), *cache)
+    torch.testing.assert_close(out[0], want[0], rtol=1e-4, atol=1e-4)
+    cache = list(out[1:])
+    pos = prompt.shape[1]
+    for t in (4, 17, 23):
+        ids = torch.tensor([[t], [t + 1]])
+        ref = m.forward_cached(ids, kv)
+        out = w(ids, torch.tensor(pos), *cache)
+        torch.testing.assert_close(out[0], ref, rtol=1e-4, atol=1e-4)
+        cache = list(out[1:])
+        pos += 1
+    w2, args = example_inputs(m, batch=1, max_len=16, tokens=4)
+    assert args[0].shape == (1, 4) and len(args) == 2 + 2 * cfg.n_layers
