@@ -63,8 +63,8 @@ class TorchStepSession:
             a = model.blocks[0].attn
             shape = (batch, a.n_heads, a.c.decode_window, a.dl)
         else:
-            c = model.cfg
-            shape = (batch, max_len, c.n_kv_heads, c.head_dim)
+            from ..export.onnx_export import spec_cache_shapes
+            shape = spec_cache_shapes(model.cfg, batch, max_len)[0]     # MLA: the latent rows
         self._ins = [TensorInfo(n, (batch, 1) if n == "input_ids" else () if n == "position" else shape) for n in ins]
         self._outs = [TensorInfo(n, ()) for n in outs]
         self.device = next(model.parameters()).device

@@ -3,8 +3,10 @@
 Runs the stages of a training plan as child processes with a time budget each
 (reference src/omnicoder/tools/run_training.py:102-1366: stage planning from a
 minute budget, `run_with_timeout`, resume by skipping finished stages, optional
-expert-parallel launch).  Stages here: `pretrain` (spec LM), `draft` (small
-draft model for speculative decoding), `export` (ONNX decode step).  Each stage
+expert-parallel launch).  Stages here: `pretrain` (spec LM), `distill`
+(knowledge distillation of the draft-sized student from the pretrained model or
+a local Hugging Face teacher), `draft` (small draft model for speculative
+decoding), `export` (ONNX decode step).  Each stage
 writes a marker file when it finishes; a rerun skips finished stages unless
 --force is given.
 """
@@ -34,8 +36,8 @@ def run_with_timeout(cmd: list[str], timeout_s: float, env=None) -> int:
 
 
 def plan(budget_minutes: float, steps_per_minute: float, stages: list[str]) -> dict:
-    """Split the budget: 80 % pretrain, 15 % draft, 5 % export."""
-    share = {"pretrain": 0.8, "draft": 0.15, "export": 0.05}
+    """Split the budget: pretrain 80, distill 10, draft 15, export 5 (relative shares)."""
+    share = {"pretrain": 0.8, "distill": 0.1, "draft": 0.15, "export": 0.05}
     tot = sum(share[s] for s in stages) or 1.0
     return {s: {"minutes": budget_minutes * share[s] / tot,
                 "steps": max(1, int(budget_minutes * share[s] / tot * steps_per_minute))} for s in stages}
@@ -53,6 +55,7 @@ def main(argv=None):
     ap.add_argument("--seq_len", type=int, default=256)
     ap.add_argument("--batch_size", type=int, default=4)
     ap.add_argument("--devices", default="", help="comma list of cuda devices: expert-parallel launch when > 1")
+    ap.add_argument("--teacher_hf", default=None, help="distill stage: local Hugging Face causal LM directory")
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--dry_run", action="store_true")
     a = ap.parse_args(argv)
@@ -77,6 +80,12 @@ def main(argv=None):
                        "--devices", ",".join(devs), "--"] + args
             else:
                 cmd = [sys.executable, "-m", "omnicoder.training.pretrain"] + args
+        elif s == "distill":
+            cmd = [sys.executable, "-m", "omnicoder.training.distill", "--student_preset", a.draft_preset,
+                   "--data", a.data, "--steps", str(p[s]["steps"]), "--seq_len", str(a.seq_len), "--batch_size",
+                   str(a.batch_size), "--out", os.path.join(a.out_dir, "student.pt")]
+            cmd += (["--teacher_hf", a.teacher_hf] if a.teacher_hf else
+                    ["--teacher_ckpt", os.path.join(a.out_dir, "pretrain.pt"), "--teacher_preset", a.preset])
         elif s == "export":
             cmd = [sys.executable, "-m", "omnicoder.export.onnx_export", "--ckpt", os.path.join(a.out_dir, "pretrain.pt"),
                    "--out", os.path.join(a.out_dir, "decode_step.onnx")]

@@ -51,3 +51,19 @@ def test_torchrun_ep_two_cpu_ranks(tmp_path):
 def test_run_training_plan_dry_run():
     out = _run(["omnicoder.tools.run_training", "--dry_run", "--budget_minutes", "1", "--stages", "pretrain,draft,export"])
     assert "omnicoder.training.pretrain" in out and "onnx_export" in out
+
+
+def test_press_play_export_to_phone_and_lets_go(tmp_path):
+    """One-button run (export, benchmarks, smoke, manifest), the phone package, and the budgeted
+    training planner (dry run with a given step rate, distill stage included)."""
+    out = tmp_path / "rel"
+    _run(["omnicoder.tools.press_play", "--out_root", str(out), "--preset", "tiny_moe", "--bench_tokens", "4"])
+    man = json.loads((out / "press_play_manifest.json").read_text())
+    assert man["steps"]["bench_native"]["tokens_per_s"] > 0 and man["steps"]["bench_decode_step"]["tokens_per_s"] > 0
+    assert (out / "export" / "int4" / "manifest.json").exists() and (out / "export" / "model.gguf").exists()
+    ph = tmp_path / "phone"
+    o = _run(["omnicoder.tools.export_to_phone", "--preset", "tiny_moe", "--out", str(ph), "--no_gguf", "--push"])
+    assert "adb push" in o and json.loads((ph / "phone_manifest.json").read_text())["artifacts"]["int4_package"]
+    o = _run(["omnicoder.tools.lets_gooooo", "--dry_run", "--steps_per_minute", "30", "--budget_minutes", "2",
+              "--out_dir", str(tmp_path / "lg")])
+    assert "omnicoder.training.distill" in o and "omnicoder.training.pretrain" in o
