@@ -405,16 +405,26 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
     t1 = time.perf_counter()
     ar = torch.arange(B, device=dev)
     skip_draft = False
+    def keep(base, grown):
+        """Sequences that already have max_new tokens stop advancing their cache: while slower
+        sequences catch up, their (ignored) writes stay within the last k + 1 rows."""
+        done = torch.tensor([len(p) >= max_new for p in produced], device=dev)
+        return torch.where(done, base, grown.to(base.dtype))
+
     while min(len(p) for p in produced) < max_new:
         ts = time.perf_counter()
         if skip_draft:
             # early exit: one target step, the draft cache follows with the same token
+            base_t, base_d = tcache.lengths.clone(), dcache.lengths.clone()
             tl = target.forward_cached(last[:, None], tcache)[:, -1]
             draft.forward_cached(last[:, None], dcache)
+            tcache.rollback(keep(base_t, tcache.lengths))
+            dcache.rollback(keep(base_d, dcache.lengths))
             pt = sampling_probs(tl, temperature, top_k, top_p)
             extra = pt.argmax(-1) if temperature <= 0 else torch.multinomial(pt, 1, generator=gen).squeeze(1)
             for b, e in enumerate(extra.tolist()):
-                produced[b].append(e)
+                if len(produced[b]) < max_new:
+                    produced[b].append(e)
             stats.steps += 1
             stats.early_exits += 1
             skip_draft = confident(tl, *early_exit)
@@ -446,11 +456,12 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
             n_acc, extra, new_len = spec_verify(tl, pd_all if temperature > 0 else None, d_tok_t, u, base_t,
                                                 temperature)
             draft.forward_cached(d_tok_t[:, -1:], dcache)
-            tcache.rollback(new_len)
-            dcache.rollback(base_d + (n_acc + 1).to(base_d.dtype))
+            tcache.rollback(keep(base_t, new_len))
+            dcache.rollback(keep(base_d, base_d + (n_acc + 1).to(base_d.dtype)))
             n_list, d_list, e_list = n_acc.tolist(), d_tok_t.tolist(), extra.tolist()
             for b in range(B):
-                produced[b].extend(d_list[b][:n_list[b]] + [e_list[b]])
+                if len(produced[b]) < max_new:
+                    produced[b].extend(d_list[b][:n_list[b]] + [e_list[b]])
             stats.accepted_draft_tokens += int(sum(n_list))
             stats.proposed_draft_tokens += B * k
             stats.steps += 1
@@ -485,13 +496,14 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
         extra = q.argmax(-1) if temperature <= 0 else torch.multinomial(q, 1, generator=gen).squeeze(1)
         # draft cache lacks the k-th draft token when everything was accepted: catch up
         draft.forward_cached(d_tok_t[:, -1:], dcache)
-        tcache.rollback(base_t + n_acc + 1)
-        dcache.rollback(base_d + n_acc + 1)
+        tcache.rollback(keep(base_t, base_t + n_acc + 1))
+        dcache.rollback(keep(base_d, base_d + n_acc + 1))
         n_list = n_acc.tolist()
         d_list = d_tok_t.tolist()
         e_list = extra.tolist()
         for b in range(B):
-            produced[b].extend(d_list[b][:n_list[b]] + [e_list[b]])
+            if len(produced[b]) < max_new:
+                produced[b].extend(d_list[b][:n_list[b]] + [e_list[b]])
         stats.accepted_draft_tokens += int(sum(n_list))
         stats.proposed_draft_tokens += B * k
         stats.steps += 1

@@ -67,3 +67,13 @@ def test_press_play_export_to_phone_and_lets_go(tmp_path):
     o = _run(["omnicoder.tools.lets_gooooo", "--dry_run", "--steps_per_minute", "30", "--budget_minutes", "2",
               "--out_dir", str(tmp_path / "lg")])
     assert "omnicoder.training.distill" in o and "omnicoder.training.pretrain" in o
+
+
+def test_draft_train_pipeline(tmp_path):
+    """KD of a LoRA draft, checkpoint, acceptance benchmark; greedy speculative decoding with the
+    draft reproduces plain decoding (sequences that finish first stop advancing their cache)."""
+    o = _run(["omnicoder.training.draft_train", "--steps", "2", "--seq_len", "32", "--batch_size", "2",
+              "--device", "cpu", "--student_preset", "tiny_moe", "--lora", "--out_ckpt", str(tmp_path / "d.pt"),
+              "--bench_out", str(tmp_path / "b.json")])
+    rep = json.loads((tmp_path / "b.json").read_text())
+    assert rep["acceptance"]["same_output"] and (tmp_path / "d.pt").exists()
