@@ -73,6 +73,9 @@ def parse_args():
                     help="expert-parallel receive slabs hold this many times the balanced per-expert load "
                          "(pairs beyond it are dropped and counted in ep_stats)")
     ap.add_argument("--decode-gen", type=int, default=512)
+    ap.add_argument("--decode-layout", default="replica", choices=["replica", "ep"],
+                    help="several GPUs: a full model replica per GPU, or experts sharded over the GPUs (expert "
+                         "parallel decode through the device-side exchange)")
     return ap.parse_args()
 
 
@@ -166,7 +169,7 @@ def decode_phase(args, dev, world, rank, barrier):
     from omnicoder.models.lm import build_model
 
     par = None
-    if world > 1:
+    if world > 1 and args.decode_layout == "ep":
         from omnicoder.parallel.expert_data import ExpertDataParallel
         c = get_preset("longctx_moe")
         # inference slabs are shared by the layers: sized for the largest call (4 prompts of prefill)
@@ -209,8 +212,10 @@ def decode_phase(args, dev, world, rank, barrier):
         "window": 4096, "memory_rows": res["memory_rows"], "p50_tpot_ms": res["p50_tpot_ms"],
         "prefill_tokens_per_s": world * 64 * 8192 / pre_s, "cuda_graphs": True,
         "parallelism": (f"ep{world}: each GPU holds {32 // world} of the 32 experts of every layer and serves its "
-                        f"own 64 sequences" if world > 1 else "one GPU, whole model (13 GB of weights)"),
-        "expert_parallel": world,
+                        f"own 64 sequences" if par is not None else
+                        (f"{world} replicas, one per GPU (13 GB of weights each)" if world > 1 else
+                         "one GPU, whole model (13 GB of weights)")),
+        "expert_parallel": world if par is not None else 1,
         "model": res["model"], "data": "synthetic (uniform random prompts, random-init N(0,0.02))",
         "e2e": {"value": world * 64 * args.decode_gen / e2e_s, "unit": "generated tokens/s (prefill + decode)",
                 "s": e2e_s, "h2d_bytes_per_step": prompts.numel() * prompts.element_size(),
