@@ -77,3 +77,27 @@ def test_draft_train_pipeline(tmp_path):
               "--bench_out", str(tmp_path / "b.json")])
     rep = json.loads((tmp_path / "b.json").read_text())
     assert rep["acceptance"]["same_output"] and (tmp_path / "d.pt").exists()
+
+
+def test_auto_benchmark_sweep(tmp_path):
+    """Throughput per KV format, multiple-choice scoring by log-likelihood, perplexity and the
+    prediction-file scorers, written to JSON and CSV."""
+    mc = tmp_path / "mc.jsonl"
+    mc.write_text("\n".join(json.dumps({"question": f"q{i}?", "choices": ["aa", "bb", "cc"], "answer": i % 3})
+                            for i in range(6)))
+    vqa = tmp_path / "vqa.jsonl"
+    vqa.write_text(json.dumps({"prediction": "Cat", "answer": "cat"}) + "\n" +
+                   json.dumps({"prediction": "dog", "answer": "cow"}))
+    asr = tmp_path / "asr.jsonl"
+    asr.write_text(json.dumps({"prediction": "a b c", "reference": "a b d"}))
+    txt = tmp_path / "t.txt"
+    txt.write_text("hello world " * 200)
+    out = tmp_path / "s.json"
+    _run(["omnicoder.eval.auto_benchmark", "--device", "cpu", "--seq_len", "16", "--gen_tokens", "4",
+          "--kv", "none,u8,nf4", "--mmlu_jsonl", str(mc), "--arc_jsonl", str(mc), "--vqa_jsonl", str(vqa),
+          "--asr_jsonl", str(asr), "--text", str(txt), "--out", str(out), "--out_csv", str(tmp_path / "s.csv")])
+    r = json.loads(out.read_text())
+    assert r["tokens_per_s_kv_none"] > 0 and r["tokens_per_s_kv_nf4"] > 0
+    assert r["mmlu"]["n"] == 6 and 0 <= r["mmlu"]["accuracy"] <= 1
+    assert r["vqa_exact_match"] == 0.5 and abs(r["asr_wer"] - 1 / 3) < 1e-6 and r["perplexity"] > 1
+    assert (tmp_path / "s.csv").exists()
