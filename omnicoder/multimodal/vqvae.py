@@ -98,6 +98,9 @@ class AudioVQ(nn.Module):
         self.mel = MelFrontend(n_mels=n_mels, out_dim=dim, sr=sample_rate)
         self.enc = nn.Sequential(nn.Conv1d(dim, dim, 3, stride, 1), nn.SiLU(), nn.Conv1d(dim, code_dim, 1))
         self.vq = VectorQuantizer(codebook_size, code_dim)
+        # codes -> log-mel frames (the input of MelVocoder); `stride` frames per code
+        self.dec = nn.Sequential(nn.ConvTranspose1d(code_dim, dim, stride, stride), nn.SiLU(),
+                                 nn.Conv1d(dim, n_mels, 3, padding=1))
 
     def _latent(self, wav):
         return self.enc(self.mel(wav).transpose(1, 2)).transpose(1, 2)    # [B, frames', D]
@@ -108,6 +111,19 @@ class AudioVQ(nn.Module):
     def forward(self, wav):
         zq, codes, loss = self.vq(self._latent(wav))
         return zq, codes, loss
+
+    def decode(self, codes: torch.Tensor) -> torch.Tensor:
+        """codes [B, n] -> log-mel frames [B, n * stride, n_mels]."""
+        z = self.vq.codebook.weight[codes]                               # [B, n, code_dim]
+        return self.dec(z.transpose(1, 2)).transpose(1, 2)
+
+    def reconstruction_loss(self, wav: torch.Tensor) -> torch.Tensor:
+        """Codebook / commitment loss + L1 between the decoded and the input log-mel frames."""
+        zq, codes, vq_loss = self.vq(self._latent(wav))
+        mel = self.mel.mel(wav)
+        rec = self.dec(zq.transpose(1, 2)).transpose(1, 2)
+        n = min(rec.shape[1], mel.shape[1])
+        return vq_loss + F.l1_loss(rec[:, :n], mel[:, :n])
 
 
 class MelVocoder(nn.Module):

@@ -1,0 +1,58 @@
+"""Vision backbone family and the full fusion-composer contract (continuous fusion with segment
+ids, code tokenisation into the unified vocabulary and back to pixels / waveforms, grounding and
+segmentation heads, video change scores, audio-video offset, router conditioning) on CPU."""
+import pytest
+import torch
+
+from omnicoder.multimodal import (AudioVQ, FusionComposer, ImageVQVAE, MelFrontend, MelVocoder, VisionBackbone)
+from omnicoder.multimodal.video import VideoEncoder
+
+
+@pytest.mark.parametrize("backend,n_tok", [("vit_tiny", 16), ("dino_tiny", 16), ("siglip_tiny", 16)])
+def test_vision_backbones(backend, n_tok):
+    vb = VisionBackbone(backend, image_size=64, patch=16, depth=2)
+    tok, pooled = vb(torch.randn(2, 3, 64, 64))
+    assert tok.shape == (2, n_tok, 192) and pooled.shape == (2, 192)
+    with pytest.raises(ValueError):
+        VisionBackbone("convnext_tiny")
+
+
+def test_fusion_composer_contract():
+    torch.manual_seed(0)
+    D = 64
+    fc = FusionComposer(D, vision=VisionBackbone("vit_tiny", image_size=64, patch=16, depth=1),
+                        video=VideoEncoder(image_size=32, patch=16, dim=48, depth=1, heads=2),
+                        audio=MelFrontend(out_dim=40), image_vq=ImageVQVAE(width=16, levels=2, codebook_size=256),
+                        audio_vq=AudioVQ(dim=32, codebook_size=128), vocoder=MelVocoder(width=32))
+    text = torch.randn(2, 5, D)
+    img = torch.randn(2, 3, 64, 64)
+    vid = torch.randn(2, 3, 3, 32, 32)
+    wav = torch.randn(2, 1600)
+    emb, seg = fc.fuse_all(text, image=img, video=vid, audio=wav)
+    n_aud = fc.audio_tokens(wav).shape[1]
+    assert emb.shape == (2, (16 + 2) + (3 + 2) + (n_aud + 2) + 5, D) and seg.shape == emb.shape[:2]
+    assert seg[0, 0] == 1 and seg[0, 18] == 2 and seg[0, -1] == 0 and (seg == 3).sum() == 2 * (n_aud + 2)
+    assert fc.fuse_text_image(text, img).shape[1] == 18 + 5
+    # discrete path: codes into the unified vocabulary and back
+    codes = fc.encode_image_to_codes(img)
+    assert codes.shape == (2, 16 * 16)
+    ids = fc.fuse_text_image_codes(torch.zeros(2, 3, dtype=torch.long), codes.view(2, 16, 16).flatten(1))
+    lo = fc.layout.image_range[0]
+    assert ids.shape == (2, 256 + 3) and int(ids[:, :256].min()) >= lo
+    assert fc.decode_image_from_codes(codes, (16, 16)).shape == (2, 3, 64, 64)
+    acodes = fc.encode_audio_to_codes(wav)
+    wave = fc.decode_audio_from_codes(acodes)
+    assert wave.dim() == 2 and wave.shape[0] == 2 and wave.abs().max() <= 1.0
+    assert fc.audio_vq.reconstruction_loss(wav) > 0
+    # heads
+    out = fc.vision_heads(fc.image_tokens(img), text, image_size=64)
+    assert out["box"].shape == (2, 4) and out["mask_logits"].shape == (2, 1, 64, 64)
+    vh = fc.video_heads(fc.video_tokens(vid))
+    assert vh["change"].shape == (2, 2) and vh["keyframe"].shape == (2,)
+    a = torch.randn(2, 12, 40)
+    v = torch.cat([torch.randn(2, 2, 48), torch.randn(2, 12, 48)], 1)
+    assert len(fc.av_sync(a, v[:, :12])["offset"]) == 2
+    cond = fc.conditioning_from_hidden(emb, seg)
+    assert set(cond) == {"text", "image", "video", "audio"} and cond["image"].shape == (2, D)
+    with pytest.raises(RuntimeError):
+        FusionComposer(D).encode_video_to_codes(vid)
