@@ -334,18 +334,26 @@ class OmniLM(nn.Module):
             if isinstance(b.ffn, MoEFFN):
                 b.ffn.aux_grad_scale = s
 
-    def hidden(self, ids: torch.Tensor, positions: torch.Tensor | None = None):
-        """Final normalised hidden states [B*S, D] and the summed auxiliary loss."""
-        B, S = ids.shape
-        if ids.is_cuda:
-            self.rope.to(ids.device)
-        flat = ids.reshape(-1)
-        if self.tp is not None:                       # sequence parallel: this rank's token shard
-            from ..parallel.tensor import scatter_seq
-            flat = scatter_seq(flat, self.tp)
-        h = embedding(flat, self.embed)
+    def hidden(self, ids: torch.Tensor | None, positions: torch.Tensor | None = None,
+               embeds: torch.Tensor | None = None):
+        """Final normalised hidden states [B*S, D] and the summed auxiliary loss.  `embeds`
+        [B, S, D] replaces the token embeddings (inputs composed with other modalities)."""
+        B, S = (embeds.shape[:2] if embeds is not None else ids.shape)
+        dev = embeds.device if embeds is not None else ids.device
+        if dev.type == "cuda":
+            self.rope.to(dev)
+        if embeds is not None:
+            if self.tp is not None:
+                raise NotImplementedError("input embeddings with tensor parallelism")
+            h = embeds.reshape(B * S, -1).to(self.embed.dtype).contiguous()
+        else:
+            flat = ids.reshape(-1)
+            if self.tp is not None:                       # sequence parallel: this rank's token shard
+                from ..parallel.tensor import scatter_seq
+                flat = scatter_seq(flat, self.tp)
+            h = embedding(flat, self.embed)
         if positions is None:
-            positions = torch.arange(S, device=ids.device).repeat(B)
+            positions = torch.arange(S, device=dev).repeat(B)
         aux_total = None
         for blk in self.blocks:
             h, aux = blk(h, self.rope, positions, S)
@@ -353,9 +361,11 @@ class OmniLM(nn.Module):
                 aux_total = aux if aux_total is None else aux_total + aux
         return self.norm_f(h), aux_total
 
-    def forward(self, ids: torch.Tensor, labels: torch.Tensor | None = None, all_logits: bool = False,
-                assume_all_valid: bool = False):
-        y, aux = self.hidden(ids)
+    def forward(self, ids: torch.Tensor | None, labels: torch.Tensor | None = None, all_logits: bool = False,
+                assume_all_valid: bool = False, embeds: torch.Tensor | None = None):
+        y, aux = self.hidden(ids, embeds=embeds)
+        if ids is None:
+            ids = torch.empty(embeds.shape[:2], dtype=torch.long, device=embeds.device)   # shape carrier
         out = {}
         if labels is not None and self.tp is not None:
             from ..parallel.tensor import scatter_seq

@@ -56,3 +56,36 @@ def test_fusion_composer_contract():
     assert set(cond) == {"text", "image", "video", "audio"} and cond["image"].shape == (2, D)
     with pytest.raises(RuntimeError):
         FusionComposer(D).encode_video_to_codes(vid)
+
+
+def test_vl_task_trainers(tmp_path):
+    """VQA / captioning over composed image features: only target tokens are trained, the loss
+    falls on a fixed batch, JSONL rows load tensor files; ASR over audio features."""
+    import json
+
+    from omnicoder.config import AttentionConfig, ModelConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.tokenizer import get_tokenizer
+    from omnicoder.training.vl_tasks import VLTaskTrainer, read_task_jsonl
+    torch.manual_seed(0)
+    cfg = ModelConfig(name="vl", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=128,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2))
+    lm = build_model(cfg, device="cpu", seed=0)
+    tok = get_tokenizer(cfg.vocab_size)
+    fc = FusionComposer(64, vision=VisionBackbone("vit_tiny", image_size=32, patch=16, depth=1),
+                        audio=MelFrontend(out_dim=32))
+    tr = VLTaskTrainer(lm, fc, tok, "vqa", lr=3e-3)
+    imgs = torch.randn(2, 3, 32, 32)
+    b = tr.build(imgs, ["Question: color? Answer:", "Question: count? Answer:"], ["red", "two"])
+    n_pre = 4 + 2                                       # 4 patches + begin / end markers
+    assert (b.labels[:, :n_pre + 5] == -100).all()      # modality and prompt positions are not trained
+    assert (b.labels != -100).sum() == len(tok.encode(" red")) + len(tok.encode(" two")) + 2
+    losses = [tr.step(imgs, ["Question: color? Answer:"] * 2, ["red", "two"]) for _ in range(15)]
+    assert losses[-1] < 0.5 * losses[0]
+    torch.save(torch.randn(3, 32, 32), tmp_path / "a.pt")
+    (tmp_path / "cap.jsonl").write_text(json.dumps({"image": str(tmp_path / "a.pt"), "caption": "a cat"}))
+    rows = read_task_jsonl(str(tmp_path / "cap.jsonl"), "caption")
+    cap = VLTaskTrainer(lm, fc, tok, "caption", lr=1e-3)
+    assert len(cap.fit(rows, steps=2, batch=2)) == 2 and isinstance(cap.answer(rows[0]["media"], "Caption:", 3), str)
+    asr = VLTaskTrainer(lm, fc, tok, "asr", lr=1e-3)
+    assert asr.step(torch.randn(2, 1600), ["Transcript:"] * 2, ["hi", "yo"]) > 0
