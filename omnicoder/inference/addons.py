@@ -105,25 +105,12 @@ def retrieval_vectors(model, texts: list[str], encode_fn, max_texts: int = 8) ->
     return torch.stack(vecs) if vecs else None
 
 
-def sfb_token_bias(prompt_text: str, encode_fn, vocab: int, device, strength: float = 1.0,
-                   floor: float = 1e-3) -> torch.Tensor | None:
-    """Structured factor bias: each sub-goal of the factorised prompt contributes the empirical
-    distribution of its tokens (smoothed by `floor`), weighted by its length; the mixture becomes
-    an additive log-bias relative to uniform."""
-    from ..reasoning.sfb import cross_bias, factorize
-    factors = factorize(prompt_text)
-    probs, weights = [], []
-    for f in factors:
-        ids = [int(i) for i in encode_fn(f["goal"]) if 0 <= int(i) < vocab]
-        if not ids:
-            continue
-        p = torch.full((vocab,), floor / vocab)
-        p.index_add_(0, torch.tensor(ids), torch.full((len(ids),), (1.0 - floor) / len(ids)))
-        probs.append(p)
-        weights.append(float(len(ids)))
-    if not probs:
-        return None
-    return cross_bias(probs, weights, strength=strength).to(device)
+def sfb_token_bias(prompt_text: str, encode_fn, vocab: int, device, strength: float = 1.0) -> torch.Tensor | None:
+    """Structured factor bias (omnicoder.sfb.sfb_bias): the prompt is factorised, belief
+    propagation over its goal families weights each sub-goal, and the weighted token
+    distributions of the goals' strings become an additive log-bias relative to uniform."""
+    from ..sfb import sfb_bias
+    return sfb_bias(prompt_text, encode_fn, vocab, device, strength=strength)
 
 
 def adapt_moe_top_k(model, logits: torch.Tensor, k_min: int, k_max: int, conf_floor: float,

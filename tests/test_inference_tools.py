@@ -255,7 +255,7 @@ def test_addon_sfb_bias_prefers_goal_tokens():
     cfg, m = _tiny()
     enc = lambda t: [ord(c) % cfg.vocab_size for c in t]
     b = sfb_token_bias("1. compute xyz\n2. write code qq", enc, cfg.vocab_size, "cpu")
-    goal_tok = set(enc("compute xyz") + enc("write code qq"))
+    goal_tok = set(enc("compute xyz") + enc("write code qq") + enc("1") + enc("2"))   # sub-goals and entities
     inside = b[torch.tensor(sorted(goal_tok))].min()
     outside = b[torch.tensor([t for t in range(cfg.vocab_size) if t not in goal_tok])].max()
     assert inside > outside

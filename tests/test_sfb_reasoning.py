@@ -1,0 +1,76 @@
+"""Structured factor blending pipeline (factorisation, belief propagation, SPN cache, fusion,
+arbiter) and the model-driven tree / graph searches, on CPU."""
+import json
+
+import pytest
+import torch
+
+from omnicoder.sfb import (BeliefPropagation, CrossBiasFusion, ProofMarginArbiter, ProofMarginInputs, SPNCompiler,
+                           factorize_prompt, sfb_bias)
+
+
+def test_factorize_prompt_factors_and_priors():
+    r = factorize_prompt('1. Implement a python function "fib" that must run in at most 10 steps\n'
+                         "2. compute the sum of Fibonacci numbers")
+    names = {f.name for f in r.factors}
+    assert {"subgoals", "entities", "constraints"} <= names
+    goals = next(f for f in r.factors if f.name == "subgoals").meta["goals"]
+    assert [g["kind"] for g in goals] == ["code", "math"]
+    ents = next(f for f in r.factors if f.name == "entities").meta["entities"]
+    assert "fib" in ents and "10" in ents and "Fibonacci" in ents
+    assert r.goal_priors["code"] > 0.5 and r.goal_priors["math"] > 0.4
+
+
+def test_belief_propagation_coupling_and_cache():
+    r = factorize_prompt("implement python code to solve the equation")
+    bp = BeliefPropagation()
+    marg = bp.marginals(r)
+    assert set(marg) >= {"code", "math"} and all(0 < v < 1 for v in marg.values())
+    # the code-math coupling lifts both marginals above their priors
+    assert marg["code"] > r.goal_priors["code"] and marg["math"] > r.goal_priors["math"]
+    spn = SPNCompiler()
+    net = spn.maybe_compile(r)
+    assert net is spn.maybe_compile(r) and spn.lookup(r) is None
+    msgs = bp.run(r)
+    spn.register(r, msgs)
+    assert spn.lookup(r) is msgs and all({"prefer_strings", "score"} <= set(m) for m in msgs)
+
+
+def test_cross_bias_and_pipeline():
+    enc = lambda t: [ord(c) % 100 for c in t]
+    msgs = [{"prefer_strings": ["ab"], "score": 1.0}, {"prefer_strings": ["zz"], "score": 0.0}]
+    b = CrossBiasFusion(enc).bias(msgs, 100)
+    assert b[ord("a") % 100] > 0 and b[ord("z") % 100] < 0
+    full = sfb_bias("compute xyz", enc, 100)
+    assert full.shape == (100,) and full[ord("x") % 100] > full[ord("q") % 100]
+    with pytest.raises(RuntimeError):
+        CrossBiasFusion().bias(msgs, 100)
+
+
+def test_proof_margin_arbiter(tmp_path):
+    arb = ProofMarginArbiter(threshold=1.0, log_path=str(tmp_path / "log.jsonl"))
+    good = ProofMarginInputs(llm_confidence=0.9, sum_log_factors=0.2, verifier_score=0.8, retrieval_hits=2)
+    bad = ProofMarginInputs(llm_confidence=0.1, sum_log_factors=-2.0, verifier_score=0.1)
+    assert arb.compute_margin(good) == pytest.approx(1.9) and arb.accept(good) and not arb.accept(bad)
+    sug = arb.suggestions(bad)
+    assert sug["request_retrieval"] and sug["request_resolve"] and sug["bump_scmoe_topk"]
+    assert arb.suggestions(good) == {}
+    for x, y in [(good, True), (bad, False)] * 10:
+        arb.log_decision(x, y)
+    w = ProofMarginArbiter.fit_weights_from_log(str(tmp_path / "log.jsonl"))
+    assert set(w) == {"w_text", "w_code", "w_img", "w_audio", "w_video"} and w["w_text"] > 1.0
+
+
+def test_lm_tree_and_graph_search():
+    from omnicoder.config import AttentionConfig, ModelConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.reasoning.lm_search import LMAdaptiveGraph, LMToTMCTS, ToTConfig
+    from omnicoder.training.tokenizer import get_tokenizer
+    cfg = ModelConfig(name="s", vocab_size=300, d_model=32, n_layers=1, n_heads=2, ffn_dim=64, max_seq_len=64,
+                      attn=AttentionConfig(kind="mha"))
+    m = build_model(cfg, device="cpu", seed=0).eval()
+    tok = get_tokenizer(cfg.vocab_size)
+    best, st = LMToTMCTS(m, tok, ToTConfig(branch=2, max_depth=3, iterations=12, rollout=2)).search("ab")
+    assert 1 <= len(best) <= 3 and isinstance(st["text"], str)
+    out = LMAdaptiveGraph(m, k=2, thought_len=2, rounds=2, beam=1).step(torch.tensor([[5, 6, 7]]))
+    assert out.shape[1] == 3 + 4 and torch.equal(out[0, :3], torch.tensor([5, 6, 7]))
