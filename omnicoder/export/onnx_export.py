@@ -32,6 +32,10 @@ class DecodeStepWrapper(nn.Module):
             model.prepare_inference()                  # MLA: absorbed projections
 
     def forward(self, input_ids, *cache):
+        from ..ops.moe import static_shapes
+        if not self.compat:
+            with static_shapes():                      # routed experts without data-dependent shapes
+                return self._spec_step(input_ids, *cache)
         if self.compat:
             L = len(self.model.blocks)
             past = [(cache[2 * i], cache[2 * i + 1]) for i in range(L)]

@@ -83,6 +83,41 @@ def moe_ffn_torch(x, router_w, w13, w2, k, capacity, renorm, aux_alpha=0.0, z_be
     return out.to(x.dtype), aux
 
 
+_STATIC = {"on": False}
+
+
+class static_shapes:
+    """Context in which the routed experts run the static-shape formulation below (for graph
+    exporters: torch.export, ONNX), i.e. without the capacity mask's data-dependent shapes."""
+
+    def __enter__(self):
+        self.prev = _STATIC["on"]
+        _STATIC["on"] = True
+        return self
+
+    def __exit__(self, *exc):
+        _STATIC["on"] = self.prev
+        return False
+
+
+def moe_ffn_static(x, router_w, w13, w2, k, renorm, add=None):
+    """Dropless routed SwiGLU with shapes independent of the routing: every token's k expert
+    weight matrices are gathered ([T, k, 2F, D], [T, k, D, F]) and applied with batched matmuls.
+    Equal to moe_ffn_torch with capacity 0; meant for exported few-token decode steps."""
+    T, D = x.shape
+    logits = x.float() @ router_w.float().t()
+    idx, w, _ = route_torch(logits, k, renorm)
+    xe = x.float()[:, None, :, None].expand(T, k, D, 1)                       # [T, k, D, 1]
+    h = torch.matmul(w13[idx].float(), xe).squeeze(-1)                         # [T, k, 2F]
+    g, u = deinterleave_cols(h.reshape(T * k, -1))
+    a = (F.silu(g) * u).reshape(T, k, -1, 1)                                   # [T, k, F, 1]
+    y = torch.matmul(w2[idx].float(), a).squeeze(-1)                           # [T, k, D]
+    out = (y * w[..., None]).sum(1)
+    if add is not None:
+        out = out + add.float()
+    return out.to(x.dtype), x.new_zeros((), dtype=torch.float32)
+
+
 class _MoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, router_w, w13, w2, add, k, capacity, renorm, aux_alpha, z_beta, grad_scale_aux):
@@ -189,6 +224,8 @@ def moe_ffn(x: torch.Tensor, router_w: torch.Tensor, w13: torch.Tensor, w2: torc
     On CUDA the auxiliary-loss gradient (scaled by `aux_grad_scale`) is injected
     inside backward and the returned aux value is for logging; on CPU it is a
     differentiable scalar the caller adds to the loss."""
+    if _STATIC["on"]:
+        return moe_ffn_static(x, router_w, w13, w2, k, renorm, add)
     if not x.is_cuda:
         return moe_ffn_torch(x, router_w, w13, w2, k, capacity, renorm, aux_alpha, z_beta, add)
     if not (torch.is_grad_enabled() and any(t.requires_grad for t in (x, router_w, w13, w2))):

@@ -9,6 +9,9 @@ a self-describing package directory:
   * GGUF file of the same weights (f16) for llama.cpp-style runtimes;
   * ONNX decode-step graph (and an optional prefill graph) when the `onnx`
     package is installed; otherwise the manifest records why it was skipped;
+  * the decode step as a `torch.export` program and, when their packages are installed, its
+    ExecuTorch (.pte) and Core ML conversions, plus an MLC compile recipe
+    (omnicoder.export.mobile_runtimes);
   * a top-level `phone_manifest.json` with every artefact, its size and the
     model configuration.
 
@@ -25,7 +28,7 @@ import time
 
 
 def export_for_phone(model, out_dir: str, onnx: bool = True, prefill: int = 0, max_len: int = 512,
-                     gguf: bool = True) -> dict:
+                     gguf: bool = True, runtimes: bool = True) -> dict:
     """Write the package; returns the manifest (also saved as phone_manifest.json)."""
     from ..export.gguf import export_model_gguf
     from ..export.mobile_packager import package_model
@@ -53,6 +56,12 @@ def export_for_phone(model, out_dir: str, onnx: bool = True, prefill: int = 0, m
                 man["artifacts"]["onnx_prefill"] = {"file": "prefill.onnx", "bytes": os.path.getsize(p)}
         except RuntimeError as e:
             man["artifacts"]["onnx_decode_step"] = {"skipped": str(e)}
+    if runtimes:
+        from ..export.mobile_runtimes import export_all
+        try:
+            man["artifacts"]["runtimes"] = export_all(model, os.path.join(out_dir, "runtimes"), max_len=max_len)
+        except Exception as e:                 # an exporter limitation is reported, not fatal
+            man["artifacts"]["runtimes"] = {"failed": f"{type(e).__name__}: {e}"}
     with open(os.path.join(out_dir, "phone_manifest.json"), "w") as f:
         json.dump(man, f, indent=1, default=str)
     return man

@@ -2,6 +2,7 @@
 server, GGUF round trip, ONNX decode-step wrappers (numerics vs the models'
 own decode paths), decode-step session runner with KV quantisation and paging."""
 import json
+import os
 
 import pytest
 import torch
@@ -339,3 +340,25 @@ def test_onnx_wrapper_mla_prefill_and_decode_match_model():
         pos += 1
     w2, args = example_inputs(m, batch=1, max_len=16, tokens=4)
     assert args[0].shape == (1, 4) and len(args) == 2 + 2 * cfg.n_layers
+
+
+def test_static_moe_and_runtime_exports(tmp_path):
+    """The export-time routed experts (static shapes) equal the dropless torch path; the MoE decode
+    step exports as a torch.export program that reproduces the wrapper; targets without their
+    package are reported as skipped."""
+    from omnicoder.config import get_preset
+    from omnicoder.export.mobile_runtimes import export_all
+    from omnicoder.export.onnx_export import example_inputs
+    from omnicoder.ops.moe import moe_ffn_static, moe_ffn_torch
+    g = torch.Generator().manual_seed(0)
+    x, r = torch.randn(7, 64, generator=g), torch.randn(8, 64, generator=g)
+    w13, w2 = torch.randn(8, 128, 64, generator=g) * 0.1, torch.randn(8, 64, 64, generator=g) * 0.1
+    torch.testing.assert_close(moe_ffn_static(x, r, w13, w2, 2, True)[0], moe_ffn_torch(x, r, w13, w2, 2, 0, True)[0],
+                               rtol=1e-5, atol=1e-5)
+    m = build_model(get_preset("tiny_moe"), device="cpu", seed=0).eval()
+    res = export_all(m, str(tmp_path), max_len=32)
+    prog = torch.export.load(res["program"]["file"])
+    w, args = example_inputs(m, 1, 32, 1)
+    torch.testing.assert_close(prog.module()(*args)[0], w(*args)[0])
+    assert "skipped" in res["executorch"] or "file" in res["executorch"]
+    assert os.path.exists(res["mlc"]["recipe"])
