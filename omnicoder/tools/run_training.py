@@ -6,7 +6,11 @@ minute budget, `run_with_timeout`, resume by skipping finished stages, optional
 expert-parallel launch).  Stages here: `pretrain` (spec LM), `distill`
 (knowledge distillation of the draft-sized student from the pretrained model or
 a local Hugging Face teacher), `draft` (small draft model for speculative
-decoding), `export` (ONNX decode step).  Each stage
+decoding), `draft_kd` (draft pipeline: KD with LoRA, export, acceptance),
+`vl` / `vqa` (vision-language pretraining and VQA over the fusion composer), `rl`
+(GRPO on programmatic rewards), `eval` (evaluation sweep), `export` (ONNX decode
+step), `package` (on-device package).  `--smoke_one_step` runs one step of every
+requested stage (wiring check, the reference's smoke mode).  Each stage
 writes a marker file when it finishes; a rerun skips finished stages unless
 --force is given.
 """
@@ -36,8 +40,9 @@ def run_with_timeout(cmd: list[str], timeout_s: float, env=None) -> int:
 
 
 def plan(budget_minutes: float, steps_per_minute: float, stages: list[str]) -> dict:
-    """Split the budget: pretrain 80, distill 10, draft 15, export 5 (relative shares)."""
-    share = {"pretrain": 0.8, "distill": 0.1, "draft": 0.15, "export": 0.05}
+    """Split the budget by relative shares of the requested stages."""
+    share = {"pretrain": 0.8, "distill": 0.1, "draft": 0.15, "draft_kd": 0.1, "vl": 0.1, "vqa": 0.05, "rl": 0.1,
+             "eval": 0.03, "export": 0.05, "package": 0.03}
     tot = sum(share[s] for s in stages) or 1.0
     return {s: {"minutes": budget_minutes * share[s] / tot,
                 "steps": max(1, int(budget_minutes * share[s] / tot * steps_per_minute))} for s in stages}
@@ -56,12 +61,19 @@ def main(argv=None):
     ap.add_argument("--batch_size", type=int, default=4)
     ap.add_argument("--devices", default="", help="comma list of cuda devices: expert-parallel launch when > 1")
     ap.add_argument("--teacher_hf", default=None, help="distill stage: local Hugging Face causal LM directory")
+    ap.add_argument("--smoke_one_step", action="store_true", help="one step per stage (wiring check)")
+    ap.add_argument("--device", default="", help="device passed to the stages (default: their own)")
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--dry_run", action="store_true")
     a = ap.parse_args(argv)
     os.makedirs(a.out_dir, exist_ok=True)
     stages = [s for s in a.stages.split(",") if s]
     p = plan(a.budget_minutes, a.steps_per_minute, stages)
+    if a.smoke_one_step:
+        for v in p.values():
+            v["steps"] = 1
+    dev = ["--device", a.device] if a.device else []
+    ckpt = os.path.join(a.out_dir, "pretrain.pt")
     results = {}
     for s in stages:
         marker = os.path.join(a.out_dir, f".stage_{s}.done")
@@ -86,8 +98,35 @@ def main(argv=None):
                    str(a.batch_size), "--out", os.path.join(a.out_dir, "student.pt")]
             cmd += (["--teacher_hf", a.teacher_hf] if a.teacher_hf else
                     ["--teacher_ckpt", os.path.join(a.out_dir, "pretrain.pt"), "--teacher_preset", a.preset])
+        elif s == "draft_kd":
+            cmd = [sys.executable, "-m", "omnicoder.training.draft_train", "--student_preset", a.draft_preset,
+                   "--steps", str(p[s]["steps"]), "--seq_len", str(a.seq_len), "--batch_size", str(a.batch_size),
+                   "--lora", "--out_ckpt", os.path.join(a.out_dir, "draft_kd.pt"),
+                   "--out_onnx", os.path.join(a.out_dir, "draft_decode_step.onnx"),
+                   "--bench_out", os.path.join(a.out_dir, "draft_acceptance.json")] + dev
+            cmd += (["--teacher_ckpt", ckpt, "--teacher_preset", a.preset] if os.path.exists(ckpt) else
+                    ["--teacher_preset", a.preset])
+        elif s in ("vl", "vqa"):
+            cmd = [sys.executable, "-m", "omnicoder.training.vl_tasks", "--task", "vl_pretrain" if s == "vl" else "vqa",
+                   "--preset", a.preset, "--steps", str(p[s]["steps"]), "--out", os.path.join(a.out_dir, f"{s}.pt")]
+            cmd += dev
+        elif s == "rl":
+            cmd = [sys.executable, "-m", "omnicoder.training.rl", "--preset", a.preset, "--steps", str(p[s]["steps"]),
+                   "--out", os.path.join(a.out_dir, "rl.pt")] + dev
+            if os.path.exists(ckpt):
+                cmd += ["--ckpt", ckpt]
+        elif s == "eval":
+            cmd = [sys.executable, "-m", "omnicoder.eval.auto_benchmark", "--preset", a.preset, "--seq_len", "32",
+                   "--gen_tokens", "8", "--out", os.path.join(a.out_dir, "bench_summary.json")]
+            if os.path.exists(ckpt):
+                cmd += ["--ckpt", ckpt]
+            if a.device:
+                cmd += ["--device", a.device]
+        elif s == "package":
+            cmd = [sys.executable, "-m", "omnicoder.tools.export_to_phone", "--preset", a.preset, "--out",
+                   os.path.join(a.out_dir, "package")] + (["--ckpt", ckpt] if os.path.exists(ckpt) else [])
         elif s == "export":
-            cmd = [sys.executable, "-m", "omnicoder.export.onnx_export", "--ckpt", os.path.join(a.out_dir, "pretrain.pt"),
+            cmd = [sys.executable, "-m", "omnicoder.export.onnx_export", "--ckpt", ckpt,
                    "--out", os.path.join(a.out_dir, "decode_step.onnx")]
         else:
             raise SystemExit(f"unknown stage {s}")

@@ -199,3 +199,66 @@ class PPOTrainer:
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
         return {"loss": float(loss), "policy": float(pol), "value": float(vl), "reward_mean": float(r.mean())}
+
+
+# ----------------------------------------------------------------------------
+# CLI: python -m omnicoder.training.rl
+# ----------------------------------------------------------------------------
+def arithmetic_prompts(n: int, seed: int = 0) -> list[dict]:
+    """Programmatic tasks with checkable answers: "a + b =" / "a * b =" with small operands."""
+    import random
+    rng = random.Random(seed)
+    out = []
+    for _ in range(n):
+        a, b = rng.randint(0, 20), rng.randint(0, 20)
+        op = rng.choice("+*")
+        out.append({"prompt": f"{a} {op} {b} =", "answer": a + b if op == "+" else a * b})
+    return out
+
+
+def main(argv=None):
+    import argparse
+    import json
+
+    from ..config import get_preset
+    from ..models.lm import build_model
+    from .tokenizer import get_tokenizer
+    ap = argparse.ArgumentParser(description="GRPO / PPO with programmatic rewards")
+    ap.add_argument("--algo", default="grpo", choices=["grpo", "ppo"])
+    ap.add_argument("--preset", default="tiny_moe")
+    ap.add_argument("--ckpt", default="")
+    ap.add_argument("--prompts", default="", help="JSONL {prompt, answer} (default: arithmetic tasks)")
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--batch", type=int, default=2, help="prompts per step")
+    ap.add_argument("--group", type=int, default=4)
+    ap.add_argument("--max_new_tokens", type=int, default=8)
+    ap.add_argument("--lr", type=float, default=1e-5)
+    ap.add_argument("--out", default="weights/rl.pt")
+    ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    a = ap.parse_args(argv)
+    if a.ckpt:
+        from ..inference.builders import load_model
+        model, _ = load_model(a.ckpt, a.device, dtype=torch.float32, preset=a.preset)
+    else:
+        model = build_model(get_preset(a.preset), device=a.device, dtype=torch.float32, seed=0)
+    tok = get_tokenizer(model.cfg.vocab_size)
+    tasks = ([json.loads(l) for l in open(a.prompts) if l.strip()] if a.prompts else arithmetic_prompts(64))
+    if a.algo == "grpo":
+        tr = GRPOTrainer(model, lr=a.lr, group=a.group, max_new_tokens=a.max_new_tokens)
+    else:
+        tr = PPOTrainer(model, lr=a.lr, max_new_tokens=a.max_new_tokens)
+    hist = []
+    for s in range(a.steps):
+        batch = [tasks[(s * a.batch + i) % len(tasks)] for i in range(a.batch)]
+        enc = [tok.encode(t["prompt"]) for t in batch]
+        L = max(len(e) for e in enc)
+        ids = torch.tensor([[0] * (L - len(e)) + e for e in enc], device=a.device)   # left-pad to one length
+        rfn = lambda i, comp, batch=batch: reward_numeric(tok.decode(comp.tolist()), batch[i]["answer"])
+        hist.append(tr.step(ids, rfn))
+    torch.save({"model": model.export_state_dict(), "config": model.cfg.to_dict(), "step": a.steps}, a.out)
+    print(json.dumps({"steps": a.steps, "last": hist[-1] if hist else None, "out": a.out}))
+    return 0
+
+
+if __name__ == "__main__":
+    main()

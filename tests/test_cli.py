@@ -101,3 +101,21 @@ def test_auto_benchmark_sweep(tmp_path):
     assert r["mmlu"]["n"] == 6 and 0 <= r["mmlu"]["accuracy"] <= 1
     assert r["vqa_exact_match"] == 0.5 and abs(r["asr_wer"] - 1 / 3) < 1e-6 and r["perplexity"] > 1
     assert (tmp_path / "s.csv").exists()
+
+
+def test_rl_and_vl_task_clis(tmp_path):
+    from omnicoder.training import rl, vl_tasks
+    assert rl.main(["--steps", "1", "--batch", "1", "--group", "2", "--max_new_tokens", "4", "--device", "cpu",
+                    "--out", str(tmp_path / "rl.pt")]) == 0
+    assert (tmp_path / "rl.pt").exists()
+    assert vl_tasks.main(["--task", "caption", "--steps", "1", "--batch", "2", "--image_size", "32", "--device", "cpu",
+                          "--out", str(tmp_path / "vl.pt")]) == 0
+    assert (tmp_path / "vl.pt").exists()
+
+
+def test_run_training_smoke_one_step(tmp_path):
+    out = _run(["omnicoder.tools.run_training", "--stages", "vqa,rl", "--out_dir", str(tmp_path),
+                "--smoke_one_step", "--device", "cpu"])
+    summary = json.loads(out[out.rindex("{\n \"plan\""):])
+    assert all(v["steps"] == 1 for v in summary["plan"].values())
+    assert {k: v["rc"] for k, v in summary["results"].items()} == {"vqa": 0, "rl": 0}
