@@ -362,3 +362,52 @@ def test_static_moe_and_runtime_exports(tmp_path):
     torch.testing.assert_close(prog.module()(*args)[0], w(*args)[0])
     assert "skipped" in res["executorch"] or "file" in res["executorch"]
     assert os.path.exists(res["mlc"]["recipe"])
+
+
+def test_export_variants_bias_heads_multimodal_longctx(tmp_path):
+    """Export variants: the logit_bias input shifts the logits; verifier / MTP head outputs equal
+    the heads applied to the final hidden state; the multimodal prefill graph equals the model on
+    the composer's embeddings; long-context copies interpolate RoPE; the sidecars are written; the
+    variants trace under torch.export."""
+    import json as _json
+
+    from omnicoder.export.onnx_export import (DecodeStepWrapper, example_inputs, io_names, longctx_model,
+                                              multimodal_example_inputs, spec_cache_shapes, write_sidecars)
+    from omnicoder.multimodal.backbones import VisionBackbone
+    from omnicoder.multimodal.composer import FusionComposer
+    cfg = ModelConfig(name="exp_v", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      mtp_heads=2, verifier_head=True)
+    m = build_model(cfg, device="cpu", seed=0).eval()
+    ids = torch.tensor([[5, 9, 2], [8, 4, 6]])
+    cache = [torch.zeros(s) for s in spec_cache_shapes(cfg, 2, 16)]
+    base = DecodeStepWrapper(m)(ids, torch.tensor(0), *cache)
+    bias = torch.zeros(2, 300)
+    bias[:, 7] = 5.0
+    wb = DecodeStepWrapper(m, logit_bias=True, heads=True)
+    out = wb(ids, torch.tensor(0), *cache, bias)
+    torch.testing.assert_close(out[0], base[0] + bias[:, None], rtol=1e-5, atol=1e-5)
+    assert wb.head_names() == ["verifier_logits", "mtp_logits_0", "mtp_logits_1"]
+    assert len(out) == 1 + 2 * cfg.n_layers + 3
+    y = m.hidden(ids)[0].reshape(2, 3, -1)                   # final-norm hidden state of the plain forward
+    torch.testing.assert_close(out[-3], y @ m.verifier.t(), rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(out[-1], y @ m.mtp_heads[1].t(), rtol=1e-4, atol=1e-4)
+    ins, outs = io_names(cfg.n_layers, spec=True, logit_bias=True, head_names=wb.head_names())
+    assert ins[-1] == "logit_bias" and outs[-1] == "mtp_logits_1"
+    w, args = example_inputs(m, 1, 16, 1, logit_bias=True, heads=True)
+    prog = torch.export.export(w, args, strict=False)
+    torch.testing.assert_close(prog.module()(*args)[0], w(*args)[0])
+    # multimodal prefill
+    comp = FusionComposer(64, vision=VisionBackbone("vit_tiny", image_size=32, depth=1)).eval()
+    mw, margs = multimodal_example_inputs(m, comp, image_size=32, text_tokens=4)
+    got = mw(*margs)[0]
+    emb, _ = comp.fuse_all(m.embed[margs[1]], image=margs[0])
+    ref = m(None, embeds=emb, all_logits=True)["logits"]
+    torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-4)
+    # long context: positions interpolated by 32768 / 64
+    lm = longctx_model(m, 32768)
+    assert lm.cfg.attn.rope_scale == 32768 / 64 and lm.rope.max_pos == 32768 and m.cfg.attn.rope_scale == 1.0
+    torch.testing.assert_close(lm.rope.cs[:, 512], m.rope.cs[:, 1])
+    # sidecars
+    paths = write_sidecars(m, str(tmp_path / "d.onnx"), 128, kv_page_len=32, kvq="nf4")
+    meta = _json.load(open(paths[0]))
+    assert meta["pages_per_layer"] == 4 and _json.load(open(paths[1]))["bits"] == 4
