@@ -12,6 +12,10 @@ Layout (Megatron-style sequence parallelism over a group of N ranks):
   * embeddings, norms and the LM head are replicated and applied to the rank's own
     tokens; their gradients are all-reduced over the group.
 Optimiser: ``torch.optim.AdamW(fused=True)`` on fp32 master copies, global-norm clip.
+``fp8=True``: the four projections of every block run their forward and input-gradient
+GEMMs through ``torch._scaled_mm`` on e4m3 operands with row-wise scales (one fp32 scale
+per token row of the activation / gradient and per row of the weight: the plain-PyTorch
+fp8 recipe on cuBLAS); weight gradients stay bf16.
 
 Nothing here imports this package's CUDA extension.  The reference has no tensor
 parallelism (its only mention is an external vLLM argument,
@@ -73,13 +77,45 @@ def _ones(n, device, dtype):
     return p
 
 
+def _q_rows(t: torch.Tensor):
+    """e4m3 copy of t [R, C] with one fp32 scale per row (max|row| / 448)."""
+    amax = t.abs().amax(-1, keepdim=True).float().clamp_min(1e-12)
+    scale = amax / 448.0
+    return (t.float() / scale).to(torch.float8_e4m3fn), scale
+
+
+def _smm(a: torch.Tensor, b: torch.Tensor, out_dtype):
+    """a [M, K] @ b[N, K]^T with row-wise e4m3 quantisation of both operands."""
+    aq, sa = _q_rows(a)
+    bq, sb = _q_rows(b)
+    return torch._scaled_mm(aq, bq.t(), scale_a=sa, scale_b=sb.t(), out_dtype=out_dtype)
+
+
+class _Fp8Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w):
+        ctx.save_for_backward(x, w)
+        return _smm(x, w, x.dtype)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dy = dy.contiguous()
+        return _smm(dy, w.t().contiguous(), dy.dtype), dy.t() @ x
+
+
+def _linear(x, w, fp8: bool):
+    return _Fp8Linear.apply(x, w) if fp8 else F.linear(x, w)
+
+
 class _Block(nn.Module):
-    def __init__(self, cfg: ModelConfig, n: int, device, dtype):
+    def __init__(self, cfg: ModelConfig, n: int, device, dtype, fp8: bool = False):
         super().__init__()
         D, H, Hk, hd, Fd, s = cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim, cfg.init_std
         if H % n or Hk % n or Fd % n:
             raise ValueError("heads, kv heads and the ffn dim must divide by the tensor-parallel size")
         self.h, self.hk, self.hd, self.eps = H // n, Hk // n, hd, cfg.norm_eps
+        self.fp8 = fp8
         self.n1 = _ones(D, device, dtype)
         self.wqkv = _p(((self.h + 2 * self.hk) * hd, D), s, device, dtype, True)
         self.wo = _p((D, self.h * hd), s, device, dtype, True)
@@ -93,7 +129,7 @@ class _Block(nn.Module):
         rs = (lambda t: _RS.apply(t, group, n)) if n > 1 else (lambda t: t)
         y = ag(F.rms_norm(h, (D,), self.n1, self.eps))
         T = y.shape[0]
-        qkv = F.linear(y, self.wqkv).view(T, self.h + 2 * self.hk, self.hd)
+        qkv = _linear(y, self.wqkv, self.fp8).view(T, self.h + 2 * self.hk, self.hd)
         qk = qkv[:, :self.h + self.hk]
         half = self.hd // 2
         q0, q1 = qk[..., :half], qk[..., half:]
@@ -102,17 +138,18 @@ class _Block(nn.Module):
         k = qk[:, self.h:].view(B, S, self.hk, self.hd).transpose(1, 2)
         v = qkv[:, self.h + self.hk:].reshape(B, S, self.hk, self.hd).transpose(1, 2)
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=self.hk != self.h)
-        h = h + rs(F.linear(o.transpose(1, 2).reshape(T, self.h * self.hd), self.wo))
+        h = h + rs(_linear(o.transpose(1, 2).reshape(T, self.h * self.hd), self.wo, self.fp8))
         y = ag(F.rms_norm(h, (D,), self.n2, self.eps))
-        g = F.linear(y, self.w13)
+        g = _linear(y, self.w13, self.fp8)
         f = g.shape[-1] // 2
-        return h + rs(F.linear(F.silu(g[:, :f]) * g[:, f:], self.w2))
+        return h + rs(_linear(F.silu(g[:, :f]) * g[:, f:], self.w2, self.fp8))
 
 
 class TorchDenseTPLM(nn.Module):
     """Dense GQA LM (RMSNorm, RoPE, SwiGLU, untied head) with tensor + sequence parallelism."""
 
-    def __init__(self, cfg: ModelConfig, device, group=None, dtype=torch.bfloat16, seed: int = 1234):
+    def __init__(self, cfg: ModelConfig, device, group=None, dtype=torch.bfloat16, seed: int = 1234,
+                 fp8: bool = False):
         super().__init__()
         torch.manual_seed(seed)
         if str(device).startswith("cuda"):
@@ -122,7 +159,7 @@ class TorchDenseTPLM(nn.Module):
         self.rank = dist.get_rank(group) if group is not None else 0
         D, V = cfg.d_model, cfg.vocab_size
         self.embed = _p((V, D), cfg.init_std, device, dtype)
-        self.blocks = nn.ModuleList([_Block(cfg, self.n, device, dtype) for _ in range(cfg.n_layers)])
+        self.blocks = nn.ModuleList([_Block(cfg, self.n, device, dtype, fp8) for _ in range(cfg.n_layers)])
         self.nf = _ones(D, device, dtype)
         self.head = _p((V, D), cfg.init_std, device, dtype)
         hd = cfg.head_dim

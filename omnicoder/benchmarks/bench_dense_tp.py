@@ -2,7 +2,7 @@
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \\
         -m omnicoder.benchmarks.bench_dense_tp [--global-batch 64] [--steps 2 --warmup 1] \\
-        [--transport nccl|p2p] [--arms ours,baseline] [--layers 48] [--pp P]
+        [--transport nccl|p2p] [--arms ours,baseline] [--layers 48] [--pp P] [--fp8]
 
 Model: dense_20b (48 layers, d_model 6144, 48 query / 8 KV heads of 128, SwiGLU 16384,
 vocab 32000), sequence 8192, random N(0, 0.02) weights, uniform random token ids; bf16
@@ -16,6 +16,9 @@ Arms (same data, same step):
             flash attention; "p2p": the fused peer-memory all-gather -> GEMM and GEMM ->
             reduce-scatter collectives);
   baseline  plain PyTorch + NCCL + cuBLAS (omnicoder.baselines.torch_tp).
+`--fp8`: the block projections' forward and input-gradient GEMMs in fp8 -- ours with
+1 x 128 / 128 x 128 block scales (power-of-two, applied by the tensor core), the baseline
+with row-wise scales through torch._scaled_mm; weight gradients bf16 in both.
 `--pp P` runs the second layout instead: P pipeline stages (1F1B over NCCL point-to-point,
 omnicoder.parallel.pipeline) x tensor parallel N / P inside each stage (rank = stage x TP +
 tp rank), the global batch split into micro-batches of one sequence; only this package's arm.
@@ -61,6 +64,7 @@ def main(argv=None):
     ap.add_argument("--arms", default="ours,baseline")
     ap.add_argument("--json", default=None)
     ap.add_argument("--pp", type=int, default=1, help="pipeline stages (tensor parallel = N / pp inside each)")
+    ap.add_argument("--fp8", action="store_true", help="block-scaled fp8 projections (forward and dgrad GEMMs)")
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -91,7 +95,7 @@ def main(argv=None):
         tp_groups = [dist.new_group(list(range(s_ * T, (s_ + 1) * T))) for s_ in range(a.pp)]
         pp_groups = [dist.new_group(list(range(t_, world, T))) for t_ in range(T)]
         stage, t = rank // T, rank % T
-        par = TensorParallel(tp_groups[stage], transport=a.transport) if T > 1 else None
+        par = TensorParallel(tp_groups[stage], transport=a.transport, fp8=a.fp8) if T > 1 else None
         model = build_model(cfg, device=dev, seed=1234, tp=par)
         pt = PipelineTrainer(model, tcfg, group=pp_groups[t], n_micro=G, tp=par)
         del model
@@ -106,13 +110,13 @@ def main(argv=None):
             from omnicoder.models.lm import build_model
             from omnicoder.parallel.tensor import TensorParallel
             from omnicoder.training.engine import Trainer
-            par = TensorParallel(dist.group.WORLD, transport=a.transport)
+            par = TensorParallel(dist.group.WORLD, transport=a.transport, fp8=a.fp8)
             model = build_model(cfg, device=dev, seed=1234, tp=par)
             tr = Trainer(model, tcfg, par)
             step = lambda i, l: tr.step(i, l, assume_all_valid=True).loss
         elif arm == "baseline":
             from omnicoder.baselines.torch_tp import TorchDenseTPLM, TorchTPTrainer
-            model = TorchDenseTPLM(cfg, dev, dist.group.WORLD, seed=1234)
+            model = TorchDenseTPLM(cfg, dev, dist.group.WORLD, seed=1234, fp8=a.fp8)
             tr = TorchTPTrainer(model, tcfg)
             step = tr.step
         else:
@@ -131,7 +135,9 @@ def main(argv=None):
         out = {"bench": "dense 20B training step, tensor + sequence parallel", "n_gpus": world,
                "parallelism": (f"pp{a.pp}xtp{world // a.pp}+sp" if a.pp > 1 else f"tp{world}+sp"),
                "transport": a.transport, "model": f"{cfg.name} {cfg.n_layers}L",
-               "global_batch": G, "seq_len": S, "dtype": "bf16 (fp32 master weights, AdamW)",
+               "global_batch": G, "seq_len": S,
+               "dtype": ("fp8 e4m3 projections (fprop + dgrad), bf16 elsewhere" if a.fp8 else "bf16")
+               + " (fp32 master weights, AdamW)",
                "data": "synthetic (uniform random token ids, random-init N(0,0.02))",
                "train_gflop_per_token": fpt / 1e9, "arms": res}
         if "ours" in res and "baseline" in res:

@@ -262,7 +262,7 @@ void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
 // ---------------------------------------------------------------------------
 // Block-scaled fp8 (1 x 128 activation scales, 128 x 128 weight scales)
 // ---------------------------------------------------------------------------
-std::vector<at::Tensor> fp8_quant_act_t(const at::Tensor& x) {
+std::vector<at::Tensor> fp8_quant_act_t(const at::Tensor& x, bool pow2) {
   CHECK_CUDA_T(x);
   CHECK_BF16(x);
   CHECK_ROWMAJOR(x);
@@ -271,12 +271,12 @@ std::vector<at::Tensor> fp8_quant_act_t(const at::Tensor& x) {
   const int64_t M = x.size(0), K = x.size(1), Mp = (M + 127) / 128 * 128;
   auto xq = at::empty({M, K}, x.options().dtype(at::kFloat8_e4m3fn));
   auto sx = at::empty({K / 128, Mp}, x.options().dtype(at::kFloat));
-  fp8_quant_act(x.data_ptr(), x.stride(0), (int)M, (int)K, xq.data_ptr(), sx.data_ptr<float>(), Mp, cur_stream());
+  fp8_quant_act(x.data_ptr(), x.stride(0), (int)M, (int)K, xq.data_ptr(), sx.data_ptr<float>(), Mp, pow2, cur_stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {xq, sx};
 }
 
-std::vector<at::Tensor> fp8_quant_weight_t(const at::Tensor& w) {
+std::vector<at::Tensor> fp8_quant_weight_t(const at::Tensor& w, bool pow2) {
   CHECK_CUDA_T(w);
   CHECK_BF16(w);
   TORCH_CHECK(w.is_contiguous() && (w.dim() == 2 || w.dim() == 3), "fp8_quant_weight: contiguous [N, K] or [G, N, K]");
@@ -285,7 +285,7 @@ std::vector<at::Tensor> fp8_quant_weight_t(const at::Tensor& w) {
   TORCH_CHECK(K % 128 == 0, "fp8_quant_weight: K % 128 == 0");
   auto wq = at::empty_like(w, w.options().dtype(at::kFloat8_e4m3fn));
   auto sw = at::empty({G, (N + 127) / 128, K / 128}, w.options().dtype(at::kFloat));
-  fp8_quant_weight(w.data_ptr(), (int)G, (int)N, (int)K, wq.data_ptr(), sw.data_ptr<float>(), cur_stream());
+  fp8_quant_weight(w.data_ptr(), (int)G, (int)N, (int)K, wq.data_ptr(), sw.data_ptr<float>(), pow2, cur_stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {wq, sw};
 }
@@ -293,7 +293,7 @@ std::vector<at::Tensor> fp8_quant_weight_t(const at::Tensor& w) {
 // C [M, N] bf16 = fp8 GEMM; grouped when offsets is given (wq [G, N, K], offsets int32 [G+1],
 // multiples of 128, rows = allocated rows of xq).
 void fp8_gemm_t(const at::Tensor& xq, const at::Tensor& sx, const at::Tensor& wq, const at::Tensor& sw, at::Tensor& C,
-                const c10::optional<at::Tensor>& offsets, int64_t max_rows) {
+                const c10::optional<at::Tensor>& offsets, int64_t max_rows, bool scaled_mma) {
   CHECK_CUDA_T(xq);
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn,
               "fp8_gemm: e4m3 operands");
@@ -333,6 +333,70 @@ void fp8_gemm_t(const at::Tensor& xq, const at::Tensor& sx, const at::Tensor& wq
     TORCH_CHECK(sw.numel() == (long long)((d.N + 127) / 128) * (d.K / 128), "fp8_gemm: sw shape");
   }
   d.status = status_ptr();
+  d.scaled_mma = scaled_mma;
+  fp8_gemm_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Block-scaled fp8 gate|up GEMM with the SwiGLU + requantisation epilogue: H [rows, N] bf16
+// pre-activation, act [rows, N/2] bf16 (optional), actq [rows, N/2] e4m3 and act_scale fp32
+// [N/256, rows padded to 128] for the down GEMM.  Grouped when offsets is given.
+void fp8_gemm_swiglu_q_t(const at::Tensor& xq, const at::Tensor& sx, const at::Tensor& wq, const at::Tensor& sw,
+                         const c10::optional<at::Tensor>& H, const c10::optional<at::Tensor>& act, at::Tensor& actq,
+                         at::Tensor& act_scale, const c10::optional<at::Tensor>& offsets, int64_t max_rows) {
+  CHECK_CUDA_T(xq);
+  TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn &&
+                  actq.scalar_type() == at::kFloat8_e4m3fn, "fp8_gemm_swiglu_q: e4m3 operands / output");
+  TORCH_CHECK(sx.scalar_type() == at::kFloat && sw.scalar_type() == at::kFloat && act_scale.scalar_type() == at::kFloat &&
+                  sx.is_contiguous() && sw.is_contiguous() && act_scale.is_contiguous(), "fp8_gemm_swiglu_q: fp32 scales");
+  CHECK_ROWMAJOR(xq);
+  CHECK_ROWMAJOR(actq);
+  TORCH_CHECK(wq.is_contiguous(), "fp8_gemm_swiglu_q: contiguous weights");
+  const c10::cuda::CUDAGuard guard(xq.device());
+  Fp8GemmDesc d;
+  d.M = (int)xq.size(0);
+  d.K = (int)xq.size(1);
+  d.N = (int)wq.size(-2);
+  TORCH_CHECK(wq.size(-1) == d.K && d.K % 128 == 0 && d.N % 256 == 0, "fp8_gemm_swiglu_q: K % 128, N % 256");
+  TORCH_CHECK(sx.dim() == 2 && sx.size(0) == d.K / 128 && sx.size(1) >= (d.M + 127) / 128 * 128, "fp8_gemm_swiglu_q: sx");
+  TORCH_CHECK(actq.size(0) == d.M && actq.size(1) == d.N / 2 && actq.stride(0) % 16 == 0, "fp8_gemm_swiglu_q: actq");
+  TORCH_CHECK(act_scale.dim() == 2 && act_scale.size(0) == d.N / 256 && act_scale.size(1) >= (d.M + 127) / 128 * 128,
+              "fp8_gemm_swiglu_q: act_scale [N/256, rows padded to 128]");
+  d.X = xq.data_ptr();
+  d.ldx = xq.stride(0);
+  d.sx = sx.data_ptr<float>();
+  d.ldsx = sx.size(1);
+  d.W = wq.data_ptr();
+  d.ldw = d.K;
+  d.sw = sw.data_ptr<float>();
+  if (H.has_value()) {
+    CHECK_BF16(*H);
+    CHECK_ROWMAJOR(*H);
+    TORCH_CHECK(H->size(0) == d.M && H->size(1) == d.N && H->stride(0) % 8 == 0, "fp8_gemm_swiglu_q: H");
+    d.C = H->data_ptr();
+    d.ldc = H->stride(0);
+  }
+  if (act.has_value()) {
+    CHECK_BF16(*act);
+    CHECK_ROWMAJOR(*act);
+    TORCH_CHECK(act->size(0) == d.M && act->size(1) == d.N / 2 && act->stride(0) % 8 == 0, "fp8_gemm_swiglu_q: act");
+    d.act = act->data_ptr();
+    d.ld_act = act->stride(0);
+  }
+  d.actq = actq.data_ptr();
+  d.ld_actq = actq.stride(0);
+  d.act_scale = act_scale.data_ptr<float>();
+  d.ld_as = act_scale.size(1);
+  if (offsets.has_value()) {
+    TORCH_CHECK(wq.dim() == 3 && offsets->scalar_type() == at::kInt && offsets->numel() == wq.size(0) + 1,
+                "fp8_gemm_swiglu_q: grouped needs wq [G, N, K] and int32 offsets [G+1]");
+    d.G = (int)wq.size(0);
+    d.offsets = offsets->data_ptr<int>();
+    d.w_group_stride = (long long)d.N * d.K;
+    d.max_rows_hint = (int)max_rows;
+  }
+  d.status = status_ptr();
+  d.scaled_mma = true;
   fp8_gemm_launch(d, cur_stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -513,10 +577,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("me"), py::arg("b_mn"), py::arg("block_n") = 256);
   m.def("peer_copy", &omni::peer_copy, py::arg("dst"), py::arg("src"), py::arg("nbytes"));
   m.def("tp_reduce", &omni::tp_reduce, py::arg("staging"), py::arg("out"), py::arg("residual") = py::none());
-  m.def("fp8_quant_act", &omni::fp8_quant_act_t, "bf16 [M, K] -> (e4m3 [M, K], fp32 scales [K/128, M padded to 128])");
-  m.def("fp8_quant_weight", &omni::fp8_quant_weight_t, "bf16 [(G,) N, K] -> (e4m3, fp32 scales [G, N/128, K/128])");
+  m.def("fp8_quant_act", &omni::fp8_quant_act_t, "bf16 [M, K] -> (e4m3 [M, K], fp32 scales [K/128, M padded to 128])",
+        py::arg("x"), py::arg("pow2") = true);
+  m.def("fp8_quant_weight", &omni::fp8_quant_weight_t, "bf16 [(G,) N, K] -> (e4m3, fp32 scales [G, N/128, K/128])",
+        py::arg("w"), py::arg("pow2") = true);
   m.def("fp8_gemm", &omni::fp8_gemm_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"), py::arg("C"),
-        py::arg("offsets") = py::none(), py::arg("max_rows") = 0);
+        py::arg("offsets") = py::none(), py::arg("max_rows") = 0, py::arg("scaled_mma") = true);
+  m.def("fp8_gemm_swiglu_q", &omni::fp8_gemm_swiglu_q_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"),
+        py::arg("H"), py::arg("act"), py::arg("actq"), py::arg("act_scale"), py::arg("offsets") = py::none(),
+        py::arg("max_rows") = 0);
   m.def("gemm_skinny_grouped", &omni::gemm_skinny_grouped, py::arg("A"), py::arg("B"), py::arg("offsets"),
         py::arg("C"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("rows") = 0);
   m.def("set_skinny_rows", &omni::set_skinny_rows, "rows up to which dense GEMMs use the few-row kernel (0: off)");

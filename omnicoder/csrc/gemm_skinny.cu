@@ -10,8 +10,8 @@
 // (tcgen05 M = 128 weight rows, N = the group's token count rounded up to 16,
 // K = 64 per pipeline stage), so every CTA streams a 128-row slab of W through
 // an 8-stage TMA ring while the token rows ride along as the small operand.
-// Work units are (group, 128-row slab, K split); the split count is chosen so
-// the persistent grid covers every SM.  Each unit adds its fp32 partial sums
+// Work units are (group, 128-row slab, K split); the split count is the largest
+// that keeps the units within one wave of the persistent grid.  Each unit adds its fp32 partial sums
 // into acc[rows, N] (red.global.add, one warp writes 32 consecutive columns of
 // one row per instruction); skinny_finalize applies the epilogue (bf16 / fp32 /
 // + residual / SwiGLU of the 32-interleaved gate|up columns).
@@ -297,7 +297,10 @@ int skinny_ksplit(const SkinnyDesc& d) {
   const int nkb = (d.K + 63) / 64;
   const int base = (d.offsets != nullptr ? d.G : 1) * nt;
   const int sms = num_sms();
-  int ks = (2 * sms + base - 1) / base;
+  // At most one wave of units: a slab streams fast enough that ~half the SMs saturate HBM, so
+  // extra K splits only add fp32 partial-sum traffic (red.global) and a ragged last wave.  With
+  // at least 3/4 of an SM's worth of slabs there is no split (direct bf16 epilogue, no workspace).
+  int ks = base * 4 >= sms * 3 ? 1 : std::max(1, sms / base);
   ks = std::max(1, std::min(ks, std::max(1, nkb / 4)));
   const int kb_per = (nkb + ks - 1) / ks;
   return (nkb + kb_per - 1) / kb_per;

@@ -108,12 +108,26 @@ struct Fp8GemmDesc {
   long long ldc = 0;
   long long rows_c = 0;  // rows of C (0: M); grouped-M outputs are as tall as A
   void* status = nullptr;
+  // every scale a power of two: the tensor core applies them (block-scaled MMA, 128 x 256 tiles);
+  // otherwise the epilogue promotes each K block's partial product with its fp32 scales
+  bool scaled_mma = false;
+  // SwiGLU + requantisation epilogue (scaled_mma, N % 256 == 0, W rows 32-interleaved gate|up):
+  // C <- gate|up pre-activation; act (optional) <- silu(g) * u bf16 [rows, N/2]; actq <- the
+  // same in e4m3 with act_scale fp32 [N/256][ld_as] (power-of-two 1 x 128 block scales)
+  void* act = nullptr;
+  long long ld_act = 0;
+  void* actq = nullptr;
+  long long ld_actq = 0;
+  float* act_scale = nullptr;
+  long long ld_as = 0;
 };
 void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream);
-// x [M, K] bf16 -> xq e4m3 [M, K], sx fp32 [K/128][ldsx] (rows >= M zero-filled up to ldsx)
-void fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sx, long long ldsx, cudaStream_t s);
+// x [M, K] bf16 -> xq e4m3 [M, K], sx fp32 [K/128][ldsx] (rows >= M zero-filled up to ldsx);
+// pow2: scales rounded up to powers of two
+void fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sx, long long ldsx, bool pow2,
+                   cudaStream_t s);
 // w [G, N, K] bf16 -> wq e4m3, sw fp32 [G][ceil(N/128)][K/128]
-void fp8_quant_weight(const void* w, int G, int N, int K, void* wq, float* sw, cudaStream_t s);
+void fp8_quant_weight(const void* w, int G, int N, int K, void* wq, float* sw, bool pow2, cudaStream_t s);
 
 // ---- few-row GEMM (decode, speculative verification) --------------------------
 // Y[rows, N] = X[rows, K] W[N, K]^T for at most kSkinnyMaxRows rows per group

@@ -113,6 +113,18 @@ class GQAttention(nn.Module):
             q, k, v = qkv[:, :self.H], qkv[:, self.H:self.H + self.Hk], qkv[:, self.H + self.Hk:]
             o = attention(q, k, v, None, seq=seq, causal=True, window=self.cfg.attn.window)
             return tp_linear_rs(o.reshape(T, -1), self.wo, self.tp, residual=h)
+        if self.tp is not None and getattr(self.tp, "fp8", False):
+            # block-scaled fp8 projections (fprop and dgrad), NCCL sequence-parallel collectives
+            from ..ops.fp8 import fp8_linear
+            from ..parallel.tensor import all_gather_seq, reduce_scatter_seq
+            yf = all_gather_seq(y, self.tp)
+            T = yf.shape[0]
+            qkv = fp8_linear(yf, self.wqkv).view(T, self.H + 2 * self.Hk, self.hd)
+            qkv = apply_rope(qkv, rope, positions, off=0, interleaved=self.cfg.attn.rope_interleaved,
+                             heads=self.H + self.Hk)
+            q, k, v = qkv[:, :self.H], qkv[:, self.H:self.H + self.Hk], qkv[:, self.H + self.Hk:]
+            o = attention(q, k, v, None, seq=seq, causal=True, window=self.cfg.attn.window)
+            return reduce_scatter_seq(fp8_linear(o.reshape(T, -1), self.wo), self.tp) + h
         if self.tp is not None:
             from ..parallel.tensor import all_gather_seq, reduce_scatter_seq
             yf = all_gather_seq(y, self.tp)
@@ -242,6 +254,10 @@ class DenseFFN(nn.Module):
             return tp_swiglu_mlp(y, self.w13, self.w2, self.tp, residual=h), None
         if self.tp is not None:
             from ..parallel.tensor import all_gather_seq, reduce_scatter_seq
+            if getattr(self.tp, "fp8", False):
+                from ..ops.fp8 import fp8_swiglu_mlp
+                return reduce_scatter_seq(fp8_swiglu_mlp(all_gather_seq(y, self.tp), self.w13, self.w2),
+                                          self.tp) + h, None
             return reduce_scatter_seq(swiglu_mlp(all_gather_seq(y, self.tp), self.w13, self.w2), self.tp) + h, None
         return swiglu_mlp(y, self.w13, self.w2, residual=h), None
 

@@ -55,6 +55,10 @@ class FusedAdamW:
         self.step_count += 1
         t = self.step_count
         b1, b2 = self.betas
+        # the kernels below write the parameters in place without moving their version
+        # counters: quantised weight copies (fp8 projections) are redone after this step
+        from .fp8 import WEIGHTS
+        WEIGHTS.bump()
         cuda = len(self.params) > 0 and self.params[0].is_cuda
         if cuda:
             C = _ext.load()

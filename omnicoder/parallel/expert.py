@@ -286,11 +286,9 @@ class _EPMoEP2P(torch.autograd.Function):
         if q13 is not None and q2 is not None:
             # block-scaled fp8 expert GEMMs (weights quantised once per optimiser step by the
             # caller; activations per 1 x 128 block here); backward uses the bf16 weights
-            from ..ops.fp8 import fp8_grouped_mm, quantize_act
-            H = fp8_grouped_mm(x_recv, q13[0], q13[1], offs_local, R)
-            g, u = deinterleave_cols(H)
-            act = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
-            aq, sa = quantize_act(act)
+            from ..ops.fp8 import fp8_grouped_swiglu
+            # SwiGLU and the requantisation of its output run in the gate|up GEMM's epilogue
+            H, act, aq, sa = fp8_grouped_swiglu(x_recv, q13[0], q13[1], offs_local, R)
             C.fp8_gemm(aq, sa, q2[0], q2[1].reshape(-1), y_recv, offs_local, R)
         else:
             act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)
@@ -387,11 +385,9 @@ class _EPMoEDev(torch.autograd.Function):
         q13 = ep.fp8_weights.get(id(w13)) if ep.fp8_weights else None
         q2 = ep.fp8_weights.get(id(w2)) if ep.fp8_weights else None
         if q13 is not None and q2 is not None:
-            from ..ops.fp8 import fp8_grouped_mm, quantize_act
-            H = fp8_grouped_mm(x_recv, q13[0], q13[1], offs_local, R)
-            g, u = deinterleave_cols(H)
-            act = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
-            aq, sa = quantize_act(act)
+            from ..ops.fp8 import fp8_grouped_swiglu
+            # SwiGLU and the requantisation of its output run in the gate|up GEMM's epilogue
+            H, act, aq, sa = fp8_grouped_swiglu(x_recv, q13[0], q13[1], offs_local, R)
             C.fp8_gemm(aq, sa, q2[0], q2[1].reshape(-1), y_recv, offs_local, R)
         else:
             act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)

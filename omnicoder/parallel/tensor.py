@@ -35,7 +35,10 @@ class TPContext:
     the reduce-scatter by the producing GEMM's epilogue (partial tiles stored
     into the row owner's staging slots, then summed locally)."""
 
-    def __init__(self, group=None, transport: str = "nccl", arena_bytes: int = 64 << 20):
+    def __init__(self, group=None, transport: str = "nccl", arena_bytes: int = 64 << 20, fp8: bool = False):
+        if fp8 and transport != "nccl":
+            raise ValueError("fp8 tensor-parallel projections run with the nccl transport")
+        self.fp8 = fp8                          # block-scaled fp8 fprop / dgrad GEMMs in the sharded projections
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
@@ -313,8 +316,8 @@ class TensorParallel:
     all-reduce of the replicated ones over the TP group (bucketed, one NCCL call
     per bucket)."""
 
-    def __init__(self, group=None, bucket_bytes: int = 64 << 20, transport: str = "nccl"):
-        self.tp = TPContext(group, transport=transport)
+    def __init__(self, group=None, bucket_bytes: int = 64 << 20, transport: str = "nccl", fp8: bool = False):
+        self.tp = TPContext(group, transport=transport, fp8=fp8)
         self.group, self.rank, self.world = self.tp.group, self.tp.rank, self.tp.world
         self.bucket_bytes = bucket_bytes
 
