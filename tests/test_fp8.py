@@ -188,8 +188,10 @@ def test_fp8_grouped_swiglu_epilogue():
     from omnicoder.ops import _ext
     y = torch.empty(rows, 256, device="cuda", dtype=torch.bfloat16)
     _ext.load().fp8_gemm(aq, sa, q2, s2.reshape(-1), y, off, rows)
-    y_ref = fp8.fp8_grouped_mm(act, q2, s2, off, rows)
-    assert _rowrel(y, y_ref) < 3e-2
+    # reference: the same quantised operands, dequantised, in fp32
+    ad, wd = fp8.dequantize_act(aq, sa), fp8.dequantize_weight(q2, s2)
+    y_ref = torch.cat([ad[int(off[g]):int(off[g + 1])] @ wd[g].t() for g in range(G)])
+    assert _rowrel(y, y_ref) < 2e-2
 
 
 def test_weight_cache_redone_after_optimiser_step():
@@ -215,11 +217,21 @@ def test_fp8_swiglu_mlp_fused_matches_fp32():
     g = torch.randn_like(y)
     y.backward(g)
     from omnicoder.ops.gemm import deinterleave_cols
+    # the same chain of quantisations emulated in fp32: tight agreement
+    xq, sx = fp8.quantize_act_torch(x.detach())
+    q13, s13 = fp8.quantize_weight_torch(w13.detach())
+    q2, s2 = fp8.quantize_weight_torch(w2.detach())
+    ge, ue = deinterleave_cols(fp8.dequantize_act(xq, sx) @ fp8.dequantize_weight(q13, s13).t())
+    aq, sa = fp8.quantize_act_torch(torch.nn.functional.silu(ge) * ue)
+    y_emul = fp8.dequantize_act(aq, sa) @ fp8.dequantize_weight(q2, s2).t()
+    assert _rowrel(y.detach(), y_emul) < 2e-2
+    # and the full-precision MLP within the fp8 quantisation error
     xr, ar, br = (t.detach().float().requires_grad_() for t in (x, w13, w2))
     gg, uu = deinterleave_cols(xr @ ar.t())
     yr = (torch.nn.functional.silu(gg) * uu) @ br.t()
     yr.backward(g.float())
-    assert _rowrel(y.detach(), yr.detach()) < 0.1
+    assert _rel(y.detach(), yr.detach()) < 0.1
+    assert ((y.detach().float() - yr).abs().mean() / yr.abs().mean()).item() < 0.05
     assert _rel(x.grad, xr.grad) < 0.1
     assert _rel(w13.grad, ar.grad) < 0.1
     assert _rel(w2.grad, br.grad) < 0.1
