@@ -290,10 +290,25 @@ std::vector<at::Tensor> fp8_quant_weight_t(const at::Tensor& w, bool pow2) {
   return {wq, sw};
 }
 
+std::vector<at::Tensor> fp8_quant_t_t(const at::Tensor& x) {
+  CHECK_CUDA_T(x);
+  CHECK_BF16(x);
+  CHECK_ROWMAJOR(x);
+  TORCH_CHECK(x.dim() == 2 && x.size(0) % 128 == 0 && x.size(1) % 8 == 0,
+              "fp8_quant_t: x [T, C] with T % 128 == 0 and C % 8 == 0");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0), Cn = x.size(1), Cp = (Cn + 255) / 256 * 256;  // A or per-row B scales
+  auto xt = at::empty({Cn, T}, x.options().dtype(at::kFloat8_e4m3fn));
+  auto st = at::ones({T / 128, Cp}, x.options().dtype(at::kFloat));
+  fp8_quant_t(x.data_ptr(), x.stride(0), (int)T, (int)Cn, xt.data_ptr(), T, st.data_ptr<float>(), Cp, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {xt, st};
+}
+
 // C [M, N] bf16 = fp8 GEMM; grouped when offsets is given (wq [G, N, K], offsets int32 [G+1],
 // multiples of 128, rows = allocated rows of xq).
 void fp8_gemm_t(const at::Tensor& xq, const at::Tensor& sx, const at::Tensor& wq, const at::Tensor& sw, at::Tensor& C,
-                const c10::optional<at::Tensor>& offsets, int64_t max_rows, bool scaled_mma) {
+                const c10::optional<at::Tensor>& offsets, int64_t max_rows, bool scaled_mma, bool sw_rows) {
   CHECK_CUDA_T(xq);
   TORCH_CHECK(xq.scalar_type() == at::kFloat8_e4m3fn && wq.scalar_type() == at::kFloat8_e4m3fn,
               "fp8_gemm: e4m3 operands");
@@ -329,6 +344,10 @@ void fp8_gemm_t(const at::Tensor& xq, const at::Tensor& sx, const at::Tensor& wq
     d.w_group_stride = (long long)d.N * d.K;
     d.max_rows_hint = (int)max_rows;
     TORCH_CHECK(sw.numel() == (long long)d.G * ((d.N + 127) / 128) * (d.K / 128), "fp8_gemm: sw shape");
+  } else if (sw_rows) {
+    TORCH_CHECK(sw.dim() == 2 && sw.size(0) == d.K / 128 && sw.size(1) >= (d.N + 255) / 256 * 256,
+                "fp8_gemm: per-row sw [K/128, >= N rounded up to 256]");
+    d.ldsw = sw.size(1);
   } else {
     TORCH_CHECK(sw.numel() == (long long)((d.N + 127) / 128) * (d.K / 128), "fp8_gemm: sw shape");
   }
@@ -582,7 +601,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quant_weight", &omni::fp8_quant_weight_t, "bf16 [(G,) N, K] -> (e4m3, fp32 scales [G, N/128, K/128])",
         py::arg("w"), py::arg("pow2") = true);
   m.def("fp8_gemm", &omni::fp8_gemm_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"), py::arg("C"),
-        py::arg("offsets") = py::none(), py::arg("max_rows") = 0, py::arg("scaled_mma") = true);
+        py::arg("offsets") = py::none(), py::arg("max_rows") = 0, py::arg("scaled_mma") = true,
+        py::arg("sw_rows") = false);
+  m.def("fp8_quant_t", &omni::fp8_quant_t_t, "bf16 [T, C] -> (e4m3 [C, T], fp32 scales [T/128, C padded to 256])");
   m.def("fp8_gemm_swiglu_q", &omni::fp8_gemm_swiglu_q_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"),
         py::arg("H"), py::arg("act"), py::arg("actq"), py::arg("act_scale"), py::arg("offsets") = py::none(),
         py::arg("max_rows") = 0);

@@ -65,6 +65,7 @@ struct F8Args {
   const float* sx;
   long long ldsx;
   const float* sw;
+  long long ldsw;  // > 0: per-row B scales sw[kb][n] (row stride ldsw) instead of 128 x 128 blocks
   bf16* C;
   long long ldc;
   StatusBlock* status;
@@ -488,13 +489,21 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const float* sxk = p.sx + (long long)kb * p.ldsx + ti.m0 + lane;
 #pragma unroll
         for (int j = 0; j < 4; ++j) a[j] = ue8m0_x4(__ldg(sxk + 32 * j));
-        const uint32_t w0 = ue8m0_x4(__ldg(swp + (long long)nb0 * nkb + kb));
-        const uint32_t w1 = ue8m0_x4(__ldg(swp + (long long)nb1 * nkb + kb));
+        if (p.ldsw > 0) {
+          // per-row B scales (both operands quantised per row and 128-wide K block)
+          const float* swk = p.sw + (long long)kb * p.ldsw + ti.n0 + lane;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          if (j >= 4) a[j] = 0u;
-          b[j] = j < 4 ? w0 : (j < 8 ? w1 : 0u);
+          for (int j = 0; j < 8; ++j) b[j] = ue8m0_x4(__ldg(swk + 32 * j));
+        } else {
+          const uint32_t w0 = ue8m0_x4(__ldg(swp + (long long)nb0 * nkb + kb));
+          const uint32_t w1 = ue8m0_x4(__ldg(swp + (long long)nb1 * nkb + kb));
+#pragma unroll
+          for (int j = 0; j < 8; ++j) b[j] = j < 4 ? w0 : w1;
         }
+#pragma unroll
+        for (int j = 4; j < 16; ++j) a[j] = 0u;
+#pragma unroll
+        for (int j = 8; j < 16; ++j) b[j] = 0u;
         bool got = mbar_wait(&empty[s], ((it / kMxStages) & 1) ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY);
         got = __all_sync(0xffffffffu, got);  // tcgen05.st is warp-collective
         if (!got) { ok = false; break; }
@@ -660,7 +669,55 @@ __global__ void fp8_quant_weight_kernel(const bf16* __restrict__ w, int N, int K
   if (tid == 0) sw[((long long)g * nbn + nb) * kbn + kb] = scale;
 }
 
+// x [T, C] bf16 -> xt [C, T] e4m3 with a power-of-two scale per column and 128-token block,
+// st [T/128][ldst] (ldst >= C): the operand of a GEMM that reduces over tokens (weight gradients).
+// One CTA (256 threads) per 128 tokens x 64 columns: four threads per column, 32 tokens each.
+__global__ void fp8_quant_t_kernel(const bf16* __restrict__ x, long long ldx, int T, int Cn, uint8_t* __restrict__ xt,
+                                   long long ldxt, float* __restrict__ st, long long ldst) {
+  __shared__ bf16 tile[128][66];
+  const int t0 = blockIdx.x * 128, c0 = blockIdx.y * 64;
+  const int tid = threadIdx.x;
+  for (int i = tid; i < 128 * 32; i += 256) {  // bf16 pairs
+    const int r = i >> 5, cp = (i & 31) * 2;
+    const int t = t0 + r, c = c0 + cp;
+    uint32_t v = 0u;
+    if (t < T && c + 1 < Cn) v = *reinterpret_cast<const uint32_t*>(x + (long long)t * ldx + c);
+    else if (t < T && c < Cn) v = (uint32_t)__bfloat16_as_ushort(x[(long long)t * ldx + c]);
+    *reinterpret_cast<uint32_t*>(&tile[r][cp]) = v;
+  }
+  __syncthreads();
+  const int col = tid >> 2, sub = tid & 3;
+  float v[32], amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    v[j] = __bfloat162float(tile[sub * 32 + j][col]);
+    amax = fmaxf(amax, fabsf(v[j]));
+  }
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const float sc = block_scale(amax, true);
+  const int c = c0 + col;
+  if (c >= Cn) return;
+  if (sub == 0) st[(long long)blockIdx.x * ldst + c] = sc;
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 32; j += 4)
+    w[j / 4] = (uint32_t)f32x2_to_e4m3x2(v[j] / sc, v[j + 1] / sc) |
+               ((uint32_t)f32x2_to_e4m3x2(v[j + 2] / sc, v[j + 3] / sc) << 16);
+  uint8_t* dst = xt + (long long)c * ldxt + t0 + sub * 32;
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 }  // namespace
+
+void fp8_quant_t(const void* x, long long ldx, int T, int Cn, void* xt, long long ldxt, float* st, long long ldst,
+                 cudaStream_t s) {
+  if (T % 128 != 0) throw std::runtime_error("fp8 quant_t: the token count must be a multiple of 128");
+  if (T == 0 || Cn == 0) return;
+  const dim3 grid(T / 128, (Cn + 63) / 64);
+  fp8_quant_t_kernel<<<grid, 256, 0, s>>>((const bf16*)x, ldx, T, Cn, (uint8_t*)xt, ldxt, st, ldst);
+}
 
 void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream) {
   if (d.K % kF8BK != 0 || d.K <= 0) throw std::runtime_error("fp8 gemm: K must be a positive multiple of 128");
@@ -694,6 +751,9 @@ void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream) {
   p.sx = d.sx;
   p.ldsx = d.ldsx;
   p.sw = d.sw;
+  p.ldsw = d.ldsw;
+  if (d.ldsw > 0 && (!d.scaled_mma || grouped))
+    throw std::runtime_error("fp8 gemm: per-row B scales need scaled_mma and a dense problem");
   p.C = reinterpret_cast<bf16*>(d.C);
   p.ldc = d.ldc;
   p.status = reinterpret_cast<StatusBlock*>(d.status);

@@ -104,6 +104,7 @@ struct Fp8GemmDesc {
   long long ldw = 0;
   long long w_group_stride = 0;
   const float* sw = nullptr;
+  long long ldsw = 0;  // > 0 (dense, scaled_mma): per-row B scales sw[K/128][ldsw], like sx
   void* C = nullptr;
   long long ldc = 0;
   long long rows_c = 0;  // rows of C (0: M); grouped-M outputs are as tall as A
@@ -126,6 +127,10 @@ void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream);
 // pow2: scales rounded up to powers of two
 void fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sx, long long ldsx, bool pow2,
                    cudaStream_t s);
+// x [T, C] bf16 -> xt [C, T] e4m3, st fp32 [T/128][ldst]: per column and 128-token block
+// (power-of-two scales); T % 128 == 0
+void fp8_quant_t(const void* x, long long ldx, int T, int Cn, void* xt, long long ldxt, float* st, long long ldst,
+                 cudaStream_t s);
 // w [G, N, K] bf16 -> wq e4m3, sw fp32 [G][ceil(N/128)][K/128]
 void fp8_quant_weight(const void* w, int G, int N, int K, void* wq, float* sw, bool pow2, cudaStream_t s);
 

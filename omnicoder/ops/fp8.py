@@ -196,13 +196,40 @@ class _Fp8LinearFn(torch.autograd.Function):
         return dx, dw
 
 
+WGRAD_FP8 = True     # weight gradients through the fp8 GEMM (token-dimension 128-blocks) when T % 128 == 0
+
+
+def quantize_t_torch(x: torch.Tensor):
+    """x [T, C] -> (x^T in e4m3 [C, T], fp32 power-of-two scales [T/128, C padded to 256]): one
+    scale per column and 128-token block (the operands of a GEMM that reduces over tokens)."""
+    T, Cn = x.shape
+    xb = x.float().view(T // 128, 128, Cn)
+    scale = _scale(xb.abs().amax(1), True)                       # [T/128, C]
+    xt = (xb / scale[:, None, :]).to(E4M3).reshape(T, Cn).t().contiguous()
+    st = torch.ones(T // 128, (Cn + 255) // 256 * 256, device=x.device)
+    st[:, :Cn] = scale
+    return xt, st
+
+
+def wgrad_fp8(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """dy^T @ x [N, K] bf16 with both operands quantised per column and 128-token block."""
+    C = _ext.load()
+    dyt, sdy = C.fp8_quant_t(dy)
+    xt, sxt = C.fp8_quant_t(x)
+    out = torch.empty(dy.shape[1], x.shape[1], device=dy.device, dtype=torch.bfloat16)
+    C.fp8_gemm(dyt, sdy, xt, sxt, out, sw_rows=True)
+    return out
+
+
 def _wgrad(dy: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    if WGRAD_FP8 and dy.shape[0] % 128 == 0 and dy.shape[1] % 8 == 0 and x.shape[1] % 8 == 0:
+        return wgrad_fp8(dy, x)
     from .gemm import mm_tn
     return mm_tn(dy, x)
 
 
 def fp8_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """y = x @ w^T with block-scaled fp8 fprop and dgrad GEMMs (bf16 weight gradient).
+    """y = x @ w^T with block-scaled fp8 fprop, dgrad and (token count % 128 == 0) wgrad GEMMs.
     x [T, K], w [N, K]; K and N multiples of 128."""
     shp = x.shape
     y = _Fp8LinearFn.apply(x.reshape(-1, shp[-1]), w)
@@ -212,7 +239,8 @@ def fp8_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
 class _Fp8SwiGLUFn(torch.autograd.Function):
     """CUDA SwiGLU MLP: fp8 gate|up GEMM whose epilogue applies the SwiGLU and requantises
     silu(g) * u, fp8 down GEMM on that copy; backward: the SwiGLU backward fused into the bf16
-    dact GEMM (as in the bf16 MLP), fp8 dgrad through w13, bf16 weight gradients."""
+    dact GEMM (as in the bf16 MLP), fp8 dgrad through w13, fp8 weight gradients (operands
+    quantised per column and 128-token block; bf16 when the token count is not a multiple of 128)."""
 
     @staticmethod
     def forward(ctx, x, w13, w2):
@@ -235,15 +263,15 @@ class _Fp8SwiGLUFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        from .gemm import EPI_SWIGLU_BWD, mm_tn
+        from .gemm import EPI_SWIGLU_BWD
         x2, w13, w2, H, act = ctx.saved_tensors
         C = _ext.load()
         dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
-        dw2 = mm_tn(dy2, act)
+        dw2 = _wgrad(dy2, act)
         dH = torch.empty_like(H)
         C.gemm(dy2, w2, dH, False, True, EPI_SWIGLU_BWD, 1.0, H, None, 256)
         dx = _mm_q(dH, WEIGHTS.get(w13, True)).view(*ctx.shape)
-        dw13 = mm_tn(dH, x2)
+        dw13 = _wgrad(dH, x2)
         return dx, dw13, dw2
 
 
