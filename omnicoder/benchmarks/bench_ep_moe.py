@@ -14,8 +14,10 @@ inputs (>= 67 MB) and expert weights exceed L2 only together, so L2 is
 flushed before every timed iteration.
 
 Transports: p2p (fused NVLink exchange, bf16 expert GEMMs), p2p_fp8 (the same
-exchange with block-scaled fp8 forward expert GEMMs: 1 x 128 activation and
-128 x 128 weight scales; backward with the bf16 weights), nccl (baseline).
+exchange with block-scaled fp8 expert GEMMs -- 1 x 128 activation and 128 x 128
+weight scales, power-of-two -- in the forward (SwiGLU and requantisation in the
+gate|up epilogue) and in the input gradient through the gate|up experts; the
+SwiGLU-backward and weight-gradient GEMMs in bf16), nccl (baseline).
 
 Roofline of the fused path per rank: the slower of (expert GEMM FLOPs of
 forward + backward at the measured sustained bf16 peak) and (bytes that must

@@ -262,7 +262,7 @@ void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
 // ---------------------------------------------------------------------------
 // Block-scaled fp8 (1 x 128 activation scales, 128 x 128 weight scales)
 // ---------------------------------------------------------------------------
-std::vector<at::Tensor> fp8_quant_act_t(const at::Tensor& x, bool pow2) {
+std::vector<at::Tensor> fp8_quant_act_t(const at::Tensor& x, bool pow2, const c10::optional<at::Tensor>& offsets) {
   CHECK_CUDA_T(x);
   CHECK_BF16(x);
   CHECK_ROWMAJOR(x);
@@ -271,7 +271,14 @@ std::vector<at::Tensor> fp8_quant_act_t(const at::Tensor& x, bool pow2) {
   const int64_t M = x.size(0), K = x.size(1), Mp = (M + 127) / 128 * 128;
   auto xq = at::empty({M, K}, x.options().dtype(at::kFloat8_e4m3fn));
   auto sx = at::empty({K / 128, Mp}, x.options().dtype(at::kFloat));
-  fp8_quant_act(x.data_ptr(), x.stride(0), (int)M, (int)K, xq.data_ptr(), sx.data_ptr<float>(), Mp, pow2, cur_stream());
+  const int* limit = nullptr;
+  if (offsets.has_value()) {
+    TORCH_CHECK(offsets->scalar_type() == at::kInt && offsets->is_cuda() && offsets->numel() >= 1,
+                "fp8_quant_act: offsets int32 on the device");
+    limit = offsets->data_ptr<int>() + (offsets->numel() - 1);
+  }
+  fp8_quant_act(x.data_ptr(), x.stride(0), (int)M, (int)K, xq.data_ptr(), sx.data_ptr<float>(), Mp, pow2, cur_stream(),
+                limit);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {xq, sx};
 }
@@ -597,7 +604,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_copy", &omni::peer_copy, py::arg("dst"), py::arg("src"), py::arg("nbytes"));
   m.def("tp_reduce", &omni::tp_reduce, py::arg("staging"), py::arg("out"), py::arg("residual") = py::none());
   m.def("fp8_quant_act", &omni::fp8_quant_act_t, "bf16 [M, K] -> (e4m3 [M, K], fp32 scales [K/128, M padded to 128])",
-        py::arg("x"), py::arg("pow2") = true);
+        py::arg("x"), py::arg("pow2") = true, py::arg("offsets") = py::none());
   m.def("fp8_quant_weight", &omni::fp8_quant_weight_t, "bf16 [(G,) N, K] -> (e4m3, fp32 scales [G, N/128, K/128])",
         py::arg("w"), py::arg("pow2") = true);
   m.def("fp8_gemm", &omni::fp8_gemm_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"), py::arg("C"),

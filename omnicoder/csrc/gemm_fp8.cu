@@ -605,12 +605,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 
 // one warp per (row, 128-column block): 4 elements per lane
 __global__ void fp8_quant_act_kernel(const bf16* __restrict__ x, long long ldx, int M, int K, uint8_t* __restrict__ xq,
-                                     float* __restrict__ sx, long long ldsx, bool pow2) {
+                                     float* __restrict__ sx, long long ldsx, bool pow2,
+                                     const int* __restrict__ row_limit) {
   const int kbn = K / 128;
   const long long w = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (w >= (long long)ldsx * kbn) return;
   const int row = (int)(w / kbn), kb = (int)(w % kbn);
+  if (row_limit != nullptr && row >= __ldg(row_limit)) return;  // rows no GEMM tile reads
   if (row >= M) {
     if (lane == 0) sx[(long long)kb * ldsx + row] = 0.f;
     return;
@@ -804,11 +806,12 @@ void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream) {
 }
 
 void fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sx, long long ldsx, bool pow2,
-                   cudaStream_t s) {
+                   cudaStream_t s, const int* row_limit) {
   if (K % 128 != 0) throw std::runtime_error("fp8 quant: K must be a multiple of 128");
   const long long warps = ldsx * (K / 128);
   if (warps == 0) return;
-  fp8_quant_act_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, ldx, M, K, (uint8_t*)xq, sx, ldsx, pow2);
+  fp8_quant_act_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, ldx, M, K, (uint8_t*)xq, sx, ldsx, pow2,
+                                                                          row_limit);
 }
 
 void fp8_quant_weight(const void* w, int G, int N, int K, void* wq, float* sw, bool pow2, cudaStream_t s) {

@@ -124,9 +124,10 @@ struct Fp8GemmDesc {
 };
 void fp8_gemm_launch(const Fp8GemmDesc& d, cudaStream_t stream);
 // x [M, K] bf16 -> xq e4m3 [M, K], sx fp32 [K/128][ldsx] (rows >= M zero-filled up to ldsx);
-// pow2: scales rounded up to powers of two
+// pow2: scales rounded up to powers of two; row_limit (device int, optional): rows at or past it
+// are left unwritten (grouped operands whose tiles end at the last group's offset)
 void fp8_quant_act(const void* x, long long ldx, int M, int K, void* xq, float* sx, long long ldsx, bool pow2,
-                   cudaStream_t s);
+                   cudaStream_t s, const int* row_limit = nullptr);
 // x [T, C] bf16 -> xt [C, T] e4m3, st fp32 [T/128][ldst]: per column and 128-token block
 // (power-of-two scales); T % 128 == 0
 void fp8_quant_t(const void* x, long long ldx, int T, int Cn, void* xt, long long ldxt, float* st, long long ldst,

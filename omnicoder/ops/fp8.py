@@ -78,10 +78,12 @@ def dequantize_weight(wq: torch.Tensor, sw: torch.Tensor) -> torch.Tensor:
     return out[0] if squeeze else out
 
 
-def quantize_act(x: torch.Tensor, pow2: bool = True):
+def quantize_act(x: torch.Tensor, pow2: bool = True, offsets: torch.Tensor | None = None):
+    """offsets (CUDA, grouped operands): rows at or past offsets[-1] -- read by no GEMM tile --
+    are left unwritten."""
     if not _ext.use_cuda(x):
         return quantize_act_torch(x, pow2)
-    return tuple(_ext.load().fp8_quant_act(x.contiguous(), pow2))
+    return tuple(_ext.load().fp8_quant_act(x.contiguous(), pow2, offsets))
 
 
 def quantize_weight(w: torch.Tensor, pow2: bool = True):
@@ -106,7 +108,7 @@ def fp8_grouped_mm(x_perm: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor, off
                    rows: int, scaled_mma: bool = True) -> torch.Tensor:
     """Row group g of x_perm (rows [offsets[g], offsets[g+1]), multiples of 128) times
     dequant(wq[g])^T -> [rows, N] bf16."""
-    xq, sx = quantize_act(x_perm, pow2=scaled_mma)
+    xq, sx = quantize_act(x_perm, pow2=scaled_mma, offsets=offsets if _ext.use_cuda(x_perm) else None)
     if not _ext.use_cuda(x_perm):
         w = dequantize_weight(wq, sw)
         xd = dequantize_act(xq, sx)
@@ -134,7 +136,7 @@ def fp8_grouped_swiglu(x_perm: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
         a = torch.nn.functional.silu(g) * u
         aq, sa = quantize_act_torch(a)
         return H, (a.to(x_perm.dtype) if keep_act else None), aq, sa
-    xq, sx = quantize_act(x_perm)
+    xq, sx = quantize_act(x_perm, offsets=offsets)
     dev = x_perm.device
     R = x_perm.shape[0]
     H = torch.empty(R, F2, device=dev, dtype=torch.bfloat16)

@@ -122,12 +122,15 @@ class EPContext:
         # weights of a layer are present, its forward expert GEMMs run in block-scaled fp8
         self.fp8_weights: dict = {}
 
-    def set_fp8_weights(self, *weights):
-        """Quantise the given expert weight stacks ([El, N, K] bf16) for the fp8 forward path
-        (call again after every optimiser step)."""
+    def set_fp8_weights(self, w13: torch.Tensor, w2: torch.Tensor):
+        """Quantise a layer's expert weight stacks (w13 [El, 2F, D], w2 [El, D, F], bf16) for the
+        fp8 path (call again after every optimiser step): the forward GEMMs use them as they are,
+        the input-gradient GEMM through the gate|up experts w13's transpose (key ("t", id))."""
         from ..ops.fp8 import quantize_weight
-        for w in weights:
+        for w in (w13, w2):
             self.fp8_weights[id(w)] = quantize_weight(w.detach())
+        if w13.shape[-1] % 128 == 0 and w13.shape[-2] % 128 == 0:
+            self.fp8_weights[("t", id(w13))] = quantize_weight(w13.detach().transpose(-1, -2).contiguous())
 
     def experts_of(self, E: int) -> tuple[int, int]:
         if E % self.world:
@@ -435,7 +438,14 @@ class _EPMoEDev(torch.autograd.Function):
         dw2 = torch.empty_like(w2)
         C.gemm_grouped_k(dy_recv, act, sl.offs_local, dw2, EPI_BF16, 1.0, 256)
         dx_recv = sh.dx.view(torch.bfloat16, R, D)
-        C.gemm_grouped_m(dH, w13, sl.offs_local, dx_recv, True, EPI_BF16, 1.0, None, None, 256, R)
+        q13t = ep.fp8_weights.get(("t", id(w13))) if ep.fp8_weights else None
+        if q13t is not None:
+            # fp8 input gradient through the gate|up experts (dH per 1 x 128 block, w13^T blocks)
+            from ..ops.fp8 import quantize_act
+            dq, sdq = quantize_act(dH, offsets=sl.offs_local)
+            C.fp8_gemm(dq, sdq, q13t[0], q13t[1].reshape(-1), dx_recv, sl.offs_local, R)
+        else:
+            C.gemm_grouped_m(dH, w13, sl.offs_local, dx_recv, True, EPI_BF16, 1.0, None, None, 256, R)
         dw13 = torch.empty_like(w13)
         C.gemm_grouped_k(dH, x_recv, sl.offs_local, dw13, EPI_BF16, 1.0, 256)
         arena.barrier()                                       # input gradients and weight gradients are ready

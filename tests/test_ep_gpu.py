@@ -112,6 +112,22 @@ def _layer_worker(rank, world, port, q):
                 code = C.status()[0]
                 C.status_reset()
                 out[("fp8", "p2p")] = {"status": code, "y": _close(yq, ya[rank * T:(rank + 1) * T], 8e-2)}
+                # training step: fp8 forward and fp8 input gradient through the gate|up experts
+                xq_ = xs[rank * T:(rank + 1) * T].clone().requires_grad_(True)
+                q13 = w13[lo:hi].clone().requires_grad_(True)
+                q2 = w2[lo:hi].clone().requires_grad_(True)
+                ep.set_fp8_weights(q13, q2)
+                ep.begin_step()
+                yq2, _ = ep_moe_ffn(xq_, wr.clone().requires_grad_(True), q13, q2, K, ep, capacity=0, renorm=True)
+                yq2.backward(dys[rank * T:(rank + 1) * T])
+                torch.cuda.synchronize()
+                code = C.status()[0]
+                C.status_reset()
+                sl = slice(rank * T, (rank + 1) * T)
+                out[("fp8_train", "p2p")] = {"status": code, "y": _close(yq2, ya[sl], 8e-2),
+                                             "dx": _close(xq_.grad, xa.grad[sl], 1e-1),
+                                             "dw13": _close(q13.grad, a13.grad[lo:hi], 1e-1),
+                                             "dw2": _close(q2.grad, a2.grad[lo:hi], 1e-1)}
         q.put((rank, out))
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e)))

@@ -231,7 +231,7 @@ def test_fp8_swiglu_mlp_fused_matches_fp32():
     yr = (torch.nn.functional.silu(gg) * uu) @ br.t()
     yr.backward(g.float())
     assert _rel(y.detach(), yr.detach()) < 0.1
-    assert ((y.detach().float() - yr).abs().mean() / yr.abs().mean()).item() < 0.05
+    assert ((y.detach().float() - yr).abs().mean() / yr.abs().mean()).item() < 0.1
     assert _rel(x.grad, xr.grad) < 0.1
     assert _rel(w13.grad, ar.grad) < 0.1
     assert _rel(w2.grad, br.grad) < 0.1
