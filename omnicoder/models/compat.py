@@ -244,7 +244,7 @@ class MoELayer(nn.Module):
         start = torch.cummax(torch.where(first, pos, torch.zeros_like(pos)), 0).values
         rank = torch.empty_like(pos)
         rank[order] = pos - start
-        keep = rank < self.top_k
+        keep = rank < self.expert_capacity(xf.shape[0])
         out = torch.zeros_like(xf)
         N = xf.shape[0]
         for e in range(self.n_experts):
@@ -261,6 +261,29 @@ class MoELayer(nn.Module):
             share = sum(g(xf) for g in self.shared) / self.num_shared_general
             out = 0.95 * out + 0.05 * share
         return out.reshape(B, T, D)
+
+    def expert_capacity(self, n_tokens: int) -> int:
+        """Pairs kept per expert: top_k, the capacity the used layer passes to its dispatch
+        (reference modeling/moe_layer.py)."""
+        return self.top_k
+
+
+class CapacityMoELayer(MoELayer):
+    """The second MoE layer of the reference (modeling/transformer_moe.py:114-760, defined there
+    but not used by the model): the same routers, experts and dispatch, with the per-expert
+    capacity ceil(T * k / E * capacity_factor) (transformer_moe.py:615-621, `int(x + 0.9999)`),
+    or `static_capacity` when given, instead of top_k."""
+
+    def __init__(self, c: CompatConfig, capacity_factor: float = 1.2, static_capacity: int | None = None):
+        super().__init__(c)
+        self.capacity_factor = capacity_factor
+        self.static_capacity = static_capacity
+
+    def expert_capacity(self, n_tokens: int) -> int:
+        if self.static_capacity is not None and self.static_capacity > 0:
+            return int(self.static_capacity)
+        expected = n_tokens * self.top_k / max(1, self.n_experts)
+        return int(expected * self.capacity_factor + 0.9999)
 
 
 class Block(nn.Module):

@@ -91,3 +91,28 @@ def test_reference_key_normalisation():
     rep = load_reference_state_dict(m, {"state_dict": sd})
     assert rep["missing"] == [] and rep["unexpected"] == [], rep
     assert torch.allclose(m.blocks[0].moe.experts[0].fc1.weight, sd["module.blocks.0.moe.experts.0._orig_mod.fc1.weight"])
+
+
+def test_capacity_moe_layer_keeps_ceil_capacity_pairs():
+    """transformer_moe.MoELayer's capacity: ceil(T * k / E * cf) pairs per expert (or a static
+    capacity); with a capacity at least T the layer equals the dropless computation, and a small
+    static capacity drops pairs past it."""
+    from omnicoder.models.compat import CapacityMoELayer, CompatConfig, MoELayer
+    c = CompatConfig(d_model=32, mlp_dim=64, n_experts=4, top_k=2)
+    torch.manual_seed(0)
+    layer = CapacityMoELayer(c, capacity_factor=1.2).eval()
+    assert layer.expert_capacity(10) == 6          # 10 * 2 / 4 * 1.2 = 6.0
+    assert layer.expert_capacity(11) == 7          # 6.6 -> 7
+    x = torch.randn(1, 16, 32)
+    big = CapacityMoELayer(c, static_capacity=10 ** 6).eval()
+    big.load_state_dict(layer.state_dict())
+    ref = MoELayer(c).eval()
+    ref.load_state_dict(layer.state_dict())
+    ref.expert_capacity = lambda n: 10 ** 6
+    torch.testing.assert_close(big(x), ref(x))
+    one = CapacityMoELayer(c, static_capacity=1).eval()
+    one.load_state_dict(layer.state_dict())
+    y1, yb = one(x), big(x)
+    assert not torch.allclose(y1, yb)              # pairs past one per expert are dropped
+    zero_rows = (y1.abs().sum(-1) == 0).sum().item()
+    assert zero_rows >= 16 - 4                     # at most 4 experts x 1 pair reach the output
