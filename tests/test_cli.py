@@ -119,3 +119,31 @@ def test_run_training_smoke_one_step(tmp_path):
     summary = json.loads(out[out.rindex("{\n \"plan\""):])
     assert all(v["steps"] == 1 for v in summary["plan"].values())
     assert {k: v["rc"] for k, v in summary["results"].items()} == {"vqa": 0, "rl": 0}
+
+
+def test_verifier_distillation(tmp_path):
+    """The verifier head learns the teacher's softened distribution: the KL falls; with
+    verifier_only nothing but the verifier moves; a teacher with another vocabulary goes
+    through the learned aligner."""
+    from omnicoder.config import ModelConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.verifier_distill import VerifierDistiller, main
+    cfg = ModelConfig(name="v", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      verifier_head=True)
+    student = build_model(cfg, "cpu", dtype=torch.float32, seed=0)
+    tcfg = ModelConfig(name="t", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64)
+    teacher = build_model(tcfg, "cpu", dtype=torch.float32, seed=1).eval()
+    before = {n: p.detach().clone() for n, p in student.named_parameters()}
+    vd = VerifierDistiller(student, lr=3e-3, verifier_only=True)
+    ids = torch.randint(0, cfg.vocab_size, (2, 32))
+    with torch.no_grad():
+        t = teacher(ids, all_logits=True)["logits"]
+    losses = [vd.step(ids, t) for _ in range(8)]
+    assert losses[-1] < losses[0]
+    moved = [n for n, p in student.named_parameters() if not torch.equal(p, before[n])]
+    assert moved == ["verifier"]
+    vd2 = VerifierDistiller(student, lr=1e-3, teacher_vocab=cfg.vocab_size + 17)
+    t2 = torch.randn(2, 32, cfg.vocab_size + 17)
+    assert vd2.step(ids, t2) > 0 and vd2.align.weight.grad is not None
+    assert main(["--steps", "1", "--seq_len", "16", "--batch_size", "1", "--device", "cpu",
+                 "--out", str(tmp_path / "v.pt")]) == 0
