@@ -89,3 +89,26 @@ def test_vl_task_trainers(tmp_path):
     assert len(cap.fit(rows, steps=2, batch=2)) == 2 and isinstance(cap.answer(rows[0]["media"], "Caption:", 3), str)
     asr = VLTaskTrainer(lm, fc, tok, "asr", lr=1e-3)
     assert asr.step(torch.randn(2, 1600), ["Transcript:"] * 2, ["hi", "yo"]) > 0
+
+
+def test_av_sync_grounding_segmentation_heads():
+    from omnicoder.multimodal.heads import ASRAdapter, AVSyncModule, RepRTAHead, TextSegHead, TTSAdapter
+    torch.manual_seed(0)
+    av = AVSyncModule(d_audio=40, d_video=24, d_model=64, num_heads=4)
+    vf, score = av(torch.randn(2, 12, 40), torch.randn(2, 9, 24))
+    assert vf.shape == (2, 9, 64) and score.shape == (2, 1) and bool(((score >= 0) & (score <= 1)).all())
+    score.sum().backward()                                         # the score trains the projections
+    assert av.audio_proj.weight.grad is not None
+    head = RepRTAHead(d_model=32, num_props=5)
+    toks, text = torch.randn(2, 16, 32), torch.randn(2, 32)
+    boxes, conf = head(toks, text)
+    assert boxes.shape == (2, 5, 4) and conf.shape == (2, 5)
+    assert bool(((boxes > 0) & (boxes < 1)).all())
+    assert not torch.allclose(boxes[:, 0], boxes[:, 1])            # proposals differ
+    b2, c2 = RepRTAHead(d_model=32, num_props=8)(torch.randn(1, 4, 32), torch.randn(1, 32))
+    assert b2.shape == (1, 8, 4) and torch.isinf(c2[0, 4:]).all()  # fewer tokens than proposals
+    mask = TextSegHead(d_model=32)(toks, text)
+    assert mask.shape == (2, 1, 4, 4) and bool(((mask >= 0) & (mask <= 1)).all())
+    assert TextSegHead(d_model=32, grid_hw=(3, 6))(toks).shape == (2, 1, 3, 6)
+    for a in (ASRAdapter(), TTSAdapter()):
+        assert isinstance(a.available(), bool)
