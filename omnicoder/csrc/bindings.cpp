@@ -259,6 +259,55 @@ void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Expert-parallel combine from the GEMM epilogue: per-expert products of A's row groups, each output
+// row r stored to its origin: peer_ptrs[s] + i * D (bf16) with (-, s, i, -) = meta[r] (int4 rows;
+// s < 0 marks padding).  dest_rows bounds i.  B [G, N, K] (b_mn: [G, K, N]).
+void gemm_grouped_m_push(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const at::Tensor& meta,
+                         const std::vector<int64_t>& peer_ptrs, int64_t dest_rows, bool b_mn, int64_t max_rows_hint) {
+  CHECK_CUDA_T(A);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_ROWMAJOR(A);
+  TORCH_CHECK(B.dim() == 3 && B.is_contiguous(), "gemm_grouped_m_push: B must be a contiguous [G, ., .] stack");
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda() && offsets.numel() == B.size(0) + 1,
+              "gemm_grouped_m_push: offsets must be int32 [G+1] on the device");
+  TORCH_CHECK(meta.scalar_type() == at::kInt && meta.is_cuda() && meta.is_contiguous() && meta.dim() == 2 &&
+                  meta.size(1) == 4 && meta.size(0) >= A.size(0), "gemm_grouped_m_push: meta int32 [rows, 4]");
+  TORCH_CHECK(!peer_ptrs.empty() && peer_ptrs.size() <= (size_t)GEMM_MAX_PEERS, "gemm_grouped_m_push: 1..8 ranks");
+  const c10::cuda::CUDAGuard guard(A.device());
+  GemmDesc d;
+  d.mode = GEMM_GROUPED_M;
+  d.epilogue = EPI_EP_PUSH;
+  d.block_n = 256;
+  d.b_mn_major = b_mn;
+  const int64_t K = A.size(1);
+  const int64_t N = b_mn ? B.size(2) : B.size(1);
+  TORCH_CHECK((b_mn ? B.size(1) : B.size(2)) == K && K % 8 == 0 && N % 8 == 0, "gemm_grouped_m_push: dims");
+  d.M = (int)A.size(0);
+  d.N = (int)N;
+  d.K = (int)K;
+  d.A = A.data_ptr();
+  d.lda = A.stride(0);
+  d.rows_a = A.size(0);
+  d.K_extent_a = K;
+  d.B = B.data_ptr();
+  d.ldb = B.stride(1);
+  d.b_group_stride = B.stride(0);
+  d.K_extent_b = K;
+  d.num_groups = (int)B.size(0);
+  d.group_offsets = offsets.data_ptr<int>();
+  d.max_rows_hint = (int)max_rows_hint;
+  d.ldc = N;
+  d.rows_c = A.size(0);
+  d.nsrc = (int)peer_ptrs.size();
+  d.src_rows = (int)dest_rows;
+  for (size_t r = 0; r < peer_ptrs.size(); ++r) d.peer_c[r] = reinterpret_cast<void*>(peer_ptrs[r]);
+  d.row_meta = meta.data_ptr();
+  d.status = status_ptr();
+  gemm_sm100_launch(d, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // ---------------------------------------------------------------------------
 // Block-scaled fp8 (1 x 128 activation scales, 128 x 128 weight scales)
 // ---------------------------------------------------------------------------
@@ -611,6 +660,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("offsets") = py::none(), py::arg("max_rows") = 0, py::arg("scaled_mma") = true,
         py::arg("sw_rows") = false);
   m.def("fp8_quant_t", &omni::fp8_quant_t_t, "bf16 [T, C] -> (e4m3 [C, T], fp32 scales [T/128, C padded to 256])");
+  m.def("gemm_grouped_m_push", &omni::gemm_grouped_m_push, py::arg("A"), py::arg("B"), py::arg("offsets"),
+        py::arg("meta"), py::arg("peer_ptrs"), py::arg("dest_rows"), py::arg("b_mn"), py::arg("max_rows") = 0);
   m.def("fp8_gemm_swiglu_q", &omni::fp8_gemm_swiglu_q_t, py::arg("xq"), py::arg("sx"), py::arg("wq"), py::arg("sw"),
         py::arg("H"), py::arg("act"), py::arg("actq"), py::arg("act_scale"), py::arg("offsets") = py::none(),
         py::arg("max_rows") = 0);

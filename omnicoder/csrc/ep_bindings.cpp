@@ -55,6 +55,53 @@ void ep_push_t(const at::Tensor& src, const at::Tensor& slot, const at::Tensor& 
           (int)slot.size(1), (int)El, (int)src.size(1), stream());
 }
 
+// out[t] = add[t] + sum_k w[t,k] ys[t*K+k] over kept pairs: the combine after the owners pushed their
+// rows into this rank's slots ys [T*K, D] (local reads).
+at::Tensor ep_combine_local_t(const at::Tensor& slot, const at::Tensor& ys, const c10::optional<at::Tensor>& w,
+                              const c10::optional<at::Tensor>& add) {
+  check(slot, at::kInt, "slot");
+  check(ys, at::kBFloat16, "ys");
+  const c10::cuda::CUDAGuard g(slot.device());
+  const int64_t T = slot.size(0), K = slot.size(1), D = ys.size(1);
+  TORCH_CHECK(K <= 16 && ys.size(0) == T * K && D % 8 == 0, "ep_combine_local: ys [T*K, D], top-k <= 16");
+  auto out = at::empty({T, D}, ys.options());
+  if (add.has_value()) check(*add, at::kBFloat16, "add");
+  if (w.has_value()) check(*w, at::kFloat, "w");
+  ep_combine(slot.data_ptr<int>(), slot.data_ptr<int>(), w.has_value() ? w->data_ptr<float>() : nullptr, EpPeers{},
+             add.has_value() ? add->data_ptr() : nullptr, out.data_ptr(), (int)T, (int)K, 1, (int)D, stream(),
+             ys.data_ptr());
+  return out;
+}
+
+void ep_return_rows_t(const at::Tensor& y, const at::Tensor& meta, const at::Tensor& offsets,
+                      const std::vector<int64_t>& ys_ptrs, const std::vector<int64_t>& ys_rows) {
+  check(y, at::kBFloat16, "y");
+  check(meta, at::kInt, "meta");
+  check(offsets, at::kInt, "offsets");
+  const c10::cuda::CUDAGuard g(y.device());
+  TORCH_CHECK(meta.dim() == 2 && meta.size(1) == 4 && meta.size(0) >= y.size(0) && y.size(1) % 8 == 0,
+              "ep_return_rows: meta [rows, 4], D % 8");
+  ep_return_rows(y.data_ptr(), meta.data_ptr(), offsets.data_ptr<int>(), (int)offsets.numel() - 1,
+                 make_peers(ys_ptrs, ys_rows), (int)y.size(0), (int)y.size(1), stream());
+}
+
+void ep_source_bwd_t(const at::Tensor& dout, const at::Tensor& ys, const at::Tensor& slot, const at::Tensor& idx,
+                     const at::Tensor& w, at::Tensor& dwts, const std::vector<int64_t>& dy_ptrs,
+                     const std::vector<int64_t>& rows, int64_t El) {
+  check(dout, at::kBFloat16, "dout");
+  check(ys, at::kBFloat16, "ys");
+  check(slot, at::kInt, "slot");
+  check(idx, at::kInt, "idx");
+  check(w, at::kFloat, "w");
+  check(dwts, at::kFloat, "dwts");
+  const c10::cuda::CUDAGuard g(dout.device());
+  const int64_t T = slot.size(0), K = slot.size(1), D = dout.size(1);
+  TORCH_CHECK(ys.size(0) == T * K && ys.size(1) == D && D % 8 == 0 && dwts.numel() == T * K,
+              "ep_source_bwd: shapes");
+  ep_source_bwd(dout.data_ptr(), ys.data_ptr(), slot.data_ptr<int>(), idx.data_ptr<int>(), w.data_ptr<float>(),
+                dwts.data_ptr<float>(), make_peers(dy_ptrs, rows), (int)T, (int)K, (int)El, (int)D, stream());
+}
+
 at::Tensor ep_combine_t(const at::Tensor& slot, const at::Tensor& idx, const c10::optional<at::Tensor>& w,
                         const std::vector<int64_t>& ptrs, const std::vector<int64_t>& rows, int64_t El, int64_t D,
                         const c10::optional<at::Tensor>& add) {
@@ -153,6 +200,9 @@ void register_ep(pybind11::module_& m) {
   m.def("ep_dispatch", &ep_dispatch_t);
   m.def("ep_push", &ep_push_t);
   m.def("ep_combine", &ep_combine_t);
+  m.def("ep_combine_local", &ep_combine_local_t);
+  m.def("ep_source_bwd", &ep_source_bwd_t);
+  m.def("ep_return_rows", &ep_return_rows_t);
   m.def("ep_owner_bwd", &ep_owner_bwd_t);
   m.def("ep_pad_rows", &ep_pad_rows_t);
   m.def("ep_barrier", &ep_barrier_t);

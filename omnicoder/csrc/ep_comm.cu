@@ -111,7 +111,8 @@ __global__ void ep_push_kernel(const bf16* __restrict__ src, const int* __restri
 template <int KMAX>
 __global__ void ep_combine_kernel(const int* __restrict__ slot, const int* __restrict__ idx,
                                   const float* __restrict__ w, EpPeers y, const bf16* __restrict__ add,
-                                  bf16* __restrict__ out, int T, int K, int El, int D) {
+                                  bf16* __restrict__ out, int T, int K, int El, int D,
+                                  const bf16* __restrict__ local) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -123,7 +124,11 @@ __global__ void ep_combine_kernel(const int* __restrict__ slot, const int* __res
     wk[k] = 0.f;
     if (k < K) {
       const int s = slot[(long long)t * K + k];
-      if (s >= 0) {
+      if (s >= 0 && local != nullptr) {
+        // the owners pushed their output rows to this rank's (token, k) slots
+        rows[k] = local + ((long long)t * K + k) * D;
+        wk[k] = w != nullptr ? w[(long long)t * K + k] : 1.f;
+      } else if (s >= 0) {
         const int owner = idx[(long long)t * K + k] / El;
         if (owner >= 0 && owner < kEpMaxRanks && s < y.rows[owner]) {
           rows[k] = reinterpret_cast<const bf16*>(y.ptr[owner]) + (long long)s * D;
@@ -143,6 +148,76 @@ __global__ void ep_combine_kernel(const int* __restrict__ slot, const int* __res
     for (int k = 0; k < KMAX; ++k)
       if (rows[k] != nullptr) acc_add8(acc, v[k], wk[k]);
     *reinterpret_cast<uint4*>(out + (long long)t * D + c) = pack8(acc);
+  }
+}
+
+// Owner rows back to their origins: row r of y (r < offsets[El]) goes to ys_peer[s] + i * D with
+// (-, s, i, -) = meta[r]; padding rows (s < 0) stay.  One warp per row, whole rows per store
+// sequence.  (The block-scaled GEMM writes its expert outputs locally and this kernel returns
+// them; the bf16 GEMM returns them from its epilogue.)
+__global__ void ep_return_rows_kernel(const bf16* __restrict__ y, const int4* __restrict__ meta,
+                                      const int* __restrict__ offsets, int El, EpPeers ys, int rows, int D,
+                                      StatusBlock* st) {
+  const int lane = threadIdx.x & 31;
+  const int total = min(rows, offsets[El]);
+  for (int r = blockIdx.x * kWarps + (threadIdx.x >> 5); r < total; r += gridDim.x * kWarps) {
+    const int4 m = meta[r];
+    if (m.y < 0) continue;
+    if (m.y >= kEpMaxRanks || m.z < 0 || m.z >= ys.rows[m.y]) {
+      if (lane == 0) report_error(st, STATUS_BAD_INDEX, m.z);
+      continue;
+    }
+    const bf16* src = y + (long long)r * D;
+    bf16* dst = reinterpret_cast<bf16*>(ys.ptr[m.y]) + (long long)m.z * D;
+    for (int c = lane * 8; c < D; c += 256)
+      *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+  }
+}
+
+// Combine backward on the source rank when the owners pushed their outputs to its (token, k)
+// slots ys: dwts[pair] = <dout[t], ys[pair]> (read locally) and the weighted output gradient
+// dout[t] * w[pair] pushed into the owner's receive row slot[pair].  One warp per pair.
+__global__ void ep_source_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ ys,
+                                     const int* __restrict__ slot, const int* __restrict__ idx,
+                                     const float* __restrict__ w, float* __restrict__ dwts, EpPeers dy, int TK, int K,
+                                     int El, int D, StatusBlock* st) {
+  const int lane = threadIdx.x & 31;
+  for (int i = blockIdx.x * kWarps + (threadIdx.x >> 5); i < TK; i += gridDim.x * kWarps) {
+    const int row = slot[i];
+    if (row < 0) {
+      if (lane == 0) dwts[i] = 0.f;
+      continue;
+    }
+    const int owner = idx[i] / El;
+    if (owner < 0 || owner >= kEpMaxRanks || row >= dy.rows[owner]) {
+      if (lane == 0) {
+        dwts[i] = 0.f;
+        report_error(st, STATUS_BAD_INDEX, row);
+      }
+      continue;
+    }
+    const float wi = w[i];
+    const bf16* g = dout + (long long)(i / K) * D;
+    const bf16* yr = ys + (long long)i * D;
+    bf16* d = reinterpret_cast<bf16*>(dy.ptr[owner]) + (long long)row * D;
+    float dot = 0.f;
+    for (int c = lane * 8; c < D; c += 256) {
+      const uint4 gv = *reinterpret_cast<const uint4*>(g + c);
+      const uint4 yv = *reinterpret_cast<const uint4*>(yr + c);
+      const uint32_t* gq = reinterpret_cast<const uint32_t*>(&gv);
+      const uint32_t* yq = reinterpret_cast<const uint32_t*>(&yv);
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float g0 = bf16_lo(gq[j]), g1 = bf16_hi(gq[j]);
+        dot += g0 * bf16_lo(yq[j]) + g1 * bf16_hi(yq[j]);
+        o[2 * j] = g0 * wi;
+        o[2 * j + 1] = g1 * wi;
+      }
+      *reinterpret_cast<uint4*>(d + c) = pack8(o);
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) dwts[i] = dot;
   }
 }
 
@@ -386,15 +461,33 @@ void ep_push(const void* src, const int* slot, const int* idx, const EpPeers& ds
 }
 
 void ep_combine(const int* slot, const int* idx, const float* w, const EpPeers& y, const void* add, void* out, int T,
-                int K, int El, int D, cudaStream_t s) {
+                int K, int El, int D, cudaStream_t s, const void* local) {
   if (T == 0) return;
   const int grid = (T + kWarps - 1) / kWarps;
   if (K <= 4)
-    ep_combine_kernel<4><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D);
+    ep_combine_kernel<4><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D,
+                                                       (const bf16*)local);
   else if (K <= 8)
-    ep_combine_kernel<8><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D);
+    ep_combine_kernel<8><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D,
+                                                       (const bf16*)local);
   else
-    ep_combine_kernel<16><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D);
+    ep_combine_kernel<16><<<grid, kWarps * 32, 0, s>>>(slot, idx, w, y, (const bf16*)add, (bf16*)out, T, K, El, D,
+                                                       (const bf16*)local);
+}
+
+void ep_return_rows(const void* y, const void* meta, const int* offsets, int El, const EpPeers& ys, int rows, int D,
+                    cudaStream_t s) {
+  if (rows == 0) return;
+  ep_return_rows_kernel<<<grid_for(rows), kWarps * 32, 0, s>>>((const bf16*)y, (const int4*)meta, offsets, El, ys,
+                                                                rows, D, (StatusBlock*)status_ptr());
+}
+
+void ep_source_bwd(const void* dout, const void* ys, const int* slot, const int* idx, const float* w, float* dwts,
+                   const EpPeers& dy, int T, int K, int El, int D, cudaStream_t s) {
+  const int TK = T * K;
+  if (TK == 0) return;
+  ep_source_bwd_kernel<<<grid_for(TK), kWarps * 32, 0, s>>>((const bf16*)dout, (const bf16*)ys, slot, idx, w, dwts,
+                                                            dy, TK, K, El, D, (StatusBlock*)status_ptr());
 }
 
 void ep_owner_bwd(void* dy, const void* y, const void* meta, const int* offsets, const int* kept, int El,

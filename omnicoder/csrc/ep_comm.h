@@ -26,8 +26,18 @@ void ep_dispatch(const void* x, const int* idx, const int* pos, const int* loc_o
 void ep_push(const void* src, const int* slot, const int* idx, const EpPeers& dst, int T, int K, int El, int D,
              cudaStream_t s);
 // out[t] = add[t] + sum_k w[t,k] * Y_owner[slot[t,k]] (w == nullptr: weight 1); peer loads.
+// local != nullptr: the owners pushed their rows into this rank's slots local[t * K + k] (read
+// locally, y unused).
 void ep_combine(const int* slot, const int* idx, const float* w, const EpPeers& y, const void* add, void* out, int T,
-                int K, int El, int D, cudaStream_t s);
+                int K, int El, int D, cudaStream_t s, const void* local = nullptr);
+// Owner output rows y [rows, D] back to their origins' (token, k) slots: row r -> ys.ptr[s] + i * D,
+// (-, s, i, -) = meta[r]; rows past offsets[El] and padding rows (s < 0) are skipped.
+void ep_return_rows(const void* y, const void* meta, const int* offsets, int El, const EpPeers& ys, int rows, int D,
+                    cudaStream_t s);
+// Combine backward on the source when the owners pushed outputs to its slots ys [T*K, D]:
+//   dwts[t,k] = <dout[t], ys[t*K+k]>;  owner's dy row slot[t,k] <- dout[t] * w[t,k] (peer store).
+void ep_source_bwd(const void* dout, const void* ys, const int* slot, const int* idx, const float* w, float* dwts,
+                   const EpPeers& dy, int T, int K, int El, int D, cudaStream_t s);
 // Owner side of the combine backward, over the local receive rows:
 //   dot = <dy[r], y[r]> -> written to dw_src_rank[pair] (peer store);  dy[r] *= w[r];
 // padding rows (beyond kept[g] in each 128-padded group) are zeroed.

@@ -22,6 +22,7 @@
 // memory.  Every wait is bounded and reports through the status block.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <stdexcept>
 
 #include "common.cuh"
@@ -301,6 +302,11 @@ int skinny_ksplit(const SkinnyDesc& d) {
   // extra K splits only add fp32 partial-sum traffic (red.global) and a ragged last wave.  With
   // at least 3/4 of an SM's worth of slabs there is no split (direct bf16 epilogue, no workspace).
   int ks = base * 4 >= sms * 3 ? 1 : std::max(1, sms / base);
+  static const int forced = [] {
+    const char* e = getenv("OMNI_SKINNY_SPLIT");  // fixed split count (measurements)
+    return e != nullptr ? std::max(0, atoi(e)) : 0;
+  }();
+  if (forced > 0) ks = forced;
   ks = std::max(1, std::min(ks, std::max(1, nkb / 4)));
   const int kb_per = (nkb + ks - 1) / ks;
   return (nkb + kb_per - 1) / kb_per;

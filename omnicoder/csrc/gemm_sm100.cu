@@ -64,6 +64,7 @@ struct GemmArgs {
   int nsrc, me, src_rows;
   int mt_rot;                      // dense raster: rotate the M tiles so a rank starts on its own rows
   void* peer_c[GEMM_MAX_PEERS];
+  const int4* row_meta;            // EPI_EP_PUSH: (weight, source rank, pair index, -) per row
   int tma_c;                       // bf16 / SwiGLU outputs leave through shared memory + TMA stores
   int rows_c;                      // rows of C (per group in grouped-K mode)
 };
@@ -724,6 +725,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_wait_ld();
           store_swiglu(p, row, ti.n0 + c * 64, gt, up, row_ok);
         }
+      } else if (EPI == EPI_EP_PUSH) {
+        // Rows go to different ranks' slots: each 32 x 64 chunk is transposed through this warp's
+        // shared-memory box so that every store instruction writes four whole 128-byte row
+        // segments (eight lanes per row) instead of 32 scattered 16-byte pieces (small writes
+        // waste most of an NVLink packet).
+        int4 m = make_int4(0, -1, 0, 0);
+        if (row_ok) m = p.row_meta[row];
+        const bool valid = m.y >= 0 && m.y < p.nsrc && m.z >= 0 && m.z < p.src_rows;
+        if (row_ok && m.y >= 0 && !valid) report_error(p.status, STATUS_BAD_INDEX, m.z);
+        const unsigned long long rp =
+            valid ? reinterpret_cast<unsigned long long>(reinterpret_cast<__nv_bfloat16*>(p.peer_c[m.y]) +
+                                                         (long long)m.z * p.ldc)
+                  : 0ull;
+        uint8_t* box = stg.base;
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          float a[32], b[32];
+          tmem_ld32(tbase + c * 64, a);
+          tmem_ld32(tbase + c * 64 + 32, b);
+          tc_wait_ld();
+          uint32_t w[32];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            w[j] = zero ? 0u : pack_bf16x2(a[2 * j] * p.alpha, a[2 * j + 1] * p.alpha);
+            w[16 + j] = zero ? 0u : pack_bf16x2(b[2 * j] * p.alpha, b[2 * j + 1] * p.alpha);
+          }
+          __syncwarp();                       // the previous chunk's reads of the box are done
+          EpiStage::put_row(box, lane, w);
+          __syncwarp();
+          const int col0 = ti.n0 + c * 64;
+#pragma unroll
+          for (int pass = 0; pass < 8; ++pass) {
+            const int r = pass * 4 + (lane >> 3), q = lane & 7;
+            const unsigned long long dst = __shfl_sync(0xffffffffu, rp, r);
+            const int colq = col0 + q * 8;
+            if (dst != 0ull && colq < p.N) {
+              const uint4 v = *reinterpret_cast<const uint4*>(box + r * 128 + ((q ^ (r & 7)) << 4));
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(dst) + colq) = v;
+            }
+          }
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -959,6 +1001,7 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
   p.src_rows = d.src_rows > 0 ? d.src_rows : 1;
   p.mt_rot = 0;
   for (int r = 0; r < GEMM_MAX_PEERS; ++r) p.peer_c[r] = d.peer_c[r];
+  p.row_meta = reinterpret_cast<const int4*>(d.row_meta);
   if (MODE == GEMM_AG) {
     p.mt_rot = d.me * (d.src_rows / kBM);               // start on this rank's own rows
   } else if (EPI == EPI_PEER_BF16) {
@@ -1060,6 +1103,7 @@ template <bool A_MN, bool B_MN, int EPI, int MODE>
 constexpr bool combo_supported() {
   if (MODE == GEMM_AG) return !A_MN && (EPI == EPI_STORE_BF16 || (EPI == EPI_SWIGLU && !B_MN));
   if (EPI == EPI_PEER_BF16) return !A_MN && MODE == GEMM_DENSE;
+  if (EPI == EPI_EP_PUSH) return !A_MN && MODE == GEMM_GROUPED_M;
   if (EPI == EPI_SWIGLU) return !A_MN && !B_MN && MODE != GEMM_GROUPED_K;
   if (EPI == EPI_SWIGLU_BWD) return !A_MN && B_MN && MODE != GEMM_GROUPED_K;
   if (EPI == EPI_ADD_BF16) return !A_MN && MODE == GEMM_DENSE;
@@ -1087,6 +1131,7 @@ static void dispatch_epi(const GemmDesc& d, cudaStream_t s) {
     case EPI_SWIGLU: dispatch_checked<A_MN, B_MN, EPI_SWIGLU, MODE>(d, s); break;
     case EPI_SWIGLU_BWD: dispatch_checked<A_MN, B_MN, EPI_SWIGLU_BWD, MODE>(d, s); break;
     case EPI_PEER_BF16: dispatch_checked<A_MN, B_MN, EPI_PEER_BF16, MODE>(d, s); break;
+    case EPI_EP_PUSH: dispatch_checked<A_MN, B_MN, EPI_EP_PUSH, MODE>(d, s); break;
     default: throw std::runtime_error("omnicoder gemm: unknown epilogue");
   }
 }
@@ -1141,7 +1186,7 @@ void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream) {
     auto aligned = [](const void* ptr, long long ld, int elem) {
       return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && (ld * elem) % 16 == 0);
     };
-    if (d.epilogue != EPI_PEER_BF16 && !aligned(d.C, d.ldc, c_elem))
+    if (d.epilogue != EPI_PEER_BF16 && d.epilogue != EPI_EP_PUSH && !aligned(d.C, d.ldc, c_elem))
       throw std::runtime_error("omnicoder gemm: output base and row stride must be 16-byte aligned");
     if (d.mode == GEMM_GROUPED_K && (d.c_group_stride * c_elem) % 16 != 0)
       throw std::runtime_error("omnicoder gemm: output group stride must be 16-byte aligned");
@@ -1151,6 +1196,9 @@ void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream) {
   if (d.epilogue == EPI_PEER_BF16 &&
       (d.nsrc < 1 || d.nsrc > GEMM_MAX_PEERS || d.src_rows <= 0 || d.src_rows % kBM != 0 || d.M != d.nsrc * d.src_rows))
     throw std::runtime_error("omnicoder gemm: peer-store epilogue needs M = ranks x src_rows, src_rows % 128 == 0");
+  if (d.epilogue == EPI_EP_PUSH &&
+      (d.row_meta == nullptr || d.nsrc < 1 || d.nsrc > GEMM_MAX_PEERS || d.src_rows <= 0 || d.ldc % 8 != 0))
+    throw std::runtime_error("omnicoder gemm: expert push epilogue needs row metadata, 1..8 ranks, rows and ldc % 8");
   if (d.num_groups > GEMM_MAX_GROUPS) throw std::runtime_error("omnicoder gemm: too many groups");
   if (d.K % 8 != 0 && !(d.mode == GEMM_GROUPED_K)) throw std::runtime_error("omnicoder gemm: K must be a multiple of 8");
   const int combo = (d.a_mn_major ? 2 : 0) | (d.b_mn_major ? 1 : 0);

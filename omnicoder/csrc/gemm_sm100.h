@@ -21,6 +21,9 @@ enum GemmEpi : int {
   EPI_SWIGLU_BWD = 5,  // acc = dAct; R = saved H; C = dH (bf16, 2N cols, interleaved by 32)
   EPI_PEER_BF16 = 6,   // bf16 partial tile stored into its row owner's staging buffer (peer memory):
                        // row -> owner r = row / src_rows, slot me: peer_c[r] + (me*src_rows + row%src_rows)*ldc
+  EPI_EP_PUSH = 7,     // grouped-M: row r goes to its origin (expert-parallel combine from the epilogue):
+                       // row_meta[r] = (weight, source rank s, pair index i, -) -> peer_c[s] + i*ldc
+                       // (rows with s < 0 are padding and are not stored; i < src_rows is checked)
 };
 
 constexpr int GEMM_MAX_PEERS = 8;
@@ -64,6 +67,7 @@ struct GemmDesc {
   int src_rows = 0;                          // rows per rank (multiple of 128)
   const void* peer_a[GEMM_MAX_PEERS] = {};   // GEMM_AG: each rank's A row block ([src_rows, K], stride lda)
   void* peer_c[GEMM_MAX_PEERS] = {};         // EPI_PEER_BF16: each rank's staging buffer
+  const void* row_meta = nullptr;            // EPI_EP_PUSH: int4 per row of A
 };
 
 // Launch on `stream`.  Throws std::runtime_error on an invalid description.

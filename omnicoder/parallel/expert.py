@@ -90,7 +90,7 @@ class EPContext:
     """Expert-parallel group of one process: rank, world, transport, arena."""
 
     def __init__(self, group=None, transport: str = "auto", device=None, arena_bytes: int = 1 << 30,
-                 layout: str = "device", buffer_factor: float = 2.0):
+                 layout: str = "device", buffer_factor: float = 2.0, epilogue_push: bool = True):
         """layout (p2p transport): "device" -- routing counts are exchanged and the receive
         layout is computed on the device; every MoE layer has fixed slabs of
         El * seg_cap rows per rank (seg_cap = the capacity, or, dropless, buffer_factor x the
@@ -99,11 +99,14 @@ class EPContext:
         rows fit its slab; when they do not, each of its experts keeps at most seg_cap rows
         (the pairs lost are counted in `dropped_pairs()`).  "host" -- counts are all-gathered
         to the host once per layer and the slabs are sized exactly (no drop beyond the
-        capacity)."""
+        capacity).  epilogue_push (device layout, bf16 experts): the expert GEMMs' epilogues
+        store their output rows into the sources' (token, k) slots; False: the rows are
+        written locally and returned by a copy kernel afterwards."""
         if layout not in ("device", "host"):
             raise ValueError(f"unknown expert-parallel layout {layout!r}")
         self.layout = layout
         self.buffer_factor = float(buffer_factor)
+        self.epilogue_push = bool(epilogue_push)
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
@@ -196,9 +199,9 @@ class EPContext:
             plan["shared"] = _Shared(arena, N, R, D, T * k, E, backward=train)
         i = self._cursor if train else 0
         if i == len(plan["slots"]):
-            plan["slots"].append(_Slot(arena, N, R, D, E, El, cap, self.device))
+            plan["slots"].append(_Slot(arena, N, R, D, E, El, cap, self.device, T * k))
         sl = plan["slots"][i]
-        if (sl.R, sl.D, sl.E, sl.cap) != (R, D, E, cap):
+        if (sl.R, sl.D, sl.E, sl.cap, sl.pairs) != (R, D, E, cap, T * k):
             raise ValueError("MoE layers of one step changed shape between steps")
         if train:
             self._cursor += 1
@@ -213,14 +216,15 @@ class EPContext:
 
 
 class _Slot:
-    """Fixed peer-mapped slabs of one MoE layer (device layout): receive rows x, routing
-    metadata, expert outputs y; plus this rank's device-computed layout tensors."""
+    """Fixed peer-mapped slabs of one MoE layer (device layout): receive rows x and their routing
+    metadata (owner side), the (token, k) slots ys that the owners' down-projection epilogues
+    push the expert outputs into (source side); plus this rank's device-computed layout."""
 
-    def __init__(self, arena, N, R, D, E, El, cap, device):
-        self.R, self.D, self.E, self.cap = R, D, E, cap
+    def __init__(self, arena, N, R, D, E, El, cap, device, pairs):
+        self.R, self.D, self.E, self.cap, self.pairs = R, D, E, cap, pairs
         self.x = arena.alloc([R * D * 2] * N)
         self.meta = arena.alloc([R * 16] * N)
-        self.y = arena.alloc([R * D * 2] * N)
+        self.ys = arena.alloc([pairs * D * 2] * N)
         z = lambda n: torch.zeros(n, dtype=torch.int32, device=device)
         self.dst_base, self.keep_lim, self.offs_local, self.kept_local = z(E), z(E), z(El + 1), z(El)
         self.rows = [R] * N
@@ -228,16 +232,15 @@ class _Slot:
 
 class _Shared:
     """Slabs shared by every MoE layer (device layout): the count board and, when training,
-    the backward's output gradients pushed to the owners, input gradients pulled back and
-    routing-weight gradients."""
+    the backward's weighted output gradients pushed to the owners (receive rows) and the input
+    gradients that the owners' epilogues push back into the sources' (token, k) slots."""
 
     def __init__(self, arena, N, R, D, pairs, E, backward: bool = True):
         self.board = arena.alloc([N * E * 4] * N)
-        self.dy = self.dx = self.dw = None
+        self.dy = self.dxs = None
         if backward:
             self.dy = arena.alloc([R * D * 2] * N)
-            self.dx = arena.alloc([R * D * 2] * N)
-            self.dw = arena.alloc([pairs * 4] * N)
+            self.dxs = arena.alloc([pairs * D * 2] * N)
         self.pairs = [pairs] * N
 
 
@@ -383,22 +386,32 @@ class _EPMoEDev(torch.autograd.Function):
         meta = sl.meta.view(torch.int32, R, 4)
         C.ep_pad_rows(x_recv, meta, sl.offs_local, sl.kept_local)
         arena.barrier()                                       # all pairs have landed
-        y_recv = sl.y.view(torch.bfloat16, R, D)
         offs_local = sl.offs_local
         q13 = ep.fp8_weights.get(id(w13)) if ep.fp8_weights else None
         q2 = ep.fp8_weights.get(id(w2)) if ep.fp8_weights else None
+        # the down projection's epilogue stores every output row into its source's (token, k)
+        # slot (over NVLink for peers), so the combine transfer overlaps the GEMM (the block-scaled
+        # GEMM writes its rows locally and ep_return_rows sends them)
         if q13 is not None and q2 is not None:
             from ..ops.fp8 import fp8_grouped_swiglu
             # SwiGLU and the requantisation of its output run in the gate|up GEMM's epilogue
             H, act, aq, sa = fp8_grouped_swiglu(x_recv, q13[0], q13[1], offs_local, R)
-            C.fp8_gemm(aq, sa, q2[0], q2[1].reshape(-1), y_recv, offs_local, R)
+            y_loc = torch.empty(R, D, device=x.device, dtype=torch.bfloat16)
+            C.fp8_gemm(aq, sa, q2[0], q2[1].reshape(-1), y_loc, offs_local, R)
+            C.ep_return_rows(y_loc, meta, offs_local, sl.ys.ptrs, [T * k] * ep.world)
         else:
             act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)
             H = torch.empty(R, F2, device=x.device, dtype=torch.bfloat16)
             C.gemm_grouped_m(x_recv, w13, offs_local, act, False, EPI_SWIGLU, 1.0, None, H, 256, R)
-            C.gemm_grouped_m(act, w2, offs_local, y_recv, False, EPI_BF16, 1.0, None, None, 256, R)
-        arena.barrier()                                       # every owner's outputs are ready
-        out = C.ep_combine(slot, idx, wts, sl.y.ptrs, sl.rows, El, D, None if add is None else add.contiguous())
+            if ep.epilogue_push:
+                C.gemm_grouped_m_push(act, w2, offs_local, meta, sl.ys.ptrs, T * k, False, R)
+            else:
+                y_loc = torch.empty(R, D, device=x.device, dtype=torch.bfloat16)
+                C.gemm_grouped_m(act, w2, offs_local, y_loc, False, EPI_BF16, 1.0, None, None, 256, R)
+                C.ep_return_rows(y_loc, meta, offs_local, sl.ys.ptrs, [T * k] * ep.world)
+        arena.barrier()                                       # every owner has pushed its outputs
+        ys = sl.ys.view(torch.bfloat16, T * k, D)
+        out = C.ep_combine_local(slot, ys, wts, None if add is None else add.contiguous())
         ctx.save_for_backward(x, router_w, w13, w2, logits, probs, idx, wts, counts, slot, H, act)
         # the slabs are views of the shared arena (kept on ctx, not saved tensors); the next
         # forward of this layer rewrites them only after this backward
@@ -425,33 +438,40 @@ class _EPMoEDev(torch.autograd.Function):
         R = sl.R
         x_recv = sl.x.view(torch.bfloat16, R, D)
         meta = sl.meta.view(torch.int32, R, 4)
-        y_recv = sl.y.view(torch.bfloat16, R, D)
+        ys = sl.ys.view(torch.bfloat16, T * k, D)
         dout = dout.contiguous()
-        dwts = sh.dw.view(torch.float32, T, k)
-        dwts.zero_()                                          # dropped pairs keep a zero gradient
-        C.ep_push(dout, slot, idx, sh.dy.ptrs, sl.rows, El)
+        # routing-weight gradients from the pushed outputs (local), weighted output gradients
+        # pushed to the owners' receive rows
+        dwts = torch.empty(T, k, device=x.device, dtype=torch.float32)
+        C.ep_source_bwd(dout, ys, slot, idx, wts, dwts, sh.dy.ptrs, sl.rows, El)
         arena.barrier()                                       # all output gradients have landed
         dy_recv = sh.dy.view(torch.bfloat16, R, D)
-        C.ep_owner_bwd(dy_recv, y_recv, meta, sl.offs_local, sl.kept_local, sh.dw.ptrs, sh.pairs)
+        C.ep_pad_rows(dy_recv, None, sl.offs_local, sl.kept_local)
         dH = torch.empty_like(H)
         C.gemm_grouped_m(dy_recv, w2, sl.offs_local, dH, True, EPI_SWIGLU_BWD, 1.0, H, None, 256, R)
         dw2 = torch.empty_like(w2)
         C.gemm_grouped_k(dy_recv, act, sl.offs_local, dw2, EPI_BF16, 1.0, 256)
-        dx_recv = sh.dx.view(torch.bfloat16, R, D)
         q13t = ep.fp8_weights.get(("t", id(w13))) if ep.fp8_weights else None
+        # input gradients pushed by the epilogue into the sources' (token, k) slots
         if q13t is not None:
             # fp8 input gradient through the gate|up experts (dH per 1 x 128 block, w13^T blocks)
             from ..ops.fp8 import quantize_act
             dq, sdq = quantize_act(dH, offsets=sl.offs_local)
-            C.fp8_gemm(dq, sdq, q13t[0], q13t[1].reshape(-1), dx_recv, sl.offs_local, R)
+            dx_loc = torch.empty(R, D, device=x.device, dtype=torch.bfloat16)
+            C.fp8_gemm(dq, sdq, q13t[0], q13t[1].reshape(-1), dx_loc, sl.offs_local, R)
+            C.ep_return_rows(dx_loc, meta, sl.offs_local, sh.dxs.ptrs, [T * k] * ep.world)
+        elif ep.epilogue_push:
+            C.gemm_grouped_m_push(dH, w13, sl.offs_local, meta, sh.dxs.ptrs, T * k, True, R)
         else:
-            C.gemm_grouped_m(dH, w13, sl.offs_local, dx_recv, True, EPI_BF16, 1.0, None, None, 256, R)
+            dx_loc = torch.empty(R, D, device=x.device, dtype=torch.bfloat16)
+            C.gemm_grouped_m(dH, w13, sl.offs_local, dx_loc, True, EPI_BF16, 1.0, None, None, 256, R)
+            C.ep_return_rows(dx_loc, meta, sl.offs_local, sh.dxs.ptrs, [T * k] * ep.world)
         dw13 = torch.empty_like(w13)
         C.gemm_grouped_k(dH, x_recv, sl.offs_local, dw13, EPI_BF16, 1.0, 256)
         arena.barrier()                                       # input gradients and weight gradients are ready
         dlogits, _ = C.router_bwd(logits, probs, idx, dwts, counts, renorm, aux_alpha * gs, z_beta * gs)
         dx_router = mm_nn(dlogits, router_w)
-        dx = C.ep_combine(slot, idx, None, sh.dx.ptrs, sl.rows, El, D, dx_router)
+        dx = C.ep_combine_local(slot, sh.dxs.view(torch.bfloat16, T * k, D), None, dx_router)
         drouter = mm_tn(dlogits, x)
         return (dx, drouter, dw13, dw2, (dout if has_add else None), None, None, None, None, None, None, None, None)
 

@@ -44,7 +44,8 @@ class ExpertDataParallel:
     @staticmethod
     def arena_bytes_for(cfg, tokens_per_rank: int, world: int, buffer_factor: float = 2.0) -> int:
         """Peer-mapped bytes per rank that the device-layout exchange of one step of `cfg` needs
-        (every MoE layer's x / metadata / y slabs, the shared backward slabs, the count board)."""
+        (every MoE layer's receive rows / metadata and (token, k) output slots, the shared
+        backward slabs, the count board)."""
         import math
         m = cfg.moe
         E, k, D = m.n_experts, m.top_k, cfg.d_model
@@ -56,8 +57,9 @@ class ExpertDataParallel:
             seg = max(128, (math.ceil(buffer_factor * world * tokens_per_rank * k / E) + 127) // 128 * 128)
         R = El * seg
         n_moe = sum(1 for i in range(cfg.n_layers) if cfg.is_moe_layer(i))
-        per_layer = 2 * R * D * 2 + R * 16
-        shared = 2 * R * D * 2 + tokens_per_rank * k * 4 + world * E * 4
+        pairs = tokens_per_rank * k
+        per_layer = R * D * 2 + R * 16 + pairs * D * 2
+        shared = R * D * 2 + pairs * D * 2 + world * E * 4
         return n_moe * (per_layer + 1024) + shared + (1 << 20)
 
     # ---- model construction -------------------------------------------------
