@@ -20,8 +20,24 @@ from omnicoder.benchmarks.timing import time_fn
 from omnicoder.ops import _ext, fp8
 
 
-def main():
+def main(argv=None):
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--calls", type=int, default=0,
+                    help="only run the 8192^3 block-scaled GEMM this many times, untimed (a small case for a profiler)")
+    a = ap.parse_args(argv)
     C = _ext.load()
+    if a.calls:
+        x = torch.randn(8192, 8192, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(8192, 8192, device="cuda") * 0.02).to(torch.bfloat16)
+        xq, sx = fp8.quantize_act(x)
+        wq, sw = fp8.quantize_weight(w)
+        out = torch.empty(8192, 8192, device="cuda", dtype=torch.bfloat16)
+        for _ in range(a.calls):
+            C.fp8_gemm(xq, sx, wq, sw.reshape(-1), out)
+        torch.cuda.synchronize()
+        _ext.check_status()
+        return
     res = []
     for name, M, N, K in [("square_8192", 8192, 8192, 8192), ("expert_gate_up_dense", 6144, 2816, 4096),
                           ("expert_down_dense", 6144, 4096, 1408 // 128 * 128)]:

@@ -1,7 +1,7 @@
 """Memory-bound kernels of the training and decode steps, each timed alone against the
 measured HBM copy bandwidth: RMSNorm forward / backward (fused residual add), RoPE,
 router top-k, the MoE permutation plan, gather and weighted combine, the int8 KV-cache
-append and the int4 weight-only GEMV.
+append, the int4 weight-only GEMV and the speculative-verification kernel.
 
     python -m omnicoder.benchmarks.bench_small_kernels [--only rmsnorm,rope,...] [--calls N]
 
@@ -78,6 +78,15 @@ def cases(dev):
     xr = torch.randn(1, K4, device=dev, dtype=bf)
     out["int4_gemv (1 x 2048 @ 4096 x 2048)"] = (lambda: C.int4_gemv(xr, packed, scale, 7.0),
                                                 packed.numel() + scale.numel() * 4 + N4 * 2 + K4 * 2)
+    # speculative verification: 64 sequences x 4 draft tokens, vocab 32000, sampled (temperature 1)
+    Bs, Ks, V = 64, 4, 32000
+    lg = torch.randn(Bs, Ks + 1, V, device=dev)
+    pd = torch.softmax(torch.randn(Bs, Ks, V, device=dev), -1)
+    dr = torch.randint(0, V, (Bs, Ks), device=dev)
+    us = torch.rand(Bs, Ks + 1, device=dev)
+    bl = torch.full((Bs,), 8192, device=dev, dtype=torch.long)
+    out["spec_verify (64 x 4 drafts, vocab 32000)"] = (lambda: C.spec_verify(lg, pd, dr, us, bl, 1.0),
+                                                      lg.numel() * 4 + pd.numel() * 4)
     return out
 
 
