@@ -14,7 +14,8 @@ inputs (>= 67 MB) and expert weights exceed L2 only together, so L2 is
 flushed before every timed iteration.
 
 Transports: p2p (fused NVLink exchange, bf16 expert GEMMs whose epilogues store the output rows
-into the sources' slots), p2p_ret (the same with local GEMM outputs returned by a copy kernel
+into the sources' slots), p2p_gate (the same, with the grouped GEMMs starting each tile as the
+sources of its rows signal instead of after a barrier), p2p_ret (local GEMM outputs returned by a copy kernel
 after the GEMM), p2p_fp8 (the same
 exchange with block-scaled fp8 expert GEMMs -- 1 x 128 activation and 128 x 128
 weight scales, power-of-two -- in the forward (SwiGLU and requantisation in the
@@ -49,7 +50,7 @@ def main(argv=None):
     ap.add_argument("--cf", type=float, default=1.25)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--transports", default="p2p,p2p_ret,p2p_fp8,nccl",
+    ap.add_argument("--transports", default="p2p,p2p_gate,p2p_ret,p2p_fp8,nccl",
                     help="p2p (bf16 expert GEMMs), p2p_fp8 (block-scaled fp8 forward expert GEMMs), nccl")
     a = ap.parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -77,7 +78,8 @@ def main(argv=None):
     for tr in a.transports.split(","):
         fp8 = tr == "p2p_fp8"
         ep = EPContext(dist.group.WORLD, transport="nccl" if tr == "nccl" else "p2p", device=dev,
-                       arena_bytes=rows * (4 * D * 2 + 16), epilogue_push=tr != "p2p_ret")
+                       arena_bytes=rows * (4 * D * 2 + 16), epilogue_push=tr != "p2p_ret",
+                       gate_tiles=tr == "p2p_gate")
         if fp8:
             ep.set_fp8_weights(w13, w2)   # once per optimiser step in training; outside the timed region
 

@@ -205,7 +205,9 @@ void gemm_skinny_grouped(const at::Tensor& A, const at::Tensor& B, const at::Ten
 // B is [G, N, K] (b_mn=false) or [G, K, N] (b_mn=true).
 void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor& C,
                     bool b_mn, int64_t epilogue, double alpha, const c10::optional<at::Tensor>& R,
-                    const c10::optional<at::Tensor>& H, int64_t block_n, int64_t max_rows_hint) {
+                    const c10::optional<at::Tensor>& H, int64_t block_n, int64_t max_rows_hint,
+                    int64_t ready_ptr, const c10::optional<at::Tensor>& ready_epoch,
+                    const c10::optional<at::Tensor>& src_pref, int64_t nsrc, int64_t me) {
   CHECK_CUDA_T(A);
   CHECK_BF16(A);
   CHECK_BF16(B);
@@ -253,6 +255,16 @@ void gemm_grouped_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   if (epilogue == EPI_SWIGLU && H.has_value()) {
     d.H = H->data_ptr();
     d.ldh = H->stride(0);
+  }
+  if (ready_ptr != 0) {
+    TORCH_CHECK(ready_epoch.has_value() && src_pref.has_value() && ready_epoch->is_cuda() &&
+                    src_pref->scalar_type() == at::kInt && src_pref->numel() == B.size(0) * (nsrc + 1),
+                "gemm_grouped_m: readiness gating needs the epoch counter and src_pref [G, ranks + 1]");
+    d.ready = reinterpret_cast<const unsigned*>(ready_ptr);
+    d.ready_epoch = reinterpret_cast<const unsigned*>(ready_epoch->data_ptr());
+    d.src_pref = src_pref->data_ptr<int>();
+    d.nsrc = (int)nsrc;
+    d.me = (int)me;
   }
   d.status = status_ptr();
   gemm_sm100_launch(d, cur_stream());
@@ -672,7 +684,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair_enabled", &omni::gemm_pair_enabled);
   m.def("gemm_grouped_m", &omni::gemm_grouped_m, py::arg("A"), py::arg("B"), py::arg("offsets"), py::arg("C"),
         py::arg("b_mn"), py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("R") = py::none(),
-        py::arg("H") = py::none(), py::arg("block_n") = 256, py::arg("max_rows_hint") = 0);
+        py::arg("H") = py::none(), py::arg("block_n") = 256, py::arg("max_rows_hint") = 0,
+        py::arg("ready_ptr") = 0, py::arg("ready_epoch") = py::none(), py::arg("src_pref") = py::none(),
+        py::arg("nsrc") = 0, py::arg("me") = 0);
   m.def("gemm_grouped_k", &omni::gemm_grouped_k, py::arg("A"), py::arg("B"), py::arg("offsets"), py::arg("C"),
         py::arg("epilogue"), py::arg("alpha") = 1.0, py::arg("block_n") = 256);
   omni::register_kernels(m);

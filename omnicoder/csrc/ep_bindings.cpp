@@ -153,7 +153,8 @@ void ep_barrier_dev_t(const std::vector<int64_t>& sig_ptrs, int64_t me, at::Tens
 void ep_exchange_layout_t(const at::Tensor& counts, const std::vector<int64_t>& board_ptrs,
                           const std::vector<int64_t>& sig_ptrs, int64_t me, at::Tensor& epoch_ctr, int64_t El,
                           int64_t capacity, int64_t seg_cap, at::Tensor& dst_base, at::Tensor& keep_lim,
-                          at::Tensor& offs_local, at::Tensor& kept_local, at::Tensor& dropped) {
+                          at::Tensor& offs_local, at::Tensor& kept_local, at::Tensor& dropped,
+                          const c10::optional<at::Tensor>& src_pref) {
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&counts, &epoch_ctr, &dst_base, &keep_lim,
                                                                        &offs_local, &kept_local, &dropped})
     check(*t, at::kInt, "ep_exchange_layout");
@@ -165,11 +166,24 @@ void ep_exchange_layout_t(const at::Tensor& counts, const std::vector<int64_t>& 
                   kept_local.numel() == El && dropped.numel() >= 1,
               "ep_exchange_layout: output sizes");
   TORCH_CHECK(seg_cap > 0 && seg_cap % 128 == 0, "ep_exchange_layout: seg_cap must be a positive multiple of 128");
+  if (src_pref.has_value()) {
+    check(*src_pref, at::kInt, "ep_exchange_layout src_pref");
+    TORCH_CHECK(src_pref->numel() == El * (n + 1), "ep_exchange_layout: src_pref [El, ranks + 1]");
+  }
   const c10::cuda::CUDAGuard g(counts.device());
   ep_exchange_layout(make_peers(board_ptrs, {}), make_peers(sig_ptrs, {}), (int)me, (int)n,
                      reinterpret_cast<unsigned*>(epoch_ctr.data_ptr<int>()), counts.data_ptr<int>(), (int)E, (int)El,
                      (int)capacity, (int)seg_cap, dst_base.data_ptr<int>(), keep_lim.data_ptr<int>(),
-                     offs_local.data_ptr<int>(), kept_local.data_ptr<int>(), dropped.data_ptr<int>(), stream());
+                     offs_local.data_ptr<int>(), kept_local.data_ptr<int>(), dropped.data_ptr<int>(), stream(),
+                     src_pref.has_value() ? src_pref->data_ptr<int>() : nullptr);
+}
+
+void ep_signal_t(const std::vector<int64_t>& flag_ptrs, int64_t me, at::Tensor& sig_ctr) {
+  check(sig_ctr, at::kInt, "ep_signal");
+  const c10::cuda::CUDAGuard g(sig_ctr.device());
+  TORCH_CHECK(!flag_ptrs.empty() && flag_ptrs.size() <= (size_t)kEpMaxRanks, "ep_signal: 1..8 ranks");
+  ep_signal(make_peers(flag_ptrs, {}), (int)me, (int)flag_ptrs.size(),
+            reinterpret_cast<unsigned*>(sig_ctr.data_ptr<int>()), stream());
 }
 
 void zero_rs_t(const std::vector<int64_t>& g_ptrs, int64_t lo, int64_t n, double scale, at::Tensor& out,
@@ -207,7 +221,11 @@ void register_ep(pybind11::module_& m) {
   m.def("ep_pad_rows", &ep_pad_rows_t);
   m.def("ep_barrier", &ep_barrier_t);
   m.def("ep_barrier_dev", &ep_barrier_dev_t);
-  m.def("ep_exchange_layout", &ep_exchange_layout_t);
+  m.def("ep_exchange_layout", &ep_exchange_layout_t, py::arg("counts"), py::arg("board_ptrs"), py::arg("sig_ptrs"),
+        py::arg("me"), py::arg("epoch_ctr"), py::arg("El"), py::arg("capacity"), py::arg("seg_cap"),
+        py::arg("dst_base"), py::arg("keep_lim"), py::arg("offs_local"), py::arg("kept_local"), py::arg("dropped"),
+        py::arg("src_pref") = py::none());
+  m.def("ep_signal", &ep_signal_t);
   m.def("zero_rs", &zero_rs_t, py::arg("g_ptrs"), py::arg("lo"), py::arg("n"), py::arg("scale"), py::arg("out"),
         py::arg("norm_sq") = py::none());
   m.def("zero_adamw_push", &zero_adamw_push_t, py::arg("p"), py::arg("m"), py::arg("v"), py::arg("g"),

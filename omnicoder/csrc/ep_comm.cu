@@ -352,6 +352,24 @@ __global__ void ep_barrier_dev_kernel(EpPeers sig, int me, int n, unsigned* epoc
   dev_barrier(sig, me, n, epoch_ctr, st);
 }
 
+// One-way readiness signal: advance this rank's signal counter and store it, with release order
+// behind everything this GPU wrote before (the preceding kernels' peer stores included), into
+// slot `me` of every rank's flag array.  Nothing is waited for here; consumers wait per source.
+__global__ void ep_signal_kernel(EpPeers flags, int me, int n, unsigned* sig_ctr) {
+  __shared__ unsigned s_epoch;
+  if (threadIdx.x == 0) {
+    s_epoch = *reinterpret_cast<volatile unsigned*>(sig_ctr) + 1u;
+    *reinterpret_cast<volatile unsigned*>(sig_ctr) = s_epoch;
+  }
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < n) {
+    __threadfence_system();
+    unsigned* f = reinterpret_cast<unsigned*>(flags.ptr[t]) + me;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(s_epoch) : "memory");
+  }
+}
+
 // Routing-count exchange and receive layout, computed on the device by every rank alike.
 // Each rank stores its per-expert pair counts into row `me` of every rank's count board
 // [N][E], passes a device barrier, then derives from the board (C[s][e] = pairs of source s
@@ -368,7 +386,7 @@ __global__ void ep_exchange_layout_kernel(EpPeers board, EpPeers sig, int me, in
                                           const int* __restrict__ counts, int E, int El, int capacity, int seg_cap,
                                           int* __restrict__ dst_base, int* __restrict__ keep_lim,
                                           int* __restrict__ offs_local, int* __restrict__ kept_local,
-                                          int* __restrict__ dropped, StatusBlock* st) {
+                                          int* __restrict__ dropped, int* __restrict__ src_pref, StatusBlock* st) {
   extern __shared__ int sh[];
   int* C = sh;                 // [n][E]
   int* seg_pad = sh + n * E;   // [E]
@@ -405,10 +423,13 @@ __global__ void ep_exchange_layout_kernel(EpPeers board, EpPeers sig, int me, in
   int kept_me = 0, before_me = 0, seg = 0, lost_me = 0;
   if (e < E) {
     const int cap = bounded ? min(cap0, seg_cap) : cap0;
+    const bool local = e / El == me;
     int before = 0;
     for (int s = 0; s < n; ++s) {
       const int c = C[s * E + e];
       const int k = max(0, min(c, cap - before));
+      // rows of source s in this rank's segment of expert e start at seg (sources in rank order)
+      if (local && src_pref != nullptr) src_pref[(e - me * El) * (n + 1) + s] = seg;
       if (s < me) before_me += k;
       if (s == me) {
         kept_me = k;
@@ -417,6 +438,7 @@ __global__ void ep_exchange_layout_kernel(EpPeers board, EpPeers sig, int me, in
       seg += k;
       before += c;
     }
+    if (local && src_pref != nullptr) src_pref[(e - me * El) * (n + 1) + n] = seg;
     seg_pad[e] = (seg + 127) / 128 * 128;
   }
   __syncthreads();
@@ -508,12 +530,16 @@ void ep_barrier_dev(const EpPeers& sig, int me, int n, unsigned* epoch_ctr, cuda
 
 void ep_exchange_layout(const EpPeers& board, const EpPeers& sig, int me, int n, unsigned* epoch_ctr,
                         const int* counts, int E, int El, int capacity, int seg_cap, int* dst_base, int* keep_lim,
-                        int* offs_local, int* kept_local, int* dropped, cudaStream_t s) {
+                        int* offs_local, int* kept_local, int* dropped, cudaStream_t s, int* src_pref) {
   const int threads = std::max(32, (E + 31) / 32 * 32);
   const size_t smem = (size_t)(n * E + E) * sizeof(int);
   ep_exchange_layout_kernel<<<1, threads, smem, s>>>(board, sig, me, n, epoch_ctr, counts, E, El, capacity, seg_cap,
-                                                     dst_base, keep_lim, offs_local, kept_local, dropped,
+                                                     dst_base, keep_lim, offs_local, kept_local, dropped, src_pref,
                                                      (StatusBlock*)status_ptr());
+}
+
+void ep_signal(const EpPeers& flags, int me, int n, unsigned* sig_ctr, cudaStream_t s) {
+  ep_signal_kernel<<<1, 32, 0, s>>>(flags, me, n, sig_ctr);
 }
 
 void ep_barrier(const EpPeers& sig, int me, int n, unsigned epoch, cudaStream_t s) {

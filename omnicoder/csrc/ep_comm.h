@@ -56,7 +56,12 @@ void ep_barrier_dev(const EpPeers& sig, int me, int n, unsigned* epoch_ctr, cuda
 // dropped and counted into *dropped).  E <= 1024.
 void ep_exchange_layout(const EpPeers& board, const EpPeers& sig, int me, int n, unsigned* epoch_ctr,
                         const int* counts, int E, int El, int capacity, int seg_cap, int* dst_base, int* keep_lim,
-                        int* offs_local, int* kept_local, int* dropped, cudaStream_t s);
+                        int* offs_local, int* kept_local, int* dropped, cudaStream_t s, int* src_pref = nullptr);
+// src_pref (optional, [El][n + 1]): row offset of each source's rows inside this rank's segment of
+// each local expert (sources in rank order; entry n = the segment's kept rows).
+// One-way readiness signal: *sig_ctr += 1, then flags.ptr[r][me] = *sig_ctr on every rank r
+// (release order behind this GPU's earlier writes).  Consumers wait per source (bounded).
+void ep_signal(const EpPeers& flags, int me, int n, unsigned* sig_ctr, cudaStream_t s);
 
 // ZeRO-1 step over peer memory (zero_p2p.cu): reduce-scatter of rank-local bf16 gradient
 // buckets g.ptr[r] into this rank's fp32 shard out[0, n) = scale * sum_r g_r[lo + i] (+ its

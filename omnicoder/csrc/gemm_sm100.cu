@@ -65,6 +65,9 @@ struct GemmArgs {
   int mt_rot;                      // dense raster: rotate the M tiles so a rank starts on its own rows
   void* peer_c[GEMM_MAX_PEERS];
   const int4* row_meta;            // EPI_EP_PUSH: (weight, source rank, pair index, -) per row
+  const unsigned* ready;           // grouped-M: per-source readiness flags (nullptr: no gating)
+  const unsigned* ready_epoch;
+  const int* src_pref;             // [G][nsrc + 1]
   int tma_c;                       // bf16 / SwiGLU outputs leave through shared memory + TMA stores
   int rows_c;                      // rows of C (per group in grouped-K mode)
 };
@@ -440,10 +443,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // expert-parallel receive rows: sources whose rows this CTA has seen ready
+      uint32_t seen = 0;
+      const unsigned epoch = (MODE == GEMM_GROUPED_M && p.ready != nullptr) ? *p.ready_epoch : 0u;
       for (int t = tile0; t < ntiles && ok; t += tile_step) {
         const TileInfo ti = tile_info<BN, MODE, TM>(p, t, s_off);
         const int am0 = ti.m0 + (int)crank * kBM;         // this CTA's rows of A
         const int bn0 = ti.n0 + (int)crank * C_::kBNc;    // this CTA's rows of B
+        if (MODE == GEMM_GROUPED_M && p.ready != nullptr) {
+          // wait (bounded) for every other source rank with rows in [m0, m0 + 128) of this group
+          const int r0 = ti.m0 - s_off[ti.g];
+          const int* pref = p.src_pref + ti.g * (p.nsrc + 1);
+          bool waited = false;
+          for (int s = 0; s < p.nsrc && ok; ++s) {
+            if (s == p.me || ((seen >> s) & 1u) || !(pref[s] < r0 + kBM && pref[s + 1] > r0)) continue;
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t spins = 0;
+            while (true) {
+              unsigned v;
+              asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p.ready + s) : "memory");
+              if ((int)(v - epoch) >= 0) break;
+              if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) {
+                report_error(p.status, STATUS_TIMEOUT_PEER_FLAG, s);
+                ok = false;
+                break;
+              }
+            }
+            seen |= 1u << s;
+            waited = true;
+          }
+          if (!ok) break;
+          if (waited) fence_proxy_async_global();  // the rows acquired above, then TMA reads them
+        }
         for (int kb = 0; kb < ti.num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, p.status, STATUS_TIMEOUT_TMA_EMPTY)) {
             ok = false;
@@ -1002,6 +1033,9 @@ static void launch_impl(const GemmDesc& d, cudaStream_t stream) {
   p.mt_rot = 0;
   for (int r = 0; r < GEMM_MAX_PEERS; ++r) p.peer_c[r] = d.peer_c[r];
   p.row_meta = reinterpret_cast<const int4*>(d.row_meta);
+  p.ready = d.ready;
+  p.ready_epoch = d.ready_epoch;
+  p.src_pref = d.src_pref;
   if (MODE == GEMM_AG) {
     p.mt_rot = d.me * (d.src_rows / kBM);               // start on this rank's own rows
   } else if (EPI == EPI_PEER_BF16) {
@@ -1196,6 +1230,9 @@ void gemm_sm100_launch(const GemmDesc& d, cudaStream_t stream) {
   if (d.epilogue == EPI_PEER_BF16 &&
       (d.nsrc < 1 || d.nsrc > GEMM_MAX_PEERS || d.src_rows <= 0 || d.src_rows % kBM != 0 || d.M != d.nsrc * d.src_rows))
     throw std::runtime_error("omnicoder gemm: peer-store epilogue needs M = ranks x src_rows, src_rows % 128 == 0");
+  if (d.ready != nullptr && (d.mode != GEMM_GROUPED_M || d.a_mn_major || d.ready_epoch == nullptr ||
+                            d.src_pref == nullptr || d.nsrc < 1 || d.nsrc > 32))
+    throw std::runtime_error("omnicoder gemm: readiness gating needs grouped-M, K-major A, an epoch and prefixes");
   if (d.epilogue == EPI_EP_PUSH &&
       (d.row_meta == nullptr || d.nsrc < 1 || d.nsrc > GEMM_MAX_PEERS || d.src_rows <= 0 || d.ldc % 8 != 0))
     throw std::runtime_error("omnicoder gemm: expert push epilogue needs row metadata, 1..8 ranks, rows and ldc % 8");

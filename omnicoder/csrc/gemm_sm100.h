@@ -68,6 +68,12 @@ struct GemmDesc {
   const void* peer_a[GEMM_MAX_PEERS] = {};   // GEMM_AG: each rank's A row block ([src_rows, K], stride lda)
   void* peer_c[GEMM_MAX_PEERS] = {};         // EPI_PEER_BF16: each rank's staging buffer
   const void* row_meta = nullptr;            // EPI_EP_PUSH: int4 per row of A
+  // grouped-M, expert-parallel receive rows: a tile is loaded once every source rank with rows in it
+  // has signalled ready[s] >= *ready_epoch (src_pref [G][nsrc+1]: row prefix of each source within
+  // group g; this rank's own rows are not waited for)
+  const unsigned* ready = nullptr;
+  const unsigned* ready_epoch = nullptr;
+  const int* src_pref = nullptr;
 };
 
 // Launch on `stream`.  Throws std::runtime_error on an invalid description.

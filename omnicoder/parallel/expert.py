@@ -90,7 +90,8 @@ class EPContext:
     """Expert-parallel group of one process: rank, world, transport, arena."""
 
     def __init__(self, group=None, transport: str = "auto", device=None, arena_bytes: int = 1 << 30,
-                 layout: str = "device", buffer_factor: float = 2.0, epilogue_push: bool = True):
+                 layout: str = "device", buffer_factor: float = 2.0, epilogue_push: bool = True,
+                 gate_tiles: bool = False):
         """layout (p2p transport): "device" -- routing counts are exchanged and the receive
         layout is computed on the device; every MoE layer has fixed slabs of
         El * seg_cap rows per rank (seg_cap = the capacity, or, dropless, buffer_factor x the
@@ -101,12 +102,16 @@ class EPContext:
         to the host once per layer and the slabs are sized exactly (no drop beyond the
         capacity).  epilogue_push (device layout, bf16 experts): the expert GEMMs' epilogues
         store their output rows into the sources' (token, k) slots; False: the rows are
-        written locally and returned by a copy kernel afterwards."""
+        written locally and returned by a copy kernel afterwards.  gate_tiles (device layout,
+        bf16 experts): instead of a barrier after the dispatch (and after the backward's
+        gradient push), each source signals once its rows are out and the grouped GEMM starts a
+        tile as soon as the sources of its rows have signalled."""
         if layout not in ("device", "host"):
             raise ValueError(f"unknown expert-parallel layout {layout!r}")
         self.layout = layout
         self.buffer_factor = float(buffer_factor)
         self.epilogue_push = bool(epilogue_push)
+        self.gate_tiles = bool(gate_tiles)
         self.group = group if group is not None else dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
@@ -227,6 +232,7 @@ class _Slot:
         self.ys = arena.alloc([pairs * D * 2] * N)
         z = lambda n: torch.zeros(n, dtype=torch.int32, device=device)
         self.dst_base, self.keep_lim, self.offs_local, self.kept_local = z(E), z(E), z(El + 1), z(El)
+        self.src_pref = z(El * (N + 1))     # row offset of each source inside each local expert segment
         self.rows = [R] * N
 
 
@@ -237,6 +243,12 @@ class _Shared:
 
     def __init__(self, arena, N, R, D, pairs, E, backward: bool = True):
         self.board = arena.alloc([N * E * 4] * N)
+        # per-source readiness flags (one-way signals after a source's stores into this rank's
+        # receive rows) and this rank's signal counter; zeroed on every rank before first use
+        self.ready = arena.alloc([max(16, N * 4)] * N)
+        self.ready.view(torch.int32, max(4, N)).zero_()
+        self.sig_ctr = torch.zeros(1, dtype=torch.int32, device=self.ready.local.device)
+        arena.barrier()
         self.dy = self.dxs = None
         if backward:
             self.dy = arena.alloc([R * D * 2] * N)
@@ -379,16 +391,23 @@ class _EPMoEDev(torch.autograd.Function):
         counts, loc_off, pos, _ = C.moe_plan(idx, E, 0, cap_rows_for(T, k, E, 0))
         # counts -> every rank's board, device barrier, layout from the board
         C.ep_exchange_layout(counts, sh.board.ptrs, arena.sig_ptrs, me, arena.epoch_ctr, El, capacity, sl.cap,
-                             sl.dst_base, sl.keep_lim, sl.offs_local, sl.kept_local, ep._dropped)
+                             sl.dst_base, sl.keep_lim, sl.offs_local, sl.kept_local, ep._dropped, sl.src_pref)
         slot = C.ep_dispatch(x, idx, pos, loc_off, sl.dst_base, sl.keep_lim, wts, sl.x.ptrs, sl.meta.ptrs, sl.rows,
                              El, me)
         x_recv = sl.x.view(torch.bfloat16, R, D)
         meta = sl.meta.view(torch.int32, R, 4)
         C.ep_pad_rows(x_recv, meta, sl.offs_local, sl.kept_local)
-        arena.barrier()                                       # all pairs have landed
         offs_local = sl.offs_local
         q13 = ep.fp8_weights.get(id(w13)) if ep.fp8_weights else None
         q2 = ep.fp8_weights.get(id(w2)) if ep.fp8_weights else None
+        gate = {}
+        if (q13 is not None and q2 is not None) or not ep.gate_tiles:
+            arena.barrier()                                   # all pairs have landed
+        else:
+            # one-way signal; the gate|up GEMM starts each tile once the sources of its rows have signalled
+            C.ep_signal(sh.ready.ptrs, me, sh.sig_ctr)
+            gate = dict(ready_ptr=sh.ready.ptrs[me], ready_epoch=sh.sig_ctr, src_pref=sl.src_pref, nsrc=ep.world,
+                        me=me)
         # the down projection's epilogue stores every output row into its source's (token, k)
         # slot (over NVLink for peers), so the combine transfer overlaps the GEMM (the block-scaled
         # GEMM writes its rows locally and ep_return_rows sends them)
@@ -402,7 +421,7 @@ class _EPMoEDev(torch.autograd.Function):
         else:
             act = torch.empty(R, F2 // 2, device=x.device, dtype=torch.bfloat16)
             H = torch.empty(R, F2, device=x.device, dtype=torch.bfloat16)
-            C.gemm_grouped_m(x_recv, w13, offs_local, act, False, EPI_SWIGLU, 1.0, None, H, 256, R)
+            C.gemm_grouped_m(x_recv, w13, offs_local, act, False, EPI_SWIGLU, 1.0, None, H, 256, R, **gate)
             if ep.epilogue_push:
                 C.gemm_grouped_m_push(act, w2, offs_local, meta, sl.ys.ptrs, T * k, False, R)
             else:
@@ -444,11 +463,18 @@ class _EPMoEDev(torch.autograd.Function):
         # pushed to the owners' receive rows
         dwts = torch.empty(T, k, device=x.device, dtype=torch.float32)
         C.ep_source_bwd(dout, ys, slot, idx, wts, dwts, sh.dy.ptrs, sl.rows, El)
-        arena.barrier()                                       # all output gradients have landed
+        gate = {}
+        if ep.gate_tiles:
+            C.ep_signal(sh.ready.ptrs, ep.rank, sh.sig_ctr)  # this rank's output gradients are out
+            # each tile of the dact GEMM starts once the sources of its rows have signalled
+            gate = dict(ready_ptr=sh.ready.ptrs[ep.rank], ready_epoch=sh.sig_ctr, src_pref=sl.src_pref,
+                        nsrc=ep.world, me=ep.rank)
+        else:
+            arena.barrier()                                   # all output gradients have landed
         dy_recv = sh.dy.view(torch.bfloat16, R, D)
         C.ep_pad_rows(dy_recv, None, sl.offs_local, sl.kept_local)
         dH = torch.empty_like(H)
-        C.gemm_grouped_m(dy_recv, w2, sl.offs_local, dH, True, EPI_SWIGLU_BWD, 1.0, H, None, 256, R)
+        C.gemm_grouped_m(dy_recv, w2, sl.offs_local, dH, True, EPI_SWIGLU_BWD, 1.0, H, None, 256, R, **gate)
         dw2 = torch.empty_like(w2)
         C.gemm_grouped_k(dy_recv, act, sl.offs_local, dw2, EPI_BF16, 1.0, 256)
         q13t = ep.fp8_weights.get(("t", id(w13))) if ep.fp8_weights else None

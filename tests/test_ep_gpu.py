@@ -60,6 +60,7 @@ def _layer_worker(rank, world, port, q):
         # variant = (name, transport, layout, buffer factor); the device layout with buffer
         # factor 0.5 bounds every expert at 256 rows, i.e. the reference with capacity 256
         cases = [(0, 0, [("p2p", "p2p", "device", 2.0), ("p2p_ret", "p2p", "device", 2.0),
+                         ("p2p_gate", "p2p", "device", 2.0),
                          ("p2p_host", "p2p", "host", 2.0), ("nccl", "nccl", "host", 2.0)]),
                  (300, 300, [("p2p", "p2p", "device", 2.0), ("p2p_host", "p2p", "host", 2.0),
                              ("nccl", "nccl", "host", 2.0)]),
@@ -74,7 +75,7 @@ def _layer_worker(rank, world, port, q):
             ya.backward(dys)
             for name, transport, layout, bf in variants:
                 ep = EPContext(dist.group.WORLD, transport=transport, device=dev, arena_bytes=64 << 20, layout=layout,
-                               buffer_factor=bf, epilogue_push=name != "p2p_ret")
+                               buffer_factor=bf, epilogue_push=name != "p2p_ret", gate_tiles=name == "p2p_gate")
                 for it in range(2):                   # the second pass reuses the device layout's slabs
                     xb = xs[rank * T:(rank + 1) * T].clone().requires_grad_(True)
                     rb = wr.clone().requires_grad_(True)
