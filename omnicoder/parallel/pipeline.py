@@ -9,9 +9,12 @@ micro-batches and runs the one-forward-one-backward schedule:
   steady:   forward of micro-batch i + warm-up, backward of micro-batch i
   cool-down: remaining backwards
 which bounds the activations a stage keeps alive to P - s micro-batches.
-Sends are non-blocking (isend), receives blocking, and every rank issues its
-point-to-point operations in schedule order, so neighbouring stages never wait
-on each other's sends.  The last stage owns the loss (mean over micro-batches);
+Every exchange is one batched point-to-point call (`batch_isend_irecv`): a send
+alone, a receive alone, or the send of this micro-batch's output paired with the
+receive of the next gradient (and the send of a gradient paired with the receive of
+the next input) -- the pairing of 1F1B schedules.  NCCL serialises unbatched
+point-to-point operations of a communicator, and separately issued send / receive
+pairs of neighbouring stages then wait on each other; batched pairs do not.  The last stage owns the loss (mean over micro-batches);
 `step()` returns it on every stage (broadcast from the last).
 
 Optimiser: FusedAdamW over the stage's parameters with the global-norm clip
@@ -97,13 +100,20 @@ class PipelineTrainer:
         self._peer = lambda s: dist.get_global_rank(self.group, s) if self.group is not dist.group.WORLD else s
 
     # ---- point-to-point -----------------------------------------------------
-    def _send(self, t: torch.Tensor, to_stage: int, pending: list):
-        pending.append(dist.isend(t.contiguous(), self._peer(to_stage), group=self.group))
-
-    def _recv(self, shape, dtype, device, from_stage: int) -> torch.Tensor:
-        t = torch.empty(shape, dtype=dtype, device=device)
-        dist.recv(t, self._peer(from_stage), group=self.group)
-        return t
+    def _p2p(self, send: torch.Tensor | None = None, send_to: int = -1, recv_like: tuple | None = None,
+             recv_from: int = -1) -> torch.Tensor | None:
+        """One batched exchange: optionally send `send` to stage send_to and receive a tensor of
+        recv_like = (shape, dtype, device) from stage recv_from."""
+        ops, out = [], None
+        if send is not None:
+            ops.append(dist.P2POp(dist.isend, send.contiguous(), self._peer(send_to), group=self.group))
+        if recv_like is not None:
+            out = torch.empty(recv_like[0], dtype=recv_like[1], device=recv_like[2])
+            ops.append(dist.P2POp(dist.irecv, out, self._peer(recv_from), group=self.group))
+        if ops:
+            for r in dist.batch_isend_irecv(ops):
+                r.wait()
+        return out
 
     # ---- one optimiser step ------------------------------------------------
     def step(self, ids: torch.Tensor, labels: torch.Tensor):
@@ -117,19 +127,21 @@ class PipelineTrainer:
         dtype = next(self.stage.parameters()).dtype
         ids_m, lab_m = ids.chunk(M), labels.chunk(M)
         saved: dict[int, tuple] = {}
-        pending: list = []
         loss_sum = torch.zeros((), device=dev, dtype=torch.float32)
 
         rows = mb * S // self.tp_world
+        first, last = st.first, st.last
+        prev, nxt = self.stage_id - 1, self.stage_id + 1
+        act_like = ((rows, D), dtype, dev)
 
-        def fwd(i):
+        def forward(i, x):
             nonlocal loss_sum
-            if st.first:
+            if first:
                 x = ids_m[i]
             else:
-                x = self._recv((rows, D), dtype, dev, self.stage_id - 1).requires_grad_(True)
+                x = x.requires_grad_(True)
             out = st(x, S, mb)
-            if st.last:
+            if last:
                 lab = lab_m[i].reshape(-1)
                 if self.tp is not None:
                     from .tensor import scatter_seq
@@ -137,30 +149,41 @@ class PipelineTrainer:
                 loss = lm_head_cross_entropy(out, st.lm_head, lab) / M
                 loss_sum = loss_sum + loss.detach().float()
                 saved[i] = (x, loss)
-            else:
-                self._send(out.detach(), self.stage_id + 1, pending)
-                saved[i] = (x, out)
+                return None
+            saved[i] = (x, out)
+            return out.detach()
 
-        def bwd(i):
+        def backward(i, g):
             x, out = saved.pop(i)
-            if st.last:
+            if last:
                 out.backward()
             else:
-                g = self._recv(out.shape, out.dtype, dev, self.stage_id + 1)
                 out.backward(g)
-            if not st.first:
-                self._send(x.grad, self.stage_id - 1, pending)
+            return None if first else x.grad
 
+        recv_fwd = lambda: None if first else self._p2p(recv_like=act_like, recv_from=prev)
         warm = min(P - self.stage_id - 1, M)
-        for i in range(warm):
-            fwd(i)
-        for i in range(M - warm):
-            fwd(i + warm)
-            bwd(i)
-        for i in range(M - warm, M):
-            bwd(i)
-        for r in pending:
-            r.wait()
+        for i in range(warm):                                   # warm-up forwards
+            out = forward(i, recv_fwd())
+            self._p2p(send=out, send_to=nxt)
+        rem = M - warm
+        x = recv_fwd() if rem > 0 else None
+        for j in range(rem):                                    # steady state: one forward, one backward
+            out = forward(warm + j, x)
+            g = None if last else self._p2p(send=out, send_to=nxt, recv_like=act_like, recv_from=nxt)
+            dx = backward(j, g)
+            if j == rem - 1:
+                if not first:
+                    self._p2p(send=dx, send_to=prev)
+            elif first:
+                x = None
+            else:
+                x = self._p2p(send=dx, send_to=prev, recv_like=act_like, recv_from=prev)
+        for j in range(rem, M):                                 # cool-down backwards
+            g = None if last else self._p2p(recv_like=act_like, recv_from=nxt)
+            dx = backward(j, g)
+            if not first:
+                self._p2p(send=dx, send_to=prev)
         # global-norm clip over all stages, then the optimiser step
         scale = 1.0
         if self.tp is not None:

@@ -1,8 +1,9 @@
-"""1F1B pipeline over 2 CPU stages (gloo point-to-point): the loss and the
-updated parameters of each stage must equal one process on the same batch."""
+"""1F1B pipeline over 2 and 4 CPU stages, and 2 stages x tensor parallel 2 (gloo point-to-point):
+the loss and the updated parameters of each stage must equal one process on the same batch."""
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -45,17 +46,19 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_pipeline_1f1b_matches_single_process():
+@pytest.mark.parametrize("stages", [2, 4])
+def test_pipeline_1f1b_matches_single_process(stages):
+    """2 and 4 stages (4: warm-up, steady state with paired exchanges and cool-down all non-trivial)."""
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, stages, port, q)) for r in range(stages)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in range(2)]
+    res = [q.get(timeout=300) for _ in range(stages)]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
