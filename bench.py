@@ -73,9 +73,9 @@ def parse_args():
                     help="expert-parallel receive slabs hold this many times the balanced per-expert load "
                          "(pairs beyond it are dropped and counted in ep_stats)")
     ap.add_argument("--decode-gen", type=int, default=512)
-    ap.add_argument("--decode-layout", default="replica", choices=["replica", "ep"],
-                    help="several GPUs: a full model replica per GPU, or experts sharded over the GPUs (expert "
-                         "parallel decode through the device-side exchange)")
+    ap.add_argument("--decode-layout", default="ep", choices=["replica", "ep"],
+                    help="several GPUs: experts sharded over the GPUs (expert-parallel decode through the "
+                         "device-side exchange, the long-context serving layout), or a full model replica per GPU")
     return ap.parse_args()
 
 
