@@ -1,5 +1,5 @@
-"""Tensor parallel (+ sequence parallel) and 1F1B pipeline training on 2 GPUs
-(one process per GPU): the group-mean loss of three steps must track one GPU
+"""Tensor parallel (+ sequence parallel) and 1F1B pipeline training on 2 GPUs, and a
+4-stage pipeline on 4 (one process per GPU): the group-mean loss of three steps must track one GPU
 training the same model on the same batch (bf16 tolerance).  Tensor parallel
 runs with NCCL collectives and with the fused peer-memory collectives
 (all-gather inside the consuming GEMM's loads, reduce-scatter in the producing
@@ -52,7 +52,7 @@ def _worker(rank, world, port, mode, q):
         else:
             from omnicoder.parallel.pipeline import PipelineTrainer
             m = build_model(_cfg(), device=dev, seed=0)
-            pt = PipelineTrainer(m, tc, n_micro=2)
+            pt = PipelineTrainer(m, tc, n_micro=2 if world == 2 else 4)
             got = [float(pt.step(ids, lab)) for _ in range(3)]
         torch.cuda.synchronize()
         C = _ext.load()
@@ -90,11 +90,11 @@ def _run(mode, world=2):
     return res
 
 
-@pytest.mark.parametrize("mode", ["tp", "tp_p2p", "pp"])
-def test_tp_and_pp_track_single_gpu(mode):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    for rank, out in _run(mode).items():
+@pytest.mark.parametrize("mode,world", [("tp", 2), ("tp_p2p", 2), ("pp", 2), ("pp", 4)])
+def test_tp_and_pp_track_single_gpu(mode, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    for rank, out in _run(mode, world).items():
         assert isinstance(out, dict), out
         assert out["status"] == 0
         for a, b in zip(out["ref"], out["got"]):
