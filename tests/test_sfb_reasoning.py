@@ -74,3 +74,53 @@ def test_lm_tree_and_graph_search():
     assert 1 <= len(best) <= 3 and isinstance(st["text"], str)
     out = LMAdaptiveGraph(m, k=2, thought_len=2, rounds=2, beam=1).step(torch.tensor([[5, 6, 7]]))
     assert out.shape[1] == 3 + 4 and torch.equal(out[0, :3], torch.tensor([5, 6, 7]))
+
+
+def test_omega_scm_goals_margins_planner():
+    from omnicoder.reasoning import omega as om
+    # SCM: X -> Y = 2 X (+ noise), Y -> Z = Y + 1
+    scm = om.SCM()
+    scm.add_variable("X", 1.0)
+    scm.add_mechanism("Y", lambda v: 2 * v["X"], parents=["X"])
+    scm.add_mechanism("Z", lambda v: v["Y"] + 1, parents=["Y"])
+    assert scm.order() == ["X", "Y", "Z"]
+    assert scm.forward()["Z"] == 3.0
+    assert scm.do({"Y": 10})["Z"] == 11 and scm.do({"X": 2.0})["Z"] == 5.0
+    # observed Y = 2.5 at X = 1 -> noise 0.5; had X been 2, Y = 4.5, Z = 5.5
+    cf = scm.counterfactual({"X": 1.0, "Y": 2.5, "Z": 3.5}, {"X": 2.0})
+    assert abs(cf["Y"] - 4.5) < 1e-9 and abs(cf["Z"] - 5.5) < 1e-9
+    assert om.abductive_score(scm, {"Z": 3.0, "Y": 2.0}) == 1.0
+    assert om.value_of_information({"a": 0.2, "b": 0.9}, 1) == [("b", 0.9)]
+    q = om.build_minimal_scm_for_query("why does the code fail the test")
+    assert q.variables["G"].value == 0.7 and q.variables["P"].value == 0.7 and q.forward()["A"] > 0.6
+    cyc = om.SCM()
+    cyc.add_variable("a", parents=["b"])
+    cyc.add_variable("b", parents=["a"])
+    with pytest.raises(ValueError):
+        cyc.order()
+    # goals
+    b = om.infer_goals("please fix this crash, error in the traceback, then verify with a test")
+    assert b.top() == "debug" and "must-verify" in b.constraints
+    assert abs(sum(h.posterior for h in om.infer_goals("x", k=10).hypotheses) - 1.0) < 1e-6
+    mem = om.infer_goals("hello", memory={"summarize": 50})
+    assert mem.top() == "summarize"
+    # margins and certificate
+    assert om.text_margin("the cat sat", "a cat sat down") == 2 / 3
+    assert om.code_margin(passed=3, total=4) == 0.75
+    c = om.pack_certificate("42", b, {"text": 1.0, "image_z": 0.0})
+    assert abs(c.margin - 0.75) < 1e-9 and '"answer": "42"' in c.to_json()
+    # planner: reach 3 from 0 with +1 / +2 steps; value = closeness
+    act, v = om.plan_search(0, lambda s: [1, 2] if s < 3 else [], lambda s, a: s + a,
+                            lambda s: 1.0 if s == 3 else 0.0, budget=64, max_depth=3)
+    assert act in (1, 2) and v > 0.4
+    tb = om.TemplateBank()
+    tb.add([1, 0], "a")
+    tb.add([0, 1], "b")
+    assert tb.query([0.9, 0.1])[0][1] == "a"
+    st = om.SymbolicState()
+    st.apply("fact: x > 0\ngoal: prove y\nfact: z\nretract: z\ndone: nothing")
+    assert st.render_context() == "FACT x > 0\nGOAL prove y"
+    om.register_kv_hint((1, 2, 3), "kv123")
+    assert om.get_kv_hint((1, 2, 3, 4)) == ((1, 2, 3), "kv123") and om.get_kv_hint((9,)) is None
+    assert om.select_branch([(-1.0, 0.2, 7), (-0.5, 0.1, 8)]) == 8
+    assert "shortest path" in om.algorithm_hints("find the shortest path in a graph")
