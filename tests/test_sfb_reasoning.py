@@ -124,3 +124,22 @@ def test_omega_scm_goals_margins_planner():
     assert om.get_kv_hint((1, 2, 3, 4)) == ((1, 2, 3), "kv123") and om.get_kv_hint((9,)) is None
     assert om.select_branch([(-1.0, 0.2, 7), (-0.5, 0.1, 8)]) == 8
     assert "shortest path" in om.algorithm_hints("find the shortest path in a graph")
+
+
+def test_code_sandboxes():
+    from omnicoder.sfb.sandbox import CppSandbox, HTTPSandbox, PythonSandbox
+    py = PythonSandbox()
+    ok = py.run("def add(a, b):\n    return a + b", "assert add(2, 3) == 5\nprint('sum', add(1, 1))")
+    assert ok.ok and "sum 2" in ok.stdout
+    bad = py.run("def add(a, b):\n    return a - b", "assert add(2, 3) == 5")
+    assert not bad.ok and "AssertionError" in bad.stderr
+    early = py.run("import sys", "sys.exit(0)")
+    assert not early.ok                                   # exited before the end marker
+    slow = py.run("import time", "time.sleep(30)", timeout=1)
+    assert not slow.ok and slow.stderr == "timeout"
+    import shutil
+    if shutil.which("g++"):
+        c = CppSandbox().run("#include <cassert>\nint sq(int x){return x*x;}", "assert(sq(3)==9);")
+        assert c.ok
+        assert not CppSandbox().run("int f(){return 1;}", "return f();").ok
+    assert not HTTPSandbox("http://127.0.0.1:9/none").run("x=1", timeout=1).ok
