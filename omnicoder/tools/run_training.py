@@ -7,7 +7,8 @@ expert-parallel launch).  Stages here: `pretrain` (spec LM), `distill`
 (knowledge distillation of the draft-sized student from the pretrained model or
 a local Hugging Face teacher), `draft` (small draft model for speculative
 decoding), `draft_kd` (draft pipeline: KD with LoRA, export, acceptance),
-`verifier` (verifier-head distillation), `vl` / `vqa` (vision-language pretraining and VQA
+`code_expert` (code distillation with router KD and balanced routing), `verifier` (verifier-head
+distillation), `vl` / `vqa` (vision-language pretraining and VQA
 over the fusion composer), `rl`
 (GRPO on programmatic rewards), `eval` (evaluation sweep), `export` (ONNX decode
 step), `package` (on-device package).  `--smoke_one_step` runs one step of every
@@ -42,7 +43,7 @@ def run_with_timeout(cmd: list[str], timeout_s: float, env=None) -> int:
 
 def plan(budget_minutes: float, steps_per_minute: float, stages: list[str]) -> dict:
     """Split the budget by relative shares of the requested stages."""
-    share = {"pretrain": 0.8, "distill": 0.1, "draft": 0.15, "draft_kd": 0.1, "verifier": 0.05, "vl": 0.1, "vqa": 0.05, "rl": 0.1,
+    share = {"pretrain": 0.8, "distill": 0.1, "draft": 0.15, "draft_kd": 0.1, "code_expert": 0.1, "verifier": 0.05, "vl": 0.1, "vqa": 0.05, "rl": 0.1,
              "eval": 0.03, "export": 0.05, "package": 0.03}
     tot = sum(share[s] for s in stages) or 1.0
     return {s: {"minutes": budget_minutes * share[s] / tot,
@@ -107,6 +108,12 @@ def main(argv=None):
                    "--bench_out", os.path.join(a.out_dir, "draft_acceptance.json")] + dev
             cmd += (["--teacher_ckpt", ckpt, "--teacher_preset", a.preset] if os.path.exists(ckpt) else
                     ["--teacher_preset", a.preset])
+        elif s == "code_expert":
+            cmd = [sys.executable, "-m", "omnicoder.training.code_expert", "--student_preset", a.preset,
+                   "--steps", str(p[s]["steps"]), "--seq_len", str(a.seq_len), "--batch_size", str(a.batch_size),
+                   "--data", a.data, "--out", os.path.join(a.out_dir, "code_expert.pt")] + dev
+            if os.path.exists(ckpt):
+                cmd += ["--teacher_ckpt", ckpt]
         elif s == "verifier":
             cmd = [sys.executable, "-m", "omnicoder.training.verifier_distill", "--student_preset", a.preset,
                    "--steps", str(p[s]["steps"]), "--seq_len", str(a.seq_len), "--batch_size", str(a.batch_size),

@@ -147,3 +147,30 @@ def test_verifier_distillation(tmp_path):
     assert vd2.step(ids, t2) > 0 and vd2.align.weight.grad is not None
     assert main(["--steps", "1", "--seq_len", "16", "--batch_size", "1", "--device", "cpu",
                  "--out", str(tmp_path / "v.pt")]) == 0
+
+
+def test_code_expert_router_kd_and_balance(tmp_path):
+    from omnicoder.config import ModelConfig, MoEConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.code_expert import RouterTap, code_expert_loss, main, sinkhorn
+    p = sinkhorn(torch.randn(64, 8), iters=30)
+    assert torch.allclose(p.sum(1), torch.ones(64), atol=1e-4) and torch.allclose(p.sum(0), torch.full((8,), 8.0),
+                                                                                     atol=1e-2)
+    cfg = ModelConfig(name="ce", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=64))
+    s = build_model(cfg, "cpu", dtype=torch.float32, seed=0)
+    t = build_model(cfg, "cpu", dtype=torch.float32, seed=1).eval()
+    st, tt = RouterTap(s), RouterTap(t)
+    ids, lab = torch.randint(0, 300, (2, 16)), torch.randint(0, 300, (2, 16))
+    loss, parts = code_expert_loss(s, t, st, tt, ids, lab)
+    assert set(parts) == {"kd", "router_kd", "balance"} and parts["router_kd"] > 0
+    loss.backward()
+    routers = [m.router for m in st.layers]
+    assert all(r.grad is not None and r.grad.abs().sum() > 0 for r in routers)
+    # the router KD term vanishes when the student's routers equal the teacher's
+    s2 = build_model(cfg, "cpu", dtype=torch.float32, seed=1)
+    st2 = RouterTap(s2)
+    _, parts2 = code_expert_loss(s2, t, st2, tt, ids, lab, balance=0.0)
+    assert parts2["router_kd"] < 1e-6
+    assert main(["--steps", "1", "--seq_len", "16", "--batch_size", "1", "--device", "cpu",
+                 "--student_preset", "tiny_moe", "--out", str(tmp_path / "c.pt")]) == 0
