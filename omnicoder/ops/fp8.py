@@ -163,13 +163,17 @@ class _WeightCache:
         self.generation += 1
 
     def get(self, w: torch.Tensor, transposed: bool):
+        import weakref
         key = (id(w), transposed)
         hit = self._d.get(key)
-        if hit is not None and hit[0] == (w._version, self.generation) and hit[1] is w:
+        if hit is not None and hit[0] == (w._version, self.generation) and hit[1]() is w:
             return hit[2]
         src = w.detach().t().contiguous() if transposed else w.detach()
         q = quantize_weight(src.to(torch.bfloat16) if src.is_cuda else src)
-        self._d[key] = ((w._version, self.generation), w, q)
+        # a weak reference: the cache neither keeps a discarded model's weights alive nor
+        # serves a new tensor that reuses a freed one's id; dead entries are dropped here
+        self._d = {k: v for k, v in self._d.items() if v[1]() is not None}
+        self._d[key] = ((w._version, self.generation), weakref.ref(w), q)
         return q
 
 

@@ -268,3 +268,17 @@ def test_fp8_weight_gradient_gemm():
     ref = deq(dq, ds, N) @ deq(xq, xs, K).t()
     assert _rowrel(dw, ref) < 2e-2
     assert _rel(dw, dy.float().t() @ x.float()) < 0.08
+
+
+def test_weight_cache_does_not_keep_weights_alive():
+    import gc
+    import weakref
+    w = torch.nn.Parameter(torch.randn(128, 128))
+    fp8.WEIGHTS.get(w, False)
+    r = weakref.ref(w)
+    del w
+    gc.collect()
+    assert r() is None
+    v = torch.nn.Parameter(torch.randn(128, 128))
+    fp8.WEIGHTS.get(v, True)                  # drops the dead entry
+    assert all(e[1]() is not None for e in fp8.WEIGHTS._d.values())
