@@ -55,7 +55,7 @@ def _run(args, cwd, timeout, mem_bytes) -> SandboxResult:
 
 
 class PythonSandbox:
-    def __init__(self, python: str | None = None, mem_bytes: int = 1 << 30):
+    def __init__(self, python: str | None = None, mem_bytes: int = 4 << 30):
         self.python, self.mem = python or sys.executable, mem_bytes
 
     def run(self, code: str, tests: str = "", timeout: int = 5) -> SandboxResult:
@@ -72,7 +72,7 @@ class PythonSandbox:
 
 
 class CppSandbox:
-    def __init__(self, cxx: str = "g++", mem_bytes: int = 1 << 30):
+    def __init__(self, cxx: str = "g++", mem_bytes: int = 4 << 30):
         self.cxx, self.mem = cxx, mem_bytes
 
     def run(self, code: str, tests: str = "", timeout: int = 10) -> SandboxResult:
