@@ -569,13 +569,57 @@ def main(argv=None):
     ap.add_argument("--verify_threshold", type=float, default=0.0,
                     help="speculative acceptance by the target's verifier head (0: rejection sampling)")
     ap.add_argument("--compress_kv_slots", type=int, default=0, help="compressed memory rows of the cache")
+    ap.add_argument("--mem_slots", type=int, default=None, help="alias of --compress_kv_slots")
+    ap.add_argument("--adaptive_layer_power", type=float, default=1.0)
+    # model / context
+    ap.add_argument("--mobile_preset", default=None, help="alias of --preset")
+    ap.add_argument("--rope_scale", type=float, default=None, help="divide RoPE positions by this factor")
+    ap.add_argument("--rope_base", type=float, default=None, help="RoPE base (theta)")
+    ap.add_argument("--target_ctx", type=int, default=0,
+                    help="extend the context to this length (RoPE position interpolation)")
+    ap.add_argument("--disable_speculative", action="store_true")
+    # prompt
+    ap.add_argument("--system_prompt", default="")
+    ap.add_argument("--prompt_template", default="{system}{prompt}",
+                    help="format string with {system} and {prompt}")
+    # retrieval from local files
+    ap.add_argument("--retrieve_path", default=None, help="folder (or file) of .txt / .md / .py documents")
+    ap.add_argument("--retrieve_k", type=int, default=3)
+    ap.add_argument("--retrieve_chunk", type=int, default=600, help="characters per chunk")
+    ap.add_argument("--retrieve_stride", type=int, default=400)
+    ap.add_argument("--retrieve_max_chars", type=int, default=2000, help="retrieved characters put in the prompt")
+    ap.add_argument("--retrieve_prepend", action="store_true", help="put the retrieved passages before the prompt")
+    # post-processing
+    ap.add_argument("--tool_use", action="store_true", help="run <tool>name(args)</tool> calls in the output")
+    ap.add_argument("--emit_cert", action="store_true", help="print a proof-carrying answer record (JSON)")
+    ap.add_argument("--proof_margin_thresh", type=float, default=0.0,
+                    help="with --emit_cert: abstain when the verification margin is below this")
     a = ap.parse_args(argv)
-    cfg = get_preset(a.preset)
+    cfg = get_preset(a.mobile_preset or a.preset)
+    if a.rope_scale is not None:
+        cfg.attn.rope_scale = a.rope_scale
+    if a.rope_base is not None:
+        cfg.attn.rope_theta = a.rope_base
+    if a.target_ctx:
+        from ..config import get_rope_scale_for_target_ctx
+        cfg.attn.rope_scale *= get_rope_scale_for_target_ctx(cfg.max_seq_len, a.target_ctx)
+        cfg.max_seq_len = max(cfg.max_seq_len, a.target_ctx)
+    if a.mem_slots is not None:
+        a.compress_kv_slots = a.mem_slots
+    if a.disable_speculative:
+        a.draft_preset, a.speculative_draft_len = None, 0
     model = build_model(cfg, device=a.device)
     if a.ckpt:
         maybe_load_checkpoint(model, a.ckpt)
     tok = get_tokenizer(cfg.vocab_size)
-    ids = torch.tensor([tok.encode(a.prompt)], device=a.device)
+    passages = []
+    if a.retrieve_path:
+        passages = retrieve_passages(a.retrieve_path, a.prompt, a.retrieve_k, a.retrieve_chunk, a.retrieve_stride)
+    context = ""
+    if a.retrieve_prepend and passages:
+        context = "\n".join(passages)[:a.retrieve_max_chars] + "\n"
+    prompt_text = context + a.prompt_template.format(system=a.system_prompt, prompt=a.prompt)
+    ids = torch.tensor([tok.encode(prompt_text)], device=a.device)
     draft = None
     if a.draft_preset:
         draft = build_model(get_preset(a.draft_preset), device=a.device)
@@ -589,6 +633,8 @@ def main(argv=None):
     if a.retrieve_texts:
         with open(a.retrieve_texts) as f:
             texts = [ln.strip() for ln in f if ln.strip()]
+    if passages:
+        texts = (texts or []) + passages
     out, st = generate(model, ids, a.max_new_tokens, a.temperature, a.top_k, a.top_p, draft_model=draft,
                        repetition_penalty=a.repetition_penalty, presence_penalty=a.presence_penalty,
                        frequency_penalty=a.frequency_penalty,
@@ -602,13 +648,43 @@ def main(argv=None):
                        adaptive_conf_floor=a.adaptive_conf_floor, adaptive_layer_ramp=a.adaptive_layer_ramp,
                        early_exit=a.early_exit, early_exit_entropy=a.early_exit_entropy,
                        early_exit_mode=a.early_exit_mode, verify_threshold=a.verify_threshold,
-                       compress_kv_slots=a.compress_kv_slots)
+                       compress_kv_slots=a.compress_kv_slots, adaptive_layer_power=a.adaptive_layer_power)
     text = tok.decode(out[0, ids.shape[1]:].tolist())
+    if a.tool_use:
+        from .tools import ToolRegistry
+        text = ToolRegistry().run_calls(text)
+    result = {"text": text, "stats": st.as_dict()}
+    if a.emit_cert:
+        from ..reasoning.omega import infer_goals, pack_certificate, text_margin
+        cert = pack_certificate(text, infer_goals(a.prompt), {"text": text_margin(text, " ".join(passages) or None)})
+        result["certificate"] = json.loads(cert.to_json())
+        if cert.margin < a.proof_margin_thresh:
+            result["abstained"] = True
+            text = ""
     if a.json:
-        print(json.dumps({"text": text, "stats": st.as_dict()}))
+        print(json.dumps(result))
     else:
         print(text)
-        print(json.dumps(st.as_dict()), file=sys.stderr)
+        print(json.dumps({k: v for k, v in result.items() if k != "text"}), file=sys.stderr)
+
+
+def retrieve_passages(path: str, query: str, k: int = 3, chunk: int = 600, stride: int = 400) -> list[str]:
+    """Top-k chunks of the documents under `path` for `query` (character windows of `chunk` with
+    step `stride`, ranked by the TF-IDF product-quantisation retriever)."""
+    import os
+
+    from ..retrieval.pq import PQRetriever
+    files = [path] if os.path.isfile(path) else [
+        os.path.join(r, f) for r, _, fs in os.walk(path) for f in sorted(fs) if f.endswith((".txt", ".md", ".py"))]
+    docs = []
+    for fp in sorted(files):
+        with open(fp, encoding="utf-8", errors="ignore") as f:
+            t = f.read()
+        docs += [t[i:i + chunk] for i in range(0, max(1, len(t) - chunk + stride), max(1, stride)) if t[i:i + chunk].strip()]
+    if not docs:
+        return []
+    r = PQRetriever(n_subspaces=4, n_centroids=min(16, len(docs))).fit(docs)
+    return [d for _, _, d in r.search(query, k)]
 
 
 if __name__ == "__main__":

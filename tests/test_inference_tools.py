@@ -411,3 +411,22 @@ def test_export_variants_bias_heads_multimodal_longctx(tmp_path):
     paths = write_sidecars(m, str(tmp_path / "d.onnx"), 128, kv_page_len=32, kvq="nf4")
     meta = _json.load(open(paths[0]))
     assert meta["pages_per_layer"] == 4 and _json.load(open(paths[1]))["bits"] == 4
+
+
+def test_generate_cli_retrieval_template_tools_certificate(tmp_path, capsys):
+    """File retrieval picks the passage about the query; the CLI formats the prompt, runs tool calls
+    in the output and emits a certificate; --target_ctx interpolates RoPE."""
+    import json as _json
+
+    from omnicoder.inference.generate import main, retrieve_passages
+    from omnicoder.inference.tools import ToolRegistry
+    (tmp_path / "a.txt").write_text("The capital of France is Paris. The Eiffel tower stands in Paris.\n" * 3)
+    (tmp_path / "b.md").write_text("Python lists support append and pop; dictionaries map keys to values.\n" * 3)
+    got = retrieve_passages(str(tmp_path), "where is the eiffel tower", k=1, chunk=120, stride=80)
+    assert len(got) == 1 and "Eiffel" in got[0]
+    assert ToolRegistry().run_calls("x <tool>calc(2*21)</tool>").endswith("<result>42</result>")
+    main(["--preset", "tiny_moe", "--device", "cpu", "--max_new_tokens", "3", "--retrieve_path", str(tmp_path),
+          "--retrieve_k", "1", "--retrieve_prepend", "--system_prompt", "S: ", "--tool_use", "--emit_cert",
+          "--json", "--target_ctx", "16384", "--prompt", "where is the eiffel tower", "--no_cuda_graph"])
+    out = _json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert "certificate" in out and out["stats"]["prompt_tokens"] > len("where is the eiffel tower")
