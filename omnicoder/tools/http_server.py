@@ -48,6 +48,25 @@ def _request_model():
     return _REQ
 
 
+_UI_HTML = """<!doctype html><html><head><meta charset="utf-8"><title>omnicoder</title></head>
+<body style="font-family:sans-serif;max-width:48em;margin:2em auto">
+<h3>omnicoder</h3>
+<textarea id="p" rows="6" style="width:100%">def fibonacci(n):</textarea><br>
+max new tokens <input id="n" type="number" value="64"> temperature <input id="t" type="number" step="0.1" value="0.8">
+<button onclick="go()">generate</button>
+<pre id="o" style="white-space:pre-wrap;background:#f4f4f4;padding:1em"></pre>
+<script>
+async function go() {
+  const body = {prompt: document.getElementById('p').value, max_new_tokens: +document.getElementById('n').value,
+                temperature: +document.getElementById('t').value};
+  const r = await fetch('/generate/text', {method: 'POST', headers: {'Content-Type': 'application/json'},
+                                           body: JSON.stringify(body)});
+  const j = await r.json();
+  document.getElementById('o').textContent = j.text !== undefined ? j.text : JSON.stringify(j);
+}
+</script></body></html>"""
+
+
 def create_app(model, tokenizer=None, max_batch: int = 16, batch_window_s: float = 0.005, image_vq=None,
                video_vq=None, vocab=None):
     """`image_vq` / `video_vq` (VQ-VAE decoders) and `vocab` (the unified vocabulary layout) enable
@@ -106,6 +125,32 @@ def create_app(model, tokenizer=None, max_batch: int = 16, batch_window_s: float
     async def health():
         return {"status": "ok", "model": model.cfg.name, "device": str(dev), "served": state["served"],
                 "batches": state["batches"]}
+
+    @app.get("/")
+    async def index():
+        return {"service": "omnicoder", "model": model.cfg.name,
+                "endpoints": ["GET /health", "GET /ui", "GET /metrics", "GET /debug/config", "POST /generate/text",
+                              "POST /generate/unified", "POST /generate/image", "POST /generate/video"]}
+
+    from fastapi.responses import HTMLResponse, PlainTextResponse
+
+    @app.get("/ui", response_class=HTMLResponse)
+    async def ui():
+        return _UI_HTML
+
+    @app.get("/metrics", response_class=PlainTextResponse)
+    async def metrics():
+        lines = ["# TYPE omnicoder_requests_served_total counter",
+                 f"omnicoder_requests_served_total {state['served']}",
+                 "# TYPE omnicoder_batches_total counter", f"omnicoder_batches_total {state['batches']}",
+                 "# TYPE omnicoder_queue_depth gauge",
+                 f"omnicoder_queue_depth {state['queue'].qsize() if state['queue'] is not None else 0}"]
+        return "\n".join(lines) + "\n"
+
+    @app.get("/debug/config")
+    async def debug_config():
+        return {"config": model.cfg.to_dict(), "max_batch": max_batch, "batch_window_s": batch_window_s,
+                "image": image_vq is not None, "video": video_vq is not None}
 
     async def _text(r):
         ids = torch.tensor([tok.encode(r.prompt) or [0]])

@@ -51,6 +51,11 @@ def test_http_server_batches_requests():
         h = cli.get("/health").json()
         assert h["served"] == 4 and h["batches"] < 4                  # at least two requests shared a batch
         assert cli.post("/generate/image", json={"prompt": "x"}).status_code == 501   # no decoder given
+        assert "/generate/text" in " ".join(cli.get("/").json()["endpoints"])
+        assert "<textarea" in cli.get("/ui").text
+        met = cli.get("/metrics").text
+        assert "omnicoder_requests_served_total 4" in met and "omnicoder_queue_depth" in met
+        assert cli.get("/debug/config").json()["config"]["d_model"] == cfg.d_model
 
 
 def test_gguf_roundtrip(tmp_path):
