@@ -138,3 +138,32 @@ def test_flow_recon_trainer_learns_latents(tmp_path):
         err = (z - z0).norm() / z0.norm()
         assert err < (0.2 if not flow else 0.5), (flow, float(err))
     assert main(["--steps", "2", "--device", "cpu", "--out", str(tmp_path / "h.pt")]) == 0
+
+
+def test_pre_align_infonce_aligns_text_and_media(tmp_path):
+    from omnicoder.multimodal.encoders import MelFrontend
+    from omnicoder.training.pre_align import PreAlignTrainer, TextEmbedder, main
+
+    class Flat(torch.nn.Module):               # tiny image encoder: mean colour -> features
+        dim = 32
+
+        def __init__(self):
+            super().__init__()
+            self.lin = torch.nn.Linear(3, 32)
+
+        def forward(self, x):
+            return self.lin(x.mean((2, 3)))
+
+    torch.manual_seed(0)
+    tr = PreAlignTrainer(TextEmbedder(64, 32), {"image": Flat(), "audio": MelFrontend(out_dim=32)}, shared=16,
+                         lr=1e-2)
+    colors = torch.rand(8, 3)
+    ids = torch.arange(1, 9)[:, None].repeat(1, 3)
+    imgs = colors[:, :, None, None].expand(-1, -1, 8, 8)
+    t = torch.arange(2000) / 16000.0
+    wav = torch.stack([torch.sin(2 * 3.14159 * (200 + 100 * i) * t) for i in range(8)])
+    first = tr.step(ids, image=imgs, audio=wav)
+    for _ in range(150):
+        last = tr.step(ids, image=imgs, audio=wav)
+    assert last["image"] < 0.5 * first["image"] and last["audio"] < first["audio"]
+    assert main(["--steps", "1", "--batch", "4", "--device", "cpu", "--out", str(tmp_path / "p.pt")]) == 0
