@@ -234,7 +234,8 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
              adaptive_moe: bool = False, adaptive_top_k_min: int = 1, adaptive_top_k_max: int = 4,
              adaptive_conf_floor: float = 0.3, adaptive_layer_ramp: bool = False, adaptive_layer_power: float = 1.0,
              early_exit: bool = False, early_exit_entropy: float = 0.0, early_exit_mode: str = "entropy",
-             verify_threshold: float = 0.0, compress_kv_slots: int = 0, prefix_embeds: torch.Tensor | None = None):
+             verify_threshold: float = 0.0, compress_kv_slots: int = 0, prefix_embeds: torch.Tensor | None = None,
+             scmoe_alpha: float = 0.0, scmoe_topk: int = 1, scmoe_frac: float = 1.0):
     """Generate `max_new_tokens` tokens after `input_ids` [B, S] (or [S]).  Returns
     [B, S + max_new_tokens] (and GenStats with return_stats).  On CUDA the
     decode step is captured once as a CUDA graph (`cuda_graph=False` runs it
@@ -252,7 +253,13 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
     that has a verifier head accepts draft tokens whose verifier probability reaches the
     threshold (the reference's policy) instead of by rejection sampling.
     `compress_kv_slots` sets the number of compressed memory rows; `prefix_embeds` [B, P, D]
-    primes the cache with feature vectors before the prompt."""
+    primes the cache with feature vectors before the prompt.
+
+    Self-contrast MoE decoding (`scmoe_alpha` > 0; reference generate.py `--scmoe_alpha / _topk /
+    _frac`): a second, weak pass of the same model routes each token to `scmoe_topk` experts in the
+    last `scmoe_frac` of the MoE layers (with its own cache), and the step samples from
+    (1 + alpha) log p_strong - alpha log p_weak, which favours what the full expert mixture adds
+    over the weakened one.  Eager decode (two passes per step)."""
     model.eval()
     squeeze = input_ids.dim() == 1
     ids = input_ids[None] if squeeze else input_ids
@@ -291,9 +298,11 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
             text = "\n\n".join(retrieved_texts[:5]) + "\n\n" + text
         addons.sfb_bias = sfb_token_bias(text, encode_fn, cfg.vocab_size, dev)
         addons.sfb_alpha = float(sfb_alpha)
+    if scmoe_alpha > 0 and adaptive_moe:
+        raise ValueError("scmoe and adaptive_moe both set the routed-expert count: use one")
     if draft_model is not None and speculative_draft_len > 0:
         if repetition_penalty != 1.0 or presence_penalty or frequency_penalty or logit_bias or addons.active \
-                or adaptive_moe:
+                or adaptive_moe or scmoe_alpha > 0:
             raise ValueError("speculative decoding samples from the unmodified target distribution: "
                              "penalties, logit_bias and the logit add-ons are not applied there")
         out = _speculative(model, draft_model, ids, max_new_tokens, speculative_draft_len, temperature, top_k, top_p,
@@ -309,6 +318,14 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
             logits, hidden = _prefill(model, ids, cache, return_hidden=True)
         else:
             logits = _prefill(model, ids, cache)
+        weak = None
+        if scmoe_alpha > 0:
+            weak = _WeakRouting(model, scmoe_topk, scmoe_frac, KVCache(cfg, B, L, dev, dtype=model.embed.dtype,
+                                                                       kv_dtype=kv_dtype), scmoe_alpha)
+            if prefix_embeds is not None:
+                with weak:
+                    prime_kv_with_features(model, prefix_embeds.to(dev), weak.cache)
+            logits = weak.contrast(logits, lambda: _prefill(model, ids, weak.cache))
         if addons.active:
             logits = addons.apply(model, logits, hidden)
         if adaptive_moe:
@@ -326,7 +343,7 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         toks = [tok]
         done = torch.zeros(B, dtype=torch.bool, device=dev)
         step = None
-        if cuda_graph and dev.type == "cuda" and max_new_tokens > 2 and not adaptive_moe:
+        if cuda_graph and dev.type == "cuda" and max_new_tokens > 2 and not adaptive_moe and weak is None:
             from .graphs import GraphedStep
             step = GraphedStep(model, cache, return_hidden=addons.needs_hidden)
         t1 = time.perf_counter()
@@ -340,6 +357,9 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
                 logits, hidden = logits[:, -1], hidden[:, -1]
             else:
                 logits = model.forward_cached(tok[:, None], cache)[:, -1]
+            if weak is not None:
+                t_in = tok[:, None]
+                logits = weak.contrast(logits, lambda: model.forward_cached(t_in, weak.cache)[:, -1])
             if addons.active:
                 logits = addons.apply(model, logits, hidden)
             if adaptive_moe:
@@ -364,6 +384,35 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         out = torch.cat([ids, torch.stack(toks, dim=1)], dim=1)
     out = out[0] if squeeze else out
     return (out, stats) if return_stats else out
+
+
+class _WeakRouting:
+    """The weak pass of self-contrast MoE decoding: `topk` routed experts in the last `frac` of the
+    MoE layers while active (context manager), its own KV cache."""
+
+    def __init__(self, model, topk: int, frac: float, cache, alpha: float):
+        from ..models.lm import MoEFFN
+        moes = [b.ffn for b in model.blocks if isinstance(b.ffn, MoEFFN)]
+        n = max(1, int(round(len(moes) * max(0.0, min(1.0, frac))))) if moes else 0
+        self.layers, self.topk, self.cache, self.alpha = moes[len(moes) - n:], int(topk), cache, float(alpha)
+        self._saved = []
+
+    def __enter__(self):
+        self._saved = [m.top_k_override for m in self.layers]
+        for m in self.layers:
+            m.top_k_override = self.topk
+        return self
+
+    def __exit__(self, *exc):
+        for m, v in zip(self.layers, self._saved):
+            m.top_k_override = v
+        return False
+
+    def contrast(self, strong: torch.Tensor, weak_fn) -> torch.Tensor:
+        with self:
+            weak = weak_fn()
+        return ((1 + self.alpha) * torch.log_softmax(strong.float(), -1)
+                - self.alpha * torch.log_softmax(weak.float(), -1)).to(strong.dtype)
 
 
 def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_dtype, L, gen, stats, eos_id,
@@ -570,6 +619,9 @@ def main(argv=None):
                     help="speculative acceptance by the target's verifier head (0: rejection sampling)")
     ap.add_argument("--compress_kv_slots", type=int, default=0, help="compressed memory rows of the cache")
     ap.add_argument("--mem_slots", type=int, default=None, help="alias of --compress_kv_slots")
+    ap.add_argument("--scmoe_alpha", type=float, default=0.0, help="self-contrast MoE strength (0: off)")
+    ap.add_argument("--scmoe_topk", type=int, default=1, help="routed experts of the weak pass")
+    ap.add_argument("--scmoe_frac", type=float, default=1.0, help="fraction of (last) MoE layers weakened")
     ap.add_argument("--adaptive_layer_power", type=float, default=1.0)
     # model / context
     ap.add_argument("--mobile_preset", default=None, help="alias of --preset")
@@ -648,7 +700,8 @@ def main(argv=None):
                        adaptive_conf_floor=a.adaptive_conf_floor, adaptive_layer_ramp=a.adaptive_layer_ramp,
                        early_exit=a.early_exit, early_exit_entropy=a.early_exit_entropy,
                        early_exit_mode=a.early_exit_mode, verify_threshold=a.verify_threshold,
-                       compress_kv_slots=a.compress_kv_slots, adaptive_layer_power=a.adaptive_layer_power)
+                       compress_kv_slots=a.compress_kv_slots, adaptive_layer_power=a.adaptive_layer_power,
+                       scmoe_alpha=a.scmoe_alpha, scmoe_topk=a.scmoe_topk, scmoe_frac=a.scmoe_frac)
     text = tok.decode(out[0, ids.shape[1]:].tolist())
     if a.tool_use:
         from .tools import ToolRegistry

@@ -435,3 +435,32 @@ def test_generate_cli_retrieval_template_tools_certificate(tmp_path, capsys):
           "--json", "--target_ctx", "16384", "--prompt", "where is the eiffel tower", "--no_cuda_graph"])
     out = _json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert "certificate" in out and out["stats"]["prompt_tokens"] > len("where is the eiffel tower")
+
+
+def test_scmoe_contrast_decoding():
+    """Self-contrast MoE: alpha 0 is plain decoding; a weak pass with as many experts as the strong
+    one contrasts to the same distribution (greedy output unchanged); the first token follows
+    (1 + a) log p_strong - a log p_weak computed by hand with top-1 routing."""
+    from omnicoder.inference.generate import _prefill, generate
+    from omnicoder.inference.kv_cache import KVCache
+    torch.manual_seed(0)
+    cfg = ModelConfig(name="sc", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64,
+                      moe=MoEConfig(n_experts=4, top_k=2, ffn_dim=64))
+    m = build_model(cfg, device="cpu", seed=0).eval()
+    ids = torch.tensor([[5, 9, 2, 7], [8, 1, 4, 6]])
+    base = generate(m, ids, 5, temperature=0.0, top_k=0, top_p=1.0)
+    assert torch.equal(generate(m, ids, 5, temperature=0.0, top_k=0, top_p=1.0, scmoe_alpha=0.0), base)
+    assert torch.equal(generate(m, ids, 5, temperature=0.0, top_k=0, top_p=1.0, scmoe_alpha=0.7, scmoe_topk=2),
+                       base)
+    got = generate(m, ids, 1, temperature=0.0, top_k=0, top_p=1.0, scmoe_alpha=1.5, scmoe_topk=1)
+    strong = _prefill(m, ids, KVCache(cfg, 2, 16, "cpu"))
+    for b in m.blocks:
+        b.ffn.top_k_override = 1
+    weak = _prefill(m, ids, KVCache(cfg, 2, 16, "cpu"))
+    for b in m.blocks:
+        b.ffn.top_k_override = None
+    want = (2.5 * torch.log_softmax(strong.float(), -1) - 1.5 * torch.log_softmax(weak.float(), -1)).argmax(-1)
+    assert torch.equal(got[:, -1], want)
+    assert all(b.ffn.top_k_override is None for b in m.blocks)      # restored after decoding
+    with pytest.raises(ValueError):
+        generate(m, ids, 2, scmoe_alpha=1.0, adaptive_moe=True)
