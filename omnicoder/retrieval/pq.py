@@ -61,3 +61,40 @@ class PQRetriever:
         dist = table[np.arange(self.M)[None, :], self.codes].sum(1)
         top = np.argsort(dist)[:k]
         return [(int(i), float(dist[i]), self.docs[i]) for i in top]
+
+    def budget_profile(self) -> dict:
+        """Bytes the index keeps resident: codes (1 byte per sub-vector when K <= 256), codebooks,
+        the projection and the vocabulary's idf weights."""
+        code_b = 1 if self.K <= 256 else 2
+        return {"docs": len(self.docs), "subspaces": self.M, "centroids": self.K, "dim": self.sub * self.M,
+                "codes_bytes": int(self.codes.shape[0] * self.M * code_b),
+                "codebooks_bytes": int(sum(c.size for c in self.codebooks) * 4),
+                "projection_bytes": int(self.proj.size * 4),
+                "idf_bytes": int(len(self.vec.idf_) * 4)}
+
+    def save(self, out_dir: str) -> None:
+        """Arrays in `pq.npz`, vocabulary / settings / documents in `pq.json` (no pickles)."""
+        import json
+        import os
+        os.makedirs(out_dir, exist_ok=True)
+        np.savez(os.path.join(out_dir, "pq.npz"), proj=self.proj, codes=self.codes,
+                 codebooks=np.stack(self.codebooks), idf=self.vec.idf_.astype(np.float64))
+        with open(os.path.join(out_dir, "pq.json"), "w", encoding="utf-8") as f:
+            json.dump({"M": self.M, "K": self.K, "dim": self.dim, "seed": self.seed, "sub": self.sub,
+                       "vocabulary": {k: int(v) for k, v in self.vec.vocabulary_.items()}, "docs": self.docs}, f)
+
+    @classmethod
+    def load(cls, out_dir: str) -> "PQRetriever":
+        import json
+        import os
+        from sklearn.feature_extraction.text import TfidfVectorizer
+        with open(os.path.join(out_dir, "pq.json"), encoding="utf-8") as f:
+            meta = json.load(f)
+        arr = np.load(os.path.join(out_dir, "pq.npz"))
+        r = cls(meta["M"], meta["K"], meta["dim"], meta["seed"])
+        r.sub, r.docs = meta["sub"], meta["docs"]
+        r.vec = TfidfVectorizer(vocabulary=meta["vocabulary"])
+        r.vec.idf_ = arr["idf"]
+        r.proj, r.codes = arr["proj"], arr["codes"]
+        r.codebooks = list(arr["codebooks"])
+        return r

@@ -1,0 +1,705 @@
+"""Small operational tools behind one command: ``python -m omnicoder.tools.utilities <tool> ...``.
+
+Each subcommand is the counterpart of one of the reference's single-purpose scripts
+(src/omnicoder/tools/*.py):
+
+  presets-export    model presets as JSON                         (presets_export.py:1-32)
+  weights-validate  an exported package: files present, sizes and checksums match its manifests
+                                                                  (weights_validator.py:1-31)
+  threshold-check   fail when a metrics JSON's tokens/s is under a floor   (threshold_check.py:1-27)
+  metrics-canary    measure decode tokens/s and write that metrics JSON    (metrics_canaries.py)
+  kv-budget         KV bytes implied by a paging / quantisation sidecar against a limit
+                                                                  (kv_budget_enforce.py:1-47)
+  mobile-budget     artefact bytes of a package + KV bytes at a target context against a budget
+                                                                  (mobile_budget_check.py:1-146)
+  kv-calibrate      per-layer, per-group statistics of the KV cache over sample prompts and the
+                    static u8 / nf4 parameters they imply                  (kv_calibrate.py:1-170)
+  pq-build          product-quantised index over a folder of .txt files    (pq_build.py:1-45)
+  router-ablate     decode tokens/s of the reference-layout MoE model with each router kind
+                                                                  (router_ablate.py:1-77)
+  env-audit         environment variables the package reads, documented-vs-used drift and the
+                    set-but-unknown ones                                   (env_audit.py:1-92)
+  gen-predictions   add a `prediction` to every row of a VQA / caption JSONL (gen_predictions.py)
+
+Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
+could not be read.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import torch
+
+GiB = 1 << 30
+MiB = 1 << 20
+
+
+def _write_json(path: str, obj) -> None:
+    if not path:
+        return
+    d = os.path.dirname(path)
+    if d:
+        os.makedirs(d, exist_ok=True)
+    with open(path, "w", encoding="utf-8") as f:
+        json.dump(obj, f, indent=1, default=str)
+
+
+# ---- presets-export -------------------------------------------------------------
+def presets_export(names: list[str] | None = None) -> dict:
+    """{preset: ModelConfig as a dict} for the named presets (default: every preset)."""
+    from ..config import get_preset, list_presets
+    return {n: get_preset(n).to_dict() for n in (names or list_presets())}
+
+
+def _cmd_presets_export(a) -> int:
+    data = presets_export(a.names)
+    _write_json(a.out, data)
+    print(json.dumps({"presets": sorted(data), "out": a.out}))
+    return 0
+
+
+# ---- weights-validate -----------------------------------------------------------
+def validate_package(root: str, required: tuple = ("phone_manifest.json",)) -> dict:
+    """Check an exported package directory.
+
+    * every `required` path exists;
+    * every artefact `phone_manifest.json` lists with a `file` exists with the recorded size;
+    * every sub-package with a `manifest.json` (the int4 package) has each listed file with the
+      recorded size and sha256.
+    Returns {"ok", "checked", "problems": [...]}.
+    """
+    from ..export.mobile_packager import _sha
+    problems, checked = [], 0
+    for rel in required:
+        checked += 1
+        if not os.path.exists(os.path.join(root, rel)):
+            problems.append(f"missing: {rel}")
+    top = os.path.join(root, "phone_manifest.json")
+    if os.path.exists(top):
+        with open(top, encoding="utf-8") as f:
+            man = json.load(f)
+        for name, art in man.get("artifacts", {}).items():
+            if not isinstance(art, dict) or "file" not in art:
+                continue
+            checked += 1
+            p = os.path.join(root, art["file"])
+            if not os.path.exists(p):
+                problems.append(f"{name}: missing {art['file']}")
+            elif "bytes" in art and os.path.getsize(p) != art["bytes"]:
+                problems.append(f"{name}: {art['file']} is {os.path.getsize(p)} bytes, manifest says {art['bytes']}")
+    for d, _, files in os.walk(root):
+        if "manifest.json" not in files:
+            continue
+        with open(os.path.join(d, "manifest.json"), encoding="utf-8") as f:
+            sub = json.load(f)
+        for fname, meta in sub.get("files", {}).items():
+            checked += 1
+            p = os.path.join(d, fname)
+            rel = os.path.relpath(p, root)
+            if not os.path.exists(p):
+                problems.append(f"missing: {rel}")
+            elif os.path.getsize(p) != meta.get("bytes", -1):
+                problems.append(f"size mismatch: {rel}")
+            elif "sha256" in meta and _sha(p) != meta["sha256"]:
+                problems.append(f"checksum mismatch: {rel}")
+    return {"ok": not problems, "checked": checked, "problems": problems}
+
+
+def _cmd_weights_validate(a) -> int:
+    r = validate_package(a.root, tuple(a.require))
+    print(json.dumps(r))
+    return 0 if r["ok"] else 2
+
+
+# ---- metrics-canary / threshold-check -------------------------------------------
+@torch.no_grad()
+def decode_tokens_per_second(model, prompt_len: int = 32, new_tokens: int = 64, batch: int = 1,
+                             kv_dtype: str = "bf16", warmup: int = 1) -> dict:
+    """Greedy cached decode through the model's own cache path; tokens/s = batch * new_tokens / time."""
+    from ..inference.kv_cache import KVCache
+    dev = next(model.parameters()).device
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(1, model.cfg.vocab_size, (batch, prompt_len), generator=g).to(dev)
+
+    def run():
+        cache = KVCache(model.cfg, batch, prompt_len + new_tokens + 1, dev, kv_dtype=kv_dtype)
+        logits = model.forward_cached(ids, cache, prefill=True, last_only=True)
+        nxt = logits[:, -1].argmax(-1, keepdim=True)
+        for _ in range(new_tokens - 1):
+            nxt = model.forward_cached(nxt, cache, last_only=True)[:, -1].argmax(-1, keepdim=True)
+        return nxt
+
+    for _ in range(warmup):
+        run()
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    run()
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+    dt = max(time.perf_counter() - t0, 1e-9)
+    return {"tokens_per_second": batch * new_tokens / dt, "seconds": dt, "batch": batch,
+            "new_tokens": new_tokens, "prompt_len": prompt_len, "kv_dtype": kv_dtype}
+
+
+def _cmd_metrics_canary(a) -> int:
+    from ..config import get_preset
+    from ..models.lm import build_model
+    dev = torch.device(a.device)
+    dt = torch.float32 if dev.type == "cpu" else torch.bfloat16
+    model = build_model(get_preset(a.preset), device=dev, dtype=dt, seed=0).eval()
+    tok = decode_tokens_per_second(model, a.prompt_len, a.new_tokens, a.batch, a.kv_dtype)
+    out = {"preset": a.preset, "device": str(dev), "tokens": tok}
+    _write_json(a.out, out)
+    print(json.dumps(out))
+    return 0
+
+
+def threshold_check(metrics_json: str, min_tps: float) -> tuple[int, str]:
+    try:
+        with open(metrics_json, encoding="utf-8") as f:
+            tps = float(json.load(f).get("tokens", {}).get("tokens_per_second", 0.0))
+    except (OSError, ValueError) as e:
+        return 3, f"[threshold] ERROR: {e}"
+    if tps < min_tps:
+        return 2, f"[threshold] FAIL: tokens/s {tps:.2f} < {min_tps:.2f}"
+    return 0, f"[threshold] OK: tokens/s {tps:.2f} >= {min_tps:.2f}"
+
+
+def _cmd_threshold_check(a) -> int:
+    code, msg = threshold_check(a.metrics_json, a.min_tps)
+    print(msg)
+    return code
+
+
+# ---- kv-budget / mobile-budget --------------------------------------------------
+def _prod(xs) -> int:
+    n = 1
+    for x in xs:
+        n *= int(x)
+    return n
+
+
+def kv_bytes_from_sidecar(meta: dict, kvq: dict | None = None, elem_bytes: int = 2) -> int:
+    """KV bytes one sequence needs, from a paging sidecar.
+
+    This framework's sidecar carries the per-layer cache shapes (`k_shape`, `v_shape`, `n_layers`):
+    bytes = n_layers * (|k| + |v|) * element bytes, or with a quantisation sidecar
+    (`bits`, `group`) |kv| * bits / 8 plus one fp32 scale per group.  The reference's form
+    (`page_len`, `heads`, `dl` or `dl_per_layer`, `spill_bytes`) is read as
+    layers * heads * dl * page_len * 2 + spill_bytes.
+    """
+    if "k_shape" in meta:
+        elems = int(meta.get("n_layers", 1)) * (_prod(meta["k_shape"]) + _prod(meta.get("v_shape", [0])))
+        if kvq and kvq.get("bits"):
+            return elems * int(kvq["bits"]) // 8 + -(-elems // max(1, int(kvq.get("group", 64)))) * 4
+        return elems * elem_bytes
+    page_len, heads = int(meta.get("page_len", 0)), int(meta.get("heads", 0))
+    per_layer = meta.get("dl_per_layer")
+    if isinstance(per_layer, list) and per_layer:
+        kv = sum(int(d) for d in per_layer) * heads * page_len * 2
+    else:
+        kv = int(meta.get("n_layers", 0)) * heads * int(meta.get("dl", 0)) * page_len * 2
+    return kv + max(0, int(meta.get("spill_bytes", 0)))
+
+
+def _read_json(path: str) -> dict:
+    with open(path, encoding="utf-8") as f:
+        return json.load(f)
+
+
+def _cmd_kv_budget(a) -> int:
+    try:
+        meta = _read_json(a.sidecar)
+        kvq = _read_json(a.kvq_sidecar) if a.kvq_sidecar else None
+    except (OSError, ValueError) as e:
+        print(json.dumps({"error": str(e)}))
+        return 3
+    mb = kv_bytes_from_sidecar(meta, kvq) / MiB
+    out = {"kv_mb": mb, "max_kv_mb": a.max_kv_mb, "pass": mb <= a.max_kv_mb, "source": a.sidecar}
+    _write_json(a.out, out)
+    print(json.dumps(out))
+    return 0 if out["pass"] else 2
+
+
+def kv_bytes_at(cfg, ctx: int, kvq: str = "bf16", group: int = 64, batch: int = 1) -> int:
+    """KV bytes of `batch` sequences of `ctx` tokens: bf16; int8 as this framework stores it (one
+    fp32 scale per latent row, or per head for GQA); u8 / nf4 with one fp32 scale per `group`."""
+    a = cfg.attn
+    if a.kind == "mla":
+        per_tok, rows = a.kv_lora_rank + a.qk_rope_dim, 1
+    else:
+        per_tok, rows = 2 * cfg.n_kv_heads * cfg.head_dim, 2 * cfg.n_kv_heads
+    n = cfg.n_layers * batch * ctx
+    if kvq == "bf16":
+        return n * per_tok * 2
+    if kvq == "int8":
+        return n * (per_tok + rows * 4)
+    bits = {"u8": 8, "nf4": 4}[kvq]
+    return n * (per_tok * bits // 8 + -(-per_tok // group) * 4)
+
+
+def mobile_budget(root: str, target_ctx: int, kvq: str, budget_gb: float, preset: str | None = None) -> dict:
+    """Resident memory of a package at `target_ctx` against `budget_gb`: the weights the runtime
+    loads (the int4 package when present, else every file), the KV cache and the decode
+    activations; also the package's total bytes on disk."""
+    from ..config import ModelConfig, get_preset
+    from ..inference.tools import estimate_memory
+    disk = sum(os.path.getsize(os.path.join(d, f)) for d, _, fs in os.walk(root) for f in fs)
+    int4 = os.path.join(root, "int4")
+    weights = sum(os.path.getsize(os.path.join(int4, f)) for f in os.listdir(int4)) if os.path.isdir(int4) else disk
+    man = os.path.join(root, "phone_manifest.json")
+    if preset:
+        cfg = get_preset(preset)
+    elif os.path.exists(man):
+        cfg = ModelConfig.from_dict(_read_json(man)["config"])
+    else:
+        raise ValueError("no phone_manifest.json in the package: pass a preset")
+    kv = kv_bytes_at(cfg, target_ctx, kvq)
+    act = estimate_memory(cfg, 1, target_ctx)["decode_activation_bytes"]
+    total = weights + kv + act
+    return {"disk_bytes": disk, "weights_bytes": weights, "kv_bytes": kv, "activation_bytes": act,
+            "resident_bytes": total, "resident_gb": total / GiB, "budget_gb": budget_gb,
+            "target_ctx": target_ctx, "kvq": kvq, "pass": total <= budget_gb * GiB}
+
+
+def _cmd_mobile_budget(a) -> int:
+    try:
+        r = mobile_budget(a.release_root, a.target_ctx, a.kvq, a.budget_gb, a.preset)
+    except (OSError, ValueError, KeyError) as e:
+        print(json.dumps({"error": str(e)}))
+        return 3
+    bench = {}
+    if a.bench_json and a.min_tps > 0:
+        code, msg = threshold_check(a.bench_json, a.min_tps)
+        bench = {"tps_check": msg, "tps_pass": code == 0}
+        r["pass"] = r["pass"] and code == 0
+    r.update(bench)
+    _write_json(a.out, r)
+    print(json.dumps(r))
+    return 0 if r["pass"] else 2
+
+
+# ---- kv-calibrate ---------------------------------------------------------------
+_SAMPLE_PROMPTS = [
+    "def fibonacci(n):\n    if n < 2:\n        return n\n    return fibonacci(n - 1) + fibonacci(n - 2)\n",
+    "The quick brown fox jumps over the lazy dog while the compiler reports no warnings.",
+    "SELECT name, count(*) FROM users GROUP BY name ORDER BY 2 DESC LIMIT 10;",
+    "for (int i = 0; i < n; ++i) { acc += a[i] * b[i]; }",
+]
+
+
+class _GroupStats:
+    """Running max / min / sum / sum of squares per (head, group) of one cache stream."""
+
+    def __init__(self):
+        self.mx = self.mn = self.s = self.ss = None
+        self.n = 0
+
+    def add(self, x: torch.Tensor, group: int):           # x [T, H, D]
+        T, H, D = x.shape
+        G = -(-D // group)
+        x = torch.nn.functional.pad(x.float(), (0, G * group - D)).view(T, H, G, group)
+        mx, mn = x.amax((0, 3)), x.amin((0, 3))
+        s, ss = x.sum((0, 3)), (x * x).sum((0, 3))
+        if self.mx is None:
+            self.mx, self.mn, self.s, self.ss = mx, mn, s, ss
+        else:
+            self.mx, self.mn = torch.maximum(self.mx, mx), torch.minimum(self.mn, mn)
+            self.s, self.ss = self.s + s, self.ss + ss
+        self.n += T * group
+
+    def params(self) -> dict:
+        mean = self.s / max(1, self.n)
+        std = (self.ss / max(1, self.n) - mean * mean).clamp_min(0).sqrt()
+        scale = ((self.mx - self.mn) / 255.0).clamp_min(1e-8)
+        return {"max": self.mx, "min": self.mn, "mean": mean, "std": std,
+                "u8_scale": scale, "u8_zero": torch.round(-self.mn / scale).clamp(0, 255),
+                "nf4_absmax": torch.maximum(self.mx.abs(), self.mn.abs())}
+
+
+def _static_u8_error(x: torch.Tensor, p: dict, group: int) -> float:
+    """Relative L2 error of quantising x [T, H, D] with the static u8 parameters."""
+    T, H, D = x.shape
+    G = p["u8_scale"].shape[-1]
+    xp = torch.nn.functional.pad(x.float(), (0, G * group - D)).view(T, H, G, group)
+    s, z = p["u8_scale"][None, :, :, None], p["u8_zero"][None, :, :, None]
+    q = torch.clamp(torch.round(xp / s) + z, 0, 255)
+    err = ((q - z) * s - xp).reshape(T, H, -1)[..., :D]
+    return float(err.norm() / x.float().norm().clamp_min(1e-12))
+
+
+@torch.no_grad()
+def kv_calibrate(model, prompts: list[list[int]], group: int = 64) -> dict:
+    """Run each prompt through the model's cached prefill and collect, per layer and per cache
+    stream (MLA: the latent row; GQA: keys and values per head), statistics per group of `group`
+    channels.  Returns {"group", "layers": [{stream: {stat: tensor [H, G]}}], "u8_rel_err": [...]}
+    where u8_rel_err is the error of the static u8 parameters on the calibration data itself."""
+    from ..inference.kv_cache import KVCache
+    dev = next(model.parameters()).device
+    L = model.cfg.n_layers
+    stats = [dict() for _ in range(L)]
+    seen = [[] for _ in range(L)]
+    for ids in prompts:
+        t = torch.tensor([ids], dtype=torch.long, device=dev)
+        cache = KVCache(model.cfg, 1, len(ids) + 1, dev)
+        model.forward_cached(t, cache, prefill=True, last_only=True)
+        lo, hi = cache.sink, cache.sink + len(ids)
+        for li in range(L):
+            streams = {"k": cache.k[li][0, lo:hi]}
+            if cache.v[li] is not None:
+                streams["v"] = cache.v[li][0, lo:hi]
+            for name, x in streams.items():
+                x = x[:, None] if x.dim() == 2 else x          # MLA latent: one "head"
+                stats[li].setdefault(name, _GroupStats()).add(x.cpu(), group)
+            seen[li].append({k: (v[:, None] if v.dim() == 2 else v).cpu() for k, v in streams.items()})
+    layers, errs = [], []
+    for li in range(L):
+        p = {name: st.params() for name, st in stats[li].items()}
+        layers.append(p)
+        e = [_static_u8_error(s[name], p[name], group) for s in seen[li] for name in s]
+        errs.append(max(e) if e else 0.0)
+    return {"group": group, "layers": layers, "u8_rel_err": errs}
+
+
+def _cmd_kv_calibrate(a) -> int:
+    from ..config import get_preset
+    from ..inference.builders import load_model
+    from ..models.lm import build_model
+    from ..training.tokenizer import get_tokenizer
+    dev = torch.device(a.device)
+    model = (load_model(a.ckpt, dev, dtype=torch.float32)[0] if a.ckpt else
+             build_model(get_preset(a.preset), device=dev, dtype=torch.float32, seed=0)).eval()
+    tok = get_tokenizer(model.cfg.vocab_size)
+    texts = _SAMPLE_PROMPTS
+    if a.prompts:
+        with open(a.prompts, encoding="utf-8") as f:
+            texts = [ln.rstrip("\n") for ln in f if ln.strip()]
+    ids = [tok.encode(t)[:a.max_tokens] or [1] for t in texts[:a.max_prompts or None]]
+    r = kv_calibrate(model, ids, a.group)
+    summary = {"scheme": a.scheme, "group": a.group, "prompts": len(ids), "layers": len(r["layers"]),
+               "u8_rel_err_max": max(r["u8_rel_err"]),
+               "per_layer": [{name: {"absmax": float(p[name]["nf4_absmax"].max()),
+                                     "std_mean": float(p[name]["std"].mean())} for name in p}
+                             for p in r["layers"]]}
+    if a.scheme == "u8":
+        summary["params"] = [{name: {"scale": p[name]["u8_scale"].tolist(), "zero": p[name]["u8_zero"].tolist()}
+                              for name in p} for p in r["layers"]]
+    else:
+        summary["params"] = [{name: {"absmax": p[name]["nf4_absmax"].tolist(), "mean": p[name]["mean"].tolist(),
+                                     "std": p[name]["std"].tolist()} for name in p} for p in r["layers"]]
+    _write_json(a.out, summary)
+    if a.stats_pt:
+        torch.save(r, a.stats_pt)
+    print(json.dumps({k: summary[k] for k in ("scheme", "group", "prompts", "layers", "u8_rel_err_max")}))
+    return 0
+
+
+# ---- pq-build ------------------------------------------------------------------
+def pq_build(root: str, out_dir: str, m: int = 8, ks: int = 64, dim: int = 256, max_docs: int = 0) -> dict:
+    """Index every .txt file under `root` (one document per file) and save it with a size profile."""
+    from ..retrieval.pq import PQRetriever
+    docs = []
+    for d, _, files in sorted(os.walk(root)):
+        for f in sorted(files):
+            if f.endswith(".txt"):
+                with open(os.path.join(d, f), encoding="utf-8", errors="replace") as fh:
+                    docs.append(fh.read())
+    if max_docs:
+        docs = docs[:max_docs]
+    if not docs:
+        raise ValueError(f"no .txt files under {root}")
+    pq = PQRetriever(m, ks, dim).fit(docs)
+    pq.save(out_dir)
+    prof = pq.budget_profile()
+    _write_json(os.path.join(out_dir, "budget_profile.json"), prof)
+    return prof
+
+
+def _cmd_pq_build(a) -> int:
+    try:
+        prof = pq_build(a.root, a.out_dir, a.m, a.ks, a.dim, a.max_docs)
+    except (OSError, ValueError) as e:
+        print(json.dumps({"error": str(e)}))
+        return 3
+    print(json.dumps({"out_dir": a.out_dir, **prof}))
+    return 0
+
+
+# ---- router-ablate --------------------------------------------------------------
+ROUTER_KINDS = ("topk", "multihead", "llm", "interaction", "hierarchical")
+
+
+def _make_router(kind: str, D: int, E: int, k: int):
+    from ..models import modules as M
+    if kind == "topk":
+        return M.TopKRouter(D, E, k=k)
+    if kind == "multihead":
+        return M.MultiHeadRouter(D, E, k=k, num_gates=4)
+    if kind == "llm":
+        return M.LLMRouter(D, E, k=k)
+    if kind == "interaction":
+        return M.InteractionRouter(D, E, k=k)
+    if kind == "hierarchical":
+        half = E // 2
+        return M.HierarchicalRouter(D, E, group_sizes=[half, E - half], k=k)
+    raise ValueError(f"router kind: one of {ROUTER_KINDS}")
+
+
+@torch.no_grad()
+def router_ablate(kinds=("topk", "llm"), new_tokens: int = 16, prompt_len: int = 8, device="cpu",
+                  **compat_kw) -> dict:
+    """Greedy decode tokens/s of the reference-layout model (models.compat.OmniTransformer, the
+    layout whose MoE layers hold a swappable `router`) with every MoE layer's router replaced by
+    each kind in turn; the same seed for every kind, so only the router differs."""
+    from ..models.compat import OmniTransformer
+    res = {}
+    for kind in kinds:
+        torch.manual_seed(0)
+        model = OmniTransformer(**compat_kw).to(device).eval()
+        c = model.c
+        for blk in model.blocks:
+            blk.moe.router = _make_router(kind, c.d_model, c.n_experts, c.top_k).to(device)
+        ids = torch.randint(1, c.vocab_size, (1, prompt_len), generator=torch.Generator().manual_seed(0)).to(device)
+        nxt, kv = model.decode_next_id(ids)                          # warm-up + first token
+        t0 = time.perf_counter()
+        for _ in range(new_tokens):
+            nxt, kv = model.decode_next_id(nxt, kv)
+        if str(device).startswith("cuda"):
+            torch.cuda.synchronize()
+        res[kind] = new_tokens / max(time.perf_counter() - t0, 1e-9)
+    base = res.get(kinds[0], 0.0)
+    return {"tokens_per_second": res, "baseline": kinds[0],
+            "speedup_x": {k: v / max(base, 1e-9) for k, v in res.items()}, "new_tokens": new_tokens}
+
+
+def _cmd_router_ablate(a) -> int:
+    from ..config import get_preset
+    kw = {}
+    if a.preset:
+        cfg = get_preset(a.preset)
+        kw = dict(vocab_size=cfg.vocab_size, n_layers=cfg.n_layers, d_model=cfg.d_model, n_heads=cfg.n_heads,
+                  mlp_dim=cfg.moe.ffn_dim if cfg.moe.enabled else cfg.ffn_dim,
+                  n_experts=max(2, cfg.moe.n_experts if cfg.moe.enabled else 2), top_k=max(1, cfg.moe.top_k),
+                  max_seq_len=cfg.max_seq_len, use_hrm=False)
+    for key in ("n_layers", "d_model", "n_experts", "vocab_size"):
+        if getattr(a, key):
+            kw[key] = getattr(a, key)
+    out = router_ablate(tuple(a.routers), a.max_new_tokens, device=a.device, **kw)
+    out["config"] = kw
+    _write_json(a.out_json, out)
+    print(json.dumps(out))
+    return 0
+
+
+# ---- env-audit ------------------------------------------------------------------
+def _documented_keys(path: str) -> list[str]:
+    """KEY names of a KEY=VALUE example file (commented `# KEY=...` lines count as documented)."""
+    keys = []
+    if path and os.path.exists(path):
+        with open(path, encoding="utf-8") as f:
+            for line in f:
+                s = line.strip().lstrip("#").strip()
+                if "=" in s:
+                    k = s.split("=", 1)[0].strip()
+                    if k.replace("_", "").isalnum() and k.upper() == k:
+                        keys.append(k)
+    return sorted(set(keys))
+
+
+def env_audit(root: str | None = None, env_example: str = "", prefix: str = "OMNICODER_") -> dict:
+    """Variables read under `root`, the drift between them and an example file, and the variables
+    with `prefix` that are set in this environment but read nowhere."""
+    from ..utils.env import scan_registry
+    reg = scan_registry(root)
+    used = {k for k in reg if k.startswith(prefix)}
+    doc = {k for k in _documented_keys(env_example) if k.startswith(prefix)}
+    unknown = sorted(k for k in os.environ if k.startswith(prefix) and k not in reg)
+    return {"registry": reg, "used_not_documented": sorted(used - doc),
+            "documented_not_used": sorted(doc - used) if env_example else [], "unknown_set": unknown}
+
+
+def _cmd_env_audit(a) -> int:
+    from ..utils.env import load_dotenv, registry_markdown
+    for p in (".env", ".env.tuned"):
+        load_dotenv(p)
+    r = env_audit(a.root or None, a.env_example, a.prefix)
+    _write_json(a.out_json, r["registry"])
+    if a.out_index:
+        os.makedirs(os.path.dirname(a.out_index) or ".", exist_ok=True)
+        with open(a.out_index, "w", encoding="utf-8") as f:
+            f.write("# Environment variables read by the package\n\n" + registry_markdown(r["registry"]) + "\n")
+    if a.sync_example and a.env_example:
+        with open(a.env_example, "a", encoding="utf-8") as f:
+            for k in r["used_not_documented"]:
+                f.write(f"# {k}=\n")
+    drift = bool(r["used_not_documented"] or r["documented_not_used"])
+    print(json.dumps({"registry_count": len(r["registry"]), "used_not_documented": r["used_not_documented"],
+                      "documented_not_used": r["documented_not_used"], "unknown_set": r["unknown_set"]}))
+    return 1 if (a.fail_on_drift and drift and not a.sync_example) else 0
+
+
+# ---- gen-predictions ------------------------------------------------------------
+def gen_predictions(rows: list[dict], task: str, lm, composer, tokenizer, image_size: int = 64,
+                    max_new_tokens: int = 16) -> list[dict]:
+    """Each row with a `prediction`: VQA rows {image, question, ...}; caption rows {image, ...}."""
+    from ..training.vl_tasks import TASKS, VLTaskTrainer, load_media
+    name = {"vqa": "vqa", "captions": "caption", "caption": "caption"}[task]
+    tr = VLTaskTrainer(lm, composer, tokenizer, name, train_lm=False)
+    modality, template, _ = TASKS[name]
+    out = []
+    for r in rows:
+        media = load_media(r[modality], image_size)
+        prompt = template.format(question=r.get("question", ""))
+        out.append({**r, "prediction": tr.answer(media, prompt, max_new_tokens).strip()})
+    return out
+
+
+def _cmd_gen_predictions(a) -> int:
+    from ..config import ModelConfig, get_preset
+    from ..models.lm import build_model
+    from ..multimodal.backbones import VisionBackbone
+    from ..multimodal.composer import FusionComposer
+    from ..training.tokenizer import get_tokenizer
+    dev = torch.device(a.device)
+    obj = torch.load(a.ckpt, map_location="cpu", weights_only=False) if a.ckpt else {}
+    cfg = ModelConfig.from_dict(obj["config"]) if "config" in obj else get_preset(a.preset)
+    lm = build_model(cfg, device=dev, dtype=torch.float32, seed=0).eval()
+    comp = FusionComposer(cfg.d_model, vision=VisionBackbone(a.vision, image_size=a.image_size, depth=2)).to(dev)
+    if "model" in obj:
+        lm.load_export_state_dict(obj["model"], strict=False)
+    if "composer" in obj:
+        comp.load_state_dict(obj["composer"], strict=False)
+    with open(a.input, encoding="utf-8") as f:
+        rows = [json.loads(ln) for ln in f if ln.strip()]
+    if a.limit:
+        rows = rows[:a.limit]
+    preds = gen_predictions(rows, a.task, lm, comp.eval(), get_tokenizer(cfg.vocab_size), a.image_size,
+                            a.max_new_tokens)
+    os.makedirs(os.path.dirname(a.out) or ".", exist_ok=True)
+    with open(a.out, "w", encoding="utf-8") as f:
+        for r in preds:
+            f.write(json.dumps(r) + "\n")
+    print(json.dumps({"task": a.task, "rows": len(preds), "out": a.out}))
+    return 0
+
+
+# ---- command line ---------------------------------------------------------------
+def _parser() -> argparse.ArgumentParser:
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    ap = argparse.ArgumentParser(description="omnicoder operational tools")
+    sub = ap.add_subparsers(dest="tool", required=True)
+
+    p = sub.add_parser("presets-export", help="model presets as JSON")
+    p.add_argument("--out", default="weights/presets.json")
+    p.add_argument("--names", nargs="*", default=None)
+    p.set_defaults(fn=_cmd_presets_export)
+
+    p = sub.add_parser("weights-validate", help="check an exported package against its manifests")
+    p.add_argument("--root", default="weights/phone")
+    p.add_argument("--require", nargs="*", default=["phone_manifest.json"])
+    p.set_defaults(fn=_cmd_weights_validate)
+
+    p = sub.add_parser("threshold-check", help="fail when tokens/s is under a floor")
+    p.add_argument("--metrics_json", default="weights/metrics_canaries.json")
+    p.add_argument("--min_tps", type=float, default=20.0)
+    p.set_defaults(fn=_cmd_threshold_check)
+
+    p = sub.add_parser("metrics-canary", help="measure cached-decode tokens/s")
+    p.add_argument("--preset", default="tiny_moe")
+    p.add_argument("--prompt_len", type=int, default=32)
+    p.add_argument("--new_tokens", type=int, default=64)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--kv_dtype", default="bf16", choices=["bf16", "int8"])
+    p.add_argument("--out", default="weights/metrics_canaries.json")
+    p.add_argument("--device", default=dev)
+    p.set_defaults(fn=_cmd_metrics_canary)
+
+    p = sub.add_parser("kv-budget", help="KV bytes of a paging sidecar against a limit")
+    p.add_argument("--sidecar", required=True)
+    p.add_argument("--kvq_sidecar", default="")
+    p.add_argument("--max_kv_mb", type=float, default=1024.0)
+    p.add_argument("--out", default="weights/kv_budget_summary.json")
+    p.set_defaults(fn=_cmd_kv_budget)
+
+    p = sub.add_parser("mobile-budget", help="resident bytes of a package at a target context")
+    p.add_argument("--release_root", default="weights/phone")
+    p.add_argument("--target_ctx", type=int, default=8192)
+    p.add_argument("--kvq", default="int8", choices=["bf16", "int8", "u8", "nf4"])
+    p.add_argument("--budget_gb", type=float, default=4.0)
+    p.add_argument("--preset", default=None, help="model config (default: the package's manifest)")
+    p.add_argument("--bench_json", default="", help="metrics JSON whose tokens/s must reach --min_tps")
+    p.add_argument("--min_tps", type=float, default=0.0)
+    p.add_argument("--out", default="weights/mobile_budget.json")
+    p.set_defaults(fn=_cmd_mobile_budget)
+
+    p = sub.add_parser("kv-calibrate", help="KV-cache statistics and static quantisation parameters")
+    p.add_argument("--preset", default="tiny_moe")
+    p.add_argument("--ckpt", default="")
+    p.add_argument("--prompts", default="", help="text file, one prompt per line (default: built-in samples)")
+    p.add_argument("--max_prompts", type=int, default=0)
+    p.add_argument("--max_tokens", type=int, default=512)
+    p.add_argument("--group", type=int, default=64)
+    p.add_argument("--scheme", default="u8", choices=["u8", "nf4"])
+    p.add_argument("--out", default="weights/kvq_calibration.json")
+    p.add_argument("--stats_pt", default="", help="also save the raw statistics tensors here")
+    p.add_argument("--device", default="cpu")
+    p.set_defaults(fn=_cmd_kv_calibrate)
+
+    p = sub.add_parser("pq-build", help="product-quantised index over a folder of .txt files")
+    p.add_argument("root")
+    p.add_argument("out_dir")
+    p.add_argument("--m", type=int, default=8)
+    p.add_argument("--ks", type=int, default=64)
+    p.add_argument("--dim", type=int, default=256)
+    p.add_argument("--max_docs", type=int, default=0)
+    p.set_defaults(fn=_cmd_pq_build)
+
+    p = sub.add_parser("router-ablate", help="decode tokens/s per router kind")
+    p.add_argument("--preset", default="", help="sizes of this preset (default: the compat defaults)")
+    p.add_argument("--routers", nargs="+", default=["topk", "llm"], choices=ROUTER_KINDS)
+    p.add_argument("--n_layers", type=int, default=0)
+    p.add_argument("--d_model", type=int, default=0)
+    p.add_argument("--n_experts", type=int, default=0)
+    p.add_argument("--vocab_size", type=int, default=0)
+    p.add_argument("--max_new_tokens", type=int, default=32)
+    p.add_argument("--out_json", default="weights/router_ablation.json")
+    p.add_argument("--device", default=dev)
+    p.set_defaults(fn=_cmd_router_ablate)
+
+    p = sub.add_parser("env-audit", help="environment variables read, drift and unknown ones")
+    p.add_argument("--root", default="", help="source root to scan (default: this package)")
+    p.add_argument("--env_example", default="")
+    p.add_argument("--prefix", default="OMNICODER_")
+    p.add_argument("--out_json", default="weights/env_registry.json")
+    p.add_argument("--out_index", default="")
+    p.add_argument("--sync_example", action="store_true", help="append undocumented keys to --env_example")
+    p.add_argument("--fail_on_drift", action="store_true")
+    p.set_defaults(fn=_cmd_env_audit)
+
+    p = sub.add_parser("gen-predictions", help="add predictions to a VQA / caption JSONL")
+    p.add_argument("--task", default="vqa", choices=["vqa", "captions"])
+    p.add_argument("--input", required=True)
+    p.add_argument("--out", default="weights/predictions.jsonl")
+    p.add_argument("--ckpt", default="", help="vision-language checkpoint (model, composer, config)")
+    p.add_argument("--preset", default="tiny_moe")
+    p.add_argument("--vision", default="vit_tiny")
+    p.add_argument("--image_size", type=int, default=64)
+    p.add_argument("--max_new_tokens", type=int, default=16)
+    p.add_argument("--limit", type=int, default=0)
+    p.add_argument("--device", default=dev)
+    p.set_defaults(fn=_cmd_gen_predictions)
+    return ap
+
+
+def main(argv=None) -> int:
+    a = _parser().parse_args(argv)
+    return int(a.fn(a) or 0)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,147 @@
+"""Operational tools (omnicoder.tools.utilities): each subcommand through its CLI entry on CPU."""
+import json
+import os
+
+import torch
+
+from omnicoder.tools import utilities as U
+
+
+def _cli(argv) -> int:
+    return U.main(argv)
+
+
+def test_presets_export_and_threshold(tmp_path):
+    out = tmp_path / "p.json"
+    assert _cli(["presets-export", "--out", str(out), "--names", "tiny_moe", "mobile_2gb"]) == 0
+    data = json.loads(out.read_text())
+    assert set(data) == {"tiny_moe", "mobile_2gb"} and data["mobile_2gb"]["n_layers"] == 8
+    m = tmp_path / "m.json"
+    assert _cli(["metrics-canary", "--preset", "tiny_moe", "--prompt_len", "4", "--new_tokens", "4", "--out", str(m),
+                 "--device", "cpu"]) == 0
+    tps = json.loads(m.read_text())["tokens"]["tokens_per_second"]
+    assert tps > 0
+    assert _cli(["threshold-check", "--metrics_json", str(m), "--min_tps", str(tps / 2)]) == 0
+    assert _cli(["threshold-check", "--metrics_json", str(m), "--min_tps", str(tps * 1e6)]) == 2
+    assert _cli(["threshold-check", "--metrics_json", str(tmp_path / "absent.json")]) == 3
+
+
+def test_package_validate_and_budgets(tmp_path):
+    from omnicoder.config import get_preset
+    from omnicoder.export.onnx_export import write_sidecars
+    from omnicoder.models.lm import build_model
+    from omnicoder.tools.export_to_phone import export_for_phone
+    model = build_model(get_preset("tiny_moe"), dtype=torch.float32).eval()
+    root = tmp_path / "phone"
+    export_for_phone(model, str(root), onnx=False, gguf=True, runtimes=False)
+    assert _cli(["weights-validate", "--root", str(root)]) == 0
+    # a corrupted int4 file is caught by its checksum, a missing required file by name
+    f = next(p for p in (root / "int4").iterdir() if p.name != "manifest.json")
+    b = bytearray(f.read_bytes())
+    b[-1] ^= 0xFF
+    f.write_bytes(bytes(b))
+    r = U.validate_package(str(root), ("phone_manifest.json", "decode_step.onnx"))
+    assert not r["ok"] and any("checksum" in p for p in r["problems"]) and "missing: decode_step.onnx" in r["problems"]
+
+    # resident budget: weights (int4 package) + KV + activations; int8 KV is smaller than bf16
+    out = tmp_path / "mb.json"
+    assert _cli(["mobile-budget", "--release_root", str(root), "--target_ctx", "256", "--kvq", "int8",
+                 "--budget_gb", "4", "--out", str(out)]) == 0
+    mb = json.loads(out.read_text())
+    assert mb["pass"] and mb["weights_bytes"] > 0 and mb["kv_bytes"] > 0
+    cfg = model.cfg
+    assert U.kv_bytes_at(cfg, 1024, "int8") < U.kv_bytes_at(cfg, 1024, "bf16")
+    assert U.kv_bytes_at(cfg, 1024, "nf4") < U.kv_bytes_at(cfg, 1024, "u8")
+    assert _cli(["mobile-budget", "--release_root", str(root), "--target_ctx", "256", "--budget_gb", "1e-6",
+                 "--out", str(out)]) == 2
+
+    # KV budget from the exporter's own sidecars (paging + u8 quantisation)
+    onnx_path = str(tmp_path / "ds.onnx")
+    side = write_sidecars(model, onnx_path, max_len=512, kv_page_len=128, kvq="u8", kvq_group=64)
+    paging, kvq = side
+    full = U.kv_bytes_from_sidecar(json.load(open(paging)))
+    quant = U.kv_bytes_from_sidecar(json.load(open(paging)), json.load(open(kvq)))
+    assert quant < full
+    assert full == U.kv_bytes_at(cfg, 512, "bf16") + cfg.n_layers * 2 * (cfg.attn.kind == "mla")
+    assert _cli(["kv-budget", "--sidecar", paging, "--max_kv_mb", "1024", "--out", str(tmp_path / "k.json")]) == 0
+    assert _cli(["kv-budget", "--sidecar", paging, "--max_kv_mb", "1e-6", "--out", str(tmp_path / "k.json")]) == 2
+    # the reference's sidecar form: layers * heads * dl * page_len * 2 + spill
+    assert U.kv_bytes_from_sidecar({"page_len": 4, "n_layers": 2, "heads": 3, "dl": 5, "spill_bytes": 7}) == \
+        2 * 3 * 5 * 4 * 2 + 7
+
+
+def test_kv_calibrate_static_u8(tmp_path):
+    from omnicoder.config import get_preset
+    from omnicoder.models.lm import build_model
+    model = build_model(get_preset("tiny_moe"), dtype=torch.float32).eval()
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(1, model.cfg.vocab_size, (n,), generator=g).tolist() for n in (5, 9)]
+    r = U.kv_calibrate(model, prompts, group=32)
+    assert len(r["layers"]) == model.cfg.n_layers
+    p = r["layers"][0]["k"]
+    assert (p["max"] >= p["min"]).all() and (p["u8_zero"] >= 0).all() and (p["u8_zero"] <= 255).all()
+    # 8-bit static parameters from the data itself reproduce it to well under 1 %
+    assert max(r["u8_rel_err"]) < 1e-2
+    out = tmp_path / "kvq.json"
+    assert _cli(["kv-calibrate", "--preset", "tiny_moe", "--max_tokens", "16", "--scheme", "nf4", "--out",
+                 str(out)]) == 0
+    d = json.loads(out.read_text())
+    assert d["scheme"] == "nf4" and len(d["params"]) == model.cfg.n_layers and "absmax" in d["params"][0]["k"]
+
+
+def test_pq_build_save_load(tmp_path):
+    from omnicoder.retrieval.pq import PQRetriever
+    docs = tmp_path / "docs"
+    docs.mkdir()
+    topics = ["cuda kernels tensor cores shared memory", "python lists dictionaries loops",
+              "sql joins indexes queries", "rust borrow checker lifetimes"]
+    for i in range(12):
+        (docs / f"d{i}.txt").write_text(f"{topics[i % 4]} note {i}")
+    out = tmp_path / "idx"
+    assert _cli(["pq-build", str(docs), str(out), "--m", "4", "--ks", "4", "--dim", "16"]) == 0
+    prof = json.loads((out / "budget_profile.json").read_text())
+    assert prof["docs"] == 12 and prof["codes_bytes"] == 12 * 4
+    pq = PQRetriever.load(str(out))
+    hit = pq.search("tensor cores kernels", k=3)
+    assert any("cuda" in d for _, _, d in hit)
+    assert _cli(["pq-build", str(tmp_path / "empty"), str(out)]) == 3
+
+
+def test_router_ablate_and_env_audit(tmp_path, monkeypatch):
+    out = tmp_path / "r.json"
+    assert _cli(["router-ablate", "--routers", "topk", "llm", "hierarchical", "--n_layers", "1", "--d_model", "64",
+                 "--n_experts", "4", "--vocab_size", "256", "--max_new_tokens", "2", "--out_json", str(out),
+                 "--device", "cpu"]) == 0
+    r = json.loads(out.read_text())
+    assert set(r["tokens_per_second"]) == {"topk", "llm", "hierarchical"} and r["speedup_x"]["topk"] == 1.0
+
+    src = tmp_path / "src"
+    src.mkdir()
+    (src / "m.py").write_text('import os\na = os.environ.get("OMNICODER_A", "1")\nb = os.getenv("OMNICODER_B")\n')
+    ex = tmp_path / "env.example"
+    ex.write_text("OMNICODER_A=1\n# OMNICODER_OLD=0\n")
+    monkeypatch.setenv("OMNICODER_STRAY", "x")
+    r = U.env_audit(str(src), str(ex))
+    assert r["used_not_documented"] == ["OMNICODER_B"] and r["documented_not_used"] == ["OMNICODER_OLD"]
+    assert "OMNICODER_STRAY" in r["unknown_set"]
+    args = ["env-audit", "--root", str(src), "--env_example", str(ex), "--out_json", str(tmp_path / "e.json"),
+            "--out_index", str(tmp_path / "e.md")]
+    assert _cli(args + ["--fail_on_drift"]) == 1
+    assert _cli(args + ["--sync_example"]) == 0 and "OMNICODER_B" in ex.read_text()
+    assert "OMNICODER_A" in (tmp_path / "e.md").read_text()
+
+
+def test_gen_predictions(tmp_path):
+    rows = []
+    for i in range(2):
+        p = tmp_path / f"img{i}.pt"
+        torch.save(torch.rand(3, 32, 32) * 2 - 1, p)
+        rows.append({"image": str(p), "question": f"what is {i}?", "answer": str(i)})
+    inp = tmp_path / "vqa.jsonl"
+    inp.write_text("\n".join(json.dumps(r) for r in rows) + "\n")
+    out = tmp_path / "pred.jsonl"
+    assert _cli(["gen-predictions", "--task", "vqa", "--input", str(inp), "--out", str(out), "--image_size", "32",
+                 "--max_new_tokens", "2", "--device", "cpu"]) == 0
+    pred = [json.loads(ln) for ln in out.read_text().splitlines()]
+    assert len(pred) == 2 and all("prediction" in p and p["answer"] == str(i) for i, p in enumerate(pred))
+    assert os.path.getsize(out) > 0
