@@ -44,7 +44,7 @@ def run_with_timeout(cmd: list[str], timeout_s: float, env=None) -> int:
 def plan(budget_minutes: float, steps_per_minute: float, stages: list[str]) -> dict:
     """Split the budget by relative shares of the requested stages."""
     share = {"pretrain": 0.8, "distill": 0.1, "draft": 0.15, "draft_kd": 0.1, "code_expert": 0.1, "verifier": 0.05, "vl": 0.1, "vqa": 0.05, "rl": 0.1,
-             "eval": 0.03, "export": 0.05, "package": 0.03}
+             "pre_align": 0.05, "align": 0.05, "flow_recon": 0.05, "audio_recon": 0.05, "eval": 0.03, "export": 0.05, "package": 0.03}
     tot = sum(share[s] for s in stages) or 1.0
     return {s: {"minutes": budget_minutes * share[s] / tot,
                 "steps": max(1, int(budget_minutes * share[s] / tot * steps_per_minute))} for s in stages}
@@ -124,6 +124,18 @@ def main(argv=None):
             cmd = [sys.executable, "-m", "omnicoder.training.vl_tasks", "--task", "vl_pretrain" if s == "vl" else "vqa",
                    "--preset", a.preset, "--steps", str(p[s]["steps"]), "--out", os.path.join(a.out_dir, f"{s}.pt")]
             cmd += dev
+        elif s == "pre_align":
+            cmd = [sys.executable, "-m", "omnicoder.training.pre_align", "--steps", str(p[s]["steps"]), "--audio",
+                   "--out", os.path.join(a.out_dir, "pre_align.pt")] + dev
+        elif s == "align":
+            pa = os.path.join(a.out_dir, "pre_align.pt")
+            cmd = [sys.executable, "-m", "omnicoder.training.concept_align", "--preset", a.preset, "--steps",
+                   str(p[s]["steps"]), "--out", os.path.join(a.out_dir, "concept_head.pt")] + dev
+            if os.path.exists(pa):
+                cmd += ["--pre_align_ckpt", pa]
+        elif s in ("flow_recon", "audio_recon"):
+            cmd = [sys.executable, "-m", f"omnicoder.training.{s}", "--preset", a.preset, "--steps",
+                   str(p[s]["steps"]), "--out", os.path.join(a.out_dir, f"{s}_head.pt")] + dev
         elif s == "rl":
             cmd = [sys.executable, "-m", "omnicoder.training.rl", "--preset", a.preset, "--steps", str(p[s]["steps"]),
                    "--out", os.path.join(a.out_dir, "rl.pt")] + dev

@@ -83,18 +83,23 @@ class FlowReconTrainer:
             y, _ = self.lm.hidden(ids)
         return y.view(ids.shape[0], ids.shape[1], -1)[:, -1]
 
-    def loss(self, images: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    def loss_and_estimate(self, z0: torch.Tensor, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Loss for target latents z0 given LM states h, and the head's estimate of z0: its output
+        (reconstruction) or x_t - t v_hat (flow: the clean latent the predicted velocity points to)."""
         from .multimodal_tasks import recon_loss
-        z0 = self.enc(images).to(ids.device)
-        h = self._state(ids)
         if not self.flow:
-            return recon_loss(self.head(h), z0, self.recon)
+            z_hat = self.head(h)
+            return recon_loss(z_hat, z0, self.recon), z_hat
         B = z0.shape[0]
         t = torch.sigmoid(torch.randn(B, device=z0.device))                    # logit-normal times
         eps = torch.randn_like(z0)
         x_t = (1 - t)[:, None, None] * z0 + t[:, None, None] * eps
         v = self.head(h, x_t, t)
-        return (_weight(t)[:, None, None] * (v - (eps - z0)) ** 2).mean()
+        loss = (_weight(t)[:, None, None] * (v - (eps - z0)) ** 2).mean()
+        return loss, x_t - t[:, None, None] * v
+
+    def loss(self, images: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+        return self.loss_and_estimate(self.enc(images).to(ids.device), self._state(ids))[0]
 
     def step(self, images: torch.Tensor, ids: torch.Tensor) -> float:
         loss = self.loss(images, ids)

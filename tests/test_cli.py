@@ -119,6 +119,12 @@ def test_run_training_smoke_one_step(tmp_path):
     summary = json.loads(out[out.rindex("{\n \"plan\""):])
     assert all(v["steps"] == 1 for v in summary["plan"].values())
     assert {k: v["rc"] for k, v in summary["results"].items()} == {"vqa": 0, "rl": 0}
+    # alignment chain: the concept-head stage picks up the pre-alignment checkpoint
+    out = _run(["omnicoder.tools.run_training", "--stages", "pre_align,align,audio_recon", "--out_dir",
+                str(tmp_path), "--smoke_one_step", "--device", "cpu"])
+    summary = json.loads(out[out.rindex("{\n \"plan\""):])
+    assert all(v["rc"] == 0 for v in summary["results"].values()), summary
+    assert (tmp_path / "pre_align.pt").exists() and (tmp_path / "concept_head.pt").exists()
 
 
 def test_verifier_distillation(tmp_path):

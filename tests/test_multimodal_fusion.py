@@ -167,3 +167,68 @@ def test_pre_align_infonce_aligns_text_and_media(tmp_path):
         last = tr.step(ids, image=imgs, audio=wav)
     assert last["image"] < 0.5 * first["image"] and last["audio"] < first["audio"]
     assert main(["--steps", "1", "--batch", "4", "--device", "cpu", "--out", str(tmp_path / "p.pt")]) == 0
+
+
+def test_audio_recon_trainer_learns_latents(tmp_path):
+    """Audio latent reconstruction with the spectral side losses: the loss falls on distinct tones
+    and the predicted latents approach the mel-pooled targets; the CLI runs one flow-mode step."""
+    from omnicoder.config import ModelConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.audio_recon import AudioReconTrainer, MelPoolEncoder, main, synthetic_tones
+    from omnicoder.training.flow_recon import LatentQueryHead
+    torch.manual_seed(0)
+    cfg = ModelConfig(name="ar", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64)
+    lm = build_model(cfg, "cpu", dtype=torch.float32, seed=0).eval()
+    enc = MelPoolEncoder(segments=2, channels=8)
+    waves, _ = synthetic_tones(3, samples=4000)
+    ids = torch.tensor([[5, 6, 7], [8, 9, 10], [11, 12, 13]])
+    z0 = enc(waves)
+    assert z0.shape == (3, 2, 8) and torch.equal(z0, MelPoolEncoder(segments=2, channels=8)(waves))
+    head = LatentQueryHead(64, 2, 8, width=64)
+    tr = AudioReconTrainer(lm, head, enc, lr=3e-3)
+    losses = [tr.step(waves, ids) for _ in range(200)]
+    assert sum(losses[-10:]) < 0.3 * sum(losses[:10]), (losses[:3], losses[-3:])
+    err = (tr.sample(ids) - z0).norm() / z0.norm()
+    assert err < 0.2, float(err)
+    assert main(["--steps", "1", "--batch", "2", "--flow_loss", "--device", "cpu", "--out",
+                 str(tmp_path / "a.pt")]) == 0
+
+
+def test_concept_align_retrieves_own_image(tmp_path):
+    """Concept-head alignment against a frozen pre-aligned teacher: InfoNCE + triplet terms fall and
+    most captions' concept embeddings end closest to their own image (the random teacher's text and
+    image embeddings of an item disagree, so the two InfoNCE terms pull against each other)."""
+    from omnicoder.config import ModelConfig
+    from omnicoder.models.heads import ConceptLatentHead
+    from omnicoder.models.lm import build_model
+    from omnicoder.multimodal.aligner import PreAligner
+    from omnicoder.training.concept_align import ConceptAligner, info_nce, main, triplet
+    from omnicoder.training.pre_align import TextEmbedder
+
+    class Flat(torch.nn.Module):
+        dim = 16
+
+        def __init__(self):
+            super().__init__()
+            self.lin = torch.nn.Linear(3, 16)
+
+        def forward(self, x):
+            return self.lin(x.mean((2, 3)))
+
+    a = torch.nn.functional.normalize(torch.randn(4, 8), dim=-1)
+    assert float(triplet(a, a, -a)) == 0.0 and float(triplet(a, -a, a)) > 2.0
+    assert float(info_nce(a * 10, a * 10)) < float(info_nce(a, a.roll(1, 0)))
+    torch.manual_seed(0)
+    cfg = ModelConfig(name="ca", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64)
+    lm = build_model(cfg, "cpu", dtype=torch.float32, seed=0).eval()
+    tr = ConceptAligner(lm, ConceptLatentHead(64, 16), TextEmbedder(300, 16), Flat(),
+                        PreAligner({"text": 16, "image": 16}, 16), lr=3e-3)
+    imgs = torch.rand(6, 3)[:, :, None, None].expand(-1, -1, 4, 4)
+    ids = torch.arange(1, 7)[:, None] * torch.tensor([[1, 7, 13]])
+    first = tr.step(imgs, ids)
+    for _ in range(150):
+        last = tr.step(imgs, ids)
+    assert last["loss"] < 0.5 * first["loss"]
+    assert tr.retrieval_accuracy(imgs, ids) >= 0.8
+    assert main(["--steps", "1", "--batch", "4", "--neg_text", "--device", "cpu", "--out",
+                 str(tmp_path / "c.pt")]) == 0
