@@ -104,8 +104,9 @@ def test_cuda_graph_training_step_matches_eager(cuda_ext):
         assert abs(a - b) < 2e-3 * abs(a), (le, lg)
 
     def dist(m1, m2):   # global relative distance of all weights
-        num = sum(float((p.float() - q.float()).pow(2).sum()) for p, q in zip(m1.parameters(), m2.parameters()))
-        den = sum(float(q.float().pow(2).sum()) for q in m2.parameters())
+        num = sum(float((p.detach().float() - q.detach().float()).pow(2).sum())
+                  for p, q in zip(m1.parameters(), m2.parameters()))
+        den = sum(float(q.detach().float().pow(2).sum()) for q in m2.parameters())
         return (num / den) ** 0.5
 
     # the MoE backward accumulates with atomics, so runs drift apart a little: Adam turns tiny

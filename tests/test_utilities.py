@@ -145,3 +145,25 @@ def test_gen_predictions(tmp_path):
     pred = [json.loads(ln) for ln in out.read_text().splitlines()]
     assert len(pred) == 2 and all("prediction" in p and p["answer"] == str(i) for i, p in enumerate(pred))
     assert os.path.getsize(out) > 0
+
+
+def test_teacher_verify_agreement(tmp_path):
+    from omnicoder.config import get_preset
+    from omnicoder.eval import teacher_verify as TV
+    from omnicoder.models.lm import build_model
+    assert TV.partial_ratio("abc", "xxABCxx") == 1.0 and TV.partial_ratio("", "a") == 0.0
+    assert 0.8 < TV.partial_ratio("hello world", "say hello wrld") < 1.0
+    assert TV.partial_ratio("abc", "xyz") == 0.0
+    model = build_model(get_preset("tiny_moe"), dtype=torch.float32, seed=0)
+    ck = tmp_path / "s.pt"
+    torch.save({"model": model.export_state_dict(), "config": model.cfg.to_dict()}, ck)
+    data = tmp_path / "d.jsonl"
+    data.write_text("\n".join(json.dumps(r) for r in [{"prompt": "def add(a, b):", "target": "return a + b"},
+                                                      {"question": "2 + 2 =", "answer": "4"}]) + "\n")
+    out = tmp_path / "tv.json"
+    assert TV.main(["--data", str(data), "--student_ckpt", str(ck), "--teachers", str(ck), "--max_new_tokens", "4",
+                    "--out", str(out), "--device", "cpu"]) == 0
+    r = json.loads(out.read_text())
+    # the same checkpoint as teacher decodes the same greedy tokens: full agreement
+    assert r["samples"] == 2 and r["teachers"][str(ck)]["agreement"] == 1.0
+    assert 0.0 <= r["overall"]["student_vs_target"] <= 1.0
