@@ -87,6 +87,16 @@ def cases(dev):
     bl = torch.full((Bs,), 8192, device=dev, dtype=torch.long)
     out["spec_verify (64 x 4 drafts, vocab 32000)"] = (lambda: C.spec_verify(lg, pd, dr, us, bl, 1.0),
                                                       lg.numel() * 4 + pd.numel() * 4)
+    # Gaussian splatting: 4 images of 256 x 256, 65536 Gaussians each, 11 x 11 footprint taps with depth;
+    # bytes = the Gaussians' parameters read once and the colour / depth images written once (the
+    # 158.6 M accumulator reductions stay in L2)
+    Bg, Ng, Hg, Wg, kg = 4, 65536, 256, 256, 11
+    gu, gv = torch.rand(Bg, Ng, device=dev) * Wg, torch.rand(Bg, Ng, device=dev) * Hg
+    gs = torch.rand(Bg, Ng, device=dev) * 1.5 + 0.5
+    go, gz = torch.rand(Bg, Ng, device=dev), torch.rand(Bg, Ng, device=dev) + 1.0
+    gc = torch.rand(Bg, Ng, 3, device=dev)
+    out["gsplat (4 x 65536 Gaussians, 11 x 11 taps, 256 x 256)"] = (
+        lambda: C.gsplat_forward(gu, gv, gs, gs, go, gc, gz, Hg, Wg, kg), Bg * Ng * 9 * 4 + Bg * 4 * Hg * Wg * 4)
     return out
 
 

@@ -155,7 +155,7 @@ void int4_dequant(const uint8_t* w, const float* scale, void* out, int N, int K,
 
 // ---- Gaussian splatting ------------------------------------------------------
 // Splat B*N projected Gaussians (u, v, sx, sy, opacity, rgb [.., 3], depth z or
-// nullptr) with a k x k footprint; acc [B, 5, H, W] fp32 scratch; writes
+// nullptr) with a k x k footprint; acc: 5 * B * H * W fp32 scratch, 16-byte aligned; writes
 // out_rgb [B, 3, H, W] and out_depth [B, 1, H, W] (when z != nullptr).
 void gsplat_forward(const float* u, const float* v, const float* sx, const float* sy, const float* opa,
                     const float* rgb, const float* z, float* acc, float* out_rgb, float* out_depth, int B, int N,

@@ -81,9 +81,15 @@ class Heartbeat:
             self._thread.join(timeout=2 * self.interval + 1)
             self._thread = None
 
-    def leave(self, reason: str = "left"):
+    def leave(self, reason: str = "left") -> bool:
+        """Stop beating and announce the departure; False when the store no longer answers (the
+        store host, rank 0, is gone), so a caller unwinding from an error keeps its own exception."""
         self.stop()
-        self.store.set(f"{self.prefix}/left/{self.rank}", reason)
+        try:
+            self.store.set(f"{self.prefix}/left/{self.rank}", reason)
+            return True
+        except (RuntimeError, ConnectionError, OSError):
+            return False
 
     # -- checking ------------------------------------------------------------
     def _read(self, r: int):

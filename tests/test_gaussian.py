@@ -75,3 +75,28 @@ def test_cuda_kernel_matches_cpu():
         args = [x.cuda() for x in (pos, cd, rgb, opa, K, R, t)]
         out_rgb, out_d = GaussianSplatRenderer3D(11)(args[0], None, *args[1:], (96, 128))
     assert torch.allclose(out_rgb.cpu(), ref_rgb, atol=1e-4) and torch.allclose(out_d.cpu(), ref_d, atol=1e-3)
+
+
+@pytest.mark.gpu
+def test_cuda_kernel_edge_cases():
+    """Footprints of 1 and 3 taps, Gaussians partly or wholly outside a small odd-sized image, scales
+    below one pixel (several taps on one pixel), one image without depth, a Gaussian count that is not
+    a multiple of the warps per block: the CUDA splat against the CPU formulation."""
+    from omnicoder.models.gaussian import splat, splat_torch
+    g = torch.Generator().manual_seed(3)
+    B, N, H, W = 3, 37, 7, 9
+    u = torch.rand(B, N, generator=g) * 13 - 2
+    v = torch.rand(B, N, generator=g) * 11 - 2
+    sx = torch.rand(B, N, generator=g) * 1.8 + 0.2
+    sy = torch.rand(B, N, generator=g) * 1.8 + 0.2
+    opa = torch.rand(B, N, generator=g)
+    rgb = torch.rand(B, N, 3, generator=g)
+    z = torch.rand(B, N, generator=g) + 0.5
+    for k in (1, 3, 5):
+        for zz in (z, None):
+            ref = splat_torch(u, v, sx, sy, opa, rgb, zz, H, W, k)
+            with torch.no_grad():
+                got = splat(*(t.cuda() for t in (u, v, sx, sy, opa, rgb)), None if zz is None else zz.cuda(), H, W, k)
+            assert torch.allclose(got[0].cpu(), ref[0], atol=1e-4), k
+            if zz is not None:
+                assert torch.allclose(got[1].cpu(), ref[1], atol=1e-4), k

@@ -52,7 +52,7 @@ def _batch(step):
     return torch.randn(4, 8, generator=g), torch.randn(4, 4, generator=g)
 
 
-def _worker(rank, world, port, fault, use_heartbeat, tmp, q):
+def _worker(rank, world, port, fault, use_heartbeat, tmp, q, release):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
     from omnicoder.parallel.health import FaultInjector, FaultSpec, Heartbeat, RankFailure
@@ -70,14 +70,17 @@ def _worker(rank, world, port, fault, use_heartbeat, tmp, q):
         q.put((rank, type(e).__name__, str(e)[:200], time.monotonic() - t0))
     q.close()
     q.join_thread()   # flush the result before leaving
+    if rank == 0:     # rank 0 hosts the store: keep it up until every surviving rank has reported
+        release.wait(timeout=30)
     os._exit(0)       # no destroy_process_group: peers may be gone
 
 
 def _run(world, fault, use_heartbeat, tmp_path, expect_exit=()):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
+    release = ctx.Event()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, fault, use_heartbeat, str(tmp_path), q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, fault, use_heartbeat, str(tmp_path), q, release))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -87,6 +90,7 @@ def _run(world, fault, use_heartbeat, tmp_path, expect_exit=()):
             rank, kind, info, secs = q.get(timeout=60)
             out[rank] = (kind, info, secs)
     finally:
+        release.set()
         for p in procs:
             p.join(timeout=5)
             if p.is_alive():      # the hung / stalled rank: our own child process
@@ -249,3 +253,16 @@ def test_async_checkpoint_is_a_consistent_snapshot(tmp_path):
         mgr.save_async(s, t.model, t)
     mgr.wait()
     assert mgr.steps() == [4, 5]
+
+
+def test_leave_survives_a_dead_store():
+    """A rank unwinding from a RankFailure after the store host is gone keeps its own exception:
+    leave() reports False instead of raising the store's network error."""
+    from omnicoder.parallel.health import Heartbeat
+
+    class DeadStore:
+        def set(self, key, value):
+            raise dist.DistNetworkError("Broken pipe")
+
+    hb = Heartbeat(store=DeadStore(), rank=1, world=3, interval=0.1, timeout=1.0)
+    assert hb.leave("RankFailure: rank 2") is False
