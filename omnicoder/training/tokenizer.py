@@ -46,6 +46,12 @@ def get_tokenizer(vocab_size: int = 32000, path: str | None = None):
     if path and os.path.isdir(path):
         try:
             return HFTokenizer(path)
-        except Exception:
-            pass
+        except Exception as e:   # a broken tokenizer directory: say so, then use the byte tokenizer
+            import warnings
+            warnings.warn(f"tokenizer at {path} could not be loaded ({type(e).__name__}: {e}); "
+                          f"using the byte tokenizer instead", RuntimeWarning, stacklevel=2)
+    elif path:
+        import warnings
+        warnings.warn(f"tokenizer directory {path} does not exist; using the byte tokenizer", RuntimeWarning,
+                      stacklevel=2)
     return ByteTokenizer(vocab_size)

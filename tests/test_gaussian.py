@@ -84,19 +84,22 @@ def test_cuda_kernel_edge_cases():
     a multiple of the warps per block: the CUDA splat against the CPU formulation."""
     from omnicoder.models.gaussian import splat, splat_torch
     g = torch.Generator().manual_seed(3)
-    B, N, H, W = 3, 37, 7, 9
-    u = torch.rand(B, N, generator=g) * 13 - 2
-    v = torch.rand(B, N, generator=g) * 11 - 2
-    sx = torch.rand(B, N, generator=g) * 1.8 + 0.2
-    sy = torch.rand(B, N, generator=g) * 1.8 + 0.2
-    opa = torch.rand(B, N, generator=g)
-    rgb = torch.rand(B, N, 3, generator=g)
-    z = torch.rand(B, N, generator=g) + 0.5
-    for k in (1, 3, 5):
-        for zz in (z, None):
-            ref = splat_torch(u, v, sx, sy, opa, rgb, zz, H, W, k)
-            with torch.no_grad():
-                got = splat(*(t.cuda() for t in (u, v, sx, sy, opa, rgb)), None if zz is None else zz.cuda(), H, W, k)
-            assert torch.allclose(got[0].cpu(), ref[0], atol=1e-4), k
-            if zz is not None:
-                assert torch.allclose(got[1].cpu(), ref[1], atol=1e-4), k
+    # one partial tile with small footprints; then 3 x 4 tiles (partial at the edges) with footprints
+    # up to ~100 pixels crossing many tiles, negative scales included
+    for B, N, H, W, smin, smax, ks in ((3, 37, 7, 9, 0.2, 2.0, (1, 3, 5)), (2, 300, 70, 100, -8.0, 8.0, (3, 11))):
+        u = torch.rand(B, N, generator=g) * (W + 4) - 2
+        v = torch.rand(B, N, generator=g) * (H + 4) - 2
+        sx = torch.rand(B, N, generator=g) * (smax - smin) + smin
+        sy = torch.rand(B, N, generator=g) * (smax - smin) + smin
+        opa = torch.rand(B, N, generator=g)
+        rgb = torch.rand(B, N, 3, generator=g)
+        z = torch.rand(B, N, generator=g) + 0.5
+        for k in ks:
+            for zz in (z, None):
+                ref = splat_torch(u, v, sx, sy, opa, rgb, zz, H, W, k)
+                with torch.no_grad():
+                    got = splat(*(t.cuda() for t in (u, v, sx, sy, opa, rgb)), None if zz is None else zz.cuda(),
+                                H, W, k)
+                assert torch.allclose(got[0].cpu(), ref[0], atol=1e-4), (H, W, k)
+                if zz is not None:
+                    assert torch.allclose(got[1].cpu(), ref[1], atol=1e-4), (H, W, k)
