@@ -20,6 +20,8 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
   env-audit         environment variables the package reads, documented-vs-used drift and the
                     set-but-unknown ones                                   (env_audit.py:1-92)
   gen-predictions   add a `prediction` to every row of a VQA / caption JSONL (gen_predictions.py)
+  latent-refine     run a latent refiner checkpoint over a .npy of continuous image / audio latents
+                                                                  (inference/mixed_latent_refine.py)
 
 Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
 could not be read.
@@ -588,6 +590,35 @@ def _cmd_gen_predictions(a) -> int:
     return 0
 
 
+# ---- latent-refine -------------------------------------------------------------
+def latent_refine(latents, state: dict | None = None, hidden_mult: int = 2, temporal: bool = False):
+    """[B, D] or [B, T, D] latents (numpy or tensor) through a LatentRefiner (weights from `state`,
+    a state_dict, or the identity-initialised refiner when None); returns a float32 numpy array."""
+    import numpy as np
+    from ..multimodal.video import LatentRefiner
+    x = torch.as_tensor(np.asarray(latents, dtype=np.float32))
+    ref = LatentRefiner(x.shape[-1], hidden_mult=hidden_mult, temporal=temporal)
+    if state is not None:
+        ref.load_state_dict(state)
+    else:                                 # no checkpoint: the residual branch off, latents pass through
+        with torch.no_grad():
+            ref.gate.zero_()
+    with torch.no_grad():
+        return ref.eval()(x).numpy()
+
+
+def _cmd_latent_refine(a) -> int:
+    import numpy as np
+    state = None
+    if a.ckpt:
+        obj = torch.load(a.ckpt, map_location="cpu", weights_only=True)
+        state = obj.get("refiner", obj) if isinstance(obj, dict) else obj
+    out = latent_refine(np.load(a.latents), state, a.hidden_mult, a.temporal)
+    np.save(a.out_latents, out)
+    print(json.dumps({"in": a.latents, "out": a.out_latents, "shape": list(out.shape)}))
+    return 0
+
+
 # ---- command line ---------------------------------------------------------------
 def _parser() -> argparse.ArgumentParser:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -693,6 +724,14 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--limit", type=int, default=0)
     p.add_argument("--device", default=dev)
     p.set_defaults(fn=_cmd_gen_predictions)
+
+    p = sub.add_parser("latent-refine", help="refine continuous latents saved as .npy")
+    p.add_argument("--latents", required=True)
+    p.add_argument("--out_latents", required=True)
+    p.add_argument("--ckpt", default="", help="refiner state_dict (or a dict with a 'refiner' entry)")
+    p.add_argument("--hidden_mult", type=int, default=2)
+    p.add_argument("--temporal", action="store_true")
+    p.set_defaults(fn=_cmd_latent_refine)
     return ap
 
 

@@ -464,3 +464,26 @@ def test_scmoe_contrast_decoding():
     assert all(b.ffn.top_k_override is None for b in m.blocks)      # restored after decoding
     with pytest.raises(ValueError):
         generate(m, ids, 2, scmoe_alpha=1.0, adaptive_moe=True)
+
+
+def test_tool_fabric():
+    from omnicoder.inference.tool_fabric import (analyze_inputs, combine_verifier_signals, invoke_tools_in_text,
+                                                 media_paths)
+    out = invoke_tools_in_text("sum: <tool>calc(2 + 3 * 4)</tool> done")
+    assert "<result>14</result>" in out
+    assert abs(combine_verifier_signals({"text": 1.0, "code": 0.0}, {"text": 3.0}) - 0.75) < 1e-9
+    assert media_paths('look at "cat.png" and (talk.wav), not notes.txt') == ["cat.png", "talk.wav"]
+
+    def detect(p):
+        return ["cat", "sofa"]
+
+    def transcribe(p):
+        raise OSError("no such file")
+
+    ctx, state, errors = analyze_inputs("is the cat.png on a sofa? listen: talk.wav clip.mp4", detect=detect,
+                                        transcribe=transcribe)
+    assert state.facts == ["cat present_in image cat.png", "sofa present_in image cat.png"]
+    assert "FACT cat present_in image cat.png" in ctx
+    assert len(errors) == 1 and "talk.wav" in errors[0] and "OSError" in errors[0]
+    ctx, state, _ = analyze_inputs("cat.png", modes="audio", detect=detect)
+    assert state.facts == [] and ctx == ""

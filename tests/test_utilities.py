@@ -167,3 +167,22 @@ def test_teacher_verify_agreement(tmp_path):
     # the same checkpoint as teacher decodes the same greedy tokens: full agreement
     assert r["samples"] == 2 and r["teachers"][str(ck)]["agreement"] == 1.0
     assert 0.0 <= r["overall"]["student_vs_target"] <= 1.0
+
+
+def test_latent_refine(tmp_path):
+    import numpy as np
+    from omnicoder.multimodal.video import LatentRefiner
+    x = np.random.default_rng(0).standard_normal((2, 5, 16)).astype(np.float32)
+    inp, out = tmp_path / "z.npy", tmp_path / "r.npy"
+    np.save(inp, x)
+    # no checkpoint: the latents pass through unchanged
+    assert _cli(["latent-refine", "--latents", str(inp), "--out_latents", str(out)]) == 0
+    assert np.allclose(np.load(out), x)
+    torch.manual_seed(0)
+    ref = LatentRefiner(16, temporal=True)
+    torch.save({"refiner": ref.state_dict()}, tmp_path / "ref.pt")
+    assert _cli(["latent-refine", "--latents", str(inp), "--out_latents", str(out), "--ckpt",
+                 str(tmp_path / "ref.pt"), "--temporal"]) == 0
+    with torch.no_grad():
+        want = ref(torch.from_numpy(x)).numpy()
+    assert np.allclose(np.load(out), want, atol=1e-6)
