@@ -84,8 +84,10 @@ class VLTaskTrainer:
                 p.requires_grad_(False)
         self.opt = torch.optim.AdamW([p for p in params if p.requires_grad], lr=lr)
 
-    def build(self, media: torch.Tensor, prompts: list[str], targets: list[str]) -> VLBatch:
-        """Compose one batch (prompt / target pairs padded to the longest with ignored positions)."""
+    def build(self, media, prompts: list[str], targets: list[str]) -> VLBatch:
+        """Compose one batch (prompt / target pairs padded to the longest with ignored positions).
+        `media`: a tensor of the task's modality, or {modality: tensor} for any subset of image,
+        video and audio (empty for text-only rows)."""
         dev = self.lm.embed.device
         seqs, masks = [], []
         for p, t in zip(prompts, targets):
@@ -101,12 +103,14 @@ class VLTaskTrainer:
             train[b, :len(s)] = torch.tensor(m)
         ids, train = ids.to(dev), train.to(dev)
         text_emb = self.lm.embed[ids]
-        emb, seg = self.composer.fuse_all(text_emb, **{self.modality: media.to(dev)})
+        kw = media if isinstance(media, dict) else {self.modality: media}
+        emb, seg = self.composer.fuse_all(text_emb, **{k: v.to(dev) for k, v in kw.items() if v is not None})
         n_pre = emb.shape[1] - T                     # modality tokens + markers in front of the text
         labels = torch.full(emb.shape[:2], -100, dtype=torch.long, device=dev)
-        # position n_pre - 1 + j predicts text token j
+        # position n_pre - 1 + j predicts text token j (without media, token 0 has no predictor)
         tgt = torch.where(train, ids, torch.full_like(ids, -100))
-        labels[:, n_pre - 1:n_pre - 1 + T] = tgt
+        first = 1 if n_pre == 0 else 0
+        labels[:, n_pre - 1 + first:n_pre - 1 + T] = tgt[:, first:]
         return VLBatch(emb, labels)
 
     def step(self, media: torch.Tensor, prompts: list[str], targets: list[str]) -> float:
@@ -139,6 +143,45 @@ class VLTaskTrainer:
         return self.tok.decode(out)
 
 
+_PROMPTS = (("question", "Question: {question} Answer:", "answer"), ("caption", "Caption:", "caption"),
+            ("transcript", "Transcript:", "transcript"), ("text", "", "text"))
+
+
+def unified_example(row: dict, image_size: int = 224) -> dict:
+    """A mixed-corpus row (the reference's unified multimodal trainer, src/omnicoder/training/
+    unified_multimodal_train.py:44-120: any subset of image / video / audio paths with a question +
+    answer, a caption, a transcript or plain text) -> {"media": {modality: tensor}, "prompt", "target"}.
+    The target is the first of answer (with its question), caption, transcript, text present."""
+    media = {m: load_media(row[m], image_size) for m in ("image", "video", "audio") if isinstance(row.get(m), str)}
+    for key, template, tkey in _PROMPTS:
+        if row.get(tkey) and (key != "question" or row.get("question")):
+            return {"media": media, "prompt": template.format(**row), "target": str(row[tkey])}
+    raise ValueError(f"row has no target (answer, caption, transcript or text): {sorted(row)}")
+
+
+class UnifiedMMTrainer(VLTaskTrainer):
+    """One model over mixed rows: each batch holds rows with the same set of modalities (so their
+    features stack), and the cross entropy counts the target text only."""
+
+    def __init__(self, lm, composer, tokenizer, lr: float = 1e-4, train_lm: bool = True, loss_on_prompt: bool = False):
+        super().__init__(lm, composer, tokenizer, "vl_pretrain", lr, train_lm, loss_on_prompt)
+
+    def fit_mixed(self, rows: list[dict], steps: int, batch: int = 4) -> list[dict]:
+        groups: dict = {}
+        for r in rows:
+            groups.setdefault(tuple(sorted(r["media"])), []).append(r)
+        keys = sorted(groups)
+        log = []
+        for i in range(steps):
+            key = keys[i % len(keys)]
+            g = groups[key]
+            chunk = [g[(i // len(keys) * batch + j) % len(g)] for j in range(min(batch, len(g)))]
+            media = {m: torch.stack([r["media"][m] for r in chunk]) for m in key}
+            loss = self.step(media, [r["prompt"] for r in chunk], [r["target"] for r in chunk])
+            log.append({"modalities": "+".join(key) or "text", "loss": loss})
+        return log
+
+
 def synthetic_rows(task: str, n: int, image_size: int = 64, seed: int = 0) -> list[dict]:
     """Rows of random media with templated questions / targets (wiring and throughput runs)."""
     g = torch.Generator().manual_seed(seed)
@@ -166,7 +209,8 @@ def main(argv=None):
     from ..multimodal.video import VideoEncoder
     from .tokenizer import get_tokenizer
     ap = argparse.ArgumentParser(description="vision / audio / video - language task training")
-    ap.add_argument("--task", default="vqa", choices=sorted(TASKS))
+    ap.add_argument("--task", default="vqa", choices=sorted(TASKS) + ["unified"],
+                    help="unified: mixed rows with any subset of image / video / audio and a text target")
     ap.add_argument("--jsonl", default="", help="task rows (default: synthetic rows)")
     ap.add_argument("--preset", default="tiny_moe")
     ap.add_argument("--vision", default="vit_tiny")
@@ -183,9 +227,21 @@ def main(argv=None):
     comp = FusionComposer(D, vision=VisionBackbone(a.vision, image_size=a.image_size, depth=2),
                           video=VideoEncoder(image_size=a.image_size, dim=192, depth=1, heads=3),
                           audio=MelFrontend(out_dim=D)).to(dev)
-    tr = VLTaskTrainer(lm, comp, get_tokenizer(lm.cfg.vocab_size), a.task, lr=a.lr)
-    rows = read_task_jsonl(a.jsonl, a.task) if a.jsonl else synthetic_rows(a.task, 4 * a.batch, a.image_size)
-    losses = tr.fit(rows, a.steps, a.batch)
+    tok = get_tokenizer(lm.cfg.vocab_size)
+    if a.task == "unified":
+        tr = UnifiedMMTrainer(lm, comp, tok, lr=a.lr)
+        if a.jsonl:
+            with open(a.jsonl) as f:
+                rows = [unified_example(json.loads(ln), a.image_size) for ln in f if ln.strip()]
+        else:
+            rows = [dict(r, media={TASKS[t][0]: r["media"]}) for t in ("vqa", "asr", "video_qa")
+                    for r in synthetic_rows(t, 2 * a.batch, a.image_size)]
+            rows += [{"media": {}, "prompt": "", "target": f"plain text row {i}"} for i in range(a.batch)]
+        losses = [e["loss"] for e in tr.fit_mixed(rows, a.steps, a.batch)]
+    else:
+        tr = VLTaskTrainer(lm, comp, tok, a.task, lr=a.lr)
+        rows = read_task_jsonl(a.jsonl, a.task) if a.jsonl else synthetic_rows(a.task, 4 * a.batch, a.image_size)
+        losses = tr.fit(rows, a.steps, a.batch)
     torch.save({"model": lm.export_state_dict(), "composer": comp.state_dict(), "config": lm.cfg.to_dict()}, a.out)
     print(json.dumps({"task": a.task, "steps": a.steps, "first_loss": losses[0], "last_loss": losses[-1],
                       "out": a.out}))

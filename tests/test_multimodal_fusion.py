@@ -232,3 +232,44 @@ def test_concept_align_retrieves_own_image(tmp_path):
     assert tr.retrieval_accuracy(imgs, ids) >= 0.8
     assert main(["--steps", "1", "--batch", "4", "--neg_text", "--device", "cpu", "--out",
                  str(tmp_path / "c.pt")]) == 0
+
+
+def test_unified_mixed_trainer(tmp_path):
+    """Mixed rows (image + question, audio + transcript, image + audio + caption, plain text): each
+    batch has one modality set, the text-only labels line up with the next token, the loss falls."""
+    import json
+
+    from omnicoder.config import AttentionConfig, ModelConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.tokenizer import get_tokenizer
+    from omnicoder.training.vl_tasks import UnifiedMMTrainer, main, unified_example
+    torch.manual_seed(0)
+    cfg = ModelConfig(name="um", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=128,
+                      attn=AttentionConfig(kind="gqa", n_kv_heads=2))
+    lm = build_model(cfg, device="cpu", seed=0)
+    tok = get_tokenizer(cfg.vocab_size)
+    fc = FusionComposer(64, vision=VisionBackbone("vit_tiny", image_size=32, patch=16, depth=1),
+                        audio=MelFrontend(out_dim=32))
+    torch.save(torch.randn(3, 32, 32), tmp_path / "i.pt")
+    torch.save(torch.randn(1600), tmp_path / "a.pt")
+    raw = [{"image": str(tmp_path / "i.pt"), "question": "what?", "answer": "a dog"},
+           {"audio": str(tmp_path / "a.pt"), "transcript": "hello"},
+           {"image": str(tmp_path / "i.pt"), "audio": str(tmp_path / "a.pt"), "caption": "a barking dog"},
+           {"text": "just text"}]
+    rows = [unified_example(r, 32) for r in raw]
+    assert rows[0]["prompt"] == "Question: what? Answer:" and rows[1]["prompt"] == "Transcript:"
+    assert sorted(rows[2]["media"]) == ["audio", "image"] and rows[3]["media"] == {}
+    with pytest.raises(ValueError):
+        unified_example({"image": str(tmp_path / "i.pt")}, 32)
+    tr = UnifiedMMTrainer(lm, fc, tok, lr=3e-3)
+    b = tr.build({}, [""], ["just text"])                 # text only: position j - 1 predicts token j
+    ids = tok.encode("just text") + [tok.eos_id]
+    assert b.labels[0, :len(ids) - 1].tolist() == ids[1:] and (b.labels[0, len(ids) - 1:] == -100).all()
+    log = tr.fit_mixed(rows, steps=40, batch=2)
+    assert {e["modalities"] for e in log} == {"image", "audio", "audio+image", "text"}
+    for m in ("image", "text"):
+        ls = [e["loss"] for e in log if e["modalities"] == m]
+        assert ls[-1] < 0.5 * ls[0], (m, ls)
+    (tmp_path / "u.jsonl").write_text("\n".join(json.dumps(r) for r in raw) + "\n")
+    assert main(["--task", "unified", "--jsonl", str(tmp_path / "u.jsonl"), "--image_size", "32", "--steps", "2",
+                 "--batch", "2", "--device", "cpu", "--out", str(tmp_path / "u.pt")]) == 0
