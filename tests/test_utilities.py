@@ -186,3 +186,27 @@ def test_latent_refine(tmp_path):
     with torch.no_grad():
         want = ref(torch.from_numpy(x)).numpy()
     assert np.allclose(np.load(out), want, atol=1e-6)
+
+
+def test_cycle_consistency(tmp_path):
+    from omnicoder.eval.cycle_consistency import cycle_records, main
+    d = tmp_path / "gen"
+    d.mkdir()
+    torch.save(torch.rand(3, 32, 32) * 2 - 1, d / "a.pt")
+    torch.save(torch.rand(3, 32, 32) * 2 - 1, d / "b.pt")
+    (d / "speech.wav").write_bytes(b"RIFF")
+    (d / "notes.md").write_text("ignored")
+    (d / "prompts.jsonl").write_text(json.dumps({"file": "a.pt", "prompt": "a red square"}) + "\n")
+    (d / "b.txt").write_text("a blue circle")
+    (d / "speech.txt").write_text("hello world")
+    caps = {"a.pt": "a red square on white", "b.pt": "a green triangle"}
+    recs, summary = cycle_records(str(d), caption=lambda p: caps[os.path.basename(p)],
+                                  transcribe=lambda p: "hello world")
+    by = {os.path.basename(r["file"]): r for r in recs}
+    assert set(by) == {"a.pt", "b.pt", "speech.wav"}
+    assert by["a.pt"]["agreement"] == 1.0 and by["b.pt"]["agreement"] < 0.7
+    assert by["speech.wav"]["agreement"] == 1.0 and summary["audio"]["files"] == 1
+    assert summary["image"]["mean_agreement"] == (1.0 + by["b.pt"]["agreement"]) / 2
+    out = tmp_path / "cc.jsonl"
+    assert main(["--media_dir", str(d), "--image_size", "32", "--out", str(out)]) == 0
+    assert len(out.read_text().splitlines()) == 3
