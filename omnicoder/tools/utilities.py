@@ -22,6 +22,10 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
   gen-predictions   add a `prediction` to every row of a VQA / caption JSONL (gen_predictions.py)
   latent-refine     run a latent refiner checkpoint over a .npy of continuous image / audio latents
                                                                   (inference/mixed_latent_refine.py)
+  act-calibrate     per-channel activation maxima of the GEMM inputs over sample prompts (prefill +
+                    a few cached decode steps) and the static int8 scales they imply (act_calibrate.py)
+  act-validate      check a calibration file (finite, positive scales) or print the effective knobs of
+                    an activation-quantisation policy sidecar                 (validate_act_quant.py)
 
 Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
 could not be read.
@@ -619,6 +623,103 @@ def _cmd_latent_refine(a) -> int:
     return 0
 
 
+# ---- act-calibrate / act-validate ----------------------------------------------
+_ACT_MODULES = ("Norm", "LayerNorm", "Linear")     # outputs that are GEMM inputs (spec Norm; compat Linear)
+
+
+@torch.no_grad()
+def collect_activation_scales(model, prompts: list[list[int]], decode_steps: int = 8) -> dict:
+    """{module name: per-channel max |activation| over the prompts} for the modules whose outputs
+    feed the projections: RMSNorm / LayerNorm outputs of this package's model, Linear / LayerNorm
+    outputs of the reference-layout model.  Each prompt runs a prefill and `decode_steps` greedy
+    cached steps, so the decode path's activations count too."""
+    stats: dict = {}
+
+    def hook(name):
+        def fn(_m, _inp, out):
+            t = out if isinstance(out, torch.Tensor) else (out[0] if isinstance(out, (tuple, list)) else None)
+            if not isinstance(t, torch.Tensor) or t.dim() == 0:
+                return
+            m = t.detach().float().abs().reshape(-1, t.shape[-1]).amax(0).cpu()
+            stats[name] = torch.maximum(stats[name], m) if name in stats else m
+        return fn
+
+    hs = [m.register_forward_hook(hook(n)) for n, m in model.named_modules() if type(m).__name__ in _ACT_MODULES]
+    dev = next(model.parameters()).device
+    try:
+        for ids in prompts:
+            x = torch.tensor([ids], dtype=torch.long, device=dev)
+            if hasattr(model, "forward_cached"):
+                from ..inference.kv_cache import KVCache
+                cache = KVCache(model.cfg, 1, len(ids) + decode_steps + 1, dev)
+                nxt = model.forward_cached(x, cache, prefill=True, last_only=True)[:, -1].argmax(-1, keepdim=True)
+                for _ in range(decode_steps):
+                    nxt = model.forward_cached(nxt, cache, last_only=True)[:, -1].argmax(-1, keepdim=True)
+            else:                                           # reference layout: prefill, then its decode path
+                model(x)
+                nxt, kv = model.decode_next_id(x)
+                for _ in range(decode_steps):
+                    nxt, kv = model.decode_next_id(nxt, kv)
+    finally:
+        for h in hs:
+            h.remove()
+    return stats
+
+
+def _cmd_act_calibrate(a) -> int:
+    from ..config import get_preset
+    from ..inference.builders import load_model
+    from ..models.lm import build_model
+    from ..training.tokenizer import get_tokenizer
+    dev = torch.device(a.device)
+    model = (load_model(a.ckpt, dev, dtype=torch.float32)[0] if a.ckpt else
+             build_model(get_preset(a.preset), device=dev, dtype=torch.float32, seed=0)).eval()
+    tok = get_tokenizer(model.cfg.vocab_size)
+    ids = [tok.encode(p)[:a.max_tokens] or [1] for p in (a.prompts or _SAMPLE_PROMPTS)]
+    st = collect_activation_scales(model, ids, a.decode_steps)
+    out = {"prompts": len(ids), "decode_steps": a.decode_steps,
+           "modules": {k: {"absmax": v.tolist(), "int8_scale": (v.clamp_min(1e-8) / 127.0).tolist()}
+                       for k, v in st.items()}}
+    _write_json(a.out, out)
+    print(json.dumps({"modules": len(st), "out": a.out,
+                      "max_absmax": max((float(v.max()) for v in st.values()), default=0.0)}))
+    return 0
+
+
+def act_validate(obj: dict, layers: int = 0) -> dict:
+    """A calibration file: every module's scales finite and positive, channel counts per module.
+    A policy sidecar (the reference's *.act_quant.json: conf_floor, min_bits, max_bits, thresholds
+    with layer_conf_floor or per-layer entries): the effective global and per-layer knobs."""
+    import math
+    if "modules" in obj:
+        bad = [k for k, v in obj["modules"].items()
+               if not v.get("int8_scale") or not all(math.isfinite(x) and x > 0 for x in v["int8_scale"])]
+        return {"kind": "calibration", "modules": len(obj["modules"]), "bad": bad, "ok": not bad,
+                "channels": sorted({len(v["int8_scale"]) for v in obj["modules"].values()})}
+    floor = float(obj.get("conf_floor", 0.3))
+    th = obj.get("thresholds", {}) if isinstance(obj.get("thresholds", {}), dict) else {}
+    per = []
+    if isinstance(th.get("layer_conf_floor"), (list, tuple)):
+        per = [float(x) for x in th["layer_conf_floor"]]
+    elif isinstance(th.get("layers"), dict):
+        per = [float(v.get("conf_floor", floor)) for _, v in sorted((int(k), v) for k, v in th["layers"].items())]
+    return {"kind": "policy", "ok": True,
+            "global": {"conf_floor": floor, "min_bits": int(obj.get("min_bits", 8)),
+                       "max_bits": int(obj.get("max_bits", 2))},
+            "per_layer_conf_floor": per[:layers] if layers else per}
+
+
+def _cmd_act_validate(a) -> int:
+    try:
+        obj = _read_json(a.policy)
+    except (OSError, ValueError) as e:
+        print(json.dumps({"error": str(e)}))
+        return 3
+    r = act_validate(obj, a.layers)
+    print(json.dumps(r))
+    return 0 if r["ok"] else 2
+
+
 # ---- command line ---------------------------------------------------------------
 def _parser() -> argparse.ArgumentParser:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -732,6 +833,21 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--hidden_mult", type=int, default=2)
     p.add_argument("--temporal", action="store_true")
     p.set_defaults(fn=_cmd_latent_refine)
+
+    p = sub.add_parser("act-calibrate", help="activation maxima of the GEMM inputs and static int8 scales")
+    p.add_argument("--preset", default="tiny_moe")
+    p.add_argument("--ckpt", default="")
+    p.add_argument("--prompts", nargs="*", default=None)
+    p.add_argument("--max_tokens", type=int, default=256)
+    p.add_argument("--decode_steps", type=int, default=8)
+    p.add_argument("--out", default="weights/act_scales.json")
+    p.add_argument("--device", default="cpu")
+    p.set_defaults(fn=_cmd_act_calibrate)
+
+    p = sub.add_parser("act-validate", help="check a calibration file or print a policy's knobs")
+    p.add_argument("--policy", required=True)
+    p.add_argument("--layers", type=int, default=0)
+    p.set_defaults(fn=_cmd_act_validate)
     return ap
 
 

@@ -210,3 +210,32 @@ def test_cycle_consistency(tmp_path):
     out = tmp_path / "cc.jsonl"
     assert main(["--media_dir", str(d), "--image_size", "32", "--out", str(out)]) == 0
     assert len(out.read_text().splitlines()) == 3
+
+
+def test_act_calibrate_and_validate(tmp_path):
+    from omnicoder.models.compat import OmniTransformer
+    out = tmp_path / "act.json"
+    assert _cli(["act-calibrate", "--preset", "tiny_moe", "--max_tokens", "8", "--decode_steps", "2", "--out",
+                 str(out)]) == 0
+    d = json.loads(out.read_text())
+    from omnicoder.config import get_preset
+    cfg = get_preset("tiny_moe")
+    # every block's two norms (and the final norm) are GEMM inputs of d_model channels
+    assert len(d["modules"]) >= 2 * cfg.n_layers and all(len(v["absmax"]) == cfg.d_model
+                                                         for k, v in d["modules"].items() if "norm" in k)
+    assert _cli(["act-validate", "--policy", str(out)]) == 0
+    d["modules"][next(iter(d["modules"]))]["int8_scale"][0] = float("nan")
+    (tmp_path / "bad.json").write_text(json.dumps(d))
+    assert _cli(["act-validate", "--policy", str(tmp_path / "bad.json")]) == 2
+    # the reference-layout model: Linear / LayerNorm outputs through its own decode path
+    torch.manual_seed(0)
+    m = OmniTransformer(vocab_size=128, n_layers=1, d_model=32, n_heads=4, mlp_dim=64, n_experts=2, top_k=1,
+                        kv_latent_dim=16, use_hrm=False).eval()
+    st = U.collect_activation_scales(m, [[1, 2, 3]], decode_steps=2)
+    assert any(k.endswith("lm_head") for k in st) and all(torch.isfinite(v).all() for v in st.values())
+    # policy sidecar in the reference's form
+    pol = tmp_path / "p.act_quant.json"
+    pol.write_text(json.dumps({"conf_floor": 0.4, "min_bits": 8, "max_bits": 4,
+                               "thresholds": {"layers": {"1": {"conf_floor": 0.5}, "0": {}}}}))
+    r = U.act_validate(json.loads(pol.read_text()))
+    assert r["global"] == {"conf_floor": 0.4, "min_bits": 8, "max_bits": 4} and r["per_layer_conf_floor"] == [0.4, 0.5]
