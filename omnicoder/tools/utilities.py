@@ -26,6 +26,10 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
                     a few cached decode steps) and the static int8 scales they imply (act_calibrate.py)
   act-validate      check a calibration file (finite, positive scales) or print the effective knobs of
                     an activation-quantisation policy sidecar                 (validate_act_quant.py)
+  kv-dump           the KV-cache rows of sample prompts, one .pt per prompt        (kv_dump.py)
+  kv-autoencoder    a linear autoencoder of the dumped rows (closed-form PCA or AdamW) and its
+                    sidecar                                                   (kv_autoencoder_train.py)
+  kv-retention      the window / compressive-slot retention sidecar          (kv_retention_write.py)
 
 Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
 could not be read.
@@ -720,6 +724,114 @@ def _cmd_act_validate(a) -> int:
     return 0 if r["ok"] else 2
 
 
+# ---- kv-dump / kv-autoencoder / kv-retention ------------------------------------
+@torch.no_grad()
+def kv_dump(model, prompts: list[list[int]], out_dir: str) -> list[str]:
+    """One file per prompt: a list with, per layer, {"k": rows [T, ...], "v": rows or None} of the
+    prompt's cache after prefill (MLA: the latent row; GQA: keys / values per head)."""
+    from ..inference.kv_cache import KVCache
+    os.makedirs(out_dir, exist_ok=True)
+    dev = next(model.parameters()).device
+    paths = []
+    for i, ids in enumerate(prompts):
+        cache = KVCache(model.cfg, 1, len(ids) + 1, dev)
+        model.forward_cached(torch.tensor([ids], dtype=torch.long, device=dev), cache, prefill=True, last_only=True)
+        lo, hi = cache.sink, cache.sink + len(ids)
+        entry = [{"k": cache.k[li][0, lo:hi].float().cpu(),
+                  "v": None if cache.v[li] is None else cache.v[li][0, lo:hi].float().cpu()}
+                 for li in range(model.cfg.n_layers)]
+        p = os.path.join(out_dir, f"kv_{i:05d}.pt")
+        torch.save(entry, p)
+        paths.append(p)
+    return paths
+
+
+class KVAutoEncoder(torch.nn.Module):
+    def __init__(self, dim: int, latent: int):
+        super().__init__()
+        self.enc = torch.nn.Linear(dim, latent, bias=False)
+        self.dec = torch.nn.Linear(latent, dim, bias=False)
+
+    def forward(self, x):
+        z = self.enc(x)
+        return self.dec(z), z
+
+
+def _kv_rows(kv_dir: str, max_files: int = 64) -> torch.Tensor:
+    import glob
+    rows = []
+    for p in sorted(glob.glob(os.path.join(kv_dir, "kv_*.pt")))[:max_files]:
+        for e in torch.load(p, map_location="cpu", weights_only=True):
+            for t in (e["k"], e["v"]):
+                if t is not None:
+                    rows.append(t.reshape(-1, t.shape[-1]).float())
+    return torch.cat(rows) if rows else torch.empty(0, 0)
+
+
+def train_kv_autoencoder(rows: torch.Tensor, latent: int, method: str = "pca", steps: int = 500,
+                         lr: float = 1e-3, seed: int = 0) -> tuple[KVAutoEncoder, float]:
+    """Fit on rows [n, dim]; returns (model, relative reconstruction error on the rows).  `pca`: the
+    optimal rank-`latent` linear autoencoder in closed form (encoder = top right singular vectors of
+    the rows, decoder = its transpose); `sgd`: AdamW on the MSE from a random start."""
+    n, dim = rows.shape
+    ae = KVAutoEncoder(dim, min(latent, dim))
+    if method == "pca":
+        _, _, vh = torch.linalg.svd(rows, full_matrices=False)
+        basis = vh[:ae.enc.out_features]                      # [latent, dim]
+        with torch.no_grad():
+            ae.enc.weight.copy_(basis)
+            ae.dec.weight.copy_(basis.t())
+    else:
+        g = torch.Generator().manual_seed(seed)
+        opt = torch.optim.AdamW(ae.parameters(), lr=lr)
+        for _ in range(steps):
+            xb = rows[torch.randint(0, n, (min(8192, n),), generator=g)]
+            loss = torch.nn.functional.mse_loss(ae(xb)[0], xb)
+            opt.zero_grad(set_to_none=True)
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(ae.parameters(), 1.0)
+            opt.step()
+    with torch.no_grad():
+        err = float((ae(rows)[0] - rows).norm() / rows.norm().clamp_min(1e-12))
+    return ae, err
+
+
+def _cmd_kv_dump(a) -> int:
+    from ..config import get_preset
+    from ..inference.builders import load_model
+    from ..models.lm import build_model
+    from ..training.tokenizer import get_tokenizer
+    dev = torch.device(a.device)
+    model = (load_model(a.ckpt, dev, dtype=torch.float32)[0] if a.ckpt else
+             build_model(get_preset(a.preset), device=dev, dtype=torch.float32, seed=0)).eval()
+    tok = get_tokenizer(model.cfg.vocab_size)
+    paths = kv_dump(model, [tok.encode(p)[:a.max_tokens] or [1] for p in (a.prompts or _SAMPLE_PROMPTS)], a.out_dir)
+    print(json.dumps({"files": len(paths), "out_dir": a.out_dir}))
+    return 0
+
+
+def _cmd_kv_autoencoder(a) -> int:
+    rows = _kv_rows(a.kv_dir)
+    if rows.numel() == 0:
+        print(json.dumps({"error": f"no kv_*.pt dumps in {a.kv_dir}"}))
+        return 3
+    ae, err = train_kv_autoencoder(rows, a.latent, a.method, a.steps, a.lr)
+    os.makedirs(os.path.dirname(a.out_pt) or ".", exist_ok=True)
+    torch.save({"dim": rows.shape[1], "latent": ae.enc.out_features, "state_dict": ae.state_dict()}, a.out_pt)
+    side = {"kv_autoencoder": {"dim": rows.shape[1], "latent": ae.enc.out_features,
+                               "weights": os.path.abspath(a.out_pt), "method": a.method, "rel_err": err}}
+    _write_json(a.out_json, side)
+    print(json.dumps(side["kv_autoencoder"]))
+    return 0
+
+
+def _cmd_kv_retention(a) -> int:
+    blob = {"compressive_slots": a.compressive_slots, "window_size": a.window_size, "schema": 1}
+    _write_json(a.out, blob)
+    print(json.dumps(blob))
+    return 0
+
+
 # ---- command line ---------------------------------------------------------------
 def _parser() -> argparse.ArgumentParser:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -848,6 +960,31 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--policy", required=True)
     p.add_argument("--layers", type=int, default=0)
     p.set_defaults(fn=_cmd_act_validate)
+
+    p = sub.add_parser("kv-dump", help="KV-cache rows of sample prompts, one .pt per prompt")
+    p.add_argument("--preset", default="tiny_moe")
+    p.add_argument("--ckpt", default="")
+    p.add_argument("--prompts", nargs="*", default=None)
+    p.add_argument("--max_tokens", type=int, default=512)
+    p.add_argument("--out_dir", default="weights/kv_dump")
+    p.add_argument("--device", default="cpu")
+    p.set_defaults(fn=_cmd_kv_dump)
+
+    p = sub.add_parser("kv-autoencoder", help="linear autoencoder of dumped KV rows")
+    p.add_argument("--kv_dir", default="weights/kv_dump")
+    p.add_argument("--latent", type=int, default=64)
+    p.add_argument("--method", default="pca", choices=["pca", "sgd"])
+    p.add_argument("--steps", type=int, default=500)
+    p.add_argument("--lr", type=float, default=1e-3)
+    p.add_argument("--out_pt", default="weights/kv_autoencoder.pt")
+    p.add_argument("--out_json", default="weights/kv_compress_sidecar.json")
+    p.set_defaults(fn=_cmd_kv_autoencoder)
+
+    p = sub.add_parser("kv-retention", help="write the KV retention sidecar")
+    p.add_argument("--out", required=True)
+    p.add_argument("--compressive_slots", type=int, default=4)
+    p.add_argument("--window_size", type=int, default=2048)
+    p.set_defaults(fn=_cmd_kv_retention)
     return ap
 
 

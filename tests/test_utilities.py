@@ -239,3 +239,29 @@ def test_act_calibrate_and_validate(tmp_path):
                                "thresholds": {"layers": {"1": {"conf_floor": 0.5}, "0": {}}}}))
     r = U.act_validate(json.loads(pol.read_text()))
     assert r["global"] == {"conf_floor": 0.4, "min_bits": 8, "max_bits": 4} and r["per_layer_conf_floor"] == [0.4, 0.5]
+
+
+def test_kv_dump_autoencoder_retention(tmp_path):
+    d = tmp_path / "dump"
+    assert _cli(["kv-dump", "--preset", "tiny_moe", "--max_tokens", "24", "--out_dir", str(d)]) == 0
+    files = sorted(d.glob("kv_*.pt"))
+    from omnicoder.config import get_preset
+    cfg = get_preset("tiny_moe")
+    e = torch.load(files[0], weights_only=True)
+    assert len(files) == 4 and len(e) == cfg.n_layers and e[0]["k"].shape[0] <= 24
+    rows = U._kv_rows(str(d))
+    dim = rows.shape[1]
+    # the closed-form (PCA) autoencoder at full rank reproduces the rows; at lower rank it beats SGD
+    _, err_full = U.train_kv_autoencoder(rows, dim, "pca")
+    assert err_full < 1e-4
+    _, err_pca = U.train_kv_autoencoder(rows, 8, "pca")
+    _, err_sgd = U.train_kv_autoencoder(rows, 8, "sgd", steps=50)
+    assert err_pca <= err_sgd + 1e-6
+    side = tmp_path / "side.json"
+    assert _cli(["kv-autoencoder", "--kv_dir", str(d), "--latent", "8", "--out_pt", str(tmp_path / "ae.pt"),
+                 "--out_json", str(side)]) == 0
+    assert json.loads(side.read_text())["kv_autoencoder"]["latent"] == 8
+    assert _cli(["kv-autoencoder", "--kv_dir", str(tmp_path / "none")]) == 3
+    ret = tmp_path / "r.json"
+    assert _cli(["kv-retention", "--out", str(ret), "--window_size", "1024"]) == 0
+    assert json.loads(ret.read_text()) == {"compressive_slots": 4, "window_size": 1024, "schema": 1}
