@@ -6,7 +6,12 @@ run a candidate program with its tests and report pass / fail with the captured 
                   and file-size limits applied in the child before it starts;
   CppSandbox      g++ -O2 -std=c++17 then the binary, same limits;
   HTTPSandbox     POST {"code", "tests", "timeout"} to a remote runner, which answers
-                  {"ok", "stdout", "stderr"}.
+                  {"ok", "stdout", "stderr"};
+  verify_with_tests  the solution as `solution.py` beside a pytest file, pytest run under the same
+                  limits (plugins not auto-loaded), with the passed / failed / error counts
+                  (reference src/omnicoder/tools/code_verifier.py:1-97; a failing pytest run is
+                  the answer here, not a reason to fall back to executing the test file, which would
+                  only define the test functions and exit 0).
 The tests run after the code; the run passes when the process exits 0 (Python: and printed the
 end marker, so a test file that exits early does not pass).  This isolates resources, not
 privileges: the child runs as the calling user, so it is meant for model-written snippets under
@@ -43,11 +48,11 @@ def _limits(cpu_s: int, mem_bytes: int):
     return apply if os.name == "posix" else None
 
 
-def _run(args, cwd, timeout, mem_bytes) -> SandboxResult:
+def _run(args, cwd, timeout, mem_bytes, env_extra: dict | None = None) -> SandboxResult:
+    env = {"PATH": os.environ.get("PATH", "/usr/bin:/bin"), "LANG": "C.UTF-8", **(env_extra or {})}
     try:
         p = subprocess.run(args, cwd=cwd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True,
-                           timeout=max(1, timeout), preexec_fn=_limits(max(1, timeout), mem_bytes),
-                           env={"PATH": os.environ.get("PATH", "/usr/bin:/bin"), "LANG": "C.UTF-8"})
+                           timeout=max(1, timeout), preexec_fn=_limits(max(1, timeout), mem_bytes), env=env)
         return SandboxResult(p.returncode == 0, p.stdout, p.stderr, p.returncode)
     except subprocess.TimeoutExpired as e:
         out = e.stdout.decode() if isinstance(e.stdout, bytes) else (e.stdout or "")
@@ -98,3 +103,35 @@ class HTTPSandbox:
             return SandboxResult(bool(d.get("ok")), str(d.get("stdout", "")), str(d.get("stderr", "")))
         except Exception as e:
             return SandboxResult(False, "", f"remote sandbox error: {e}")
+
+
+@dataclass
+class VerifyReport:
+    ok: bool
+    passed: int
+    failed: int
+    errors: int
+    returncode: int | None
+    log: str
+
+
+def verify_with_tests(code: str, tests: str, tests_name: str = "test_solution.py", timeout: int = 30,
+                      mem_bytes: int = 4 << 30, python: str | None = None) -> VerifyReport:
+    import re
+    if not tests_name.startswith("test_") or not tests_name.endswith(".py"):
+        raise ValueError("tests_name must look like test_*.py so that pytest collects it")
+    with tempfile.TemporaryDirectory() as td:
+        with open(os.path.join(td, "solution.py"), "w", encoding="utf-8") as f:
+            f.write(code)
+        with open(os.path.join(td, tests_name), "w", encoding="utf-8") as f:
+            f.write(tests)
+        r = _run([python or sys.executable, "-I", "-m", "pytest", "-q", "-p", "no:cacheprovider", tests_name], td,
+                 timeout, mem_bytes, {"PYTEST_DISABLE_PLUGIN_AUTOLOAD": "1", "PYTHONPATH": td})
+    out = r.stdout + "\n" + r.stderr
+
+    def count(word):
+        m = re.findall(rf"(\d+) {word}", out)
+        return int(m[-1]) if m else 0
+    passed, failed, errors = count("passed"), count("failed"), count("errors?")
+    return VerifyReport(r.returncode == 0 and passed > 0 and failed == 0 and errors == 0, passed, failed, errors,
+                      r.returncode, out[-20000:])

@@ -30,6 +30,8 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
   kv-autoencoder    a linear autoencoder of the dumped rows (closed-form PCA or AdamW) and its
                     sidecar                                                   (kv_autoencoder_train.py)
   kv-retention      the window / compressive-slot retention sidecar          (kv_retention_write.py)
+  code-verify       a solution against a pytest file in the sandbox, with pass / fail counts
+                                                                  (code_verifier.py:1-97)
 
 Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
 could not be read.
@@ -832,6 +834,25 @@ def _cmd_kv_retention(a) -> int:
     return 0
 
 
+# ---- code-verify ---------------------------------------------------------------
+def _cmd_code_verify(a) -> int:
+    from ..sfb.sandbox import verify_with_tests
+    if a.code_file:
+        with open(a.code_file, encoding="utf-8") as f:
+            code = f.read()
+    else:
+        code = a.code_text
+    with open(a.tests_file, encoding="utf-8") as f:
+        tests = f.read()
+    name = os.path.basename(a.tests_file)
+    r = verify_with_tests(code, tests, name if name.startswith("test_") else "test_" + name, a.timeout)
+    out = {"ok": r.ok, "passed": r.passed, "failed": r.failed, "errors": r.errors, "returncode": r.returncode,
+           "log": r.log}
+    _write_json(a.out_json, out)
+    print(json.dumps({k: v for k, v in out.items() if k != "log"}))
+    return 0 if r.ok else 2
+
+
 # ---- command line ---------------------------------------------------------------
 def _parser() -> argparse.ArgumentParser:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -985,6 +1006,14 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--compressive_slots", type=int, default=4)
     p.add_argument("--window_size", type=int, default=2048)
     p.set_defaults(fn=_cmd_kv_retention)
+
+    p = sub.add_parser("code-verify", help="run a solution against a pytest file in the sandbox")
+    p.add_argument("--code_file", default="")
+    p.add_argument("--code_text", default="")
+    p.add_argument("--tests_file", required=True)
+    p.add_argument("--timeout", type=int, default=30)
+    p.add_argument("--out_json", default="weights/code_verify_result.json")
+    p.set_defaults(fn=_cmd_code_verify)
     return ap
 
 

@@ -265,3 +265,22 @@ def test_kv_dump_autoencoder_retention(tmp_path):
     ret = tmp_path / "r.json"
     assert _cli(["kv-retention", "--out", str(ret), "--window_size", "1024"]) == 0
     assert json.loads(ret.read_text()) == {"compressive_slots": 4, "window_size": 1024, "schema": 1}
+
+
+def test_code_verify(tmp_path):
+    from omnicoder.sfb.sandbox import verify_with_tests
+    tests = "from solution import add\n\ndef test_one():\n    assert add(1, 2) == 3\n\ndef test_two():\n    assert add(2, 2) == 4\n"
+    r = verify_with_tests("def add(a, b):\n    return a + b\n", tests)
+    assert r.ok and (r.passed, r.failed, r.errors) == (2, 0, 0)
+    r = verify_with_tests("def add(a, b):\n    return a - b\n", tests)
+    assert not r.ok and r.failed == 2
+    r = verify_with_tests("def add(:\n", tests)               # a syntax error is a collection error
+    assert not r.ok and r.errors >= 1 and r.passed == 0
+    t = tmp_path / "tests_add.py"
+    t.write_text(tests)
+    out = tmp_path / "v.json"
+    assert _cli(["code-verify", "--code_text", "def add(a, b):\n    return a + b\n", "--tests_file", str(t),
+                 "--out_json", str(out)]) == 0
+    assert json.loads(out.read_text())["passed"] == 2
+    assert _cli(["code-verify", "--code_text", "def add(a, b):\n    return 0\n", "--tests_file", str(t),
+                 "--out_json", str(out)]) == 2
