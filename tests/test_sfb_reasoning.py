@@ -143,3 +143,31 @@ def test_code_sandboxes():
         assert c.ok
         assert not CppSandbox().run("int f(){return 1;}", "return f();").ok
     assert not HTTPSandbox("http://127.0.0.1:9/none").run("x=1", timeout=1).ok
+
+
+def test_multi_solution_variants(tmp_path):
+    import json
+
+    from omnicoder.training.multi_solution import canonical, code_variants, main, math_variants, rename_locals
+    src = ("import math\nTOTAL = 3\n\ndef f(n, scale=2):\n    acc = 0\n    for i in range(n):\n"
+           "        acc += i * scale\n    try:\n        q = 1 / n\n    except ZeroDivisionError as e:\n"
+           "        q = 0\n    sq = [i * i for i in range(n)]\n    g = lambda z: z + acc\n"
+           "    s = 'i q acc'\n    return acc + TOTAL + q + sum(sq) + g(1) + math.floor(1.5) + len(s)\n")
+    alt = rename_locals(src)
+    assert "for v" in alt and "'i q acc'" in alt and "except ZeroDivisionError as e" in alt
+    ns1, ns2 = {}, {}
+    exec(src, ns1)
+    exec(alt, ns2)
+    assert all(ns1["f"](n) == ns2["f"](n) for n in (0, 1, 5))
+    assert canonical("x = ( 1+2 )\n") == "x = 1 + 2"
+    tests = "from solution import f\n\ndef test_f():\n    assert f(3) == 9\n"
+    vs = code_variants("def f(n):\n    t = n*n  # square\n    return t\n", tests)
+    assert {v["variant"] for v in vs} == {"rename_locals", "canonical"} and all(v["verified"] for v in vs)
+    mv = {v["variant"]: v for v in math_variants("x**2 - 5*x + 6 = 0")}
+    assert mv["solved"]["solution"] == "x = 2, x = 3" and mv["factored"]["verified"]
+    inp = tmp_path / "m.jsonl"
+    inp.write_text(json.dumps({"question": "solve", "answer": "2*y + 4 = 10"}) + "\n")
+    out = tmp_path / "o.jsonl"
+    assert main(["--input", str(inp), "--domain", "math", "--out", str(out)]) == 0
+    rows = [json.loads(ln) for ln in out.read_text().splitlines()]
+    assert {r["alt_solution"] for r in rows} >= {"y = 3", "2*y - 6 = 0"}
