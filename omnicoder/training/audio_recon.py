@@ -50,7 +50,7 @@ class MelPoolEncoder(nn.Module):
 class AudioReconTrainer(FlowReconTrainer):
     def __init__(self, lm, head: LatentQueryHead, encoder: MelPoolEncoder, lr: float = 1e-3, flow: bool = False,
                  recon: str = "mse", train_lm: bool = False, mel_weight: float = 0.1, stft_weight: float = 0.05,
-                 n_fft: int = 1024, hop: int = 256):
+                 n_fft: int = 1024, hop: int = 256, refiner: nn.Module | None = None):
         C = head.mlp[-1].out_features
         n_mels = encoder.proj.shape[0]
         self.proj_mel = nn.Sequential(nn.LayerNorm(C), nn.Linear(C, 128), nn.GELU(), nn.Linear(128, n_mels))
@@ -58,7 +58,7 @@ class AudioReconTrainer(FlowReconTrainer):
         dev = head.q.device
         self.proj_mel.to(dev)
         self.proj_stft.to(dev)
-        super().__init__(lm, head, encoder, lr, flow, recon, train_lm)
+        super().__init__(lm, head, encoder, lr, flow, recon, train_lm, refiner=refiner)
         self.opt.add_param_group({"params": list(self.proj_mel.parameters()) + list(self.proj_stft.parameters())})
         self.mel_weight, self.stft_weight, self.n_fft, self.hop = mel_weight, stft_weight, n_fft, hop
 
@@ -100,6 +100,7 @@ def main(argv=None):
     ap.add_argument("--flow_loss", action="store_true")
     ap.add_argument("--mel_weight", type=float, default=0.1)
     ap.add_argument("--stft_weight", type=float, default=0.05)
+    ap.add_argument("--use_refiner", action="store_true", help="train a latent refiner beside the head")
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--out", default="weights/audio_recon_head.pt")
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
@@ -108,8 +109,10 @@ def main(argv=None):
     lm = build_model(get_preset(a.preset), device=dev, dtype=torch.float32, seed=0).eval()
     head = LatentQueryHead(lm.cfg.d_model, a.segments, a.latent_dim).to(dev)
     enc = MelPoolEncoder(a.segments, a.latent_dim).to(dev)
+    from ..multimodal.video import LatentRefiner
+    refiner = LatentRefiner(a.latent_dim).to(dev) if a.use_refiner else None
     tr = AudioReconTrainer(lm, head, enc, a.lr, a.flow_loss, a.recon_loss, mel_weight=a.mel_weight,
-                           stft_weight=a.stft_weight)
+                           stft_weight=a.stft_weight, refiner=refiner)
     tok = get_tokenizer(lm.cfg.vocab_size)
     waves, caps = synthetic_tones(8)
     g = torch.Generator().manual_seed(0)
@@ -121,7 +124,8 @@ def main(argv=None):
         ids = torch.tensor([e + [0] * (L - len(e)) for e in enc_ids], device=dev)
         losses.append(tr.step(waves[idx].to(dev), ids))
     torch.save({"head": head.state_dict(), "proj_mel": tr.proj_mel.state_dict(),
-                "proj_stft": tr.proj_stft.state_dict(), "flow": a.flow_loss}, a.out)
+                "proj_stft": tr.proj_stft.state_dict(), "flow": a.flow_loss,
+                **({"refiner": refiner.state_dict()} if refiner is not None else {})}, a.out)
     print(json.dumps({"steps": a.steps, "first_loss": losses[0], "last_loss": losses[-1], "out": a.out}))
     return 0
 

@@ -10,6 +10,9 @@ reconstruction loss and optionally a flow / diffusion loss on noised latents).
       the head predicts the velocity v = eps - z0 from (h, x_t, t);  loss = E[w(t) |v_hat - v|^2]
       with w(t) = 1 / (t^2 + (1 - t)^2) (the weighting that equalises the noise-prediction scale).
 `sample()` integrates the learned velocity from noise (t = 1 -> 0, Euler) to a latent.
+With a refiner (the reference's --use_refiner: a small residual MLP over latents), the refiner is
+trained beside the head to map the head's estimate (detached) to the target, and `sample()` applies
+it last; its weights go into the checkpoint under "refiner" (the latent-refine tool reads them).
 
 `PatchPoolEncoder` is the stand-in encoder when no pretrained image autoencoder is available
 (the reference's IdentityAdapter): average pooling to a P-patch grid and a fixed random projection
@@ -71,9 +74,11 @@ def _weight(t: torch.Tensor) -> torch.Tensor:
 
 class FlowReconTrainer:
     def __init__(self, lm, head: LatentQueryHead, encoder: nn.Module, lr: float = 1e-3, flow: bool = False,
-                 recon: str = "mse", train_lm: bool = False):
+                 recon: str = "mse", train_lm: bool = False, refiner: nn.Module | None = None):
         self.lm, self.head, self.enc, self.flow, self.recon = lm, head, encoder, flow, recon
+        self.refiner = refiner
         params = list(head.parameters()) + ([p for p in lm.parameters() if p.requires_grad] if train_lm else [])
+        params += list(refiner.parameters()) if refiner is not None else []
         self.train_lm = train_lm
         self.opt = torch.optim.AdamW(params, lr=lr)
 
@@ -89,14 +94,18 @@ class FlowReconTrainer:
         from .multimodal_tasks import recon_loss
         if not self.flow:
             z_hat = self.head(h)
-            return recon_loss(z_hat, z0, self.recon), z_hat
-        B = z0.shape[0]
-        t = torch.sigmoid(torch.randn(B, device=z0.device))                    # logit-normal times
-        eps = torch.randn_like(z0)
-        x_t = (1 - t)[:, None, None] * z0 + t[:, None, None] * eps
-        v = self.head(h, x_t, t)
-        loss = (_weight(t)[:, None, None] * (v - (eps - z0)) ** 2).mean()
-        return loss, x_t - t[:, None, None] * v
+            loss = recon_loss(z_hat, z0, self.recon)
+        else:
+            B = z0.shape[0]
+            t = torch.sigmoid(torch.randn(B, device=z0.device))                # logit-normal times
+            eps = torch.randn_like(z0)
+            x_t = (1 - t)[:, None, None] * z0 + t[:, None, None] * eps
+            v = self.head(h, x_t, t)
+            loss = (_weight(t)[:, None, None] * (v - (eps - z0)) ** 2).mean()
+            z_hat = x_t - t[:, None, None] * v
+        if self.refiner is not None:       # a post-processor of the head's estimate, trained beside it
+            loss = loss + recon_loss(self.refiner(z_hat.detach()), z0, self.recon)
+        return loss, z_hat
 
     def loss(self, images: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
         return self.loss_and_estimate(self.enc(images).to(ids.device), self._state(ids))[0]
@@ -114,15 +123,16 @@ class FlowReconTrainer:
         the learned velocity from noise at t = 1 to t = 0."""
         h = self._state(ids)
         if not self.flow:
-            return self.head(h)
-        P, C = self.head.q.shape[0], self.head.mlp[-1].out_features
-        g = torch.Generator(device=ids.device).manual_seed(seed)
-        x = torch.randn(ids.shape[0], P, C, generator=g, device=ids.device)
-        ts = torch.linspace(1.0, 0.0, steps + 1, device=ids.device)
-        for i in range(steps):
-            t = ts[i].expand(ids.shape[0])
-            x = x + (ts[i + 1] - ts[i]) * self.head(h, x, t)                   # dx/dt = v
-        return x
+            x = self.head(h)
+        else:
+            P, C = self.head.q.shape[0], self.head.mlp[-1].out_features
+            g = torch.Generator(device=ids.device).manual_seed(seed)
+            x = torch.randn(ids.shape[0], P, C, generator=g, device=ids.device)
+            ts = torch.linspace(1.0, 0.0, steps + 1, device=ids.device)
+            for i in range(steps):
+                t = ts[i].expand(ids.shape[0])
+                x = x + (ts[i + 1] - ts[i]) * self.head(h, x, t)               # dx/dt = v
+        return self.refiner(x) if self.refiner is not None else x
 
 
 def main(argv=None):
@@ -138,6 +148,7 @@ def main(argv=None):
     ap.add_argument("--channels", type=int, default=16)
     ap.add_argument("--flow_loss", action="store_true")
     ap.add_argument("--recon_loss", default="mse", choices=["mse", "mae", "huber"])
+    ap.add_argument("--use_refiner", action="store_true", help="train a latent refiner beside the head")
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--out", default="weights/flow_recon_head.pt")
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
@@ -145,7 +156,10 @@ def main(argv=None):
     dev = torch.device(a.device)
     lm = build_model(get_preset(a.preset), device=dev, dtype=torch.float32, seed=0).eval()
     head = LatentQueryHead(lm.cfg.d_model, a.grid * a.grid, a.channels).to(dev)
-    tr = FlowReconTrainer(lm, head, PatchPoolEncoder(a.grid, a.channels).to(dev), a.lr, a.flow_loss, a.recon_loss)
+    from ..multimodal.video import LatentRefiner
+    refiner = LatentRefiner(a.channels).to(dev) if a.use_refiner else None
+    tr = FlowReconTrainer(lm, head, PatchPoolEncoder(a.grid, a.channels).to(dev), a.lr, a.flow_loss, a.recon_loss,
+                          refiner=refiner)
     tok = get_tokenizer(lm.cfg.vocab_size)
     g = torch.Generator().manual_seed(0)
     colors = torch.rand(8, 3, generator=g)
@@ -158,7 +172,8 @@ def main(argv=None):
         L = max(len(e) for e in enc)
         ids = torch.tensor([e + [0] * (L - len(e)) for e in enc], device=dev)
         losses.append(tr.step(imgs, ids))
-    torch.save({"head": head.state_dict(), "flow": a.flow_loss}, a.out)
+    torch.save({"head": head.state_dict(), "flow": a.flow_loss,
+                **({"refiner": refiner.state_dict()} if refiner is not None else {})}, a.out)
     print(json.dumps({"steps": a.steps, "first_loss": losses[0], "last_loss": losses[-1], "out": a.out}))
     return 0
 

@@ -273,3 +273,36 @@ def test_unified_mixed_trainer(tmp_path):
     (tmp_path / "u.jsonl").write_text("\n".join(json.dumps(r) for r in raw) + "\n")
     assert main(["--task", "unified", "--jsonl", str(tmp_path / "u.jsonl"), "--image_size", "32", "--steps", "2",
                  "--batch", "2", "--device", "cpu", "--out", str(tmp_path / "u.pt")]) == 0
+
+
+def test_latent_refiner_trained_beside_the_head(tmp_path):
+    """--use_refiner: the refiner learns to map the head's estimate to the target, sample() applies it,
+    and the checkpoint's refiner runs through the latent-refine tool."""
+    import numpy as np
+
+    from omnicoder.config import ModelConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.multimodal.video import LatentRefiner
+    from omnicoder.tools.utilities import main as tools_main
+    from omnicoder.training.flow_recon import FlowReconTrainer, LatentQueryHead, PatchPoolEncoder, main
+    torch.manual_seed(0)
+    cfg = ModelConfig(name="lr", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64)
+    lm = build_model(cfg, "cpu", dtype=torch.float32, seed=0).eval()
+    enc = PatchPoolEncoder(grid=2, channels=8)
+    imgs = torch.stack([torch.zeros(3, 16, 16), torch.ones(3, 16, 16)])
+    ids = torch.tensor([[5, 6, 7], [8, 9, 10]])
+    z0 = enc(imgs)
+    ref = LatentRefiner(8)
+    tr = FlowReconTrainer(lm, LatentQueryHead(64, 4, 8, width=64), enc, lr=3e-3, refiner=ref)
+    losses = [tr.step(imgs, ids) for _ in range(200)]
+    assert sum(losses[-10:]) < 0.3 * sum(losses[:10])
+    with torch.no_grad():
+        raw = tr.head(tr._state(ids))
+        assert torch.allclose(tr.sample(ids), ref(raw))
+        assert (ref(raw) - z0).norm() / z0.norm() < 0.2
+    out = tmp_path / "h.pt"
+    assert main(["--steps", "2", "--use_refiner", "--device", "cpu", "--channels", "8", "--out", str(out)]) == 0
+    assert "refiner" in torch.load(out, weights_only=False)
+    np.save(tmp_path / "z.npy", np.random.default_rng(0).standard_normal((2, 4, 8)).astype(np.float32))
+    assert tools_main(["latent-refine", "--latents", str(tmp_path / "z.npy"), "--out_latents",
+                       str(tmp_path / "r.npy"), "--ckpt", str(out)]) == 0
