@@ -180,3 +180,22 @@ def test_code_expert_router_kd_and_balance(tmp_path):
     assert parts2["router_kd"] < 1e-6
     assert main(["--steps", "1", "--seq_len", "16", "--batch_size", "1", "--device", "cpu",
                  "--student_preset", "tiny_moe", "--out", str(tmp_path / "c.pt")]) == 0
+
+
+def test_run_training_probe_sizes_the_plan(tmp_path):
+    """The probe runs each stage for 1 and 3 steps and the plan uses the measured rates."""
+    from omnicoder.tools.run_training import plan
+    out = _run(["omnicoder.tools.run_training", "--stages", "audio_recon,pre_align", "--out_dir", str(tmp_path),
+                "--probe_only", "--device", "cpu"])
+    pr = json.loads((tmp_path / "train_probe_summary.json").read_text())
+    assert set(pr) == {"audio_recon", "pre_align"} and all(v["rc"] == 0 and v["steps_per_minute"] > 0
+                                                           for v in pr.values()), out
+    p = plan(10.0, {k: v["steps_per_minute"] for k, v in pr.items()}, ["audio_recon", "pre_align"])
+    for s in p:
+        assert p[s]["steps"] == max(1, int(p[s]["minutes"] * pr[s]["steps_per_minute"]))
+    # an unknown stage in the plan takes the mean measured rate
+    q = plan(10.0, {"pre_align": 30.0}, ["pre_align", "audio_recon"])
+    assert q["audio_recon"]["steps"] == int(q["audio_recon"]["minutes"] * 30.0)
+    out = _run(["omnicoder.tools.run_training", "--stages", "pre_align", "--out_dir", str(tmp_path / "r"),
+                "--probe_json", str(tmp_path / "train_probe_summary.json"), "--dry_run"])
+    assert "omnicoder.training.pre_align" in out
