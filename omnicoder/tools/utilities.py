@@ -32,6 +32,8 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
   kv-retention      the window / compressive-slot retention sidecar          (kv_retention_write.py)
   code-verify       a solution against a pytest file in the sandbox, with pass / fail counts
                                                                   (code_verifier.py:1-97)
+  auto-tune         the speculative draft length that maximises expected throughput, from a measured
+                    acceptance benchmark                                       (auto_tune.py:1-138)
 
 Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
 could not be read.
@@ -853,6 +855,58 @@ def _cmd_code_verify(a) -> int:
     return 0 if r.ok else 2
 
 
+# ---- auto-tune -----------------------------------------------------------------
+def expected_tokens(alpha: float, k: int) -> float:
+    """Tokens per verification round with k drafts accepted independently with probability alpha:
+    1 + alpha + ... + alpha^k (Leviathan et al., 2023)."""
+    return float(k + 1) if alpha >= 1.0 else (1.0 - alpha ** (k + 1)) / (1.0 - alpha)
+
+
+def alpha_from_ratio(ratio: float, k: int) -> float:
+    """Per-token acceptance alpha from the measured accepted / proposed ratio of k-draft rounds:
+    solves (alpha + alpha^2 + ... + alpha^k) / k = ratio by bisection (the ratio grows with alpha)."""
+    ratio = min(max(ratio, 0.0), 1.0)
+    lo, hi = 0.0, 1.0
+    for _ in range(60):
+        mid = 0.5 * (lo + hi)
+        if (expected_tokens(mid, k) - 1.0) / k < ratio:
+            lo = mid
+        else:
+            hi = mid
+    return 0.5 * (lo + hi)
+
+
+def tune_draft_len(report: dict, max_k: int = 16) -> dict:
+    """From an acceptance benchmark (acceptance = accepted / proposed, draft_len k, plain and
+    speculative tokens/s): per-token alpha, the draft-to-target step cost c implied by the measured
+    speed-up (speculative / plain = E(k) / (k c + 1)), and the k in 1..max_k that maximises
+    E(k) / (k c + 1); k = 0 (no drafting) when no k beats plain decoding."""
+    r = report.get("acceptance", report)
+    rep = r if isinstance(r, dict) else report          # nested (draft-pipeline report) or flat
+    k0 = int(rep["draft_len"])
+    alpha = alpha_from_ratio(float(rep["acceptance"]), k0)
+    measured = float(rep["speculative_tokens_per_s"]) / max(float(rep["plain_tokens_per_s"]), 1e-9)
+    c = max((expected_tokens(alpha, k0) / max(measured, 1e-9) - 1.0) / k0, 0.0)
+    table = [{"draft_len": k, "expected_speedup": expected_tokens(alpha, k) / (k * c + 1.0)} for k in range(1, max_k + 1)]
+    best = max(table, key=lambda t: t["expected_speedup"])
+    k = best["draft_len"] if best["expected_speedup"] > 1.0 else 0
+    return {"alpha": alpha, "cost_ratio": c, "measured_speedup": measured, "best_draft_len": k,
+            "expected_speedup": best["expected_speedup"] if k else 1.0, "table": table,
+            "generate_flags": f"--speculative_draft_len {k}" if k else "--disable_speculative"}
+
+
+def _cmd_auto_tune(a) -> int:
+    try:
+        rep = _read_json(a.acceptance_json)
+    except (OSError, ValueError) as e:
+        print(json.dumps({"error": str(e)}))
+        return 3
+    out = tune_draft_len(rep, a.max_draft_len)
+    _write_json(a.out, out)
+    print(json.dumps({k: v for k, v in out.items() if k != "table"}))
+    return 0
+
+
 # ---- command line ---------------------------------------------------------------
 def _parser() -> argparse.ArgumentParser:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -1014,6 +1068,12 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--timeout", type=int, default=30)
     p.add_argument("--out_json", default="weights/code_verify_result.json")
     p.set_defaults(fn=_cmd_code_verify)
+
+    p = sub.add_parser("auto-tune", help="speculative draft length from a measured acceptance benchmark")
+    p.add_argument("--acceptance_json", default="weights/draft_acceptance.json")
+    p.add_argument("--max_draft_len", type=int, default=16)
+    p.add_argument("--out", default="weights/auto_tune.json")
+    p.set_defaults(fn=_cmd_auto_tune)
     return ap
 
 

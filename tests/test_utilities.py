@@ -284,3 +284,24 @@ def test_code_verify(tmp_path):
     assert json.loads(out.read_text())["passed"] == 2
     assert _cli(["code-verify", "--code_text", "def add(a, b):\n    return 0\n", "--tests_file", str(t),
                  "--out_json", str(out)]) == 2
+
+
+def test_auto_tune_draft_len(tmp_path):
+    # accepted / proposed of 4-draft rounds back to the per-token alpha
+    a = 0.8
+    ratio = (U.expected_tokens(a, 4) - 1) / 4
+    assert abs(U.alpha_from_ratio(ratio, 4) - a) < 1e-9
+    # a report made from alpha 0.8 and a draft step costing 5 % of a target step
+    c = 0.05
+    rep = {"acceptance": {"acceptance": ratio, "draft_len": 4, "plain_tokens_per_s": 100.0,
+                          "speculative_tokens_per_s": 100.0 * U.expected_tokens(a, 4) / (4 * c + 1)}}
+    out = U.tune_draft_len(rep)
+    assert abs(out["alpha"] - a) < 1e-6 and abs(out["cost_ratio"] - c) < 1e-6
+    best = max(range(1, 17), key=lambda k: U.expected_tokens(a, k) / (k * c + 1))
+    assert out["best_draft_len"] == best and out["generate_flags"] == f"--speculative_draft_len {best}"
+    # a draft that is rarely accepted: no k beats plain decoding
+    low = {"acceptance": 0.0001, "draft_len": 4, "plain_tokens_per_s": 100.0, "speculative_tokens_per_s": 30.0}
+    assert U.tune_draft_len(low)["best_draft_len"] == 0
+    (tmp_path / "acc.json").write_text(json.dumps(rep))
+    assert _cli(["auto-tune", "--acceptance_json", str(tmp_path / "acc.json"), "--out", str(tmp_path / "t.json")]) == 0
+    assert json.loads((tmp_path / "t.json").read_text())["best_draft_len"] == best
