@@ -34,6 +34,8 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
                                                                   (code_verifier.py:1-97)
   auto-tune         the speculative draft length that maximises expected throughput, from a measured
                     acceptance benchmark                                       (auto_tune.py:1-138)
+  plot-metrics      SVG charts written as text: bars of the numbers in a metrics JSON, lines of keys
+                    of a JSONL training log                                  (visualize_metrics.py)
 
 Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
 could not be read.
@@ -907,6 +909,83 @@ def _cmd_auto_tune(a) -> int:
     return 0
 
 
+# ---- plot-metrics --------------------------------------------------------------
+def _esc(t) -> str:
+    return str(t).replace("&", "&amp;").replace("<", "&lt;").replace(">", "&gt;")
+
+
+def svg_bars(data: dict, title: str = "", width: int = 640) -> str:
+    """Horizontal bars, one per (label, value >= 0)."""
+    items = [(k, max(0.0, float(v))) for k, v in data.items()]
+    left, top, bar = 200, 30, 22
+    height = top + bar * max(1, len(items)) + 10
+    mx = max([v for _, v in items] + [1e-12])
+    out = [f"<svg xmlns='http://www.w3.org/2000/svg' width='{width}' height='{height}'>",
+           f"<text x='10' y='20' font-size='14' font-weight='bold'>{_esc(title)}</text>"]
+    for i, (k, v) in enumerate(items):
+        y = top + i * bar
+        w = int((v / mx) * (width - left - 120))
+        out.append(f"<text x='10' y='{y + 15}' font-size='12'>{_esc(k)[:28]}</text>")
+        out.append(f"<rect x='{left}' y='{y + 2}' width='{w}' height='{bar - 6}' fill='#4C78A8'/>")
+        out.append(f"<text x='{left + w + 6}' y='{y + 15}' font-size='12'>{v:.4g}</text>")
+    out.append("</svg>")
+    return "".join(out)
+
+
+def svg_lines(series: dict, title: str = "", width: int = 640, height: int = 320) -> str:
+    """One polyline per name of {name: [(x, y), ...]}, on shared axes."""
+    pts = [p for ps in series.values() for p in ps]
+    if not pts:
+        return f"<svg xmlns='http://www.w3.org/2000/svg' width='{width}' height='60'><text x='10' y='30'>no data</text></svg>"
+    x0, x1 = min(p[0] for p in pts), max(p[0] for p in pts)
+    y0, y1 = min(p[1] for p in pts), max(p[1] for p in pts)
+    sx = (width - 90) / ((x1 - x0) or 1.0)
+    sy = (height - 70) / ((y1 - y0) or 1.0)
+    colors = ["#4C78A8", "#F58518", "#54A24B", "#E45756", "#72B7B2", "#B279A2"]
+    out = [f"<svg xmlns='http://www.w3.org/2000/svg' width='{width}' height='{height}'>",
+           f"<text x='10' y='20' font-size='14' font-weight='bold'>{_esc(title)}</text>",
+           f"<text x='10' y='{height - 30}' font-size='11'>{y0:.4g}</text><text x='10' y='45' font-size='11'>{y1:.4g}</text>",
+           f"<text x='60' y='{height - 10}' font-size='11'>{x0:.4g}</text>"
+           f"<text x='{width - 60}' y='{height - 10}' font-size='11'>{x1:.4g}</text>"]
+    for i, (name, ps) in enumerate(series.items()):
+        c = colors[i % len(colors)]
+        path = " ".join(f"{60 + (x - x0) * sx:.1f},{height - 30 - (y - y0) * sy:.1f}" for x, y in ps)
+        out.append(f"<polyline fill='none' stroke='{c}' stroke-width='1.5' points='{path}'/>")
+        out.append(f"<text x='{width - 150}' y='{40 + 14 * i}' font-size='12' fill='{c}'>{_esc(name)}</text>")
+    out.append("</svg>")
+    return "".join(out)
+
+
+def _numbers(obj, prefix: str = "") -> dict:
+    out = {}
+    if isinstance(obj, dict):
+        for k, v in obj.items():
+            out.update(_numbers(v, f"{prefix}{k}."))
+    elif isinstance(obj, (int, float)) and not isinstance(obj, bool):
+        out[prefix[:-1]] = float(obj)
+    return out
+
+
+def _cmd_plot_metrics(a) -> int:
+    if a.log_jsonl:
+        with open(a.log_jsonl, encoding="utf-8") as f:
+            rows = [json.loads(ln) for ln in f if ln.strip()]
+        keys = [k for k in a.keys.split(",") if k]
+        series = {k: [(float(r.get(a.x, i)), float(r[k])) for i, r in enumerate(rows)
+                      if isinstance(r.get(k), (int, float))] for k in keys}
+        svg = svg_lines(series, a.title or os.path.basename(a.log_jsonl))
+    else:
+        nums = _numbers(_read_json(a.bench_json))
+        if a.keys:
+            nums = {k: v for k, v in nums.items() if any(s in k for s in a.keys.split(","))}
+        svg = svg_bars(nums, a.title or os.path.basename(a.bench_json))
+    os.makedirs(os.path.dirname(a.out_svg) or ".", exist_ok=True)
+    with open(a.out_svg, "w", encoding="utf-8") as f:
+        f.write(svg)
+    print(json.dumps({"out_svg": a.out_svg}))
+    return 0
+
+
 # ---- command line ---------------------------------------------------------------
 def _parser() -> argparse.ArgumentParser:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -1074,6 +1153,15 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--max_draft_len", type=int, default=16)
     p.add_argument("--out", default="weights/auto_tune.json")
     p.set_defaults(fn=_cmd_auto_tune)
+
+    p = sub.add_parser("plot-metrics", help="SVG chart of a metrics JSON or of a JSONL training log")
+    p.add_argument("--bench_json", default="")
+    p.add_argument("--log_jsonl", default="")
+    p.add_argument("--keys", default="", help="log: comma-separated keys to plot; JSON: substrings to keep")
+    p.add_argument("--x", default="step", help="log: the x key (default: the row index when absent)")
+    p.add_argument("--title", default="")
+    p.add_argument("--out_svg", default="weights/metrics.svg")
+    p.set_defaults(fn=_cmd_plot_metrics)
     return ap
 
 

@@ -305,3 +305,20 @@ def test_auto_tune_draft_len(tmp_path):
     (tmp_path / "acc.json").write_text(json.dumps(rep))
     assert _cli(["auto-tune", "--acceptance_json", str(tmp_path / "acc.json"), "--out", str(tmp_path / "t.json")]) == 0
     assert json.loads((tmp_path / "t.json").read_text())["best_draft_len"] == best
+
+
+def test_plot_metrics_svg(tmp_path):
+    import xml.etree.ElementTree as ET
+    bench = tmp_path / "b.json"
+    bench.write_text(json.dumps({"tokens": {"tokens_per_second": 120.5, "seconds": 2.0}, "name": "x", "ok": True}))
+    out = tmp_path / "b.svg"
+    assert _cli(["plot-metrics", "--bench_json", str(bench), "--out_svg", str(out)]) == 0
+    root = ET.fromstring(out.read_text())
+    rects = [e for e in root.iter() if e.tag.endswith("rect")]
+    assert len(rects) == 2                                  # the two numbers; strings and booleans skipped
+    log = tmp_path / "l.jsonl"
+    log.write_text("\n".join(json.dumps({"step": i, "loss": 5.0 / (i + 1), "lr": 1e-3}) for i in range(10)))
+    assert _cli(["plot-metrics", "--log_jsonl", str(log), "--keys", "loss,lr", "--out_svg", str(out)]) == 0
+    root = ET.fromstring(out.read_text())
+    lines = [e for e in root.iter() if e.tag.endswith("polyline")]
+    assert len(lines) == 2 and len(lines[0].get("points").split()) == 10
