@@ -36,6 +36,8 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
                     acceptance benchmark                                       (auto_tune.py:1-138)
   plot-metrics      SVG charts written as text: bars of the numbers in a metrics JSON, lines of keys
                     of a JSONL training log                                  (visualize_metrics.py)
+  write-threshold   the write-policy acceptance threshold per preset from teacher marks
+                                                                  (write_policy_acceptance.py:1-103)
 
 Exit codes follow the reference's scripts: 0 pass, 2 a checked limit was violated, 3 the input
 could not be read.
@@ -986,6 +988,43 @@ def _cmd_plot_metrics(a) -> int:
     return 0
 
 
+# ---- write-threshold -------------------------------------------------------------
+def write_threshold(marks: list[dict]) -> dict:
+    """Marks {"write": 0 | 1, optional "score": the write head's probability}.  Without scores the
+    threshold is the teacher's acceptance rate (the reference's fallback).  With scores it is the
+    score quantile that accepts that same fraction of rows, and the F1-best threshold is reported
+    beside it."""
+    y = [int(m["write"]) for m in marks if "write" in m]
+    rate = sum(y) / len(y) if y else 0.5
+    scored = [(float(m["score"]), int(m["write"])) for m in marks if "score" in m and "write" in m]
+    if not scored:
+        return {"threshold": rate, "acceptance_rate": rate, "rows": len(y), "from": "labels"}
+    sc = sorted((s for s, _ in scored), reverse=True)
+    n_acc = round(rate * len(sc))
+    thr = sc[n_acc - 1] if n_acc > 0 else sc[0] + 1e-6
+    best = (0.0, thr)
+    for t in sorted(set(sc)):
+        tp = sum(1 for s, l in scored if s >= t and l)
+        fp = sum(1 for s, l in scored if s >= t and not l)
+        fn = sum(1 for s, l in scored if s < t and l)
+        f1 = 2 * tp / max(1, 2 * tp + fp + fn)
+        if f1 > best[0]:
+            best = (f1, t)
+    return {"threshold": thr, "acceptance_rate": rate, "rows": len(scored), "from": "scores",
+            "f1_best_threshold": best[1], "f1": best[0]}
+
+
+def _cmd_write_threshold(a) -> int:
+    with open(a.marks, encoding="utf-8") as f:
+        marks = [json.loads(ln) for ln in f if ln.strip()]
+    r = write_threshold(marks)
+    data = _read_json(a.out) if os.path.exists(a.out) else {}
+    data[a.preset] = r["threshold"]
+    _write_json(a.out, data)
+    print(json.dumps({"preset": a.preset, **r, "out": a.out}))
+    return 0
+
+
 # ---- command line ---------------------------------------------------------------
 def _parser() -> argparse.ArgumentParser:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
@@ -1162,6 +1201,12 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--title", default="")
     p.add_argument("--out_svg", default="weights/metrics.svg")
     p.set_defaults(fn=_cmd_plot_metrics)
+
+    p = sub.add_parser("write-threshold", help="write-policy acceptance threshold from teacher marks")
+    p.add_argument("--marks", required=True, help="JSONL rows {text, write, optional score}")
+    p.add_argument("--preset", default="tiny_moe")
+    p.add_argument("--out", default="weights/write_policy_thresholds.json")
+    p.set_defaults(fn=_cmd_write_threshold)
     return ap
 
 

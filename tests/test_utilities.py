@@ -322,3 +322,19 @@ def test_plot_metrics_svg(tmp_path):
     root = ET.fromstring(out.read_text())
     lines = [e for e in root.iter() if e.tag.endswith("polyline")]
     assert len(lines) == 2 and len(lines[0].get("points").split()) == 10
+
+
+def test_write_threshold(tmp_path):
+    marks = [{"text": f"t{i}", "write": int(i % 4 == 0), "score": (0.9 if i % 4 == 0 else 0.1) + i * 1e-3}
+             for i in range(20)]
+    r = U.write_threshold(marks)
+    assert r["acceptance_rate"] == 0.25 and r["from"] == "scores"
+    assert sum(m["score"] >= r["threshold"] for m in marks) == 5 and r["f1"] == 1.0
+    assert U.write_threshold([{"write": 1}, {"write": 0}])["threshold"] == 0.5
+    f = tmp_path / "m.jsonl"
+    f.write_text("\n".join(json.dumps(m) for m in marks))
+    out = tmp_path / "thr.json"
+    out.write_text(json.dumps({"other": 0.3}))
+    assert _cli(["write-threshold", "--marks", str(f), "--preset", "p1", "--out", str(out)]) == 0
+    d = json.loads(out.read_text())
+    assert d["other"] == 0.3 and abs(d["p1"] - r["threshold"]) < 1e-12
