@@ -641,6 +641,9 @@ def main(argv=None):
     ap.add_argument("--retrieve_stride", type=int, default=400)
     ap.add_argument("--retrieve_max_chars", type=int, default=2000, help="retrieved characters put in the prompt")
     ap.add_argument("--retrieve_prepend", action="store_true", help="put the retrieved passages before the prompt")
+    ap.add_argument("--pref_lora", default=None, help="preference-expert LoRA adapters to load onto the model")
+    ap.add_argument("--pref_index", default=None, help="preference-expert retrieval index (a saved PQ index)")
+    ap.add_argument("--pref_k", type=int, default=2, help="passages taken from --pref_index")
     # post-processing
     ap.add_argument("--tool_use", action="store_true", help="run <tool>name(args)</tool> calls in the output")
     ap.add_argument("--emit_cert", action="store_true", help="print a proof-carrying answer record (JSON)")
@@ -663,10 +666,16 @@ def main(argv=None):
     model = build_model(cfg, device=a.device)
     if a.ckpt:
         maybe_load_checkpoint(model, a.ckpt)
+    if a.pref_lora:
+        from ..training.preference_expert import load_preference_lora
+        load_preference_lora(model, a.pref_lora)
     tok = get_tokenizer(cfg.vocab_size)
     passages = []
     if a.retrieve_path:
         passages = retrieve_passages(a.retrieve_path, a.prompt, a.retrieve_k, a.retrieve_chunk, a.retrieve_stride)
+    if a.pref_index:
+        from ..retrieval.pq import PQRetriever
+        passages += [d for _, _, d in PQRetriever.load(a.pref_index).search(a.prompt, a.pref_k)]
     context = ""
     if a.retrieve_prepend and passages:
         context = "\n".join(passages)[:a.retrieve_max_chars] + "\n"

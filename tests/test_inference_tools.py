@@ -487,3 +487,37 @@ def test_tool_fabric():
     assert len(errors) == 1 and "talk.wav" in errors[0] and "OSError" in errors[0]
     ctx, state, _ = analyze_inputs("cat.png", modes="audio", detect=detect)
     assert state.facts == [] and ctx == ""
+
+
+def test_preference_expert_adapters_and_index(tmp_path):
+    from omnicoder.config import ModelConfig
+    from omnicoder.models.lm import build_model
+    from omnicoder.training.preference_expert import (load_preference_lora, main, read_texts, token_windows,
+                                                      train_preference_lora)
+    from omnicoder.training.tokenizer import get_tokenizer
+    d = tmp_path / "notes"
+    d.mkdir()
+    for i, t in enumerate(["I prefer tabs over spaces in Makefiles.", "My favourite language is Rust.",
+                           "Always answer in British English, please."]):
+        (d / f"n{i}.txt").write_text(t)
+    texts = read_texts(str(d))
+    assert len(texts) == 3
+    cfg = ModelConfig(name="pe", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=64)
+    model = build_model(cfg, "cpu", dtype=torch.float32, seed=0)
+    w = token_windows(texts, get_tokenizer(300), 16)
+    assert w.shape[1] == 17
+    base = {k: v.clone() for k, v in model.state_dict().items()}
+    losses = train_preference_lora(model, w, steps=100, batch=4, lr=1e-2)
+    assert sum(losses[-5:]) / 5 < 0.9 * losses[0]
+    # only adapters trained: the frozen weights did not move
+    sd = model.state_dict()
+    assert all(torch.equal(sd[k], v) for k, v in base.items() if k in sd)
+    out = tmp_path / "pref"
+    assert main(["--data", str(d), "--preset", "tiny_moe", "--steps", "1", "--seq_len", "16", "--out_dir", str(out),
+                 "--device", "cpu"]) == 0
+    fresh = build_model(cfg.__class__.from_dict(__import__("omnicoder.config", fromlist=["get_preset"])
+                                                .get_preset("tiny_moe").to_dict()), "cpu", dtype=torch.float32)
+    assert load_preference_lora(fresh, str(out / "pref_lora.pt")) > 0
+    from omnicoder.inference.generate import main as gen_main
+    gen_main(["--preset", "tiny_moe", "--prompt", "which language", "--max_new_tokens", "2", "--device", "cpu",
+              "--pref_lora", str(out / "pref_lora.pt"), "--pref_index", str(out / "index"), "--no_cuda_graph"])
