@@ -105,6 +105,21 @@ class PagingConfig:
     max_pages_ram: int
     prefetch_ahead: int = 1
 
+    @classmethod
+    def from_sidecars(cls, paging_json: str, prefetch_json: str | None = None,
+                      prefetch_ahead: int = 1) -> "PagingConfig":
+        """From the exporter's `.kv_paging.json` (page_len, n_layers) and a prefetch sidecar
+        {"keep_pages": k}: k resident pages per layer (default 2)."""
+        import json
+        with open(paging_json) as f:
+            pg = json.load(f)
+        keep = 2
+        if prefetch_json:
+            with open(prefetch_json) as f:
+                keep = max(1, int(json.load(f).get("keep_pages", keep)))
+        L = int(pg["n_layers"])
+        return cls(n_layers=L, page_len=int(pg["page_len"]), max_pages_ram=keep * L, prefetch_ahead=prefetch_ahead)
+
 
 class LRUKVPager:
     """Pages keyed (layer, position // page_len) in an LRU of `max_pages_ram`

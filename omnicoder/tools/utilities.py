@@ -30,6 +30,8 @@ Each subcommand is the counterpart of one of the reference's single-purpose scri
   kv-autoencoder    a linear autoencoder of the dumped rows (closed-form PCA or AdamW) and its
                     sidecar                                                   (kv_autoencoder_train.py)
   kv-retention      the window / compressive-slot retention sidecar          (kv_retention_write.py)
+  kv-prefetch       the pages-kept sidecar of the paged decode runner, capped at half the pages of a
+                    paging sidecar                                           (kv_prefetch_write.py)
   code-verify       a solution against a pytest file in the sandbox, with pass / fail counts
                                                                   (code_verifier.py:1-97)
   auto-tune         the speculative draft length that maximises expected throughput, from a measured
@@ -833,6 +835,22 @@ def _cmd_kv_autoencoder(a) -> int:
     return 0
 
 
+def kv_prefetch(keep_pages: int, paging: dict | None = None) -> dict:
+    keep = max(1, int(keep_pages))
+    if paging:
+        total = int(paging.get("total_pages", 0)) or int(paging.get("pages_per_layer", 0))
+        if total > 0:
+            keep = max(1, min(keep, total // 2))
+    return {"keep_pages": keep}
+
+
+def _cmd_kv_prefetch(a) -> int:
+    out = kv_prefetch(a.keep_pages, _read_json(a.kv_paging_sidecar) if a.kv_paging_sidecar else None)
+    _write_json(a.out, out)
+    print(json.dumps(out))
+    return 0
+
+
 def _cmd_kv_retention(a) -> int:
     blob = {"compressive_slots": a.compressive_slots, "window_size": a.window_size, "schema": 1}
     _write_json(a.out, blob)
@@ -1172,6 +1190,12 @@ def _parser() -> argparse.ArgumentParser:
     p.add_argument("--out_pt", default="weights/kv_autoencoder.pt")
     p.add_argument("--out_json", default="weights/kv_compress_sidecar.json")
     p.set_defaults(fn=_cmd_kv_autoencoder)
+
+    p = sub.add_parser("kv-prefetch", help="write the KV prefetch (pages kept) sidecar")
+    p.add_argument("--out", default="weights/kv_prefetch.json")
+    p.add_argument("--keep_pages", type=int, default=2)
+    p.add_argument("--kv_paging_sidecar", default="")
+    p.set_defaults(fn=_cmd_kv_prefetch)
 
     p = sub.add_parser("kv-retention", help="write the KV retention sidecar")
     p.add_argument("--out", required=True)

@@ -338,3 +338,19 @@ def test_write_threshold(tmp_path):
     assert _cli(["write-threshold", "--marks", str(f), "--preset", "p1", "--out", str(out)]) == 0
     d = json.loads(out.read_text())
     assert d["other"] == 0.3 and abs(d["p1"] - r["threshold"]) < 1e-12
+
+
+def test_kv_prefetch_sidecar_and_pager(tmp_path):
+    from omnicoder.config import get_preset
+    from omnicoder.export.onnx_export import write_sidecars
+    from omnicoder.inference.runtimes import LRUKVPager, PagingConfig
+    from omnicoder.models.lm import build_model
+    model = build_model(get_preset("tiny_moe"), dtype=torch.float32).eval()
+    paging = write_sidecars(model, str(tmp_path / "ds.onnx"), max_len=512, kv_page_len=128)[0]
+    out = tmp_path / "pf.json"
+    assert _cli(["kv-prefetch", "--out", str(out), "--keep_pages", "8", "--kv_paging_sidecar", paging]) == 0
+    assert json.loads(out.read_text()) == {"keep_pages": 2}           # 4 pages per layer -> at most half
+    assert U.kv_prefetch(3, {"total_pages": 100}) == {"keep_pages": 3}
+    cfg = PagingConfig.from_sidecars(paging, str(out))
+    assert (cfg.page_len, cfg.n_layers, cfg.max_pages_ram) == (128, model.cfg.n_layers, 2 * model.cfg.n_layers)
+    assert LRUKVPager(cfg) is not None
