@@ -103,3 +103,19 @@ def test_moe_inference_path_matches_training_path(cuda_ext, T):
     xg = x.clone().requires_grad_(True)
     y_tr, _ = moe_ffn(xg, rw, w13, w2, k)
     assert _rel(y_inf, y_tr.detach()) < 2e-2
+
+
+@pytest.mark.gpu
+def test_few_row_library_route(cuda_ext):
+    """Plain few-row projections (decode steps) on the library GEMM, with and without the residual,
+    against the fp32 product; more rows stay on the tcgen05 kernels."""
+    from omnicoder.ops import gemm as G
+    assert G.FEW_ROW_LIBRARY_MAX >= 64
+    torch.manual_seed(0)
+    for M in (1, 37, 64):
+        x = torch.randn(M, 2048, device="cuda").to(torch.bfloat16)
+        w = (0.02 * torch.randn(576, 2048, device="cuda")).to(torch.bfloat16)
+        r = torch.randn(M, 576, device="cuda").to(torch.bfloat16)
+        ref = x.float() @ w.float().t()
+        assert (G.mm_nt(x, w).float() - ref).abs().max() / ref.abs().max() < 1e-2
+        assert (G.mm_nt(x, w, residual=r).float() - (ref + r.float())).abs().max() / ref.abs().max() < 2e-2
