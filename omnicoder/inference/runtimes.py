@@ -202,6 +202,22 @@ class DecodeRunner:
         self.kv_quant, self.group, self.pager = kv_quant, group, pager
         self.logit_bias, self.bias_alpha = logit_bias or {}, bias_alpha
 
+    @classmethod
+    def from_sidecars(cls, session, model_path: str, prefetch_json: str | None = None, **kw) -> "DecodeRunner":
+        """A runner configured by the sidecars the exporter wrote beside `model_path`: `.kvq.json`
+        (cache format and group) and `.kv_paging.json` (+ an optional prefetch sidecar) for the pager."""
+        import json
+        import os
+        base = model_path[:-5] if model_path.endswith(".onnx") else model_path
+        kvq, group, pager = None, 64, None
+        if os.path.exists(base + ".kvq.json"):
+            with open(base + ".kvq.json") as f:
+                meta = json.load(f)
+            kvq, group = meta["scheme"], int(meta.get("group", 64))
+        if os.path.exists(base + ".kv_paging.json"):
+            pager = LRUKVPager(PagingConfig.from_sidecars(base + ".kv_paging.json", prefetch_json))
+        return cls(session, kv_quant=kvq, group=group, pager=pager, **kw)
+
     def _zeros(self, batch: int) -> list[np.ndarray]:
         out = []
         for _, _, shape in self.layers:

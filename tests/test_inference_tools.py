@@ -521,3 +521,21 @@ def test_preference_expert_adapters_and_index(tmp_path):
     from omnicoder.inference.generate import main as gen_main
     gen_main(["--preset", "tiny_moe", "--prompt", "which language", "--max_new_tokens", "2", "--device", "cpu",
               "--pref_lora", str(out / "pref_lora.pt"), "--pref_index", str(out / "index"), "--no_cuda_graph"])
+
+
+def test_decode_runner_from_sidecars(tmp_path):
+    import json
+
+    import numpy as np
+    from omnicoder.export.onnx_export import write_sidecars
+    from omnicoder.inference.runtimes import DecodeRunner, TorchStepSession
+    cfg, m = _tiny()
+    path = str(tmp_path / "ds.onnx")
+    write_sidecars(m, path, max_len=32, kv_page_len=8, kvq="u8", kvq_group=16)
+    (tmp_path / "pf.json").write_text(json.dumps({"keep_pages": 1}))
+    r = DecodeRunner.from_sidecars(TorchStepSession(m, max_len=32), path, str(tmp_path / "pf.json"))
+    assert r.kv_quant == "u8" and r.group == 16 and r.pager.cfg.max_pages_ram == cfg.n_layers
+    out = r.generate(np.array([[4, 9, 17, 3]]), 4)
+    assert out.shape == (1, 8) and r.pager.stats()["hits"] + r.pager.stats()["misses"] > 0
+    plain = DecodeRunner.from_sidecars(TorchStepSession(m, max_len=32), str(tmp_path / "none.onnx"))
+    assert plain.kv_quant is None and plain.pager is None
