@@ -199,3 +199,23 @@ def test_run_training_probe_sizes_the_plan(tmp_path):
     out = _run(["omnicoder.tools.run_training", "--stages", "pre_align", "--out_dir", str(tmp_path / "r"),
                 "--probe_json", str(tmp_path / "train_probe_summary.json"), "--dry_run"])
     assert "omnicoder.training.pre_align" in out
+
+
+def test_prepare_data_feeds_the_trainers(tmp_path):
+    """Generated workspace data runs through the VQA / unified trainers, the code verifier and the
+    write-threshold tool; a rerun writes nothing."""
+    from omnicoder.sfb.sandbox import verify_with_tests
+    from omnicoder.tools.prepare_data import prepare
+    from omnicoder.tools.utilities import main as tools_main
+    from omnicoder.training import vl_tasks
+    root = tmp_path / "data"
+    r = prepare(str(root))
+    assert len(r["written"]) > 10 and prepare(str(root))["written"] == []
+    task = json.loads((root / "code" / "tasks.jsonl").read_text().splitlines()[2])
+    assert verify_with_tests(task["target"], task["tests"]).ok
+    assert vl_tasks.main(["--task", "vqa", "--jsonl", str(root / "vl" / "vqa.jsonl"), "--image_size", "32",
+                          "--steps", "1", "--batch", "2", "--device", "cpu", "--out", str(tmp_path / "v.pt")]) == 0
+    assert vl_tasks.main(["--task", "unified", "--jsonl", str(root / "unified.jsonl"), "--image_size", "32",
+                          "--steps", "2", "--batch", "2", "--device", "cpu", "--out", str(tmp_path / "u.pt")]) == 0
+    assert tools_main(["write-threshold", "--marks", str(root / "marks.jsonl"), "--out",
+                       str(tmp_path / "thr.json")]) == 0
