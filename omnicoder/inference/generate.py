@@ -607,7 +607,8 @@ def main(argv=None):
     ap.add_argument("--retrieval_bias_alpha", type=float, default=0.0)
     ap.add_argument("--sfb", action="store_true", help="structured factor bias from the factorised prompt")
     ap.add_argument("--sfb_alpha", type=float, default=1.0)
-    ap.add_argument("--adaptive_moe", action="store_true", help="confidence-driven routed experts per token")
+    ap.add_argument("--adaptive_moe", "--adaptive_gating", dest="adaptive_moe", action="store_true",
+                    help="confidence-driven routed experts per token")
     ap.add_argument("--adaptive_top_k_min", type=int, default=1)
     ap.add_argument("--adaptive_top_k_max", type=int, default=4)
     ap.add_argument("--adaptive_conf_floor", type=float, default=0.3)
@@ -642,8 +643,26 @@ def main(argv=None):
     ap.add_argument("--retrieve_max_chars", type=int, default=2000, help="retrieved characters put in the prompt")
     ap.add_argument("--retrieve_prepend", action="store_true", help="put the retrieved passages before the prompt")
     ap.add_argument("--pref_lora", default=None, help="preference-expert LoRA adapters to load onto the model")
-    ap.add_argument("--pref_index", default=None, help="preference-expert retrieval index (a saved PQ index)")
-    ap.add_argument("--pref_k", type=int, default=2, help="passages taken from --pref_index")
+    ap.add_argument("--pref_index", "--pref_rag_index", dest="pref_index", default=None,
+                    help="preference-expert retrieval index (a saved PQ index)")
+    ap.add_argument("--pref_k", "--pref_rag_topk", dest="pref_k", type=int, default=2,
+                    help="passages taken from --pref_index")
+    ap.add_argument("--pref_rag_alpha", type=float, default=None,
+                    help="retrieval-bias strength of the preference passages (sets --retrieval_bias_alpha)")
+    ap.add_argument("--pref_lora_r", type=int, default=None, help="expected adapter rank (checked against the file)")
+    ap.add_argument("--pref_lora_alpha", type=int, default=None, help="expected adapter alpha (checked)")
+    ap.add_argument("--pref_lora_dropout", type=float, default=0.0, help="accepted; adapters run without dropout")
+    ap.add_argument("--retrieve_pq_index", default=None, help="a saved PQ index (pq-build) to retrieve from")
+    ap.add_argument("--multi_index_root", default=None,
+                    help="folder of saved PQ indexes: each is searched and the best passages merged")
+    ap.add_argument("--mi_topk", type=int, default=3, help="passages kept from --multi_index_root")
+    ap.add_argument("--mi_alpha", type=float, default=None,
+                    help="retrieval-bias strength of the multi-index passages (sets --retrieval_bias_alpha)")
+    ap.add_argument("--retrieve_budget_bytes", type=int, default=0,
+                    help="cap the retrieved passages at this many UTF-8 bytes (0: no cap)")
+    ap.add_argument("--retrieve_faiss", default=None, help="not available: FAISS is not installed (use pq-build)")
+    ap.add_argument("--retrieve_partition", default=None, help="not available (use --multi_index_root)")
+    ap.add_argument("--compile", action="store_true", help="not used: decode steps replay CUDA graphs instead")
     # post-processing
     ap.add_argument("--tool_use", action="store_true", help="run <tool>name(args)</tool> calls in the output")
     ap.add_argument("--emit_cert", action="store_true", help="print a proof-carrying answer record (JSON)")
@@ -666,16 +685,51 @@ def main(argv=None):
     model = build_model(cfg, device=a.device)
     if a.ckpt:
         maybe_load_checkpoint(model, a.ckpt)
+    for flag in ("retrieve_faiss", "retrieve_partition"):
+        if getattr(a, flag):
+            raise SystemExit(f"--{flag} is not available here: FAISS is not installed; build a PQ index with "
+                             f"`python -m omnicoder.tools.utilities pq-build` and pass --retrieve_pq_index")
+    if a.compile:
+        print("[generate] --compile has no effect: decode steps are captured as CUDA graphs", file=sys.stderr)
     if a.pref_lora:
         from ..training.preference_expert import load_preference_lora
+        if a.pref_lora_r is not None or a.pref_lora_alpha is not None:
+            meta = torch.load(a.pref_lora, map_location="cpu", weights_only=True)
+            for key, want in (("r", a.pref_lora_r), ("alpha", a.pref_lora_alpha)):
+                if want is not None and int(meta[key]) != want:
+                    raise SystemExit(f"--pref_lora_{key} {want} does not match the adapters ({meta[key]})")
         load_preference_lora(model, a.pref_lora)
+    for alpha in (a.pref_rag_alpha, a.mi_alpha):
+        if alpha is not None:
+            a.retrieval_bias_alpha = alpha
     tok = get_tokenizer(cfg.vocab_size)
     passages = []
     if a.retrieve_path:
         passages = retrieve_passages(a.retrieve_path, a.prompt, a.retrieve_k, a.retrieve_chunk, a.retrieve_stride)
-    if a.pref_index:
+    if a.pref_index or a.retrieve_pq_index or a.multi_index_root:
         from ..retrieval.pq import PQRetriever
-        passages += [d for _, _, d in PQRetriever.load(a.pref_index).search(a.prompt, a.pref_k)]
+        if a.pref_index:
+            passages += [d for _, _, d in PQRetriever.load(a.pref_index).search(a.prompt, a.pref_k)]
+        if a.retrieve_pq_index:
+            passages += [d for _, _, d in PQRetriever.load(a.retrieve_pq_index).search(a.prompt, a.retrieve_k)]
+        if a.multi_index_root:
+            import os
+            hits = []
+            for d in sorted(os.listdir(a.multi_index_root)):
+                sub = os.path.join(a.multi_index_root, d)
+                if os.path.exists(os.path.join(sub, "pq.json")):
+                    # distances of different indexes are comparable: unit-norm vectors in each
+                    hits += [(dist, doc) for _, dist, doc in PQRetriever.load(sub).search(a.prompt, a.mi_topk)]
+            passages += [doc for _, doc in sorted(hits, key=lambda t: t[0])[:a.mi_topk]]
+    if a.retrieve_budget_bytes > 0:
+        kept, used = [], 0
+        for ptxt in passages:
+            b = len(ptxt.encode("utf-8"))
+            if used + b > a.retrieve_budget_bytes:
+                break
+            kept.append(ptxt)
+            used += b
+        passages = kept
     context = ""
     if a.retrieve_prepend and passages:
         context = "\n".join(passages)[:a.retrieve_max_chars] + "\n"
@@ -715,7 +769,7 @@ def main(argv=None):
     if a.tool_use:
         from .tools import ToolRegistry
         text = ToolRegistry().run_calls(text)
-    result = {"text": text, "stats": st.as_dict()}
+    result = {"text": text, "stats": st.as_dict(), "retrieved_passages": len(passages)}
     if a.emit_cert:
         from ..reasoning.omega import infer_goals, pack_certificate, text_margin
         cert = pack_certificate(text, infer_goals(a.prompt), {"text": text_margin(text, " ".join(passages) or None)})

@@ -539,3 +539,32 @@ def test_decode_runner_from_sidecars(tmp_path):
     assert out.shape == (1, 8) and r.pager.stats()["hits"] + r.pager.stats()["misses"] > 0
     plain = DecodeRunner.from_sidecars(TorchStepSession(m, max_len=32), str(tmp_path / "none.onnx"))
     assert plain.kv_quant is None and plain.pager is None
+
+
+def test_generate_cli_reference_flags(tmp_path, capsys):
+    """The reference's generate flags that map onto this package: aliases, saved-index retrieval,
+    multi-index search with a byte budget; FAISS-only flags fail with a clear message."""
+    import json
+
+    import pytest
+    from omnicoder.inference.generate import main as gen_main
+    from omnicoder.tools.utilities import main as tools_main
+    for name, topic in (("a", "cuda kernels and tensor cores"), ("b", "python lists and loops")):
+        d = tmp_path / "docs" / name
+        d.mkdir(parents=True)
+        for i in range(4):
+            (d / f"{i}.txt").write_text(f"{topic} note number {i} " * 3)
+        assert tools_main(["pq-build", str(d), str(tmp_path / "idx" / name), "--m", "2", "--ks", "2",
+                           "--dim", "8"]) == 0
+    base = ["--preset", "tiny_moe", "--prompt", "tensor cores", "--max_new_tokens", "1", "--device", "cpu",
+            "--no_cuda_graph", "--json"]
+    capsys.readouterr()
+    gen_main(base + ["--multi_index_root", str(tmp_path / "idx"), "--mi_topk", "3", "--adaptive_gating",
+                     "--retrieve_pq_index", str(tmp_path / "idx" / "a"), "--retrieve_k", "2"])
+    got = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert got["retrieved_passages"] == 5
+    gen_main(base + ["--multi_index_root", str(tmp_path / "idx"), "--retrieve_budget_bytes", "300"])
+    got = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert got["retrieved_passages"] == 2                              # two 132-byte passages fit in 300
+    with pytest.raises(SystemExit):
+        gen_main(base + ["--retrieve_faiss", "x"])
