@@ -235,7 +235,7 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
              adaptive_conf_floor: float = 0.3, adaptive_layer_ramp: bool = False, adaptive_layer_power: float = 1.0,
              early_exit: bool = False, early_exit_entropy: float = 0.0, early_exit_mode: str = "entropy",
              verify_threshold: float = 0.0, compress_kv_slots: int = 0, prefix_embeds: torch.Tensor | None = None,
-             scmoe_alpha: float = 0.0, scmoe_topk: int = 1, scmoe_frac: float = 1.0):
+             scmoe_alpha: float = 0.0, scmoe_topk: int = 1, scmoe_frac: float = 1.0, mtp_draft: bool = False):
     """Generate `max_new_tokens` tokens after `input_ids` [B, S] (or [S]).  Returns
     [B, S + max_new_tokens] (and GenStats with return_stats).  On CUDA the
     decode step is captured once as a CUDA graph (`cuda_graph=False` runs it
@@ -300,14 +300,19 @@ def generate(model, input_ids: torch.Tensor, max_new_tokens: int, temperature: f
         addons.sfb_alpha = float(sfb_alpha)
     if scmoe_alpha > 0 and adaptive_moe:
         raise ValueError("scmoe and adaptive_moe both set the routed-expert count: use one")
-    if draft_model is not None and speculative_draft_len > 0:
+    if (draft_model is not None or mtp_draft) and speculative_draft_len > 0:
         if repetition_penalty != 1.0 or presence_penalty or frequency_penalty or logit_bias or addons.active \
                 or adaptive_moe or scmoe_alpha > 0:
             raise ValueError("speculative decoding samples from the unmodified target distribution: "
                              "penalties, logit_bias and the logit add-ons are not applied there")
-        out = _speculative(model, draft_model, ids, max_new_tokens, speculative_draft_len, temperature, top_k, top_p,
-                           kv_dtype, L, gen, stats, eos_id, early_exit=(early_exit_mode, early_exit_entropy)
-                           if early_exit else None, verify_threshold=verify_threshold, prefix_embeds=prefix_embeds)
+        if draft_model is None:
+            out = _speculative_mtp(model, ids, max_new_tokens, speculative_draft_len, temperature, top_k, top_p,
+                                   kv_dtype, L, gen, stats)
+        else:
+            out = _speculative(model, draft_model, ids, max_new_tokens, speculative_draft_len, temperature, top_k,
+                               top_p, kv_dtype, L, gen, stats, eos_id, early_exit=(early_exit_mode,
+                               early_exit_entropy) if early_exit else None, verify_threshold=verify_threshold,
+                               prefix_embeds=prefix_embeds)
     else:
         cache = KVCache(cfg, B, L, dev, dtype=model.embed.dtype, kv_dtype=kv_dtype)
         t0 = time.perf_counter()
@@ -567,6 +572,87 @@ def _speculative(target, draft, ids, max_new, k, temperature, top_k, top_p, kv_d
     return torch.cat([ids, out], dim=1)
 
 
+def _speculative_mtp(target, ids, max_new, k, temperature, top_k, top_p, kv_dtype, L, gen, stats):
+    """Self-speculative decoding from the target's multi-token-prediction heads (the reference's
+    --multi_token_heads lookahead, src/omnicoder/inference/generate.py:3970).  The final hidden state h
+    at the position that produced `last` gives, through MTP head j, a proposal for the token j + 1
+    places after `last` (the heads are trained that way: head j at position t predicts token
+    t + 2 + j).  The k proposals (k <= number of MTP heads) are verified with one target forward of
+    [last, d_1 .. d_k] exactly as a draft model's would be (rejection sampling, or equality when
+    greedy), and the hidden state at the position that produced the next token feeds the next round's
+    proposals; the cache is rolled back per sequence to the accepted length."""
+    from ..ops.layers import linear
+    from ..ops.spec import spec_verify
+    heads = list(target.mtp_heads)
+    if not heads:
+        raise ValueError("self-speculative decoding needs a model with MTP heads (cfg.mtp_heads > 0)")
+    k = min(k, len(heads))
+    B, S = ids.shape
+    dev = ids.device
+    tcache = KVCache(target.cfg, B, L, dev, dtype=target.embed.dtype, kv_dtype=kv_dtype)
+    t0 = time.perf_counter()
+    produced = [[] for _ in range(B)]
+    if S > 1:
+        _, h = target.forward_cached(ids[:, :-1], tcache, prefill=True, last_only=True, return_hidden=True)
+        h = h[:, -1]
+        last = ids[:, -1]
+    else:                                             # no prompt context yet: one plain step first
+        tl, h = target.forward_cached(ids, tcache, prefill=True, last_only=True, return_hidden=True)
+        pt = sampling_probs(tl[:, -1], temperature, top_k, top_p)
+        last = pt.argmax(-1) if temperature <= 0 else torch.multinomial(pt, 1, generator=gen).squeeze(1)
+        h = h[:, -1]
+        for b, e in enumerate(last.tolist()):
+            produced[b].append(e)
+    _sync(last)
+    stats.prefill_s = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    ar = torch.arange(B, device=dev)
+    while min(len(p) for p in produced) < max_new:
+        ts = time.perf_counter()
+        base_t = tcache.lengths.clone()
+        d_tok, d_prob = [], []
+        for j in range(k):
+            pd = sampling_probs(linear(h, heads[j]).float(), temperature, top_k, top_p)
+            d_tok.append(pd.argmax(-1) if temperature <= 0 else torch.multinomial(pd, 1, generator=gen).squeeze(1))
+            d_prob.append(pd)
+        d_tok_t = torch.stack(d_tok, dim=1)                                  # [B, k]
+        pd_all = torch.stack(d_prob, dim=1)                                  # [B, k, V]
+        tl, th = target.forward_cached(torch.cat([last[:, None], d_tok_t], 1), tcache, return_hidden=True)
+        if temperature <= 0 or ((not top_k or top_k <= 0) and (top_p is None or top_p >= 1.0)):
+            u = torch.rand(B, k + 1, device=dev, generator=gen) if temperature > 0 else None
+            n_acc, extra, new_len = spec_verify(tl, pd_all if temperature > 0 else None, d_tok_t, u, base_t,
+                                                temperature)
+        else:
+            pt = sampling_probs(tl, temperature, top_k, top_p)
+            pt_d = pt[:, :k].gather(-1, d_tok_t[..., None]).squeeze(-1)
+            pd_d = pd_all.gather(-1, d_tok_t[..., None]).squeeze(-1)
+            acc = torch.rand(B, k, device=dev, generator=gen) < torch.clamp(pt_d / pd_d.clamp_min(1e-20), max=1.0)
+            n_acc = torch.cumprod(acc.int(), dim=1).sum(1)
+            p_next = pt[ar, n_acc]
+            resid = torch.clamp(p_next - torch.cat([pd_all, torch.zeros_like(pd_all[:, :1])], 1)[ar, n_acc], min=0)
+            q = torch.where((n_acc < k)[:, None], resid, p_next)
+            q = q / q.sum(-1, keepdim=True).clamp_min(1e-20)
+            extra = torch.multinomial(q, 1, generator=gen).squeeze(1)
+            new_len = base_t + n_acc + 1
+        done = torch.tensor([len(p) >= max_new for p in produced], device=dev)
+        tcache.rollback(torch.where(done, base_t, new_len.to(base_t.dtype)))
+        n_list, d_list, e_list = n_acc.tolist(), d_tok_t.tolist(), extra.tolist()
+        for b in range(B):
+            if len(produced[b]) < max_new:
+                produced[b].extend(d_list[b][:n_list[b]] + [e_list[b]])
+        stats.accepted_draft_tokens += int(sum(n_list))
+        stats.proposed_draft_tokens += B * k
+        stats.steps += 1
+        h = th[ar, n_acc.long()]                    # the hidden state that produced `extra`
+        last = extra
+        _sync(last)
+        stats.step_times_s.append(time.perf_counter() - ts)
+    stats.decode_s = time.perf_counter() - t1
+    stats.new_tokens = B * max_new
+    out = torch.tensor([p[:max_new] for p in produced], device=dev, dtype=ids.dtype)
+    return torch.cat([ids, out], dim=1)
+
+
 # ----------------------------------------------------------------------------
 # CLI (python -m omnicoder.inference.generate)
 # ----------------------------------------------------------------------------
@@ -631,6 +717,9 @@ def main(argv=None):
     ap.add_argument("--target_ctx", type=int, default=0,
                     help="extend the context to this length (RoPE position interpolation)")
     ap.add_argument("--disable_speculative", action="store_true")
+    ap.add_argument("--multi_token_heads", type=int, default=0,
+                    help="build the model with this many prediction heads (main + MTP); with > 1 and no draft "
+                         "model, decoding drafts from the MTP heads (self-speculative)")
     # prompt
     ap.add_argument("--system_prompt", default="")
     ap.add_argument("--prompt_template", default="{system}{prompt}",
@@ -670,6 +759,8 @@ def main(argv=None):
                     help="with --emit_cert: abstain when the verification margin is below this")
     a = ap.parse_args(argv)
     cfg = get_preset(a.mobile_preset or a.preset)
+    if a.multi_token_heads > 1:
+        cfg.mtp_heads = a.multi_token_heads - 1
     if a.rope_scale is not None:
         cfg.attn.rope_scale = a.rope_scale
     if a.rope_base is not None:
@@ -754,7 +845,9 @@ def main(argv=None):
                        repetition_penalty=a.repetition_penalty, presence_penalty=a.presence_penalty,
                        frequency_penalty=a.frequency_penalty,
                        logit_bias=load_logit_bias(a.logit_bias_file) if a.logit_bias_file else None,
-                       speculative_draft_len=a.speculative_draft_len, kvq=a.kvq, window_size=a.window_size,
+                       speculative_draft_len=(a.speculative_draft_len or max(0, a.multi_token_heads - 1))
+                       if not a.disable_speculative else 0,
+                       mtp_draft=a.multi_token_heads > 1 and draft is None, kvq=a.kvq, window_size=a.window_size,
                        return_stats=True, seed=a.seed, eos_id=a.eos_id, cuda_graph=not a.no_cuda_graph,
                        penalty_window=a.penalty_window, knn_cache=knn, knn_k=a.knn_k, knn_lambda=a.knn_lambda,
                        retrieved_texts=texts, retrieval_bias_alpha=a.retrieval_bias_alpha, encode_fn=tok.encode,

@@ -568,3 +568,24 @@ def test_generate_cli_reference_flags(tmp_path, capsys):
     assert got["retrieved_passages"] == 2                              # two 132-byte passages fit in 300
     with pytest.raises(SystemExit):
         gen_main(base + ["--retrieve_faiss", "x"])
+
+
+def test_mtp_self_speculative_decoding_is_exact():
+    """Drafts from the MTP heads, verified by the model itself: greedy output equals plain greedy decoding
+    for prompts of one and several tokens; sampled decoding runs and counts its proposals."""
+    from omnicoder.config import ModelConfig
+    from omnicoder.inference.generate import generate
+    from omnicoder.models.lm import build_model
+    cfg = ModelConfig(name="mtp", vocab_size=300, d_model=64, n_layers=2, n_heads=4, ffn_dim=128, max_seq_len=128,
+                      mtp_heads=3)
+    m = build_model(cfg, "cpu", dtype=torch.float32, seed=0).eval()
+    for prompt in (torch.tensor([[5]]), torch.tensor([[4, 9, 17, 3], [7, 7, 8, 1]])):
+        want = generate(m, prompt, 12, temperature=0.0)
+        got, st = generate(m, prompt, 12, temperature=0.0, speculative_draft_len=3, mtp_draft=True, return_stats=True)
+        assert torch.equal(got, want) and st.proposed_draft_tokens > 0
+    out, st = generate(m, torch.tensor([[4, 9, 17, 3]]), 8, temperature=0.9, speculative_draft_len=2,
+                       mtp_draft=True, return_stats=True, seed=1)
+    assert out.shape == (1, 12) and st.proposed_draft_tokens >= 2
+    from omnicoder.inference.generate import main as gen_main
+    gen_main(["--preset", "tiny_moe", "--prompt", "hi", "--max_new_tokens", "3", "--device", "cpu",
+              "--no_cuda_graph", "--multi_token_heads", "3"])
