@@ -59,3 +59,22 @@ def test_verify_kernel_matches_restatement(cuda_ext):
         assert torch.equal(got[2].cpu(), ref[2]), temp
         same = (got[1].cpu() == ref[1]).float().mean().item()
         assert same == 1.0 if temp == 0 else same >= 0.98, (temp, same)
+
+
+@pytest.mark.gpu
+def test_mtp_self_speculative_on_gpu(cuda_ext):
+    """Self-speculative decoding from the MTP heads on the device (verify kernel, few-row projections):
+    greedy output equals plain greedy decoding."""
+    from omnicoder.config import AttentionConfig, ModelConfig, MoEConfig
+    from omnicoder.inference.generate import generate
+    from omnicoder.models.lm import build_model
+    cfg = ModelConfig(name="mtp_gpu", vocab_size=4096, d_model=512, n_layers=2, n_heads=4, ffn_dim=512,
+                      max_seq_len=512, mtp_heads=3,
+                      attn=AttentionConfig(kind="mla", kv_lora_rank=256, qk_rope_dim=64, qk_nope_dim=128,
+                                           v_head_dim=128),
+                      moe=MoEConfig(n_experts=8, top_k=2, ffn_dim=256, n_shared_experts=1))
+    m = build_model(cfg, device="cuda", seed=0).eval()
+    prompt = torch.randint(1, 4096, (4, 16), generator=torch.Generator().manual_seed(0)).cuda()
+    want = generate(m, prompt, 24, temperature=0.0)
+    got, st = generate(m, prompt, 24, temperature=0.0, speculative_draft_len=3, mtp_draft=True, return_stats=True)
+    assert torch.equal(got, want) and st.proposed_draft_tokens > 0
