@@ -717,6 +717,12 @@ def main(argv=None):
     ap.add_argument("--target_ctx", type=int, default=0,
                     help="extend the context to this length (RoPE position interpolation)")
     ap.add_argument("--disable_speculative", action="store_true")
+    ap.add_argument("--reasoner", default="none", choices=["none", "tot", "omega"],
+                    help="tot: a tree-of-thoughts MCTS over the next tokens picks the opening of the answer; "
+                         "omega: attach the verification certificate (as --emit_cert)")
+    ap.add_argument("--tree_depth", type=int, default=3, help="tokens chosen by the tree search")
+    ap.add_argument("--tree_width", type=int, default=3, help="next tokens expanded per node")
+    ap.add_argument("--tree_iterations", type=int, default=24)
     ap.add_argument("--multi_token_heads", type=int, default=0,
                     help="build the model with this many prediction heads (main + MTP); with > 1 and no draft "
                          "model, decoding drafts from the MTP heads (self-speculative)")
@@ -826,6 +832,16 @@ def main(argv=None):
         context = "\n".join(passages)[:a.retrieve_max_chars] + "\n"
     prompt_text = context + a.prompt_template.format(system=a.system_prompt, prompt=a.prompt)
     ids = torch.tensor([tok.encode(prompt_text)], device=a.device)
+    if a.reasoner == "omega":
+        a.emit_cert = True
+    tree_ids = []
+    if a.reasoner == "tot" and a.tree_depth > 0:
+        from ..reasoning.lm_search import LMToTMCTS, ToTConfig
+        search = LMToTMCTS(model.eval(), tok, ToTConfig(branch=a.tree_width, max_depth=a.tree_depth,
+                                                        iterations=a.tree_iterations))
+        tree_ids, _ = search.search(prompt_text)
+        ids = torch.cat([ids, torch.tensor([tree_ids], device=a.device, dtype=ids.dtype)], 1)
+        a.max_new_tokens = max(1, a.max_new_tokens - len(tree_ids))
     draft = None
     if a.draft_preset:
         draft = build_model(get_preset(a.draft_preset), device=a.device)
@@ -858,7 +874,7 @@ def main(argv=None):
                        early_exit_mode=a.early_exit_mode, verify_threshold=a.verify_threshold,
                        compress_kv_slots=a.compress_kv_slots, adaptive_layer_power=a.adaptive_layer_power,
                        scmoe_alpha=a.scmoe_alpha, scmoe_topk=a.scmoe_topk, scmoe_frac=a.scmoe_frac)
-    text = tok.decode(out[0, ids.shape[1]:].tolist())
+    text = tok.decode(tree_ids + out[0, ids.shape[1]:].tolist())
     if a.tool_use:
         from .tools import ToolRegistry
         text = ToolRegistry().run_calls(text)

@@ -589,3 +589,18 @@ def test_mtp_self_speculative_decoding_is_exact():
     from omnicoder.inference.generate import main as gen_main
     gen_main(["--preset", "tiny_moe", "--prompt", "hi", "--max_new_tokens", "3", "--device", "cpu",
               "--no_cuda_graph", "--multi_token_heads", "3"])
+
+
+def test_generate_cli_tree_reasoner(capsys):
+    import json
+    from omnicoder.inference.generate import main as gen_main
+    capsys.readouterr()
+    gen_main(["--preset", "tiny_moe", "--prompt", "2 + 2 =", "--max_new_tokens", "4", "--device", "cpu",
+              "--no_cuda_graph", "--json", "--reasoner", "tot", "--tree_depth", "2", "--tree_width", "2",
+              "--tree_iterations", "4"])
+    got = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert "text" in got
+    gen_main(["--preset", "tiny_moe", "--prompt", "hello", "--max_new_tokens", "2", "--device", "cpu",
+              "--no_cuda_graph", "--json", "--reasoner", "omega"])
+    got = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert "certificate" in got
